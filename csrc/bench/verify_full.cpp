@@ -1,0 +1,266 @@
+// verify_full: check ring-attention output dumps against exact attention
+// computed on the host over the whole (unsharded) sequence.
+//
+//   verify_full [output_dir] [num_gpus] [kv_size_bytes] [options]
+//
+// Positional arguments, defaults ("bench", 2, 262144), file names
+// (<dir>/ring_output_rank<r>.bin, raw little-endian fp32 [tokens x heads x dim])
+// and the report text follow the reference checker (ring/attention/verify_full.c).
+//
+// --init legacy (default): the reference's deterministic inputs (K == V, no
+//   softmax scale, one head, dim 64, contiguous shards); the oracle runs the
+//   same fp32 two-pass softmax as the reference; PASS iff no NaN/Inf and
+//   (max_abs < 0.05 or max_rel < 1e-5) -- verify_full.c:140-142.
+// --init randn: seeded N(0,1) Q, K, V from the shared counter-based generator,
+//   softmax scale 1/sqrt(dim) (or --scale), optional --causal, --layout
+//   contiguous|zigzag|striped, --heads H, --head-dim D; the oracle runs in fp64;
+//   PASS iff no NaN/Inf and max_abs <= --atol (default 1e-4).
+#include <algorithm>
+#include <cfloat>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../common/synth.hpp"
+#include "../sched/shard_plan.hpp"
+
+using namespace mgfa;
+
+namespace {
+
+struct Options {
+  std::string dir = "bench";
+  int num_gpus = 2;
+  long long kv_size = 262144;
+  bool randn = false;
+  uint64_t seed = 0;
+  int heads = 1;
+  int dim = 64;
+  bool causal = false;
+  std::string layout = "contiguous";
+  double scale = -1.0;
+  double atol = 1e-4;
+};
+
+template <class F>
+void parallel_for(int64_t n, F&& f) {
+  const int nt = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+  std::vector<std::thread> ts;
+  for (int t = 0; t < nt; ++t)
+    ts.emplace_back([&, t] {
+      for (int64_t i = t; i < n; i += nt) f(i);
+    });
+  for (auto& th : ts) th.join();
+}
+
+// Reference-faithful fp32 oracle (two passes, fp32 sums, no scale, K == V).
+void legacy_attention(const std::vector<float>& Q, int seq_q, const std::vector<float>& KV,
+                      int total_k, int dim, std::vector<float>& out) {
+  parallel_for(seq_q, [&](int64_t i) {
+    std::vector<float> scores(total_k);
+    float row_max = -FLT_MAX;
+    for (int j = 0; j < total_k; ++j) {
+      float s = 0.0f;
+      for (int d = 0; d < dim; ++d) s += Q[i * dim + d] * KV[size_t(j) * dim + d];
+      scores[j] = s;
+      row_max = std::max(row_max, s);
+    }
+    float row_sum = 0.0f;
+    std::vector<float> acc(dim, 0.0f);
+    for (int j = 0; j < total_k; ++j) {
+      const float w = std::exp(scores[j] - row_max);
+      row_sum += w;
+      for (int d = 0; d < dim; ++d) acc[d] += w * KV[size_t(j) * dim + d];
+    }
+    for (int d = 0; d < dim; ++d) out[i * dim + d] = acc[d] / row_sum;
+  });
+}
+
+bool read_dump(const std::string& path, std::vector<float>& buf, size_t n, size_t* got) {
+  FILE* fp = std::fopen(path.c_str(), "rb");
+  if (!fp) return false;
+  buf.assign(n, 0.0f);
+  *got = std::fread(buf.data(), sizeof(float), n, fp);
+  std::fclose(fp);
+  return true;
+}
+
+struct Cmp {
+  float max_abs = 0, max_rel = 0;
+  int worst = 0;
+  int nan_count = 0;
+};
+
+Cmp compare(const std::vector<float>& ring, const std::vector<float>& ref) {
+  Cmp c;
+  for (size_t i = 0; i < ref.size(); ++i) {
+    if (std::isnan(ring[i]) || std::isinf(ring[i])) { c.nan_count++; continue; }
+    const float a = std::fabs(ring[i] - ref[i]);
+    const float r = std::fabs(ref[i]) > 1e-6f ? a / std::fabs(ref[i]) : 0.0f;
+    if (a > c.max_abs) { c.max_abs = a; c.worst = int(i); }
+    c.max_rel = std::max(c.max_rel, r);
+  }
+  return c;
+}
+
+void report(int r, bool pass, size_t n, const Cmp& c, const std::vector<float>& ref,
+            const std::vector<float>& ring) {
+  std::printf("=== Rank %d === %s\n", r, pass ? "PASS" : "FAIL");
+  std::printf("  Elements compared : %d\n", int(n));
+  std::printf("  Max absolute error: %.6f\n", c.max_abs);
+  std::printf("  Max relative error: %.8f\n", c.max_rel);
+  std::printf("  Worst index       : %d (ref=%.4f, ring=%.4f)\n", c.worst, ref[c.worst],
+              ring[c.worst]);
+  std::printf("  NaN/Inf count     : %d\n\n", c.nan_count);
+}
+
+int run_legacy(const Options& o) {
+  const int dim = 64;
+  const int seq_k = int(o.kv_size / (dim * 4)), seq_q = seq_k;
+  const int total_k = seq_k * o.num_gpus;
+  const size_t n = size_t(seq_q) * dim;
+  std::vector<float> KV(size_t(total_k) * dim);
+  for (int r = 0; r < o.num_gpus; ++r)
+    for (int64_t i = 0; i < int64_t(seq_k) * dim; ++i)
+      KV[size_t(r) * seq_k * dim + i] = synth::legacy_kv(r, i);
+  std::vector<float> Q(n), ref(n), ring;
+  bool all_pass = true;
+  for (int r = 0; r < o.num_gpus; ++r) {
+    for (size_t i = 0; i < n; ++i) Q[i] = synth::legacy_q(r, int64_t(i), dim);
+    legacy_attention(Q, seq_q, KV, total_k, dim, ref);
+    const std::string fname = o.dir + "/ring_output_rank" + std::to_string(r) + ".bin";
+    size_t got = 0;
+    if (!read_dump(fname, ring, n, &got)) {
+      std::printf("=== Rank %d === SKIP (file not found)\n  Run ring code first to generate %s\n\n",
+                  r, fname.c_str());
+      all_pass = false;
+      continue;
+    }
+    if (got != n) {
+      std::printf("=== Rank %d === FAIL (read %zu of %d floats)\n\n", r, got, int(n));
+      all_pass = false;
+      continue;
+    }
+    const Cmp c = compare(ring, ref);
+    const bool pass = c.nan_count == 0 && (c.max_abs < 0.05f || c.max_rel < 1e-5f);
+    all_pass = all_pass && pass;
+    report(r, pass, n, c, ref, ring);
+  }
+  std::printf("============================\n");
+  std::printf("Overall: %s\n", all_pass ? "ALL PASS" : "SOME FAILED");
+  return all_pass ? 0 : 1;
+}
+
+int run_randn(const Options& o) {
+  const int H = o.heads, D = o.dim, P = o.num_gpus;
+  const int64_t local = o.kv_size / (int64_t(H) * D * 4);
+  const int64_t seq = local * P;
+  sched::ShardPlan plan;
+  sched::LayoutKind kind;
+  if (!sched::parse_layout(o.layout, &kind) || kind == sched::LayoutKind::Scheduler) {
+    std::fprintf(stderr, "unsupported --layout %s\n", o.layout.c_str());
+    return 2;
+  }
+  plan = kind == sched::LayoutKind::Zigzag   ? sched::make_zigzag(seq, P)
+         : kind == sched::LayoutKind::Striped ? sched::make_striped(seq, P)
+                                              : sched::make_contiguous(seq, P);
+  const double scale = o.scale > 0 ? o.scale : 1.0 / std::sqrt(double(D));
+  // Global K and V, [seq x H x D], fp32 values of the seeded streams.
+  std::vector<float> K(size_t(seq) * H * D), V(K.size());
+  parallel_for(seq, [&](int64_t t) {
+    for (int64_t e = t * H * D; e < (t + 1) * H * D; ++e) {
+      K[e] = float(synth::randn(o.seed, synth::kK, uint64_t(e)));
+      V[e] = float(synth::randn(o.seed, synth::kV, uint64_t(e)));
+    }
+  });
+  bool all_pass = true;
+  for (int r = 0; r < P; ++r) {
+    const std::vector<int64_t> pos = plan.positions(r);
+    const size_t n = size_t(local) * H * D;
+    std::vector<float> ref(n), ring;
+    parallel_for(local * H, [&](int64_t li) {
+      const int64_t i = li / H, h = li % H;
+      const int64_t qg = pos[i];
+      std::vector<double> q(D), acc(D, 0.0);
+      for (int d = 0; d < D; ++d)
+        q[d] = float(synth::randn(o.seed, synth::kQ, uint64_t((qg * H + h) * D + d)));
+      const int64_t kend = o.causal ? qg + 1 : seq;
+      double m = -1e300;
+      std::vector<double> s(static_cast<size_t>(kend));
+      for (int64_t j = 0; j < kend; ++j) {
+        double dot = 0.0;
+        const float* kr = &K[size_t((j * H + h) * D)];
+        for (int d = 0; d < D; ++d) dot += q[d] * double(kr[d]);
+        s[j] = dot * scale;
+        m = std::max(m, s[j]);
+      }
+      double l = 0.0;
+      for (int64_t j = 0; j < kend; ++j) {
+        const double w = std::exp(s[j] - m);
+        l += w;
+        const float* vr = &V[size_t((j * H + h) * D)];
+        for (int d = 0; d < D; ++d) acc[d] += w * double(vr[d]);
+      }
+      for (int d = 0; d < D; ++d) ref[size_t((i * H + h) * D + d)] = float(acc[d] / l);
+    });
+    const std::string fname = o.dir + "/ring_output_rank" + std::to_string(r) + ".bin";
+    size_t got = 0;
+    if (!read_dump(fname, ring, n, &got)) {
+      std::printf("=== Rank %d === SKIP (file not found)\n  Run ring code first to generate %s\n\n",
+                  r, fname.c_str());
+      all_pass = false;
+      continue;
+    }
+    if (got != n) {
+      std::printf("=== Rank %d === FAIL (read %zu of %d floats)\n\n", r, got, int(n));
+      all_pass = false;
+      continue;
+    }
+    const Cmp c = compare(ring, ref);
+    const bool pass = c.nan_count == 0 && c.max_abs <= o.atol;
+    all_pass = all_pass && pass;
+    report(r, pass, n, c, ref, ring);
+  }
+  std::printf("============================\n");
+  std::printf("Overall: %s\n", all_pass ? "ALL PASS" : "SOME FAILED");
+  return all_pass ? 0 : 1;
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+  Options o;
+  std::vector<std::string> pos;
+  for (int i = 1; i < argc; ++i) {
+    const std::string a = argv[i];
+    auto val = [&]() -> std::string {
+      if (i + 1 >= argc) { std::fprintf(stderr, "missing value for %s\n", a.c_str()); std::exit(2); }
+      return argv[++i];
+    };
+    if (a == "--init") o.randn = val() == "randn";
+    else if (a == "--seed") o.seed = std::strtoull(val().c_str(), nullptr, 10);
+    else if (a == "--heads") o.heads = std::atoi(val().c_str());
+    else if (a == "--head-dim") o.dim = std::atoi(val().c_str());
+    else if (a == "--causal") o.causal = true;
+    else if (a == "--layout") o.layout = val();
+    else if (a == "--scale") o.scale = std::atof(val().c_str());
+    else if (a == "--atol") o.atol = std::atof(val().c_str());
+    else pos.push_back(a);
+  }
+  if (pos.size() > 0) o.dir = pos[0];
+  if (pos.size() > 1) o.num_gpus = std::atoi(pos[1].c_str());
+  if (pos.size() > 2) o.kv_size = std::atoll(pos[2].c_str());
+  const long long unit = (o.randn ? (long long)o.heads * o.dim : 64) * 4;
+  if (o.num_gpus <= 0 || o.kv_size <= 0 || o.kv_size % unit != 0 || o.heads <= 0 || o.dim <= 0) {
+    std::fprintf(stderr,
+                 "Usage: %s [output_dir] [num_gpus] [kv_size_bytes]\n"
+                 "kv_size_bytes must be a positive multiple of %lld bytes.\n",
+                 argv[0], unit);
+    return 1;
+  }
+  return o.randn ? run_randn(o) : run_legacy(o);
+}

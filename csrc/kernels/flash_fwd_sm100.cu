@@ -1,0 +1,485 @@
+// Attention forward on sm_100a tensor cores (tcgen05 + TMEM + TMA), head_dim 128,
+// bf16 in, fp32 accumulate, bf16 or fp32-state out, with
+//   * causal masking from per-tile global token positions (contiguous, zigzag,
+//     striped and scheduler-driven shards all reduce to this),
+//   * an in-kernel LSE merge with the running output of earlier ring steps
+//     (the reference merges with a separate kernel and normalises on the host:
+//     ring/attention/bench/ring_attention_nccl_gpu_bench.cu:114-135, 398-407),
+//   * an optional in-kernel ring push of the current KV shard to the right
+//     neighbour's receive slot (peer stores + system-scope arrival counters).
+//
+// CTA = two 128-row query tiles of one (batch, head). Warp roles:
+//   warps 0-3  softmax for query tile 0 (thread t owns row t / TMEM lane t)
+//   warps 4-7  softmax for query tile 1
+//   warp  8    TMA producer (Q once, then K and V tiles, 2-stage rings)
+//   warp  9    MMA issuer (one thread): S = Q K^T (SS form), O += P V (TS form,
+//              P read from TMEM where it overwrote S)
+//   warp 10    ring push (only when a RingPush is enabled)
+// TMEM (512 columns): S0/P0 [0,128) S1/P1 [128,256) O0 [256,384) O1 [384,512).
+// The MMA order S0(j+1) after PV0(j) and S1(j+1) after PV1(j) lets one softmax
+// warpgroup work while the tensor core runs the other tile's GEMMs; a commit
+// for S(j+1) also proves PV(j) finished, so softmax may rescale O right away.
+// O is rescaled only when the running max grows by more than 2^8 (the stale
+// max keeps P <= 256, exact in fp32 sums and bf16 P).
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+
+#include <cmath>
+
+#include "flash_fwd_sm100.cuh"
+#include "sm100_ptx.cuh"
+#include "tma_host.hpp"
+
+namespace mgfa {
+namespace {
+
+using namespace mgfa::dev;
+
+constexpr int kD = 128;
+constexpr int kTile = 128;
+constexpr int kHalfBytes = kTile * 64 * 2;   // one 128 x 64 bf16 swizzled box
+constexpr int kTileBytes = 2 * kHalfBytes;   // 128 x 128 bf16
+constexpr int kWarps = 11;
+constexpr int kThreads = kWarps * 32;
+constexpr float kRescaleThreshold = 8.0f;    // log2 units
+
+struct __align__(1024) FwdSmem {
+  __nv_bfloat16 q[2][2][kTile * 64];  // [query tile][d half]
+  __nv_bfloat16 k[2][2][kTile * 64];  // [stage][d half]
+  __nv_bfloat16 v[2][2][kTile * 64];
+  uint64_t q_full;
+  uint64_t k_full[2], k_empty[2];
+  uint64_t v_full[2], v_empty[2];
+  uint64_t s_full[2], p_full[2];
+  uint64_t o_full;
+  uint64_t drain;
+  uint32_t tmem_base;
+  uint32_t abort_flag;
+};
+
+__device__ __forceinline__ bool q_tile_sees(const FwdParams& p, int qt, int kv_pos) {
+  if (qt >= p.n_q_tiles) return false;
+  return kv_pos <= p.q_tile_pos[qt] + (kTile - 1);
+}
+
+__device__ __forceinline__ bool tile_active(const FwdParams& p, int qt0, int j) {
+  if (!p.causal) return true;
+  const int kv_pos = p.kv_tile_pos[j];
+  return q_tile_sees(p, qt0, kv_pos) || q_tile_sees(p, qt0 + 1, kv_pos);
+}
+
+__device__ __forceinline__ int count_active(const FwdParams& p, int qt0) {
+  if (!p.causal) return p.n_kv_tiles;
+  int n = 0;
+  for (int j = 0; j < p.n_kv_tiles; ++j) n += tile_active(p, qt0, j) ? 1 : 0;
+  return n;
+}
+
+// ------------------------------------------------------------------ ring push
+__device__ void ring_push_warp(const RingPush& rp, uint32_t* status, uint64_t limit_ns,
+                               volatile uint32_t* abort_flag) {
+  const uint32_t lane = lane_id();
+  // Wait until the right neighbour is done with the slot we overwrite.
+  if (lane == 0) {
+    if (!wait_flag_geq(rp.credit, rp.credit_target, limit_ns, status, 10, 0)) *abort_flag = 1;
+  }
+  __syncwarp();
+  if (*abort_flag) return;
+  const uint64_t total = 2 * rp.bytes;
+  const uint64_t chunk = ((total / rp.n_chunks) + 15) & ~uint64_t(15);
+  const uint32_t linear_cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  const uint32_t n_ctas = gridDim.x * gridDim.y * gridDim.z;
+  for (uint32_t c = linear_cta; c < rp.n_chunks; c += n_ctas) {
+    const uint64_t b = uint64_t(c) * chunk;
+    const uint64_t e = b + chunk < total ? b + chunk : total;
+    // Copy [b, e) of the virtual concatenation K | V, 16 bytes per lane, 4 in flight.
+    for (uint64_t off = b + uint64_t(lane) * 16; off < e; off += 32 * 16 * 4) {
+      uint4 r[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint64_t o = off + uint64_t(u) * 32 * 16;
+        if (o < e) {
+          const uint8_t* src = o < rp.bytes ? rp.src_k + o : rp.src_v + (o - rp.bytes);
+          r[u] = __ldg(reinterpret_cast<const uint4*>(src));
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint64_t o = off + uint64_t(u) * 32 * 16;
+        if (o < e) {
+          uint8_t* dst = o < rp.bytes ? rp.dst_k + o : rp.dst_v + (o - rp.bytes);
+          *reinterpret_cast<uint4*>(dst) = r[u];
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) {
+      fence_sys();
+      red_release_sys_add(rp.peer_arrivals, 1u);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ kernel
+__global__ void __launch_bounds__(kThreads, 1)
+    flash_fwd_kernel(const __grid_constant__ CUtensorMap map_q,
+                     const __grid_constant__ CUtensorMap map_k,
+                     const __grid_constant__ CUtensorMap map_v, const FwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  FwdSmem& s = *reinterpret_cast<FwdSmem*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+  const uint32_t warp = warp_id(), lane = lane_id();
+  const int h = blockIdx.x;                 // query head
+  const int pair = gridDim.y - 1 - blockIdx.y;  // heaviest query tiles first (causal)
+  const int b = blockIdx.z;
+  const int hk = h / (p.hq / p.hkv);
+  const int qt0 = 2 * pair;
+
+  const int n_active = count_active(p, qt0);
+  const bool has_prior = p.merge != 0;
+  // No visible key tile: the running state is already correct unless this is
+  // the final step, which still has to convert it to the bf16 output.
+  const bool skip_compute = n_active == 0;
+  if (skip_compute && has_prior && !p.final_out && !p.push.enabled && !p.consume.enabled) return;
+
+  AbortState ab{&s.abort_flag, p.status, p.wait_limit_ns};
+  if (warp == 0) tmem_alloc<512>(&s.tmem_base);
+  if (threadIdx.x == 0) {
+    s.abort_flag = 0;
+    mbar_init(&s.q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.k_full[i], 1);
+      mbar_init(&s.k_empty[i], 1);
+      mbar_init(&s.v_full[i], 1);
+      mbar_init(&s.v_empty[i], 1);
+      mbar_init(&s.s_full[i], 1);
+      mbar_init(&s.p_full[i], 128);
+    }
+    mbar_init(&s.o_full, 1);
+    mbar_init(&s.drain, 1);
+    fence_mbar_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0 && !skip_compute) {
+      tma_prefetch_desc(&map_q);
+      tma_prefetch_desc(&map_k);
+      tma_prefetch_desc(&map_v);
+      mbar_arrive_expect_tx(&s.q_full, 2 * kTileBytes);
+      for (int t = 0; t < 2; ++t)
+        for (int hf = 0; hf < 2; ++hf)
+          tma_load_4d(s.q[t][hf], &map_q, &s.q_full, hf * 64, h, (qt0 + t) * kTile, b);
+      bool ok = true;
+      if (p.consume.enabled) {
+        ok = wait_flag_geq(p.consume.arrivals, p.consume.arrivals_target, p.wait_limit_ns,
+                           p.status, 8, 0);
+        if (!ok) s.abort_flag = 1;
+        // Data written by peers' generic stores, read here by the async proxy.
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+      }
+      int it = 0;
+      int last_k_phase[2] = {-1, -1}, last_v_phase[2] = {-1, -1};
+      for (int j = 0; ok && j < p.n_kv_tiles; ++j) {
+        if (!tile_active(p, qt0, j)) continue;
+        const int st = it & 1;
+        const uint32_t ph = (it >> 1) & 1;
+        if (!mbar_wait(&s.k_empty[st], ph ^ 1, ab, 81)) break;
+        mbar_arrive_expect_tx(&s.k_full[st], kTileBytes);
+        tma_load_4d(s.k[st][0], &map_k, &s.k_full[st], 0, hk, j * kTile, b);
+        tma_load_4d(s.k[st][1], &map_k, &s.k_full[st], 64, hk, j * kTile, b);
+        last_k_phase[st] = int(ph);
+        if (!mbar_wait(&s.v_empty[st], ph ^ 1, ab, 82)) break;
+        mbar_arrive_expect_tx(&s.v_full[st], kTileBytes);
+        tma_load_4d(s.v[st][0], &map_v, &s.v_full[st], 0, hk, j * kTile, b);
+        tma_load_4d(s.v[st][1], &map_v, &s.v_full[st], 64, hk, j * kTile, b);
+        last_v_phase[st] = int(ph);
+        ++it;
+      }
+      // Drain: never leave the CTA with a TMA write outstanding.
+      AbortState drain_ab{&s.abort_flag, nullptr, p.wait_limit_ns};
+      volatile uint32_t never = 0;
+      drain_ab.flag = &never;
+      mbar_wait(&s.q_full, 0, drain_ab, 0);
+      for (int st = 0; st < 2; ++st) {
+        if (last_k_phase[st] >= 0) mbar_wait(&s.k_full[st], uint32_t(last_k_phase[st]), drain_ab, 0);
+        if (last_v_phase[st] >= 0) mbar_wait(&s.v_full[st], uint32_t(last_v_phase[st]), drain_ab, 0);
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && !skip_compute) {
+      const uint32_t idesc_s = make_idesc_bf16(128, 128, 0, 0);
+      const uint32_t idesc_o = make_idesc_bf16(128, 128, 0, 1);
+      const uint32_t q_base[2] = {smem_u32(s.q[0][0]), smem_u32(s.q[1][0])};
+      auto issue_s = [&](int t, int st) {
+        const uint32_t kb = smem_u32(s.k[st][0]);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+          mma_ss(tmem + t * 128, make_sdesc_sw128(q_base[t] + off, 16, 1024),
+                 make_sdesc_sw128(kb + off, 16, 1024), idesc_s, kk > 0);
+        }
+      };
+      auto issue_o = [&](int t, int st, uint32_t acc) {
+        const uint32_t vb = smem_u32(s.v[st][0]);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          mma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
+                 make_sdesc_sw128(vb + kk * 2048, kHalfBytes, 1024), idesc_o,
+                 (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(&s.q_full, 0, ab, 90);
+      if (ok) ok = mbar_wait(&s.k_full[0], 0, ab, 91);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        mma_commit(&s.s_full[0]);
+        issue_s(1, 0);
+        mma_commit(&s.s_full[1]);
+        mma_commit(&s.k_empty[0]);
+      }
+      for (int it = 0; ok && it < n_active; ++it) {
+        const int st = it & 1;
+        const uint32_t ph = (it >> 1) & 1;
+        const int st1 = (it + 1) & 1;
+        const uint32_t ph1 = ((it + 1) >> 1) & 1;
+        const bool more = it + 1 < n_active;
+        if (!(ok = mbar_wait(&s.v_full[st], ph, ab, 92))) break;
+        if (!(ok = mbar_wait(&s.p_full[0], it & 1, ab, 93))) break;
+        tc_fence_after();
+        issue_o(0, st, it > 0);
+        if (more) {
+          if (!(ok = mbar_wait(&s.k_full[st1], ph1, ab, 94))) break;
+          tc_fence_after();
+          issue_s(0, st1);
+          mma_commit(&s.s_full[0]);
+        }
+        if (!(ok = mbar_wait(&s.p_full[1], it & 1, ab, 95))) break;
+        tc_fence_after();
+        issue_o(1, st, it > 0);
+        mma_commit(&s.v_empty[st]);
+        if (more) {
+          issue_s(1, st1);
+          mma_commit(&s.s_full[1]);
+          mma_commit(&s.k_empty[st1]);
+        }
+      }
+      if (ok) mma_commit(&s.o_full);
+      // Drain: every issued MMA has finished before TMEM is released.
+      mma_commit(&s.drain);
+      volatile uint32_t never = 0;
+      AbortState drain_ab{&never, nullptr, p.wait_limit_ns};
+      mbar_wait(&s.drain, 0, drain_ab, 0);
+    }
+  } else if (warp == 10) {
+    // ------------------------------------------------------------ ring push
+    if (p.push.enabled) ring_push_warp(p.push, p.status, p.wait_limit_ns, &s.abort_flag);
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue
+    const int t = warp >> 2;                // query tile within the CTA
+    const int qt = qt0 + t;
+    const int r = threadIdx.x & 127;        // row within the tile == TMEM lane
+    const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;
+    const uint32_t s_addr = tmem + lane_off + t * 128;
+    const uint32_t o_addr = tmem + lane_off + 256 + t * 128;
+    const int q_pos = (p.causal && qt < p.n_q_tiles) ? p.q_tile_pos[qt] + r : 0;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    int it = 0;
+    for (int j = 0; !skip_compute && j < p.n_kv_tiles; ++j) {
+      if (!tile_active(p, qt0, j)) continue;
+      ok = __all_sync(0xffffffffu, mbar_wait(&s.s_full[t], it & 1, ab, 20 + t));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t sr[128];
+      tmem_ld32(s_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+      tmem_ld32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+      tmem_ld32(s_addr + 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
+      tmem_ld32(s_addr + 96, *reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
+      tmem_wait_ld();
+      // Number of leading keys of this tile visible to this row.
+      int n_vis = p.sk - j * kTile;
+      if (p.causal) {
+        const int lim = q_pos - p.kv_tile_pos[j] + 1;
+        n_vis = lim < n_vis ? lim : n_vis;
+        if (qt >= p.n_q_tiles) n_vis = 0;
+      }
+      float x[128];
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        x[c] = (c < n_vis) ? __uint_as_float(sr[c]) * p.scale_log2 : -INFINITY;
+        tmax = fmaxf(tmax, x[c]);
+      }
+      const float m_new = fmaxf(m, tmax);
+      float alpha = 1.f;
+      bool rescale = false;
+      if (it == 0) {
+        m = m_new;
+      } else if (m_new > m + kRescaleThreshold) {
+        alpha = ex2_approx(m - m_new);
+        m = m_new;
+        rescale = true;
+      }
+      const float m_use = (m == -INFINITY) ? 0.f : m;
+      l *= alpha;
+      uint32_t pk[64];
+      float psum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const float p0 = ex2_approx(x[2 * c] - m_use);
+        const float p1 = ex2_approx(x[2 * c + 1] - m_use);
+        psum += p0 + p1;
+        pk[c] = pack_bf16(p0, p1);
+      }
+      l += psum;
+      tmem_st32(s_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
+      tmem_st32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
+      if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+          uint32_t orow[32];
+          tmem_ld32(o_addr + ch * 32, orow);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) orow[c] = __float_as_uint(__uint_as_float(orow[c]) * alpha);
+          tmem_st32(o_addr + ch * 32, orow);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&s.p_full[t]);
+      ++it;
+    }
+    if (!skip_compute && ok) ok = __all_sync(0xffffffffu, mbar_wait(&s.o_full, 0, ab, 30 + t));
+    ok = __all_sync(0xffffffffu, ok);
+    tc_fence_after();
+
+    // ---- epilogue: normalise, merge with the running state, store
+    const int row = qt * kTile + r;
+    const bool row_valid = qt < p.n_q_tiles && row < p.sq;
+    const float lse2_new = (l > 0.f) ? m + log2f(l) : -INFINITY;
+    const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
+    float w_prev = 0.f, w_new = 1.f, lse2 = lse2_new;
+    float* lse_ptr = p.lse + (int64_t(b) * p.hq + h) * p.sq + (row_valid ? row : 0);
+    const int64_t o_off = int64_t(b) * p.o_batch_stride + int64_t(row_valid ? row : 0) * p.o_row_stride +
+                          int64_t(h) * kD;
+    if (has_prior && row_valid) {
+      const float lse2_prev = *lse_ptr * 1.4426950408889634f;
+      const float mx = fmaxf(lse2_prev, lse2_new);
+      if (mx == -INFINITY) {
+        w_prev = 0.f;
+        w_new = 0.f;
+        lse2 = -INFINITY;
+      } else {
+        w_prev = ex2_approx(lse2_prev - mx);
+        w_new = ex2_approx(lse2_new - mx);
+        const float tot = w_prev + w_new;
+        w_prev /= tot;
+        w_new /= tot;
+        lse2 = mx + log2f(tot);
+      }
+    }
+    const float scale_new = w_new * inv_l;
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch) {
+      uint32_t orow[32];
+      if (!skip_compute && ok) {
+        tmem_ld32(o_addr + ch * 32, orow);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) orow[c] = 0u;
+      }
+      if (!row_valid || !ok) continue;
+      float v[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) v[c] = __uint_as_float(orow[c]) * scale_new;
+      if (has_prior) {
+        const float4* prev = reinterpret_cast<const float4*>(p.o_state + o_off + ch * 32);
+#pragma unroll
+        for (int q4 = 0; q4 < 8; ++q4) {
+          const float4 pv = prev[q4];
+          v[4 * q4 + 0] += w_prev * pv.x;
+          v[4 * q4 + 1] += w_prev * pv.y;
+          v[4 * q4 + 2] += w_prev * pv.z;
+          v[4 * q4 + 3] += w_prev * pv.w;
+        }
+      }
+      if (p.final_out) {
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.o) + o_off + ch * 32);
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8)
+          dst[q8] = make_uint4(pack_bf16(v[8 * q8 + 0], v[8 * q8 + 1]),
+                               pack_bf16(v[8 * q8 + 2], v[8 * q8 + 3]),
+                               pack_bf16(v[8 * q8 + 4], v[8 * q8 + 5]),
+                               pack_bf16(v[8 * q8 + 6], v[8 * q8 + 7]));
+      } else {
+        float4* dst = reinterpret_cast<float4*>(p.o_state + o_off + ch * 32);
+#pragma unroll
+        for (int q4 = 0; q4 < 8; ++q4)
+          dst[q4] = make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
+      }
+    }
+    if (row_valid && ok) *lse_ptr = lse2 * 0.6931471805599453f;
+  }
+
+  // ---- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc<512>(tmem);
+  if (p.consume.enabled && threadIdx.x == 0) {
+    // The last CTA to finish tells the left neighbour this slot may be reused.
+    __threadfence();
+    const uint32_t prev = atomicAdd(p.consume.done_counter, 1u);
+    if (prev == p.consume.done_target) {
+      fence_sys();
+      st_release_sys(p.consume.left_credit, p.consume.left_credit_value);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ host side
+CUtensorMap map_bshd(const torch::Tensor& t) {
+  // t: [B, S, H, 128] bf16, last dim contiguous.
+  TORCH_CHECK(t.stride(3) == 1, "head_dim must be contiguous");
+  const uint64_t dims[4] = {uint64_t(t.size(3)), uint64_t(t.size(2)), uint64_t(t.size(1)),
+                            uint64_t(t.size(0))};
+  const uint64_t strides[3] = {uint64_t(t.stride(2)) * 2, uint64_t(t.stride(1)) * 2,
+                               uint64_t(t.stride(0)) * 2};
+  const uint32_t box[4] = {64, 1, kTile, 1};
+  return host::make_bf16_map(t.data_ptr(), 4, dims, strides, box);
+}
+
+}  // namespace
+
+size_t flash_fwd_smem_bytes() { return sizeof(FwdSmem) + 1024; }
+
+void flash_fwd_launch(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v,
+                      FwdParams& p, cudaStream_t stream) {
+  const CUtensorMap mq = map_bshd(q), mk = map_bshd(k), mv = map_bshd(v);
+  static bool attr_set = false;
+  const int smem = int(flash_fwd_smem_bytes());
+  if (!attr_set) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(flash_fwd_kernel,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr_set = true;
+  }
+  const int n_pairs = (p.n_q_tiles + 1) / 2;
+  dim3 grid(p.hq, n_pairs, p.batch);
+  flash_fwd_kernel<<<grid, kThreads, smem, stream>>>(mq, mk, mv, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+int flash_fwd_grid_ctas(int hq, int n_q_tiles, int batch) {
+  return hq * ((n_q_tiles + 1) / 2) * batch;
+}
+
+}  // namespace mgfa

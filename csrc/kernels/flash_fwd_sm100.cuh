@@ -1,0 +1,60 @@
+// Parameters of the sm_100a attention forward kernel (shared by the launcher,
+// the ring engine and the kernel).
+#pragma once
+
+#include <cuda.h>
+#include <cstdint>
+
+namespace mgfa {
+
+// Optional in-kernel ring transport for one ring step: while the CTAs compute
+// on the current KV shard, one warp per CTA pushes a slice of that shard into
+// the right neighbour's receive slot with 16-byte stores through the peer
+// mapping, then bumps the neighbour's arrival counter (release, system scope).
+struct RingPush {
+  const uint8_t* src_k = nullptr;  // current shard (local memory)
+  const uint8_t* src_v = nullptr;
+  uint8_t* dst_k = nullptr;        // right neighbour's slot (peer memory)
+  uint8_t* dst_v = nullptr;
+  uint64_t bytes = 0;              // bytes of K (== bytes of V); multiple of 16
+  uint32_t* peer_arrivals = nullptr;  // right neighbour's arrival counter for that slot
+  const uint32_t* credit = nullptr;   // local: right neighbour's uses of that slot finished
+  uint32_t credit_target = 0;         // wait until *credit >= credit_target before writing
+  uint32_t n_chunks = 0;              // chunks the shard is cut into (same on every rank)
+  int enabled = 0;
+};
+
+// Consumer side of one ring step.
+struct RingConsume {
+  const uint32_t* arrivals = nullptr;  // local arrival counter of the slot being read
+  uint32_t arrivals_target = 0;        // wait until *arrivals >= target before reading
+  uint32_t* done_counter = nullptr;    // local counter of CTAs finished with this step
+  uint32_t done_target = 0;            // value the last CTA sees (uses * grid size - 1)
+  uint32_t* left_credit = nullptr;     // left neighbour's credit word for this slot
+  uint32_t left_credit_value = 0;      // value the last CTA publishes
+  int enabled = 0;
+};
+
+struct FwdParams {
+  int batch = 1, hq = 1, hkv = 1;
+  int sq = 0;              // query rows per sequence in this call
+  int sk = 0;              // key rows per sequence in the KV buffer
+  int n_q_tiles = 0, n_kv_tiles = 0;
+  float scale_log2 = 0.f;  // softmax scale * log2(e)
+  int causal = 0;
+  const int* q_tile_pos = nullptr;   // [n_q_tiles]  global start of each 128-row query tile
+  const int* kv_tile_pos = nullptr;  // [n_kv_tiles] global start of each 128-row key tile
+  // outputs; row strides in elements, [B, S, H, D] order
+  void* o = nullptr;                 // bf16 final output (when `final_out`)
+  float* o_state = nullptr;          // fp32 running output (normalised)
+  float* lse = nullptr;              // [B, Hq, sq] natural-log LSE
+  int64_t o_batch_stride = 0, o_row_stride = 0;
+  int merge = 0;                     // combine with the state already in o_state / lse
+  int final_out = 1;                 // 1: write bf16 `o`; 0: write fp32 `o_state`
+  uint32_t* status = nullptr;        // error word (0 = ok)
+  uint64_t wait_limit_ns = 2000000000ull;
+  RingPush push;
+  RingConsume consume;
+};
+
+}  // namespace mgfa

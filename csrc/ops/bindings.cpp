@@ -1,0 +1,34 @@
+// Module multi_gpu_flashattention_b200._C: the CUDA kernels and the native ring engine.
+#include <torch/extension.h>
+
+namespace mgfa {
+std::vector<torch::Tensor> umma_probe(torch::Tensor a, torch::Tensor b, torch::Tensor v);
+void flash_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, c10::optional<torch::Tensor> o,
+               c10::optional<torch::Tensor> o_state, torch::Tensor lse, double scale, bool causal,
+               c10::optional<torch::Tensor> q_tile_pos, c10::optional<torch::Tensor> kv_tile_pos,
+               bool merge, bool final_out, torch::Tensor status, int64_t wait_limit_ns);
+size_t flash_fwd_smem_bytes();
+void legacy_partial(torch::Tensor q, torch::Tensor k, torch::Tensor v, double scale,
+                    c10::optional<torch::Tensor> q_pos, c10::optional<torch::Tensor> k_pos,
+                    bool causal, torch::Tensor acc, torch::Tensor m, torch::Tensor l, bool merge);
+void legacy_merge(torch::Tensor m_run, torch::Tensor l_run, torch::Tensor acc_run,
+                  torch::Tensor m_new, torch::Tensor l_new, torch::Tensor acc_new);
+void legacy_normalize(torch::Tensor acc, torch::Tensor l, torch::Tensor out,
+                      c10::optional<torch::Tensor> lse, c10::optional<torch::Tensor> m);
+}  // namespace mgfa
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "sm_100a attention kernels and ring transport";
+  m.def("umma_probe", &mgfa::umma_probe, "tcgen05 self-test: (A B^T, A V, status)");
+  m.def("flash_fwd", &mgfa::flash_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"),
+        py::arg("o_state"), py::arg("lse"), py::arg("scale"), py::arg("causal"),
+        py::arg("q_tile_pos"), py::arg("kv_tile_pos"), py::arg("merge"), py::arg("final_out"),
+        py::arg("status"), py::arg("wait_limit_ns") = int64_t(2000000000));
+  m.def("flash_fwd_smem_bytes", &mgfa::flash_fwd_smem_bytes);
+  m.def("legacy_partial", &mgfa::legacy_partial, py::arg("q"), py::arg("k"), py::arg("v"),
+        py::arg("scale"), py::arg("q_pos"), py::arg("k_pos"), py::arg("causal"), py::arg("acc"),
+        py::arg("m"), py::arg("l"), py::arg("merge"));
+  m.def("legacy_merge", &mgfa::legacy_merge);
+  m.def("legacy_normalize", &mgfa::legacy_normalize, py::arg("acc"), py::arg("l"),
+        py::arg("out"), py::arg("lse") = py::none(), py::arg("m") = py::none());
+}

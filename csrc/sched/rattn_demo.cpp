@@ -1,0 +1,128 @@
+// rattn_demo: compare static partitions of one attention workload.
+//
+//   rattn_demo --seq N --gpus G [--block B] [--mask causal|full] [--alpha a]
+//              [--beta b] [--report] [--max-tasks T] [--max-rows R]
+//
+// Without --report it prints the one fixed-width table row of the reference
+// demo (workload/demo.c:108-118): seq, gpus, mask, blocks, then makespan and
+// imbalance for round-robin, block LPT, row LPT and contiguous DP, then the
+// ideal makespan. Conventions kept from the reference (workload/demo.c:14-124):
+//   * defaults block 128, alpha 1.21, beta 3.84e-6, causal;
+//   * tasks are costed with alpha = 0 and alpha is added once to every makespan;
+//   * imbalance = makespan / ideal, ideal = alpha + total / G;
+//   * at most 4096 block tasks and 256 block rows (the table is cut short the
+//     same way); --max-tasks / --max-rows lift those caps;
+//   * only "--mask full" changes the mask, any other word leaves it as it was.
+// --report adds per-gpu loads and max/mean imbalance for every partition.
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "scheduler.hpp"
+#include "workload.hpp"
+
+using namespace mgfa::sched;
+
+static void usage(const char* prog) {
+  std::printf(
+      "Usage: %s --seq <N> --gpus <G> [--block <B>] [--mask causal|full] [--alpha <a>] "
+      "[--beta <b>]\n",
+      prog);
+}
+
+static void print_loads(const char* name, const std::vector<double>& loads, double alpha) {
+  double mx = 0.0, sum = 0.0;
+  for (double l : loads) { mx = l > mx ? l : mx; sum += l; }
+  const double mean = loads.empty() ? 0.0 : sum / double(loads.size());
+  std::printf("  %-8s max/mean=%.4f loads:", name, mean > 0 ? mx / mean : 1.0);
+  for (double l : loads) std::printf(" %.4f", alpha + l);
+  std::printf("\n");
+}
+
+int main(int argc, char** argv) {
+  int seq = 0, gpus = 0, block = 128;
+  MaskKind mask = MaskKind::Causal;
+  double alpha = 1.21, beta = 0.00000384;
+  bool report = false;
+  long long max_tasks = 4096, max_rows = 256;
+
+  for (int i = 1; i < argc; ++i) {
+    const bool has_val = i + 1 < argc;
+    if (!std::strcmp(argv[i], "--seq") && has_val) seq = std::atoi(argv[++i]);
+    else if (!std::strcmp(argv[i], "--gpus") && has_val) gpus = std::atoi(argv[++i]);
+    else if (!std::strcmp(argv[i], "--block") && has_val) block = std::atoi(argv[++i]);
+    else if (!std::strcmp(argv[i], "--mask") && has_val) {
+      ++i;
+      if (!std::strcmp(argv[i], "full")) mask = MaskKind::Full;
+    } else if (!std::strcmp(argv[i], "--alpha") && has_val) alpha = std::atof(argv[++i]);
+    else if (!std::strcmp(argv[i], "--beta") && has_val) beta = std::atof(argv[++i]);
+    else if (!std::strcmp(argv[i], "--max-tasks") && has_val) max_tasks = std::atoll(argv[++i]);
+    else if (!std::strcmp(argv[i], "--max-rows") && has_val) max_rows = std::atoll(argv[++i]);
+    else if (!std::strcmp(argv[i], "--report")) report = true;
+  }
+  if (seq <= 0 || gpus <= 0 || block <= 0) {
+    usage(argv[0]);
+    return 1;
+  }
+
+  const WorkloadShape shape{seq, seq, block, block};
+  const CostModel task_model{0.0, beta};
+  std::vector<BlockTask> tasks =
+      build_block_tasks(shape, mask, task_model, size_t(max_tasks < 0 ? 0 : max_tasks));
+  const int count = int(tasks.size());
+
+  double total = 0.0;
+  for (const BlockTask& t : tasks) total += t.cost;
+  const double ideal = alpha + total / gpus;
+
+  Assignment rr = assign_round_robin(tasks, gpus);
+  const double rr_ms = alpha + rr.makespan();
+  Assignment blk = assign_block_lpt(tasks, gpus, LptMode::Scan);
+  const double blk_ms = alpha + blk.makespan();
+
+  if (num_row_blocks(shape) > max_rows) {
+    std::fprintf(stderr, "%d block rows exceed --max-rows %lld\n", num_row_blocks(shape),
+                 max_rows);
+    return 1;
+  }
+  std::vector<RowTask> rows = build_row_tasks(shape, tasks);
+  Assignment row = assign_row_lpt(rows, gpus, LptMode::Scan);
+  const double row_ms = alpha + row.makespan();
+
+  ContiguousPartition dp = partition_rows_contiguous(rows, gpus);
+  const double dp_ms = dp.ok ? alpha + dp.makespan() : -1.0;
+
+  std::printf("%-6d %-5d %-6s %-6d | %-10.2f %-6.3f | %-10.2f %-6.3f | %-10.2f %-6.3f | ", seq,
+              gpus, mask_name(mask), count, rr_ms, rr_ms / ideal, blk_ms, blk_ms / ideal, row_ms,
+              row_ms / ideal);
+  if (dp_ms >= 0) std::printf("%-10.2f %-6.3f | ", dp_ms, dp_ms / ideal);
+  else std::printf("%-10s %-6s | ", "N/A", "N/A");
+  std::printf("%-10.2f\n", ideal);
+
+  if (report) {
+    std::printf("per-gpu loads (alpha added once per gpu):\n");
+    auto loads_of = [](const Assignment& a) {
+      std::vector<double> v;
+      for (const GpuLoad& g : a.gpus) v.push_back(g.total_cost);
+      return v;
+    };
+    print_loads("RR", loads_of(rr), alpha);
+    print_loads("BlkLPT", loads_of(blk), alpha);
+    print_loads("RowLPT", loads_of(row), alpha);
+    if (dp.ok) {
+      std::vector<double> v;
+      for (const RowShard& s : dp.shards) v.push_back(s.total_cost);
+      print_loads("DP", v, alpha);
+      std::printf("  DP shards (block rows):");
+      for (const RowShard& s : dp.shards) std::printf(" [%d,%d)", s.row_begin, s.row_end);
+      std::printf("\n");
+    }
+    std::printf("block rows:");
+    for (const RowTask& r : rows)
+      std::printf(" %d:%d/%d", r.row, r.num_blocks, r.num_cols_needed);
+    std::printf("\n");
+  }
+  return 0;
+}

@@ -1,0 +1,87 @@
+"""Single-GPU attention on the sm_100a kernels.
+
+Tensors use the [batch, seq, heads, head_dim] layout. The tcgen05 kernel takes
+bf16 q/k/v with head_dim 128, any number of query heads that is a multiple of
+the kv heads (GQA/MQA), and writes a bf16 output plus an fp32 natural-log LSE
+[batch, heads, seq].
+
+Causal masking is expressed with per-tile global token positions: key tile j
+is visible to query tile i where kv_tile_pos[j] + c <= q_tile_pos[i] + r for
+row r, column c. Contiguous self-attention uses tile t -> 128 * t for both
+sides (top-left aligned); sharded layouts pass the positions of their tiles.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from .._ext import C
+
+TILE = 128
+DEFAULT_WAIT_LIMIT_NS = 2_000_000_000
+
+
+class KernelStatusError(RuntimeError):
+    """A kernel reported a non-zero status word (timeout, tag mismatch...)."""
+
+
+_CODES = {1: "mbarrier wait timed out", 2: "peer flag wait timed out",
+          3: "received slot carried the wrong tag", 4: "bad argument"}
+
+
+def check_status(status: torch.Tensor, what: str = "kernel") -> None:
+    """Raise KernelStatusError when `status` (int32 CUDA tensor) is non-zero.
+    Synchronises with the device."""
+    v = int(status.view(-1)[0].item()) & 0xFFFFFFFF
+    if v:
+        code, site, step = v & 0xFF, (v >> 8) & 0xFF, v >> 16
+        raise KernelStatusError(
+            f"{what}: {_CODES.get(code, 'error')} (code {code}, site {site}, step {step})")
+
+
+def tile_positions(n_tokens: int, device, start: int = 0) -> torch.Tensor:
+    """Global start positions of the 128-token tiles of a contiguous run."""
+    n = (n_tokens + TILE - 1) // TILE
+    return torch.arange(n, dtype=torch.int32, device=device) * TILE + start
+
+
+def _scale(q: torch.Tensor, softmax_scale: Optional[float]) -> float:
+    return softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(q.shape[-1])
+
+
+def flash_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
+                   softmax_scale: Optional[float] = None,
+                   q_tile_pos: Optional[torch.Tensor] = None,
+                   kv_tile_pos: Optional[torch.Tensor] = None,
+                   out: Optional[torch.Tensor] = None,
+                   status: Optional[torch.Tensor] = None,
+                   wait_limit_ns: int = DEFAULT_WAIT_LIMIT_NS):
+    """Forward attention; returns (out bf16 [B,Sq,Hq,D], lse fp32 [B,Hq,Sq])."""
+    B, Sq, Hq, _ = q.shape
+    if causal:
+        if q_tile_pos is None:
+            q_tile_pos = tile_positions(Sq, q.device)
+        if kv_tile_pos is None:
+            kv_tile_pos = tile_positions(k.shape[1], q.device)
+    o = out if out is not None else torch.empty_like(q)
+    lse = torch.empty(B, Hq, Sq, dtype=torch.float32, device=q.device)
+    st = status if status is not None else torch.zeros(1, dtype=torch.int32, device=q.device)
+    C().flash_fwd(q, k, v, o, None, lse, _scale(q, softmax_scale), causal, q_tile_pos,
+                  kv_tile_pos, False, True, st, int(wait_limit_ns))
+    return o, lse
+
+
+def flash_attn_fwd_step(q, k, v, o_state, lse, *, causal, softmax_scale=None, q_tile_pos=None,
+                        kv_tile_pos=None, merge: bool, final_out: bool, out=None, status=None,
+                        wait_limit_ns: int = DEFAULT_WAIT_LIMIT_NS):
+    """One partial pass of q over (k, v) merged into the running (o_state, lse).
+
+    o_state: fp32 [B,Sq,Hq,D] normalised running output; lse: fp32 [B,Hq,Sq].
+    With merge=False the pass starts a new state; with final_out=True the merged
+    result is written to `out` (bf16) instead of o_state."""
+    st = status if status is not None else torch.zeros(1, dtype=torch.int32, device=q.device)
+    C().flash_fwd(q, k, v, out, o_state, lse, _scale(q, softmax_scale), causal, q_tile_pos,
+                  kv_tile_pos, merge, final_out, st, int(wait_limit_ns))
+    return st
