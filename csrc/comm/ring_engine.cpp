@@ -1,0 +1,215 @@
+// Native ring-attention forward engine (fused transport).
+//
+// One call runs the whole ring on the caller's stream: P launches of the
+// sm_100a attention kernel, one per ring step. Step t computes the local
+// queries against the KV shard of owner (rank - t) mod P (the reference's
+// schedule, ring/attention/common/shard_utils.cuh:29-35) and, inside the same
+// kernel, pushes that shard to the right neighbour's receive slot (t+1) % 2
+// and merges its partial result into the running output. There is no host
+// synchronisation between steps: ordering across ranks is carried entirely by
+// the flag words of the symmetric buffer.
+//
+// Flags (see comm/symmetric.hpp):
+//   arrivals[s]  on the receiver, +1 per pushed chunk; the kernels of a step
+//                that reads slot s wait for n_chunks, the last CTA rearms it
+//   credit[s]    on the sender, the receiver's count of finished uses of its
+//                slot s; a push into slot s waits until it equals the uses so
+//                far (double buffering with back-pressure)
+//   done[s]      CTAs finished with slot s in this step (last CTA publishes)
+// All ranks call forward() in the same order, so the per-slot use counts kept
+// on the host agree everywhere.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include <memory>
+
+#include "../kernels/flash_fwd_sm100.cuh"
+#include "symmetric.hpp"
+
+namespace mgfa {
+
+class RingEngine {
+ public:
+  RingEngine(int rank, int world, int device, int64_t slot_bytes, int n_chunks)
+      : buf_(size_t(4 * slot_bytes), rank, world, device),
+        slot_bytes_(size_t(slot_bytes)),
+        n_chunks_(uint32_t(n_chunks)) {
+    TORCH_CHECK(slot_bytes > 0 && slot_bytes % 4096 == 0, "slot_bytes must be a multiple of 4096");
+    TORCH_CHECK(n_chunks > 0, "n_chunks must be positive");
+  }
+
+  py::bytes ipc_handle() const { return py::bytes(buf_.ipc_handle()); }
+
+  void connect(const std::vector<std::string>& handles) { buf_.open_peers(handles); }
+
+  int64_t slot_bytes() const { return int64_t(slot_bytes_); }
+  std::vector<int64_t> uses() const { return {int64_t(uses_[0]), int64_t(uses_[1])}; }
+
+  // q [B,Sq,Hq,128] bf16; k, v [B,L,Hkv,128] bf16 contiguous local shards (same L on
+  // every rank; owner o's first kv_lens[o] rows are valid).
+  // kv_tile_pos [P, ceil(L/128)] int32: tile positions of each owner's shard as seen
+  // from this rank's queries; q_tile_pos [ceil(Sq/128)] int32 (causal only).
+  std::vector<torch::Tensor> forward(torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                     double scale, bool causal,
+                                     c10::optional<torch::Tensor> q_tile_pos,
+                                     c10::optional<torch::Tensor> kv_tile_pos,
+                                     std::vector<int64_t> kv_lens, torch::Tensor status,
+                                     int64_t wait_limit_ns) {
+    return run(q, k, v, scale, causal, q_tile_pos, kv_tile_pos, kv_lens, status, wait_limit_ns,
+               /*transport=*/true);
+  }
+
+  // The same P launches with the transport switched off: every step computes on
+  // the local shard with the step's masks and lengths. The gap to forward() is
+  // the exposed communication time.
+  std::vector<torch::Tensor> forward_compute_only(torch::Tensor q, torch::Tensor k,
+                                                  torch::Tensor v, double scale, bool causal,
+                                                  c10::optional<torch::Tensor> q_tile_pos,
+                                                  c10::optional<torch::Tensor> kv_tile_pos,
+                                                  std::vector<int64_t> kv_lens,
+                                                  torch::Tensor status) {
+    return run(q, k, v, scale, causal, q_tile_pos, kv_tile_pos, kv_lens, status,
+               int64_t(2000000000), /*transport=*/false);
+  }
+
+ private:
+  std::vector<torch::Tensor> run(torch::Tensor q, torch::Tensor k, torch::Tensor v, double scale,
+                                 bool causal, c10::optional<torch::Tensor> q_tile_pos,
+                                 c10::optional<torch::Tensor> kv_tile_pos,
+                                 std::vector<int64_t> kv_lens, torch::Tensor status,
+                                 int64_t wait_limit_ns, bool transport) {
+    TORCH_CHECK(buf_.connected() || buf_.world() == 1, "RingEngine.connect() was not called");
+    TORCH_CHECK(q.is_cuda() && q.scalar_type() == at::kBFloat16 && q.dim() == 4 &&
+                    q.size(3) == 128 && q.is_contiguous(),
+                "q must be a contiguous bf16 [B,S,H,128] CUDA tensor");
+    TORCH_CHECK(k.scalar_type() == at::kBFloat16 && k.is_contiguous() && v.is_contiguous() &&
+                    k.sizes() == v.sizes() && k.dim() == 4 && k.size(3) == 128,
+                "k and v must be contiguous bf16 [B,L,Hkv,128] tensors of equal shape");
+    const int P = buf_.world(), r = buf_.rank();
+    const int right = (r + 1) % P, left = (r - 1 + P) % P;
+    const int64_t B = q.size(0), Sq = q.size(1), Hq = q.size(2), L = k.size(1), Hkv = k.size(2);
+    TORCH_CHECK(Hq % Hkv == 0, "query heads must be a multiple of kv heads");
+    const size_t shard_bytes = size_t(B * L * Hkv * 128 * 2);
+    TORCH_CHECK(P == 1 || shard_bytes <= slot_bytes_, "KV shard (", shard_bytes,
+                " B) exceeds the engine's slot (", slot_bytes_, " B)");
+    TORCH_CHECK(int64_t(kv_lens.size()) == P, "kv_lens needs one entry per rank");
+    const int n_q_tiles = int((Sq + 127) / 128), n_kv_tiles = int((L + 127) / 128);
+    if (causal) {
+      TORCH_CHECK(q_tile_pos.has_value() && q_tile_pos->scalar_type() == at::kInt &&
+                      q_tile_pos->numel() >= n_q_tiles,
+                  "causal ring attention needs int32 q_tile_pos");
+      TORCH_CHECK(kv_tile_pos.has_value() && kv_tile_pos->scalar_type() == at::kInt &&
+                      kv_tile_pos->is_contiguous() && kv_tile_pos->dim() == 2 &&
+                      kv_tile_pos->size(0) == P && kv_tile_pos->size(1) >= n_kv_tiles,
+                  "causal ring attention needs int32 kv_tile_pos [P, n_kv_tiles]");
+    }
+    c10::cuda::CUDAGuard guard(q.device());
+    cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+
+    auto o = torch::empty_like(q);
+    auto lse = torch::empty({B, Hq, Sq}, q.options().dtype(at::kFloat));
+    torch::Tensor o_state;
+    if (P > 1) o_state = torch::empty(q.sizes(), q.options().dtype(at::kFloat));
+
+    const CUtensorMap mq = make_bshd_map(q.data_ptr(), B, Sq, Hq, q.stride(0), q.stride(1),
+                                         q.stride(2));
+    const int64_t sb = L * Hkv * 128, ss = Hkv * 128, sh = 128;
+    auto slot_k = [&](int rank, int s) { return buf_.payload(rank) + size_t(s) * 2 * slot_bytes_; };
+    auto slot_v = [&](int rank, int s) { return slot_k(rank, s) + slot_bytes_; };
+    const int grid = flash_fwd_grid_ctas(int(Hq), n_q_tiles, int(B));
+
+    for (int t = 0; t < P; ++t) {
+      const int owner = ((r - t) % P + P) % P;
+      const int s = t & 1;
+      const bool own = t == 0 || !transport;
+      const uint8_t* cur_k = own ? static_cast<const uint8_t*>(k.data_ptr()) : slot_k(r, s);
+      const uint8_t* cur_v = own ? static_cast<const uint8_t*>(v.data_ptr()) : slot_v(r, s);
+      const CUtensorMap mk = make_bshd_map(cur_k, B, L, Hkv, sb, ss, sh);
+      const CUtensorMap mv = make_bshd_map(cur_v, B, L, Hkv, sb, ss, sh);
+
+      FwdParams p;
+      p.batch = int(B);
+      p.hq = int(Hq);
+      p.hkv = int(Hkv);
+      p.sq = int(Sq);
+      p.sk = int(kv_lens[owner]);
+      p.n_q_tiles = n_q_tiles;
+      p.n_kv_tiles = int((p.sk + 127) / 128);
+      p.scale_log2 = float(scale * 1.4426950408889634);
+      p.causal = causal ? 1 : 0;
+      if (causal) {
+        p.q_tile_pos = q_tile_pos->data_ptr<int>();
+        p.kv_tile_pos = kv_tile_pos->data_ptr<int>() + int64_t(owner) * kv_tile_pos->size(1);
+      }
+      p.o = o.data_ptr();
+      p.o_state = P > 1 ? o_state.data_ptr<float>() : nullptr;
+      p.lse = lse.data_ptr<float>();
+      p.o_batch_stride = q.stride(0);
+      p.o_row_stride = q.stride(1);
+      p.merge = t > 0 ? 1 : 0;
+      p.final_out = t == P - 1 ? 1 : 0;
+      p.status = reinterpret_cast<uint32_t*>(status.data_ptr<int>());
+      p.wait_limit_ns = uint64_t(wait_limit_ns);
+
+      if (transport && t < P - 1) {
+        const int sn = (t + 1) & 1;
+        p.push.enabled = 1;
+        p.push.src_k = cur_k;
+        p.push.src_v = cur_v;
+        p.push.dst_k = slot_k(right, sn);
+        p.push.dst_v = slot_v(right, sn);
+        p.push.bytes = shard_bytes;
+        p.push.peer_arrivals = buf_.flag(right, sn == 0 ? comm::kArrivals0 : comm::kArrivals1);
+        p.push.credit = buf_.flag(r, sn == 0 ? comm::kCredit0 : comm::kCredit1);
+        p.push.credit_target = uses_[sn];
+        p.push.n_chunks = n_chunks_;
+      }
+      if (transport && t > 0) {
+        p.consume.enabled = 1;
+        p.consume.arrivals = buf_.flag(r, s == 0 ? comm::kArrivals0 : comm::kArrivals1);
+        p.consume.arrivals_target = n_chunks_;
+        p.consume.done_counter = buf_.flag(r, s == 0 ? comm::kDone0 : comm::kDone1);
+        p.consume.done_target = uint32_t(grid - 1);
+        p.consume.left_credit = buf_.flag(left, s == 0 ? comm::kCredit0 : comm::kCredit1);
+        p.consume.left_credit_value = uses_[s] + 1;
+      }
+      flash_fwd_launch_maps(mq, mk, mv, p, stream);
+      if (transport && t > 0) uses_[s] += 1;
+    }
+    return {o, lse};
+  }
+
+ public:
+
+  // Zero local flags and use counts (collective: every rank, then a barrier).
+  void reset() {
+    buf_.reset_flags(at::cuda::getCurrentCUDAStream());
+    uses_[0] = uses_[1] = 0;
+  }
+
+ private:
+  comm::SymmetricBuffer buf_;
+  size_t slot_bytes_;
+  uint32_t n_chunks_;
+  uint32_t uses_[2] = {0, 0};
+};
+
+void register_ring_engine(py::module& m) {
+  py::class_<RingEngine, std::shared_ptr<RingEngine>>(m, "RingEngine")
+      .def(py::init<int, int, int, int64_t, int>(), py::arg("rank"), py::arg("world"),
+           py::arg("device"), py::arg("slot_bytes"), py::arg("n_chunks") = 1024)
+      .def("ipc_handle", &RingEngine::ipc_handle)
+      .def("connect", &RingEngine::connect)
+      .def("slot_bytes", &RingEngine::slot_bytes)
+      .def("uses", &RingEngine::uses)
+      .def("reset", &RingEngine::reset)
+      .def("forward", &RingEngine::forward, py::arg("q"), py::arg("k"), py::arg("v"),
+           py::arg("scale"), py::arg("causal"), py::arg("q_tile_pos"), py::arg("kv_tile_pos"),
+           py::arg("kv_lens"), py::arg("status"), py::arg("wait_limit_ns"))
+      .def("forward_compute_only", &RingEngine::forward_compute_only, py::arg("q"), py::arg("k"),
+           py::arg("v"), py::arg("scale"), py::arg("causal"), py::arg("q_tile_pos"),
+           py::arg("kv_tile_pos"), py::arg("kv_lens"), py::arg("status"));
+}
+
+}  // namespace mgfa

@@ -1,0 +1,71 @@
+// Symmetric device buffers: every rank allocates the same layout with
+// cudaMalloc, exports a CUDA IPC handle, and maps every peer's buffer into its
+// own address space, so kernels can store into (and signal) a neighbour's
+// memory over NVLink. Handles travel through whatever bootstrap the caller has
+// (torch.distributed from Python, a TCP store from the standalone benchmarks).
+//
+// Layout of one buffer:
+//   [0, kFlagBytes)          flag words, each on its own 128-byte line
+//   [kFlagBytes, ...)        payload (receive slots), 4 KB aligned
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+#include <vector>
+
+namespace mgfa::comm {
+
+constexpr size_t kFlagBytes = 64 * 1024;
+constexpr size_t kFlagStride = 128;  // bytes between flag words
+
+// Flag word indices.
+enum FlagIndex : int {
+  kArrivals0 = 0,   // chunks of slot 0 received (written by the left neighbour)
+  kArrivals1 = 1,
+  kCredit0 = 2,     // uses of the right neighbour's slot 0 it finished (written by it)
+  kCredit1 = 3,
+  kDone0 = 4,       // CTAs of this rank finished with slot 0 in the current step
+  kDone1 = 5,
+  kLoopArrivals = 8,  // pure-exchange benchmark counters
+  kLoopCredit = 9,
+  kStatus = 16,     // device error word of the last call
+};
+
+class SymmetricBuffer {
+ public:
+  SymmetricBuffer(size_t payload_bytes, int rank, int world, int device);
+  ~SymmetricBuffer();
+  SymmetricBuffer(const SymmetricBuffer&) = delete;
+  SymmetricBuffer& operator=(const SymmetricBuffer&) = delete;
+
+  // 64-byte cudaIpcMemHandle_t of the local allocation.
+  std::string ipc_handle() const;
+  // Map every peer's buffer; `handles[r]` is rank r's ipc_handle().
+  void open_peers(const std::vector<std::string>& handles);
+
+  int rank() const { return rank_; }
+  int world() const { return world_; }
+  int device() const { return device_; }
+  size_t payload_bytes() const { return payload_bytes_; }
+  bool connected() const { return connected_; }
+
+  uint8_t* base(int r) const { return r == rank_ ? local_ : peers_.at(r); }
+  uint8_t* payload(int r) const { return base(r) + kFlagBytes; }
+  uint32_t* flag(int r, int index) const {
+    return reinterpret_cast<uint32_t*>(base(r) + size_t(index) * kFlagStride);
+  }
+  // Zero the local flag words (call on every rank, then barrier, before use).
+  void reset_flags(cudaStream_t stream);
+
+ private:
+  int rank_, world_, device_;
+  size_t payload_bytes_;
+  uint8_t* local_ = nullptr;
+  std::vector<uint8_t*> peers_;
+  bool connected_ = false;
+};
+
+}  // namespace mgfa::comm

@@ -76,12 +76,17 @@ __device__ __forceinline__ int count_active(const FwdParams& p, int qt0) {
 }
 
 // ------------------------------------------------------------------ ring push
-__device__ void ring_push_warp(const RingPush& rp, uint32_t* status, uint64_t limit_ns,
-                               volatile uint32_t* abort_flag) {
+__device__ void ring_push_warp(const RingPush& rp, const RingConsume& rc, uint32_t* status,
+                               uint64_t limit_ns, volatile uint32_t* abort_flag) {
   const uint32_t lane = lane_id();
-  // Wait until the right neighbour is done with the slot we overwrite.
   if (lane == 0) {
-    if (!wait_flag_geq(rp.credit, rp.credit_target, limit_ns, status, 10, 0)) *abort_flag = 1;
+    // The shard we forward must have fully arrived here first...
+    if (rc.enabled &&
+        !wait_flag_geq(rc.arrivals, rc.arrivals_target, limit_ns, status, 11, 0))
+      *abort_flag = 1;
+    // ...and the right neighbour must be done with the slot we overwrite.
+    if (!*abort_flag && !wait_flag_geq(rp.credit, rp.credit_target, limit_ns, status, 10, 0))
+      *abort_flag = 1;
   }
   __syncwarp();
   if (*abort_flag) return;
@@ -100,7 +105,8 @@ __device__ void ring_push_warp(const RingPush& rp, uint32_t* status, uint64_t li
         const uint64_t o = off + uint64_t(u) * 32 * 16;
         if (o < e) {
           const uint8_t* src = o < rp.bytes ? rp.src_k + o : rp.src_v + (o - rp.bytes);
-          r[u] = __ldg(reinterpret_cast<const uint4*>(src));
+          // plain (coherent) load: the slot was written by a peer in this epoch
+          r[u] = *reinterpret_cast<const uint4*>(src);
         }
       }
 #pragma unroll
@@ -280,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 10) {
     // ------------------------------------------------------------ ring push
-    if (p.push.enabled) ring_push_warp(p.push, p.status, p.wait_limit_ns, &s.abort_flag);
+    if (p.push.enabled) ring_push_warp(p.push, p.consume, p.status, p.wait_limit_ns, &s.abort_flag);
   } else {
     // ------------------------------------------------------------ softmax + epilogue
     const int t = warp >> 2;                // query tile within the CTA
@@ -440,6 +446,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     __threadfence();
     const uint32_t prev = atomicAdd(p.consume.done_counter, 1u);
     if (prev == p.consume.done_target) {
+      // Every CTA has finished reading the slot: rearm the local counters, then
+      // hand the slot back to the left neighbour.
+      *p.consume.done_counter = 0u;
+      *p.consume.arrivals = 0u;
       fence_sys();
       st_release_sys(p.consume.left_credit, p.consume.left_credit_value);
     }
@@ -447,35 +457,44 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------ host side
-CUtensorMap map_bshd(const torch::Tensor& t) {
-  // t: [B, S, H, 128] bf16, last dim contiguous.
-  TORCH_CHECK(t.stride(3) == 1, "head_dim must be contiguous");
-  const uint64_t dims[4] = {uint64_t(t.size(3)), uint64_t(t.size(2)), uint64_t(t.size(1)),
-                            uint64_t(t.size(0))};
-  const uint64_t strides[3] = {uint64_t(t.stride(2)) * 2, uint64_t(t.stride(1)) * 2,
-                               uint64_t(t.stride(0)) * 2};
-  const uint32_t box[4] = {64, 1, kTile, 1};
-  return host::make_bf16_map(t.data_ptr(), 4, dims, strides, box);
-}
-
 }  // namespace
+
+CUtensorMap make_bshd_map(const void* base, int64_t B, int64_t S, int64_t H, int64_t stride_b,
+                          int64_t stride_s, int64_t stride_h) {
+  const uint64_t dims[4] = {uint64_t(kD), uint64_t(H), uint64_t(S), uint64_t(B)};
+  const uint64_t strides[3] = {uint64_t(stride_h) * 2, uint64_t(stride_s) * 2,
+                               uint64_t(stride_b) * 2};
+  const uint32_t box[4] = {64, 1, kTile, 1};
+  return host::make_bf16_map(base, 4, dims, strides, box);
+}
 
 size_t flash_fwd_smem_bytes() { return sizeof(FwdSmem) + 1024; }
 
-void flash_fwd_launch(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v,
-                      FwdParams& p, cudaStream_t stream) {
-  const CUtensorMap mq = map_bshd(q), mk = map_bshd(k), mv = map_bshd(v);
-  static bool attr_set = false;
+void flash_fwd_launch_maps(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                           FwdParams& p, cudaStream_t stream) {
+  static int attr_device = -1;
   const int smem = int(flash_fwd_smem_bytes());
-  if (!attr_set) {
+  int dev = 0;
+  C10_CUDA_CHECK(cudaGetDevice(&dev));
+  if (attr_device != dev) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(flash_fwd_kernel,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr_set = true;
+    attr_device = dev;
   }
   const int n_pairs = (p.n_q_tiles + 1) / 2;
   dim3 grid(p.hq, n_pairs, p.batch);
   flash_fwd_kernel<<<grid, kThreads, smem, stream>>>(mq, mk, mv, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void flash_fwd_launch(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v,
+                      FwdParams& p, cudaStream_t stream) {
+  auto map = [](const torch::Tensor& t) {
+    TORCH_CHECK(t.stride(3) == 1, "head_dim must be contiguous");
+    return make_bshd_map(t.data_ptr(), t.size(0), t.size(1), t.size(2), t.stride(0), t.stride(1),
+                         t.stride(2));
+  };
+  flash_fwd_launch_maps(map(q), map(k), map(v), p, stream);
 }
 
 int flash_fwd_grid_ctas(int hq, int n_q_tiles, int batch) {

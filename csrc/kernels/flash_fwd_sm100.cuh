@@ -26,10 +26,12 @@ struct RingPush {
 
 // Consumer side of one ring step.
 struct RingConsume {
-  const uint32_t* arrivals = nullptr;  // local arrival counter of the slot being read
-  uint32_t arrivals_target = 0;        // wait until *arrivals >= target before reading
+  uint32_t* arrivals = nullptr;        // local arrival counter of the slot being read
+  uint32_t arrivals_target = 0;        // wait until *arrivals >= target before reading;
+                                       // the last CTA resets it to 0
   uint32_t* done_counter = nullptr;    // local counter of CTAs finished with this step
-  uint32_t done_target = 0;            // value the last CTA sees (uses * grid size - 1)
+  uint32_t done_target = 0;            // value the last CTA sees (grid size - 1); it
+                                       // resets the counter to 0
   uint32_t* left_credit = nullptr;     // left neighbour's credit word for this slot
   uint32_t left_credit_value = 0;      // value the last CTA publishes
   int enabled = 0;
@@ -56,5 +58,13 @@ struct FwdParams {
   RingPush push;
   RingConsume consume;
 };
+
+// Host helpers (flash_fwd_sm100.cu).
+// Tensor map of a [B, S, H, 128] bf16 tensor with the given element strides.
+CUtensorMap make_bshd_map(const void* base, int64_t B, int64_t S, int64_t H,
+                          int64_t stride_b, int64_t stride_s, int64_t stride_h);
+void flash_fwd_launch_maps(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                           FwdParams& p, cudaStream_t stream);
+int flash_fwd_grid_ctas(int hq, int n_q_tiles, int batch);
 
 }  // namespace mgfa

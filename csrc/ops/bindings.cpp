@@ -15,6 +15,7 @@ void legacy_merge(torch::Tensor m_run, torch::Tensor l_run, torch::Tensor acc_ru
                   torch::Tensor m_new, torch::Tensor l_new, torch::Tensor acc_new);
 void legacy_normalize(torch::Tensor acc, torch::Tensor l, torch::Tensor out,
                       c10::optional<torch::Tensor> lse, c10::optional<torch::Tensor> m);
+void register_ring_engine(py::module& m);
 }  // namespace mgfa
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -31,4 +32,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("legacy_merge", &mgfa::legacy_merge);
   m.def("legacy_normalize", &mgfa::legacy_normalize, py::arg("acc"), py::arg("l"),
         py::arg("out"), py::arg("lse") = py::none(), py::arg("m") = py::none());
+  mgfa::register_ring_engine(m);
 }

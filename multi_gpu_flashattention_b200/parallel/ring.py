@@ -1,0 +1,256 @@
+"""Ring attention over a torch.distributed process group.
+
+Every rank holds the local shard (given by a RingLayout) of q, k and v in the
+[batch, local_seq, heads, head_dim] layout. Over P ring steps the KV shards
+travel to the right neighbour while each rank attends its queries to the shard
+it currently holds; the partial results are merged with their log-sum-exp.
+The schedule is the reference's: at step t rank r computes on the shard of
+owner (r - t) mod P and receives the shard of owner (r - t - 1) mod P
+(ring/attention/common/shard_utils.cuh:29-35,
+ring/attention/bench/ring_attention_nccl_gpu_bench.cu:349-397).
+
+Backends
+--------
+fused   (default on CUDA) one sm_100a kernel per step that computes, merges
+        in-kernel and pushes the current shard into the right neighbour's
+        receive slot with peer stores (native RingEngine).
+nccl    baseline: NCCL send/recv on a side stream, overlapped with the same
+        attention kernel (merge in-kernel).
+staged  baseline: device -> pinned host -> gloo send/recv -> device, the
+        reference's staged-MPI path re-expressed without MPI.
+torch   pure PyTorch fp32 on any device (the protocol oracle; CPU + gloo).
+"""
+from __future__ import annotations
+
+import math
+import os
+from typing import Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+from .._ext import C
+from ..ops.flash import (DEFAULT_WAIT_LIMIT_NS, check_status, flash_attn_fwd,
+                         flash_attn_fwd_step)
+from ..ops.reference import attention_ref
+from .layouts import RingLayout
+
+BACKENDS = ("fused", "nccl", "staged", "torch")
+
+
+def _world(group) -> Tuple[int, int]:
+    if group is None and not dist.is_initialized():
+        return 0, 1
+    return dist.get_rank(group), dist.get_world_size(group)
+
+
+def _global_rank(group, r: int) -> int:
+    return dist.get_global_rank(group, r) if group is not None else r
+
+
+# ---------------------------------------------------------------------- engine cache
+class _Engines:
+    """One native RingEngine per (process group, device); grown on demand.
+    Creating or growing an engine is collective over the group."""
+
+    def __init__(self):
+        self._by_key = {}
+
+    def get(self, group, device: torch.device, slot_bytes: int):
+        rank, world = _world(group)
+        key = (id(group), device.index)
+        eng = self._by_key.get(key)
+        if eng is not None and eng.slot_bytes() >= slot_bytes:
+            return eng
+        slot = max(slot_bytes, 1 << 20)
+        slot = (slot + (2 << 20) - 1) // (2 << 20) * (2 << 20)
+        if eng is not None:
+            torch.cuda.synchronize(device)
+            dist.barrier(group)  # every rank is past its last use of the old slots
+            self._by_key.pop(key)
+            del eng
+        eng = C().RingEngine(rank, world, device.index, slot, int(os.environ.get("MGFA_RING_CHUNKS", 1024)))
+        handles = [None] * world
+        dist.all_gather_object(handles, eng.ipc_handle(), group=group)
+        eng.connect(handles)
+        torch.cuda.synchronize(device)
+        dist.barrier(group)
+        self._by_key[key] = eng
+        return eng
+
+    def clear(self):
+        self._by_key.clear()
+
+
+ENGINES = _Engines()
+
+
+# ---------------------------------------------------------------------- metadata cache
+_META = {}
+
+
+def _meta(layout: RingLayout, rank: int, device):
+    key = (layout.kind, layout.seq, layout.world, layout.policy, layout.block, rank, str(device))
+    m = _META.get(key)
+    if m is None:
+        m = (layout.q_tile_pos(rank, device), layout.kv_tile_pos_by_owner(rank, device).contiguous(),
+             layout.kv_lens())
+        _META[key] = m
+    return m
+
+
+# ---------------------------------------------------------------------- forward backends
+def _fwd_fused(q, k, v, layout, causal, scale, group, status, wait_ns):
+    rank, world = _world(group)
+    qtp, kvtp, kv_lens = _meta(layout, rank, q.device)
+    shard_bytes = k.numel() * k.element_size()
+    eng = ENGINES.get(group, q.device, shard_bytes)
+    o, lse = eng.forward(q, k, v, scale, causal, qtp if causal else None,
+                         kvtp if causal else None, kv_lens, status, int(wait_ns))
+    return o, lse
+
+
+def _fwd_nccl(q, k, v, layout, causal, scale, group, status, wait_ns, overlap=True):
+    rank, world = _world(group)
+    qtp, kvtp, kv_lens = _meta(layout, rank, q.device)
+    right = _global_rank(group, (rank + 1) % world)
+    left = _global_rank(group, (rank - 1) % world)
+    compute = torch.cuda.current_stream(q.device)
+    comm = torch.cuda.Stream(q.device) if overlap else compute
+    o_state = torch.empty(q.shape, dtype=torch.float32, device=q.device)
+    lse = torch.empty(q.shape[0], q.shape[2], q.shape[1], dtype=torch.float32, device=q.device)
+    out = torch.empty_like(q)
+    cur = (k, v)
+    nxt = (torch.empty_like(k), torch.empty_like(v))
+    for t in range(world):
+        owner = (rank - t) % world
+        reqs = []
+        if t < world - 1:
+            comm.wait_stream(compute)
+            with torch.cuda.stream(comm):
+                ops = [dist.P2POp(dist.isend, cur[0], right, group),
+                       dist.P2POp(dist.isend, cur[1], right, group),
+                       dist.P2POp(dist.irecv, nxt[0], left, group),
+                       dist.P2POp(dist.irecv, nxt[1], left, group)]
+                reqs = dist.batch_isend_irecv(ops)
+            if not overlap:
+                for rq in reqs:
+                    rq.wait()
+        kl = kv_lens[owner]
+        flash_attn_fwd_step(q, cur[0][:, :kl], cur[1][:, :kl], o_state, lse, causal=causal,
+                            softmax_scale=scale, q_tile_pos=qtp, kv_tile_pos=kvtp[owner],
+                            merge=t > 0, final_out=t == world - 1, out=out, status=status,
+                            wait_limit_ns=wait_ns)
+        if t < world - 1:
+            if overlap:
+                with torch.cuda.stream(comm):
+                    for rq in reqs:
+                        rq.wait()
+                compute.wait_stream(comm)
+            cur, nxt = nxt, cur
+    return out, lse
+
+
+def _fwd_staged(q, k, v, layout, causal, scale, group, status, wait_ns, cpu_group=None):
+    """Device -> pinned host -> gloo -> pinned host -> device per step."""
+    rank, world = _world(cpu_group)
+    qtp, kvtp, kv_lens = _meta(layout, rank, q.device)
+    right, left = (rank + 1) % world, (rank - 1) % world
+    o_state = torch.empty(q.shape, dtype=torch.float32, device=q.device)
+    lse = torch.empty(q.shape[0], q.shape[2], q.shape[1], dtype=torch.float32, device=q.device)
+    out = torch.empty_like(q)
+    cur = (k, v)
+    h_send = [torch.empty(k.shape, dtype=k.dtype, pin_memory=True) for _ in range(2)]
+    h_recv = [torch.empty(k.shape, dtype=k.dtype, pin_memory=True) for _ in range(2)]
+    for t in range(world):
+        owner = (rank - t) % world
+        kl = kv_lens[owner]
+        flash_attn_fwd_step(q, cur[0][:, :kl], cur[1][:, :kl], o_state, lse, causal=causal,
+                            softmax_scale=scale, q_tile_pos=qtp, kv_tile_pos=kvtp[owner],
+                            merge=t > 0, final_out=t == world - 1, out=out, status=status,
+                            wait_limit_ns=wait_ns)
+        if t < world - 1:
+            for i in range(2):
+                h_send[i].copy_(cur[i], non_blocking=False)
+            reqs = []
+            for i in range(2):
+                reqs.append(dist.isend(h_send[i].view(torch.int16), _global_rank(cpu_group, right),
+                                       group=cpu_group))
+                reqs.append(dist.irecv(h_recv[i].view(torch.int16), _global_rank(cpu_group, left),
+                                       group=cpu_group))
+            for rq in reqs:
+                rq.wait()
+            cur = (h_recv[0].to(q.device, non_blocking=False), h_recv[1].to(q.device, non_blocking=False))
+    return out, lse
+
+
+def _fwd_torch(q, k, v, layout, causal, scale, group):
+    """Pure PyTorch fp32 ring (any device; gloo on CPU). Returns fp32 out, lse."""
+    rank, world = _world(group)
+    right = _global_rank(group, (rank + 1) % world)
+    left = _global_rank(group, (rank - 1) % world)
+    q_pos = layout.q_positions_for_mask(rank).to(q.device)
+    kv_lens = layout.kv_lens()
+    cur = (k.contiguous(), v.contiguous())
+    o = lse = None
+    for t in range(world):
+        owner = (rank - t) % world
+        reqs, nxt = [], None
+        if t < world - 1:
+            nxt = (torch.empty_like(cur[0]), torch.empty_like(cur[1]))
+            for i in range(2):
+                reqs.append(dist.isend(cur[i], right, group=group))
+                reqs.append(dist.irecv(nxt[i], left, group=group))
+        kl = kv_lens[owner]
+        k_pos = layout.k_positions_for_mask(rank, owner)[:kl].to(q.device)
+        o_t, lse_t = attention_ref(q, cur[0][:, :kl], cur[1][:, :kl], causal=causal,
+                                   softmax_scale=scale, q_pos=q_pos, k_pos=k_pos)
+        if o is None:
+            o, lse = o_t, lse_t
+        else:
+            new = torch.logaddexp(lse, lse_t)
+            w_old = torch.exp(lse - new).nan_to_num(0.0).transpose(1, 2).unsqueeze(-1)
+            w_new = torch.exp(lse_t - new).nan_to_num(0.0).transpose(1, 2).unsqueeze(-1)
+            o = o * w_old + o_t * w_new
+            lse = new
+        for rq in reqs:
+            rq.wait()
+        if nxt is not None:
+            cur = nxt
+    return o, lse
+
+
+def ring_attention_forward(q, k, v, layout: RingLayout, causal: bool = False,
+                           softmax_scale: Optional[float] = None, group=None,
+                           backend: Optional[str] = None, status: Optional[torch.Tensor] = None,
+                           wait_limit_ns: int = DEFAULT_WAIT_LIMIT_NS, check: bool = False,
+                           cpu_group=None):
+    """Forward ring attention on local shards; returns (out, lse).
+
+    out has q's dtype ([B, L, Hq, D]); lse is fp32 [B, Hq, L] (natural log).
+    With check=True the kernels' status word is read back (a device sync) and a
+    KernelStatusError raised on any timeout."""
+    scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    if backend is None:
+        backend = "fused" if q.is_cuda else "torch"
+    if backend not in BACKENDS:
+        raise ValueError(f"backend must be one of {BACKENDS}")
+    rank, world = _world(group)
+    if backend == "torch":
+        return _fwd_torch(q, k, v, layout, causal, scale, group)
+    st = status if status is not None else torch.zeros(1, dtype=torch.int32, device=q.device)
+    if world == 1:
+        qtp, kvtp, kv_lens = _meta(layout, rank, q.device)
+        out, lse = flash_attn_fwd(q, k[:, :kv_lens[0]], v[:, :kv_lens[0]], causal=causal,
+                                  softmax_scale=scale, q_tile_pos=qtp, kv_tile_pos=kvtp[0],
+                                  status=st, wait_limit_ns=wait_limit_ns)
+    elif backend == "fused":
+        out, lse = _fwd_fused(q, k, v, layout, causal, scale, group, st, wait_limit_ns)
+    elif backend == "nccl":
+        out, lse = _fwd_nccl(q, k, v, layout, causal, scale, group, st, wait_limit_ns)
+    else:
+        out, lse = _fwd_staged(q, k, v, layout, causal, scale, group, st, wait_limit_ns,
+                               cpu_group=cpu_group)
+    if check:
+        check_status(st, f"ring attention ({backend})")
+    return out, lse

@@ -50,6 +50,8 @@ if which in ("all", "cuda"):
                 "csrc/kernels/umma_probe.cu",
                 "csrc/kernels/flash_fwd_sm100.cu",
                 "csrc/kernels/legacy_fp32.cu",
+                "csrc/comm/symmetric.cpp",
+                "csrc/comm/ring_engine.cpp",
             ],
             include_dirs=[os.path.join(ROOT, "csrc")],
             extra_compile_args={

@@ -1,0 +1,55 @@
+"""Shard layouts: ownership, tile positions, shard/unshard round trips."""
+import pytest
+import torch
+
+from multi_gpu_flashattention_b200.parallel.layouts import RingLayout
+
+
+@pytest.mark.parametrize("kind", ["contiguous", "zigzag", "striped", "scheduler"])
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_layout_partitions_sequence(kind, world):
+    seq = 2048 * world if kind != "scheduler" else 4096
+    lay = RingLayout(kind, seq, world)
+    allpos = torch.cat([lay.positions(r) for r in range(world)])
+    assert torch.equal(allpos.sort().values, torch.arange(seq))
+    x = torch.randn(1, seq, 3, 4)
+    shards = [lay.shard(x, r) for r in range(world)]
+    assert all(s.shape[1] == lay.max_local_len for s in shards)
+    torch.testing.assert_close(lay.unshard(shards), x)
+
+
+def test_reference_ring_schedule():
+    lay = RingLayout("contiguous", 4096, 4)
+    # step s: compute on owner (r - s) mod P, receive (r - s - 1) mod P
+    for r in range(4):
+        for s in range(3):
+            assert lay.compute_owner(r, s) == (r - s) % 4
+            assert lay.receive_owner(r, s) == (r - s - 1) % 4
+    assert lay.describe(1) == "[1024,2048)"
+
+
+def test_zigzag_tile_positions_and_balance():
+    lay = RingLayout("zigzag", 8 * 1024, 4)
+    assert lay.describe(0) == "[0,1024)+[7168,8192)"
+    qtp = lay.q_tile_pos(0, "cpu")
+    assert qtp.tolist() == [0, 128, 256, 384, 512, 640, 768, 896] + [7168 + 128 * i for i in range(8)]
+    work = [sum(lay.step_work(r, o) for o in range(4)) for r in range(4)]
+    assert max(work) == min(work)  # zigzag balances causal work exactly
+
+
+def test_striped_tile_offsets():
+    lay = RingLayout("striped", 1024, 4)
+    assert lay.kv_tile_pos(2, 1, "cpu")[:2].tolist() == [0, 128]
+    assert lay.kv_tile_pos(2, 3, "cpu")[:2].tolist() == [1, 129]
+    assert lay.positions(1)[:3].tolist() == [1, 5, 9]
+
+
+def test_scheduler_layout_balances_better_than_contiguous():
+    seq, world = 8192, 4
+    cont = RingLayout("contiguous", seq, world)
+    dp = RingLayout("scheduler", seq, world, policy="dp")
+    def imbalance(lay):
+        w = [sum(lay.step_work(r, o) for o in range(world)) for r in range(world)]
+        return max(w) / (sum(w) / world)
+    assert imbalance(dp) < imbalance(cont)
+    assert dp.max_local_len > seq // world  # uneven shards, padded
