@@ -1,0 +1,633 @@
+// Attention backward on sm_100a tensor cores, head_dim 128, bf16 in, fp32 grads.
+//
+// Two kernels, no atomics (deterministic):
+//   dK/dV: CTA = one 128-key tile of one kv head; loops over every visible
+//          128-row query tile of every query head in its GQA group.
+//            S^T  = K Q^T     (SS)        -> TMEM [0,128)
+//            dP^T = V dO^T    (SS)        -> TMEM [128,256)
+//            P^T  = exp2(S^T*scale_log2 - lse2)     (bf16, over S^T in TMEM)
+//            dS^T = P^T * (dP^T - delta)           (bf16, over dP^T in TMEM)
+//            dV  += P^T dO    (TS, dO MN-major)     -> TMEM [256,384)
+//            dK  += dS^T Q    (TS, Q MN-major)      -> TMEM [384,512), * scale
+//   dQ:    CTA = one 128-row query tile; loops over visible key tiles.
+//            S  = Q K^T, dP = dO V^T (SS), dS = P * (dP - delta) written as bf16
+//            over dP, dQ += dS K (TS, K MN-major), * scale at the end.
+// MMA issue order lets the tensor core compute the next S while softmax
+// threads work on the current tile (S is read into registers before the next
+// S may overwrite it; P/dS buffers are consumed by MMAs issued earlier, and the
+// tensor pipe runs a thread's MMAs in order).
+// The reference prototype has no backward pass at all.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+
+#include <cmath>
+
+#include "flash_bwd_sm100.cuh"
+#include "sm100_ptx.cuh"
+
+namespace mgfa {
+namespace {
+
+using namespace mgfa::dev;
+
+constexpr int kTile = 128;
+constexpr int kHalfBytes = kTile * 64 * 2;
+constexpr int kTileBytes = 2 * kHalfBytes;
+constexpr int kThreads = 192;  // 4 softmax warps, 1 TMA warp, 1 MMA warp
+
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(smem_dst)),
+      "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void load_tile(void* dst, const CUtensorMap* m, uint64_t* bar, int h,
+                                          int row, int b) {
+  uint8_t* d = static_cast<uint8_t*>(dst);
+  tma_load_4d(d, m, bar, 0, h, row, b);
+  tma_load_4d(d + kHalfBytes, m, bar, 64, h, row, b);
+}
+
+// K-major 128x128 operand (two 64-column swizzled halves), k-step kk of 16.
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int kk) {
+  return make_sdesc_sw128(base + (kk >> 2) * kHalfBytes + (kk & 3) * 32, 16, 1024);
+}
+// MN-major B operand: rows are the K dimension (128 B each), N halves 16 KB apart.
+__device__ __forceinline__ uint64_t mnmajor_desc(uint32_t base, int kk) {
+  return make_sdesc_sw128(base + kk * 2048, kHalfBytes, 1024);
+}
+
+__device__ __forceinline__ void tmem_ld128(uint32_t addr, uint32_t (&r)[128]) {
+  tmem_ld32(addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+  tmem_ld32(addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+  tmem_ld32(addr + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[64]));
+  tmem_ld32(addr + 96, *reinterpret_cast<uint32_t(*)[32]>(&r[96]));
+  tmem_wait_ld();
+}
+
+__device__ __forceinline__ void store_grad_row(float* dst, const uint32_t (&acc)[128], float mul,
+                                               bool accumulate) {
+  float4* d = reinterpret_cast<float4*>(dst);
+#pragma unroll
+  for (int q4 = 0; q4 < 32; ++q4) {
+    float4 v = make_float4(__uint_as_float(acc[4 * q4]) * mul, __uint_as_float(acc[4 * q4 + 1]) * mul,
+                           __uint_as_float(acc[4 * q4 + 2]) * mul,
+                           __uint_as_float(acc[4 * q4 + 3]) * mul);
+    if (accumulate) {
+      const float4 o = d[q4];
+      v.x += o.x;
+      v.y += o.y;
+      v.z += o.z;
+      v.w += o.w;
+    }
+    d[q4] = v;
+  }
+}
+
+// ====================================================================== dQ
+struct __align__(1024) DqSmem {
+  __nv_bfloat16 q[kTile * 128];
+  __nv_bfloat16 dout[kTile * 128];
+  __nv_bfloat16 k[2][kTile * 128];
+  __nv_bfloat16 v[2][kTile * 128];
+  uint64_t qd_full;
+  uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
+  uint64_t s_full, s_free, dp_full, ds_full, dq_full, drain;
+  uint32_t tmem_base;
+  uint32_t abort_flag;
+};
+
+__device__ __forceinline__ bool dq_tile_active(const BwdParams& p, int qt, int j) {
+  if (!p.causal) return true;
+  return p.kv_tile_pos[j] <= p.q_tile_pos[qt] + (kTile - 1);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap map_q,
+                        const __grid_constant__ CUtensorMap map_do,
+                        const __grid_constant__ CUtensorMap map_k,
+                        const __grid_constant__ CUtensorMap map_v, const BwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  DqSmem& s = *reinterpret_cast<DqSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                         ~uintptr_t(1023));
+  const uint32_t warp = warp_id(), lane = lane_id();
+  const int h = blockIdx.x, qt = gridDim.y - 1 - blockIdx.y, b = blockIdx.z;
+  const int hk = h / (p.hq / p.hkv);
+  int n_active = 0;
+  for (int j = 0; j < p.n_kv_tiles; ++j) n_active += dq_tile_active(p, qt, j) ? 1 : 0;
+  if (n_active == 0 && p.accumulate) return;  // nothing to add
+
+  AbortState ab{&s.abort_flag, p.status, p.wait_limit_ns};
+  if (warp == 0) tmem_alloc<512>(&s.tmem_base);
+  if (threadIdx.x == 0) {
+    s.abort_flag = 0;
+    mbar_init(&s.qd_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.k_full[i], 1);
+      mbar_init(&s.k_empty[i], 1);
+      mbar_init(&s.v_full[i], 1);
+      mbar_init(&s.v_empty[i], 1);
+    }
+    mbar_init(&s.s_full, 1);
+    mbar_init(&s.s_free, 128);
+    mbar_init(&s.dp_full, 1);
+    mbar_init(&s.ds_full, 128);
+    mbar_init(&s.dq_full, 1);
+    mbar_init(&s.drain, 1);
+    fence_mbar_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+  const uint32_t S_COL = 0, DP_COL = 128, DQ_COL = 256;
+
+  if (warp == 4) {
+    if (lane == 0 && n_active > 0) {
+      mbar_arrive_expect_tx(&s.qd_full, 2 * kTileBytes);
+      load_tile(s.q, &map_q, &s.qd_full, h, qt * kTile, b);
+      load_tile(s.dout, &map_do, &s.qd_full, h, qt * kTile, b);
+      int it = 0;
+      int last_k[2] = {-1, -1}, last_v[2] = {-1, -1};
+      for (int j = 0; j < p.n_kv_tiles; ++j) {
+        if (!dq_tile_active(p, qt, j)) continue;
+        const int st = it & 1;
+        const uint32_t ph = (it >> 1) & 1;
+        if (!mbar_wait(&s.k_empty[st], ph ^ 1, ab, 41)) break;
+        mbar_arrive_expect_tx(&s.k_full[st], kTileBytes);
+        load_tile(s.k[st], &map_k, &s.k_full[st], hk, j * kTile, b);
+        last_k[st] = int(ph);
+        if (!mbar_wait(&s.v_empty[st], ph ^ 1, ab, 42)) break;
+        mbar_arrive_expect_tx(&s.v_full[st], kTileBytes);
+        load_tile(s.v[st], &map_v, &s.v_full[st], hk, j * kTile, b);
+        last_v[st] = int(ph);
+        ++it;
+      }
+      volatile uint32_t never = 0;
+      AbortState dab{&never, nullptr, p.wait_limit_ns};
+      mbar_wait(&s.qd_full, 0, dab, 0);
+      for (int st = 0; st < 2; ++st) {
+        if (last_k[st] >= 0) mbar_wait(&s.k_full[st], uint32_t(last_k[st]), dab, 0);
+        if (last_v[st] >= 0) mbar_wait(&s.v_full[st], uint32_t(last_v[st]), dab, 0);
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0 && n_active > 0) {
+      const uint32_t idesc_ss = make_idesc_bf16(128, 128, 0, 0);
+      const uint32_t idesc_ts = make_idesc_bf16(128, 128, 0, 1);
+      const uint32_t qb = smem_u32(s.q), db = smem_u32(s.dout);
+      auto gemm_s = [&](int st) {
+        const uint32_t kb = smem_u32(s.k[st]);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_ss(tmem + S_COL, kmajor_desc(qb, kk), kmajor_desc(kb, kk), idesc_ss, kk > 0);
+      };
+      auto gemm_dp = [&](int st) {
+        const uint32_t vb = smem_u32(s.v[st]);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_ss(tmem + DP_COL, kmajor_desc(db, kk), kmajor_desc(vb, kk), idesc_ss, kk > 0);
+      };
+      bool ok = mbar_wait(&s.qd_full, 0, ab, 50) && mbar_wait(&s.k_full[0], 0, ab, 51);
+      if (ok) {
+        tc_fence_after();
+        gemm_s(0);
+        mma_commit(&s.s_full);
+        ok = mbar_wait(&s.v_full[0], 0, ab, 52);
+        if (ok) {
+          tc_fence_after();
+          gemm_dp(0);
+          mma_commit(&s.dp_full);
+        }
+      }
+      for (int it = 0; ok && it < n_active; ++it) {
+        const int st = it & 1, st1 = (it + 1) & 1;
+        const uint32_t ph1 = ((it + 1) >> 1) & 1;
+        const bool more = it + 1 < n_active;
+        if (more) {
+          if (!(ok = mbar_wait(&s.k_full[st1], ph1, ab, 53))) break;
+          if (!(ok = mbar_wait(&s.s_free, it & 1, ab, 54))) break;
+          tc_fence_after();
+          gemm_s(st1);
+          mma_commit(&s.s_full);
+        }
+        if (!(ok = mbar_wait(&s.ds_full, it & 1, ab, 55))) break;
+        tc_fence_after();
+        const uint32_t kb = smem_u32(s.k[st]);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_ts(tmem + DQ_COL, tmem + DP_COL + kk * 8, mnmajor_desc(kb, kk), idesc_ts,
+                 (it > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&s.k_empty[st]);
+        mma_commit(&s.v_empty[st]);
+        if (more) {
+          if (!(ok = mbar_wait(&s.v_full[st1], ph1, ab, 56))) break;
+          tc_fence_after();
+          gemm_dp(st1);
+          mma_commit(&s.dp_full);
+        }
+      }
+      if (ok) mma_commit(&s.dq_full);
+      mma_commit(&s.drain);
+      volatile uint32_t never = 0;
+      AbortState dab{&never, nullptr, p.wait_limit_ns};
+      mbar_wait(&s.drain, 0, dab, 0);
+    }
+  } else if (warp < 4) {
+    const int r = threadIdx.x;
+    const uint32_t lane_off = uint32_t(warp * 32) << 16;
+    const int row = qt * kTile + r;
+    const bool row_valid = row < p.sq;
+    const int64_t ml = (int64_t(b) * p.hq + h) * p.sq_pad + row;
+    const float lse2 = p.lse2[ml];
+    const float dlt = p.delta[ml];
+    const int q_pos = p.causal ? p.q_tile_pos[qt] + r : 0;
+    bool ok = true;
+    int it = 0;
+    for (int j = 0; n_active > 0 && j < p.n_kv_tiles; ++j) {
+      if (!dq_tile_active(p, qt, j)) continue;
+      ok = __all_sync(0xffffffffu, mbar_wait(&s.s_full, it & 1, ab, 60));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t sr[128];
+      tmem_ld128(tmem + lane_off + S_COL, sr);
+      tc_fence_before();
+      mbar_arrive(&s.s_free);
+      int n_vis = p.sk - j * kTile;
+      if (p.causal) {
+        const int lim = q_pos - p.kv_tile_pos[j] + 1;
+        n_vis = lim < n_vis ? lim : n_vis;
+      }
+      if (!row_valid) n_vis = 0;
+      float pr[128];
+#pragma unroll
+      for (int c = 0; c < 128; ++c)
+        pr[c] = (c < n_vis) ? ex2_approx(__uint_as_float(sr[c]) * p.scale_log2 - lse2) : 0.f;
+      ok = __all_sync(0xffffffffu, mbar_wait(&s.dp_full, it & 1, ab, 61));
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t dpr[32];
+        tmem_ld32(tmem + lane_off + DP_COL + ch * 32, dpr);
+        tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const float d0 = pr[ch * 32 + 2 * c] * (__uint_as_float(dpr[2 * c]) - dlt);
+          const float d1 = pr[ch * 32 + 2 * c + 1] * (__uint_as_float(dpr[2 * c + 1]) - dlt);
+          pk[c] = pack_bf16(d0, d1);
+        }
+        // dS over the first 64 columns of the dP region (column ch*16.. holds
+        // keys ch*32 .. ch*32+31); the chunk just read is never overwritten before
+        // it is read because chunk ch's output lands in columns [16ch, 16ch+16).
+        tmem_st16(tmem + lane_off + DP_COL + ch * 16, pk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&s.ds_full);
+      ++it;
+    }
+    if (n_active > 0 && ok) ok = __all_sync(0xffffffffu, mbar_wait(&s.dq_full, 0, ab, 62));
+    ok = __all_sync(0xffffffffu, ok);
+    tc_fence_after();
+    uint32_t acc[128];
+    if (n_active > 0 && ok) {
+      tmem_ld128(tmem + lane_off + DQ_COL, acc);
+    } else {
+#pragma unroll
+      for (int c = 0; c < 128; ++c) acc[c] = 0u;
+    }
+    if (row_valid && ok)
+      store_grad_row(p.dq + int64_t(b) * p.dq_batch_stride + int64_t(row) * p.dq_row_stride +
+                         int64_t(h) * 128,
+                     acc, p.scale, p.accumulate != 0);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc<512>(tmem);
+}
+
+// ====================================================================== dK / dV
+struct __align__(1024) DkvSmem {
+  __nv_bfloat16 k[kTile * 128];
+  __nv_bfloat16 v[kTile * 128];
+  __nv_bfloat16 q[2][kTile * 128];
+  __nv_bfloat16 dout[2][kTile * 128];
+  float lse2[2][kTile];
+  float delta[2][kTile];
+  uint64_t kv_full;
+  uint64_t qd_full[2], qd_empty[2];
+  uint64_t s_full, dp_full, p_full, ds_full, dkv_full, drain;
+  uint32_t tmem_base;
+  uint32_t abort_flag;
+};
+
+__device__ __forceinline__ bool kv_sees(const BwdParams& p, int j, int qt) {
+  if (!p.causal) return true;
+  return p.kv_tile_pos[j] <= p.q_tile_pos[qt] + (kTile - 1);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap map_q,
+                          const __grid_constant__ CUtensorMap map_do,
+                          const __grid_constant__ CUtensorMap map_k,
+                          const __grid_constant__ CUtensorMap map_v, const BwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  DkvSmem& s = *reinterpret_cast<DkvSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                           ~uintptr_t(1023));
+  const uint32_t warp = warp_id(), lane = lane_id();
+  const int hk = blockIdx.x, j = gridDim.y - 1 - blockIdx.y, b = blockIdx.z;
+  const int G = p.hq / p.hkv;
+  int n_q_active = 0;
+  for (int qt = 0; qt < p.n_q_tiles; ++qt) n_q_active += kv_sees(p, j, qt) ? 1 : 0;
+  const int n_iter = n_q_active * G;
+  if (n_iter == 0 && p.accumulate) return;
+
+  AbortState ab{&s.abort_flag, p.status, p.wait_limit_ns};
+  if (warp == 0) tmem_alloc<512>(&s.tmem_base);
+  if (threadIdx.x == 0) {
+    s.abort_flag = 0;
+    mbar_init(&s.kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.qd_full[i], 1);
+      mbar_init(&s.qd_empty[i], 1);
+    }
+    mbar_init(&s.s_full, 1);
+    mbar_init(&s.dp_full, 1);
+    mbar_init(&s.p_full, 128);
+    mbar_init(&s.ds_full, 128);
+    mbar_init(&s.dkv_full, 1);
+    mbar_init(&s.drain, 1);
+    fence_mbar_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+  const uint32_t ST_COL = 0, DPT_COL = 128, DV_COL = 256, DK_COL = 384;
+
+  if (warp == 4) {
+    if (lane == 0 && n_iter > 0) {
+      mbar_arrive_expect_tx(&s.kv_full, 2 * kTileBytes);
+      load_tile(s.k, &map_k, &s.kv_full, hk, j * kTile, b);
+      load_tile(s.v, &map_v, &s.kv_full, hk, j * kTile, b);
+      int it = 0;
+      int last[2] = {-1, -1};
+      bool ok = true;
+      for (int g = 0; ok && g < G; ++g) {
+        const int h = hk * G + g;
+        const int64_t mlbase = (int64_t(b) * p.hq + h) * p.sq_pad;
+        for (int qt = 0; qt < p.n_q_tiles; ++qt) {
+          if (!kv_sees(p, j, qt)) continue;
+          const int st = it & 1;
+          const uint32_t ph = (it >> 1) & 1;
+          if (!(ok = mbar_wait(&s.qd_empty[st], ph ^ 1, ab, 71))) break;
+          mbar_arrive_expect_tx(&s.qd_full[st], 2 * kTileBytes + 2 * kTile * 4);
+          load_tile(s.q[st], &map_q, &s.qd_full[st], h, qt * kTile, b);
+          load_tile(s.dout[st], &map_do, &s.qd_full[st], h, qt * kTile, b);
+          bulk_load(s.lse2[st], p.lse2 + mlbase + qt * kTile, kTile * 4, &s.qd_full[st]);
+          bulk_load(s.delta[st], p.delta + mlbase + qt * kTile, kTile * 4, &s.qd_full[st]);
+          last[st] = int(ph);
+          ++it;
+        }
+      }
+      volatile uint32_t never = 0;
+      AbortState dab{&never, nullptr, p.wait_limit_ns};
+      mbar_wait(&s.kv_full, 0, dab, 0);
+      for (int st = 0; st < 2; ++st)
+        if (last[st] >= 0) mbar_wait(&s.qd_full[st], uint32_t(last[st]), dab, 0);
+    }
+  } else if (warp == 5) {
+    if (lane == 0 && n_iter > 0) {
+      const uint32_t idesc_ss = make_idesc_bf16(128, 128, 0, 0);
+      const uint32_t idesc_ts = make_idesc_bf16(128, 128, 0, 1);
+      const uint32_t kb = smem_u32(s.k), vb = smem_u32(s.v);
+      auto gemm_st = [&](int st) {
+        const uint32_t qb = smem_u32(s.q[st]);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_ss(tmem + ST_COL, kmajor_desc(kb, kk), kmajor_desc(qb, kk), idesc_ss, kk > 0);
+      };
+      auto gemm_dpt = [&](int st) {
+        const uint32_t db = smem_u32(s.dout[st]);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_ss(tmem + DPT_COL, kmajor_desc(vb, kk), kmajor_desc(db, kk), idesc_ss, kk > 0);
+      };
+      bool ok = mbar_wait(&s.kv_full, 0, ab, 80) && mbar_wait(&s.qd_full[0], 0, ab, 81);
+      if (ok) {
+        tc_fence_after();
+        gemm_st(0);
+        mma_commit(&s.s_full);
+        gemm_dpt(0);
+        mma_commit(&s.dp_full);
+      }
+      for (int it = 0; ok && it < n_iter; ++it) {
+        const int st = it & 1, st1 = (it + 1) & 1;
+        const uint32_t ph1 = ((it + 1) >> 1) & 1;
+        const bool more = it + 1 < n_iter;
+        if (!(ok = mbar_wait(&s.p_full, it & 1, ab, 82))) break;
+        tc_fence_after();
+        const uint32_t db = smem_u32(s.dout[st]), qb = smem_u32(s.q[st]);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_ts(tmem + DV_COL, tmem + ST_COL + kk * 8, mnmajor_desc(db, kk), idesc_ts,
+                 (it > 0 || kk > 0) ? 1u : 0u);
+        if (more) {
+          if (!(ok = mbar_wait(&s.qd_full[st1], ph1, ab, 83))) break;
+          tc_fence_after();
+          gemm_st(st1);
+          mma_commit(&s.s_full);
+        }
+        if (!(ok = mbar_wait(&s.ds_full, it & 1, ab, 84))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_ts(tmem + DK_COL, tmem + DPT_COL + kk * 8, mnmajor_desc(qb, kk), idesc_ts,
+                 (it > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&s.qd_empty[st]);
+        if (more) {
+          gemm_dpt(st1);
+          mma_commit(&s.dp_full);
+        }
+      }
+      if (ok) mma_commit(&s.dkv_full);
+      mma_commit(&s.drain);
+      volatile uint32_t never = 0;
+      AbortState dab{&never, nullptr, p.wait_limit_ns};
+      mbar_wait(&s.drain, 0, dab, 0);
+    }
+  } else if (warp < 4) {
+    const int r = threadIdx.x;  // key row within the tile == TMEM lane
+    const uint32_t lane_off = uint32_t(warp * 32) << 16;
+    const int key = j * kTile + r;
+    const bool key_valid = key < p.sk;
+    const int k_pos = p.causal ? p.kv_tile_pos[j] + r : 0;
+    bool ok = true;
+    int it = 0;
+    for (int g = 0; ok && g < G; ++g) {
+      for (int qt = 0; qt < p.n_q_tiles; ++qt) {
+        if (!kv_sees(p, j, qt)) continue;
+        const int st = it & 1;
+        ok = __all_sync(0xffffffffu, mbar_wait(&s.s_full, it & 1, ab, 90));
+        if (!ok) break;
+        tc_fence_after();
+        uint32_t sr[128];
+        tmem_ld128(tmem + lane_off + ST_COL, sr);
+        // visible query columns c: q_pos(c) >= k_pos and the query row exists
+        int c_lo = 0;
+        int c_hi = p.sq - qt * kTile;  // exclusive
+        if (p.causal) {
+          const int lo = k_pos - p.q_tile_pos[qt];
+          c_lo = lo > 0 ? lo : 0;
+        }
+        if (!key_valid) c_hi = 0;
+        const float* lse2 = s.lse2[st];
+        float pr[128];
+#pragma unroll
+        for (int c = 0; c < 128; ++c)
+          pr[c] = (c >= c_lo && c < c_hi)
+                      ? ex2_approx(__uint_as_float(sr[c]) * p.scale_log2 - lse2[c])
+                      : 0.f;
+        uint32_t pk[64];
+#pragma unroll
+        for (int c = 0; c < 64; ++c) pk[c] = pack_bf16(pr[2 * c], pr[2 * c + 1]);
+        tmem_st32(tmem + lane_off + ST_COL, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
+        tmem_st32(tmem + lane_off + ST_COL + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&s.p_full);
+        ok = __all_sync(0xffffffffu, mbar_wait(&s.dp_full, it & 1, ab, 91));
+        if (!ok) break;
+        tc_fence_after();
+        const float* dl = s.delta[st];
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+          uint32_t dpr[32];
+          tmem_ld32(tmem + lane_off + DPT_COL + ch * 32, dpr);
+          tmem_wait_ld();
+          uint32_t dk[16];
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const int c0 = ch * 32 + 2 * c;
+            const float d0 = pr[c0] * (__uint_as_float(dpr[2 * c]) - dl[c0]);
+            const float d1 = pr[c0 + 1] * (__uint_as_float(dpr[2 * c + 1]) - dl[c0 + 1]);
+            dk[c] = pack_bf16(d0, d1);
+          }
+          tmem_st16(tmem + lane_off + DPT_COL + ch * 16, dk);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&s.ds_full);
+        ++it;
+      }
+    }
+    if (n_iter > 0 && ok) ok = __all_sync(0xffffffffu, mbar_wait(&s.dkv_full, 0, ab, 92));
+    ok = __all_sync(0xffffffffu, ok);
+    tc_fence_after();
+    uint32_t acc[128];
+    const int64_t off = int64_t(b) * p.dkv_batch_stride + int64_t(key) * p.dkv_row_stride +
+                        int64_t(hk) * 128;
+    if (n_iter > 0 && ok) {
+      tmem_ld128(tmem + lane_off + DV_COL, acc);
+    } else {
+#pragma unroll
+      for (int c = 0; c < 128; ++c) acc[c] = 0u;
+    }
+    if (key_valid && ok) store_grad_row(p.dv + off, acc, 1.f, p.accumulate != 0);
+    if (n_iter > 0 && ok) tmem_ld128(tmem + lane_off + DK_COL, acc);
+    if (key_valid && ok) store_grad_row(p.dk + off, acc, p.scale, p.accumulate != 0);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc<512>(tmem);
+}
+
+// ====================================================================== preprocess
+__global__ void bwd_preprocess_kernel(const __nv_bfloat16* __restrict__ o,
+                                      const __nv_bfloat16* __restrict__ dout, int64_t o_sb,
+                                      int64_t o_ss, int64_t do_sb, int64_t do_ss,
+                                      const float* __restrict__ lse, int S, int H, int s_pad,
+                                      float* __restrict__ lse2, float* __restrict__ delta) {
+  // one warp per (b, h, row); row in [0, s_pad)
+  const int64_t wid = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wid >= int64_t(H) * s_pad) return;
+  const int row = int(wid % s_pad);
+  const int h = int(wid / s_pad);
+  const int b = blockIdx.y;
+  float acc = 0.f;
+  float l2 = INFINITY;
+  if (row < S) {
+    const __nv_bfloat16* op = o + b * o_sb + int64_t(row) * o_ss + int64_t(h) * 128;
+    const __nv_bfloat16* dp = dout + b * do_sb + int64_t(row) * do_ss + int64_t(h) * 128;
+    const uint2 ov = reinterpret_cast<const uint2*>(op)[lane];
+    const uint2 dv = reinterpret_cast<const uint2*>(dp)[lane];
+    const __nv_bfloat162* o2 = reinterpret_cast<const __nv_bfloat162*>(&ov);
+    const __nv_bfloat162* d2 = reinterpret_cast<const __nv_bfloat162*>(&dv);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float2 a = __bfloat1622float2(o2[i]), c = __bfloat1622float2(d2[i]);
+      acc += a.x * c.x + a.y * c.y;
+    }
+    const float lv = lse[(int64_t(b) * H + h) * S + row];
+    l2 = (lv == -INFINITY) ? INFINITY : lv * 1.4426950408889634f;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) {
+    const int64_t idx = (int64_t(b) * H + h) * s_pad + row;
+    delta[idx] = acc;
+    lse2[idx] = l2;
+  }
+}
+
+template <class Smem, class Kernel>
+void set_smem(Kernel k, int& done_dev) {
+  int dev = 0;
+  C10_CUDA_CHECK(cudaGetDevice(&dev));
+  if (done_dev != dev) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        int(sizeof(Smem) + 1024)));
+    done_dev = dev;
+  }
+}
+
+}  // namespace
+
+void flash_bwd_dq_launch(const CUtensorMap& mq, const CUtensorMap& mdo, const CUtensorMap& mk,
+                         const CUtensorMap& mv, BwdParams& p, cudaStream_t stream) {
+  static int done_dev = -1;
+  set_smem<DqSmem>(flash_bwd_dq_kernel, done_dev);
+  dim3 grid(p.hq, p.n_q_tiles, p.batch);
+  flash_bwd_dq_kernel<<<grid, kThreads, sizeof(DqSmem) + 1024, stream>>>(mq, mdo, mk, mv, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void flash_bwd_dkdv_launch(const CUtensorMap& mq, const CUtensorMap& mdo, const CUtensorMap& mk,
+                           const CUtensorMap& mv, BwdParams& p, cudaStream_t stream) {
+  static int done_dev = -1;
+  set_smem<DkvSmem>(flash_bwd_dkdv_kernel, done_dev);
+  dim3 grid(p.hkv, p.n_kv_tiles, p.batch);
+  flash_bwd_dkdv_kernel<<<grid, kThreads, sizeof(DkvSmem) + 1024, stream>>>(mq, mdo, mk, mv, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void flash_bwd_preprocess_launch(const void* o, const void* dout, int64_t o_sb, int64_t o_ss,
+                                 int64_t do_sb, int64_t do_ss, const float* lse, int B, int S,
+                                 int H, int s_pad, float* lse2, float* delta,
+                                 cudaStream_t stream) {
+  const int64_t warps = int64_t(H) * s_pad;
+  const int threads = 256;
+  dim3 grid(unsigned((warps * 32 + threads - 1) / threads), B);
+  bwd_preprocess_kernel<<<grid, threads, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(o), static_cast<const __nv_bfloat16*>(dout), o_sb, o_ss,
+      do_sb, do_ss, lse, S, H, s_pad, lse2, delta);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace mgfa

@@ -1,0 +1,43 @@
+// Parameters of the sm_100a attention backward kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cstdint>
+
+namespace mgfa {
+
+struct BwdParams {
+  int batch = 1, hq = 1, hkv = 1;
+  int sq = 0, sk = 0;
+  int n_q_tiles = 0, n_kv_tiles = 0;
+  int sq_pad = 0;                      // n_q_tiles * 128: row stride of lse2 / delta
+  float scale = 0.f;                   // softmax scale
+  float scale_log2 = 0.f;              // softmax scale * log2(e)
+  int causal = 0;
+  const int* q_tile_pos = nullptr;     // [n_q_tiles]
+  const int* kv_tile_pos = nullptr;    // [n_kv_tiles]
+  const float* lse2 = nullptr;         // [B, Hq, sq_pad] LSE in log2 units
+  const float* delta = nullptr;        // [B, Hq, sq_pad] rowsum(dO * O)
+  // fp32 gradient outputs, [B, S, H, 128]; accumulate adds into what is there
+  float* dq = nullptr;
+  float* dk = nullptr;
+  float* dv = nullptr;
+  int64_t dq_batch_stride = 0, dq_row_stride = 0;
+  int64_t dkv_batch_stride = 0, dkv_row_stride = 0;
+  int accumulate = 0;
+  uint32_t* status = nullptr;
+  uint64_t wait_limit_ns = 2000000000ull;
+};
+
+CUtensorMap make_bshd_map(const void* base, int64_t B, int64_t S, int64_t H,
+                          int64_t stride_b, int64_t stride_s, int64_t stride_h);
+void flash_bwd_dq_launch(const CUtensorMap& mq, const CUtensorMap& mdo, const CUtensorMap& mk,
+                         const CUtensorMap& mv, BwdParams& p, cudaStream_t stream);
+void flash_bwd_dkdv_launch(const CUtensorMap& mq, const CUtensorMap& mdo, const CUtensorMap& mk,
+                           const CUtensorMap& mv, BwdParams& p, cudaStream_t stream);
+// delta[b,h,i] = sum_d dO*O, lse2 = lse * log2(e); padded rows get lse2 = +inf.
+void flash_bwd_preprocess_launch(const void* o, const void* dout, int64_t o_sb, int64_t o_ss,
+                                 int64_t do_sb, int64_t do_ss, const float* lse, int B, int S,
+                                 int H, int s_pad, float* lse2, float* delta, cudaStream_t stream);
+
+}  // namespace mgfa

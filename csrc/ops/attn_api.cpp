@@ -108,3 +108,109 @@ void flash_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, c10::optional<
 }
 
 }  // namespace mgfa
+
+// ---------------------------------------------------------------------- backward
+#include "../kernels/flash_bwd_sm100.cuh"
+
+namespace mgfa {
+
+// Gradients of one attention pass (fp32 accumulators, [B,S,H,128]).
+//   dout, out: [B,Sq,Hq,128] bf16; lse [B,Hq,Sq] fp32 (of the FULL attention).
+//   With accumulate the results are added to dq / dk / dv.
+//   lse2 / delta: optional precomputed [B,Hq,ceil(Sq/128)*128] fp32 buffers
+//   (flash_bwd_preprocess); computed here when absent.
+void flash_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
+               torch::Tensor out, torch::Tensor lse, torch::Tensor dq, torch::Tensor dk,
+               torch::Tensor dv, double scale, bool causal,
+               c10::optional<torch::Tensor> q_tile_pos, c10::optional<torch::Tensor> kv_tile_pos,
+               bool accumulate, c10::optional<torch::Tensor> lse2_in,
+               c10::optional<torch::Tensor> delta_in, torch::Tensor status,
+               int64_t wait_limit_ns) {
+  check_bshd(q, "q");
+  check_bshd(k, "k");
+  check_bshd(v, "v");
+  check_bshd(dout, "dout");
+  check_bshd(out, "out");
+  TORCH_CHECK(dout.sizes() == q.sizes() && out.sizes() == q.sizes(), "dout/out must match q");
+  TORCH_CHECK(k.sizes() == v.sizes() && k.strides() == v.strides(), "k and v must match");
+  const int B = int(q.size(0)), Sq = int(q.size(1)), Hq = int(q.size(2));
+  const int Sk = int(k.size(1)), Hkv = int(k.size(2));
+  TORCH_CHECK(Hq % Hkv == 0, "query heads must be a multiple of kv heads");
+  for (auto* t : {&dq, &dk, &dv})
+    TORCH_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous() && t->dim() == 4,
+                "gradient buffers must be contiguous fp32");
+  TORCH_CHECK(dq.sizes() == q.sizes() && dk.sizes() == k.sizes() && dv.sizes() == v.sizes(),
+              "gradient buffers must match their inputs");
+  c10::cuda::CUDAGuard guard(q.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int n_q_tiles = (Sq + 127) / 128, sq_pad = n_q_tiles * 128;
+  torch::Tensor lse2, delta;
+  if (lse2_in.has_value() && delta_in.has_value()) {
+    lse2 = *lse2_in;
+    delta = *delta_in;
+    TORCH_CHECK(lse2.numel() == int64_t(B) * Hq * sq_pad && delta.numel() == lse2.numel(),
+                "lse2/delta must be [B, Hq, ceil(Sq/128)*128]");
+  } else {
+    lse2 = torch::empty({B, Hq, sq_pad}, q.options().dtype(at::kFloat));
+    delta = torch::empty({B, Hq, sq_pad}, q.options().dtype(at::kFloat));
+    flash_bwd_preprocess_launch(out.data_ptr(), dout.data_ptr(), out.stride(0), out.stride(1),
+                                dout.stride(0), dout.stride(1), lse.data_ptr<float>(), B, Sq, Hq,
+                                sq_pad, lse2.data_ptr<float>(), delta.data_ptr<float>(), stream);
+  }
+  BwdParams p;
+  p.batch = B;
+  p.hq = Hq;
+  p.hkv = Hkv;
+  p.sq = Sq;
+  p.sk = Sk;
+  p.n_q_tiles = n_q_tiles;
+  p.n_kv_tiles = (Sk + 127) / 128;
+  p.sq_pad = sq_pad;
+  p.scale = float(scale);
+  p.scale_log2 = float(scale * 1.4426950408889634);
+  p.causal = causal ? 1 : 0;
+  if (causal) {
+    p.q_tile_pos = tile_pos_ptr(q_tile_pos, p.n_q_tiles, "q_tile_pos");
+    p.kv_tile_pos = tile_pos_ptr(kv_tile_pos, p.n_kv_tiles, "kv_tile_pos");
+  }
+  p.lse2 = lse2.data_ptr<float>();
+  p.delta = delta.data_ptr<float>();
+  p.dq = dq.data_ptr<float>();
+  p.dk = dk.data_ptr<float>();
+  p.dv = dv.data_ptr<float>();
+  p.dq_batch_stride = dq.stride(0);
+  p.dq_row_stride = dq.stride(1);
+  p.dkv_batch_stride = dk.stride(0);
+  p.dkv_row_stride = dk.stride(1);
+  p.accumulate = accumulate ? 1 : 0;
+  p.status = reinterpret_cast<uint32_t*>(status.data_ptr<int>());
+  p.wait_limit_ns = uint64_t(wait_limit_ns);
+  if (B == 0 || Sq == 0 || Sk == 0) return;
+  auto map = [](const torch::Tensor& t) {
+    return make_bshd_map(t.data_ptr(), t.size(0), t.size(1), t.size(2), t.stride(0), t.stride(1),
+                         t.stride(2));
+  };
+  const CUtensorMap mq = map(q), mdo = map(dout), mk = map(k), mv = map(v);
+  flash_bwd_dkdv_launch(mq, mdo, mk, mv, p, stream);
+  flash_bwd_dq_launch(mq, mdo, mk, mv, p, stream);
+}
+
+// lse2 = lse * log2(e) (+inf for rows without keys), delta = rowsum(dout * out), both
+// [B, Hq, ceil(Sq/128)*128].
+std::vector<torch::Tensor> flash_bwd_preprocess(torch::Tensor dout, torch::Tensor out,
+                                                torch::Tensor lse) {
+  check_bshd(dout, "dout");
+  check_bshd(out, "out");
+  const int B = int(out.size(0)), Sq = int(out.size(1)), Hq = int(out.size(2));
+  const int sq_pad = (Sq + 127) / 128 * 128;
+  c10::cuda::CUDAGuard guard(out.device());
+  auto lse2 = torch::empty({B, Hq, sq_pad}, out.options().dtype(at::kFloat));
+  auto delta = torch::empty({B, Hq, sq_pad}, out.options().dtype(at::kFloat));
+  flash_bwd_preprocess_launch(out.data_ptr(), dout.data_ptr(), out.stride(0), out.stride(1),
+                              dout.stride(0), dout.stride(1), lse.data_ptr<float>(), B, Sq, Hq,
+                              sq_pad, lse2.data_ptr<float>(), delta.data_ptr<float>(),
+                              at::cuda::getCurrentCUDAStream());
+  return {lse2, delta};
+}
+
+}  // namespace mgfa

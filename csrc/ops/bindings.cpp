@@ -16,6 +16,14 @@ void legacy_merge(torch::Tensor m_run, torch::Tensor l_run, torch::Tensor acc_ru
 void legacy_normalize(torch::Tensor acc, torch::Tensor l, torch::Tensor out,
                       c10::optional<torch::Tensor> lse, c10::optional<torch::Tensor> m);
 void register_ring_engine(py::module& m);
+void flash_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
+               torch::Tensor out, torch::Tensor lse, torch::Tensor dq, torch::Tensor dk,
+               torch::Tensor dv, double scale, bool causal,
+               c10::optional<torch::Tensor> q_tile_pos, c10::optional<torch::Tensor> kv_tile_pos,
+               bool accumulate, c10::optional<torch::Tensor> lse2_in,
+               c10::optional<torch::Tensor> delta_in, torch::Tensor status, int64_t wait_limit_ns);
+std::vector<torch::Tensor> flash_bwd_preprocess(torch::Tensor dout, torch::Tensor out,
+                                                torch::Tensor lse);
 }  // namespace mgfa
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -32,5 +40,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("legacy_merge", &mgfa::legacy_merge);
   m.def("legacy_normalize", &mgfa::legacy_normalize, py::arg("acc"), py::arg("l"),
         py::arg("out"), py::arg("lse") = py::none(), py::arg("m") = py::none());
+  m.def("flash_bwd", &mgfa::flash_bwd, py::arg("dout"), py::arg("q"), py::arg("k"),
+        py::arg("v"), py::arg("out"), py::arg("lse"), py::arg("dq"), py::arg("dk"), py::arg("dv"),
+        py::arg("scale"), py::arg("causal"), py::arg("q_tile_pos"), py::arg("kv_tile_pos"),
+        py::arg("accumulate"), py::arg("lse2") = py::none(), py::arg("delta") = py::none(),
+        py::arg("status"), py::arg("wait_limit_ns") = int64_t(2000000000));
+  m.def("flash_bwd_preprocess", &mgfa::flash_bwd_preprocess);
   mgfa::register_ring_engine(m);
 }

@@ -49,6 +49,7 @@ if which in ("all", "cuda"):
                 "csrc/ops/attn_api.cpp",
                 "csrc/kernels/umma_probe.cu",
                 "csrc/kernels/flash_fwd_sm100.cu",
+                "csrc/kernels/flash_bwd_sm100.cu",
                 "csrc/kernels/legacy_fp32.cu",
                 "csrc/comm/symmetric.cpp",
                 "csrc/comm/ring_engine.cpp",
