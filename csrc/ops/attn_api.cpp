@@ -137,8 +137,10 @@ void flash_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tens
   const int Sk = int(k.size(1)), Hkv = int(k.size(2));
   TORCH_CHECK(Hq % Hkv == 0, "query heads must be a multiple of kv heads");
   for (auto* t : {&dq, &dk, &dv})
-    TORCH_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous() && t->dim() == 4,
-                "gradient buffers must be contiguous fp32");
+    TORCH_CHECK(t->scalar_type() == at::kFloat && t->dim() == 4 && t->stride(3) == 1 &&
+                    t->stride(2) == 128,
+                "gradient buffers must be fp32 [B,S,H,128] with packed heads");
+  TORCH_CHECK(dk.strides() == dv.strides(), "dk and dv must share strides");
   TORCH_CHECK(dq.sizes() == q.sizes() && dk.sizes() == k.sizes() && dv.sizes() == v.sizes(),
               "gradient buffers must match their inputs");
   c10::cuda::CUDAGuard guard(q.device());

@@ -85,3 +85,51 @@ def flash_attn_fwd_step(q, k, v, o_state, lse, *, causal, softmax_scale=None, q_
     C().flash_fwd(q, k, v, out, o_state, lse, _scale(q, softmax_scale), causal, q_tile_pos,
                   kv_tile_pos, merge, final_out, st, int(wait_limit_ns))
     return st
+
+
+# ---------------------------------------------------------------------- backward
+def flash_attn_bwd(dout, q, k, v, out, lse, causal: bool = False,
+                   softmax_scale: Optional[float] = None, q_tile_pos=None, kv_tile_pos=None,
+                   dq=None, dk=None, dv=None, accumulate: bool = False, lse2=None, delta=None,
+                   status=None, wait_limit_ns: int = DEFAULT_WAIT_LIMIT_NS):
+    """Gradients of one attention pass into fp32 buffers (allocated when None).
+
+    lse is the natural-log LSE of the complete attention the output came from
+    (for ring attention: the merged LSE over all steps). Returns (dq, dk, dv) fp32."""
+    if causal:
+        if q_tile_pos is None:
+            q_tile_pos = tile_positions(q.shape[1], q.device)
+        if kv_tile_pos is None:
+            kv_tile_pos = tile_positions(k.shape[1], q.device)
+    f32 = dict(dtype=torch.float32, device=q.device)
+    dq = dq if dq is not None else torch.empty(q.shape, **f32)
+    dk = dk if dk is not None else torch.empty(k.shape, **f32)
+    dv = dv if dv is not None else torch.empty(v.shape, **f32)
+    st = status if status is not None else torch.zeros(1, dtype=torch.int32, device=q.device)
+    C().flash_bwd(dout.contiguous(), q, k, v, out, lse, dq, dk, dv, _scale(q, softmax_scale),
+                  causal, q_tile_pos, kv_tile_pos, accumulate, lse2, delta, st, int(wait_limit_ns))
+    return dq, dk, dv
+
+
+class _FlashAttnFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, causal, softmax_scale):
+        out, lse = flash_attn_fwd(q, k, v, causal=causal, softmax_scale=softmax_scale)
+        ctx.save_for_backward(q, k, v, out, lse)
+        ctx.cfg = (causal, softmax_scale)
+        return out, lse
+
+    @staticmethod
+    def backward(ctx, d_out, d_lse):
+        q, k, v, out, lse = ctx.saved_tensors
+        causal, scale = ctx.cfg
+        dq, dk, dv = flash_attn_bwd(d_out, q, k, v, out, lse, causal=causal, softmax_scale=scale)
+        return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), None, None
+
+
+def flash_attn(q, k, v, causal: bool = False, softmax_scale: Optional[float] = None,
+               return_lse: bool = False):
+    """Differentiable single-GPU attention on the sm_100a kernels.
+    q [B,S,Hq,128], k/v [B,S,Hkv,128] bf16 -> out [B,S,Hq,128] bf16."""
+    out, lse = _FlashAttnFn.apply(q, k, v, causal, softmax_scale)
+    return (out, lse) if return_lse else out

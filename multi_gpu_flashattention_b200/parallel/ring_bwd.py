@@ -1,0 +1,140 @@
+"""Ring attention backward.
+
+Each rank keeps its queries, output, dO and the merged LSE of the forward; the
+KV shards travel around the ring again, this time together with fp32
+accumulators for their dK and dV. At step t rank r adds its contribution to
+owner (r - t) mod P's accumulators and passes shard + accumulators on; after
+P steps each accumulator holds every rank's contribution and takes one last
+hop to its owner. dQ accumulates locally.
+
+Backends: "nccl" (and "fused", which currently shares the NCCL transport for
+the backward) move the payload with NCCL send/recv on a side stream overlapped
+with the sm_100a kernels; "torch" is the fp32 PyTorch oracle on any device.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from .._ext import C
+from ..ops.flash import flash_attn_bwd
+from .layouts import RingLayout
+
+
+def _world(group):
+    if group is None and not dist.is_initialized():
+        return 0, 1
+    return dist.get_rank(group), dist.get_world_size(group)
+
+
+def _global(group, r):
+    return dist.get_global_rank(group, r) if group is not None else r
+
+
+def _p2p(group, sends, recvs, right, left):
+    ops = [dist.P2POp(dist.isend, t, right, group) for t in sends]
+    ops += [dist.P2POp(dist.irecv, t, left, group) for t in recvs]
+    return dist.batch_isend_irecv(ops) if ops else []
+
+
+def ring_attention_backward(dout, q, k, v, out, lse, layout: RingLayout, causal: bool = False,
+                            softmax_scale: Optional[float] = None, group=None,
+                            backend: Optional[str] = None):
+    scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    rank, world = _world(group)
+    if backend == "torch" or not q.is_cuda:
+        return _bwd_torch(dout, q, k, v, layout, causal, scale, group)
+    from .ring import _meta
+    qtp, kvtp, kv_lens = _meta(layout, rank, q.device)
+    dout = dout.contiguous()
+    if world == 1:
+        dq, dk, dv = flash_attn_bwd(dout, q, k[:, :kv_lens[0]], v[:, :kv_lens[0]], out, lse,
+                                    causal=causal, softmax_scale=scale, q_tile_pos=qtp,
+                                    kv_tile_pos=kvtp[0])
+        dk_full = torch.zeros(k.shape, dtype=torch.float32, device=q.device)
+        dv_full = torch.zeros(v.shape, dtype=torch.float32, device=q.device)
+        dk_full[:, :kv_lens[0]] = dk
+        dv_full[:, :kv_lens[0]] = dv
+        return dq.to(q.dtype), dk_full.to(k.dtype), dv_full.to(v.dtype)
+
+    right, left = _global(group, (rank + 1) % world), _global(group, (rank - 1) % world)
+    lse2, delta = C().flash_bwd_preprocess(dout, out, lse)
+    compute = torch.cuda.current_stream(q.device)
+    comm = torch.cuda.Stream(q.device)
+    f32 = dict(dtype=torch.float32, device=q.device)
+    dq = torch.empty(q.shape, **f32)
+    cur = [k.contiguous(), v.contiguous(), torch.empty(k.shape, **f32), torch.empty(v.shape, **f32)]
+    nxt = [torch.empty_like(t) for t in cur]
+    for t in range(world):
+        owner = (rank - t) % world
+        kl = kv_lens[owner]
+        # K/V of the next step can move while this step computes
+        reqs = []
+        if t < world - 1:
+            comm.wait_stream(compute)
+            with torch.cuda.stream(comm):
+                reqs = _p2p(group, cur[:2], nxt[:2], right, left)
+        flash_attn_bwd(dout, q, cur[0][:, :kl], cur[1][:, :kl], out, lse, causal=causal,
+                       softmax_scale=scale, q_tile_pos=qtp, kv_tile_pos=kvtp[owner],
+                       dq=dq, dk=cur[2][:, :kl], dv=cur[3][:, :kl], accumulate=t > 0,
+                       lse2=lse2, delta=delta)
+        if kl < k.shape[1] and t == 0:
+            cur[2][:, kl:].zero_()
+            cur[3][:, kl:].zero_()
+        # the accumulators follow once this step's contribution is in
+        comm.wait_stream(compute)
+        with torch.cuda.stream(comm):
+            for rq in reqs:
+                rq.wait()
+            if t < world - 1:
+                acc_reqs = _p2p(group, cur[2:], nxt[2:], right, left)
+            else:  # last hop: each accumulator goes home
+                home = [torch.empty_like(cur[2]), torch.empty_like(cur[3])]
+                acc_reqs = _p2p(group, cur[2:], home, right, left)
+            for rq in acc_reqs:
+                rq.wait()
+        compute.wait_stream(comm)
+        if t < world - 1:
+            cur, nxt = nxt, cur
+    return dq.to(q.dtype), home[0].to(k.dtype), home[1].to(v.dtype)
+
+
+def _bwd_torch(dout, q, k, v, layout, causal, scale, group):
+    """fp32 oracle: gradients of the ring forward computed with autograd on
+    all-gathered keys/values (exact, for tests)."""
+    rank, world = _world(group)
+    from ..ops.reference import attention_ref
+    ks = [torch.empty_like(k) for _ in range(world)]
+    vs = [torch.empty_like(v) for _ in range(world)]
+    if world > 1:
+        dist.all_gather(ks, k.contiguous(), group=group)
+        dist.all_gather(vs, v.contiguous(), group=group)
+    else:
+        ks, vs = [k], [v]
+    kv_lens = layout.kv_lens()
+    kfull = torch.cat([ks[o][:, :kv_lens[o]] for o in range(world)], 1).float().requires_grad_()
+    vfull = torch.cat([vs[o][:, :kv_lens[o]] for o in range(world)], 1).float().requires_grad_()
+    qf = q.float().requires_grad_()
+    q_pos = layout.q_positions_for_mask(rank).to(q.device)
+    k_pos = torch.cat([layout.k_positions_for_mask(rank, o)[:kv_lens[o]] for o in range(world)])
+    o_ref, _ = attention_ref(qf, kfull, vfull, causal=causal, softmax_scale=scale, q_pos=q_pos,
+                             k_pos=k_pos.to(q.device))
+    dq, dkf, dvf = torch.autograd.grad(o_ref, (qf, kfull, vfull), dout.float())
+    # gradients of every owner's keys: sum over ranks, then keep ours
+    offs = [0]
+    for o in range(world):
+        offs.append(offs[-1] + kv_lens[o])
+    dk_parts = [torch.zeros(k.shape, dtype=torch.float32, device=q.device) for _ in range(world)]
+    dv_parts = [torch.zeros(v.shape, dtype=torch.float32, device=q.device) for _ in range(world)]
+    for o in range(world):
+        dk_parts[o][:, :kv_lens[o]] = dkf[:, offs[o]:offs[o + 1]]
+        dv_parts[o][:, :kv_lens[o]] = dvf[:, offs[o]:offs[o + 1]]
+    dk_all = torch.stack(dk_parts)
+    dv_all = torch.stack(dv_parts)
+    if world > 1:
+        dist.all_reduce(dk_all, group=group)
+        dist.all_reduce(dv_all, group=group)
+    return dq.to(q.dtype), dk_all[rank].to(k.dtype), dv_all[rank].to(v.dtype)
