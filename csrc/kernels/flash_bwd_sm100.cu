@@ -631,3 +631,41 @@ void flash_bwd_preprocess_launch(const void* o, const void* dout, int64_t o_sb, 
 }
 
 }  // namespace mgfa
+
+// ---------------------------------------------------------------------- no-throw launchers
+// Used by the allocation-free C entry point (attn_bwd_noalloc.cu); they report
+// errors through the return value instead of exceptions.
+namespace mgfa {
+
+cudaError_t flash_bwd_preprocess_raw(const void* o, const void* dout, int64_t o_sb, int64_t o_ss,
+                                     int64_t do_sb, int64_t do_ss, const float* lse, int B, int S,
+                                     int H, int s_pad, float* lse2, float* delta,
+                                     cudaStream_t stream) {
+  const int64_t warps = int64_t(H) * s_pad;
+  const int threads = 256;
+  dim3 grid(unsigned((warps * 32 + threads - 1) / threads), B);
+  bwd_preprocess_kernel<<<grid, threads, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(o), static_cast<const __nv_bfloat16*>(dout), o_sb, o_ss,
+      do_sb, do_ss, lse, S, H, s_pad, lse2, delta);
+  return cudaGetLastError();
+}
+
+cudaError_t flash_bwd_kernels_raw(const CUtensorMap& mq, const CUtensorMap& mdo,
+                                  const CUtensorMap& mk, const CUtensorMap& mv,
+                                  const BwdParams& p, cudaStream_t stream) {
+  cudaError_t e = cudaFuncSetAttribute(flash_bwd_dkdv_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(sizeof(DkvSmem) + 1024));
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(flash_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           int(sizeof(DqSmem) + 1024));
+  if (e != cudaSuccess) return e;
+  flash_bwd_dkdv_kernel<<<dim3(p.hkv, p.n_kv_tiles, p.batch), kThreads, sizeof(DkvSmem) + 1024,
+                          stream>>>(mq, mdo, mk, mv, p);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  flash_bwd_dq_kernel<<<dim3(p.hq, p.n_q_tiles, p.batch), kThreads, sizeof(DqSmem) + 1024,
+                        stream>>>(mq, mdo, mk, mv, p);
+  return cudaGetLastError();
+}
+
+}  // namespace mgfa

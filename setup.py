@@ -50,6 +50,7 @@ if which in ("all", "cuda"):
                 "csrc/kernels/umma_probe.cu",
                 "csrc/kernels/flash_fwd_sm100.cu",
                 "csrc/kernels/flash_bwd_sm100.cu",
+                "csrc/kernels/attn_bwd_noalloc.cu",
                 "csrc/kernels/legacy_fp32.cu",
                 "csrc/comm/symmetric.cpp",
                 "csrc/comm/ring_engine.cpp",
