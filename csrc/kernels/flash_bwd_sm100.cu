@@ -114,7 +114,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   DqSmem& s = *reinterpret_cast<DqSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                          ~uintptr_t(1023));
   const uint32_t warp = warp_id(), lane = lane_id();
-  const int h = blockIdx.x, qt = gridDim.y - 1 - blockIdx.y, b = blockIdx.z;
+  // query tiles vary fastest: resident CTAs share one head's K/V in L2
+  const int qt = gridDim.x - 1 - blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int hk = h / (p.hq / p.hkv);
   int n_active = 0;
   for (int j = 0; j < p.n_kv_tiles; ++j) n_active += dq_tile_active(p, qt, j) ? 1 : 0;
@@ -340,7 +341,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   DkvSmem& s = *reinterpret_cast<DkvSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~uintptr_t(1023));
   const uint32_t warp = warp_id(), lane = lane_id();
-  const int hk = blockIdx.x, j = gridDim.y - 1 - blockIdx.y, b = blockIdx.z;
+  // key tiles vary fastest: resident CTAs share the group's Q/dO stream in L2
+  const int j = gridDim.x - 1 - blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
   const int G = p.hq / p.hkv;
   int n_q_active = 0;
   for (int qt = 0; qt < p.n_q_tiles; ++qt) n_q_active += kv_sees(p, j, qt) ? 1 : 0;
@@ -603,7 +605,7 @@ void flash_bwd_dq_launch(const CUtensorMap& mq, const CUtensorMap& mdo, const CU
                          const CUtensorMap& mv, BwdParams& p, cudaStream_t stream) {
   static int done_dev = -1;
   set_smem<DqSmem>(flash_bwd_dq_kernel, done_dev);
-  dim3 grid(p.hq, p.n_q_tiles, p.batch);
+  dim3 grid(p.n_q_tiles, p.hq, p.batch);
   flash_bwd_dq_kernel<<<grid, kThreads, sizeof(DqSmem) + 1024, stream>>>(mq, mdo, mk, mv, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -612,7 +614,7 @@ void flash_bwd_dkdv_launch(const CUtensorMap& mq, const CUtensorMap& mdo, const 
                            const CUtensorMap& mv, BwdParams& p, cudaStream_t stream) {
   static int done_dev = -1;
   set_smem<DkvSmem>(flash_bwd_dkdv_kernel, done_dev);
-  dim3 grid(p.hkv, p.n_kv_tiles, p.batch);
+  dim3 grid(p.n_kv_tiles, p.hkv, p.batch);
   flash_bwd_dkdv_kernel<<<grid, kThreads, sizeof(DkvSmem) + 1024, stream>>>(mq, mdo, mk, mv, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -660,10 +662,10 @@ cudaError_t flash_bwd_kernels_raw(const CUtensorMap& mq, const CUtensorMap& mdo,
   e = cudaFuncSetAttribute(flash_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            int(sizeof(DqSmem) + 1024));
   if (e != cudaSuccess) return e;
-  flash_bwd_dkdv_kernel<<<dim3(p.hkv, p.n_kv_tiles, p.batch), kThreads, sizeof(DkvSmem) + 1024,
+  flash_bwd_dkdv_kernel<<<dim3(p.n_kv_tiles, p.hkv, p.batch), kThreads, sizeof(DkvSmem) + 1024,
                           stream>>>(mq, mdo, mk, mv, p);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  flash_bwd_dq_kernel<<<dim3(p.hq, p.n_q_tiles, p.batch), kThreads, sizeof(DqSmem) + 1024,
+  flash_bwd_dq_kernel<<<dim3(p.n_q_tiles, p.hq, p.batch), kThreads, sizeof(DqSmem) + 1024,
                         stream>>>(mq, mdo, mk, mv, p);
   return cudaGetLastError();
 }

@@ -25,6 +25,7 @@
 #include <ATen/cuda/CUDAContext.h>
 
 #include <cmath>
+#include <cstdlib>
 
 #include "flash_fwd_sm100.cuh"
 #include "sm100_ptx.cuh"
@@ -57,22 +58,28 @@ struct __align__(1024) FwdSmem {
   uint32_t abort_flag;
 };
 
-__device__ __forceinline__ bool q_tile_sees(const FwdParams& p, int qt, int kv_pos) {
-  if (qt >= p.n_q_tiles) return false;
-  return kv_pos <= p.q_tile_pos[qt] + (kTile - 1);
-}
-
-__device__ __forceinline__ bool tile_active(const FwdParams& p, int qt0, int j) {
-  if (!p.causal) return true;
-  const int kv_pos = p.kv_tile_pos[j];
-  return q_tile_sees(p, qt0, kv_pos) || q_tile_sees(p, qt0 + 1, kv_pos);
-}
-
-__device__ __forceinline__ int count_active(const FwdParams& p, int qt0) {
-  if (!p.causal) return p.n_kv_tiles;
-  int n = 0;
-  for (int j = 0; j < p.n_kv_tiles; ++j) n += tile_active(p, qt0, j) ? 1 : 0;
-  return n;
+// Number of leading entries of the non-decreasing `pos[0..n)` that are <= `limit`
+// (every shard layout lists its key tiles in increasing global position, so the
+// key tiles a query tile can see form a prefix). Warp-cooperative; every lane
+// returns the result.
+__device__ __forceinline__ int visible_prefix(const int* pos, int n, int limit) {
+  const uint32_t lane = lane_id();
+  int lo = 0, hi = n;  // answer in [lo, hi]
+  while (hi - lo > 0) {
+    const int span = hi - lo;
+    const int step = (span + 31) / 32;
+    const int idx = lo + int(lane) * step;
+    const bool le = idx < hi && __ldg(pos + idx) <= limit;
+    const uint32_t m = __ballot_sync(0xffffffffu, le);
+    const int cnt = __popc(m);  // probes [0, cnt) are <= limit
+    if (cnt == 0) return lo;    // pos[lo] > limit
+    if (step == 1) return lo + cnt;
+    const int new_lo = lo + (cnt - 1) * step + 1;
+    const int new_hi = lo + cnt * step < hi ? lo + cnt * step : hi;
+    lo = new_lo;
+    hi = new_hi;
+  }
+  return lo;
 }
 
 // ------------------------------------------------------------------ ring push
@@ -127,6 +134,10 @@ __device__ void ring_push_warp(const RingPush& rp, const RingConsume& rc, uint32
 }
 
 // ------------------------------------------------------------------ kernel
+// kF2: packed f32x2 arithmetic in the softmax; kPolyStart: first bf16 pair index
+// (of 64 per row) whose exponentials run on the FMA pipe in unmasked tiles
+// (64 = none).
+template <bool kF2, int kPolyStart>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap map_q,
                      const __grid_constant__ CUtensorMap map_k,
@@ -136,13 +147,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
   const uint32_t warp = warp_id(), lane = lane_id();
-  const int h = blockIdx.x;                 // query head
-  const int pair = gridDim.y - 1 - blockIdx.y;  // heaviest query tiles first (causal)
+  // Query-tile pairs vary fastest so that the CTAs resident at one time work on
+  // the same head and share its K/V stream in L2; heaviest pairs first (causal).
+  const int pair = gridDim.x - 1 - blockIdx.x;
+  const int h = blockIdx.y;                 // query head
   const int b = blockIdx.z;
   const int hk = h / (p.hq / p.hkv);
   const int qt0 = 2 * pair;
 
-  const int n_active = count_active(p, qt0);
+  // Key tiles [0, n_active) are visible to at least one of the CTA's query tiles;
+  // tiles [0, full_hi[t]) are fully visible to query tile t (no mask needed).
+  const bool has_q1 = qt0 + 1 < p.n_q_tiles;
+  const int q_pos0 = p.causal ? __ldg(p.q_tile_pos + qt0) : 0;
+  const int q_pos1 = (p.causal && has_q1) ? __ldg(p.q_tile_pos + qt0 + 1) : q_pos0;
+  const int ragged = (p.sk % kTile) != 0 ? 1 : 0;
+  int n_active = p.n_kv_tiles;
+  if (p.causal)
+    n_active = visible_prefix(p.kv_tile_pos, p.n_kv_tiles,
+                              (q_pos0 > q_pos1 ? q_pos0 : q_pos1) + (kTile - 1));
   const bool has_prior = p.merge != 0;
   // No visible key tile: the running state is already correct unless this is
   // the final step, which still has to convert it to the bf16 output.
@@ -191,8 +213,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       int it = 0;
       int last_k_phase[2] = {-1, -1}, last_v_phase[2] = {-1, -1};
-      for (int j = 0; ok && j < p.n_kv_tiles; ++j) {
-        if (!tile_active(p, qt0, j)) continue;
+      for (int j = 0; ok && j < n_active; ++j) {
         const int st = it & 1;
         const uint32_t ph = (it >> 1) & 1;
         if (!mbar_wait(&s.k_empty[st], ph ^ 1, ab, 81)) break;
@@ -295,12 +316,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;
     const uint32_t s_addr = tmem + lane_off + t * 128;
     const uint32_t o_addr = tmem + lane_off + 256 + t * 128;
-    const int q_pos = (p.causal && qt < p.n_q_tiles) ? p.q_tile_pos[qt] + r : 0;
+    const bool q_valid_tile = qt < p.n_q_tiles;
+    const int q_tile_pos = t == 0 ? q_pos0 : q_pos1;
+    const int q_pos = q_tile_pos + r;
+    // key tiles [0, full_hi) need no mask for this query tile
+    int full_hi = p.n_kv_tiles - ragged;
+    if (p.causal) {
+      const int f = visible_prefix(p.kv_tile_pos, n_active, q_tile_pos - (kTile - 1));
+      full_hi = f < full_hi ? f : full_hi;
+    }
+    if (!q_valid_tile) full_hi = 0;
+    const uint64_t scale2 = f2_pack(p.scale_log2, p.scale_log2);
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    int it = 0;
-    for (int j = 0; !skip_compute && j < p.n_kv_tiles; ++j) {
-      if (!tile_active(p, qt0, j)) continue;
+    for (int it = 0; !skip_compute && it < n_active; ++it) {
       ok = __all_sync(0xffffffffu, mbar_wait(&s.s_full[t], it & 1, ab, 20 + t));
       if (!ok) break;
       tc_fence_after();
@@ -309,21 +338,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
       tmem_ld32(s_addr + 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
       tmem_ld32(s_addr + 96, *reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
+      const bool full = it < full_hi;  // warp-uniform
+      int n_vis = 128;
+      if (!full) {  // diagonal / ragged / invisible tile: count this row's visible keys
+        n_vis = p.sk - it * kTile;
+        if (p.causal) {
+          const int lim = q_pos - __ldg(p.kv_tile_pos + it) + 1;
+          n_vis = lim < n_vis ? lim : n_vis;
+        }
+        if (!q_valid_tile) n_vis = 0;
+      }
       tmem_wait_ld();
-      // Number of leading keys of this tile visible to this row.
-      int n_vis = p.sk - j * kTile;
-      if (p.causal) {
-        const int lim = q_pos - p.kv_tile_pos[j] + 1;
-        n_vis = lim < n_vis ? lim : n_vis;
-        if (qt >= p.n_q_tiles) n_vis = 0;
-      }
-      float x[128];
-      float tmax = -INFINITY;
+      if (!full) {
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        x[c] = (c < n_vis) ? __uint_as_float(sr[c]) * p.scale_log2 : -INFINITY;
-        tmax = fmaxf(tmax, x[c]);
+        for (int c = 0; c < 128; ++c)
+          if (c >= n_vis) sr[c] = 0xff800000u;  // -inf
       }
+      // row max of the raw scores (scale > 0 commutes with max)
+      float mx0 = __uint_as_float(sr[0]), mx1 = __uint_as_float(sr[1]);
+      float mx2 = __uint_as_float(sr[2]), mx3 = __uint_as_float(sr[3]);
+#pragma unroll
+      for (int c = 4; c < 128; c += 8) {
+        mx0 = max3f(mx0, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+        mx1 = max3f(mx1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
+        mx2 = max3f(mx2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
+        mx3 = max3f(mx3, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
+      }
+      const float tmax = fmaxf(max3f(mx0, mx1, mx2), mx3) * p.scale_log2;
       const float m_new = fmaxf(m, tmax);
       float alpha = 1.f;
       bool rescale = false;
@@ -336,18 +377,56 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float m_use = (m == -INFINITY) ? 0.f : m;
       l *= alpha;
-      uint32_t pk[64];
-      float psum = 0.f;
+      if constexpr (kF2) {
+        const uint64_t neg_m = f2_pack(-m_use, -m_use);
+        uint64_t acc0 = 0, acc1 = 0;  // packed partial row sums (0.0f, 0.0f)
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float p0 = ex2_approx(x[2 * c] - m_use);
-        const float p1 = ex2_approx(x[2 * c + 1] - m_use);
-        psum += p0 + p1;
-        pk[c] = pack_bf16(p0, p1);
+        for (int half = 0; half < 2; ++half) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int cc = 0; cc < 32; ++cc) {
+            const int c = half * 32 + cc;
+            const uint64_t x2 =
+                f2_fma(f2_pack(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])),
+                       scale2, neg_m);
+            uint64_t p2;
+            if (full && c >= kPolyStart) {
+              p2 = exp2_poly2(x2);  // exponentials on the FMA pipe
+            } else {
+              float x0, x1;
+              f2_unpack(x2, x0, x1);
+              p2 = f2_pack(ex2_approx(x0), ex2_approx(x1));
+            }
+            if (c & 1) acc1 = f2_add(acc1, p2);
+            else acc0 = f2_add(acc0, p2);
+            float p0, p1;
+            f2_unpack(p2, p0, p1);
+            pk[cc] = pack_bf16(p0, p1);
+          }
+          tmem_st32(s_addr + half * 32, pk);
+        }
+        float a0, a1, b0, b1;
+        f2_unpack(acc0, a0, a1);
+        f2_unpack(acc1, b0, b1);
+        l += (a0 + a1) + (b0 + b1);
+      } else {
+        const float neg_m = -m_use;
+        float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int cc = 0; cc < 32; ++cc) {
+            const int c = half * 32 + cc;
+            const float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * c]), p.scale_log2, neg_m));
+            const float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * c + 1]), p.scale_log2, neg_m));
+            if (c & 1) { l2 += p0; l3 += p1; } else { l0 += p0; l1 += p1; }
+            pk[cc] = pack_bf16(p0, p1);
+          }
+          tmem_st32(s_addr + half * 32, pk);
+        }
+        l += (l0 + l1) + (l2 + l3);
       }
-      l += psum;
-      tmem_st32(s_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
-      tmem_st32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
       if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
         for (int ch = 0; ch < 4; ++ch) {
@@ -362,7 +441,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&s.p_full[t]);
-      ++it;
     }
     if (!skip_compute && ok) ok = __all_sync(0xffffffffu, mbar_wait(&s.o_full, 0, ab, 30 + t));
     ok = __all_sync(0xffffffffu, ok);
@@ -470,20 +548,39 @@ CUtensorMap make_bshd_map(const void* base, int64_t B, int64_t S, int64_t H, int
 
 size_t flash_fwd_smem_bytes() { return sizeof(FwdSmem) + 1024; }
 
+namespace {
+using FwdKernelFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap,
+                             const FwdParams);
+// Softmax variants: 0 scalar/MUFU, 1 f32x2/MUFU, 2 f32x2 + 1/8 on FMA, 3 f32x2 + 1/4 on FMA.
+FwdKernelFn fwd_variant(int v) {
+  switch (v) {
+    case 0: return flash_fwd_kernel<false, 64>;
+    case 1: return flash_fwd_kernel<true, 64>;
+    case 2: return flash_fwd_kernel<true, 56>;
+    default: return flash_fwd_kernel<true, 48>;
+  }
+}
+int fwd_variant_from_env() {
+  const char* e = std::getenv("MGFA_FWD_VARIANT");
+  return e ? std::atoi(e) : 0;  // measured fastest on B200: scalar math, all-MUFU
+}
+}  // namespace
+
 void flash_fwd_launch_maps(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                            FwdParams& p, cudaStream_t stream) {
-  static int attr_device = -1;
+  static const int variant = fwd_variant_from_env();
+  static int attr_device[4] = {-1, -1, -1, -1};
+  const FwdKernelFn kern = fwd_variant(variant);
   const int smem = int(flash_fwd_smem_bytes());
   int dev = 0;
   C10_CUDA_CHECK(cudaGetDevice(&dev));
-  if (attr_device != dev) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(flash_fwd_kernel,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr_device = dev;
+  if (attr_device[variant & 3] != dev) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr_device[variant & 3] = dev;
   }
   const int n_pairs = (p.n_q_tiles + 1) / 2;
-  dim3 grid(p.hq, n_pairs, p.batch);
-  flash_fwd_kernel<<<grid, kThreads, smem, stream>>>(mq, mk, mv, p);
+  dim3 grid(n_pairs, p.hq, p.batch);
+  kern<<<grid, kThreads, smem, stream>>>(mq, mk, mv, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -70,11 +70,12 @@ def test_flash_fwd_tile_positions_mask():
     """Causal mask driven by non-contiguous tile positions (zigzag-like shard)."""
     from multi_gpu_flashattention_b200.ops.flash import check_status, flash_attn_fwd
     q, k, v = _inputs(1, 256, 512, 2, 2, seed=5)
-    # query tiles live at global 640 and 128; key tiles at 0, 768, 128, 512
-    qtp = torch.tensor([640, 128], dtype=torch.int32, device="cuda")
-    ktp = torch.tensor([0, 768, 128, 512], dtype=torch.int32, device="cuda")
-    q_pos = torch.cat([torch.arange(128) + 640, torch.arange(128) + 128]).cuda()
-    k_pos = torch.cat([torch.arange(128) + t for t in (0, 768, 128, 512)]).cuda()
+    # query tiles live at global 128 and 640; key tiles at 0, 128, 512, 768
+    # (shards always list their tiles in increasing global position)
+    qtp = torch.tensor([128, 640], dtype=torch.int32, device="cuda")
+    ktp = torch.tensor([0, 128, 512, 768], dtype=torch.int32, device="cuda")
+    q_pos = torch.cat([torch.arange(128) + 128, torch.arange(128) + 640]).cuda()
+    k_pos = torch.cat([torch.arange(128) + t for t in (0, 128, 512, 768)]).cuda()
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     o, lse = flash_attn_fwd(q, k, v, causal=True, q_tile_pos=qtp, kv_tile_pos=ktp, status=status)
     check_status(status)
