@@ -1,0 +1,65 @@
+#!/usr/bin/env bash
+# Ring-attention correctness pipeline (the reference's
+# ring/attention/bench/check_attention_correctness.sh, on torchrun + this
+# framework): run backend pairs with ATTENTION_DUMP_OUTPUT=1, check every dump
+# against the full single-device reference with verify_full, and compare each
+# pair element-wise (PASS iff max_abs <= ABS_TOL or max_rel <= REL_TOL).
+#
+# Env: NP (2) SIZE (262144) WARMUP (1) ITERS (1) ABS_TOL (1e-3) REL_TOL (1e-5)
+#      RESULTS_ROOT (results) RUN_LABEL (timestamp) INIT (legacy|randn)
+set -euo pipefail
+cd "$(dirname "$0")/.."
+NP=${NP:-2}
+SIZE=${SIZE:-262144}
+WARMUP=${WARMUP:-1}
+ITERS=${ITERS:-1}
+ABS_TOL=${ABS_TOL:-1e-3}
+REL_TOL=${REL_TOL:-1e-5}
+INIT=${INIT:-legacy}
+RESULTS_ROOT=${RESULTS_ROOT:-results}
+RUN_LABEL=${RUN_LABEL:-$(date +%Y%m%d_%H%M%S)}
+OUT="$RESULTS_ROOT/$RUN_LABEL"
+PORT=${PORT:-29531}
+mkdir -p "$OUT"
+make -s build/bin/verify_full
+VERIFY_ARGS=()
+[[ "$INIT" == randn ]] && VERIFY_ARGS=(--init randn)
+
+run_bench() {  # label, extra args...
+  local label=$1; shift
+  local dir="$OUT/$label"
+  mkdir -p "$dir"
+  (cd "$dir" && ATTENTION_DUMP_OUTPUT=1 timeout -k 30 600 python -m torch.distributed.run \
+      --nnodes=1 --nproc-per-node "$NP" --master-addr 127.0.0.1 --master-port "$PORT" \
+      -m multi_gpu_flashattention_b200.benchmarks.ring_attention "$SIZE" "$WARMUP" "$ITERS" \
+      --init "$INIT" "$@" > bench.log 2>&1)
+  PORT=$((PORT + 1))
+  ./build/bin/verify_full "$dir" "$NP" "$SIZE" "${VERIFY_ARGS[@]}" | tee "$dir/verify.log" | tail -1
+}
+
+compare_pair() {  # name, dirA, dirB
+  python - "$1" "$2" "$3" "$NP" "$ABS_TOL" "$REL_TOL" <<'PY'
+import sys
+import numpy as np
+name, a, b, npr, atol, rtol = sys.argv[1], sys.argv[2], sys.argv[3], int(sys.argv[4]), float(sys.argv[5]), float(sys.argv[6])
+ok = True
+for r in range(npr):
+    x = np.fromfile(f"{a}/ring_output_rank{r}.bin", dtype="<f4")
+    y = np.fromfile(f"{b}/ring_output_rank{r}.bin", dtype="<f4")
+    if x.shape != y.shape or not (np.isfinite(x).all() and np.isfinite(y).all()):
+        ok = False
+        continue
+    d = np.abs(x.astype(np.float64) - y)
+    rel = d / np.maximum(np.maximum(np.abs(x), np.abs(y)), 1e-12)
+    ok = ok and (d.max() <= atol or rel.max() <= rtol)
+print(f"{name}: {'PASS' if ok else 'FAIL'}")
+sys.exit(0 if ok else 1)
+PY
+}
+
+run_bench nccl --backend nccl
+run_bench nccl_overlap --backend nccl --overlap
+run_bench staged --backend staged
+run_bench staged_overlap --backend staged --overlap
+compare_pair nccl_vs_overlap "$OUT/nccl" "$OUT/nccl_overlap"
+compare_pair staged_vs_overlap "$OUT/staged" "$OUT/staged_overlap"

@@ -16,6 +16,7 @@ void legacy_merge(torch::Tensor m_run, torch::Tensor l_run, torch::Tensor acc_ru
 void legacy_normalize(torch::Tensor acc, torch::Tensor l, torch::Tensor out,
                       c10::optional<torch::Tensor> lse, c10::optional<torch::Tensor> m);
 void register_ring_engine(py::module& m);
+void register_ring_exchange(py::module& m);
 void flash_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
                torch::Tensor out, torch::Tensor lse, torch::Tensor dq, torch::Tensor dk,
                torch::Tensor dv, double scale, bool causal,
@@ -47,4 +48,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("status"), py::arg("wait_limit_ns") = int64_t(2000000000));
   m.def("flash_bwd_preprocess", &mgfa::flash_bwd_preprocess);
   mgfa::register_ring_engine(m);
+  mgfa::register_ring_exchange(m);
 }

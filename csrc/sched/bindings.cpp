@@ -3,6 +3,7 @@
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
 
+#include "../common/device_select.hpp"
 #include "../common/synth.hpp"
 #include "scheduler.hpp"
 #include "shard_plan.hpp"
@@ -174,6 +175,17 @@ PYBIND11_MODULE(_sched, m) {
       py::arg("policy") = "dp", py::arg("beta") = 1.0);
   m.def("step_active", [](const ShardPlan& p, int q, int kv, const std::string& mk) {
     return step_active(p, q, kv, to_mask(mk));
+  });
+
+  // Device binding.
+  m.def("local_rank_from_env", []() {
+    std::string src;
+    const int r = mgfa::local_rank_from_env(&src);
+    return py::make_tuple(r, src);
+  });
+  m.def("choose_device", [](int device_count, int fallback_local_rank) {
+    const mgfa::DeviceChoice c = mgfa::choose_device(device_count, fallback_local_rank);
+    return py::make_tuple(c.device, c.local_rank, c.source, c.error);
   });
 
   // Synthetic inputs (fills a Python buffer-protocol object of float32).

@@ -54,6 +54,8 @@ if which in ("all", "cuda"):
                 "csrc/kernels/legacy_fp32.cu",
                 "csrc/comm/symmetric.cpp",
                 "csrc/comm/ring_engine.cpp",
+                "csrc/comm/ring_exchange.cpp",
+                "csrc/kernels/ring_exchange.cu",
             ],
             include_dirs=[os.path.join(ROOT, "csrc")],
             extra_compile_args={
