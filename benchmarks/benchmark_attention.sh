@@ -3,6 +3,7 @@
 # Env: NP (2) SIZES ("262144 524288 1048576") WARMUP (10) ITERS (100) NUMERICS (fp32|bf16)
 set -euo pipefail
 cd "$(dirname "$0")/.."
+export PYTHONPATH="$PWD${PYTHONPATH:+:$PYTHONPATH}"
 NP=${NP:-2}
 SIZES=${SIZES:-"262144 524288 1048576"}
 WARMUP=${WARMUP:-10}

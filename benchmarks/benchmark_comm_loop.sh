@@ -4,6 +4,7 @@
 #      BACKENDS ("p2p ce nccl staged") TOKENS (set to sweep the bf16 K+V payload instead)
 set -euo pipefail
 cd "$(dirname "$0")/.."
+export PYTHONPATH="$PWD${PYTHONPATH:+:$PYTHONPATH}"
 NP=${NP:-2}
 SIZES=${SIZES:-"262144 1048576 4194304 16777216"}
 WARMUP=${WARMUP:-10}

@@ -9,6 +9,7 @@
 #      RESULTS_ROOT (results) RUN_LABEL (timestamp) INIT (legacy|randn)
 set -euo pipefail
 cd "$(dirname "$0")/.."
+export PYTHONPATH="$PWD${PYTHONPATH:+:$PYTHONPATH}"
 NP=${NP:-2}
 SIZE=${SIZE:-262144}
 WARMUP=${WARMUP:-1}
