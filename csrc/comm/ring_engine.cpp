@@ -36,7 +36,7 @@ class RingEngine {
         slot_bytes_(size_t(slot_bytes)),
         n_chunks_(uint32_t(n_chunks)) {
     TORCH_CHECK(slot_bytes > 0 && slot_bytes % 4096 == 0, "slot_bytes must be a multiple of 4096");
-    TORCH_CHECK(n_chunks > 0, "n_chunks must be positive");
+    TORCH_CHECK(n_chunks >= 0, "n_chunks must be >= 0 (0 = one chunk per CTA)");
   }
 
   py::bytes ipc_handle() const { return py::bytes(buf_.ipc_handle()); }
@@ -163,12 +163,15 @@ class RingEngine {
         p.push.peer_arrivals = buf_.flag(right, sn == 0 ? comm::kArrivals0 : comm::kArrivals1);
         p.push.credit = buf_.flag(r, sn == 0 ? comm::kCredit0 : comm::kCredit1);
         p.push.credit_target = uses_[sn];
-        p.push.n_chunks = n_chunks_;
+        // one chunk per CTA: every rank launches the same grid (shards are padded
+        // to one length), so the receiver's arrival target is the same number
+        p.push.n_chunks = n_chunks_ ? n_chunks_ : uint32_t(grid);
+        p.push.drop_signal = (drop_signal_step_ == t) ? 1 : 0;
       }
       if (transport && t > 0) {
         p.consume.enabled = 1;
         p.consume.arrivals = buf_.flag(r, s == 0 ? comm::kArrivals0 : comm::kArrivals1);
-        p.consume.arrivals_target = n_chunks_;
+        p.consume.arrivals_target = n_chunks_ ? n_chunks_ : uint32_t(grid);
         p.consume.done_counter = buf_.flag(r, s == 0 ? comm::kDone0 : comm::kDone1);
         p.consume.done_target = uint32_t(grid - 1);
         p.consume.left_credit = buf_.flag(left, s == 0 ? comm::kCredit0 : comm::kCredit1);
@@ -182,6 +185,10 @@ class RingEngine {
 
  public:
 
+  // Fault injection for tests (off by default): at ring step `step` of the next
+  // forward calls, the push copies its data but skips one arrival signal.
+  void set_drop_signal_step(int step) { drop_signal_step_ = step; }
+
   // Zero local flags and use counts (collective: every rank, then a barrier).
   void reset() {
     buf_.reset_flags(at::cuda::getCurrentCUDAStream());
@@ -193,17 +200,19 @@ class RingEngine {
   size_t slot_bytes_;
   uint32_t n_chunks_;
   uint32_t uses_[2] = {0, 0};
+  int drop_signal_step_ = -1;
 };
 
 void register_ring_engine(py::module& m) {
   py::class_<RingEngine, std::shared_ptr<RingEngine>>(m, "RingEngine")
       .def(py::init<int, int, int, int64_t, int>(), py::arg("rank"), py::arg("world"),
-           py::arg("device"), py::arg("slot_bytes"), py::arg("n_chunks") = 1024)
+           py::arg("device"), py::arg("slot_bytes"), py::arg("n_chunks") = 0)
       .def("ipc_handle", &RingEngine::ipc_handle)
       .def("connect", &RingEngine::connect)
       .def("slot_bytes", &RingEngine::slot_bytes)
       .def("uses", &RingEngine::uses)
       .def("reset", &RingEngine::reset)
+      .def("set_drop_signal_step", &RingEngine::set_drop_signal_step)
       .def("forward", &RingEngine::forward, py::arg("q"), py::arg("k"), py::arg("v"),
            py::arg("scale"), py::arg("causal"), py::arg("q_tile_pos"), py::arg("kv_tile_pos"),
            py::arg("kv_lens"), py::arg("status"), py::arg("wait_limit_ns"))

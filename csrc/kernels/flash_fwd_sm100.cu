@@ -104,11 +104,11 @@ __device__ void ring_push_warp(const RingPush& rp, const RingConsume& rc, uint32
   for (uint32_t c = linear_cta; c < rp.n_chunks; c += n_ctas) {
     const uint64_t b = uint64_t(c) * chunk;
     const uint64_t e = b + chunk < total ? b + chunk : total;
-    // Copy [b, e) of the virtual concatenation K | V, 16 bytes per lane, 4 in flight.
-    for (uint64_t off = b + uint64_t(lane) * 16; off < e; off += 32 * 16 * 4) {
-      uint4 r[4];
+    // Copy [b, e) of the virtual concatenation K | V, 16 bytes per lane, 8 in flight.
+    for (uint64_t off = b + uint64_t(lane) * 16; off < e; off += 32 * 16 * 8) {
+      uint4 r[8];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < 8; ++u) {
         const uint64_t o = off + uint64_t(u) * 32 * 16;
         if (o < e) {
           const uint8_t* src = o < rp.bytes ? rp.src_k + o : rp.src_v + (o - rp.bytes);
@@ -117,7 +117,7 @@ __device__ void ring_push_warp(const RingPush& rp, const RingConsume& rc, uint32
         }
       }
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < 8; ++u) {
         const uint64_t o = off + uint64_t(u) * 32 * 16;
         if (o < e) {
           uint8_t* dst = o < rp.bytes ? rp.dst_k + o : rp.dst_v + (o - rp.bytes);
@@ -126,7 +126,7 @@ __device__ void ring_push_warp(const RingPush& rp, const RingConsume& rc, uint32
       }
     }
     __syncwarp();
-    if (lane == 0) {
+    if (lane == 0 && !(rp.drop_signal && c == 0)) {
       fence_sys();
       red_release_sys_add(rp.peer_arrivals, 1u);
     }

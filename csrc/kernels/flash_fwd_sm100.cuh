@@ -22,6 +22,8 @@ struct RingPush {
   uint32_t credit_target = 0;         // wait until *credit >= credit_target before writing
   uint32_t n_chunks = 0;              // chunks the shard is cut into (same on every rank)
   int enabled = 0;
+  int drop_signal = 0;                // fault injection for tests: chunk 0 is copied but
+                                      // never signalled, so the receiver's wait must expire
 };
 
 // Consumer side of one ring step.

@@ -216,3 +216,48 @@ std::vector<torch::Tensor> flash_bwd_preprocess(torch::Tensor dout, torch::Tenso
 }
 
 }  // namespace mgfa
+
+namespace mgfa {
+
+// Failure-path check: one forward launch whose KV "arrival" flag is a local word
+// that nothing ever sets. The producer's bounded wait must expire after
+// wait_limit_ns, record kErrPeerTimeout in the status word and end the kernel
+// cleanly (no hang, no fault). Returns the status word (int32 CUDA tensor).
+torch::Tensor fwd_timeout_probe(torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                int64_t wait_limit_ns) {
+  check_bshd(q, "q");
+  check_bshd(k, "k");
+  check_bshd(v, "v");
+  c10::cuda::CUDAGuard guard(q.device());
+  auto flags = torch::zeros({64}, q.options().dtype(at::kInt));
+  auto status = torch::zeros({1}, q.options().dtype(at::kInt));
+  auto o = torch::empty_like(q);
+  auto lse = torch::empty({q.size(0), q.size(2), q.size(1)}, q.options().dtype(at::kFloat));
+  FwdParams p;
+  p.batch = int(q.size(0));
+  p.hq = int(q.size(2));
+  p.hkv = int(k.size(2));
+  p.sq = int(q.size(1));
+  p.sk = int(k.size(1));
+  p.n_q_tiles = (p.sq + 127) / 128;
+  p.n_kv_tiles = (p.sk + 127) / 128;
+  p.scale_log2 = 0.1f;
+  p.o = o.data_ptr();
+  p.lse = lse.data_ptr<float>();
+  p.o_batch_stride = q.stride(0);
+  p.o_row_stride = q.stride(1);
+  p.status = reinterpret_cast<uint32_t*>(status.data_ptr<int>());
+  p.wait_limit_ns = uint64_t(wait_limit_ns);
+  uint32_t* f = reinterpret_cast<uint32_t*>(flags.data_ptr<int>());
+  p.consume.enabled = 1;
+  p.consume.arrivals = f;            // never incremented
+  p.consume.arrivals_target = 1;
+  p.consume.done_counter = f + 16;
+  p.consume.done_target = uint32_t((p.n_q_tiles + 1) / 2 * p.hq * p.batch - 1);
+  p.consume.left_credit = f + 32;
+  p.consume.left_credit_value = 1;
+  flash_fwd_launch(q, k, v, p, at::cuda::getCurrentCUDAStream());
+  return status;
+}
+
+}  // namespace mgfa

@@ -17,6 +17,8 @@ void legacy_normalize(torch::Tensor acc, torch::Tensor l, torch::Tensor out,
                       c10::optional<torch::Tensor> lse, c10::optional<torch::Tensor> m);
 void register_ring_engine(py::module& m);
 void register_ring_exchange(py::module& m);
+torch::Tensor fwd_timeout_probe(torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                int64_t wait_limit_ns);
 void flash_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
                torch::Tensor out, torch::Tensor lse, torch::Tensor dq, torch::Tensor dk,
                torch::Tensor dv, double scale, bool causal,
@@ -47,6 +49,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("accumulate"), py::arg("lse2") = py::none(), py::arg("delta") = py::none(),
         py::arg("status"), py::arg("wait_limit_ns") = int64_t(2000000000));
   m.def("flash_bwd_preprocess", &mgfa::flash_bwd_preprocess);
+  m.def("fwd_timeout_probe", &mgfa::fwd_timeout_probe,
+        "forward launch whose arrival flag is never set (bounded-wait failure path)");
   mgfa::register_ring_engine(m);
   mgfa::register_ring_exchange(m);
 }

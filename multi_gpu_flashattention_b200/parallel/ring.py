@@ -69,7 +69,7 @@ class _Engines:
             dist.barrier(group)  # every rank is past its last use of the old slots
             self._by_key.pop(key)
             del eng
-        eng = C().RingEngine(rank, world, device.index, slot, int(os.environ.get("MGFA_RING_CHUNKS", 1024)))
+        eng = C().RingEngine(rank, world, device.index, slot, int(os.environ.get("MGFA_RING_CHUNKS", 0)))
         handles = [None] * world
         dist.all_gather_object(handles, eng.ipc_handle(), group=group)
         eng.connect(handles)

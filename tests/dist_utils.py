@@ -12,7 +12,7 @@ def free_port() -> int:
         return s.getsockname()[1]
 
 
-def _entry(rank, world, port, backend, fn, args, errq):
+def _entry(rank, world, port, backend, fn, args, errq, final_barrier=True, pg_timeout=60):
     import torch
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
@@ -22,26 +22,36 @@ def _entry(rank, world, port, backend, fn, args, errq):
             torch.cuda.set_device(rank)
         import datetime
         dist.init_process_group(backend, rank=rank, world_size=world,
-                                timeout=datetime.timedelta(seconds=60),
+                                timeout=datetime.timedelta(seconds=pg_timeout),
                                 **({"device_id": torch.device("cuda", rank)} if backend == "nccl" else {}))
         fn(rank, world, *args)
-        dist.barrier()
+        if final_barrier:
+            dist.barrier()
     except BaseException:
         errq.put((rank, traceback.format_exc()))
         raise
     finally:
-        if dist.is_initialized():
+        if dist.is_initialized() and final_barrier:
             dist.destroy_process_group()
 
 
-def run_ranks(fn, world, *args, backend="gloo", timeout=240):
+def run_ranks(fn, world, *args, backend="gloo", timeout=240, final_barrier=True, pg_timeout=60,
+              env=None):
     ctx = mp.get_context("spawn")
     errq = ctx.SimpleQueue()
     port = free_port()
-    procs = [ctx.Process(target=_entry, args=(r, world, port, backend, fn, args, errq))
+    saved = {k: os.environ.get(k) for k in (env or {})}
+    os.environ.update(env or {})
+    procs = [ctx.Process(target=_entry, args=(r, world, port, backend, fn, args, errq,
+                                               final_barrier, pg_timeout))
              for r in range(world)]
     for p in procs:
         p.start()
+    for k, v in saved.items():
+        if v is None:
+            os.environ.pop(k, None)
+        else:
+            os.environ[k] = v
     for p in procs:
         p.join(timeout)
     alive = [p for p in procs if p.is_alive()]

@@ -1,0 +1,61 @@
+"""Failure detection on CPU ranks (gloo): the failure is made on the host --
+a rank that raises, leaves, or goes silent -- and the others must end with an
+error instead of hanging."""
+import time
+
+import pytest
+import torch
+
+from dist_utils import run_ranks
+
+
+def _raising_rank(rank, world):
+    from multi_gpu_flashattention_b200.parallel.layouts import RingLayout
+    from multi_gpu_flashattention_b200.parallel.ring import ring_attention_forward
+    lay = RingLayout("contiguous", 256, world, mask="full")
+    q = torch.randn(1, 128, 1, 16)
+    if rank == 1:
+        raise RuntimeError("injected failure on rank 1")
+    ring_attention_forward(q, q, q, lay, backend="torch")  # rank 0 waits for rank 1
+
+
+def test_rank_exception_ends_peers_with_error():
+    t0 = time.monotonic()
+    with pytest.raises(AssertionError) as e:
+        run_ranks(_raising_rank, 2, pg_timeout=5, timeout=90)
+    assert "injected failure on rank 1" in str(e.value)
+    assert time.monotonic() - t0 < 90
+
+
+def _leaving_rank(rank, world):
+    from multi_gpu_flashattention_b200.parallel.health import PeerLostError, RingHealth
+    h = RingHealth()
+    h.step(0, timeout_s=20)          # both ranks take call 0
+    if rank == 1:
+        h.leave()                    # leaves between calls, nothing in flight
+        return
+    h.beat(1)
+    with pytest.raises(PeerLostError, match="rank 1 left"):
+        h.check(1, timeout_s=20)
+
+
+def test_health_detects_departed_rank():
+    run_ranks(_leaving_rank, 2, final_barrier=False)
+
+
+def _silent_rank(rank, world):
+    from multi_gpu_flashattention_b200.parallel.health import PeerLostError, RingHealth
+    h = RingHealth()
+    h.step(0, timeout_s=20)
+    if rank == 1:
+        time.sleep(4)                # never announces call 1
+        return
+    h.beat(1)
+    t0 = time.monotonic()
+    with pytest.raises(PeerLostError, match="did not reach call 1"):
+        h.check(1, timeout_s=1.0)
+    assert time.monotonic() - t0 < 3
+
+
+def test_health_times_out_on_silent_rank():
+    run_ranks(_silent_rank, 2, final_barrier=False)
