@@ -22,7 +22,10 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <cstdio>
 #include <memory>
+
+#include <nvtx3/nvToolsExt.h>
 
 #include "../kernels/flash_fwd_sm100.cuh"
 #include "symmetric.hpp"
@@ -118,6 +121,9 @@ class RingEngine {
     auto slot_k = [&](int rank, int s) { return buf_.payload(rank) + size_t(s) * 2 * slot_bytes_; };
     auto slot_v = [&](int rank, int s) { return slot_k(rank, s) + slot_bytes_; };
     const int grid = flash_fwd_grid_ctas(int(Hq), n_q_tiles, int(B));
+    if (trace_) {
+      last_trace_ = torch::zeros({P, grid, kTraceWords}, q.options().dtype(at::kLong));
+    }
 
     for (int t = 0; t < P; ++t) {
       const int owner = ((r - t) % P + P) % P;
@@ -177,13 +183,25 @@ class RingEngine {
         p.consume.left_credit = buf_.flag(left, s == 0 ? comm::kCredit0 : comm::kCredit1);
         p.consume.left_credit_value = uses_[s] + 1;
       }
+      if (trace_)
+        p.trace = reinterpret_cast<uint64_t*>(last_trace_.data_ptr<int64_t>()) +
+                  int64_t(t) * grid * kTraceWords;
+      char label[64];
+      std::snprintf(label, sizeof(label), "ring step %d (kv owner %d)", t, owner);
+      nvtxRangePushA(label);
       flash_fwd_launch_maps(mq, mk, mv, p, stream);
+      nvtxRangePop();
       if (transport && t > 0) uses_[s] += 1;
     }
     return {o, lse};
   }
 
  public:
+
+  // Per-CTA kernel timelines of the following calls ([P, grid, 8] int64, see
+  // FwdParams::trace), readable with last_trace().
+  void set_trace(bool on) { trace_ = on; }
+  torch::Tensor last_trace() const { return last_trace_; }
 
   // Fault injection for tests (off by default): at ring step `step` of the next
   // forward calls, the push copies its data but skips one arrival signal.
@@ -201,6 +219,8 @@ class RingEngine {
   uint32_t n_chunks_;
   uint32_t uses_[2] = {0, 0};
   int drop_signal_step_ = -1;
+  bool trace_ = false;
+  torch::Tensor last_trace_;
 };
 
 void register_ring_engine(py::module& m) {
@@ -213,6 +233,8 @@ void register_ring_engine(py::module& m) {
       .def("uses", &RingEngine::uses)
       .def("reset", &RingEngine::reset)
       .def("set_drop_signal_step", &RingEngine::set_drop_signal_step)
+      .def("set_trace", &RingEngine::set_trace)
+      .def("last_trace", &RingEngine::last_trace)
       .def("forward", &RingEngine::forward, py::arg("q"), py::arg("k"), py::arg("v"),
            py::arg("scale"), py::arg("causal"), py::arg("q_tile_pos"), py::arg("kv_tile_pos"),
            py::arg("kv_lens"), py::arg("status"), py::arg("wait_limit_ns"))

@@ -54,9 +54,16 @@ struct __align__(1024) FwdSmem {
   uint64_t s_full[2], p_full[2];
   uint64_t o_full;
   uint64_t drain;
+  uint64_t trace[kTraceWords];
   uint32_t tmem_base;
   uint32_t abort_flag;
 };
+
+__device__ __forceinline__ uint32_t sm_id() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%smid;" : "=r"(r));
+  return r;
+}
 
 // Number of leading entries of the non-decreasing `pos[0..n)` that are <= `limit`
 // (every shard layout lists its key tiles in increasing global position, so the
@@ -84,7 +91,8 @@ __device__ __forceinline__ int visible_prefix(const int* pos, int n, int limit) 
 
 // ------------------------------------------------------------------ ring push
 __device__ void ring_push_warp(const RingPush& rp, const RingConsume& rc, uint32_t* status,
-                               uint64_t limit_ns, volatile uint32_t* abort_flag) {
+                               uint64_t limit_ns, volatile uint32_t* abort_flag,
+                               uint64_t* trace_slots) {
   const uint32_t lane = lane_id();
   if (lane == 0) {
     // The shard we forward must have fully arrived here first...
@@ -97,6 +105,7 @@ __device__ void ring_push_warp(const RingPush& rp, const RingConsume& rc, uint32
   }
   __syncwarp();
   if (*abort_flag) return;
+  if (lane == 0) trace_slots[4] = globaltimer();
   const uint64_t total = 2 * rp.bytes;
   const uint64_t chunk = ((total / rp.n_chunks) + 15) & ~uint64_t(15);
   const uint32_t linear_cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
@@ -131,6 +140,7 @@ __device__ void ring_push_warp(const RingPush& rp, const RingConsume& rc, uint32
       red_release_sys_add(rp.peer_arrivals, 1u);
     }
   }
+  if (lane == 0) trace_slots[5] = globaltimer();
 }
 
 // ------------------------------------------------------------------ kernel
@@ -175,6 +185,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) tmem_alloc<512>(&s.tmem_base);
   if (threadIdx.x == 0) {
     s.abort_flag = 0;
+    if (p.trace) {
+      for (int i = 0; i < kTraceWords; ++i) s.trace[i] = 0;
+      s.trace[1] = globaltimer();
+    }
     mbar_init(&s.q_full, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.k_full[i], 1);
@@ -211,6 +225,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Data written by peers' generic stores, read here by the async proxy.
         asm volatile("fence.proxy.async.global;" ::: "memory");
       }
+      if (p.trace) s.trace[2] = globaltimer();
       int it = 0;
       int last_k_phase[2] = {-1, -1}, last_v_phase[2] = {-1, -1};
       for (int j = 0; ok && j < n_active; ++j) {
@@ -307,7 +322,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 10) {
     // ------------------------------------------------------------ ring push
-    if (p.push.enabled) ring_push_warp(p.push, p.consume, p.status, p.wait_limit_ns, &s.abort_flag);
+    if (p.push.enabled)
+      ring_push_warp(p.push, p.consume, p.status, p.wait_limit_ns, &s.abort_flag, s.trace);
   } else {
     // ------------------------------------------------------------ softmax + epilogue
     const int t = warp >> 2;                // query tile within the CTA
@@ -445,6 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!skip_compute && ok) ok = __all_sync(0xffffffffu, mbar_wait(&s.o_full, 0, ab, 30 + t));
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
+    if (p.trace && threadIdx.x == 0) s.trace[3] = globaltimer();
 
     // ---- epilogue: normalise, merge with the running state, store
     const int row = qt * kTile + r;
@@ -519,6 +536,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc<512>(tmem);
+  if (p.trace && threadIdx.x == 0) {
+    const uint32_t linear_cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+    s.trace[0] = (uint64_t(sm_id()) << 32) | linear_cta;
+    s.trace[6] = globaltimer();
+    s.trace[7] = uint64_t(n_active);
+    uint64_t* dst = p.trace + uint64_t(linear_cta) * kTraceWords;
+    for (int i = 0; i < kTraceWords; ++i) dst[i] = s.trace[i];
+  }
   if (p.consume.enabled && threadIdx.x == 0) {
     // The last CTA to finish tells the left neighbour this slot may be reused.
     __threadfence();

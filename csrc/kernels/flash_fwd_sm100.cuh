@@ -59,7 +59,13 @@ struct FwdParams {
   uint64_t wait_limit_ns = 2000000000ull;
   RingPush push;
   RingConsume consume;
+  // Optional per-CTA timeline (%globaltimer ns), kTraceWords u64 per CTA at
+  // trace[linear_cta * kTraceWords]: {sm << 32 | cta, start, kv_ready,
+  // epilogue, push_start, push_end, end, visible key tiles}.
+  uint64_t* trace = nullptr;
 };
+
+constexpr int kTraceWords = 8;
 
 // Host helpers (flash_fwd_sm100.cu).
 // Tensor map of a [B, S, H, 128] bf16 tensor with the given element strides.

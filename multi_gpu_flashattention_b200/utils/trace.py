@@ -1,0 +1,66 @@
+"""Kernel timelines of the fused ring engine as Chrome trace events.
+
+Enable with `ENGINES.get(...).set_trace(True)` (or `ring_trace(...)` below),
+run a forward, then `engine.last_trace()` holds [steps, CTAs, 8] int64 words
+per call: {sm << 32 | cta, start, kv_ready, epilogue, push_start, push_end,
+end, visible key tiles} in %globaltimer nanoseconds. `to_chrome_events` turns
+them into complete ("X") events -- one process per rank, one thread per SM --
+for chrome://tracing or Perfetto."""
+from __future__ import annotations
+
+import json
+from typing import Iterable, List, Optional
+
+import torch
+
+
+def to_chrome_events(trace: torch.Tensor, rank: int = 0, t0_ns: Optional[int] = None) -> List[dict]:
+    t = trace.detach().cpu().to(torch.int64)
+    valid = t[..., 6] != 0
+    if t0_ns is None:
+        t0_ns = int(t[..., 1][valid].min().item()) if valid.any() else 0
+    ev = []
+    steps, ctas, _ = t.shape
+    for s in range(steps):
+        for c in range(ctas):
+            w = t[s, c].tolist()
+            if w[6] == 0:
+                continue
+            sm = w[0] >> 32
+            us = lambda x: (x - t0_ns) / 1e3
+            args = {"step": s, "cta": w[0] & 0xFFFFFFFF, "key_tiles": w[7]}
+            kv = w[2] or w[1]
+            if kv > w[1]:
+                ev.append({"name": "wait kv", "ph": "X", "pid": rank, "tid": sm, "ts": us(w[1]),
+                           "dur": (kv - w[1]) / 1e3, "args": args})
+            end_c = w[3] or w[6]
+            ev.append({"name": f"attn step {s}", "ph": "X", "pid": rank, "tid": sm, "ts": us(kv),
+                       "dur": max(0, end_c - kv) / 1e3, "args": args})
+            ev.append({"name": "epilogue", "ph": "X", "pid": rank, "tid": sm, "ts": us(end_c),
+                       "dur": max(0, w[6] - end_c) / 1e3, "args": args})
+            if w[4] and w[5]:
+                ev.append({"name": "push", "ph": "X", "pid": rank, "tid": 1000 + sm,
+                           "ts": us(w[4]), "dur": (w[5] - w[4]) / 1e3, "args": args})
+    return ev
+
+
+def write_chrome_trace(events: Iterable[dict], path: str) -> None:
+    with open(path, "w") as f:
+        json.dump({"traceEvents": list(events), "displayTimeUnit": "ns"}, f)
+
+
+def summarize(trace: torch.Tensor) -> dict:
+    """Per-step wall span, summed CTA compute and push time (ms)."""
+    t = trace.detach().cpu().to(torch.int64)
+    out = []
+    for s in range(t.shape[0]):
+        w = t[s]
+        ok = w[:, 6] != 0
+        if not ok.any():
+            continue
+        w = w[ok]
+        span = (w[:, 6].max() - w[:, 1].min()).item() / 1e6
+        kv_wait = ((w[:, 2] - w[:, 1]).clamp(min=0) * (w[:, 2] != 0)).max().item() / 1e6
+        push = ((w[:, 5] - w[:, 4]) * (w[:, 4] != 0)).float().mean().item() / 1e6
+        out.append({"step": s, "span_ms": span, "max_kv_wait_ms": kv_wait, "mean_push_ms": push})
+    return {"steps": out}

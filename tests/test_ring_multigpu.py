@@ -74,3 +74,30 @@ def _bwd_case(rank, world, kind, causal):
                                          ("striped", True)])
 def test_ring_backward_matches_reference(kind, causal):
     run_ranks(_bwd_case, _world(), kind, causal, backend="nccl")
+
+
+def _trace_case(rank, world):
+    from multi_gpu_flashattention_b200.parallel.layouts import RingLayout
+    from multi_gpu_flashattention_b200.parallel.ring import ENGINES, ring_attention_forward
+    from multi_gpu_flashattention_b200.utils.trace import summarize, to_chrome_events
+    dev = torch.device("cuda", rank)
+    lay = RingLayout("zigzag", 4096, world, mask="causal")
+    q = (torch.randn(1, lay.max_local_len, 2, 128, device=dev) * 0.5).bfloat16()
+    ring_attention_forward(q, q, q, lay, causal=True, backend="fused", check=True)
+    eng = ENGINES.get(None, dev, q.numel() * 2)
+    eng.set_trace(True)
+    ring_attention_forward(q, q, q, lay, causal=True, backend="fused", check=True)
+    eng.set_trace(False)
+    tr = eng.last_trace()
+    assert tr.shape[0] == world and tr.shape[2] == 8
+    assert (tr[..., 6] >= tr[..., 1]).all() and (tr[..., 6] > 0).all()
+    pushed = tr[: world - 1, :, 4] > 0
+    assert pushed.all(), "every CTA of a pushing step records its push"
+    assert (tr[world - 1, :, 4] == 0).all(), "the last step pushes nothing"
+    ev = to_chrome_events(tr, rank)
+    assert any(e["name"] == "push" for e in ev)
+    assert len(summarize(tr)["steps"]) == world
+
+
+def test_ring_forward_trace_records_timeline():
+    run_ranks(_trace_case, _world(), backend="nccl")
