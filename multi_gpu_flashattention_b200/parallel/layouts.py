@@ -113,8 +113,16 @@ class RingLayout:
         far = 1 << 30
         return starts + [far] * (n_tiles - len(starts))
 
+    @staticmethod
+    def _check_monotone(starts: List[int], what: str) -> List[int]:
+        # the kernels find visible key tiles by prefix search over these tables
+        if any(b < a for a, b in zip(starts, starts[1:])):
+            raise ValueError(f"{what}: tile positions must be non-decreasing, got {starts[:8]}...")
+        return starts
+
     def q_tile_pos(self, rank: int, device) -> torch.Tensor:
-        return torch.tensor(self._tile_starts(rank), dtype=torch.int32, device=device)
+        return torch.tensor(self._check_monotone(self._tile_starts(rank), f"rank {rank}"),
+                            dtype=torch.int32, device=device)
 
     def kv_tile_pos(self, rank: int, owner: int, device) -> torch.Tensor:
         """Tile positions of owner's shard as seen by rank's queries."""
@@ -122,7 +130,8 @@ class RingLayout:
             n = (self.max_local_len + TILE - 1) // TILE
             off = 1 if owner > rank else 0
             return torch.arange(n, dtype=torch.int32, device=device) * TILE + off
-        return torch.tensor(self._tile_starts(owner), dtype=torch.int32, device=device)
+        return torch.tensor(self._check_monotone(self._tile_starts(owner), f"owner {owner}"),
+                            dtype=torch.int32, device=device)
 
     def kv_tile_pos_by_owner(self, rank: int, device) -> torch.Tensor:
         return torch.stack([self.kv_tile_pos(rank, o, device) for o in range(self.world)])

@@ -115,14 +115,17 @@ def _bwd_torch(dout, q, k, v, layout, causal, scale, group):
     else:
         ks, vs = [k], [v]
     kv_lens = layout.kv_lens()
-    kfull = torch.cat([ks[o][:, :kv_lens[o]] for o in range(world)], 1).float().requires_grad_()
-    vfull = torch.cat([vs[o][:, :kv_lens[o]] for o in range(world)], 1).float().requires_grad_()
-    qf = q.float().requires_grad_()
     q_pos = layout.q_positions_for_mask(rank).to(q.device)
     k_pos = torch.cat([layout.k_positions_for_mask(rank, o)[:kv_lens[o]] for o in range(world)])
-    o_ref, _ = attention_ref(qf, kfull, vfull, causal=causal, softmax_scale=scale, q_pos=q_pos,
-                             k_pos=k_pos.to(q.device))
-    dq, dkf, dvf = torch.autograd.grad(o_ref, (qf, kfull, vfull), dout.float())
+    with torch.enable_grad():  # also when called from an autograd.Function backward
+        kfull = torch.cat([ks[o][:, :kv_lens[o]] for o in range(world)], 1).detach().float()
+        vfull = torch.cat([vs[o][:, :kv_lens[o]] for o in range(world)], 1).detach().float()
+        kfull.requires_grad_()
+        vfull.requires_grad_()
+        qf = q.detach().float().requires_grad_()
+        o_ref, _ = attention_ref(qf, kfull, vfull, causal=causal, softmax_scale=scale,
+                                 q_pos=q_pos, k_pos=k_pos.to(q.device))
+        dq, dkf, dvf = torch.autograd.grad(o_ref, (qf, kfull, vfull), dout.float())
     # gradients of every owner's keys: sum over ranks, then keep ours
     offs = [0]
     for o in range(world):
