@@ -157,6 +157,9 @@ class RingEngine {
       p.final_out = t == P - 1 ? 1 : 0;
       p.status = reinterpret_cast<uint32_t*>(status.data_ptr<int>());
       p.wait_limit_ns = uint64_t(wait_limit_ns);
+      // steps after the first overlap the previous step's tail (PDL); the first
+      // step of a call is fully ordered after everything before it
+      p.dependent_launch = (t > 0 && pdl_) ? 1 : 0;
 
       if (transport && t < P - 1) {
         const int sn = (t + 1) & 1;
@@ -201,6 +204,8 @@ class RingEngine {
   // Per-CTA kernel timelines of the following calls ([P, grid, 8] int64, see
   // FwdParams::trace), readable with last_trace().
   void set_trace(bool on) { trace_ = on; }
+  // Programmatic dependent launch between ring steps (on by default).
+  void set_dependent_launch(bool on) { pdl_ = on; }
   torch::Tensor last_trace() const { return last_trace_; }
 
   // Fault injection for tests (off by default): at ring step `step` of the next
@@ -220,6 +225,7 @@ class RingEngine {
   uint32_t uses_[2] = {0, 0};
   int drop_signal_step_ = -1;
   bool trace_ = false;
+  bool pdl_ = true;
   torch::Tensor last_trace_;
 };
 
@@ -234,6 +240,7 @@ void register_ring_engine(py::module& m) {
       .def("reset", &RingEngine::reset)
       .def("set_drop_signal_step", &RingEngine::set_drop_signal_step)
       .def("set_trace", &RingEngine::set_trace)
+      .def("set_dependent_launch", &RingEngine::set_dependent_launch)
       .def("last_trace", &RingEngine::last_trace)
       .def("forward", &RingEngine::forward, py::arg("q"), py::arg("k"), py::arg("v"),
            py::arg("scale"), py::arg("causal"), py::arg("q_tile_pos"), py::arg("kv_tile_pos"),

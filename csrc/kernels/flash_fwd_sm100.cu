@@ -181,6 +181,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool skip_compute = n_active == 0;
   if (skip_compute && has_prior && !p.final_out && !p.push.enabled && !p.consume.enabled) return;
 
+  // Let the next ring step's grid start filling SMs as this grid's CTAs retire.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   AbortState ab{&s.abort_flag, p.status, p.wait_limit_ns};
   if (warp == 0) tmem_alloc<512>(&s.tmem_base);
   if (threadIdx.x == 0) {
@@ -464,6 +466,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (p.trace && threadIdx.x == 0) s.trace[3] = globaltimer();
 
     // ---- epilogue: normalise, merge with the running state, store
+    // Everything above only read q and this step's K/V; the running state was
+    // written by the previous step's grid, which must be complete from here on.
+    if (p.dependent_launch) asm volatile("griddepcontrol.wait;" ::: "memory");
     const int row = qt * kTile + r;
     const bool row_valid = qt < p.n_q_tiles && row < p.sq;
     const float lse2_new = (l > 0.f) ? m + log2f(l) : -INFINITY;
@@ -605,8 +610,22 @@ void flash_fwd_launch_maps(const CUtensorMap& mq, const CUtensorMap& mk, const C
   }
   const int n_pairs = (p.n_q_tiles + 1) / 2;
   dim3 grid(n_pairs, p.hq, p.batch);
-  kern<<<grid, kThreads, smem, stream>>>(mq, mk, mv, p);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  if (p.dependent_launch) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = size_t(smem);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, p));
+  } else {
+    kern<<<grid, kThreads, smem, stream>>>(mq, mk, mv, p);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
 }
 
 void flash_fwd_launch(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v,

@@ -63,6 +63,10 @@ struct FwdParams {
   // trace[linear_cta * kTraceWords]: {sm << 32 | cta, start, kv_ready,
   // epilogue, push_start, push_end, end, visible key tiles}.
   uint64_t* trace = nullptr;
+  // Launched with programmatic dependent launch: the kernel may start while the
+  // previous step's grid is still running; it waits for that grid only before
+  // its epilogue touches the running state (o_state / lse / o).
+  int dependent_launch = 0;
 };
 
 constexpr int kTraceWords = 8;
