@@ -9,12 +9,17 @@
 // synchronisation between steps: ordering across ranks is carried entirely by
 // the flag words of the symmetric buffer.
 //
+// Receive slots are triple-buffered: step t (t >= 1) reads slot t % 3 and
+// pushes into the neighbour's slot (t + 1) % 3, whose previous use (step t - 2)
+// finished long ago, so a push never waits on the neighbour's current step
+// (the next step's CTAs start during this step's tail, see dependent launch).
 // Flags (see comm/symmetric.hpp):
-//   arrivals[s]  on the receiver, +1 per pushed chunk; the kernels of a step
-//                that reads slot s wait for n_chunks, the last CTA rearms it
+//   arrivals[s]  on the receiver, +1 per pushed chunk part; the kernels of a
+//                step that reads slot s wait for all of them, the last CTA
+//                rearms it
 //   credit[s]    on the sender, the receiver's count of finished uses of its
 //                slot s; a push into slot s waits until it equals the uses so
-//                far (double buffering with back-pressure)
+//                far (back-pressure)
 //   done[s]      CTAs finished with slot s in this step (last CTA publishes)
 // All ranks call forward() in the same order, so the per-slot use counts kept
 // on the host agree everywhere.
@@ -35,11 +40,12 @@ namespace mgfa {
 class RingEngine {
  public:
   RingEngine(int rank, int world, int device, int64_t slot_bytes, int n_chunks)
-      : buf_(size_t(4 * slot_bytes), rank, world, device),
+      : buf_(size_t(2 * kSlots * slot_bytes), rank, world, device),
         slot_bytes_(size_t(slot_bytes)),
-        n_chunks_(uint32_t(n_chunks)) {
+        n_chunks_(n_chunks) {
     TORCH_CHECK(slot_bytes > 0 && slot_bytes % 4096 == 0, "slot_bytes must be a multiple of 4096");
-    TORCH_CHECK(n_chunks >= 0, "n_chunks must be >= 0 (0 = one chunk per CTA)");
+    // n_chunks: > 0 fixed, 0 two waves of CTAs, < 0 one chunk per CTA
+    C10_CUDA_CHECK(cudaDeviceGetAttribute(&num_sms_, cudaDevAttrMultiProcessorCount, device));
   }
 
   py::bytes ipc_handle() const { return py::bytes(buf_.ipc_handle()); }
@@ -47,7 +53,9 @@ class RingEngine {
   void connect(const std::vector<std::string>& handles) { buf_.open_peers(handles); }
 
   int64_t slot_bytes() const { return int64_t(slot_bytes_); }
-  std::vector<int64_t> uses() const { return {int64_t(uses_[0]), int64_t(uses_[1])}; }
+  std::vector<int64_t> uses() const {
+    return {int64_t(uses_[0]), int64_t(uses_[1]), int64_t(uses_[2])};
+  }
 
   // q [B,Sq,Hq,128] bf16; k, v [B,L,Hkv,128] bf16 contiguous local shards (same L on
   // every rank; owner o's first kv_lens[o] rows are valid).
@@ -77,6 +85,14 @@ class RingEngine {
   }
 
  private:
+  // n_chunks > 0: that many; 0: two waves of CTAs; < 0: one chunk per CTA.
+  uint32_t push_chunks(int grid) const {
+    if (n_chunks_ < 0) return uint32_t(grid);
+    if (n_chunks_ > 0) return uint32_t(n_chunks_) < uint32_t(grid) ? uint32_t(n_chunks_) : uint32_t(grid);
+    const uint32_t two_waves = 2u * uint32_t(num_sms_);
+    return two_waves < uint32_t(grid) ? two_waves : uint32_t(grid);
+  }
+
   std::vector<torch::Tensor> run(torch::Tensor q, torch::Tensor k, torch::Tensor v, double scale,
                                  bool causal, c10::optional<torch::Tensor> q_tile_pos,
                                  c10::optional<torch::Tensor> kv_tile_pos,
@@ -127,7 +143,7 @@ class RingEngine {
 
     for (int t = 0; t < P; ++t) {
       const int owner = ((r - t) % P + P) % P;
-      const int s = t & 1;
+      const int s = t % kSlots;
       const bool own = t == 0 || !transport;
       const uint8_t* cur_k = own ? static_cast<const uint8_t*>(k.data_ptr()) : slot_k(r, s);
       const uint8_t* cur_v = own ? static_cast<const uint8_t*>(v.data_ptr()) : slot_v(r, s);
@@ -162,28 +178,30 @@ class RingEngine {
       p.dependent_launch = (t > 0 && pdl_) ? 1 : 0;
 
       if (transport && t < P - 1) {
-        const int sn = (t + 1) & 1;
+        const int sn = (t + 1) % kSlots;
         p.push.enabled = 1;
         p.push.src_k = cur_k;
         p.push.src_v = cur_v;
         p.push.dst_k = slot_k(right, sn);
         p.push.dst_v = slot_v(right, sn);
         p.push.bytes = shard_bytes;
-        p.push.peer_arrivals = buf_.flag(right, sn == 0 ? comm::kArrivals0 : comm::kArrivals1);
-        p.push.credit = buf_.flag(r, sn == 0 ? comm::kCredit0 : comm::kCredit1);
+        p.push.peer_arrivals = buf_.flag(right, comm::kArrivals0 + sn);
+        p.push.credit = buf_.flag(r, comm::kCredit0 + sn);
         p.push.credit_target = uses_[sn];
-        // one chunk per CTA: every rank launches the same grid (shards are padded
-        // to one length), so the receiver's arrival target is the same number
-        p.push.n_chunks = n_chunks_ ? n_chunks_ : uint32_t(grid);
+        // The first chunks CTAs of the grid push (two waves by default, so the
+        // shard reaches the neighbour early in the step). Every rank launches the
+        // same grid (shards are padded to one length), so the receiver's arrival
+        // target is the same number.
+        p.push.n_chunks = push_chunks(grid);
         p.push.drop_signal = (drop_signal_step_ == t) ? 1 : 0;
       }
       if (transport && t > 0) {
         p.consume.enabled = 1;
-        p.consume.arrivals = buf_.flag(r, s == 0 ? comm::kArrivals0 : comm::kArrivals1);
-        p.consume.arrivals_target = n_chunks_ ? n_chunks_ : uint32_t(grid);
-        p.consume.done_counter = buf_.flag(r, s == 0 ? comm::kDone0 : comm::kDone1);
+        p.consume.arrivals = buf_.flag(r, comm::kArrivals0 + s);
+        p.consume.arrivals_target = push_chunks(grid) * kFwdPushParts;
+        p.consume.done_counter = buf_.flag(r, comm::kDone0 + s);
         p.consume.done_target = uint32_t(grid - 1);
-        p.consume.left_credit = buf_.flag(left, s == 0 ? comm::kCredit0 : comm::kCredit1);
+        p.consume.left_credit = buf_.flag(left, comm::kCredit0 + s);
         p.consume.left_credit_value = uses_[s] + 1;
       }
       if (trace_)
@@ -215,17 +233,19 @@ class RingEngine {
   // Zero local flags and use counts (collective: every rank, then a barrier).
   void reset() {
     buf_.reset_flags(at::cuda::getCurrentCUDAStream());
-    uses_[0] = uses_[1] = 0;
+    for (auto& u : uses_) u = 0;
   }
 
  private:
   comm::SymmetricBuffer buf_;
   size_t slot_bytes_;
-  uint32_t n_chunks_;
-  uint32_t uses_[2] = {0, 0};
+  int n_chunks_;
+  static constexpr int kSlots = 3;
+  uint32_t uses_[kSlots] = {0, 0, 0};
   int drop_signal_step_ = -1;
   bool trace_ = false;
   bool pdl_ = true;
+  int num_sms_ = 148;
   torch::Tensor last_trace_;
 };
 

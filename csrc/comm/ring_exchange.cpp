@@ -62,18 +62,18 @@ class RingExchange {
     push.dst_k = buf_.payload(right) + size_t(sn) * slot_bytes_;
     push.dst_v = push.dst_k + half;
     push.bytes = half;
-    push.peer_arrivals = buf_.flag(right, sn == 0 ? comm::kArrivals0 : comm::kArrivals1);
-    push.credit = buf_.flag(r, sn == 0 ? comm::kCredit0 : comm::kCredit1);
+    push.peer_arrivals = buf_.flag(right, comm::kArrivals0 + sn);
+    push.credit = buf_.flag(r, comm::kCredit0 + sn);
     push.credit_target = uses_[sn];
     push.n_chunks = chunks;
     RingConsume consume;
     if (t > 0) {  // slot s was filled by the left neighbour during step t-1
       consume.enabled = 1;
-      consume.arrivals = buf_.flag(r, s == 0 ? comm::kArrivals0 : comm::kArrivals1);
+      consume.arrivals = buf_.flag(r, comm::kArrivals0 + s);
       consume.arrivals_target = chunks;
-      consume.done_counter = buf_.flag(r, s == 0 ? comm::kDone0 : comm::kDone1);
+      consume.done_counter = buf_.flag(r, comm::kDone0 + s);
       consume.done_target = uint32_t(n_ctas_ - 1);
-      consume.left_credit = buf_.flag(left, s == 0 ? comm::kCredit0 : comm::kCredit1);
+      consume.left_credit = buf_.flag(left, comm::kCredit0 + s);
       consume.left_credit_value = uses_[s] + 1;
     }
     uint32_t* st = reinterpret_cast<uint32_t*>(status.data_ptr<int>());
@@ -102,9 +102,9 @@ class RingExchange {
     RingPush none;
     RingConsume consume;
     consume.enabled = 1;
-    consume.arrivals = buf_.flag(r, s == 0 ? comm::kArrivals0 : comm::kArrivals1);
+    consume.arrivals = buf_.flag(r, comm::kArrivals0 + s);
     consume.arrivals_target = transport == "p2p" ? uint32_t(n_ctas_) : 1u;
-    consume.left_credit = buf_.flag(left, s == 0 ? comm::kCredit0 : comm::kCredit1);
+    consume.left_credit = buf_.flag(left, comm::kCredit0 + s);
     consume.left_credit_value = uses_[s] + 1;
     uint32_t* st = reinterpret_cast<uint32_t*>(status.data_ptr<int>());
     C10_CUDA_CHECK(ring_wait_launch(none, consume, st, uint64_t(wait_limit_ns), stream));

@@ -21,16 +21,13 @@ namespace mgfa::comm {
 constexpr size_t kFlagBytes = 64 * 1024;
 constexpr size_t kFlagStride = 128;  // bytes between flag words
 
-// Flag word indices.
+// Flag word indices (slot s of a ring buffer uses kArrivals0 + s, kCredit0 + s,
+// kDone0 + s; up to kMaxSlots slots).
+constexpr int kMaxSlots = 4;
 enum FlagIndex : int {
-  kArrivals0 = 0,   // chunks of slot 0 received (written by the left neighbour)
-  kArrivals1 = 1,
-  kCredit0 = 2,     // uses of the right neighbour's slot 0 it finished (written by it)
-  kCredit1 = 3,
-  kDone0 = 4,       // CTAs of this rank finished with slot 0 in the current step
-  kDone1 = 5,
-  kLoopArrivals = 8,  // pure-exchange benchmark counters
-  kLoopCredit = 9,
+  kArrivals0 = 0,   // chunks of slot s received (written by the left neighbour)
+  kCredit0 = 4,     // uses of the right neighbour's slot s it finished (written by it)
+  kDone0 = 8,       // CTAs of this rank finished with slot s in the current step
   kStatus = 16,     // device error word of the last call
 };
 

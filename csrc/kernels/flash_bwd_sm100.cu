@@ -100,10 +100,6 @@ struct __align__(1024) DqSmem {
   uint32_t abort_flag;
 };
 
-__device__ __forceinline__ bool dq_tile_active(const BwdParams& p, int qt, int j) {
-  if (!p.causal) return true;
-  return p.kv_tile_pos[j] <= p.q_tile_pos[qt] + (kTile - 1);
-}
 
 __global__ void __launch_bounds__(kThreads, 1)
     flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap map_q,
@@ -117,8 +113,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   // query tiles vary fastest: resident CTAs share one head's K/V in L2
   const int qt = gridDim.x - 1 - blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int hk = h / (p.hq / p.hkv);
-  int n_active = 0;
-  for (int j = 0; j < p.n_kv_tiles; ++j) n_active += dq_tile_active(p, qt, j) ? 1 : 0;
+  // key tiles [0, n_active) are visible to this query tile, [0, full_hi) unmasked
+  const int q_tile_pos = p.causal ? __ldg(p.q_tile_pos + qt) : 0;
+  const int n_active = p.causal ? visible_prefix(p.kv_tile_pos, p.n_kv_tiles, q_tile_pos + (kTile - 1))
+                                : p.n_kv_tiles;
   if (n_active == 0 && p.accumulate) return;  // nothing to add
 
   AbortState ab{&s.abort_flag, p.status, p.wait_limit_ns};
@@ -153,8 +151,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       load_tile(s.dout, &map_do, &s.qd_full, h, qt * kTile, b);
       int it = 0;
       int last_k[2] = {-1, -1}, last_v[2] = {-1, -1};
-      for (int j = 0; j < p.n_kv_tiles; ++j) {
-        if (!dq_tile_active(p, qt, j)) continue;
+      for (int j = 0; j < n_active; ++j) {
         const int st = it & 1;
         const uint32_t ph = (it >> 1) & 1;
         if (!mbar_wait(&s.k_empty[st], ph ^ 1, ab, 41)) break;
@@ -245,11 +242,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t ml = (int64_t(b) * p.hq + h) * p.sq_pad + row;
     const float lse2 = p.lse2[ml];
     const float dlt = p.delta[ml];
-    const int q_pos = p.causal ? p.q_tile_pos[qt] + r : 0;
+    const int q_pos = q_tile_pos + r;
+    int full_hi = p.n_kv_tiles - ((p.sk % kTile) != 0 ? 1 : 0);
+    if (p.causal) {
+      const int f = visible_prefix(p.kv_tile_pos, n_active, q_tile_pos - (kTile - 1));
+      full_hi = f < full_hi ? f : full_hi;
+    }
     bool ok = true;
     int it = 0;
-    for (int j = 0; n_active > 0 && j < p.n_kv_tiles; ++j) {
-      if (!dq_tile_active(p, qt, j)) continue;
+    for (int j = 0; j < n_active; ++j) {
       ok = __all_sync(0xffffffffu, mbar_wait(&s.s_full, it & 1, ab, 60));
       if (!ok) break;
       tc_fence_after();
@@ -257,16 +258,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld128(tmem + lane_off + S_COL, sr);
       tc_fence_before();
       mbar_arrive(&s.s_free);
-      int n_vis = p.sk - j * kTile;
-      if (p.causal) {
-        const int lim = q_pos - p.kv_tile_pos[j] + 1;
-        n_vis = lim < n_vis ? lim : n_vis;
-      }
-      if (!row_valid) n_vis = 0;
       float pr[128];
+      if (j < full_hi) {  // warp-uniform fast path: no mask
 #pragma unroll
-      for (int c = 0; c < 128; ++c)
-        pr[c] = (c < n_vis) ? ex2_approx(__uint_as_float(sr[c]) * p.scale_log2 - lse2) : 0.f;
+        for (int c = 0; c < 128; ++c)
+          pr[c] = ex2_approx(fmaf(__uint_as_float(sr[c]), p.scale_log2, -lse2));
+      } else {
+        int n_vis = p.sk - j * kTile;
+        if (p.causal) {
+          const int lim = q_pos - __ldg(p.kv_tile_pos + j) + 1;
+          n_vis = lim < n_vis ? lim : n_vis;
+        }
+        if (!row_valid) n_vis = 0;
+#pragma unroll
+        for (int c = 0; c < 128; ++c)
+          pr[c] = (c < n_vis) ? ex2_approx(fmaf(__uint_as_float(sr[c]), p.scale_log2, -lse2)) : 0.f;
+      }
       ok = __all_sync(0xffffffffu, mbar_wait(&s.dp_full, it & 1, ab, 61));
       if (!ok) break;
       tc_fence_after();
@@ -327,10 +334,6 @@ struct __align__(1024) DkvSmem {
   uint32_t abort_flag;
 };
 
-__device__ __forceinline__ bool kv_sees(const BwdParams& p, int j, int qt) {
-  if (!p.causal) return true;
-  return p.kv_tile_pos[j] <= p.q_tile_pos[qt] + (kTile - 1);
-}
 
 __global__ void __launch_bounds__(kThreads, 1)
     flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap map_q,
@@ -344,8 +347,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   // key tiles vary fastest: resident CTAs share the group's Q/dO stream in L2
   const int j = gridDim.x - 1 - blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
   const int G = p.hq / p.hkv;
-  int n_q_active = 0;
-  for (int qt = 0; qt < p.n_q_tiles; ++qt) n_q_active += kv_sees(p, j, qt) ? 1 : 0;
+  // query tiles [q_lo, n_q_tiles) see this key tile (a suffix: positions increase)
+  const int kv_tile_pos = p.causal ? __ldg(p.kv_tile_pos + j) : 0;
+  const int q_lo = p.causal ? visible_prefix(p.q_tile_pos, p.n_q_tiles, kv_tile_pos - kTile) : 0;
+  const int n_q_active = p.n_q_tiles - q_lo;
   const int n_iter = n_q_active * G;
   if (n_iter == 0 && p.accumulate) return;
 
@@ -383,8 +388,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int g = 0; ok && g < G; ++g) {
         const int h = hk * G + g;
         const int64_t mlbase = (int64_t(b) * p.hq + h) * p.sq_pad;
-        for (int qt = 0; qt < p.n_q_tiles; ++qt) {
-          if (!kv_sees(p, j, qt)) continue;
+        for (int qt = q_lo; qt < p.n_q_tiles; ++qt) {
           const int st = it & 1;
           const uint32_t ph = (it >> 1) & 1;
           if (!(ok = mbar_wait(&s.qd_empty[st], ph ^ 1, ab, 71))) break;
@@ -468,12 +472,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_off = uint32_t(warp * 32) << 16;
     const int key = j * kTile + r;
     const bool key_valid = key < p.sk;
-    const int k_pos = p.causal ? p.kv_tile_pos[j] + r : 0;
+    const int k_pos = kv_tile_pos + r;
+    // query tiles [q_lo, q_full) are partially visible; [q_full, n) fully
+    // (tile starts at or after this key tile's last key)
+    const int q_full = p.causal ? visible_prefix(p.q_tile_pos, p.n_q_tiles, kv_tile_pos + kTile - 2)
+                                : 0;
     bool ok = true;
     int it = 0;
     for (int g = 0; ok && g < G; ++g) {
-      for (int qt = 0; qt < p.n_q_tiles; ++qt) {
-        if (!kv_sees(p, j, qt)) continue;
+      for (int qt = q_lo; qt < p.n_q_tiles; ++qt) {
         const int st = it & 1;
         ok = __all_sync(0xffffffffu, mbar_wait(&s.s_full, it & 1, ab, 90));
         if (!ok) break;
@@ -481,20 +488,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t sr[128];
         tmem_ld128(tmem + lane_off + ST_COL, sr);
         // visible query columns c: q_pos(c) >= k_pos and the query row exists
-        int c_lo = 0;
-        int c_hi = p.sq - qt * kTile;  // exclusive
-        if (p.causal) {
-          const int lo = k_pos - p.q_tile_pos[qt];
-          c_lo = lo > 0 ? lo : 0;
-        }
-        if (!key_valid) c_hi = 0;
         const float* lse2 = s.lse2[st];
         float pr[128];
+        // rows past sq have lse2 = +inf (P = 0); keys past sk never get stored
+        if (qt >= q_full && key_valid) {  // fast path: every query sees this key
 #pragma unroll
-        for (int c = 0; c < 128; ++c)
-          pr[c] = (c >= c_lo && c < c_hi)
-                      ? ex2_approx(__uint_as_float(sr[c]) * p.scale_log2 - lse2[c])
-                      : 0.f;
+          for (int c = 0; c < 128; ++c)
+            pr[c] = ex2_approx(fmaf(__uint_as_float(sr[c]), p.scale_log2, -lse2[c]));
+        } else {
+          int c_lo = 0;
+          if (p.causal) {
+            const int lo = k_pos - __ldg(p.q_tile_pos + qt);
+            c_lo = lo > 0 ? lo : 0;
+          }
+          const int c_hi = key_valid ? p.sq - qt * kTile : 0;  // exclusive
+#pragma unroll
+          for (int c = 0; c < 128; ++c)
+            pr[c] = (c >= c_lo && c < c_hi)
+                        ? ex2_approx(fmaf(__uint_as_float(sr[c]), p.scale_log2, -lse2[c]))
+                        : 0.f;
+        }
         uint32_t pk[64];
 #pragma unroll
         for (int c = 0; c < 64; ++c) pk[c] = pack_bf16(pr[2 * c], pr[2 * c + 1]);

@@ -14,7 +14,7 @@
 //   warp  8    TMA producer (Q once, then K and V tiles, 2-stage rings)
 //   warp  9    MMA issuer (one thread): S = Q K^T (SS form), O += P V (TS form,
 //              P read from TMEM where it overwrote S)
-//   warp 10    ring push (only when a RingPush is enabled)
+//   warps 10-11 ring push (only when a RingPush is enabled)
 // TMEM (512 columns): S0/P0 [0,128) S1/P1 [128,256) O0 [256,384) O1 [384,512).
 // The MMA order S0(j+1) after PV0(j) and S1(j+1) after PV1(j) lets one softmax
 // warpgroup work while the tensor core runs the other tile's GEMMs; a commit
@@ -40,7 +40,8 @@ constexpr int kD = 128;
 constexpr int kTile = 128;
 constexpr int kHalfBytes = kTile * 64 * 2;   // one 128 x 64 bf16 swizzled box
 constexpr int kTileBytes = 2 * kHalfBytes;   // 128 x 128 bf16
-constexpr int kWarps = 11;
+constexpr int kWarps = 12;
+constexpr int kPushWarps = 2;  // warps 10 and 11
 constexpr int kThreads = kWarps * 32;
 constexpr float kRescaleThreshold = 8.0f;    // log2 units
 
@@ -65,34 +66,12 @@ __device__ __forceinline__ uint32_t sm_id() {
   return r;
 }
 
-// Number of leading entries of the non-decreasing `pos[0..n)` that are <= `limit`
-// (every shard layout lists its key tiles in increasing global position, so the
-// key tiles a query tile can see form a prefix). Warp-cooperative; every lane
-// returns the result.
-__device__ __forceinline__ int visible_prefix(const int* pos, int n, int limit) {
-  const uint32_t lane = lane_id();
-  int lo = 0, hi = n;  // answer in [lo, hi]
-  while (hi - lo > 0) {
-    const int span = hi - lo;
-    const int step = (span + 31) / 32;
-    const int idx = lo + int(lane) * step;
-    const bool le = idx < hi && __ldg(pos + idx) <= limit;
-    const uint32_t m = __ballot_sync(0xffffffffu, le);
-    const int cnt = __popc(m);  // probes [0, cnt) are <= limit
-    if (cnt == 0) return lo;    // pos[lo] > limit
-    if (step == 1) return lo + cnt;
-    const int new_lo = lo + (cnt - 1) * step + 1;
-    const int new_hi = lo + cnt * step < hi ? lo + cnt * step : hi;
-    lo = new_lo;
-    hi = new_hi;
-  }
-  return lo;
-}
-
 // ------------------------------------------------------------------ ring push
+// Push warp `sub` of kPushWarps copies part `sub` of each of this CTA's chunks
+// and signals it separately (the receiver waits for n_chunks * kPushWarps).
 __device__ void ring_push_warp(const RingPush& rp, const RingConsume& rc, uint32_t* status,
                                uint64_t limit_ns, volatile uint32_t* abort_flag,
-                               uint64_t* trace_slots) {
+                               uint64_t* trace_slots, int sub) {
   const uint32_t lane = lane_id();
   if (lane == 0) {
     // The shard we forward must have fully arrived here first...
@@ -105,14 +84,18 @@ __device__ void ring_push_warp(const RingPush& rp, const RingConsume& rc, uint32
   }
   __syncwarp();
   if (*abort_flag) return;
-  if (lane == 0) trace_slots[4] = globaltimer();
+  if (lane == 0 && sub == 0) trace_slots[4] = globaltimer();
   const uint64_t total = 2 * rp.bytes;
   const uint64_t chunk = ((total / rp.n_chunks) + 15) & ~uint64_t(15);
   const uint32_t linear_cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
   const uint32_t n_ctas = gridDim.x * gridDim.y * gridDim.z;
   for (uint32_t c = linear_cta; c < rp.n_chunks; c += n_ctas) {
-    const uint64_t b = uint64_t(c) * chunk;
-    const uint64_t e = b + chunk < total ? b + chunk : total;
+    const uint64_t cb = uint64_t(c) * chunk;
+    const uint64_t ce = cb + chunk < total ? cb + chunk : total;
+    const uint64_t part = (((ce > cb ? ce - cb : 0) / kPushWarps) + 15) & ~uint64_t(15);
+    const uint64_t b0 = cb + uint64_t(sub) * part;
+    const uint64_t b = b0 < ce ? b0 : ce;
+    const uint64_t e = b + part < ce ? b + part : ce;
     // Copy [b, e) of the virtual concatenation K | V, 16 bytes per lane, 8 in flight.
     for (uint64_t off = b + uint64_t(lane) * 16; off < e; off += 32 * 16 * 8) {
       uint4 r[8];
@@ -140,7 +123,7 @@ __device__ void ring_push_warp(const RingPush& rp, const RingConsume& rc, uint32
       red_release_sys_add(rp.peer_arrivals, 1u);
     }
   }
-  if (lane == 0) trace_slots[5] = globaltimer();
+  if (lane == 0 && sub == 0) trace_slots[5] = globaltimer();
 }
 
 // ------------------------------------------------------------------ kernel
@@ -322,10 +305,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       AbortState drain_ab{&never, nullptr, p.wait_limit_ns};
       mbar_wait(&s.drain, 0, drain_ab, 0);
     }
-  } else if (warp == 10) {
+  } else if (warp >= 10) {
     // ------------------------------------------------------------ ring push
     if (p.push.enabled)
-      ring_push_warp(p.push, p.consume, p.status, p.wait_limit_ns, &s.abort_flag, s.trace);
+      ring_push_warp(p.push, p.consume, p.status, p.wait_limit_ns, &s.abort_flag, s.trace,
+                     int(warp) - 10);
   } else {
     // ------------------------------------------------------------ softmax + epilogue
     const int t = warp >> 2;                // query tile within the CTA

@@ -8,7 +8,7 @@
 namespace mgfa {
 
 // Optional in-kernel ring transport for one ring step: while the CTAs compute
-// on the current KV shard, one warp per CTA pushes a slice of that shard into
+// on the current KV shard, two warps per CTA push a slice of that shard into
 // the right neighbour's receive slot with 16-byte stores through the peer
 // mapping, then bumps the neighbour's arrival counter (release, system scope).
 struct RingPush {
@@ -20,7 +20,9 @@ struct RingPush {
   uint32_t* peer_arrivals = nullptr;  // right neighbour's arrival counter for that slot
   const uint32_t* credit = nullptr;   // local: right neighbour's uses of that slot finished
   uint32_t credit_target = 0;         // wait until *credit >= credit_target before writing
-  uint32_t n_chunks = 0;              // chunks the shard is cut into (same on every rank)
+  uint32_t n_chunks = 0;              // chunks the shard is cut into (same on every rank);
+                                      // CTAs with linear index < n_chunks push one each,
+                                      // signalled in kFwdPushParts parts
   int enabled = 0;
   int drop_signal = 0;                // fault injection for tests: chunk 0 is copied but
                                       // never signalled, so the receiver's wait must expire
@@ -70,6 +72,7 @@ struct FwdParams {
 };
 
 constexpr int kTraceWords = 8;
+constexpr int kFwdPushParts = 2;  // push warps per CTA (arrivals per chunk)
 
 // Host helpers (flash_fwd_sm100.cu).
 // Tensor map of a [B, S, H, 128] bf16 tensor with the given element strides.

@@ -331,6 +331,30 @@ __device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
   return f2_pack(__uint_as_float(__float_as_uint(p0) + e0), __uint_as_float(__float_as_uint(p1) + e1));
 }
 
+// Number of leading entries of the non-decreasing `pos[0..n)` that are <= `limit`
+// (every shard layout lists its key tiles in increasing global position, so the
+// key tiles a query tile can see form a prefix). Warp-cooperative; every lane
+// returns the result.
+__device__ __forceinline__ int visible_prefix(const int* pos, int n, int limit) {
+  const uint32_t lane = lane_id();
+  int lo = 0, hi = n;  // answer in [lo, hi]
+  while (hi - lo > 0) {
+    const int span = hi - lo;
+    const int step = (span + 31) / 32;
+    const int idx = lo + int(lane) * step;
+    const bool le = idx < hi && __ldg(pos + idx) <= limit;
+    const uint32_t m = __ballot_sync(0xffffffffu, le);
+    const int cnt = __popc(m);  // probes [0, cnt) are <= limit
+    if (cnt == 0) return lo;    // pos[lo] > limit
+    if (step == 1) return lo + cnt;
+    const int new_lo = lo + (cnt - 1) * step + 1;
+    const int new_hi = lo + cnt * step < hi ? lo + cnt * step : hi;
+    lo = new_lo;
+    hi = new_hi;
+  }
+  return lo;
+}
+
 // ---------------------------------------------------------------- flags (system scope)
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
