@@ -1,0 +1,60 @@
+"""Record the fused ring kernel's per-CTA timeline for one forward call.
+
+    torchrun --nproc-per-node N -m multi_gpu_flashattention_b200.benchmarks.ring_trace \
+        [--seq 131072] [--heads 32] [--out DIR]
+
+After 3 untraced calls, one traced call writes DIR/summary_rank<r>.json (per
+step: wall span, longest wait for the KV shard, mean push time per pushing
+CTA) and DIR/trace_rank0.json (Chrome trace of rank 0)."""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+import torch.distributed as dist
+
+from ..parallel.layouts import RingLayout
+from ..parallel.ring import ENGINES, ring_attention_forward
+from ..utils.trace import summarize, to_chrome_events, write_chrome_trace
+from . import common
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--seq", type=int, default=131072)
+    ap.add_argument("--heads", type=int, default=32)
+    ap.add_argument("--layout", default="zigzag")
+    ap.add_argument("--out", default="ring_trace")
+    a = ap.parse_args()
+    ctx = common.init(need_world_gt1=True)
+    lay = RingLayout(a.layout, a.seq, ctx.world, mask="causal")
+    L = lay.max_local_len
+    g = torch.Generator(device=ctx.device).manual_seed(ctx.rank)
+    mk = lambda: (torch.randn(1, L, a.heads, 128, device=ctx.device, generator=g) * 0.5).bfloat16()
+    q, k, v = mk(), mk(), mk()
+    for _ in range(3):
+        ring_attention_forward(q, k, v, lay, causal=True, backend="fused", check=True)
+    eng = ENGINES.get(None, ctx.device, k.numel() * 2)
+    eng.set_trace(True)
+    torch.cuda.synchronize()
+    ctx.barrier()
+    ring_attention_forward(q, k, v, lay, causal=True, backend="fused", check=True)
+    torch.cuda.synchronize()
+    eng.set_trace(False)
+    tr = eng.last_trace().cpu()
+    os.makedirs(a.out, exist_ok=True)
+    summ = summarize(tr)
+    with open(os.path.join(a.out, f"summary_rank{ctx.rank}.json"), "w") as f:
+        json.dump(summ, f, indent=1)
+    if ctx.rank == 0:
+        write_chrome_trace(to_chrome_events(tr, ctx.rank), os.path.join(a.out, "trace_rank0.json"))
+        print(json.dumps(summ), flush=True)
+    ENGINES.clear()
+    ctx.close()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
