@@ -194,6 +194,8 @@ class RingEngine {
         // target is the same number.
         p.push.n_chunks = push_chunks(grid);
         p.push.drop_signal = (drop_signal_step_ == t) ? 1 : 0;
+        p.push.peer_tag = buf_.flag(right, comm::kTag0 + sn);
+        p.push.tag = slot_tag(owner, calls_);
       }
       if (transport && t > 0) {
         p.consume.enabled = 1;
@@ -203,6 +205,8 @@ class RingEngine {
         p.consume.done_target = uint32_t(grid - 1);
         p.consume.left_credit = buf_.flag(left, comm::kCredit0 + s);
         p.consume.left_credit_value = uses_[s] + 1;
+        p.consume.tag = buf_.flag(r, comm::kTag0 + s);
+        p.consume.expected_tag = slot_tag(owner, calls_);
       }
       if (trace_)
         p.trace = reinterpret_cast<uint64_t*>(last_trace_.data_ptr<int64_t>()) +
@@ -214,8 +218,11 @@ class RingEngine {
       nvtxRangePop();
       if (transport && t > 0) uses_[s] += 1;
     }
+    if (transport) calls_ += 1;
     return {o, lse};
   }
+
+  static uint32_t slot_tag(int owner, uint32_t call) { return uint32_t(owner + 1) | (call << 8); }
 
  public:
 
@@ -224,6 +231,16 @@ class RingEngine {
   void set_trace(bool on) { trace_ = on; }
   // Programmatic dependent launch between ring steps (on by default).
   void set_dependent_launch(bool on) { pdl_ = on; }
+  // Debug: NaN-fill this rank's receive slots (on the current stream), so that a
+  // read racing ahead of its data shows up as NaNs in the next call's output.
+  // Call only while the ring is quiescent on every rank (all ranks synchronised
+  // and past a barrier; barrier again before the next call).
+  void poison_slots() {
+    c10::cuda::CUDAGuard guard(buf_.device());
+    C10_CUDA_CHECK(cudaMemsetAsync(buf_.payload(buf_.rank()), 0xFF,
+                                   size_t(2 * kSlots) * slot_bytes_,
+                                   at::cuda::getCurrentCUDAStream()));
+  }
   torch::Tensor last_trace() const { return last_trace_; }
 
   // Fault injection for tests (off by default): at ring step `step` of the next
@@ -234,6 +251,7 @@ class RingEngine {
   void reset() {
     buf_.reset_flags(at::cuda::getCurrentCUDAStream());
     for (auto& u : uses_) u = 0;
+    calls_ = 0;
   }
 
  private:
@@ -245,6 +263,7 @@ class RingEngine {
   int drop_signal_step_ = -1;
   bool trace_ = false;
   bool pdl_ = true;
+  uint32_t calls_ = 0;
   int num_sms_ = 148;
   torch::Tensor last_trace_;
 };
@@ -261,6 +280,7 @@ void register_ring_engine(py::module& m) {
       .def("set_drop_signal_step", &RingEngine::set_drop_signal_step)
       .def("set_trace", &RingEngine::set_trace)
       .def("set_dependent_launch", &RingEngine::set_dependent_launch)
+      .def("poison_slots", &RingEngine::poison_slots)
       .def("last_trace", &RingEngine::last_trace)
       .def("forward", &RingEngine::forward, py::arg("q"), py::arg("k"), py::arg("v"),
            py::arg("scale"), py::arg("causal"), py::arg("q_tile_pos"), py::arg("kv_tile_pos"),

@@ -28,6 +28,7 @@ enum FlagIndex : int {
   kArrivals0 = 0,   // chunks of slot s received (written by the left neighbour)
   kCredit0 = 4,     // uses of the right neighbour's slot s it finished (written by it)
   kDone0 = 8,       // CTAs of this rank finished with slot s in the current step
+  kTag0 = 12,       // owner tag of the data in slot s (written by the left neighbour)
   kStatus = 16,     // device error word of the last call
 };
 

@@ -85,6 +85,9 @@ __device__ void ring_push_warp(const RingPush& rp, const RingConsume& rc, uint32
   __syncwarp();
   if (*abort_flag) return;
   if (lane == 0 && sub == 0) trace_slots[4] = globaltimer();
+  // The slot's owner tag: written (same value by every pushing CTA) before any
+  // arrival signal, so a consumer that saw all arrivals also sees the tag.
+  if (lane == 0 && rp.peer_tag) *reinterpret_cast<volatile uint32_t*>(rp.peer_tag) = rp.tag;
   const uint64_t total = 2 * rp.bytes;
   const uint64_t chunk = ((total / rp.n_chunks) + 15) & ~uint64_t(15);
   const uint32_t linear_cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
@@ -207,6 +210,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = wait_flag_geq(p.consume.arrivals, p.consume.arrivals_target, p.wait_limit_ns,
                            p.status, 8, 0);
         if (!ok) s.abort_flag = 1;
+        // The shard must be the one this step expects (owner and call).
+        if (ok && p.consume.tag && ld_acquire_sys(p.consume.tag) != p.consume.expected_tag) {
+          record_error(p.status, kErrTagMismatch, 8, 0);
+          s.abort_flag = 1;
+          ok = false;
+        }
         // Data written by peers' generic stores, read here by the async proxy.
         asm volatile("fence.proxy.async.global;" ::: "memory");
       }

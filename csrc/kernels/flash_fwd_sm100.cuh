@@ -26,6 +26,8 @@ struct RingPush {
   int enabled = 0;
   int drop_signal = 0;                // fault injection for tests: chunk 0 is copied but
                                       // never signalled, so the receiver's wait must expire
+  uint32_t* peer_tag = nullptr;       // right neighbour's tag word for that slot
+  uint32_t tag = 0;                   // (owner + 1) | (call << 8): written before signalling
 };
 
 // Consumer side of one ring step.
@@ -38,6 +40,8 @@ struct RingConsume {
                                        // resets the counter to 0
   uint32_t* left_credit = nullptr;     // left neighbour's credit word for this slot
   uint32_t left_credit_value = 0;      // value the last CTA publishes
+  const uint32_t* tag = nullptr;       // tag word of the slot being read
+  uint32_t expected_tag = 0;           // must match once the shard has arrived
   int enabled = 0;
 };
 

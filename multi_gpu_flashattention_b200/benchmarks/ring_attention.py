@@ -47,7 +47,14 @@ def parse():
     ap.add_argument("--backend", default=None, choices=["fused", "nccl", "staged"])
     ap.add_argument("--numerics", default="fp32", choices=["fp32", "bf16"])
     ap.add_argument("--init", default="legacy", choices=["legacy", "randn"])
-    ap.add_argument("--layout", default="contiguous", choices=["contiguous", "zigzag", "striped"])
+    ap.add_argument("--layout", default="contiguous",
+                    choices=["contiguous", "zigzag", "striped", "scheduler"])
+    ap.add_argument("--policy", default="dp", choices=["dp", "lpt"],
+                    help="scheduler layout: contiguous-row DP or row LPT partition")
+    ap.add_argument("--dump-format", default="bin", choices=["bin", "npy", "pt"],
+                    help="with ATTENTION_DUMP_OUTPUT: raw fp32 (reference format), or .npy / .pt "
+                         "with the output and the fp32 LSE")
+    ap.add_argument("--json", action="store_true", help="also print one JSON summary line")
     ap.add_argument("--causal", action="store_true")
     ap.add_argument("--heads", type=int, default=1)
     ap.add_argument("--kv-heads", type=int, default=0)
@@ -269,6 +276,7 @@ class Bf16Ring:
                                           cpu_group=ctx.cpu_group)
         e1.record()
         host = out[0].float().cpu()
+        self.lse = lse[0].cpu()
         e2.record()
         torch.cuda.synchronize()
         total = e0.elapsed_time(e2)
@@ -321,7 +329,8 @@ def main():
         return 1
     L = args.kv_size // unit
     seq = L * P
-    lay = RingLayout(args.layout, seq, P, mask="causal" if args.causal else "full")
+    lay = RingLayout(args.layout, seq, P, mask="causal" if args.causal else "full",
+                     policy=args.policy)
     props = torch.cuda.get_device_properties(dev)
     lr = int(os.environ.get("LOCAL_RANK", r))
     ctx.log(f"[Rank {r} local_rank {lr}] GPU {dev.index}: {props.name} "
@@ -357,9 +366,33 @@ def main():
         print(f"avg_total={sums[0] / n:.3f} ms avg_{comm}={sums[1] / n:.3f} "
               f"avg_attn={sums[2] / n:.3f} avg_merge={sums[3] / n:.3f} avg_final={sums[4] / n:.3f}",
               flush=True)
+    if r == 0 and args.json:
+        n = args.iters
+        S_tot = lay.seq
+        pairs = S_tot * (S_tot + 1) // 2 if args.causal else S_tot * S_tot
+        flops = 4.0 * D * H * pairs
+        ms = sums[0] / n
+        import json as _json
+        print(_json.dumps({"backend": name, "numerics": args.numerics, "ranks": P,
+                           "seq": S_tot, "heads": H, "head_dim": D, "causal": args.causal,
+                           "layout": args.layout, "avg_total_ms": ms,
+                           "avg_comm_ms": sums[1] / n, "avg_attn_ms": sums[2] / n,
+                           "tflops_per_gpu": flops / (ms * 1e-3) / 1e12 / P,
+                           "comm_fraction": (sums[1] / n) / ms if ms > 0 else None}), flush=True)
     if os.environ.get("ATTENTION_DUMP_OUTPUT") is not None:
-        fname = f"ring_output_rank{r}.bin"
-        host.contiguous().numpy().astype("<f4").tofile(fname)
+        lse = getattr(ring, "lse", None)
+        if args.dump_format == "bin":
+            fname = f"ring_output_rank{r}.bin"
+            host.contiguous().numpy().astype("<f4").tofile(fname)
+        elif args.dump_format == "npy":
+            import numpy as np
+            fname = f"ring_output_rank{r}.npy"
+            np.save(fname, host.contiguous().numpy().astype("<f4"))
+            if lse is not None:
+                np.save(f"ring_lse_rank{r}.npy", lse.numpy().astype("<f4"))
+        else:
+            fname = f"ring_output_rank{r}.pt"
+            torch.save({"out": host, "lse": lse, "positions": lay.positions(r)}, fname)
         ctx.log(f"[Rank {r}] output dumped to {fname}")
     ctx.close()
     return 0

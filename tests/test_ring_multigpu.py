@@ -101,3 +101,29 @@ def _trace_case(rank, world):
 
 def test_ring_forward_trace_records_timeline():
     run_ranks(_trace_case, _world(), backend="nccl")
+
+
+def _poison_case(rank, world):
+    """NaN-poisoned receive slots must never leak into the output (no read races
+    ahead of its data), and every slot carries the right owner tag."""
+    from multi_gpu_flashattention_b200.parallel.layouts import RingLayout
+    from multi_gpu_flashattention_b200.parallel.ring import ENGINES, ring_attention_forward
+    dev = torch.device("cuda", rank)
+    lay = RingLayout("zigzag", 8192, world, mask="causal")
+    g = torch.Generator(device=dev).manual_seed(rank)
+    q = (torch.randn(1, lay.max_local_len, 4, 128, device=dev, generator=g) * 0.5).bfloat16()
+    ref, _ = ring_attention_forward(q, q, q, lay, causal=True, backend="fused", check=True)
+    eng = ENGINES.get(None, dev, q.numel() * 2)
+    for _ in range(3):
+        torch.cuda.synchronize()
+        torch.distributed.barrier()
+        eng.poison_slots()
+        torch.cuda.synchronize()
+        torch.distributed.barrier()
+        out, _ = ring_attention_forward(q, q, q, lay, causal=True, backend="fused", check=True)
+        assert torch.isfinite(out.float()).all()
+        torch.testing.assert_close(out, ref, rtol=0, atol=0)
+
+
+def test_ring_forward_poisoned_slots_and_tags():
+    run_ranks(_poison_case, _world(), backend="nccl")
