@@ -30,6 +30,8 @@ enum FlagIndex : int {
   kDone0 = 8,       // CTAs of this rank finished with slot s in the current step
   kTag0 = 12,       // owner tag of the data in slot s (written by the left neighbour)
   kStatus = 16,     // device error word of the last call
+  kHomeArrivals = 20,  // backward: final dK/dV of this rank's shard arrived (CTA count)
+  kHomeCredit = 21,    // backward: right neighbour's finished uses of its home buffer
 };
 
 class SymmetricBuffer {

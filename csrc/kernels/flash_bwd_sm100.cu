@@ -24,6 +24,7 @@
 
 #include "flash_bwd_sm100.cuh"
 #include "sm100_ptx.cuh"
+#include "ring_push.cuh"
 
 namespace mgfa {
 namespace {
@@ -100,7 +101,6 @@ struct __align__(1024) DqSmem {
   uint32_t abort_flag;
 };
 
-
 __global__ void __launch_bounds__(kThreads, 1)
     flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap map_q,
                         const __grid_constant__ CUtensorMap map_do,
@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int q_tile_pos = p.causal ? __ldg(p.q_tile_pos + qt) : 0;
   const int n_active = p.causal ? visible_prefix(p.kv_tile_pos, p.n_kv_tiles, q_tile_pos + (kTile - 1))
                                 : p.n_kv_tiles;
-  if (n_active == 0 && p.accumulate) return;  // nothing to add
+  if (n_active == 0 && p.accumulate && !p.consume.enabled) return;  // nothing to add
 
   AbortState ab{&s.abort_flag, p.status, p.wait_limit_ns};
   if (warp == 0) tmem_alloc<512>(&s.tmem_base);
@@ -317,6 +317,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc<512>(tmem);
+  if (p.consume.enabled && p.consume.done_counter && threadIdx.x == 0) {
+    // the dQ kernel is the last reader of this step's slot: the last CTA re-arms
+    // it and hands it back to the left neighbour
+    __threadfence();
+    const uint32_t prev = atomicAdd(p.consume.done_counter, 1u);
+    if (prev == p.consume.done_target) {
+      *p.consume.done_counter = 0u;
+      *p.consume.arrivals = 0u;
+      fence_sys();
+      st_release_sys(p.consume.left_credit, p.consume.left_credit_value);
+    }
+  }
 }
 
 // ====================================================================== dK / dV
@@ -330,12 +342,12 @@ struct __align__(1024) DkvSmem {
   uint64_t kv_full;
   uint64_t qd_full[2], qd_empty[2];
   uint64_t s_full, dp_full, p_full, ds_full, dkv_full, drain;
+  uint64_t trace[8];
   uint32_t tmem_base;
   uint32_t abort_flag;
 };
 
-
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kDkdvThreads, 1)
     flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap map_q,
                           const __grid_constant__ CUtensorMap map_do,
                           const __grid_constant__ CUtensorMap map_k,
@@ -352,7 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int q_lo = p.causal ? visible_prefix(p.q_tile_pos, p.n_q_tiles, kv_tile_pos - kTile) : 0;
   const int n_q_active = p.n_q_tiles - q_lo;
   const int n_iter = n_q_active * G;
-  if (n_iter == 0 && p.accumulate) return;
+  if (n_iter == 0 && p.accumulate && !p.ring.enabled && !p.push.enabled) return;
 
   AbortState ab{&s.abort_flag, p.status, p.wait_limit_ns};
   if (warp == 0) tmem_alloc<512>(&s.tmem_base);
@@ -379,12 +391,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 4) {
     if (lane == 0 && n_iter > 0) {
-      mbar_arrive_expect_tx(&s.kv_full, 2 * kTileBytes);
-      load_tile(s.k, &map_k, &s.kv_full, hk, j * kTile, b);
-      load_tile(s.v, &map_v, &s.kv_full, hk, j * kTile, b);
+      bool ok = true;
+      if (p.consume.enabled) {  // K/V (and accumulators) of this step arrived?
+        ok = wait_flag_geq(p.consume.arrivals, p.consume.arrivals_target, p.wait_limit_ns,
+                           p.status, 70, 0);
+        if (ok && p.consume.tag && ld_acquire_sys(p.consume.tag) != p.consume.expected_tag) {
+          record_error(p.status, kErrTagMismatch, 70, 0);
+          ok = false;
+        }
+        if (!ok) s.abort_flag = 1;
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+      }
+      const bool kv_issued = ok;
+      if (ok) {
+        mbar_arrive_expect_tx(&s.kv_full, 2 * kTileBytes);
+        load_tile(s.k, &map_k, &s.kv_full, hk, j * kTile, b);
+        load_tile(s.v, &map_v, &s.kv_full, hk, j * kTile, b);
+      }
       int it = 0;
       int last[2] = {-1, -1};
-      bool ok = true;
       for (int g = 0; ok && g < G; ++g) {
         const int h = hk * G + g;
         const int64_t mlbase = (int64_t(b) * p.hq + h) * p.sq_pad;
@@ -403,7 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       volatile uint32_t never = 0;
       AbortState dab{&never, nullptr, p.wait_limit_ns};
-      mbar_wait(&s.kv_full, 0, dab, 0);
+      if (kv_issued) mbar_wait(&s.kv_full, 0, dab, 0);
       for (int st = 0; st < 2; ++st)
         if (last[st] >= 0) mbar_wait(&s.qd_full[st], uint32_t(last[st]), dab, 0);
     }
@@ -467,6 +492,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       AbortState dab{&never, nullptr, p.wait_limit_ns};
       mbar_wait(&s.drain, 0, dab, 0);
     }
+  } else if (warp >= 6) {
+    if (p.push.enabled)
+      ring_push_warp(p.push, p.consume, p.status, p.wait_limit_ns, &s.abort_flag, s.trace,
+                     int(warp) - 6);
   } else if (warp < 4) {
     const int r = threadIdx.x;  // key row within the tile == TMEM lane
     const uint32_t lane_off = uint32_t(warp * 32) << 16;
@@ -553,9 +582,56 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < 128; ++c) acc[c] = 0u;
     }
-    if (key_valid && ok) store_grad_row(p.dv + off, acc, 1.f, p.accumulate != 0);
-    if (n_iter > 0 && ok) tmem_ld128(tmem + lane_off + DK_COL, acc);
-    if (key_valid && ok) store_grad_row(p.dk + off, acc, p.scale, p.accumulate != 0);
+    if (!p.ring.enabled) {
+      if (key_valid && ok) store_grad_row(p.dv + off, acc, 1.f, p.accumulate != 0);
+      if (n_iter > 0 && ok) tmem_ld128(tmem + lane_off + DK_COL, acc);
+      if (key_valid && ok) store_grad_row(p.dk + off, acc, p.scale, p.accumulate != 0);
+    } else {
+      // ring: out = incoming accumulator + this rank's contribution, stored into
+      // the right neighbour's buffer once it is free
+      volatile uint32_t* abort_flag = &s.abort_flag;
+      if (lane == 0 && ok) {
+        // the incoming accumulators must have arrived (a CTA without work gets
+        // here before its neighbour is done) and the destination must be free
+        if (p.consume.enabled &&
+            !wait_flag_geq(p.consume.arrivals, p.consume.arrivals_target, p.wait_limit_ns,
+                           p.status, 94, 0))
+          *abort_flag = 1;
+        if (!*abort_flag && !wait_flag_geq(p.ring.acc_credit, p.ring.acc_credit_target,
+                                           p.wait_limit_ns, p.status, 93, 0))
+          *abort_flag = 1;
+      }
+      __syncwarp();
+      ok = __all_sync(0xffffffffu, ok && *abort_flag == 0);
+      auto add_store = [&](float* dst, const float* src, float mul) {
+        float4* d = reinterpret_cast<float4*>(dst + off);
+        const float4* a = src ? reinterpret_cast<const float4*>(src + off) : nullptr;
+#pragma unroll
+        for (int q4 = 0; q4 < 32; ++q4) {
+          float4 v = make_float4(__uint_as_float(acc[4 * q4]) * mul,
+                                 __uint_as_float(acc[4 * q4 + 1]) * mul,
+                                 __uint_as_float(acc[4 * q4 + 2]) * mul,
+                                 __uint_as_float(acc[4 * q4 + 3]) * mul);
+          if (a) {
+            const float4 o = a[q4];
+            v.x += o.x;
+            v.y += o.y;
+            v.z += o.z;
+            v.w += o.w;
+          }
+          d[q4] = v;
+        }
+      };
+      if (key_valid && ok) add_store(p.ring.acc_out_dv, p.ring.acc_in_dv, 1.f);
+      if (n_iter > 0 && ok) tmem_ld128(tmem + lane_off + DK_COL, acc);
+      if (key_valid && ok) add_store(p.ring.acc_out_dk, p.ring.acc_in_dk, p.scale);
+      // all four epilogue warps stored their rows: signal the neighbour once
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (threadIdx.x == 0 && ok) {
+        fence_sys();
+        red_release_sys_add(p.ring.acc_arrivals, 1u);
+      }
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -628,7 +704,7 @@ void flash_bwd_dkdv_launch(const CUtensorMap& mq, const CUtensorMap& mdo, const 
   static int done_dev = -1;
   set_smem<DkvSmem>(flash_bwd_dkdv_kernel, done_dev);
   dim3 grid(p.n_kv_tiles, p.hkv, p.batch);
-  flash_bwd_dkdv_kernel<<<grid, kThreads, sizeof(DkvSmem) + 1024, stream>>>(mq, mdo, mk, mv, p);
+  flash_bwd_dkdv_kernel<<<grid, kDkdvThreads, sizeof(DkvSmem) + 1024, stream>>>(mq, mdo, mk, mv, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -675,8 +751,8 @@ cudaError_t flash_bwd_kernels_raw(const CUtensorMap& mq, const CUtensorMap& mdo,
   e = cudaFuncSetAttribute(flash_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            int(sizeof(DqSmem) + 1024));
   if (e != cudaSuccess) return e;
-  flash_bwd_dkdv_kernel<<<dim3(p.n_kv_tiles, p.hkv, p.batch), kThreads, sizeof(DkvSmem) + 1024,
-                          stream>>>(mq, mdo, mk, mv, p);
+  flash_bwd_dkdv_kernel<<<dim3(p.n_kv_tiles, p.hkv, p.batch), kDkdvThreads,
+                          sizeof(DkvSmem) + 1024, stream>>>(mq, mdo, mk, mv, p);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   flash_bwd_dq_kernel<<<dim3(p.n_q_tiles, p.hq, p.batch), kThreads, sizeof(DqSmem) + 1024,
                         stream>>>(mq, mdo, mk, mv, p);

@@ -4,7 +4,25 @@
 #include <cuda.h>
 #include <cstdint>
 
+#include "flash_fwd_sm100.cuh"  // RingPush / RingConsume
+
 namespace mgfa {
+
+// Fused ring transport of the backward pass (dK/dV kernel side): the incoming
+// accumulators of the current KV owner are read from this rank's receive slot,
+// this rank's contribution is added, and the sum is stored straight into the
+// right neighbour's slot (or, after the last step, its home buffer) through the
+// peer mapping; one release-add per CTA signals the neighbour.
+struct BwdRing {
+  const float* acc_in_dk = nullptr;   // incoming accumulators (local), null = zeros
+  const float* acc_in_dv = nullptr;
+  float* acc_out_dk = nullptr;        // destination (peer memory)
+  float* acc_out_dv = nullptr;
+  uint32_t* acc_arrivals = nullptr;   // right neighbour's arrival counter of the destination
+  const uint32_t* acc_credit = nullptr;  // local: right's finished uses of the destination
+  uint32_t acc_credit_target = 0;
+  int enabled = 0;
+};
 
 struct BwdParams {
   int batch = 1, hq = 1, hkv = 1;
@@ -27,7 +45,14 @@ struct BwdParams {
   int accumulate = 0;
   uint32_t* status = nullptr;
   uint64_t wait_limit_ns = 2000000000ull;
+  // fused ring transport (dK/dV kernel: push K/V + move accumulators; dQ kernel:
+  // release the slot through consume.done_counter / left_credit)
+  RingPush push;
+  RingConsume consume;
+  BwdRing ring;
 };
+
+constexpr int kDkdvThreads = 256;  // 4 softmax, TMA, MMA, 2 push warps
 
 CUtensorMap make_bshd_map(const void* base, int64_t B, int64_t S, int64_t H,
                           int64_t stride_b, int64_t stride_s, int64_t stride_h);

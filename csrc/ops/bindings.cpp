@@ -17,6 +17,7 @@ void legacy_normalize(torch::Tensor acc, torch::Tensor l, torch::Tensor out,
                       c10::optional<torch::Tensor> lse, c10::optional<torch::Tensor> m);
 void register_ring_engine(py::module& m);
 void register_ring_exchange(py::module& m);
+void register_ring_bwd_engine(py::module& m);
 torch::Tensor fwd_timeout_probe(torch::Tensor q, torch::Tensor k, torch::Tensor v,
                                 int64_t wait_limit_ns);
 void flash_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
@@ -53,4 +54,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "forward launch whose arrival flag is never set (bounded-wait failure path)");
   mgfa::register_ring_engine(m);
   mgfa::register_ring_exchange(m);
+  mgfa::register_ring_bwd_engine(m);
 }

@@ -7,9 +7,11 @@ owner (r - t) mod P's accumulators and passes shard + accumulators on; after
 P steps each accumulator holds every rank's contribution and takes one last
 hop to its owner. dQ accumulates locally.
 
-Backends: "nccl" (and "fused", which currently shares the NCCL transport for
-the backward) move the payload with NCCL send/recv on a side stream overlapped
-with the sm_100a kernels; "torch" is the fp32 PyTorch oracle on any device.
+Backends: "fused" (default on CUDA) runs the native RingBwdEngine: the dK/dV
+kernel pushes K/V to the right neighbour and stores the updated accumulators
+straight into its receive slot over NVLink (see csrc/comm/ring_bwd_engine.cpp);
+"nccl" is the baseline that moves K/V and the accumulators with NCCL send/recv
+on a side stream; "torch" is the fp32 PyTorch oracle on any device.
 """
 from __future__ import annotations
 
@@ -60,6 +62,8 @@ def ring_attention_backward(dout, q, k, v, out, lse, layout: RingLayout, causal:
         dv_full[:, :kv_lens[0]] = dv
         return dq.to(q.dtype), dk_full.to(k.dtype), dv_full.to(v.dtype)
 
+    if backend in (None, "fused"):
+        return _bwd_fused(dout, q, k, v, out, lse, causal, scale, group, qtp, kvtp, kv_lens)
     right, left = _global(group, (rank + 1) % world), _global(group, (rank - 1) % world)
     lse2, delta = C().flash_bwd_preprocess(dout, out, lse)
     compute = torch.cuda.current_stream(q.device)
@@ -141,3 +145,53 @@ def _bwd_torch(dout, q, k, v, layout, causal, scale, group):
         dist.all_reduce(dk_all, group=group)
         dist.all_reduce(dv_all, group=group)
     return dq.to(q.dtype), dk_all[rank].to(k.dtype), dv_all[rank].to(v.dtype)
+
+
+class _BwdEngines:
+    """One native RingBwdEngine per (process group, device); creation is collective."""
+
+    def __init__(self):
+        self._by_key = {}
+
+    def get(self, group, device, kv_bytes):
+        rank, world = _world(group)
+        key = (id(group), device.index)
+        eng = self._by_key.get(key)
+        if eng is not None and eng.kv_bytes() >= kv_bytes:
+            return eng
+        if eng is not None:
+            torch.cuda.synchronize(device)
+            dist.barrier(group)
+            self._by_key.pop(key)
+            del eng
+        size = max(kv_bytes, 1 << 20)
+        size = (size + (2 << 20) - 1) // (2 << 20) * (2 << 20)
+        eng = C().RingBwdEngine(rank, world, device.index, size, 0)
+        handles = [None] * world
+        dist.all_gather_object(handles, eng.ipc_handle(), group=group)
+        eng.connect(handles)
+        torch.cuda.synchronize(device)
+        dist.barrier(group)
+        self._by_key[key] = eng
+        return eng
+
+    def clear(self):
+        self._by_key.clear()
+
+
+BWD_ENGINES = _BwdEngines()
+
+
+def _bwd_fused(dout, q, k, v, out, lse, causal, scale, group, qtp, kvtp, kv_lens,
+               status=None, wait_limit_ns=2_000_000_000):
+    rank, world = _world(group)
+    eng = BWD_ENGINES.get(group, q.device, k.numel() * k.element_size())
+    st = status if status is not None else torch.zeros(1, dtype=torch.int32, device=q.device)
+    dq, dk, dv = eng.backward(dout, q.contiguous(), k.contiguous(), v.contiguous(), out.contiguous(),
+                              lse, scale, causal, qtp if causal else None,
+                              kvtp if causal else None, kv_lens, st, int(wait_limit_ns))
+    kl = kv_lens[rank]
+    if kl < k.shape[1]:  # padding rows of a shorter shard carry no gradient
+        dk[:, kl:].zero_()
+        dv[:, kl:].zero_()
+    return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype)

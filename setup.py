@@ -55,6 +55,7 @@ if which in ("all", "cuda"):
                 "csrc/comm/symmetric.cpp",
                 "csrc/comm/ring_engine.cpp",
                 "csrc/comm/ring_exchange.cpp",
+                "csrc/comm/ring_bwd_engine.cpp",
                 "csrc/kernels/ring_exchange.cu",
             ],
             include_dirs=[os.path.join(ROOT, "csrc")],

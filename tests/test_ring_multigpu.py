@@ -47,7 +47,7 @@ def test_ring_forward_scheduler_layout_fused():
     run_ranks(_case, _world(), "scheduler", True, "fused", 4096, 2, 2, 2, backend="nccl")
 
 
-def _bwd_case(rank, world, kind, causal):
+def _bwd_case(rank, world, kind, causal, bwd_backend="nccl"):
     from multi_gpu_flashattention_b200.parallel.layouts import RingLayout
     from multi_gpu_flashattention_b200.parallel.ring import ring_attention_forward
     from multi_gpu_flashattention_b200.parallel.ring_bwd import ring_attention_backward
@@ -60,7 +60,7 @@ def _bwd_case(rank, world, kind, causal):
     ql, kl, vl, dol = (lay.shard(t, rank) for t in (q, k, v, do))
     out, lse = ring_attention_forward(ql, kl, vl, lay, causal=causal, backend="fused", check=True)
     dq, dk, dv = ring_attention_backward(dol, ql, kl, vl, out, lse, lay, causal=causal,
-                                         backend="nccl")
+                                         backend=bwd_backend)
     rq, rk, rv = ring_attention_backward(dol, ql, kl, vl, out, lse, lay, causal=causal,
                                          backend="torch")
     n = lay.local_len(rank)
@@ -70,10 +70,33 @@ def _bwd_case(rank, world, kind, causal):
         assert err <= 3e-2 * b.abs().max().item() + 1e-3, (rank, name, err)
 
 
+@pytest.mark.parametrize("bwd_backend", ["fused", "nccl"])
 @pytest.mark.parametrize("kind,causal", [("zigzag", True), ("contiguous", False),
                                          ("striped", True)])
-def test_ring_backward_matches_reference(kind, causal):
-    run_ranks(_bwd_case, _world(), kind, causal, backend="nccl")
+def test_ring_backward_matches_reference(kind, causal, bwd_backend):
+    run_ranks(_bwd_case, _world(), kind, causal, bwd_backend, backend="nccl")
+
+
+def _bwd_repeat_case(rank, world):
+    """Repeated fused backward calls reuse slots, home buffer and flags."""
+    from multi_gpu_flashattention_b200.parallel.layouts import RingLayout
+    from multi_gpu_flashattention_b200.parallel.ring import ring_attention_forward
+    from multi_gpu_flashattention_b200.parallel.ring_bwd import ring_attention_backward
+    dev = torch.device("cuda", rank)
+    lay = RingLayout("zigzag", 4096, world, mask="causal")
+    g = torch.Generator(device=dev).manual_seed(17 + rank)
+    mk = lambda h: (torch.randn(1, lay.max_local_len, h, 128, device=dev, generator=g) * 0.5).bfloat16()
+    q, k, v, do = mk(4), mk(2), mk(2), mk(4)
+    out, lse = ring_attention_forward(q, k, v, lay, causal=True, backend="fused", check=True)
+    ref = ring_attention_backward(do, q, k, v, out, lse, lay, causal=True, backend="fused")
+    for _ in range(3):
+        got = ring_attention_backward(do, q, k, v, out, lse, lay, causal=True, backend="fused")
+        for a, b in zip(got, ref):
+            torch.testing.assert_close(a, b, rtol=0, atol=0)
+
+
+def test_ring_backward_fused_repeated_calls():
+    run_ranks(_bwd_repeat_case, _world(), backend="nccl")
 
 
 def _trace_case(rank, world):
