@@ -15,6 +15,7 @@
 // holds this rank's complete dK/dV (fp32), which are converted to bf16 before
 // the home buffer is handed back. Slots are triple-buffered as in the forward.
 #include <torch/extension.h>
+#include "../common/check.hpp"
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
@@ -39,7 +40,7 @@ class RingBwdEngine {
         slot_bytes_(6 * kv_bytes_),
         buf_(size_t(kSlots) * 6 * kv_bytes_ + 4 * kv_bytes_, rank, world, device),
         n_chunks_(n_chunks) {
-    TORCH_CHECK(kv_bytes > 0, "kv_bytes must be positive");
+    MGFA_CHECK(kv_bytes > 0, "kv_bytes must be positive");
     C10_CUDA_CHECK(cudaDeviceGetAttribute(&num_sms_, cudaDevAttrMultiProcessorCount, device));
   }
 
@@ -63,20 +64,23 @@ class RingBwdEngine {
                                       c10::optional<torch::Tensor> kv_tile_pos,
                                       std::vector<int64_t> kv_lens, torch::Tensor status,
                                       int64_t wait_limit_ns) {
-    TORCH_CHECK(buf_.connected(), "RingBwdEngine.connect() was not called");
+    MGFA_CHECK(buf_.connected(), "RingBwdEngine.connect() was not called");
+    const int64_t D = q.size(3);
+    const bool f16 = q.scalar_type() == at::kHalf;
     for (auto* t : {&dout, &q, &k, &v, &out})
-      TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->is_contiguous() &&
-                      t->dim() == 4 && t->size(3) == 128,
-                  "dout/q/k/v/out must be contiguous bf16 [B,S,H,128]");
+      MGFA_CHECK(t->is_cuda() && t->scalar_type() == q.scalar_type() &&
+                      (q.scalar_type() == at::kBFloat16 || f16) && t->is_contiguous() &&
+                      t->dim() == 4 && t->size(3) == D && (D == 64 || D == 128),
+                  "dout/q/k/v/out must be contiguous bf16/fp16 [B,S,H,64|128] of one dtype");
     const int P = buf_.world(), r = buf_.rank();
     const int right = (r + 1) % P, left = (r - 1 + P) % P;
     const int64_t B = q.size(0), Sq = q.size(1), Hq = q.size(2), L = k.size(1), Hkv = k.size(2);
-    const size_t kvb = size_t(B * L * Hkv * 128 * 2);
-    TORCH_CHECK(kvb <= kv_bytes_, "KV shard exceeds the engine's buffers");
-    TORCH_CHECK(int64_t(kv_lens.size()) == P, "kv_lens needs one entry per rank");
+    const size_t kvb = size_t(B * L * Hkv * D * 2);
+    MGFA_CHECK(kvb <= kv_bytes_, "KV shard exceeds the engine's buffers");
+    MGFA_CHECK(int64_t(kv_lens.size()) == P, "kv_lens needs one entry per rank");
     const int n_q_tiles = int((Sq + 127) / 128), n_kv_tiles = int((L + 127) / 128);
     if (causal)
-      TORCH_CHECK(q_tile_pos.has_value() && kv_tile_pos.has_value() &&
+      MGFA_CHECK(q_tile_pos.has_value() && kv_tile_pos.has_value() &&
                       kv_tile_pos->size(0) == P && kv_tile_pos->size(1) >= n_kv_tiles,
                   "causal needs q_tile_pos and kv_tile_pos [P, n_kv_tiles]");
     c10::cuda::CUDAGuard guard(q.device());
@@ -89,13 +93,13 @@ class RingBwdEngine {
     flash_bwd_preprocess_launch(out.data_ptr(), dout.data_ptr(), out.stride(0), out.stride(1),
                                 dout.stride(0), dout.stride(1), lse.data_ptr<float>(), int(B),
                                 int(Sq), int(Hq), sq_pad, lse2.data_ptr<float>(),
-                                delta.data_ptr<float>(), stream);
+                                delta.data_ptr<float>(), stream, int(D), f16);
     auto dq = torch::empty(q.sizes(), f32);
 
-    const int64_t sb = L * Hkv * 128, ss = Hkv * 128;
-    const int64_t qsb = Sq * Hq * 128, qss = Hq * 128;
-    const CUtensorMap mq = make_bshd_map(q.data_ptr(), B, Sq, Hq, qsb, qss, 128);
-    const CUtensorMap mdo = make_bshd_map(dout.data_ptr(), B, Sq, Hq, qsb, qss, 128);
+    const int64_t sb = L * Hkv * D, ss = Hkv * D;
+    const int64_t qsb = Sq * Hq * D, qss = Hq * D;
+    const CUtensorMap mq = make_bshd_map_dt(q.data_ptr(), B, Sq, Hq, qsb, qss, D, int(D), f16);
+    const CUtensorMap mdo = make_bshd_map_dt(dout.data_ptr(), B, Sq, Hq, qsb, qss, D, int(D), f16);
     auto slot = [&](int rank, int s) { return buf_.payload(rank) + size_t(s) * slot_bytes_; };
     auto home = [&](int rank) { return buf_.payload(rank) + size_t(kSlots) * slot_bytes_; };
     const int dkdv_grid = n_kv_tiles * int(Hkv) * int(B);
@@ -110,10 +114,12 @@ class RingBwdEngine {
       const bool own = t == 0;
       const uint8_t* cur_k = own ? static_cast<const uint8_t*>(k.data_ptr()) : slot(r, s);
       const uint8_t* cur_v = own ? static_cast<const uint8_t*>(v.data_ptr()) : slot(r, s) + kv_bytes_;
-      const CUtensorMap mk = make_bshd_map(cur_k, B, L, Hkv, sb, ss, 128);
-      const CUtensorMap mv = make_bshd_map(cur_v, B, L, Hkv, sb, ss, 128);
+      const CUtensorMap mk = make_bshd_map_dt(cur_k, B, L, Hkv, sb, ss, D, int(D), f16);
+      const CUtensorMap mv = make_bshd_map_dt(cur_v, B, L, Hkv, sb, ss, D, int(D), f16);
 
       BwdParams p;
+      p.head_dim = int(D);
+      p.fp16 = f16 ? 1 : 0;
       p.batch = int(B);
       p.hq = int(Hq);
       p.hkv = int(Hkv);
@@ -203,8 +209,8 @@ class RingBwdEngine {
     hc.left_credit_value = home_uses_ + 1;
     C10_CUDA_CHECK(ring_wait_launch(none, hc, st, uint64_t(wait_limit_ns), stream));
     auto opts = torch::TensorOptions().dtype(torch::kFloat).device(q.device());
-    auto hk = torch::from_blob(home(r), {B, L, Hkv, 128}, opts);
-    auto hv = torch::from_blob(home(r) + 2 * kv_bytes_, {B, L, Hkv, 128}, opts);
+    auto hk = torch::from_blob(home(r), {B, L, Hkv, D}, opts);
+    auto hv = torch::from_blob(home(r) + 2 * kv_bytes_, {B, L, Hkv, D}, opts);
     auto dk = hk.clone();
     auto dv = hv.clone();
     C10_CUDA_CHECK(ring_signal_launch(none, hc, stream));  // hand the home buffer back

@@ -24,6 +24,7 @@
 // All ranks call forward() in the same order, so the per-slot use counts kept
 // on the host agree everywhere.
 #include <torch/extension.h>
+#include "../common/check.hpp"
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
@@ -43,7 +44,7 @@ class RingEngine {
       : buf_(size_t(2 * kSlots * slot_bytes), rank, world, device),
         slot_bytes_(size_t(slot_bytes)),
         n_chunks_(n_chunks) {
-    TORCH_CHECK(slot_bytes > 0 && slot_bytes % 4096 == 0, "slot_bytes must be a multiple of 4096");
+    MGFA_CHECK(slot_bytes > 0 && slot_bytes % 4096 == 0, "slot_bytes must be a multiple of 4096");
     // n_chunks: > 0 fixed, 0 two waves of CTAs, < 0 one chunk per CTA
     C10_CUDA_CHECK(cudaDeviceGetAttribute(&num_sms_, cudaDevAttrMultiProcessorCount, device));
   }
@@ -98,27 +99,30 @@ class RingEngine {
                                  c10::optional<torch::Tensor> kv_tile_pos,
                                  std::vector<int64_t> kv_lens, torch::Tensor status,
                                  int64_t wait_limit_ns, bool transport) {
-    TORCH_CHECK(buf_.connected() || buf_.world() == 1, "RingEngine.connect() was not called");
-    TORCH_CHECK(q.is_cuda() && q.scalar_type() == at::kBFloat16 && q.dim() == 4 &&
-                    q.size(3) == 128 && q.is_contiguous(),
-                "q must be a contiguous bf16 [B,S,H,128] CUDA tensor");
-    TORCH_CHECK(k.scalar_type() == at::kBFloat16 && k.is_contiguous() && v.is_contiguous() &&
-                    k.sizes() == v.sizes() && k.dim() == 4 && k.size(3) == 128,
-                "k and v must be contiguous bf16 [B,L,Hkv,128] tensors of equal shape");
+    MGFA_CHECK(buf_.connected() || buf_.world() == 1, "RingEngine.connect() was not called");
+    MGFA_CHECK(q.is_cuda() && (q.scalar_type() == at::kBFloat16 || q.scalar_type() == at::kHalf) &&
+                    q.dim() == 4 && (q.size(3) == 128 || q.size(3) == 64) && q.is_contiguous(),
+                "q must be a contiguous bf16/fp16 [B,S,H,64|128] CUDA tensor");
+    MGFA_CHECK(k.scalar_type() == q.scalar_type() && v.scalar_type() == q.scalar_type() &&
+                    k.is_contiguous() && v.is_contiguous() && k.sizes() == v.sizes() &&
+                    k.dim() == 4 && k.size(3) == q.size(3),
+                "k and v must be contiguous tensors like q, [B,L,Hkv,D], of equal shape");
     const int P = buf_.world(), r = buf_.rank();
     const int right = (r + 1) % P, left = (r - 1 + P) % P;
     const int64_t B = q.size(0), Sq = q.size(1), Hq = q.size(2), L = k.size(1), Hkv = k.size(2);
-    TORCH_CHECK(Hq % Hkv == 0, "query heads must be a multiple of kv heads");
-    const size_t shard_bytes = size_t(B * L * Hkv * 128 * 2);
-    TORCH_CHECK(P == 1 || shard_bytes <= slot_bytes_, "KV shard (", shard_bytes,
+    const int64_t D = q.size(3);
+    const bool f16 = q.scalar_type() == at::kHalf;
+    MGFA_CHECK(Hq % Hkv == 0, "query heads must be a multiple of kv heads");
+    const size_t shard_bytes = size_t(B * L * Hkv * D * 2);
+    MGFA_CHECK(P == 1 || shard_bytes <= slot_bytes_, "KV shard (", shard_bytes,
                 " B) exceeds the engine's slot (", slot_bytes_, " B)");
-    TORCH_CHECK(int64_t(kv_lens.size()) == P, "kv_lens needs one entry per rank");
+    MGFA_CHECK(int64_t(kv_lens.size()) == P, "kv_lens needs one entry per rank");
     const int n_q_tiles = int((Sq + 127) / 128), n_kv_tiles = int((L + 127) / 128);
     if (causal) {
-      TORCH_CHECK(q_tile_pos.has_value() && q_tile_pos->scalar_type() == at::kInt &&
+      MGFA_CHECK(q_tile_pos.has_value() && q_tile_pos->scalar_type() == at::kInt &&
                       q_tile_pos->numel() >= n_q_tiles,
                   "causal ring attention needs int32 q_tile_pos");
-      TORCH_CHECK(kv_tile_pos.has_value() && kv_tile_pos->scalar_type() == at::kInt &&
+      MGFA_CHECK(kv_tile_pos.has_value() && kv_tile_pos->scalar_type() == at::kInt &&
                       kv_tile_pos->is_contiguous() && kv_tile_pos->dim() == 2 &&
                       kv_tile_pos->size(0) == P && kv_tile_pos->size(1) >= n_kv_tiles,
                   "causal ring attention needs int32 kv_tile_pos [P, n_kv_tiles]");
@@ -131,9 +135,9 @@ class RingEngine {
     torch::Tensor o_state;
     if (P > 1) o_state = torch::empty(q.sizes(), q.options().dtype(at::kFloat));
 
-    const CUtensorMap mq = make_bshd_map(q.data_ptr(), B, Sq, Hq, q.stride(0), q.stride(1),
-                                         q.stride(2));
-    const int64_t sb = L * Hkv * 128, ss = Hkv * 128, sh = 128;
+    const CUtensorMap mq = make_bshd_map_dt(q.data_ptr(), B, Sq, Hq, q.stride(0), q.stride(1),
+                                            q.stride(2), int(D), f16);
+    const int64_t sb = L * Hkv * D, ss = Hkv * D, sh = D;
     auto slot_k = [&](int rank, int s) { return buf_.payload(rank) + size_t(s) * 2 * slot_bytes_; };
     auto slot_v = [&](int rank, int s) { return slot_k(rank, s) + slot_bytes_; };
     const int grid = flash_fwd_grid_ctas(int(Hq), n_q_tiles, int(B));
@@ -147,10 +151,12 @@ class RingEngine {
       const bool own = t == 0 || !transport;
       const uint8_t* cur_k = own ? static_cast<const uint8_t*>(k.data_ptr()) : slot_k(r, s);
       const uint8_t* cur_v = own ? static_cast<const uint8_t*>(v.data_ptr()) : slot_v(r, s);
-      const CUtensorMap mk = make_bshd_map(cur_k, B, L, Hkv, sb, ss, sh);
-      const CUtensorMap mv = make_bshd_map(cur_v, B, L, Hkv, sb, ss, sh);
+      const CUtensorMap mk = make_bshd_map_dt(cur_k, B, L, Hkv, sb, ss, sh, int(D), f16);
+      const CUtensorMap mv = make_bshd_map_dt(cur_v, B, L, Hkv, sb, ss, sh, int(D), f16);
 
       FwdParams p;
+      p.head_dim = int(D);
+      p.fp16 = f16 ? 1 : 0;
       p.batch = int(B);
       p.hq = int(Hq);
       p.hkv = int(Hkv);

@@ -6,6 +6,7 @@
 //          mapping, flag-signal kernel
 // The schedule and flags match the fused attention engine (ring_engine.cpp).
 #include <torch/extension.h>
+#include "../common/check.hpp"
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
@@ -29,7 +30,7 @@ class RingExchange {
       : buf_(size_t(2 * slot_bytes), rank, world, device),
         slot_bytes_(size_t(slot_bytes)),
         n_ctas_(n_ctas) {
-    TORCH_CHECK(slot_bytes > 0 && slot_bytes % 32 == 0, "slot_bytes must be a multiple of 32");
+    MGFA_CHECK(slot_bytes > 0 && slot_bytes % 32 == 0, "slot_bytes must be a multiple of 32");
   }
 
   py::bytes ipc_handle() const { return py::bytes(buf_.ipc_handle()); }
@@ -46,8 +47,8 @@ class RingExchange {
   // neighbour's slot (t+1)%2. `bytes` <= slot_bytes (multiple of 32).
   void step(int t, int64_t bytes, const std::string& transport, torch::Tensor status,
             int64_t wait_limit_ns) {
-    TORCH_CHECK(buf_.connected(), "RingExchange.connect() was not called");
-    TORCH_CHECK(bytes > 0 && size_t(bytes) <= slot_bytes_ && bytes % 32 == 0, "bad byte count");
+    MGFA_CHECK(buf_.connected(), "RingExchange.connect() was not called");
+    MGFA_CHECK(bytes > 0 && size_t(bytes) <= slot_bytes_ && bytes % 32 == 0, "bad byte count");
     const int P = buf_.world(), r = buf_.rank();
     const int right = (r + 1) % P, left = (r - 1 + P) % P;
     const int s = t & 1, sn = (t + 1) & 1;
@@ -85,7 +86,7 @@ class RingExchange {
                                      cudaMemcpyDeviceToDevice, stream));
       C10_CUDA_CHECK(ring_signal_launch(push, consume, stream));
     } else {
-      TORCH_CHECK(false, "transport must be p2p or ce");
+      MGFA_CHECK(false, "transport must be p2p or ce");
     }
     if (t > 0) uses_[s] += 1;
   }

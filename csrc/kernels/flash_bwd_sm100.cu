@@ -18,6 +18,7 @@
 // tensor pipe runs a thread's MMAs in order).
 // The reference prototype has no backward pass at all.
 #include <torch/extension.h>
+#include "../common/check.hpp"
 #include <ATen/cuda/CUDAContext.h>
 
 #include <cmath>
@@ -32,8 +33,7 @@ namespace {
 using namespace mgfa::dev;
 
 constexpr int kTile = 128;
-constexpr int kHalfBytes = kTile * 64 * 2;
-constexpr int kTileBytes = 2 * kHalfBytes;
+constexpr int kHalfBytes = kTile * 64 * 2;  // one 128 x 64 16-bit swizzled box
 constexpr int kThreads = 192;  // 4 softmax warps, 1 TMA warp, 1 MMA warp
 
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes,
@@ -45,11 +45,12 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint
       : "memory");
 }
 
+template <int kD>
 __device__ __forceinline__ void load_tile(void* dst, const CUtensorMap* m, uint64_t* bar, int h,
                                           int row, int b) {
   uint8_t* d = static_cast<uint8_t*>(dst);
-  tma_load_4d(d, m, bar, 0, h, row, b);
-  tma_load_4d(d + kHalfBytes, m, bar, 64, h, row, b);
+#pragma unroll
+  for (int hf = 0; hf < kD / 64; ++hf) tma_load_4d(d + hf * kHalfBytes, m, bar, hf * 64, h, row, b);
 }
 
 // K-major 128x128 operand (two 64-column swizzled halves), k-step kk of 16.
@@ -61,19 +62,23 @@ __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t base, int kk) {
   return make_sdesc_sw128(base + kk * 2048, kHalfBytes, 1024);
 }
 
-__device__ __forceinline__ void tmem_ld128(uint32_t addr, uint32_t (&r)[128]) {
-  tmem_ld32(addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-  tmem_ld32(addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-  tmem_ld32(addr + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[64]));
-  tmem_ld32(addr + 96, *reinterpret_cast<uint32_t(*)[32]>(&r[96]));
+template <int kN>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t addr, uint32_t (&r)[kN]) {
+#pragma unroll
+  for (int c = 0; c < kN; c += 32) tmem_ld32(addr + c, *reinterpret_cast<uint32_t(*)[32]>(&r[c]));
   tmem_wait_ld();
 }
 
-__device__ __forceinline__ void store_grad_row(float* dst, const uint32_t (&acc)[128], float mul,
+__device__ __forceinline__ void tmem_ld128(uint32_t addr, uint32_t (&r)[128]) {
+  tmem_ld_cols<128>(addr, r);
+}
+
+template <int kD>
+__device__ __forceinline__ void store_grad_row(float* dst, const uint32_t (&acc)[kD], float mul,
                                                bool accumulate) {
   float4* d = reinterpret_cast<float4*>(dst);
 #pragma unroll
-  for (int q4 = 0; q4 < 32; ++q4) {
+  for (int q4 = 0; q4 < kD / 4; ++q4) {
     float4 v = make_float4(__uint_as_float(acc[4 * q4]) * mul, __uint_as_float(acc[4 * q4 + 1]) * mul,
                            __uint_as_float(acc[4 * q4 + 2]) * mul,
                            __uint_as_float(acc[4 * q4 + 3]) * mul);
@@ -89,11 +94,12 @@ __device__ __forceinline__ void store_grad_row(float* dst, const uint32_t (&acc)
 }
 
 // ====================================================================== dQ
+template <int kD>
 struct __align__(1024) DqSmem {
-  __nv_bfloat16 q[kTile * 128];
-  __nv_bfloat16 dout[kTile * 128];
-  __nv_bfloat16 k[2][kTile * 128];
-  __nv_bfloat16 v[2][kTile * 128];
+  uint16_t q[kTile * kD];
+  uint16_t dout[kTile * kD];
+  uint16_t k[2][kTile * kD];
+  uint16_t v[2][kTile * kD];
   uint64_t qd_full;
   uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
   uint64_t s_full, s_free, dp_full, ds_full, dq_full, drain;
@@ -101,14 +107,16 @@ struct __align__(1024) DqSmem {
   uint32_t abort_flag;
 };
 
+template <int kD, bool kF16>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap map_q,
                         const __grid_constant__ CUtensorMap map_do,
                         const __grid_constant__ CUtensorMap map_k,
                         const __grid_constant__ CUtensorMap map_v, const BwdParams p) {
+  constexpr int kTileBytes = (kD / 64) * kHalfBytes;
   extern __shared__ uint8_t smem_raw[];
-  DqSmem& s = *reinterpret_cast<DqSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                         ~uintptr_t(1023));
+  DqSmem<kD>& s = *reinterpret_cast<DqSmem<kD>*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t warp = warp_id(), lane = lane_id();
   // query tiles vary fastest: resident CTAs share one head's K/V in L2
   const int qt = gridDim.x - 1 - blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -147,8 +155,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 4) {
     if (lane == 0 && n_active > 0) {
       mbar_arrive_expect_tx(&s.qd_full, 2 * kTileBytes);
-      load_tile(s.q, &map_q, &s.qd_full, h, qt * kTile, b);
-      load_tile(s.dout, &map_do, &s.qd_full, h, qt * kTile, b);
+      load_tile<kD>(s.q, &map_q, &s.qd_full, h, qt * kTile, b);
+      load_tile<kD>(s.dout, &map_do, &s.qd_full, h, qt * kTile, b);
       int it = 0;
       int last_k[2] = {-1, -1}, last_v[2] = {-1, -1};
       for (int j = 0; j < n_active; ++j) {
@@ -156,11 +164,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t ph = (it >> 1) & 1;
         if (!mbar_wait(&s.k_empty[st], ph ^ 1, ab, 41)) break;
         mbar_arrive_expect_tx(&s.k_full[st], kTileBytes);
-        load_tile(s.k[st], &map_k, &s.k_full[st], hk, j * kTile, b);
+        load_tile<kD>(s.k[st], &map_k, &s.k_full[st], hk, j * kTile, b);
         last_k[st] = int(ph);
         if (!mbar_wait(&s.v_empty[st], ph ^ 1, ab, 42)) break;
         mbar_arrive_expect_tx(&s.v_full[st], kTileBytes);
-        load_tile(s.v[st], &map_v, &s.v_full[st], hk, j * kTile, b);
+        load_tile<kD>(s.v[st], &map_v, &s.v_full[st], hk, j * kTile, b);
         last_v[st] = int(ph);
         ++it;
       }
@@ -174,19 +182,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 5) {
     if (lane == 0 && n_active > 0) {
-      const uint32_t idesc_ss = make_idesc_bf16(128, 128, 0, 0);
-      const uint32_t idesc_ts = make_idesc_bf16(128, 128, 0, 1);
+      const uint32_t idesc_ss = make_idesc_16(128, 128, 0, 0, kF16);
+      const uint32_t idesc_ts = make_idesc_16(128, kD, 0, 1, kF16);
       const uint32_t qb = smem_u32(s.q), db = smem_u32(s.dout);
       auto gemm_s = [&](int st) {
         const uint32_t kb = smem_u32(s.k[st]);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
+        for (int kk = 0; kk < kD / 16; ++kk)
           mma_ss(tmem + S_COL, kmajor_desc(qb, kk), kmajor_desc(kb, kk), idesc_ss, kk > 0);
       };
       auto gemm_dp = [&](int st) {
         const uint32_t vb = smem_u32(s.v[st]);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
+        for (int kk = 0; kk < kD / 16; ++kk)
           mma_ss(tmem + DP_COL, kmajor_desc(db, kk), kmajor_desc(vb, kk), idesc_ss, kk > 0);
       };
       bool ok = mbar_wait(&s.qd_full, 0, ab, 50) && mbar_wait(&s.k_full[0], 0, ab, 51);
@@ -287,7 +295,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 16; ++c) {
           const float d0 = pr[ch * 32 + 2 * c] * (__uint_as_float(dpr[2 * c]) - dlt);
           const float d1 = pr[ch * 32 + 2 * c + 1] * (__uint_as_float(dpr[2 * c + 1]) - dlt);
-          pk[c] = pack_bf16(d0, d1);
+          pk[c] = pack16<kF16>(d0, d1);
         }
         // dS over the first 64 columns of the dP region (column ch*16.. holds
         // keys ch*32 .. ch*32+31); the chunk just read is never overwritten before
@@ -302,17 +310,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (n_active > 0 && ok) ok = __all_sync(0xffffffffu, mbar_wait(&s.dq_full, 0, ab, 62));
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
-    uint32_t acc[128];
+    uint32_t acc[kD];
     if (n_active > 0 && ok) {
-      tmem_ld128(tmem + lane_off + DQ_COL, acc);
+      tmem_ld_cols<kD>(tmem + lane_off + DQ_COL, acc);
     } else {
 #pragma unroll
-      for (int c = 0; c < 128; ++c) acc[c] = 0u;
+      for (int c = 0; c < kD; ++c) acc[c] = 0u;
     }
     if (row_valid && ok)
-      store_grad_row(p.dq + int64_t(b) * p.dq_batch_stride + int64_t(row) * p.dq_row_stride +
-                         int64_t(h) * 128,
-                     acc, p.scale, p.accumulate != 0);
+      store_grad_row<kD>(p.dq + int64_t(b) * p.dq_batch_stride + int64_t(row) * p.dq_row_stride +
+                             int64_t(h) * kD,
+                         acc, p.scale, p.accumulate != 0);
   }
   tc_fence_before();
   __syncthreads();
@@ -332,11 +340,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ====================================================================== dK / dV
+template <int kD>
 struct __align__(1024) DkvSmem {
-  __nv_bfloat16 k[kTile * 128];
-  __nv_bfloat16 v[kTile * 128];
-  __nv_bfloat16 q[2][kTile * 128];
-  __nv_bfloat16 dout[2][kTile * 128];
+  uint16_t k[kTile * kD];
+  uint16_t v[kTile * kD];
+  uint16_t q[2][kTile * kD];
+  uint16_t dout[2][kTile * kD];
   float lse2[2][kTile];
   float delta[2][kTile];
   uint64_t kv_full;
@@ -347,14 +356,16 @@ struct __align__(1024) DkvSmem {
   uint32_t abort_flag;
 };
 
+template <int kD, bool kF16>
 __global__ void __launch_bounds__(kDkdvThreads, 1)
     flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap map_q,
                           const __grid_constant__ CUtensorMap map_do,
                           const __grid_constant__ CUtensorMap map_k,
                           const __grid_constant__ CUtensorMap map_v, const BwdParams p) {
+  constexpr int kTileBytes = (kD / 64) * kHalfBytes;
   extern __shared__ uint8_t smem_raw[];
-  DkvSmem& s = *reinterpret_cast<DkvSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                           ~uintptr_t(1023));
+  DkvSmem<kD>& s = *reinterpret_cast<DkvSmem<kD>*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t warp = warp_id(), lane = lane_id();
   // key tiles vary fastest: resident CTAs share the group's Q/dO stream in L2
   const int j = gridDim.x - 1 - blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
@@ -387,7 +398,7 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
-  const uint32_t ST_COL = 0, DPT_COL = 128, DV_COL = 256, DK_COL = 384;
+  const uint32_t ST_COL = 0, DPT_COL = 128, DV_COL = 256, DK_COL = 256 + kD;
 
   if (warp == 4) {
     if (lane == 0 && n_iter > 0) {
@@ -405,8 +416,8 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
       const bool kv_issued = ok;
       if (ok) {
         mbar_arrive_expect_tx(&s.kv_full, 2 * kTileBytes);
-        load_tile(s.k, &map_k, &s.kv_full, hk, j * kTile, b);
-        load_tile(s.v, &map_v, &s.kv_full, hk, j * kTile, b);
+        load_tile<kD>(s.k, &map_k, &s.kv_full, hk, j * kTile, b);
+        load_tile<kD>(s.v, &map_v, &s.kv_full, hk, j * kTile, b);
       }
       int it = 0;
       int last[2] = {-1, -1};
@@ -418,8 +429,8 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
           const uint32_t ph = (it >> 1) & 1;
           if (!(ok = mbar_wait(&s.qd_empty[st], ph ^ 1, ab, 71))) break;
           mbar_arrive_expect_tx(&s.qd_full[st], 2 * kTileBytes + 2 * kTile * 4);
-          load_tile(s.q[st], &map_q, &s.qd_full[st], h, qt * kTile, b);
-          load_tile(s.dout[st], &map_do, &s.qd_full[st], h, qt * kTile, b);
+          load_tile<kD>(s.q[st], &map_q, &s.qd_full[st], h, qt * kTile, b);
+          load_tile<kD>(s.dout[st], &map_do, &s.qd_full[st], h, qt * kTile, b);
           bulk_load(s.lse2[st], p.lse2 + mlbase + qt * kTile, kTile * 4, &s.qd_full[st]);
           bulk_load(s.delta[st], p.delta + mlbase + qt * kTile, kTile * 4, &s.qd_full[st]);
           last[st] = int(ph);
@@ -434,19 +445,19 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
     }
   } else if (warp == 5) {
     if (lane == 0 && n_iter > 0) {
-      const uint32_t idesc_ss = make_idesc_bf16(128, 128, 0, 0);
-      const uint32_t idesc_ts = make_idesc_bf16(128, 128, 0, 1);
+      const uint32_t idesc_ss = make_idesc_16(128, 128, 0, 0, kF16);
+      const uint32_t idesc_ts = make_idesc_16(128, kD, 0, 1, kF16);
       const uint32_t kb = smem_u32(s.k), vb = smem_u32(s.v);
       auto gemm_st = [&](int st) {
         const uint32_t qb = smem_u32(s.q[st]);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
+        for (int kk = 0; kk < kD / 16; ++kk)
           mma_ss(tmem + ST_COL, kmajor_desc(kb, kk), kmajor_desc(qb, kk), idesc_ss, kk > 0);
       };
       auto gemm_dpt = [&](int st) {
         const uint32_t db = smem_u32(s.dout[st]);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
+        for (int kk = 0; kk < kD / 16; ++kk)
           mma_ss(tmem + DPT_COL, kmajor_desc(vb, kk), kmajor_desc(db, kk), idesc_ss, kk > 0);
       };
       bool ok = mbar_wait(&s.kv_full, 0, ab, 80) && mbar_wait(&s.qd_full[0], 0, ab, 81);
@@ -539,7 +550,7 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
         }
         uint32_t pk[64];
 #pragma unroll
-        for (int c = 0; c < 64; ++c) pk[c] = pack_bf16(pr[2 * c], pr[2 * c + 1]);
+        for (int c = 0; c < 64; ++c) pk[c] = pack16<kF16>(pr[2 * c], pr[2 * c + 1]);
         tmem_st32(tmem + lane_off + ST_COL, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
         tmem_st32(tmem + lane_off + ST_COL + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
         tmem_wait_st();
@@ -560,7 +571,7 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
             const int c0 = ch * 32 + 2 * c;
             const float d0 = pr[c0] * (__uint_as_float(dpr[2 * c]) - dl[c0]);
             const float d1 = pr[c0 + 1] * (__uint_as_float(dpr[2 * c + 1]) - dl[c0 + 1]);
-            dk[c] = pack_bf16(d0, d1);
+            dk[c] = pack16<kF16>(d0, d1);
           }
           tmem_st16(tmem + lane_off + DPT_COL + ch * 16, dk);
         }
@@ -573,19 +584,19 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
     if (n_iter > 0 && ok) ok = __all_sync(0xffffffffu, mbar_wait(&s.dkv_full, 0, ab, 92));
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
-    uint32_t acc[128];
+    uint32_t acc[kD];
     const int64_t off = int64_t(b) * p.dkv_batch_stride + int64_t(key) * p.dkv_row_stride +
-                        int64_t(hk) * 128;
+                        int64_t(hk) * kD;
     if (n_iter > 0 && ok) {
-      tmem_ld128(tmem + lane_off + DV_COL, acc);
+      tmem_ld_cols<kD>(tmem + lane_off + DV_COL, acc);
     } else {
 #pragma unroll
-      for (int c = 0; c < 128; ++c) acc[c] = 0u;
+      for (int c = 0; c < kD; ++c) acc[c] = 0u;
     }
     if (!p.ring.enabled) {
-      if (key_valid && ok) store_grad_row(p.dv + off, acc, 1.f, p.accumulate != 0);
-      if (n_iter > 0 && ok) tmem_ld128(tmem + lane_off + DK_COL, acc);
-      if (key_valid && ok) store_grad_row(p.dk + off, acc, p.scale, p.accumulate != 0);
+      if (key_valid && ok) store_grad_row<kD>(p.dv + off, acc, 1.f, p.accumulate != 0);
+      if (n_iter > 0 && ok) tmem_ld_cols<kD>(tmem + lane_off + DK_COL, acc);
+      if (key_valid && ok) store_grad_row<kD>(p.dk + off, acc, p.scale, p.accumulate != 0);
     } else {
       // ring: out = incoming accumulator + this rank's contribution, stored into
       // the right neighbour's buffer once it is free
@@ -607,7 +618,7 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
         float4* d = reinterpret_cast<float4*>(dst + off);
         const float4* a = src ? reinterpret_cast<const float4*>(src + off) : nullptr;
 #pragma unroll
-        for (int q4 = 0; q4 < 32; ++q4) {
+        for (int q4 = 0; q4 < kD / 4; ++q4) {
           float4 v = make_float4(__uint_as_float(acc[4 * q4]) * mul,
                                  __uint_as_float(acc[4 * q4 + 1]) * mul,
                                  __uint_as_float(acc[4 * q4 + 2]) * mul,
@@ -623,7 +634,7 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
         }
       };
       if (key_valid && ok) add_store(p.ring.acc_out_dv, p.ring.acc_in_dv, 1.f);
-      if (n_iter > 0 && ok) tmem_ld128(tmem + lane_off + DK_COL, acc);
+      if (n_iter > 0 && ok) tmem_ld_cols<kD>(tmem + lane_off + DK_COL, acc);
       if (key_valid && ok) add_store(p.ring.acc_out_dk, p.ring.acc_in_dk, p.scale);
       // all four epilogue warps stored their rows: signal the neighbour once
       asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -639,12 +650,14 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
 }
 
 // ====================================================================== preprocess
-__global__ void bwd_preprocess_kernel(const __nv_bfloat16* __restrict__ o,
-                                      const __nv_bfloat16* __restrict__ dout, int64_t o_sb,
+template <int kD, bool kF16>
+__global__ void bwd_preprocess_kernel(const uint16_t* __restrict__ o,
+                                      const uint16_t* __restrict__ dout, int64_t o_sb,
                                       int64_t o_ss, int64_t do_sb, int64_t do_ss,
                                       const float* __restrict__ lse, int S, int H, int s_pad,
                                       float* __restrict__ lse2, float* __restrict__ delta) {
-  // one warp per (b, h, row); row in [0, s_pad)
+  // one warp per (b, h, row); row in [0, s_pad); lane handles kD / 32 elements
+  constexpr int kPer = kD / 32;
   const int64_t wid = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (wid >= int64_t(H) * s_pad) return;
@@ -654,15 +667,12 @@ __global__ void bwd_preprocess_kernel(const __nv_bfloat16* __restrict__ o,
   float acc = 0.f;
   float l2 = INFINITY;
   if (row < S) {
-    const __nv_bfloat16* op = o + b * o_sb + int64_t(row) * o_ss + int64_t(h) * 128;
-    const __nv_bfloat16* dp = dout + b * do_sb + int64_t(row) * do_ss + int64_t(h) * 128;
-    const uint2 ov = reinterpret_cast<const uint2*>(op)[lane];
-    const uint2 dv = reinterpret_cast<const uint2*>(dp)[lane];
-    const __nv_bfloat162* o2 = reinterpret_cast<const __nv_bfloat162*>(&ov);
-    const __nv_bfloat162* d2 = reinterpret_cast<const __nv_bfloat162*>(&dv);
+    const uint16_t* op = o + b * o_sb + int64_t(row) * o_ss + int64_t(h) * kD + lane * kPer;
+    const uint16_t* dp = dout + b * do_sb + int64_t(row) * do_ss + int64_t(h) * kD + lane * kPer;
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const float2 a = __bfloat1622float2(o2[i]), c = __bfloat1622float2(d2[i]);
+    for (int i = 0; i < kPer; i += 2) {
+      const float2 a = unpack16<kF16>(*reinterpret_cast<const uint32_t*>(op + i));
+      const float2 c = unpack16<kF16>(*reinterpret_cast<const uint32_t*>(dp + i));
       acc += a.x * c.x + a.y * c.y;
     }
     const float lv = lse[(int64_t(b) * H + h) * S + row];
@@ -677,55 +687,90 @@ __global__ void bwd_preprocess_kernel(const __nv_bfloat16* __restrict__ o,
   }
 }
 
-template <class Smem, class Kernel>
-void set_smem(Kernel k, int& done_dev) {
+template <class Kernel>
+void set_smem(Kernel k, int smem, int& done_dev) {
   int dev = 0;
   C10_CUDA_CHECK(cudaGetDevice(&dev));
   if (done_dev != dev) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        int(sizeof(Smem) + 1024)));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     done_dev = dev;
   }
 }
 
+template <int kD, bool kF16>
+void launch_dq(const CUtensorMap& mq, const CUtensorMap& mdo, const CUtensorMap& mk,
+               const CUtensorMap& mv, const BwdParams& p, cudaStream_t stream) {
+  static int done_dev = -1;
+  const int smem = int(sizeof(DqSmem<kD>) + 1024);
+  set_smem(flash_bwd_dq_kernel<kD, kF16>, smem, done_dev);
+  flash_bwd_dq_kernel<kD, kF16><<<dim3(p.n_q_tiles, p.hq, p.batch), kThreads, smem, stream>>>(
+      mq, mdo, mk, mv, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+template <int kD, bool kF16>
+void launch_dkdv(const CUtensorMap& mq, const CUtensorMap& mdo, const CUtensorMap& mk,
+                 const CUtensorMap& mv, const BwdParams& p, cudaStream_t stream) {
+  static int done_dev = -1;
+  const int smem = int(sizeof(DkvSmem<kD>) + 1024);
+  set_smem(flash_bwd_dkdv_kernel<kD, kF16>, smem, done_dev);
+  flash_bwd_dkdv_kernel<kD, kF16><<<dim3(p.n_kv_tiles, p.hkv, p.batch), kDkdvThreads, smem,
+                                    stream>>>(mq, mdo, mk, mv, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+template <int kD, bool kF16>
+void launch_preprocess(const void* o, const void* dout, int64_t o_sb, int64_t o_ss, int64_t do_sb,
+                       int64_t do_ss, const float* lse, int B, int S, int H, int s_pad,
+                       float* lse2, float* delta, cudaStream_t stream) {
+  const int64_t warps = int64_t(H) * s_pad;
+  const int threads = 256;
+  dim3 grid(unsigned((warps * 32 + threads - 1) / threads), B);
+  bwd_preprocess_kernel<kD, kF16><<<grid, threads, 0, stream>>>(
+      static_cast<const uint16_t*>(o), static_cast<const uint16_t*>(dout), o_sb, o_ss, do_sb,
+      do_ss, lse, S, H, s_pad, lse2, delta);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 }  // namespace
+
+#define MGFA_BWD_DISPATCH(fn, ...)                                          \
+  do {                                                                      \
+    MGFA_CHECK(p.head_dim == 64 || p.head_dim == 128, "head_dim must be 64 or 128"); \
+    if (p.head_dim == 64) {                                                 \
+      if (p.fp16) fn<64, true>(__VA_ARGS__); else fn<64, false>(__VA_ARGS__); \
+    } else {                                                                \
+      if (p.fp16) fn<128, true>(__VA_ARGS__); else fn<128, false>(__VA_ARGS__); \
+    }                                                                       \
+  } while (0)
 
 void flash_bwd_dq_launch(const CUtensorMap& mq, const CUtensorMap& mdo, const CUtensorMap& mk,
                          const CUtensorMap& mv, BwdParams& p, cudaStream_t stream) {
-  static int done_dev = -1;
-  set_smem<DqSmem>(flash_bwd_dq_kernel, done_dev);
-  dim3 grid(p.n_q_tiles, p.hq, p.batch);
-  flash_bwd_dq_kernel<<<grid, kThreads, sizeof(DqSmem) + 1024, stream>>>(mq, mdo, mk, mv, p);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  MGFA_BWD_DISPATCH(launch_dq, mq, mdo, mk, mv, p, stream);
 }
 
 void flash_bwd_dkdv_launch(const CUtensorMap& mq, const CUtensorMap& mdo, const CUtensorMap& mk,
                            const CUtensorMap& mv, BwdParams& p, cudaStream_t stream) {
-  static int done_dev = -1;
-  set_smem<DkvSmem>(flash_bwd_dkdv_kernel, done_dev);
-  dim3 grid(p.n_kv_tiles, p.hkv, p.batch);
-  flash_bwd_dkdv_kernel<<<grid, kDkdvThreads, sizeof(DkvSmem) + 1024, stream>>>(mq, mdo, mk, mv, p);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  MGFA_BWD_DISPATCH(launch_dkdv, mq, mdo, mk, mv, p, stream);
 }
 
 void flash_bwd_preprocess_launch(const void* o, const void* dout, int64_t o_sb, int64_t o_ss,
                                  int64_t do_sb, int64_t do_ss, const float* lse, int B, int S,
                                  int H, int s_pad, float* lse2, float* delta,
-                                 cudaStream_t stream) {
-  const int64_t warps = int64_t(H) * s_pad;
-  const int threads = 256;
-  dim3 grid(unsigned((warps * 32 + threads - 1) / threads), B);
-  bwd_preprocess_kernel<<<grid, threads, 0, stream>>>(
-      static_cast<const __nv_bfloat16*>(o), static_cast<const __nv_bfloat16*>(dout), o_sb, o_ss,
-      do_sb, do_ss, lse, S, H, s_pad, lse2, delta);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+                                 cudaStream_t stream, int head_dim, bool fp16) {
+  struct {
+    int head_dim, fp16;
+  } p{head_dim, fp16 ? 1 : 0};
+  MGFA_BWD_DISPATCH(launch_preprocess, o, dout, o_sb, o_ss, do_sb, do_ss, lse, B, S, H, s_pad,
+                    lse2, delta, stream);
 }
 
 }  // namespace mgfa
 
 // ---------------------------------------------------------------------- no-throw launchers
 // Used by the allocation-free C entry point (attn_bwd_noalloc.cu); they report
-// errors through the return value instead of exceptions.
+// errors through the return value instead of exceptions. They run the bf16,
+// head_dim 128 kernels.
 namespace mgfa {
 
 cudaError_t flash_bwd_preprocess_raw(const void* o, const void* dout, int64_t o_sb, int64_t o_ss,
@@ -735,27 +780,28 @@ cudaError_t flash_bwd_preprocess_raw(const void* o, const void* dout, int64_t o_
   const int64_t warps = int64_t(H) * s_pad;
   const int threads = 256;
   dim3 grid(unsigned((warps * 32 + threads - 1) / threads), B);
-  bwd_preprocess_kernel<<<grid, threads, 0, stream>>>(
-      static_cast<const __nv_bfloat16*>(o), static_cast<const __nv_bfloat16*>(dout), o_sb, o_ss,
-      do_sb, do_ss, lse, S, H, s_pad, lse2, delta);
+  bwd_preprocess_kernel<128, false><<<grid, threads, 0, stream>>>(
+      static_cast<const uint16_t*>(o), static_cast<const uint16_t*>(dout), o_sb, o_ss, do_sb,
+      do_ss, lse, S, H, s_pad, lse2, delta);
   return cudaGetLastError();
 }
 
 cudaError_t flash_bwd_kernels_raw(const CUtensorMap& mq, const CUtensorMap& mdo,
                                   const CUtensorMap& mk, const CUtensorMap& mv,
                                   const BwdParams& p, cudaStream_t stream) {
-  cudaError_t e = cudaFuncSetAttribute(flash_bwd_dkdv_kernel,
+  cudaError_t e = cudaFuncSetAttribute(flash_bwd_dkdv_kernel<128, false>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       int(sizeof(DkvSmem) + 1024));
+                                       int(sizeof(DkvSmem<128>) + 1024));
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(flash_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           int(sizeof(DqSmem) + 1024));
+  e = cudaFuncSetAttribute(flash_bwd_dq_kernel<128, false>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           int(sizeof(DqSmem<128>) + 1024));
   if (e != cudaSuccess) return e;
-  flash_bwd_dkdv_kernel<<<dim3(p.n_kv_tiles, p.hkv, p.batch), kDkdvThreads,
-                          sizeof(DkvSmem) + 1024, stream>>>(mq, mdo, mk, mv, p);
+  flash_bwd_dkdv_kernel<128, false><<<dim3(p.n_kv_tiles, p.hkv, p.batch), kDkdvThreads,
+                                      sizeof(DkvSmem<128>) + 1024, stream>>>(mq, mdo, mk, mv, p);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  flash_bwd_dq_kernel<<<dim3(p.n_q_tiles, p.hq, p.batch), kThreads, sizeof(DqSmem) + 1024,
-                        stream>>>(mq, mdo, mk, mv, p);
+  flash_bwd_dq_kernel<128, false><<<dim3(p.n_q_tiles, p.hq, p.batch), kThreads,
+                                    sizeof(DqSmem<128>) + 1024, stream>>>(mq, mdo, mk, mv, p);
   return cudaGetLastError();
 }
 

@@ -26,6 +26,8 @@ struct BwdRing {
 
 struct BwdParams {
   int batch = 1, hq = 1, hkv = 1;
+  int head_dim = 128;                  // 64 or 128
+  int fp16 = 0;                        // fp16 inputs instead of bf16
   int sq = 0, sk = 0;
   int n_q_tiles = 0, n_kv_tiles = 0;
   int sq_pad = 0;                      // n_q_tiles * 128: row stride of lse2 / delta
@@ -36,7 +38,7 @@ struct BwdParams {
   const int* kv_tile_pos = nullptr;    // [n_kv_tiles]
   const float* lse2 = nullptr;         // [B, Hq, sq_pad] LSE in log2 units
   const float* delta = nullptr;        // [B, Hq, sq_pad] rowsum(dO * O)
-  // fp32 gradient outputs, [B, S, H, 128]; accumulate adds into what is there
+  // fp32 gradient outputs, [B, S, H, head_dim]; accumulate adds into what is there
   float* dq = nullptr;
   float* dk = nullptr;
   float* dv = nullptr;
@@ -63,6 +65,7 @@ void flash_bwd_dkdv_launch(const CUtensorMap& mq, const CUtensorMap& mdo, const 
 // delta[b,h,i] = sum_d dO*O, lse2 = lse * log2(e); padded rows get lse2 = +inf.
 void flash_bwd_preprocess_launch(const void* o, const void* dout, int64_t o_sb, int64_t o_ss,
                                  int64_t do_sb, int64_t do_ss, const float* lse, int B, int S,
-                                 int H, int s_pad, float* lse2, float* delta, cudaStream_t stream);
+                                 int H, int s_pad, float* lse2, float* delta, cudaStream_t stream,
+                                 int head_dim = 128, bool fp16 = false);
 
 }  // namespace mgfa

@@ -22,10 +22,10 @@
 // O is rescaled only when the running max grows by more than 2^8 (the stale
 // max keeps P <= 256, exact in fp32 sums and bf16 P).
 #include <torch/extension.h>
+#include "../common/check.hpp"
 #include <ATen/cuda/CUDAContext.h>
 
 #include <cmath>
-#include <cstdlib>
 
 #include "flash_fwd_sm100.cuh"
 #include "sm100_ptx.cuh"
@@ -37,18 +37,19 @@ namespace {
 
 using namespace mgfa::dev;
 
-constexpr int kD = 128;
 constexpr int kTile = 128;
-constexpr int kHalfBytes = kTile * 64 * 2;   // one 128 x 64 bf16 swizzled box
-constexpr int kTileBytes = 2 * kHalfBytes;   // 128 x 128 bf16
+constexpr int kHalfBytes = kTile * 64 * 2;   // one 128 x 64 16-bit swizzled box
 constexpr int kWarps = 12;
 constexpr int kThreads = kWarps * 32;
 constexpr float kRescaleThreshold = 8.0f;    // log2 units
 
+// kD = head_dim (64 or 128) is kD / 64 swizzled 64-column boxes per 128-row tile.
+template <int kD>
 struct __align__(1024) FwdSmem {
-  __nv_bfloat16 q[2][2][kTile * 64];  // [query tile][d half]
-  __nv_bfloat16 k[2][2][kTile * 64];  // [stage][d half]
-  __nv_bfloat16 v[2][2][kTile * 64];
+  static constexpr int kHalves = kD / 64;
+  uint16_t q[2][kHalves][kTile * 64];  // [query tile][d half], bf16 or fp16 bits
+  uint16_t k[2][kHalves][kTile * 64];  // [stage][d half]
+  uint16_t v[2][kHalves][kTile * 64];
   uint64_t q_full;
   uint64_t k_full[2], k_empty[2];
   uint64_t v_full[2], v_empty[2];
@@ -67,16 +68,18 @@ __device__ __forceinline__ uint32_t sm_id() {
 }
 
 // ------------------------------------------------------------------ kernel
-// kF2: packed f32x2 arithmetic in the softmax; kPolyStart: first bf16 pair index
-// (of 64 per row) whose exponentials run on the FMA pipe in unmasked tiles
-// (64 = none).
-template <bool kF2, int kPolyStart>
+// kD: head_dim (64 or 128); kF16: fp16 inputs/outputs (else bf16).
+template <int kD, bool kF16>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap map_q,
                      const __grid_constant__ CUtensorMap map_k,
                      const __grid_constant__ CUtensorMap map_v, const FwdParams p) {
+  constexpr int kHalves = kD / 64;
+  constexpr int kTileBytes = kHalves * kHalfBytes;  // one 128 x kD tile
+  constexpr int kKSteps = kD / 16;                  // MMA K steps of S = Q K^T
+  constexpr int kOChunks = kD / 32;                 // 32-column TMEM chunks of O
   extern __shared__ uint8_t smem_raw[];
-  FwdSmem& s = *reinterpret_cast<FwdSmem*>(
+  FwdSmem<kD>& s = *reinterpret_cast<FwdSmem<kD>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
   const uint32_t warp = warp_id(), lane = lane_id();
@@ -100,7 +103,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                               (q_pos0 > q_pos1 ? q_pos0 : q_pos1) + (kTile - 1));
   const bool has_prior = p.merge != 0;
   // No visible key tile: the running state is already correct unless this is
-  // the final step, which still has to convert it to the bf16 output.
+  // the final step, which still has to convert it to the 16-bit output.
   const bool skip_compute = n_active == 0;
   if (skip_compute && has_prior && !p.final_out && !p.push.enabled && !p.consume.enabled) return;
 
@@ -131,6 +134,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
+  // TMEM columns: S0/P0 [0,128), S1/P1 [128,256), O0 [256, 256+kD), O1 after it
+  constexpr uint32_t kOCol = 256;
 
   if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
@@ -140,7 +145,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&map_v);
       mbar_arrive_expect_tx(&s.q_full, 2 * kTileBytes);
       for (int t = 0; t < 2; ++t)
-        for (int hf = 0; hf < 2; ++hf)
+        for (int hf = 0; hf < kHalves; ++hf)
           tma_load_4d(s.q[t][hf], &map_q, &s.q_full, hf * 64, h, (qt0 + t) * kTile, b);
       bool ok = true;
       if (p.consume.enabled) {
@@ -164,20 +169,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t ph = (it >> 1) & 1;
         if (!mbar_wait(&s.k_empty[st], ph ^ 1, ab, 81)) break;
         mbar_arrive_expect_tx(&s.k_full[st], kTileBytes);
-        tma_load_4d(s.k[st][0], &map_k, &s.k_full[st], 0, hk, j * kTile, b);
-        tma_load_4d(s.k[st][1], &map_k, &s.k_full[st], 64, hk, j * kTile, b);
+        for (int hf = 0; hf < kHalves; ++hf)
+          tma_load_4d(s.k[st][hf], &map_k, &s.k_full[st], hf * 64, hk, j * kTile, b);
         last_k_phase[st] = int(ph);
         if (!mbar_wait(&s.v_empty[st], ph ^ 1, ab, 82)) break;
         mbar_arrive_expect_tx(&s.v_full[st], kTileBytes);
-        tma_load_4d(s.v[st][0], &map_v, &s.v_full[st], 0, hk, j * kTile, b);
-        tma_load_4d(s.v[st][1], &map_v, &s.v_full[st], 64, hk, j * kTile, b);
+        for (int hf = 0; hf < kHalves; ++hf)
+          tma_load_4d(s.v[st][hf], &map_v, &s.v_full[st], hf * 64, hk, j * kTile, b);
         last_v_phase[st] = int(ph);
         ++it;
       }
       // Drain: never leave the CTA with a TMA write outstanding.
-      AbortState drain_ab{&s.abort_flag, nullptr, p.wait_limit_ns};
       volatile uint32_t never = 0;
-      drain_ab.flag = &never;
+      AbortState drain_ab{&never, nullptr, p.wait_limit_ns};
       mbar_wait(&s.q_full, 0, drain_ab, 0);
       for (int st = 0; st < 2; ++st) {
         if (last_k_phase[st] >= 0) mbar_wait(&s.k_full[st], uint32_t(last_k_phase[st]), drain_ab, 0);
@@ -187,13 +191,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && !skip_compute) {
-      const uint32_t idesc_s = make_idesc_bf16(128, 128, 0, 0);
-      const uint32_t idesc_o = make_idesc_bf16(128, 128, 0, 1);
+      const uint32_t idesc_s = make_idesc_16(128, 128, 0, 0, kF16);
+      const uint32_t idesc_o = make_idesc_16(128, kD, 0, 1, kF16);
       const uint32_t q_base[2] = {smem_u32(s.q[0][0]), smem_u32(s.q[1][0])};
       auto issue_s = [&](int t, int st) {
         const uint32_t kb = smem_u32(s.k[st][0]);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
+        for (int kk = 0; kk < kKSteps; ++kk) {
           const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
           mma_ss(tmem + t * 128, make_sdesc_sw128(q_base[t] + off, 16, 1024),
                  make_sdesc_sw128(kb + off, 16, 1024), idesc_s, kk > 0);
@@ -202,8 +206,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto issue_o = [&](int t, int st, uint32_t acc) {
         const uint32_t vb = smem_u32(s.v[st][0]);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          mma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
+        for (int kk = 0; kk < 8; ++kk) {  // 128 keys, 16 per step
+          mma_ts(tmem + kOCol + t * kD, tmem + t * 128 + kk * 8,
                  make_sdesc_sw128(vb + kk * 2048, kHalfBytes, 1024), idesc_o,
                  (acc || kk > 0) ? 1u : 0u);
         }
@@ -263,7 +267,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = threadIdx.x & 127;        // row within the tile == TMEM lane
     const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;
     const uint32_t s_addr = tmem + lane_off + t * 128;
-    const uint32_t o_addr = tmem + lane_off + 256 + t * 128;
+    const uint32_t o_addr = tmem + lane_off + kOCol + t * kD;
     const bool q_valid_tile = qt < p.n_q_tiles;
     const int q_tile_pos = t == 0 ? q_pos0 : q_pos1;
     const int q_pos = q_tile_pos + r;
@@ -274,7 +278,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       full_hi = f < full_hi ? f : full_hi;
     }
     if (!q_valid_tile) full_hi = 0;
-    const uint64_t scale2 = f2_pack(p.scale_log2, p.scale_log2);
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int it = 0; !skip_compute && it < n_active; ++it) {
@@ -325,59 +328,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float m_use = (m == -INFINITY) ? 0.f : m;
       l *= alpha;
-      if constexpr (kF2) {
-        const uint64_t neg_m = f2_pack(-m_use, -m_use);
-        uint64_t acc0 = 0, acc1 = 0;  // packed partial row sums (0.0f, 0.0f)
+      const float neg_m = -m_use;
+      float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t pk[32];
+      for (int half = 0; half < 2; ++half) {
+        uint32_t pk[32];
 #pragma unroll
-          for (int cc = 0; cc < 32; ++cc) {
-            const int c = half * 32 + cc;
-            const uint64_t x2 =
-                f2_fma(f2_pack(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])),
-                       scale2, neg_m);
-            uint64_t p2;
-            if (full && c >= kPolyStart) {
-              p2 = exp2_poly2(x2);  // exponentials on the FMA pipe
-            } else {
-              float x0, x1;
-              f2_unpack(x2, x0, x1);
-              p2 = f2_pack(ex2_approx(x0), ex2_approx(x1));
-            }
-            if (c & 1) acc1 = f2_add(acc1, p2);
-            else acc0 = f2_add(acc0, p2);
-            float p0, p1;
-            f2_unpack(p2, p0, p1);
-            pk[cc] = pack_bf16(p0, p1);
-          }
-          tmem_st32(s_addr + half * 32, pk);
+        for (int cc = 0; cc < 32; ++cc) {
+          const int c = half * 32 + cc;
+          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * c]), p.scale_log2, neg_m));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * c + 1]), p.scale_log2, neg_m));
+          if (c & 1) { l2 += p0; l3 += p1; } else { l0 += p0; l1 += p1; }
+          pk[cc] = pack16<kF16>(p0, p1);
         }
-        float a0, a1, b0, b1;
-        f2_unpack(acc0, a0, a1);
-        f2_unpack(acc1, b0, b1);
-        l += (a0 + a1) + (b0 + b1);
-      } else {
-        const float neg_m = -m_use;
-        float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t pk[32];
-#pragma unroll
-          for (int cc = 0; cc < 32; ++cc) {
-            const int c = half * 32 + cc;
-            const float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * c]), p.scale_log2, neg_m));
-            const float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * c + 1]), p.scale_log2, neg_m));
-            if (c & 1) { l2 += p0; l3 += p1; } else { l0 += p0; l1 += p1; }
-            pk[cc] = pack_bf16(p0, p1);
-          }
-          tmem_st32(s_addr + half * 32, pk);
-        }
-        l += (l0 + l1) + (l2 + l3);
+        tmem_st32(s_addr + half * 32, pk);
       }
+      l += (l0 + l1) + (l2 + l3);
       if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
+        for (int ch = 0; ch < kOChunks; ++ch) {
           uint32_t orow[32];
           tmem_ld32(o_addr + ch * 32, orow);
           tmem_wait_ld();
@@ -425,7 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     const float scale_new = w_new * inv_l;
 #pragma unroll
-    for (int ch = 0; ch < 4; ++ch) {
+    for (int ch = 0; ch < kOChunks; ++ch) {
       uint32_t orow[32];
       if (!skip_compute && ok) {
         tmem_ld32(o_addr + ch * 32, orow);
@@ -450,13 +419,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (p.final_out) {
-        uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.o) + o_off + ch * 32);
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.o) + o_off + ch * 32);
 #pragma unroll
         for (int q8 = 0; q8 < 4; ++q8)
-          dst[q8] = make_uint4(pack_bf16(v[8 * q8 + 0], v[8 * q8 + 1]),
-                               pack_bf16(v[8 * q8 + 2], v[8 * q8 + 3]),
-                               pack_bf16(v[8 * q8 + 4], v[8 * q8 + 5]),
-                               pack_bf16(v[8 * q8 + 6], v[8 * q8 + 7]));
+          dst[q8] = make_uint4(pack16<kF16>(v[8 * q8 + 0], v[8 * q8 + 1]),
+                               pack16<kF16>(v[8 * q8 + 2], v[8 * q8 + 3]),
+                               pack16<kF16>(v[8 * q8 + 4], v[8 * q8 + 5]),
+                               pack16<kF16>(v[8 * q8 + 6], v[8 * q8 + 7]));
       } else {
         float4* dst = reinterpret_cast<float4*>(p.o_state + o_off + ch * 32);
 #pragma unroll
@@ -497,46 +466,52 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ------------------------------------------------------------------ host side
 }  // namespace
 
-CUtensorMap make_bshd_map(const void* base, int64_t B, int64_t S, int64_t H, int64_t stride_b,
-                          int64_t stride_s, int64_t stride_h) {
-  const uint64_t dims[4] = {uint64_t(kD), uint64_t(H), uint64_t(S), uint64_t(B)};
+CUtensorMap make_bshd_map_dt(const void* base, int64_t B, int64_t S, int64_t H, int64_t stride_b,
+                             int64_t stride_s, int64_t stride_h, int D, bool fp16) {
+  const uint64_t dims[4] = {uint64_t(D), uint64_t(H), uint64_t(S), uint64_t(B)};
   const uint64_t strides[3] = {uint64_t(stride_h) * 2, uint64_t(stride_s) * 2,
                                uint64_t(stride_b) * 2};
   const uint32_t box[4] = {64, 1, kTile, 1};
-  return host::make_bf16_map(base, 4, dims, strides, box);
+  return host::make_bf16_map(base, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                             fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                  : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
 }
 
-size_t flash_fwd_smem_bytes() { return sizeof(FwdSmem) + 1024; }
+CUtensorMap make_bshd_map(const void* base, int64_t B, int64_t S, int64_t H, int64_t stride_b,
+                          int64_t stride_s, int64_t stride_h) {
+  return make_bshd_map_dt(base, B, S, H, stride_b, stride_s, stride_h, 128, false);
+}
+
+size_t flash_fwd_smem_bytes() { return sizeof(FwdSmem<128>) + 1024; }
 
 namespace {
 using FwdKernelFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap,
                              const FwdParams);
-// Softmax variants: 0 scalar/MUFU, 1 f32x2/MUFU, 2 f32x2 + 1/8 on FMA, 3 f32x2 + 1/4 on FMA.
-FwdKernelFn fwd_variant(int v) {
-  switch (v) {
-    case 0: return flash_fwd_kernel<false, 64>;
-    case 1: return flash_fwd_kernel<true, 64>;
-    case 2: return flash_fwd_kernel<true, 56>;
-    default: return flash_fwd_kernel<true, 48>;
-  }
-}
-int fwd_variant_from_env() {
-  const char* e = std::getenv("MGFA_FWD_VARIANT");
-  return e ? std::atoi(e) : 0;  // measured fastest on B200: scalar math, all-MUFU
+struct FwdVariant {
+  FwdKernelFn fn;
+  int smem;
+};
+FwdVariant fwd_variant(int head_dim, bool fp16) {
+  if (head_dim == 64)
+    return fp16 ? FwdVariant{flash_fwd_kernel<64, true>, int(sizeof(FwdSmem<64>) + 1024)}
+                : FwdVariant{flash_fwd_kernel<64, false>, int(sizeof(FwdSmem<64>) + 1024)};
+  return fp16 ? FwdVariant{flash_fwd_kernel<128, true>, int(sizeof(FwdSmem<128>) + 1024)}
+              : FwdVariant{flash_fwd_kernel<128, false>, int(sizeof(FwdSmem<128>) + 1024)};
 }
 }  // namespace
 
 void flash_fwd_launch_maps(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                            FwdParams& p, cudaStream_t stream) {
-  static const int variant = fwd_variant_from_env();
+  MGFA_CHECK(p.head_dim == 64 || p.head_dim == 128, "head_dim must be 64 or 128");
   static int attr_device[4] = {-1, -1, -1, -1};
-  const FwdKernelFn kern = fwd_variant(variant);
-  const int smem = int(flash_fwd_smem_bytes());
+  const FwdVariant var = fwd_variant(p.head_dim, p.fp16 != 0);
+  const int vi = (p.head_dim == 64 ? 0 : 2) + (p.fp16 ? 1 : 0);
   int dev = 0;
   C10_CUDA_CHECK(cudaGetDevice(&dev));
-  if (attr_device[variant & 3] != dev) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr_device[variant & 3] = dev;
+  if (attr_device[vi] != dev) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(var.fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        var.smem));
+    attr_device[vi] = dev;
   }
   const int n_pairs = (p.n_q_tiles + 1) / 2;
   dim3 grid(n_pairs, p.hq, p.batch);
@@ -544,26 +519,26 @@ void flash_fwd_launch_maps(const CUtensorMap& mq, const CUtensorMap& mk, const C
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = size_t(smem);
+    cfg.dynamicSmemBytes = size_t(var.smem);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, p));
+    C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, var.fn, mq, mk, mv, p));
   } else {
-    kern<<<grid, kThreads, smem, stream>>>(mq, mk, mv, p);
+    var.fn<<<grid, kThreads, var.smem, stream>>>(mq, mk, mv, p);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 }
 
 void flash_fwd_launch(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v,
                       FwdParams& p, cudaStream_t stream) {
-  auto map = [](const torch::Tensor& t) {
-    TORCH_CHECK(t.stride(3) == 1, "head_dim must be contiguous");
-    return make_bshd_map(t.data_ptr(), t.size(0), t.size(1), t.size(2), t.stride(0), t.stride(1),
-                         t.stride(2));
+  auto map = [&](const torch::Tensor& t) {
+    MGFA_CHECK(t.stride(3) == 1, "head_dim must be contiguous");
+    return make_bshd_map_dt(t.data_ptr(), t.size(0), t.size(1), t.size(2), t.stride(0),
+                            t.stride(1), t.stride(2), p.head_dim, p.fp16 != 0);
   };
   flash_fwd_launch_maps(map(q), map(k), map(v), p, stream);
 }

@@ -47,6 +47,8 @@ struct RingConsume {
 
 struct FwdParams {
   int batch = 1, hq = 1, hkv = 1;
+  int head_dim = 128;      // 64 or 128
+  int fp16 = 0;            // inputs/outputs fp16 instead of bf16
   int sq = 0;              // query rows per sequence in this call
   int sk = 0;              // key rows per sequence in the KV buffer
   int n_q_tiles = 0, n_kv_tiles = 0;
@@ -82,6 +84,10 @@ constexpr int kFwdPushParts = 2;  // push warps per CTA (arrivals per chunk)
 // Tensor map of a [B, S, H, 128] bf16 tensor with the given element strides.
 CUtensorMap make_bshd_map(const void* base, int64_t B, int64_t S, int64_t H,
                           int64_t stride_b, int64_t stride_s, int64_t stride_h);
+// Same for head_dim `D` (64 or 128) and fp16 / bf16 elements.
+CUtensorMap make_bshd_map_dt(const void* base, int64_t B, int64_t S, int64_t H,
+                             int64_t stride_b, int64_t stride_s, int64_t stride_h, int D,
+                             bool fp16);
 void flash_fwd_launch_maps(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                            FwdParams& p, cudaStream_t stream);
 int flash_fwd_grid_ctas(int hq, int n_q_tiles, int batch);

@@ -13,6 +13,7 @@
 //   legacy_merge:   the reference's merge (scale each side by exp(m_i - max)).
 //   legacy_normalize: acc / l on the device.
 #include <torch/extension.h>
+#include "../common/check.hpp"
 #include <ATen/cuda/CUDAContext.h>
 
 #include <cfloat>
@@ -131,7 +132,7 @@ __global__ void legacy_normalize_kernel(const float* __restrict__ acc, const flo
 }
 
 void check_f32(const torch::Tensor& t, const char* name) {
-  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kFloat && t.is_contiguous(), name,
+  MGFA_CHECK(t.is_cuda() && t.scalar_type() == at::kFloat && t.is_contiguous(), name,
               " must be a contiguous float32 CUDA tensor");
 }
 
@@ -148,16 +149,17 @@ void legacy_partial(torch::Tensor q, torch::Tensor k, torch::Tensor v, double sc
   check_f32(acc, "acc");
   check_f32(m, "m");
   check_f32(l, "l");
-  TORCH_CHECK(q.dim() == 3 && q.size(2) == kD && k.size(2) == kD && v.size(2) == kD,
+  MGFA_CHECK(q.dim() == 3 && q.size(2) == kD && k.size(2) == kD && v.size(2) == kD,
               "legacy kernels need head_dim 64");
   const int sq = int(q.size(0)), hq = int(q.size(1)), sk = int(k.size(0)), hkv = int(k.size(1));
-  TORCH_CHECK(hq % hkv == 0, "query heads must be a multiple of kv heads");
+  MGFA_CHECK(hq % hkv == 0, "query heads must be a multiple of kv heads");
   const int64_t* qp = nullptr;
   const int64_t* kp = nullptr;
   if (causal) {
-    TORCH_CHECK(q_pos.has_value() && k_pos.has_value(), "causal needs q_pos and k_pos");
-    TORCH_CHECK(q_pos->scalar_type() == at::kLong && k_pos->scalar_type() == at::kLong);
-    TORCH_CHECK(q_pos->numel() >= sq && k_pos->numel() >= sk);
+    MGFA_CHECK(q_pos.has_value() && k_pos.has_value(), "causal needs q_pos and k_pos");
+    MGFA_CHECK(q_pos->scalar_type() == at::kLong && k_pos->scalar_type() == at::kLong,
+               "positions must be int64");
+    MGFA_CHECK(q_pos->numel() >= sq && k_pos->numel() >= sk, "too few positions");
     qp = q_pos->data_ptr<int64_t>();
     kp = k_pos->data_ptr<int64_t>();
   }
@@ -193,7 +195,7 @@ void legacy_normalize(torch::Tensor acc, torch::Tensor l, torch::Tensor out,
   float* lse_p = nullptr;
   const float* m_p = nullptr;
   if (lse.has_value()) {
-    TORCH_CHECK(m.has_value(), "lse output needs m");
+    MGFA_CHECK(m.has_value(), "lse output needs m");
     lse_p = lse->data_ptr<float>();
     m_p = m->data_ptr<float>();
   }

@@ -17,6 +17,7 @@
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 namespace mgfa::dev {
@@ -256,6 +257,15 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(uint32_t M, uint32_t N, u
          | (a_mn << 15) | (b_mn << 16) | ((N >> 3) << 17) | ((M >> 4) << 24);
 }
 
+// 16-bit inputs (fp16 when f16, else bf16) x 16-bit -> fp32, M x N tile.
+__host__ __device__ constexpr uint32_t make_idesc_16(uint32_t M, uint32_t N, uint32_t a_mn,
+                                                     uint32_t b_mn, bool f16) {
+  return (1u << 4)                       // D format: f32
+         | ((f16 ? 0u : 1u) << 7)        // A format: f16 = 0, bf16 = 1
+         | ((f16 ? 0u : 1u) << 10)       // B format
+         | (a_mn << 15) | (b_mn << 16) | ((N >> 3) << 17) | ((M >> 4) << 24);
+}
+
 // 128-byte-swizzled operand tile in shared memory (1024-byte aligned atoms).
 __device__ __forceinline__ uint64_t make_sdesc_sw128(uint32_t smem_addr, uint32_t lbo_bytes,
                                                      uint32_t sbo_bytes) {
@@ -273,6 +283,24 @@ __device__ __forceinline__ float ex2_approx(float x) {
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);  // .x = lo (low 16 bits)
   return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ uint32_t pack_f16(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <bool kF16>
+__device__ __forceinline__ uint32_t pack16(float lo, float hi) {
+  if constexpr (kF16) return pack_f16(lo, hi);
+  else return pack_bf16(lo, hi);
+}
+
+// two 16-bit values (bf16 or fp16) -> floats
+template <bool kF16>
+__device__ __forceinline__ float2 unpack16(uint32_t w) {
+  if constexpr (kF16) return __half22float2(*reinterpret_cast<const __half2*>(&w));
+  else return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
 }
 
 // Packed fp32 pairs (sm_100 f32x2 arithmetic): a 64-bit register holds (lo, hi).

@@ -26,12 +26,14 @@ inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// bf16 tensor map with `rank` dims (innermost first), byte strides of dims 1..rank-1,
+// 16-bit (bf16 by default, or `dtype`) tensor map with `rank` dims (innermost first),
+// byte strides of dims 1..rank-1,
 // a box of `box` elements per dim and 128-byte swizzle. The innermost box extent
 // must be 64 elements (128 bytes).
 inline CUtensorMap make_bf16_map(const void* base, int rank, const uint64_t* dims,
                                  const uint64_t* byte_strides, const uint32_t* box,
-                                 CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
+                                 CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
   if (reinterpret_cast<uintptr_t>(base) % 16 != 0)
     throw std::invalid_argument("TMA base address must be 16-byte aligned");
   for (int i = 0; i < rank - 1; ++i)
@@ -40,7 +42,7 @@ inline CUtensorMap make_bf16_map(const void* base, int rank, const uint64_t* dim
   CUtensorMap m;
   cuuint32_t elem_strides[5] = {1, 1, 1, 1, 1};
   CUresult r = tensor_map_encoder()(
-      &m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, cuuint32_t(rank), const_cast<void*>(base),
+      &m, dtype, cuuint32_t(rank), const_cast<void*>(base),
       reinterpret_cast<const cuuint64_t*>(dims), reinterpret_cast<const cuuint64_t*>(byte_strides),
       reinterpret_cast<const cuuint32_t*>(box), elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
       swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);

@@ -6,6 +6,7 @@
 //                  V [64 x 128] bf16 MN-major (N contiguous), loaded by TMA
 // Both accumulators are read back with tcgen05.ld (32x32b) and stored as fp32.
 #include <torch/extension.h>
+#include "../common/check.hpp"
 #include <ATen/cuda/CUDAContext.h>
 
 #include "sm100_ptx.cuh"
@@ -114,10 +115,13 @@ __global__ void __launch_bounds__(128, 1)
 
 // Returns (C1, C2, status) for A [128,64], B [128,64], V [64,128] bf16 CUDA tensors.
 std::vector<torch::Tensor> umma_probe(torch::Tensor a, torch::Tensor b, torch::Tensor v) {
-  TORCH_CHECK(a.is_cuda() && a.scalar_type() == at::kBFloat16 && a.is_contiguous());
-  TORCH_CHECK(b.is_cuda() && b.scalar_type() == at::kBFloat16 && b.is_contiguous());
-  TORCH_CHECK(v.is_cuda() && v.scalar_type() == at::kBFloat16 && v.is_contiguous());
-  TORCH_CHECK(a.size(0) == 128 && a.size(1) == 64 && b.size(0) == 128 && b.size(1) == 64 &&
+  MGFA_CHECK(a.is_cuda() && a.scalar_type() == at::kBFloat16 && a.is_contiguous(),
+             "a must be a contiguous bf16 CUDA tensor");
+  MGFA_CHECK(b.is_cuda() && b.scalar_type() == at::kBFloat16 && b.is_contiguous(),
+             "b must be a contiguous bf16 CUDA tensor");
+  MGFA_CHECK(v.is_cuda() && v.scalar_type() == at::kBFloat16 && v.is_contiguous(),
+             "v must be a contiguous bf16 CUDA tensor");
+  MGFA_CHECK(a.size(0) == 128 && a.size(1) == 64 && b.size(0) == 128 && b.size(1) == 64 &&
               v.size(0) == 64 && v.size(1) == 128);
   auto opts = a.options().dtype(at::kFloat);
   auto c1 = torch::zeros({128, 128}, opts), c2 = torch::zeros({128, 128}, opts);

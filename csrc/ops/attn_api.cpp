@@ -1,5 +1,6 @@
 // Torch-facing entry points of the attention kernels.
 #include <torch/extension.h>
+#include "../common/check.hpp"
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
@@ -15,21 +16,32 @@ size_t flash_fwd_smem_bytes();
 
 namespace {
 
-void check_bshd(const torch::Tensor& t, const char* name) {
-  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
-  TORCH_CHECK(t.scalar_type() == at::kBFloat16, name, " must be bfloat16");
-  TORCH_CHECK(t.dim() == 4, name, " must be [batch, seq, heads, head_dim]");
-  TORCH_CHECK(t.size(3) == 128, name, ": the sm_100a kernel supports head_dim 128");
-  TORCH_CHECK(t.stride(3) == 1, name, " must have a contiguous head_dim");
-  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name,
+// bf16 / fp16 [B, S, H, D] CUDA tensor with D in `dims` and a contiguous head_dim.
+void check_bshd_dims(const torch::Tensor& t, const char* name, std::initializer_list<int> dims) {
+  MGFA_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  MGFA_CHECK(t.scalar_type() == at::kBFloat16 || t.scalar_type() == at::kHalf, name,
+              " must be bfloat16 or float16");
+  MGFA_CHECK(t.dim() == 4, name, " must be [batch, seq, heads, head_dim]");
+  bool ok = false;
+  for (int d : dims) ok = ok || t.size(3) == d;
+  MGFA_CHECK(ok, name, ": unsupported head_dim ", t.size(3));
+  MGFA_CHECK(t.stride(3) == 1, name, " must have a contiguous head_dim");
+  MGFA_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name,
               " must be 16-byte aligned");
 }
 
+void check_bshd(const torch::Tensor& t, const char* name) { check_bshd_dims(t, name, {64, 128}); }
+
+void check_same_kind(const torch::Tensor& a, const torch::Tensor& b, const char* what) {
+  MGFA_CHECK(a.scalar_type() == b.scalar_type() && a.size(3) == b.size(3), what,
+              ": dtype and head_dim must match");
+}
+
 const int* tile_pos_ptr(const c10::optional<torch::Tensor>& t, int n, const char* name) {
-  TORCH_CHECK(t.has_value(), "causal attention needs ", name);
-  TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kInt && t->is_contiguous(), name,
+  MGFA_CHECK(t.has_value(), "causal attention needs ", name);
+  MGFA_CHECK(t->is_cuda() && t->scalar_type() == at::kInt && t->is_contiguous(), name,
               " must be a contiguous int32 CUDA tensor");
-  TORCH_CHECK(t->numel() >= n, name, " has ", t->numel(), " entries, need ", n);
+  MGFA_CHECK(t->numel() >= n, name, " has ", t->numel(), " entries, need ", n);
   return t->data_ptr<int>();
 }
 
@@ -49,19 +61,23 @@ void flash_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, c10::optional<
   check_bshd(q, "q");
   check_bshd(k, "k");
   check_bshd(v, "v");
-  TORCH_CHECK(k.sizes() == v.sizes() && k.strides() == v.strides(), "k and v must match");
-  TORCH_CHECK(q.size(0) == k.size(0), "batch mismatch");
+  MGFA_CHECK(k.sizes() == v.sizes() && k.strides() == v.strides(), "k and v must match");
+  check_same_kind(q, k, "q/k");
+  check_same_kind(q, v, "q/v");
+  MGFA_CHECK(q.size(0) == k.size(0), "batch mismatch");
   const int B = int(q.size(0)), Sq = int(q.size(1)), Hq = int(q.size(2));
   const int Sk = int(k.size(1)), Hkv = int(k.size(2));
-  TORCH_CHECK(Hq % Hkv == 0, "query heads must be a multiple of kv heads");
-  TORCH_CHECK(lse.is_cuda() && lse.scalar_type() == at::kFloat && lse.is_contiguous() &&
+  MGFA_CHECK(Hq % Hkv == 0, "query heads must be a multiple of kv heads");
+  MGFA_CHECK(lse.is_cuda() && lse.scalar_type() == at::kFloat && lse.is_contiguous() &&
                   lse.numel() == int64_t(B) * Hq * Sq,
               "lse must be a contiguous float32 [B, Hq, Sq] tensor");
-  TORCH_CHECK(status.is_cuda() && status.scalar_type() == at::kInt && status.numel() >= 1,
+  MGFA_CHECK(status.is_cuda() && status.scalar_type() == at::kInt && status.numel() >= 1,
               "status must be an int32 CUDA tensor");
   c10::cuda::CUDAGuard guard(q.device());
 
   FwdParams p;
+  p.head_dim = int(q.size(3));
+  p.fp16 = q.scalar_type() == at::kHalf ? 1 : 0;
   p.batch = B;
   p.hq = Hq;
   p.hkv = Hkv;
@@ -76,28 +92,29 @@ void flash_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, c10::optional<
     p.kv_tile_pos = tile_pos_ptr(kv_tile_pos, p.n_kv_tiles, "kv_tile_pos");
   }
   if (final_out) {
-    TORCH_CHECK(o.has_value(), "final_out needs o");
-    TORCH_CHECK(o->scalar_type() == at::kBFloat16 && o->sizes() == q.sizes() && o->stride(3) == 1,
-                "o must be bf16 shaped like q");
+    MGFA_CHECK(o.has_value(), "final_out needs o");
+    MGFA_CHECK(o->scalar_type() == q.scalar_type() && o->sizes() == q.sizes() &&
+                    o->stride(3) == 1,
+                "o must have q's dtype and shape");
     p.o = o->data_ptr();
   } else {
-    TORCH_CHECK(o_state.has_value(), "state output needs o_state");
+    MGFA_CHECK(o_state.has_value(), "state output needs o_state");
   }
   if (merge || !final_out) {
-    TORCH_CHECK(o_state.has_value() && o_state->scalar_type() == at::kFloat &&
+    MGFA_CHECK(o_state.has_value() && o_state->scalar_type() == at::kFloat &&
                     o_state->sizes() == q.sizes() && o_state->is_contiguous(),
                 "o_state must be a contiguous fp32 tensor shaped like q");
     p.o_state = o_state->data_ptr<float>();
   }
   if (final_out && merge) {
-    TORCH_CHECK(o->stride(0) == o_state->stride(0) && o->stride(1) == o_state->stride(1) &&
+    MGFA_CHECK(o->stride(0) == o_state->stride(0) && o->stride(1) == o_state->stride(1) &&
                     o->stride(2) == o_state->stride(2),
                 "o and o_state must share strides");
   }
   const torch::Tensor& ref = final_out ? *o : *o_state;
   p.o_batch_stride = ref.stride(0);
   p.o_row_stride = ref.stride(1);
-  TORCH_CHECK(ref.stride(2) == 128, "outputs must have packed heads");
+  MGFA_CHECK(ref.stride(2) == q.size(3), "outputs must have packed heads");
   p.lse = lse.data_ptr<float>();
   p.merge = merge ? 1 : 0;
   p.final_out = final_out ? 1 : 0;
@@ -131,17 +148,23 @@ void flash_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tens
   check_bshd(v, "v");
   check_bshd(dout, "dout");
   check_bshd(out, "out");
-  TORCH_CHECK(dout.sizes() == q.sizes() && out.sizes() == q.sizes(), "dout/out must match q");
-  TORCH_CHECK(k.sizes() == v.sizes() && k.strides() == v.strides(), "k and v must match");
+  MGFA_CHECK(dout.sizes() == q.sizes() && out.sizes() == q.sizes(), "dout/out must match q");
+  check_same_kind(q, k, "q/k");
+  check_same_kind(q, v, "q/v");
+  check_same_kind(q, dout, "q/dout");
+  check_same_kind(q, out, "q/out");
+  const int D = int(q.size(3));
+  const bool f16 = q.scalar_type() == at::kHalf;
+  MGFA_CHECK(k.sizes() == v.sizes() && k.strides() == v.strides(), "k and v must match");
   const int B = int(q.size(0)), Sq = int(q.size(1)), Hq = int(q.size(2));
   const int Sk = int(k.size(1)), Hkv = int(k.size(2));
-  TORCH_CHECK(Hq % Hkv == 0, "query heads must be a multiple of kv heads");
+  MGFA_CHECK(Hq % Hkv == 0, "query heads must be a multiple of kv heads");
   for (auto* t : {&dq, &dk, &dv})
-    TORCH_CHECK(t->scalar_type() == at::kFloat && t->dim() == 4 && t->stride(3) == 1 &&
-                    t->stride(2) == 128,
-                "gradient buffers must be fp32 [B,S,H,128] with packed heads");
-  TORCH_CHECK(dk.strides() == dv.strides(), "dk and dv must share strides");
-  TORCH_CHECK(dq.sizes() == q.sizes() && dk.sizes() == k.sizes() && dv.sizes() == v.sizes(),
+    MGFA_CHECK(t->scalar_type() == at::kFloat && t->dim() == 4 && t->stride(3) == 1 &&
+                    t->stride(2) == q.size(3),
+                "gradient buffers must be fp32 [B,S,H,D] with packed heads");
+  MGFA_CHECK(dk.strides() == dv.strides(), "dk and dv must share strides");
+  MGFA_CHECK(dq.sizes() == q.sizes() && dk.sizes() == k.sizes() && dv.sizes() == v.sizes(),
               "gradient buffers must match their inputs");
   c10::cuda::CUDAGuard guard(q.device());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
@@ -150,16 +173,19 @@ void flash_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tens
   if (lse2_in.has_value() && delta_in.has_value()) {
     lse2 = *lse2_in;
     delta = *delta_in;
-    TORCH_CHECK(lse2.numel() == int64_t(B) * Hq * sq_pad && delta.numel() == lse2.numel(),
+    MGFA_CHECK(lse2.numel() == int64_t(B) * Hq * sq_pad && delta.numel() == lse2.numel(),
                 "lse2/delta must be [B, Hq, ceil(Sq/128)*128]");
   } else {
     lse2 = torch::empty({B, Hq, sq_pad}, q.options().dtype(at::kFloat));
     delta = torch::empty({B, Hq, sq_pad}, q.options().dtype(at::kFloat));
     flash_bwd_preprocess_launch(out.data_ptr(), dout.data_ptr(), out.stride(0), out.stride(1),
                                 dout.stride(0), dout.stride(1), lse.data_ptr<float>(), B, Sq, Hq,
-                                sq_pad, lse2.data_ptr<float>(), delta.data_ptr<float>(), stream);
+                                sq_pad, lse2.data_ptr<float>(), delta.data_ptr<float>(), stream, D,
+                                f16);
   }
   BwdParams p;
+  p.head_dim = D;
+  p.fp16 = f16 ? 1 : 0;
   p.batch = B;
   p.hq = Hq;
   p.hkv = Hkv;
@@ -188,9 +214,9 @@ void flash_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tens
   p.status = reinterpret_cast<uint32_t*>(status.data_ptr<int>());
   p.wait_limit_ns = uint64_t(wait_limit_ns);
   if (B == 0 || Sq == 0 || Sk == 0) return;
-  auto map = [](const torch::Tensor& t) {
-    return make_bshd_map(t.data_ptr(), t.size(0), t.size(1), t.size(2), t.stride(0), t.stride(1),
-                         t.stride(2));
+  auto map = [&](const torch::Tensor& t) {
+    return make_bshd_map_dt(t.data_ptr(), t.size(0), t.size(1), t.size(2), t.stride(0),
+                            t.stride(1), t.stride(2), D, f16);
   };
   const CUtensorMap mq = map(q), mdo = map(dout), mk = map(k), mv = map(v);
   flash_bwd_dkdv_launch(mq, mdo, mk, mv, p, stream);
@@ -211,7 +237,8 @@ std::vector<torch::Tensor> flash_bwd_preprocess(torch::Tensor dout, torch::Tenso
   flash_bwd_preprocess_launch(out.data_ptr(), dout.data_ptr(), out.stride(0), out.stride(1),
                               dout.stride(0), dout.stride(1), lse.data_ptr<float>(), B, Sq, Hq,
                               sq_pad, lse2.data_ptr<float>(), delta.data_ptr<float>(),
-                              at::cuda::getCurrentCUDAStream());
+                              at::cuda::getCurrentCUDAStream(), int(out.size(3)),
+                              out.scalar_type() == at::kHalf);
   return {lse2, delta};
 }
 
@@ -234,6 +261,8 @@ torch::Tensor fwd_timeout_probe(torch::Tensor q, torch::Tensor k, torch::Tensor 
   auto o = torch::empty_like(q);
   auto lse = torch::empty({q.size(0), q.size(2), q.size(1)}, q.options().dtype(at::kFloat));
   FwdParams p;
+  p.head_dim = int(q.size(3));
+  p.fp16 = q.scalar_type() == at::kHalf ? 1 : 0;
   p.batch = int(q.size(0));
   p.hq = int(q.size(2));
   p.hkv = int(k.size(2));

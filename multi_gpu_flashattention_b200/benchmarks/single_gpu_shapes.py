@@ -3,7 +3,7 @@ tests/benchmark_single_gpu_shapes.py, on this framework's sm_100a kernels).
 
     python -m multi_gpu_flashattention_b200.benchmarks.single_gpu_shapes \
         [--shapes 256x256 1024x1024 ...] [--batch-size 2] [--num-heads 8]
-        [--head-dim 128] [--warmup 10] [--repeats 50] [--causal|--no-causal]
+        [--head-dim 64|128] [--dtype bf16|fp16] [--warmup 10] [--repeats 50] [--causal|--no-causal]
         [--backward] [--csv-out results/single_gpu_shapes.csv]
 
 Same columns as the reference's CSV plus TFLOP/s. Causal active elements are
@@ -16,6 +16,8 @@ import os
 from statistics import mean, pstdev
 
 import torch
+
+DTYPES = {"bf16": torch.bfloat16, "fp16": torch.float16}
 
 from ..ops.flash import flash_attn_bwd, flash_attn_fwd
 
@@ -45,7 +47,7 @@ def bench(sq, sk, a):
     dev = torch.device("cuda", a.device)
     g = torch.Generator(device=dev).manual_seed(0)
     mk = lambda s: torch.randn(a.batch_size, s, a.num_heads, a.head_dim, device=dev,
-                               generator=g, dtype=torch.bfloat16)
+                               generator=g, dtype=DTYPES[a.dtype])
     q, k, v = mk(sq), mk(sk), mk(sk)
     out, lse = flash_attn_fwd(q, k, v, causal=a.causal)
     do = torch.randn_like(out)
@@ -70,7 +72,7 @@ def bench(sq, sk, a):
     act = active_elements(sq, sk, a.causal) * a.batch_size * a.num_heads
     flops = 4 * act * a.head_dim * (2.5 if a.backward else 1.0)
     return {"seq_q": sq, "seq_k": sk, "batch_size": a.batch_size, "num_heads": a.num_heads,
-            "head_dim": a.head_dim, "dtype": "bfloat16", "causal": a.causal,
+            "head_dim": a.head_dim, "dtype": str(DTYPES[a.dtype]).replace("torch.", ""), "causal": a.causal,
             "active_elements": act, "avg_ms": mean(times), "std_ms": pstdev(times),
             "min_ms": min(times), "max_ms": max(times),
             "peak_mem_mb": torch.cuda.max_memory_allocated(dev) / 2 ** 20,
@@ -82,7 +84,8 @@ def main():
     ap.add_argument("--shapes", nargs="+", default=DEFAULT_SHAPES)
     ap.add_argument("--batch-size", type=int, default=2)
     ap.add_argument("--num-heads", type=int, default=8)
-    ap.add_argument("--head-dim", type=int, default=128)
+    ap.add_argument("--head-dim", type=int, default=128, choices=[64, 128])
+    ap.add_argument("--dtype", default="bf16", choices=sorted(DTYPES))
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--repeats", type=int, default=50)
     ap.add_argument("--device", type=int, default=0)
@@ -93,8 +96,6 @@ def main():
     ap.set_defaults(causal=True)
     ap.add_argument("--csv-out", default="")
     a = ap.parse_args()
-    if a.head_dim != 128:
-        raise SystemExit("the sm_100a kernels support head_dim 128")
     rows = []
     for sh in a.shapes:
         r = bench(*parse_shape(sh), a)

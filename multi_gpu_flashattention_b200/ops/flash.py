@@ -1,9 +1,10 @@
 """Single-GPU attention on the sm_100a kernels.
 
-Tensors use the [batch, seq, heads, head_dim] layout. The tcgen05 kernel takes
-bf16 q/k/v with head_dim 128, any number of query heads that is a multiple of
-the kv heads (GQA/MQA), and writes a bf16 output plus an fp32 natural-log LSE
-[batch, heads, seq].
+Tensors use the [batch, seq, heads, head_dim] layout. The tcgen05 kernels take
+bf16 or fp16 q/k/v (one dtype) with head_dim 64 or 128, any number of query
+heads that is a multiple of the kv heads (GQA/MQA), and write an output of the
+input dtype plus an fp32 natural-log LSE [batch, heads, seq]; gradients are
+fp32.
 
 Causal masking is expressed with per-tile global token positions: key tile j
 is visible to query tile i where kv_tile_pos[j] + c <= q_tile_pos[i] + r for
@@ -58,7 +59,7 @@ def flash_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bo
                    out: Optional[torch.Tensor] = None,
                    status: Optional[torch.Tensor] = None,
                    wait_limit_ns: int = DEFAULT_WAIT_LIMIT_NS):
-    """Forward attention; returns (out bf16 [B,Sq,Hq,D], lse fp32 [B,Hq,Sq])."""
+    """Forward attention; returns (out [B,Sq,Hq,D] in q's dtype, lse fp32 [B,Hq,Sq])."""
     B, Sq, Hq, _ = q.shape
     if causal:
         if q_tile_pos is None:
@@ -80,7 +81,7 @@ def flash_attn_fwd_step(q, k, v, o_state, lse, *, causal, softmax_scale=None, q_
 
     o_state: fp32 [B,Sq,Hq,D] normalised running output; lse: fp32 [B,Hq,Sq].
     With merge=False the pass starts a new state; with final_out=True the merged
-    result is written to `out` (bf16) instead of o_state."""
+    result is written to `out` (q's dtype) instead of o_state."""
     st = status if status is not None else torch.zeros(1, dtype=torch.int32, device=q.device)
     C().flash_fwd(q, k, v, out, o_state, lse, _scale(q, softmax_scale), causal, q_tile_pos,
                   kv_tile_pos, merge, final_out, st, int(wait_limit_ns))
@@ -130,6 +131,6 @@ class _FlashAttnFn(torch.autograd.Function):
 def flash_attn(q, k, v, causal: bool = False, softmax_scale: Optional[float] = None,
                return_lse: bool = False):
     """Differentiable single-GPU attention on the sm_100a kernels.
-    q [B,S,Hq,128], k/v [B,S,Hkv,128] bf16 -> out [B,S,Hq,128] bf16."""
+    q [B,S,Hq,D], k/v [B,S,Hkv,D] bf16 or fp16 (D = 64 or 128) -> out [B,S,Hq,D]."""
     out, lse = _FlashAttnFn.apply(q, k, v, causal, softmax_scale)
     return (out, lse) if return_lse else out

@@ -47,18 +47,26 @@ def test_ring_forward_scheduler_layout_fused():
     run_ranks(_case, _world(), "scheduler", True, "fused", 4096, 2, 2, 2, backend="nccl")
 
 
-def _bwd_case(rank, world, kind, causal, bwd_backend="nccl"):
+def _bwd_case(rank, world, kind, causal, bwd_backend="nccl", head_dim=128,
+              dtype=torch.bfloat16):
+    from multi_gpu_flashattention_b200.ops.reference import attention_ref
     from multi_gpu_flashattention_b200.parallel.layouts import RingLayout
     from multi_gpu_flashattention_b200.parallel.ring import ring_attention_forward
     from multi_gpu_flashattention_b200.parallel.ring_bwd import ring_attention_backward
     dev = torch.device("cuda", rank)
     seq, hq, hkv = 2048, 4, 2
     g = torch.Generator(device=dev).manual_seed(5)
-    mk = lambda h: (torch.randn(1, seq, h, 128, device=dev, generator=g) * 0.5).bfloat16()
+    mk = lambda h: (torch.randn(1, seq, h, head_dim, device=dev, generator=g) * 0.5).to(dtype)
     q, k, v, do = mk(hq), mk(hkv), mk(hkv), mk(hq)
     lay = RingLayout(kind, seq, world, mask="causal" if causal else "full")
     ql, kl, vl, dol = (lay.shard(t, rank) for t in (q, k, v, do))
     out, lse = ring_attention_forward(ql, kl, vl, lay, causal=causal, backend="fused", check=True)
+    assert out.dtype == dtype
+    if head_dim != 128 or dtype != torch.bfloat16:
+        ref, _ = attention_ref(q, k, v, causal=causal)
+        m = lay.local_len(rank)
+        err = (out[:, :m].float() - lay.shard(ref, rank)[:, :m]).abs().max().item()
+        assert err < 2e-2, (rank, "out", err)
     dq, dk, dv = ring_attention_backward(dol, ql, kl, vl, out, lse, lay, causal=causal,
                                          backend=bwd_backend)
     rq, rk, rv = ring_attention_backward(dol, ql, kl, vl, out, lse, lay, causal=causal,
@@ -75,6 +83,12 @@ def _bwd_case(rank, world, kind, causal, bwd_backend="nccl"):
                                          ("striped", True)])
 def test_ring_backward_matches_reference(kind, causal, bwd_backend):
     run_ranks(_bwd_case, _world(), kind, causal, bwd_backend, backend="nccl")
+
+
+@pytest.mark.parametrize("head_dim,dtype", [(64, torch.bfloat16), (64, torch.float16),
+                                           (128, torch.float16)])
+def test_ring_fused_head_dim_and_dtype(head_dim, dtype):
+    run_ranks(_bwd_case, _world(), "zigzag", True, "fused", head_dim, dtype, backend="nccl")
 
 
 def _bwd_repeat_case(rank, world):
