@@ -1,10 +1,12 @@
-// Python bindings of the workload model, the schedulers, the shard plans and
-// the synthetic-input generator (module multi_gpu_flashattention_b200._sched).
+// Python bindings of the workload model, the schedulers, the shard plans, the
+// synthetic-input generator and the host (CPU) attention of the legacy ring
+// (module multi_gpu_flashattention_b200._sched).
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
 
 #include "../common/device_select.hpp"
 #include "../common/synth.hpp"
+#include "../host/cpu_attention.hpp"
 #include "scheduler.hpp"
 #include "shard_plan.hpp"
 #include "workload.hpp"
@@ -186,6 +188,52 @@ PYBIND11_MODULE(_sched, m) {
   m.def("choose_device", [](int device_count, int fallback_local_rank) {
     const mgfa::DeviceChoice c = mgfa::choose_device(device_count, fallback_local_rank);
     return py::make_tuple(c.device, c.local_rank, c.source, c.error);
+  });
+
+  // Host attention of the legacy CPU-compute ring (float32 buffers, row-major).
+  auto f32 = [](py::buffer& b, int64_t n, const char* what) {
+    py::buffer_info info = b.request(true);
+    if (info.itemsize != 4 || info.format != py::format_descriptor<float>::format() ||
+        info.size < n)
+      throw std::invalid_argument(std::string(what) + ": needs a float32 buffer of " +
+                                  std::to_string(n) + " elements");
+    return static_cast<float*>(info.ptr);
+  };
+  m.def(
+      "cpu_attention_partial",
+      [f32](py::buffer q, py::buffer k, py::buffer v, int64_t seq_q, int64_t seq_k, int64_t dim,
+            float scale, py::buffer acc, py::buffer mx, py::buffer l, int threads) {
+        const float* pq = f32(q, seq_q * dim, "q");
+        const float* pk = f32(k, seq_k * dim, "k");
+        const float* pv = f32(v, seq_k * dim, "v");
+        float* pa = f32(acc, seq_q * dim, "acc");
+        float* pm = f32(mx, seq_q, "m");
+        float* pl = f32(l, seq_q, "l");
+        py::gil_scoped_release nogil;
+        mgfa::host::cpu_attention_partial(pq, seq_q, pk, pv, seq_k, dim, scale, pa, pm, pl,
+                                          threads);
+      },
+      py::arg("q"), py::arg("k"), py::arg("v"), py::arg("seq_q"), py::arg("seq_k"),
+      py::arg("dim"), py::arg("scale"), py::arg("acc"), py::arg("m"), py::arg("l"),
+      py::arg("threads") = 0);
+  m.def(
+      "cpu_merge_online_softmax",
+      [f32](py::buffer mr, py::buffer lr, py::buffer ar, py::buffer mn, py::buffer ln,
+            py::buffer an, int64_t seq_q, int64_t dim) {
+        float* pm = f32(mr, seq_q, "m");
+        float* pl = f32(lr, seq_q, "l");
+        float* pa = f32(ar, seq_q * dim, "acc");
+        const float* qm = f32(mn, seq_q, "m_new");
+        const float* ql = f32(ln, seq_q, "l_new");
+        const float* qa = f32(an, seq_q * dim, "acc_new");
+        py::gil_scoped_release nogil;
+        mgfa::host::cpu_merge_online_softmax(pm, pl, pa, qm, ql, qa, seq_q, dim);
+      });
+  m.def("cpu_normalize", [f32](py::buffer acc, py::buffer l, int64_t seq_q, int64_t dim) {
+    float* pa = f32(acc, seq_q * dim, "acc");
+    const float* pl = f32(l, seq_q, "l");
+    py::gil_scoped_release nogil;
+    mgfa::host::cpu_normalize(pa, pl, seq_q, dim);
   });
 
   // Synthetic inputs (fills a Python buffer-protocol object of float32).

@@ -3,11 +3,14 @@ tests/benchmark_single_gpu_shapes.py, on this framework's sm_100a kernels).
 
     python -m multi_gpu_flashattention_b200.benchmarks.single_gpu_shapes \
         [--shapes 256x256 1024x1024 ...] [--batch-size 2] [--num-heads 8]
-        [--head-dim 64|128] [--dtype bf16|fp16] [--warmup 10] [--repeats 50] [--causal|--no-causal]
-        [--backward] [--csv-out results/single_gpu_shapes.csv]
+        [--head-dim 64|128] [--dtype float16|bfloat16] [--warmup 5] [--repeats 20]
+        [--causal|--no-causal] [--backward] [--csv-out results/single_gpu_shapes.csv]
 
-Same columns as the reference's CSV plus TFLOP/s. Causal active elements are
-counted top-left aligned like the reference (query i sees keys 0..i)."""
+Defaults, table and CSV columns are the reference's (fp16, head_dim 64, batch 2,
+8 heads, causal; tests/benchmark_single_gpu_shapes.py:188-210), with a TFLOP/s
+column added. Causal active elements are counted top-left aligned like the
+reference (query i sees keys 0..i). A shape that fails (e.g. out of memory) is
+reported and skipped."""
 from __future__ import annotations
 
 import argparse
@@ -17,7 +20,8 @@ from statistics import mean, pstdev
 
 import torch
 
-DTYPES = {"bf16": torch.bfloat16, "fp16": torch.float16}
+DTYPES = {"float16": torch.float16, "bfloat16": torch.bfloat16,
+          "fp16": torch.float16, "bf16": torch.bfloat16}
 
 from ..ops.flash import flash_attn_bwd, flash_attn_fwd
 
@@ -69,14 +73,26 @@ def bench(sq, sk, a):
         e.record()
         e.synchronize()
         times.append(s.elapsed_time(e))
-    act = active_elements(sq, sk, a.causal) * a.batch_size * a.num_heads
-    flops = 4 * act * a.head_dim * (2.5 if a.backward else 1.0)
+    per_seq = active_elements(sq, sk, a.causal)
+    flops = 4 * per_seq * a.batch_size * a.num_heads * a.head_dim * (2.5 if a.backward else 1.0)
     return {"seq_q": sq, "seq_k": sk, "batch_size": a.batch_size, "num_heads": a.num_heads,
-            "head_dim": a.head_dim, "dtype": str(DTYPES[a.dtype]).replace("torch.", ""), "causal": a.causal,
-            "active_elements": act, "avg_ms": mean(times), "std_ms": pstdev(times),
-            "min_ms": min(times), "max_ms": max(times),
-            "peak_mem_mb": torch.cuda.max_memory_allocated(dev) / 2 ** 20,
+            "head_dim": a.head_dim, "dtype": str(DTYPES[a.dtype]).replace("torch.", ""),
+            "causal": a.causal, "active_per_seq": per_seq, "total_active": per_seq * a.batch_size,
+            "avg_ms": mean(times), "std_ms": pstdev(times), "min_ms": min(times),
+            "max_ms": max(times), "peak_mem_mb": torch.cuda.max_memory_allocated(dev) / 2 ** 20,
             "tflops": flops / (mean(times) * 1e-3) / 1e12}
+
+
+def print_results(rows):
+    header = (f"{'shape':>12} {'active/seq':>12} {'avg_ms':>10} {'std_ms':>10} {'min_ms':>10} "
+              f"{'max_ms':>10} {'peak_mem(MB)':>14} {'TFLOP/s':>9}")
+    print(header)
+    print("-" * len(header))
+    for r in rows:
+        shape = f"{r['seq_q']}x{r['seq_k']}"
+        print(f"{shape:>12} {r['active_per_seq']:>12d} {r['avg_ms']:>10.3f} {r['std_ms']:>10.3f} "
+              f"{r['min_ms']:>10.3f} {r['max_ms']:>10.3f} {r['peak_mem_mb']:>14.1f} "
+              f"{r['tflops']:>9.1f}", flush=True)
 
 
 def main():
@@ -84,30 +100,33 @@ def main():
     ap.add_argument("--shapes", nargs="+", default=DEFAULT_SHAPES)
     ap.add_argument("--batch-size", type=int, default=2)
     ap.add_argument("--num-heads", type=int, default=8)
-    ap.add_argument("--head-dim", type=int, default=128, choices=[64, 128])
-    ap.add_argument("--dtype", default="bf16", choices=sorted(DTYPES))
-    ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--repeats", type=int, default=50)
+    ap.add_argument("--head-dim", type=int, default=64, choices=[64, 128])
+    ap.add_argument("--dtype", default="float16", choices=sorted(DTYPES))
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--repeats", type=int, default=20)
     ap.add_argument("--device", type=int, default=0)
     ap.add_argument("--backward", action="store_true")
-    g = ap.add_mutually_exclusive_group()
-    g.add_argument("--causal", dest="causal", action="store_true")
-    g.add_argument("--no-causal", dest="causal", action="store_false")
-    ap.set_defaults(causal=True)
-    ap.add_argument("--csv-out", default="")
+    ap.add_argument("--causal", action=argparse.BooleanOptionalAction, default=True)
+    ap.add_argument("--csv-out", default="results/single_gpu_shapes.csv")
     a = ap.parse_args()
+    if not torch.cuda.is_available():
+        raise RuntimeError("CUDA is not available.")
     rows = []
     for sh in a.shapes:
-        r = bench(*parse_shape(sh), a)
-        rows.append(r)
-        print(f"{r['seq_q']}x{r['seq_k']}: {r['avg_ms']:.3f} ms (+/- {r['std_ms']:.3f}) "
-              f"{r['tflops']:.1f} TFLOP/s peak_mem={r['peak_mem_mb']:.1f} MB", flush=True)
-    if a.csv_out:
+        sq, sk = parse_shape(sh)
+        try:
+            rows.append(bench(sq, sk, a))
+        except RuntimeError as exc:
+            print(f"Skipping {sh}: {exc}")
+        torch.cuda.empty_cache()
+    print_results(rows)
+    if a.csv_out and rows:
         os.makedirs(os.path.dirname(a.csv_out) or ".", exist_ok=True)
         with open(a.csv_out, "w", newline="") as f:
             w = csv.DictWriter(f, fieldnames=list(rows[0].keys()))
             w.writeheader()
             w.writerows(rows)
+        print(f"\nCSV saved to: {a.csv_out}")
     return 0
 
 

@@ -31,10 +31,12 @@ if which in ("all", "sched"):
                 "csrc/sched/scheduler.cpp",
                 "csrc/sched/shard_plan.cpp",
                 "csrc/sched/bindings.cpp",
+                "csrc/host/cpu_attention.cpp",
             ],
             include_dirs=[pybind11.get_include()],
             language="c++",
-            extra_compile_args=CXX_FLAGS + ["-fvisibility=hidden"],
+            extra_compile_args=CXX_FLAGS + ["-fvisibility=hidden", "-pthread"],
+            extra_link_args=["-pthread"],
         )
     )
 

@@ -164,3 +164,27 @@ def _poison_case(rank, world):
 
 def test_ring_forward_poisoned_slots_and_tags():
     run_ranks(_poison_case, _world(), backend="nccl")
+
+
+def _oneshot_case(rank, world, attention, backend, out_dir):
+    import numpy as np
+    import torch.distributed as dist
+    from multi_gpu_flashattention_b200.benchmarks import common, ring_oneshot
+    torch.cuda.set_device(rank)
+    ctx = common.Ctx(rank, world, torch.device("cuda", rank), dist.new_group(backend="gloo"))
+    args = ring_oneshot.parse(["--attention", attention, "--backend", backend, "--seq", "1024",
+                               "--out-dir", out_dir])
+    ring_oneshot.run(ctx, args)
+    seq, dim = 1024, 64
+    kv = torch.cat([ring_oneshot.legacy_inputs(r, seq, dim)[1] for r in range(world)]).double()
+    q = ring_oneshot.legacy_inputs(rank, seq, dim)[0].double()
+    ref = torch.softmax(q @ kv.T, dim=-1) @ kv
+    got = torch.from_numpy(np.fromfile(f"{out_dir}/ring_output_rank{rank}.bin", dtype="<f4"))
+    err = (got.double() - ref.view(-1)).abs().max().item()
+    assert err < 0.05, (rank, attention, backend, err)
+
+
+@pytest.mark.parametrize("attention,backend", [("gpu", "staged"), ("gpu", "nccl"),
+                                               ("gpu", "p2p"), ("cpu", "nccl")])
+def test_oneshot_legacy_ring(tmp_path, attention, backend):
+    run_ranks(_oneshot_case, _world(), attention, backend, str(tmp_path), backend="nccl")
