@@ -154,6 +154,14 @@ def run(ctx, args):
         bufs = None
     else:
         bufs = [kv_h.to(dev), torch.empty(seq, dim, device=dev)]
+    if args.backend == "nccl":
+        # NCCL connects a peer pair on its first send/recv; do that untimed so the
+        # step time is the transfer (the reference creates its communicator
+        # before timing, too)
+        warm = [torch.zeros(1, device=dev), torch.empty(1, device=dev)]
+        for w in dist.batch_isend_irecv([dist.P2POp(dist.isend, warm[0], right),
+                                         dist.P2POp(dist.irecv, warm[1], left)]):
+            w.wait()
     if cuda:
         torch.cuda.synchronize()
     ctx.barrier()

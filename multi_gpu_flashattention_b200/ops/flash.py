@@ -48,6 +48,34 @@ def tile_positions(n_tokens: int, device, start: int = 0) -> torch.Tensor:
     return torch.arange(n, dtype=torch.int32, device=device) * TILE + start
 
 
+_POS_CACHE: dict = {}
+_STATUS_CACHE: dict = {}
+
+
+def _default_positions(n_tokens: int, device) -> torch.Tensor:
+    """Cached read-only tile positions 0, 128, 256, ... (top-left aligned causal
+    self-attention); built once per (tile count, device) with a synchronous copy,
+    so later launches on any stream see finished data."""
+    n = (n_tokens + TILE - 1) // TILE
+    key = (n, str(device))
+    t = _POS_CACHE.get(key)
+    if t is None:
+        t = torch.tensor([i * TILE for i in range(n)], dtype=torch.int32).to(device)
+        _POS_CACHE[key] = t
+    return t
+
+
+def _scratch_status(device) -> torch.Tensor:
+    """Status word for calls that pass none: kernels only write it on an error
+    nobody asked to see, so one zeroed word per device serves every such call."""
+    key = str(device)
+    t = _STATUS_CACHE.get(key)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=device)
+        _STATUS_CACHE[key] = t
+    return t
+
+
 def _scale(q: torch.Tensor, softmax_scale: Optional[float]) -> float:
     return softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(q.shape[-1])
 
@@ -63,12 +91,12 @@ def flash_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bo
     B, Sq, Hq, _ = q.shape
     if causal:
         if q_tile_pos is None:
-            q_tile_pos = tile_positions(Sq, q.device)
+            q_tile_pos = _default_positions(Sq, q.device)
         if kv_tile_pos is None:
-            kv_tile_pos = tile_positions(k.shape[1], q.device)
+            kv_tile_pos = _default_positions(k.shape[1], q.device)
     o = out if out is not None else torch.empty_like(q)
     lse = torch.empty(B, Hq, Sq, dtype=torch.float32, device=q.device)
-    st = status if status is not None else torch.zeros(1, dtype=torch.int32, device=q.device)
+    st = status if status is not None else _scratch_status(q.device)
     C().flash_fwd(q, k, v, o, None, lse, _scale(q, softmax_scale), causal, q_tile_pos,
                   kv_tile_pos, False, True, st, int(wait_limit_ns))
     return o, lse
@@ -99,14 +127,14 @@ def flash_attn_bwd(dout, q, k, v, out, lse, causal: bool = False,
     (for ring attention: the merged LSE over all steps). Returns (dq, dk, dv) fp32."""
     if causal:
         if q_tile_pos is None:
-            q_tile_pos = tile_positions(q.shape[1], q.device)
+            q_tile_pos = _default_positions(q.shape[1], q.device)
         if kv_tile_pos is None:
-            kv_tile_pos = tile_positions(k.shape[1], q.device)
+            kv_tile_pos = _default_positions(k.shape[1], q.device)
     f32 = dict(dtype=torch.float32, device=q.device)
     dq = dq if dq is not None else torch.empty(q.shape, **f32)
     dk = dk if dk is not None else torch.empty(k.shape, **f32)
     dv = dv if dv is not None else torch.empty(v.shape, **f32)
-    st = status if status is not None else torch.zeros(1, dtype=torch.int32, device=q.device)
+    st = status if status is not None else _scratch_status(q.device)
     C().flash_bwd(dout.contiguous(), q, k, v, out, lse, dq, dk, dv, _scale(q, softmax_scale),
                   causal, q_tile_pos, kv_tile_pos, accumulate, lse2, delta, st, int(wait_limit_ns))
     return dq, dk, dv
