@@ -1,17 +1,22 @@
-# Standalone native tools (no Python needed):
-#   build/bin/rattn_demo     scheduler comparison CLI
-#   build/bin/verify_full    full-reference checker for output dumps
-# `make cuda-tools` adds the GPU benchmarks (see csrc/bench).
+# Standalone native tools (no Python needed to run them):
+#   build/bin/rattn_demo           scheduler comparison CLI
+#   build/bin/verify_full          full-reference checker for output dumps
+# `make cuda-tools` adds the GPU benchmark executables, linked against libtorch,
+# NCCL and this tree's sm_100a kernels (launch with `torchrun --no-python`):
+#   build/bin/ring_loop_bench      pure ring exchange (p2p | ce | nccl | staged)
+#   build/bin/ring_attention_bench ring attention (fused | nccl | staged; fp32 | bf16)
 CXX      ?= g++
 NVCC     ?= nvcc
+PY       ?= python
 CXXFLAGS ?= -O2 -std=c++17 -Wall -Wextra
 BIN      := build/bin
+OBJ      := build/obj
 SCHED    := csrc/sched/workload.cpp csrc/sched/scheduler.cpp csrc/sched/shard_plan.cpp
 
 all: $(BIN)/rattn_demo $(BIN)/verify_full
 
-$(BIN):
-	mkdir -p $(BIN)
+$(BIN) $(OBJ):
+	mkdir -p $@
 
 $(BIN)/rattn_demo: csrc/sched/rattn_demo.cpp $(SCHED) $(wildcard csrc/sched/*.hpp) | $(BIN)
 	$(CXX) $(CXXFLAGS) -o $@ csrc/sched/rattn_demo.cpp $(SCHED)
@@ -19,7 +24,45 @@ $(BIN)/rattn_demo: csrc/sched/rattn_demo.cpp $(SCHED) $(wildcard csrc/sched/*.hp
 $(BIN)/verify_full: csrc/bench/verify_full.cpp $(SCHED) csrc/common/synth.hpp | $(BIN)
 	$(CXX) $(CXXFLAGS) -pthread -o $@ csrc/bench/verify_full.cpp $(SCHED)
 
-clean:
-	rm -rf $(BIN)
+# ---------------------------------------------------------------- GPU executables
+TORCH_DIR := $(shell $(PY) -c "import os, torch; print(os.path.dirname(torch.__file__))" 2>/dev/null)
+NCCL_DIR  := $(shell $(PY) -c "import nvidia.nccl as n; print(list(n.__path__)[0])" 2>/dev/null)
+CUDA_HOME ?= /usr/local/cuda
+TORCH_INC := -isystem $(TORCH_DIR)/include -isystem $(TORCH_DIR)/include/torch/csrc/api/include \
+             -isystem $(NCCL_DIR)/include -isystem $(CUDA_HOME)/include -Icsrc
+TORCH_DEF := -D_GLIBCXX_USE_CXX11_ABI=1
+GPU_CXX   := $(CXX) -O3 -std=c++17 -fPIC -pthread $(TORCH_DEF) $(TORCH_INC)
+GPU_NVCC  := $(NVCC) -O3 -std=c++17 -lineinfo --expt-relaxed-constexpr \
+             -gencode arch=compute_100a,code=sm_100a -Xcompiler -fPIC $(TORCH_DEF) $(TORCH_INC) \
+             -D__CUDA_NO_HALF_OPERATORS__ -D__CUDA_NO_HALF_CONVERSIONS__ \
+             -D__CUDA_NO_BFLOAT16_CONVERSIONS__ -D__CUDA_NO_HALF2_OPERATORS__
+GPU_LIBS  := -L$(TORCH_DIR)/lib -Wl,-rpath,$(TORCH_DIR)/lib -ltorch -ltorch_cpu -ltorch_cuda \
+             -lc10 -lc10_cuda -L$(NCCL_DIR)/lib -Wl,-rpath,$(NCCL_DIR)/lib -l:libnccl.so.2 \
+             -L$(CUDA_HOME)/lib64 -lcudart -pthread
+HDRS      := $(wildcard csrc/*/*.hpp csrc/*/*.cuh csrc/*/*.h)
 
-.PHONY: all clean
+$(OBJ)/%.o: csrc/%.cpp $(HDRS) | $(OBJ)
+	@mkdir -p $(dir $@)
+	$(GPU_CXX) -c $< -o $@
+
+$(OBJ)/%.o: csrc/%.cu $(HDRS) | $(OBJ)
+	@mkdir -p $(dir $@)
+	$(GPU_NVCC) -c $< -o $@
+
+SCHED_OBJ := $(OBJ)/sched/workload.o $(OBJ)/sched/scheduler.o $(OBJ)/sched/shard_plan.o
+COMM_OBJ  := $(OBJ)/bench/dist_env.o $(OBJ)/comm/symmetric.o $(OBJ)/kernels/ring_exchange.o
+
+$(BIN)/ring_loop_bench: $(OBJ)/bench/ring_loop_bench.o $(COMM_OBJ) | $(BIN)
+	$(CXX) -o $@ $^ $(GPU_LIBS)
+
+$(BIN)/ring_attention_bench: $(OBJ)/bench/ring_attention_bench.o $(COMM_OBJ) $(SCHED_OBJ) \
+    $(OBJ)/kernels/flash_fwd_sm100.o $(OBJ)/kernels/flash_bwd_sm100.o $(OBJ)/kernels/legacy_fp32.o \
+    $(OBJ)/ops/attn_api.o | $(BIN)
+	$(CXX) -o $@ $^ $(GPU_LIBS)
+
+cuda-tools: $(BIN)/ring_loop_bench $(BIN)/ring_attention_bench
+
+clean:
+	rm -rf $(BIN) $(OBJ)
+
+.PHONY: all cuda-tools clean

@@ -1,0 +1,135 @@
+#include "dist_env.hpp"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstdlib>
+#include <cstring>
+#include <stdexcept>
+#include <thread>
+
+#include "../common/device_select.hpp"
+
+namespace mgfa::bench {
+
+namespace {
+
+int env_int(const char* name, int dflt) {
+  const char* v = std::getenv(name);
+  return (v && *v) ? std::atoi(v) : dflt;
+}
+
+std::vector<uint8_t> to_bytes(const void* p, size_t n) {
+  const uint8_t* b = static_cast<const uint8_t*>(p);
+  return std::vector<uint8_t>(b, b + n);
+}
+
+}  // namespace
+
+void nccl_check(ncclResult_t r, const char* what) {
+  if (r != ncclSuccess)
+    throw std::runtime_error(std::string(what) + ": " + ncclGetErrorString(r));
+}
+
+Dist Dist::from_env(int timeout_s) {
+  Dist d;
+  d.world_ = env_int("WORLD_SIZE", 1);
+  d.rank_ = env_int("RANK", 0);
+  if (d.world_ < 1 || d.rank_ < 0 || d.rank_ >= d.world_)
+    throw std::runtime_error("bad RANK / WORLD_SIZE");
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0)
+    throw std::runtime_error("no CUDA device");
+  const auto choice = mgfa::choose_device(count, d.rank_);
+  if (!choice.error.empty()) throw std::runtime_error(choice.error);
+  d.local_rank_ = choice.local_rank;
+  d.device_ = choice.device;
+  if (cudaSetDevice(d.device_) != cudaSuccess) throw std::runtime_error("cudaSetDevice failed");
+  if (d.world_ > 1) {
+    const char* addr = std::getenv("MASTER_ADDR");
+    c10d::TCPStoreOptions o;
+    o.port = uint16_t(env_int("MASTER_PORT", 29500));
+    const char* agent = std::getenv("TORCHELASTIC_USE_AGENT_STORE");
+    const bool use_agent = agent && std::string(agent) == "True";
+    o.isServer = !use_agent && d.rank_ == 0;
+    o.numWorkers = use_agent ? std::nullopt : std::optional<size_t>(size_t(d.world_));
+    o.waitWorkers = !use_agent;
+    o.timeout = std::chrono::seconds(timeout_s);
+    d.store_ = c10::make_intrusive<c10d::TCPStore>(addr && *addr ? addr : "127.0.0.1", o);
+  }
+  return d;
+}
+
+Dist::~Dist() {
+  if (comm_) ncclCommDestroy(comm_);
+}
+
+// Keys live under torchrun's run id (when set), so a reused agent store never
+// hands a later run an earlier run's values.
+std::string Dist::key(const char* kind, uint64_t seq) const {
+  const char* run = std::getenv("TORCHELASTIC_RUN_ID");
+  return std::string("mgfa_bench/") + (run ? run : "") + "/" + kind + "/" + std::to_string(seq);
+}
+
+void Dist::barrier() {
+  if (world_ == 1) return;
+  const std::string k = key("barrier", coll_seq_++);
+  if (store_->add(k, 1) == world_) store_->set(k + "/done", {1});
+  store_->wait({k + "/done"});
+}
+
+std::vector<std::string> Dist::all_gather(const std::string& mine) {
+  if (world_ == 1) return {mine};
+  const std::string k = key("gather", coll_seq_++);
+  store_->set(k + "/" + std::to_string(rank_), to_bytes(mine.data(), mine.size()));
+  std::vector<std::string> out(static_cast<size_t>(world_));
+  for (int r = 0; r < world_; ++r) {
+    const auto v = store_->get(k + "/" + std::to_string(r));
+    out[size_t(r)].assign(v.begin(), v.end());
+  }
+  return out;
+}
+
+std::vector<double> Dist::max(const std::vector<double>& v) {
+  const auto all = all_gather(std::string(reinterpret_cast<const char*>(v.data()),
+                                          v.size() * sizeof(double)));
+  std::vector<double> out = v;
+  for (const auto& s : all) {
+    if (s.size() != v.size() * sizeof(double)) throw std::runtime_error("max: size mismatch");
+    const double* p = reinterpret_cast<const double*>(s.data());
+    for (size_t i = 0; i < v.size(); ++i) out[i] = std::max(out[i], p[i]);
+  }
+  return out;
+}
+
+void Dist::host_sendrecv(const void* send, size_t n, int to, void* recv, int from) {
+  const uint64_t seq = p2p_seq_++;
+  const std::string out_key =
+      key("p2p", seq) + "/" + std::to_string(rank_) + "->" + std::to_string(to);
+  const std::string in_key =
+      key("p2p", seq) + "/" + std::to_string(from) + "->" + std::to_string(rank_);
+  store_->set(out_key, to_bytes(send, n));
+  const auto v = store_->get(in_key);
+  if (v.size() != n) throw std::runtime_error("host_sendrecv: size mismatch");
+  std::memcpy(recv, v.data(), n);
+  store_->deleteKey(in_key);
+}
+
+ncclComm_t Dist::nccl() {
+  if (comm_) return comm_;
+  ncclUniqueId id;
+  const std::string k = key("nccl_id", coll_seq_++);
+  if (rank_ == 0) {
+    nccl_check(ncclGetUniqueId(&id), "ncclGetUniqueId");
+    store_->set(k, to_bytes(&id, sizeof(id)));
+  } else {
+    const auto v = store_->get(k);
+    if (v.size() != sizeof(id)) throw std::runtime_error("bad NCCL id");
+    std::memcpy(&id, v.data(), sizeof(id));
+  }
+  nccl_check(ncclCommInitRank(&comm_, world_, id, rank_), "ncclCommInitRank");
+  return comm_;
+}
+
+}  // namespace mgfa::bench

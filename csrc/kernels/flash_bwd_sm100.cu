@@ -17,7 +17,7 @@
 // S may overwrite it; P/dS buffers are consumed by MMAs issued earlier, and the
 // tensor pipe runs a thread's MMAs in order).
 // The reference prototype has no backward pass at all.
-#include <torch/extension.h>
+#include <torch/types.h>
 #include "../common/check.hpp"
 #include <ATen/cuda/CUDAContext.h>
 

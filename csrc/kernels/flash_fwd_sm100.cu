@@ -21,7 +21,7 @@
 // for S(j+1) also proves PV(j) finished, so softmax may rescale O right away.
 // O is rescaled only when the running max grows by more than 2^8 (the stale
 // max keeps P <= 256, exact in fp32 sums and bf16 P).
-#include <torch/extension.h>
+#include <torch/types.h>
 #include "../common/check.hpp"
 #include <ATen/cuda/CUDAContext.h>
 

@@ -12,7 +12,7 @@
 //     the merged state back (no separate merge kernel needed).
 //   legacy_merge:   the reference's merge (scale each side by exp(m_i - max)).
 //   legacy_normalize: acc / l on the device.
-#include <torch/extension.h>
+#include <torch/types.h>
 #include "../common/check.hpp"
 #include <ATen/cuda/CUDAContext.h>
 

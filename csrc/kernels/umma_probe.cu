@@ -5,7 +5,7 @@
 //   C2 = A * V     A copied into TMEM as packed bf16 pairs (TS form),
 //                  V [64 x 128] bf16 MN-major (N contiguous), loaded by TMA
 // Both accumulators are read back with tcgen05.ld (32x32b) and stored as fp32.
-#include <torch/extension.h>
+#include <torch/types.h>
 #include "../common/check.hpp"
 #include <ATen/cuda/CUDAContext.h>
 

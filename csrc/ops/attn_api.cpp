@@ -1,5 +1,5 @@
 // Torch-facing entry points of the attention kernels.
-#include <torch/extension.h>
+#include <torch/types.h>
 #include "../common/check.hpp"
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>

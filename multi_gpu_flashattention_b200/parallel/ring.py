@@ -120,12 +120,15 @@ def _fwd_nccl(q, k, v, layout, causal, scale, group, status, wait_ns, overlap=Tr
     o_state = torch.empty(q.shape, dtype=torch.float32, device=q.device)
     lse = torch.empty(q.shape[0], q.shape[2], q.shape[1], dtype=torch.float32, device=q.device)
     out = torch.empty_like(q)
+    # step t computes on cur while receive pair t % 2 fills; the caller's k and v
+    # (saved for the backward pass) are never written
     cur = (k, v)
-    nxt = (torch.empty_like(k), torch.empty_like(v))
+    recv = [(torch.empty_like(k), torch.empty_like(v)) for _ in range(min(2, world - 1))]
     for t in range(world):
         owner = (rank - t) % world
         reqs = []
         if t < world - 1:
+            nxt = recv[t % 2]
             comm.wait_stream(compute)
             with torch.cuda.stream(comm):
                 ops = [dist.P2POp(dist.isend, cur[0], right, group),
@@ -147,7 +150,7 @@ def _fwd_nccl(q, k, v, layout, causal, scale, group, status, wait_ns, overlap=Tr
                     for rq in reqs:
                         rq.wait()
                 compute.wait_stream(comm)
-            cur, nxt = nxt, cur
+            cur = nxt
     return out, lse
 
 
