@@ -61,8 +61,7 @@ class RingEngine {
   }
 
   // q [B,Sq,Hq,D]; k, v [B,L,Hkv,D] contiguous local shards, bf16 or fp16, D = 64 or
-  // 128 (same L on
-  // every rank; owner o's first kv_lens[o] rows are valid).
+  // 128 (same L on every rank; owner o's first kv_lens[o] rows are valid).
   // kv_tile_pos [P, ceil(L/128)] int32: tile positions of each owner's shard as seen
   // from this rank's queries; q_tile_pos [ceil(Sq/128)] int32 (causal only).
   std::vector<torch::Tensor> forward(torch::Tensor q, torch::Tensor k, torch::Tensor v,

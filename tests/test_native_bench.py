@@ -1,0 +1,116 @@
+"""Native benchmark executables (build/bin/ring_loop_bench, ring_attention_bench)
+launched by torchrun --no-python: argument handling on the host, and on 2+ GPUs
+the RESULT lines, the reference checker on fp32 dumps and the bf16 dumps
+against the fp32 oracle."""
+import os
+import socket
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+BIN = os.path.join(ROOT, "build", "bin")
+
+
+def _exe(name):
+    p = os.path.join(BIN, name)
+    if not os.path.exists(p):
+        pytest.skip(f"{name} not built (make cuda-tools)")
+    return p
+
+
+def test_usage_and_bad_arguments():
+    for name in ("ring_loop_bench", "ring_attention_bench"):
+        exe = _exe(name)
+        p = subprocess.run([exe, "--no-such-flag"], capture_output=True, text=True, timeout=60)
+        assert p.returncode == 1 and "Usage:" in p.stdout
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _torchrun(exe, args, nproc, cwd, env=None, timeout=300):
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={nproc}", "--master-addr=127.0.0.1", f"--master-port={_port()}",
+           "--no-python", exe] + [str(a) for a in args]
+    e = dict(os.environ)
+    e.update(env or {})
+    p = subprocess.run(cmd, capture_output=True, text=True, cwd=cwd, env=e, timeout=timeout)
+    assert p.returncode == 0, p.stdout[-3000:] + p.stderr[-3000:]
+    return p.stdout
+
+
+def _world():
+    return min(torch.cuda.device_count(), 4)
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+@pytest.mark.parametrize("backend", ["p2p", "ce", "nccl", "staged"])
+def test_ring_loop_bench(tmp_path, backend):
+    out = _torchrun(_exe("ring_loop_bench"), [1 << 20, 2, 3, "--backend", backend], _world(),
+                    tmp_path)
+    line = [l for l in out.splitlines() if l.startswith("RESULT")]
+    assert len(line) == 1 and f"backend={backend}" in line[0] and f"ranks={_world()}" in line[0]
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+def test_ring_loop_bench_payload_mode(tmp_path):
+    out = _torchrun(_exe("ring_loop_bench"), [0, 1, 2, "--payload-tokens", 256], _world(), tmp_path)
+    assert f"bytes={256 * 8 * 128 * 4}" in out
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+@pytest.mark.parametrize("extra", [["--backend", "nccl"], ["--backend", "staged"],
+                                   ["--backend", "nccl", "--overlap"]])
+def test_ring_attention_bench_fp32_passes_verify_full(tmp_path, extra):
+    size = 1024 * 64 * 4
+    out = _torchrun(_exe("ring_attention_bench"), [size, 1, 2] + extra, _world(), tmp_path,
+                    env={"ATTENTION_DUMP_OUTPUT": "1", "ATTENTION_PRINT_SHARDS": "1"})
+    assert "avg_total=" in out
+    assert "kv_owner=" in out  # ATTENTION_PRINT_SHARDS step lines
+    vf = os.path.join(BIN, "verify_full")
+    if not os.path.exists(vf):
+        pytest.skip("verify_full not built")
+    p = subprocess.run([vf, str(tmp_path), str(_world()), str(size)], capture_output=True,
+                       text=True, timeout=300)
+    assert p.returncode == 0 and "ALL PASS" in p.stdout, p.stdout[-2000:]
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+@pytest.mark.parametrize("backend,layout", [("fused", "zigzag"), ("nccl", "zigzag"),
+                                            ("staged", "contiguous")])
+def test_ring_attention_bench_bf16_dumps(tmp_path, backend, layout):
+    from multi_gpu_flashattention_b200._ext import sched
+    from multi_gpu_flashattention_b200.ops.reference import attention_ref
+    from multi_gpu_flashattention_b200.parallel.layouts import RingLayout
+    P, H, D, L = _world(), 2, 128, 1024
+    size = L * H * D * 4
+    _torchrun(_exe("ring_attention_bench"),
+              [size, 1, 2, "--numerics", "bf16", "--init", "randn", "--backend", backend,
+               "--layout", layout, "--causal", "--heads", H, "--seed", 3, "--json"],
+              P, tmp_path, env={"ATTENTION_DUMP_OUTPUT": "1"})
+    seq = L * P
+    S = sched()
+    full = []
+    for stream in (0, 1, 2):
+        buf = np.empty(seq * H * D, dtype=np.float32)
+        S.fill_randn_rows(buf, 3, stream, list(range(seq)), H * D)
+        full.append(torch.from_numpy(buf).view(1, seq, H, D).bfloat16())
+    ref, _ = attention_ref(*full, causal=True)
+    lay = RingLayout(layout, seq, P)
+    for r in range(P):
+        got = torch.from_numpy(np.fromfile(tmp_path / f"ring_output_rank{r}.bin", dtype="<f4"))
+        got = got.view(-1, H, D)[: lay.local_len(r)]
+        exp = lay.shard(ref, r)[0, : lay.local_len(r)]
+        err = (got - exp).abs().max().item()
+        assert err < 2e-2, (r, err)
