@@ -4,7 +4,7 @@
 // executable with a --backend flag, without MPI.
 //
 //   torchrun --nproc-per-node N --no-python build/bin/ring_attention_bench \
-//       <kv_size_bytes> [warmup=10] [iters=100] [--backend fused|nccl|staged]
+//       <kv_size_bytes> [warmup=10] [iters=100] [--backend fused|p2p_unfused|nccl|staged]
 //       [--numerics fp32|bf16] [--init legacy|randn] [--layout contiguous|zigzag|
 //       striped|scheduler] [--policy dp|lpt] [--causal] [--heads H] [--kv-heads H]
 //       [--head-dim D] [--seed S] [--overlap] [--json]
@@ -17,7 +17,8 @@
 //     reproduces the reference's inputs (K == V, no softmax scale) so
 //     `verify_full <dir> N kv_size` checks the dumps.
 //   --numerics bf16 (head_dim 64 or 128): the sm_100a kernels; fused (transport
-//     inside the attention kernel), nccl (attention kernel per step + NCCL
+//     inside the attention kernel), p2p_unfused (the same NVLink push transport as
+//     a separate kernel on a second stream), nccl (attention kernel per step + NCCL
 //     send/recv on a second stream) or staged (device -> host -> store -> device).
 // Environment as in the reference: ATTENTION_PRINT_SHARDS=1 prints token ranges
 // and per-step owners of iteration 0; ATTENTION_DUMP_OUTPUT=1 writes
@@ -112,7 +113,8 @@ bool parse(int argc, char** argv, Args* a) {
   }
   if (a->backend.empty()) a->backend = a->numerics == "bf16" ? "fused" : "nccl";
   return (a->numerics == "fp32" || a->numerics == "bf16") &&
-         (a->backend == "fused" || a->backend == "nccl" || a->backend == "staged") &&
+         (a->backend == "fused" || a->backend == "p2p_unfused" || a->backend == "nccl" ||
+          a->backend == "staged") &&
          (a->init == "legacy" || a->init == "randn");
 }
 
@@ -429,13 +431,14 @@ class Bf16Ring {
       kv_lens_.push_back(m.plan.local_len(o));
     }
     kvtp_ = i32_dev(all, dev).view({P, -1});
-    if (a.backend == "fused") {
+    if (a.backend == "fused" || a.backend == "p2p_unfused") {
       const int64_t shard = k.numel() * k.element_size();
       int64_t slot = std::max<int64_t>(shard, 1 << 20);
       slot = (slot + (2 << 20) - 1) / (2 << 20) * (2 << 20);
       const char* ch = std::getenv("MGFA_RING_CHUNKS");
       eng_ = std::make_unique<mgfa::RingEngine>(r, P, dev, slot, ch ? std::atoi(ch) : 0);
       eng_->connect(d.all_gather(eng_->ipc_handle()));
+      eng_->set_fused(a.backend == "fused");
       cudaDeviceSynchronize();
       d.barrier();
     } else {
@@ -580,7 +583,8 @@ static int run_main(int argc, char** argv) {
   Args a;
   if (!parse(argc, argv, &a)) {
     std::printf("Usage: ring_attention_bench <kv_size_bytes> [warmup] [iters] "
-                "[--backend fused|nccl|staged] [--numerics fp32|bf16] [--init legacy|randn] "
+                "[--backend fused|p2p_unfused|nccl|staged] [--numerics fp32|bf16] "
+                "[--init legacy|randn] "
                 "[--layout contiguous|zigzag|striped|scheduler] [--policy dp|lpt] [--causal] "
                 "[--heads H] [--kv-heads H] [--head-dim D] [--seed S] [--overlap] [--json]\n");
     return 1;
@@ -607,7 +611,7 @@ static int run_main(int argc, char** argv) {
          ", warmup >= 0, iters > 0.");
     return 1;
   }
-  if (a.numerics == "fp32" && (D != 64 || a.backend == "fused")) {
+  if (a.numerics == "fp32" && (D != 64 || a.backend == "fused" || a.backend == "p2p_unfused")) {
     log0("fp32 numerics: head_dim 64, backends nccl or staged");
     return 1;
   }

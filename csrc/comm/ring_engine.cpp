@@ -17,6 +17,8 @@ void register_ring_engine(py::module& m) {
       .def("set_drop_signal_step", &RingEngine::set_drop_signal_step)
       .def("set_trace", &RingEngine::set_trace)
       .def("set_dependent_launch", &RingEngine::set_dependent_launch)
+      .def("set_fused", &RingEngine::set_fused)
+      .def("fused", &RingEngine::fused)
       .def("poison_slots", &RingEngine::poison_slots)
       .def("last_trace", &RingEngine::last_trace)
       .def("forward", &RingEngine::forward, py::arg("q"), py::arg("k"), py::arg("v"),

@@ -29,6 +29,7 @@
 #include "../common/check.hpp"
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
 
 #include <cstdio>
 #include <memory>
@@ -39,6 +40,11 @@
 #include "symmetric.hpp"
 
 namespace mgfa {
+
+cudaError_t ring_push_launch(const RingPush& push, const RingConsume& consume, uint32_t* status,
+                             uint64_t limit_ns, int n_ctas, cudaStream_t stream);
+cudaError_t ring_signal_launch(const RingPush& push, const RingConsume& consume,
+                               cudaStream_t stream);
 
 class RingEngine {
  public:
@@ -185,6 +191,8 @@ class RingEngine {
       // step of a call is fully ordered after everything before it
       p.dependent_launch = (t > 0 && pdl_) ? 1 : 0;
 
+      RingPush push_x;     // the standalone push kernel's (unfused transport)
+      RingConsume wait_x;  // its wait for the slot it forwards
       if (transport && t < P - 1) {
         const int sn = (t + 1) % kSlots;
         p.push.enabled = 1;
@@ -216,13 +224,58 @@ class RingEngine {
         p.consume.tag = buf_.flag(r, comm::kTag0 + s);
         p.consume.expected_tag = slot_tag(owner, calls_);
       }
+      if (transport && !fused_) {
+        // Unfused transport: the same flags, but the shard moves in the
+        // standalone all-SM push kernel on a second stream; the attention kernel
+        // only waits for its slot, and a signal kernel releases the slot once
+        // both the attention and the push kernel are done with it. Step t+1's
+        // attention is stream-ordered after step t's push, so a grid spinning
+        // on its arrivals never holds SMs that a push it waits for needs.
+        p.dependent_launch = 0;
+        push_x = p.push;
+        push_x.n_chunks = uint32_t(2 * num_sms_);
+        push_x.peer_tag = nullptr;
+        p.push = RingPush();
+        if (t > 0) {
+          p.consume.arrivals_target = uint32_t(2 * num_sms_);
+          p.consume.done_counter = nullptr;
+          p.consume.tag = nullptr;
+          wait_x = p.consume;
+        }
+      }
       if (trace_)
         p.trace = reinterpret_cast<uint64_t*>(last_trace_.data_ptr<int64_t>()) +
                   int64_t(t) * grid * kTraceWords;
       char label[64];
       std::snprintf(label, sizeof(label), "ring step %d (kv owner %d)", t, owner);
       nvtxRangePushA(label);
-      flash_fwd_launch_maps(mq, mk, mv, p, stream);
+      cudaEvent_t pushed = nullptr;
+      if (transport && !fused_ && push_x.enabled) {
+        if (!push_stream_) push_stream_ = c10::cuda::getStreamFromPool(false, buf_.device());
+        cudaStream_t ps = push_stream_->stream();
+        cudaEvent_t start;
+        C10_CUDA_CHECK(cudaEventCreateWithFlags(&start, cudaEventDisableTiming));
+        C10_CUDA_CHECK(cudaEventRecord(start, stream));
+        C10_CUDA_CHECK(cudaStreamWaitEvent(ps, start, 0));
+        C10_CUDA_CHECK(cudaEventDestroy(start));
+        flash_fwd_launch_maps(mq, mk, mv, p, stream);
+        C10_CUDA_CHECK(ring_push_launch(push_x, wait_x, p.status, uint64_t(wait_limit_ns),
+                                        2 * num_sms_, ps));
+        C10_CUDA_CHECK(cudaEventCreateWithFlags(&pushed, cudaEventDisableTiming));
+        C10_CUDA_CHECK(cudaEventRecord(pushed, ps));
+        C10_CUDA_CHECK(cudaStreamWaitEvent(stream, pushed, 0));
+        C10_CUDA_CHECK(cudaEventDestroy(pushed));
+      } else {
+        flash_fwd_launch_maps(mq, mk, mv, p, stream);
+      }
+      if (transport && !fused_ && t > 0) {
+        RingConsume rel;
+        rel.enabled = 1;
+        rel.arrivals = buf_.flag(r, comm::kArrivals0 + s);
+        rel.left_credit = buf_.flag(left, comm::kCredit0 + s);
+        rel.left_credit_value = uses_[s] + 1;
+        C10_CUDA_CHECK(ring_signal_launch(RingPush(), rel, stream));
+      }
       nvtxRangePop();
       if (transport && t > 0) uses_[s] += 1;
     }
@@ -231,6 +284,14 @@ class RingEngine {
   }
 
   static uint32_t slot_tag(int owner, uint32_t call) { return uint32_t(owner + 1) | (call << 8); }
+
+ public:
+  // false: move the shard with the standalone push kernel instead of the
+  // attention kernel's push warps (the unfused ablation of the same transport).
+  void set_fused(bool on) { fused_ = on; }
+  bool fused() const { return fused_; }
+
+ private:
 
  public:
 
@@ -271,6 +332,8 @@ class RingEngine {
   int drop_signal_step_ = -1;
   bool trace_ = false;
   bool pdl_ = true;
+  bool fused_ = true;
+  c10::optional<c10::cuda::CUDAStream> push_stream_;
   uint32_t calls_ = 0;
   int num_sms_ = 148;
   torch::Tensor last_trace_;

@@ -448,8 +448,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* dst = p.trace + uint64_t(linear_cta) * kTraceWords;
     for (int i = 0; i < kTraceWords; ++i) dst[i] = s.trace[i];
   }
-  if (p.consume.enabled && threadIdx.x == 0) {
-    // The last CTA to finish tells the left neighbour this slot may be reused.
+  if (p.consume.enabled && p.consume.done_counter && threadIdx.x == 0) {
+    // The last CTA to finish tells the left neighbour this slot may be reused
+    // (without a done counter a separate signal kernel releases the slot).
     __threadfence();
     const uint32_t prev = atomicAdd(p.consume.done_counter, 1u);
     if (prev == p.consume.done_target) {

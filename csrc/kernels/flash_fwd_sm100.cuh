@@ -35,7 +35,8 @@ struct RingConsume {
   uint32_t* arrivals = nullptr;        // local arrival counter of the slot being read
   uint32_t arrivals_target = 0;        // wait until *arrivals >= target before reading;
                                        // the last CTA resets it to 0
-  uint32_t* done_counter = nullptr;    // local counter of CTAs finished with this step
+  uint32_t* done_counter = nullptr;    // local counter of CTAs finished with this step;
+                                       // null: only wait, a separate kernel releases
   uint32_t done_target = 0;            // value the last CTA sees (grid size - 1); it
                                        // resets the counter to 0
   uint32_t* left_credit = nullptr;     // left neighbour's credit word for this slot

@@ -60,7 +60,7 @@ __global__ void __launch_bounds__(512)
     }
   }
   __syncthreads();
-  if (consume.enabled && threadIdx.x == 0) {
+  if (consume.enabled && consume.done_counter && threadIdx.x == 0) {
     __threadfence();
     const uint32_t prev = atomicAdd(consume.done_counter, 1u);
     if (prev == consume.done_target) {

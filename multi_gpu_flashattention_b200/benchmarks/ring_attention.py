@@ -14,7 +14,9 @@ Shapes follow the reference: tokens per rank = kv_size_bytes / (heads * head_dim
   no softmax scale) so `verify_full <dir> N kv_size` checks the dumps;
   --init randn uses the seeded N(0,1) streams and scale 1/sqrt(d)
   (`verify_full <dir> N kv_size --init randn`).
---numerics bf16 (head_dim 128): the sm_100a kernels, backends fused | nccl | staged.
+--numerics bf16 (head_dim 128): the sm_100a kernels, backends fused | p2p_unfused |
+  nccl | staged (p2p_unfused: the fused path's NVLink push transport as a separate
+  kernel on a second stream, the ablation that isolates the fusion).
 
 Environment (as in the reference): ATTENTION_PRINT_SHARDS=1 prints token ranges
 and the owner of the shard computed/received at each step of iteration 0;
@@ -36,7 +38,7 @@ from .._ext import C, sched as _sched
 from ..parallel.layouts import RingLayout
 from . import common
 
-COMM_NAME = {"nccl": "NCCL", "staged": "MPI", "fused": "P2P"}
+COMM_NAME = {"nccl": "NCCL", "staged": "MPI", "fused": "P2P", "p2p_unfused": "P2P"}
 
 
 def parse():
@@ -44,7 +46,7 @@ def parse():
     ap.add_argument("kv_size", type=int, nargs="?")
     ap.add_argument("warmup", type=int, nargs="?", default=10)
     ap.add_argument("iters", type=int, nargs="?", default=100)
-    ap.add_argument("--backend", default=None, choices=["fused", "nccl", "staged"])
+    ap.add_argument("--backend", default=None, choices=["fused", "p2p_unfused", "nccl", "staged"])
     ap.add_argument("--numerics", default="fp32", choices=["fp32", "bf16"])
     ap.add_argument("--init", default="legacy", choices=["legacy", "randn"])
     ap.add_argument("--layout", default="contiguous",
@@ -282,7 +284,7 @@ class Bf16Ring:
         total = e0.elapsed_time(e2)
         t_attn = e0.elapsed_time(e1)
         t_comm = 0.0
-        if self.args.backend == "fused" and P > 1:
+        if self.args.backend in ("fused", "p2p_unfused") and P > 1:
             eng = ENGINES.get(None, ctx.device, self.k.numel() * self.k.element_size())
             qtp, kvtp, kv_lens = _meta(lay, r, ctx.device)
             c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

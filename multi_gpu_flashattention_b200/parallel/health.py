@@ -28,17 +28,21 @@ class RingHealth:
         self.world = dist.get_world_size(group)
         self.store = store if store is not None else dist.distributed_c10d._get_default_store()
         self.prefix = prefix
+        self._last = -1  # last call this rank announced
 
     def _key(self, r: int) -> str:
         return f"{self.prefix}/{r}"
 
     def beat(self, step: int) -> None:
         """Announce that this rank is about to run call `step`."""
+        self._last = step
         self.store.set(self._key(self.rank), str(step))
 
     def leave(self) -> None:
-        """Announce a clean departure (call between steps, with no kernel in flight)."""
-        self.store.set(self._key(self.rank), "left")
+        """Announce a clean departure (call between steps, with no kernel in flight).
+        The value keeps the last call this rank took part in, so a peer still
+        checking that call is not told the rank is gone."""
+        self.store.set(self._key(self.rank), f"left:{self._last}")
 
     def check(self, step: int, timeout_s: float = 10.0, poll_s: float = 0.01) -> None:
         """Return once every peer has announced `step` (or later); raise
@@ -52,7 +56,9 @@ class RingHealth:
                     still.append(r)
                     continue
                 v = self.store.get(self._key(r)).decode()
-                if v == "left":
+                if v.startswith("left"):
+                    if int(v.split(":", 1)[1]) >= step:
+                        continue  # it took part in this call before leaving
                     raise PeerLostError(f"rank {r} left the ring")
                 if int(v) < step:
                     still.append(r)

@@ -35,7 +35,7 @@ from ..ops.flash import (DEFAULT_WAIT_LIMIT_NS, check_status, flash_attn_fwd,
 from ..ops.reference import attention_ref
 from .layouts import RingLayout
 
-BACKENDS = ("fused", "nccl", "staged", "torch")
+BACKENDS = ("fused", "p2p_unfused", "nccl", "staged", "torch")
 
 
 def _world(group) -> Tuple[int, int]:
@@ -100,13 +100,20 @@ def _meta(layout: RingLayout, rank: int, device):
 
 
 # ---------------------------------------------------------------------- forward backends
-def _fwd_fused(q, k, v, layout, causal, scale, group, status, wait_ns):
+def _fwd_fused(q, k, v, layout, causal, scale, group, status, wait_ns, fused=True):
+    """Transport inside the attention kernel (fused=True), or the same NVLink push
+    transport as a separate all-SM kernel on a second stream (fused=False, the
+    `p2p_unfused` ablation)."""
     rank, world = _world(group)
     qtp, kvtp, kv_lens = _meta(layout, rank, q.device)
     shard_bytes = k.numel() * k.element_size()
     eng = ENGINES.get(group, q.device, shard_bytes)
-    o, lse = eng.forward(q, k, v, scale, causal, qtp if causal else None,
-                         kvtp if causal else None, kv_lens, status, int(wait_ns))
+    eng.set_fused(fused)
+    try:
+        o, lse = eng.forward(q, k, v, scale, causal, qtp if causal else None,
+                             kvtp if causal else None, kv_lens, status, int(wait_ns))
+    finally:
+        eng.set_fused(True)
     return o, lse
 
 
@@ -247,8 +254,9 @@ def ring_attention_forward(q, k, v, layout: RingLayout, causal: bool = False,
         out, lse = flash_attn_fwd(q, k[:, :kv_lens[0]], v[:, :kv_lens[0]], causal=causal,
                                   softmax_scale=scale, q_tile_pos=qtp, kv_tile_pos=kvtp[0],
                                   status=st, wait_limit_ns=wait_limit_ns)
-    elif backend == "fused":
-        out, lse = _fwd_fused(q, k, v, layout, causal, scale, group, st, wait_limit_ns)
+    elif backend in ("fused", "p2p_unfused"):
+        out, lse = _fwd_fused(q, k, v, layout, causal, scale, group, st, wait_limit_ns,
+                              fused=backend == "fused")
     elif backend == "nccl":
         out, lse = _fwd_nccl(q, k, v, layout, causal, scale, group, st, wait_limit_ns)
     else:

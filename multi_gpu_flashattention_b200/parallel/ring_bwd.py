@@ -70,11 +70,15 @@ def ring_attention_backward(dout, q, k, v, out, lse, layout: RingLayout, causal:
     comm = torch.cuda.Stream(q.device)
     f32 = dict(dtype=torch.float32, device=q.device)
     dq = torch.empty(q.shape, **f32)
-    cur = [k.contiguous(), v.contiguous(), torch.empty(k.shape, **f32), torch.empty(v.shape, **f32)]
-    nxt = [torch.empty_like(t) for t in cur]
+    # K/V arrive in two alternating receive pairs (the caller's k and v, which
+    # autograd saved, are never written); the fp32 accumulators alternate too
+    kv_recv = [[torch.empty_like(k), torch.empty_like(v)] for _ in range(min(2, world - 1))]
+    acc = [[torch.empty(k.shape, **f32), torch.empty(v.shape, **f32)] for _ in range(2)]
+    cur = [k.contiguous(), v.contiguous()] + acc[0]
     for t in range(world):
         owner = (rank - t) % world
         kl = kv_lens[owner]
+        nxt = (kv_recv[t % 2] if t < world - 1 else [None, None]) + acc[(t + 1) % 2]
         # K/V of the next step can move while this step computes
         reqs = []
         if t < world - 1:
@@ -102,7 +106,7 @@ def ring_attention_backward(dout, q, k, v, out, lse, layout: RingLayout, causal:
                 rq.wait()
         compute.wait_stream(comm)
         if t < world - 1:
-            cur, nxt = nxt, cur
+            cur = nxt
     return dq.to(q.dtype), home[0].to(k.dtype), home[1].to(v.dtype)
 
 

@@ -22,9 +22,11 @@ def _case(rank, world, kind, causal, backend, seq, hq, hkv, iters):
     ref, ref_lse = attention_ref(q, k, v, causal=causal)
     n = lay.local_len(rank)
     exp = lay.shard(ref, rank)[:, :n]
+    k0, v0 = kl.clone(), vl.clone()
     for _ in range(iters):  # repeated calls reuse the slots and flags
         out, lse = ring_attention_forward(ql, kl, vl, lay, causal=causal, backend=backend,
                                           check=True)
+        assert torch.equal(kl, k0) and torch.equal(vl, v0), "inputs must not be written"
         err = (out[:, :n].float() - exp).abs()
         assert err.max().item() < 2e-2, (rank, err.max().item())
         assert err.mean().item() < 2e-3, (rank, err.mean().item())
@@ -36,7 +38,7 @@ def _world():
     return min(torch.cuda.device_count(), 4)
 
 
-@pytest.mark.parametrize("backend", ["fused", "nccl"])
+@pytest.mark.parametrize("backend", ["fused", "p2p_unfused", "nccl"])
 @pytest.mark.parametrize("kind,causal", [("zigzag", True), ("striped", True),
                                          ("contiguous", False), ("contiguous", True)])
 def test_ring_forward_matches_reference(backend, kind, causal):
@@ -60,6 +62,7 @@ def _bwd_case(rank, world, kind, causal, bwd_backend="nccl", head_dim=128,
     q, k, v, do = mk(hq), mk(hkv), mk(hkv), mk(hq)
     lay = RingLayout(kind, seq, world, mask="causal" if causal else "full")
     ql, kl, vl, dol = (lay.shard(t, rank) for t in (q, k, v, do))
+    k0, v0 = kl.clone(), vl.clone()
     out, lse = ring_attention_forward(ql, kl, vl, lay, causal=causal, backend="fused", check=True)
     assert out.dtype == dtype
     if head_dim != 128 or dtype != torch.bfloat16:
@@ -69,6 +72,8 @@ def _bwd_case(rank, world, kind, causal, bwd_backend="nccl", head_dim=128,
         assert err < 2e-2, (rank, "out", err)
     dq, dk, dv = ring_attention_backward(dol, ql, kl, vl, out, lse, lay, causal=causal,
                                          backend=bwd_backend)
+    # no backend writes the caller's k / v (autograd saved them)
+    assert torch.equal(kl, k0) and torch.equal(vl, v0), rank
     rq, rk, rv = ring_attention_backward(dol, ql, kl, vl, out, lse, lay, causal=causal,
                                          backend="torch")
     n = lay.local_len(rank)
