@@ -1,6 +1,11 @@
-"""Helpers to run a function on N local ranks (gloo on CPU or nccl on GPUs)."""
+"""Helpers to run a function on N local ranks (gloo on CPU or nccl on GPUs).
+
+Ranks rendezvous through a file store in a fresh temporary directory, so
+concurrent or back-to-back runs never race for a TCP port."""
 import os
+import shutil
 import socket
+import tempfile
 import traceback
 
 import torch.multiprocessing as mp
@@ -12,7 +17,8 @@ def free_port() -> int:
         return s.getsockname()[1]
 
 
-def _entry(rank, world, port, backend, fn, args, errq, final_barrier=True, pg_timeout=60):
+def _entry(rank, world, port, backend, fn, args, errq, final_barrier=True, pg_timeout=60,
+           store_path=None):
     import torch
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
@@ -21,7 +27,8 @@ def _entry(rank, world, port, backend, fn, args, errq, final_barrier=True, pg_ti
         if backend == "nccl":
             torch.cuda.set_device(rank)
         import datetime
-        dist.init_process_group(backend, rank=rank, world_size=world,
+        dist.init_process_group(backend, init_method=f"file://{store_path}", rank=rank,
+                                world_size=world,
                                 timeout=datetime.timedelta(seconds=pg_timeout),
                                 **({"device_id": torch.device("cuda", rank)} if backend == "nccl" else {}))
         fn(rank, world, *args)
@@ -39,11 +46,13 @@ def run_ranks(fn, world, *args, backend="gloo", timeout=240, final_barrier=True,
               env=None):
     ctx = mp.get_context("spawn")
     errq = ctx.SimpleQueue()
-    port = free_port()
+    port = free_port()  # exported as MASTER_PORT for code that reads it; not bound
+    tmp = tempfile.mkdtemp(prefix="mgfa_pg_")
+    store_path = os.path.join(tmp, "store")
     saved = {k: os.environ.get(k) for k in (env or {})}
     os.environ.update(env or {})
     procs = [ctx.Process(target=_entry, args=(r, world, port, backend, fn, args, errq,
-                                               final_barrier, pg_timeout))
+                                               final_barrier, pg_timeout, store_path))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -57,6 +66,7 @@ def run_ranks(fn, world, *args, backend="gloo", timeout=240, final_barrier=True,
     alive = [p for p in procs if p.is_alive()]
     for p in alive:
         p.kill()
+    shutil.rmtree(tmp, ignore_errors=True)
     errors = []
     while not errq.empty():
         errors.append(errq.get())
