@@ -270,6 +270,23 @@ class Bf16Ring:
                         f"receiving_kv_owner={ro} KV tokens={tokens(lay, ro)}")
             o = lay.compute_owner(r, P - 1)
             ctx.log(f"[Rank {r}] final compute_kv_owner={o} KV tokens={tokens(lay, o)}")
+        fused = self.args.backend in ("fused", "p2p_unfused") and P > 1
+        if fused:
+            eng = ENGINES.get(None, ctx.device, self.k.numel() * self.k.element_size())
+            qtp, kvtp, kv_lens = _meta(lay, r, ctx.device)
+
+            def compute_only():
+                c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                c0.record()
+                eng.forward_compute_only(self.q, self.k, self.v, self.scale, self.args.causal,
+                                         qtp if self.args.causal else None,
+                                         kvtp if self.args.causal else None, kv_lens, self.status)
+                c1.record()
+                torch.cuda.synchronize()
+                return c0.elapsed_time(c1)
+            # the compute-only reference runs before and after the ring and the two
+            # are averaged, so clock drift does not land on one side
+            before = compute_only()
         e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         e0.record()
         out, lse = ring_attention_forward(self.q, self.k, self.v, lay, causal=self.args.causal,
@@ -284,17 +301,8 @@ class Bf16Ring:
         total = e0.elapsed_time(e2)
         t_attn = e0.elapsed_time(e1)
         t_comm = 0.0
-        if self.args.backend in ("fused", "p2p_unfused") and P > 1:
-            eng = ENGINES.get(None, ctx.device, self.k.numel() * self.k.element_size())
-            qtp, kvtp, kv_lens = _meta(lay, r, ctx.device)
-            c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            c0.record()
-            eng.forward_compute_only(self.q, self.k, self.v, self.scale, self.args.causal,
-                                     qtp if self.args.causal else None,
-                                     kvtp if self.args.causal else None, kv_lens, self.status)
-            c1.record()
-            torch.cuda.synchronize()
-            t_comp = c0.elapsed_time(c1)
+        if fused:
+            t_comp = 0.5 * (before + compute_only())
             t_comm = max(0.0, t_attn - t_comp)  # exposed communication
             t_attn = t_comp
         return total, t_comm, t_attn, 0.0, e1.elapsed_time(e2), host

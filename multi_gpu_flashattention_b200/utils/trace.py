@@ -50,7 +50,9 @@ def write_chrome_trace(events: Iterable[dict], path: str) -> None:
 
 
 def summarize(trace: torch.Tensor) -> dict:
-    """Per-step wall span, summed CTA compute and push time (ms)."""
+    """Per step (ms): wall span, longest wait for the KV shard, push time (mean over
+    all CTAs and over the pushing CTAs), CTA duration (all, pushing, other) and
+    when the last chunk was pushed."""
     t = trace.detach().cpu().to(torch.int64)
     out = []
     for s in range(t.shape[0]):
@@ -62,5 +64,18 @@ def summarize(trace: torch.Tensor) -> dict:
         span = (w[:, 6].max() - w[:, 1].min()).item() / 1e6
         kv_wait = ((w[:, 2] - w[:, 1]).clamp(min=0) * (w[:, 2] != 0)).max().item() / 1e6
         push = ((w[:, 5] - w[:, 4]) * (w[:, 4] != 0)).float().mean().item() / 1e6
-        out.append({"step": s, "span_ms": span, "max_kv_wait_ms": kv_wait, "mean_push_ms": push})
+        pushing = w[:, 4] != 0
+        cta = (w[:, 6] - w[:, 1]).float()
+        entry = {"step": s, "span_ms": span, "max_kv_wait_ms": kv_wait, "mean_push_ms": push,
+                 "mean_cta_ms": cta.mean().item() / 1e6, "n_ctas": int(w.shape[0]),
+                 "n_pushing": int(pushing.sum().item())}
+        if pushing.any():
+            pw = w[pushing]
+            entry["mean_push_ms_pushing"] = (pw[:, 5] - pw[:, 4]).float().mean().item() / 1e6
+            entry["mean_cta_ms_pushing"] = cta[pushing].mean().item() / 1e6
+            entry["mean_cta_ms_other"] = (cta[~pushing].mean().item() / 1e6
+                                          if (~pushing).any() else None)
+            # when the last chunk of the shard was pushed, relative to the step start
+            entry["push_done_ms"] = (pw[:, 5].max() - w[:, 1].min()).item() / 1e6
+        out.append(entry)
     return {"steps": out}
