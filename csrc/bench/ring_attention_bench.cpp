@@ -214,6 +214,23 @@ torch::Tensor randn_rows(uint64_t seed, uint64_t stream, const std::vector<int64
   return out;
 }
 
+// Measured sustained bf16 tensor peak (TFLOP/s) from MEASURED_PEAKS.json in the
+// working directory, else 1400.
+double sustained_peak_tflops() {
+  FILE* f = std::fopen("MEASURED_PEAKS.json", "r");
+  if (!f) return 1400.0;
+  std::string text;
+  char buf[4096];
+  size_t n;
+  while ((n = std::fread(buf, 1, sizeof(buf), f)) > 0) text.append(buf, n);
+  std::fclose(f);
+  const std::string key = "\"bf16_tflops_sustained\"";
+  const size_t at = text.find(key);
+  if (at == std::string::npos) return 1400.0;
+  const size_t colon = text.find(':', at + key.size());
+  return colon == std::string::npos ? 1400.0 : std::atof(text.c_str() + colon + 1);
+}
+
 // ----------------------------------------------------------------- timing helpers
 struct Ev {
   cudaEvent_t e;
@@ -717,13 +734,20 @@ static int run_main(int argc, char** argv) {
       // ring time: comm + attention + merge, without the final normalisation /
       // download of the output
       const double flops = 4.0 * D * H * pairs, ring = (sums[1] + sums[2] + sums[3]) / n;
+      // roofline: the slower of the per-GPU FLOPs at the measured sustained bf16
+      // peak and the KV bytes each rank sends at 770 GB/s (bf16 only)
+      const double kv_bytes = double(P - 1) * 2.0 * double(meta.L) * Hkv * D * 2.0;
+      const double t_roof =
+          std::max(flops / P / (sustained_peak_tflops() * 1e12), kv_bytes / 770e9) * 1e3;
+      const std::string roof =
+          a.numerics == "bf16" && ring > 0 ? std::to_string(t_roof / ring) : "null";
       std::printf("{\"backend\": \"%s\", \"numerics\": \"%s\", \"ranks\": %d, \"seq\": %lld, "
                   "\"heads\": %d, \"head_dim\": %d, \"causal\": %s, \"layout\": \"%s\", "
                   "\"avg_total_ms\": %.4f, \"ring_ms\": %.4f, \"avg_comm_ms\": %.4f, "
-                  "\"avg_attn_ms\": %.4f, \"tflops_per_gpu\": %.2f}\n",
+                  "\"avg_attn_ms\": %.4f, \"tflops_per_gpu\": %.2f, \"roofline_fraction\": %s}\n",
                   name.c_str(), a.numerics.c_str(), P, (long long)seq, H, D,
                   a.causal ? "true" : "false", a.layout.c_str(), sums[0] / n, ring, sums[1] / n,
-                  sums[2] / n, flops / (ring * 1e-3) / 1e12 / P);
+                  sums[2] / n, flops / (ring * 1e-3) / 1e12 / P, roof.c_str());
     }
     std::fflush(stdout);
   }

@@ -4,7 +4,7 @@
 //
 //   torchrun --nproc-per-node N --no-python build/bin/ring_loop_bench \
 //       <kv_size_bytes> [warmup=10] [iters=100] [--backend p2p|ce|nccl|staged]
-//       [--payload-tokens T] [--kv-heads 8] [--ctas C] [--seed S]
+//       [--payload-tokens T] [--kv-heads 8] [--ctas C] [--seed S] [--json]
 //
 // A kv_size_bytes buffer (float32 rank*1000 + i, ring_loop_nccl.cu:131-140)
 // rotates around the ring for world-1 steps. One untimed pass first checks the
@@ -47,6 +47,7 @@ struct Args {
   int kv_heads = 8;
   int ctas = 0;
   uint64_t seed = 0;
+  bool json = false;
 };
 
 bool parse(int argc, char** argv, Args* a) {
@@ -74,6 +75,8 @@ bool parse(int argc, char** argv, Args* a) {
       const char* v = next();
       if (!v) return false;
       a->seed = uint64_t(std::atoll(v));
+    } else if (s == "--json") {
+      a->json = true;
     } else if (!s.empty() && s[0] == '-') {
       return false;
     } else {
@@ -125,7 +128,7 @@ static int run_main(int argc, char** argv) {
   if (!parse(argc, argv, &a)) {
     std::printf("Usage: ring_loop_bench <kv_size_bytes> [warmup] [iters] "
                 "[--backend p2p|ce|nccl|staged] [--payload-tokens T] [--kv-heads H] "
-                "[--ctas C] [--seed S]\n");
+                "[--ctas C] [--seed S] [--json]\n");
     return 1;
   }
   Dist d = Dist::from_env();
@@ -292,6 +295,14 @@ static int run_main(int argc, char** argv) {
                 "avg_total_ms=%.3f total_GBps=%.3f %s_GBps=%.3f\n",
                 b, (long long)nbytes, P, a.warmup, a.iters, b, avg_c, avg_t,
                 payload / (avg_t / 1e3) / 1e9, b, payload / (avg_c / 1e3) / 1e9);
+    if (a.json) {
+      // per-direction GB/s against the measured 770 GB/s peer-copy bandwidth
+      const double gbps = payload / (avg_c / 1e3) / 1e9;
+      std::printf("{\"backend\": \"%s\", \"bytes\": %lld, \"ranks\": %d, \"avg_ms\": %.4f, "
+                  "\"per_direction_GBps\": %.2f, \"link_fraction\": %.3f, "
+                  "\"payload_tokens\": %lld}\n",
+                  b, (long long)nbytes, P, avg_c, gbps, gbps / 770.0, (long long)a.payload_tokens);
+    }
     std::fflush(stdout);
   }
   d.barrier();

@@ -385,13 +385,25 @@ def main():
         # the final normalisation / download of the output
         ring_ms = (sums[1] + sums[2] + sums[3]) / n
         import json as _json
+        roof = None
+        if args.numerics == "bf16":
+            # slower of the per-GPU attention FLOPs at the measured sustained bf16
+            # peak and the KV bytes each rank sends over NVLink at 770 GB/s
+            here = os.path.dirname(os.path.abspath(__file__))
+            peaks = os.path.join(here, "..", "..", "MEASURED_PEAKS.json")
+            peak = _json.load(open(peaks))["bf16_tflops_sustained"] if os.path.exists(peaks) \
+                else 1400.0
+            kv_bytes = (P - 1) * 2 * L * Hkv * D * 2
+            t_roof = max(flops / P / (peak * 1e12), kv_bytes / 770e9) * 1e3
+            roof = t_roof / ring_ms if ring_ms > 0 else None
         print(_json.dumps({"backend": name, "numerics": args.numerics, "ranks": P,
                            "seq": S_tot, "heads": H, "head_dim": D, "causal": args.causal,
                            "layout": args.layout, "avg_total_ms": sums[0] / n,
                            "ring_ms": ring_ms, "avg_comm_ms": sums[1] / n,
                            "avg_attn_ms": sums[2] / n,
                            "tflops_per_gpu": flops / (ring_ms * 1e-3) / 1e12 / P,
-                           "comm_fraction": (sums[1] / n) / ring_ms if ring_ms > 0 else None}),
+                           "comm_fraction": (sums[1] / n) / ring_ms if ring_ms > 0 else None,
+                           "roofline_fraction": roof}),
               flush=True)
     if os.environ.get("ATTENTION_DUMP_OUTPUT") is not None:
         lse = getattr(ring, "lse", None)

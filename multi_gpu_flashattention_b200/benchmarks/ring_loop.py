@@ -194,8 +194,10 @@ def main():
               f"total_GBps={payload / (avg_t / 1e3) / 1e9:.3f} {b}_GBps={payload / (avg_c / 1e3) / 1e9:.3f}",
               flush=True)
         if args.json:
+            gbps = payload / (avg_c / 1e3) / 1e9
             print(json.dumps({"backend": b, "bytes": nbytes, "ranks": P, "avg_ms": avg_c,
-                              "per_direction_GBps": payload / (avg_c / 1e3) / 1e9,
+                              "per_direction_GBps": gbps,
+                              "link_fraction": gbps / 770.0,  # of the measured peer copy
                               "payload_tokens": args.payload_tokens}), flush=True)
     ctx.close()
     return 0
