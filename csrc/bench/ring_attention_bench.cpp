@@ -78,6 +78,7 @@ struct Args {
   bool causal = false, overlap = false, json = false;
   int heads = 1, kv_heads = 0, head_dim = 0;
   uint64_t seed = 0;
+  int print_tables = 0;  // > 0: print the layout tables for that many ranks and exit
 };
 
 bool parse(int argc, char** argv, Args* a) {
@@ -99,6 +100,7 @@ bool parse(int argc, char** argv, Args* a) {
     else if (s == "--kv-heads") { if (!val(&v)) return false; a->kv_heads = std::atoi(v.c_str()); }
     else if (s == "--head-dim") { if (!val(&v)) return false; a->head_dim = std::atoi(v.c_str()); }
     else if (s == "--seed") { if (!val(&v)) return false; a->seed = uint64_t(std::atoll(v.c_str())); }
+    else if (s == "--print-tables") { if (!val(&v)) return false; a->print_tables = std::atoi(v.c_str()); }
     else if (s == "--causal") a->causal = true;
     else if (s == "--overlap") a->overlap = true;
     else if (s == "--json") a->json = true;
@@ -602,6 +604,35 @@ class Bf16Ring {
   c10::cuda::CUDAStream comm_ = c10::cuda::getDefaultCUDAStream();
 };
 
+template <class T>
+std::string json_list(const std::vector<T>& v) {
+  std::string s = "[";
+  for (size_t i = 0; i < v.size(); ++i) s += (i ? ", " : "") + std::to_string(v[i]);
+  return s + "]";
+}
+
+// The kernels' tables for every rank of a `world`-rank ring (one JSON line per
+// rank), without touching a GPU: the layout logic is checked against the Python
+// layer on the host.
+int print_tables(const Args& a) {
+  const int P = a.print_tables, D = a.head_dim ? a.head_dim : 128;
+  const int64_t L = a.kv_size / (int64_t(a.heads) * D * 4);
+  const Meta m = make_meta(a, L * P, P);
+  for (int r = 0; r < P; ++r) {
+    std::string kv = "[", kpos = "[";
+    for (int o = 0; o < P; ++o) {
+      kv += (o ? ", " : "") + json_list(m.kv_tile_pos(r, o));
+      kpos += (o ? ", " : "") + json_list(m.k_positions(r, o));
+    }
+    std::printf("{\"rank\": %d, \"L\": %lld, \"q_tile_pos\": %s, \"kv_tile_pos\": %s]"
+                ", \"q_positions\": %s, \"k_positions\": %s], \"local_len\": %lld}\n",
+                r, (long long)m.L, json_list(m.tile_starts(r)).c_str(), kv.c_str(),
+                json_list(m.q_positions(r)).c_str(), kpos.c_str(),
+                (long long)m.plan.local_len(r));
+  }
+  return 0;
+}
+
 }  // namespace
 
 static int run_main(int argc, char** argv) {
@@ -614,6 +645,7 @@ static int run_main(int argc, char** argv) {
                 "[--heads H] [--kv-heads H] [--head-dim D] [--seed S] [--overlap] [--json]\n");
     return 1;
   }
+  if (a.print_tables > 0) return print_tables(a);
   Dist d = Dist::from_env();
   const int P = d.world(), r = d.rank();
   auto log0 = [&](const std::string& s) {

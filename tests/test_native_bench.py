@@ -114,3 +114,30 @@ def test_ring_attention_bench_bf16_dumps(tmp_path, backend, layout):
         exp = lay.shard(ref, r)[0, : lay.local_len(r)]
         err = (got - exp).abs().max().item()
         assert err < 2e-2, (r, err)
+
+
+@pytest.mark.parametrize("layout,world,causal", [("contiguous", 2, False), ("contiguous", 3, True),
+                                                 ("zigzag", 2, True), ("zigzag", 4, True),
+                                                 ("striped", 3, True), ("scheduler", 4, True),
+                                                 ("scheduler", 3, False)])
+def test_native_layout_tables_match_python(layout, world, causal):
+    """The native benchmark's kernel tables (tile positions per owner, mask
+    positions, lengths) equal the Python layer's for every layout."""
+    import json
+    from multi_gpu_flashattention_b200.parallel.layouts import RingLayout
+    exe = _exe("ring_attention_bench")
+    H, D, L = 2, 64, 768
+    args = [exe, str(L * H * D * 4), "--print-tables", str(world), "--layout", layout,
+            "--heads", str(H), "--head-dim", str(D)] + (["--causal"] if causal else [])
+    p = subprocess.run(args, capture_output=True, text=True, timeout=60)
+    assert p.returncode == 0, p.stdout + p.stderr
+    rows = [json.loads(l) for l in p.stdout.splitlines()]
+    lay = RingLayout(layout, L * world, world, mask="causal" if causal else "full")
+    assert len(rows) == world
+    for r, row in enumerate(rows):
+        assert row["L"] == lay.max_local_len and row["local_len"] == lay.local_len(r)
+        assert row["q_tile_pos"] == lay.q_tile_pos(r, "cpu").tolist()
+        assert row["kv_tile_pos"] == lay.kv_tile_pos_by_owner(r, "cpu").tolist()
+        assert row["q_positions"] == lay.q_positions_for_mask(r).tolist()
+        assert row["k_positions"] == [lay.k_positions_for_mask(r, o).tolist()
+                                      for o in range(world)]
