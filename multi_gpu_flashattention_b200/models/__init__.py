@@ -1,2 +1,3 @@
 """Model building blocks that use ring attention."""
-from .transformer import RingAttentionBlock, RMSNorm, rotary  # noqa: F401
+from .transformer import (IGNORE_INDEX, RingAttentionBlock, RingTransformerLM, RMSNorm,  # noqa: F401
+                          rotary, shard_targets)

@@ -74,3 +74,68 @@ class RingAttentionBlock(nn.Module):
         x = x + self.wo(a.reshape(B, L, self.h * self.d).to(x.dtype))
         h = self.norm2(x)
         return x + self.w2(F.silu(self.w1(h)) * self.w3(h))
+
+
+IGNORE_INDEX = -100
+
+
+def shard_targets(ids: torch.Tensor, layout: RingLayout, rank: int) -> torch.Tensor:
+    """Next-token targets of rank's shard, in the layout's local order.
+
+    ids: the full sequence [B, S] (int64). The target of the token at global
+    position p is ids[:, p + 1]; the last position and padding rows get
+    IGNORE_INDEX. With zigzag or striped layouts the next token usually lives on
+    another rank, so targets are cut from the full sequence on the host."""
+    B, S = ids.shape
+    nxt = torch.full_like(ids, IGNORE_INDEX)
+    nxt[:, :-1] = ids[:, 1:]
+    out = layout.shard(nxt, rank)
+    n = layout.local_len(rank)
+    out[:, n:] = IGNORE_INDEX
+    return out
+
+
+class RingTransformerLM(nn.Module):
+    """Decoder-only language model with context-parallel ring attention.
+
+    Each rank runs every layer on its own token shard (ids [B, L] in the
+    layout's local order, padded to the layout's max_local_len); attention is
+    the ring over `group`, everything else is per token. Parameters are
+    replicated, so after `loss(...).backward()` the gradients are summed over
+    the group (all-reduce, as in data parallelism) to give the unsharded
+    model's gradients."""
+
+    def __init__(self, vocab: int, d_model: int, n_layers: int, n_heads: int,
+                 n_kv_heads: Optional[int] = None, head_dim: int = 128, mlp_mult: int = 4,
+                 tie_embeddings: bool = True):
+        super().__init__()
+        self.embed = nn.Embedding(vocab, d_model)
+        self.blocks = nn.ModuleList(
+            RingAttentionBlock(d_model, n_heads, n_kv_heads, head_dim, mlp_mult, causal=True)
+            for _ in range(n_layers))
+        self.norm = RMSNorm(d_model)
+        self.head = nn.Linear(d_model, vocab, bias=False)
+        if tie_embeddings:
+            self.head.weight = self.embed.weight
+
+    def forward(self, ids: torch.Tensor, layout: RingLayout, rank: int = 0, group=None,
+                backend: Optional[str] = None) -> torch.Tensor:
+        """Logits [B, L, vocab] of the local shard."""
+        x = self.embed(ids)
+        for blk in self.blocks:
+            x = blk(x, layout, rank, group=group, backend=backend)
+        return self.head(self.norm(x))
+
+    def loss(self, ids: torch.Tensor, targets: torch.Tensor, layout: RingLayout, rank: int = 0,
+             group=None, backend: Optional[str] = None) -> torch.Tensor:
+        """Mean next-token cross entropy over every real token of the sequence:
+        this shard's summed loss divided by the token count of all shards."""
+        import torch.distributed as dist
+        logits = self(ids, layout, rank, group=group, backend=backend)
+        local = F.cross_entropy(logits.float().flatten(0, 1), targets.flatten(),
+                                ignore_index=IGNORE_INDEX, reduction="sum")
+        count = (targets != IGNORE_INDEX).sum().to(torch.float32)
+        if dist.is_initialized() and dist.get_world_size(group) > 1:
+            count = count.clone()
+            dist.all_reduce(count, group=group)
+        return local / count.clamp(min=1.0)
