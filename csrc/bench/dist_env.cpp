@@ -61,6 +61,22 @@ Dist Dist::from_env(int timeout_s) {
   return d;
 }
 
+Dist& Dist::operator=(Dist&& o) noexcept {
+  if (this != &o) {
+    if (comm_) ncclCommDestroy(comm_);
+    rank_ = o.rank_;
+    world_ = o.world_;
+    local_rank_ = o.local_rank_;
+    device_ = o.device_;
+    store_ = std::move(o.store_);
+    coll_seq_ = o.coll_seq_;
+    p2p_seq_ = o.p2p_seq_;
+    comm_ = o.comm_;
+    o.comm_ = nullptr;
+  }
+  return *this;
+}
+
 Dist::~Dist() {
   if (comm_) ncclCommDestroy(comm_);
 }

@@ -17,6 +17,7 @@
 
 #include <cstdint>
 #include <string>
+#include <utility>
 #include <vector>
 
 namespace mgfa::bench {
@@ -28,8 +29,11 @@ class Dist {
   // connects to the store. Throws std::runtime_error on a bad environment.
   static Dist from_env(int timeout_s = 300);
 
-  Dist(Dist&&) = default;
-  Dist& operator=(Dist&&) = default;
+  // Movable, not copyable: the NCCL communicator has one owner.
+  Dist(Dist&& o) noexcept { *this = std::move(o); }
+  Dist& operator=(Dist&& o) noexcept;
+  Dist(const Dist&) = delete;
+  Dist& operator=(const Dist&) = delete;
   ~Dist();
 
   int rank() const { return rank_; }

@@ -4,7 +4,7 @@
 // sm_100a attention kernel, one per ring step. Step t computes the local
 // queries against the KV shard of owner (rank - t) mod P (the reference's
 // schedule, ring/attention/common/shard_utils.cuh:29-35) and, inside the same
-// kernel, pushes that shard to the right neighbour's receive slot (t+1) % 2
+// kernel, pushes that shard to the right neighbour's receive slot (t+1) % 3
 // and merges its partial result into the running output. There is no host
 // synchronisation between steps: ordering across ranks is carried entirely by
 // the flag words of the symmetric buffer.
