@@ -4,7 +4,8 @@
 // executable with a --backend flag, without MPI.
 //
 //   torchrun --nproc-per-node N --no-python build/bin/ring_attention_bench \
-//       <kv_size_bytes> [warmup=10] [iters=100] [--backend fused|p2p_unfused|nccl|staged]
+//       <kv_size_bytes> [warmup=10] [iters=100]
+//       [--backend fused|p2p_unfused|ce_unfused|nccl|staged]
 //       [--numerics fp32|bf16] [--init legacy|randn] [--layout contiguous|zigzag|
 //       striped|scheduler] [--policy dp|lpt] [--causal] [--heads H] [--kv-heads H]
 //       [--head-dim D] [--seed S] [--overlap] [--json]
@@ -18,7 +19,8 @@
 //     `verify_full <dir> N kv_size` checks the dumps.
 //   --numerics bf16 (head_dim 64 or 128): the sm_100a kernels; fused (transport
 //     inside the attention kernel), p2p_unfused (the same NVLink push transport as
-//     a separate kernel on a second stream), nccl (attention kernel per step + NCCL
+//     a separate kernel on a second stream), ce_unfused (the copy engine moves the
+//     shard on a second stream), nccl (attention kernel per step + NCCL
 //     send/recv on a second stream) or staged (device -> host -> store -> device).
 // Environment as in the reference: ATTENTION_PRINT_SHARDS=1 prints token ranges
 // and per-step owners of iteration 0; ATTENTION_DUMP_OUTPUT=1 writes
@@ -115,8 +117,8 @@ bool parse(int argc, char** argv, Args* a) {
   }
   if (a->backend.empty()) a->backend = a->numerics == "bf16" ? "fused" : "nccl";
   return (a->numerics == "fp32" || a->numerics == "bf16") &&
-         (a->backend == "fused" || a->backend == "p2p_unfused" || a->backend == "nccl" ||
-          a->backend == "staged") &&
+         (a->backend == "fused" || a->backend == "p2p_unfused" || a->backend == "ce_unfused" ||
+          a->backend == "nccl" || a->backend == "staged") &&
          (a->init == "legacy" || a->init == "randn");
 }
 
@@ -450,14 +452,16 @@ class Bf16Ring {
       kv_lens_.push_back(m.plan.local_len(o));
     }
     kvtp_ = i32_dev(all, dev).view({P, -1});
-    if (a.backend == "fused" || a.backend == "p2p_unfused") {
+    if (a.backend == "fused" || a.backend == "p2p_unfused" || a.backend == "ce_unfused") {
       const int64_t shard = k.numel() * k.element_size();
       int64_t slot = std::max<int64_t>(shard, 1 << 20);
       slot = (slot + (2 << 20) - 1) / (2 << 20) * (2 << 20);
       const char* ch = std::getenv("MGFA_RING_CHUNKS");
       eng_ = std::make_unique<mgfa::RingEngine>(r, P, dev, slot, ch ? std::atoi(ch) : 0);
       eng_->connect(d.all_gather(eng_->ipc_handle()));
-      eng_->set_fused(a.backend == "fused");
+      eng_->set_transport_mode(a.backend == "fused"         ? mgfa::RingEngine::kFusedPush
+                               : a.backend == "p2p_unfused" ? mgfa::RingEngine::kPushKernel
+                                                            : mgfa::RingEngine::kCopyEngine);
       cudaDeviceSynchronize();
       d.barrier();
     } else {
@@ -639,7 +643,7 @@ static int run_main(int argc, char** argv) {
   Args a;
   if (!parse(argc, argv, &a)) {
     std::printf("Usage: ring_attention_bench <kv_size_bytes> [warmup] [iters] "
-                "[--backend fused|p2p_unfused|nccl|staged] [--numerics fp32|bf16] "
+                "[--backend fused|p2p_unfused|ce_unfused|nccl|staged] [--numerics fp32|bf16] "
                 "[--init legacy|randn] "
                 "[--layout contiguous|zigzag|striped|scheduler] [--policy dp|lpt] [--causal] "
                 "[--heads H] [--kv-heads H] [--head-dim D] [--seed S] [--overlap] [--json]\n");
@@ -668,7 +672,7 @@ static int run_main(int argc, char** argv) {
          ", warmup >= 0, iters > 0.");
     return 1;
   }
-  if (a.numerics == "fp32" && (D != 64 || a.backend == "fused" || a.backend == "p2p_unfused")) {
+  if (a.numerics == "fp32" && (D != 64 || (a.backend != "nccl" && a.backend != "staged"))) {
     log0("fp32 numerics: head_dim 64, backends nccl or staged");
     return 1;
   }
@@ -755,7 +759,10 @@ static int run_main(int argc, char** argv) {
     }
   }
   const std::string name = a.backend + (a.overlap ? "_overlap" : "");
-  const char* comm_name = a.backend == "nccl" ? "NCCL" : a.backend == "staged" ? "MPI" : "P2P";
+  const char* comm_name = a.backend == "nccl"         ? "NCCL"
+                          : a.backend == "staged"     ? "MPI"
+                          : a.backend == "ce_unfused" ? "CE"
+                                                      : "P2P";
   if (r == 0) {
     const double n = a.iters;
     std::printf("%s bench: warmup=%d iters=%d\n", name.c_str(), a.warmup, a.iters);

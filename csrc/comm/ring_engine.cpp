@@ -19,6 +19,8 @@ void register_ring_engine(py::module& m) {
       .def("set_dependent_launch", &RingEngine::set_dependent_launch)
       .def("set_fused", &RingEngine::set_fused)
       .def("fused", &RingEngine::fused)
+      .def("set_transport_mode", &RingEngine::set_transport_mode)
+      .def("transport_mode", &RingEngine::transport_mode)
       .def("poison_slots", &RingEngine::poison_slots)
       .def("last_trace", &RingEngine::last_trace)
       .def("forward", &RingEngine::forward, py::arg("q"), py::arg("k"), py::arg("v"),

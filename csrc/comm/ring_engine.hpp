@@ -45,6 +45,8 @@ cudaError_t ring_push_launch(const RingPush& push, const RingConsume& consume, u
                              uint64_t limit_ns, int n_ctas, cudaStream_t stream);
 cudaError_t ring_signal_launch(const RingPush& push, const RingConsume& consume,
                                cudaStream_t stream);
+cudaError_t ring_wait_launch(const RingPush& push, const RingConsume& consume, uint32_t* status,
+                             uint64_t limit_ns, cudaStream_t stream);
 
 class RingEngine {
  public:
@@ -224,20 +226,26 @@ class RingEngine {
         p.consume.tag = buf_.flag(r, comm::kTag0 + s);
         p.consume.expected_tag = slot_tag(owner, calls_);
       }
-      if (transport && !fused_) {
-        // Unfused transport: the same flags, but the shard moves in the
-        // standalone all-SM push kernel on a second stream; the attention kernel
-        // only waits for its slot, and a signal kernel releases the slot once
-        // both the attention and the push kernel are done with it. Step t+1's
-        // attention is stream-ordered after step t's push, so a grid spinning
-        // on its arrivals never holds SMs that a push it waits for needs.
+      const bool unfused = transport && mode_ != kFusedPush;
+      // chunks (= arrival signals) of the unfused transports
+      const uint32_t x_chunks = mode_ == kCopyEngine ? 1u : uint32_t(2 * num_sms_);
+      if (unfused) {
+        // Unfused transports: the same flags, but the shard moves on a second
+        // stream -- in the standalone all-SM push kernel, or by the copy engine
+        // (cudaMemcpyAsync into the peer slot between a one-thread wait kernel
+        // and a one-thread signal kernel, no SMs for the data). The attention
+        // kernel only waits for its slot, and a signal kernel releases the slot
+        // once both the attention and the transfer are done with it. Step t+1's
+        // attention is stream-ordered after step t's transfer, so a grid
+        // spinning on its arrivals never holds SMs that a transfer it waits for
+        // needs.
         p.dependent_launch = 0;
         push_x = p.push;
-        push_x.n_chunks = uint32_t(2 * num_sms_);
+        push_x.n_chunks = x_chunks;
         push_x.peer_tag = nullptr;
         p.push = RingPush();
         if (t > 0) {
-          p.consume.arrivals_target = uint32_t(2 * num_sms_);
+          p.consume.arrivals_target = x_chunks;
           p.consume.done_counter = nullptr;
           p.consume.tag = nullptr;
           wait_x = p.consume;
@@ -250,7 +258,7 @@ class RingEngine {
       std::snprintf(label, sizeof(label), "ring step %d (kv owner %d)", t, owner);
       nvtxRangePushA(label);
       cudaEvent_t pushed = nullptr;
-      if (transport && !fused_ && push_x.enabled) {
+      if (unfused && push_x.enabled) {
         if (!push_stream_) push_stream_ = c10::cuda::getStreamFromPool(false, buf_.device());
         cudaStream_t ps = push_stream_->stream();
         cudaEvent_t start;
@@ -259,8 +267,19 @@ class RingEngine {
         C10_CUDA_CHECK(cudaStreamWaitEvent(ps, start, 0));
         C10_CUDA_CHECK(cudaEventDestroy(start));
         flash_fwd_launch_maps(mq, mk, mv, p, stream);
-        C10_CUDA_CHECK(ring_push_launch(push_x, wait_x, p.status, uint64_t(wait_limit_ns),
-                                        2 * num_sms_, ps));
+        if (mode_ == kCopyEngine) {
+          // wait until the shard we forward has arrived and the right neighbour
+          // has released the destination slot, copy, then signal one arrival
+          C10_CUDA_CHECK(ring_wait_launch(push_x, wait_x, p.status, uint64_t(wait_limit_ns), ps));
+          C10_CUDA_CHECK(cudaMemcpyAsync(push_x.dst_k, push_x.src_k, shard_bytes,
+                                         cudaMemcpyDeviceToDevice, ps));
+          C10_CUDA_CHECK(cudaMemcpyAsync(push_x.dst_v, push_x.src_v, shard_bytes,
+                                         cudaMemcpyDeviceToDevice, ps));
+          C10_CUDA_CHECK(ring_signal_launch(push_x, RingConsume(), ps));
+        } else {
+          C10_CUDA_CHECK(ring_push_launch(push_x, wait_x, p.status, uint64_t(wait_limit_ns),
+                                          2 * num_sms_, ps));
+        }
         C10_CUDA_CHECK(cudaEventCreateWithFlags(&pushed, cudaEventDisableTiming));
         C10_CUDA_CHECK(cudaEventRecord(pushed, ps));
         C10_CUDA_CHECK(cudaStreamWaitEvent(stream, pushed, 0));
@@ -268,7 +287,7 @@ class RingEngine {
       } else {
         flash_fwd_launch_maps(mq, mk, mv, p, stream);
       }
-      if (transport && !fused_ && t > 0) {
+      if (unfused && t > 0) {
         RingConsume rel;
         rel.enabled = 1;
         rel.arrivals = buf_.flag(r, comm::kArrivals0 + s);
@@ -286,10 +305,18 @@ class RingEngine {
   static uint32_t slot_tag(int owner, uint32_t call) { return uint32_t(owner + 1) | (call << 8); }
 
  public:
-  // false: move the shard with the standalone push kernel instead of the
-  // attention kernel's push warps (the unfused ablation of the same transport).
-  void set_fused(bool on) { fused_ = on; }
-  bool fused() const { return fused_; }
+  // Transport of forward(): the attention kernel's push warps (fused, the
+  // default), the standalone all-SM push kernel on a second stream, or the copy
+  // engine on a second stream (the last two are ablations of the same flags).
+  enum Mode : int { kFusedPush = 0, kPushKernel = 1, kCopyEngine = 2 };
+  void set_transport_mode(int m) {
+    MGFA_CHECK(m >= kFusedPush && m <= kCopyEngine, "transport mode must be 0, 1 or 2");
+    mode_ = m;
+  }
+  int transport_mode() const { return mode_; }
+  // false: the standalone push kernel (kept for callers of the two-way switch).
+  void set_fused(bool on) { mode_ = on ? kFusedPush : kPushKernel; }
+  bool fused() const { return mode_ == kFusedPush; }
 
  private:
 
@@ -332,7 +359,7 @@ class RingEngine {
   int drop_signal_step_ = -1;
   bool trace_ = false;
   bool pdl_ = true;
-  bool fused_ = true;
+  int mode_ = kFusedPush;
   c10::optional<c10::cuda::CUDAStream> push_stream_;
   uint32_t calls_ = 0;
   int num_sms_ = 148;

@@ -15,8 +15,9 @@ Shapes follow the reference: tokens per rank = kv_size_bytes / (heads * head_dim
   --init randn uses the seeded N(0,1) streams and scale 1/sqrt(d)
   (`verify_full <dir> N kv_size --init randn`).
 --numerics bf16 (head_dim 128): the sm_100a kernels, backends fused | p2p_unfused |
-  nccl | staged (p2p_unfused: the fused path's NVLink push transport as a separate
-  kernel on a second stream, the ablation that isolates the fusion).
+  ce_unfused | nccl | staged (p2p_unfused: the fused path's NVLink push transport as
+  a separate kernel on a second stream; ce_unfused: the copy engine moves the shard
+  on a second stream -- the ablations that isolate the fusion).
 
 Environment (as in the reference): ATTENTION_PRINT_SHARDS=1 prints token ranges
 and the owner of the shard computed/received at each step of iteration 0;
@@ -38,7 +39,8 @@ from .._ext import C, sched as _sched
 from ..parallel.layouts import RingLayout
 from . import common
 
-COMM_NAME = {"nccl": "NCCL", "staged": "MPI", "fused": "P2P", "p2p_unfused": "P2P"}
+COMM_NAME = {"nccl": "NCCL", "staged": "MPI", "fused": "P2P", "p2p_unfused": "P2P",
+             "ce_unfused": "CE"}
 
 
 def parse():
@@ -46,7 +48,8 @@ def parse():
     ap.add_argument("kv_size", type=int, nargs="?")
     ap.add_argument("warmup", type=int, nargs="?", default=10)
     ap.add_argument("iters", type=int, nargs="?", default=100)
-    ap.add_argument("--backend", default=None, choices=["fused", "p2p_unfused", "nccl", "staged"])
+    ap.add_argument("--backend", default=None,
+                    choices=["fused", "p2p_unfused", "ce_unfused", "nccl", "staged"])
     ap.add_argument("--numerics", default="fp32", choices=["fp32", "bf16"])
     ap.add_argument("--init", default="legacy", choices=["legacy", "randn"])
     ap.add_argument("--layout", default="contiguous",
@@ -270,7 +273,7 @@ class Bf16Ring:
                         f"receiving_kv_owner={ro} KV tokens={tokens(lay, ro)}")
             o = lay.compute_owner(r, P - 1)
             ctx.log(f"[Rank {r}] final compute_kv_owner={o} KV tokens={tokens(lay, o)}")
-        fused = self.args.backend in ("fused", "p2p_unfused") and P > 1
+        fused = self.args.backend in ("fused", "p2p_unfused", "ce_unfused") and P > 1
         if fused:
             eng = ENGINES.get(None, ctx.device, self.k.numel() * self.k.element_size())
             qtp, kvtp, kv_lens = _meta(lay, r, ctx.device)

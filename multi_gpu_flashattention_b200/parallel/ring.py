@@ -35,7 +35,9 @@ from ..ops.flash import (DEFAULT_WAIT_LIMIT_NS, check_status, flash_attn_fwd,
 from ..ops.reference import attention_ref
 from .layouts import RingLayout
 
-BACKENDS = ("fused", "p2p_unfused", "nccl", "staged", "torch")
+BACKENDS = ("fused", "p2p_unfused", "ce_unfused", "nccl", "staged", "torch")
+# transport modes of the fused engine (RingEngine.set_transport_mode)
+_ENGINE_MODES = {"fused": 0, "p2p_unfused": 1, "ce_unfused": 2}
 
 
 def _world(group) -> Tuple[int, int]:
@@ -100,20 +102,21 @@ def _meta(layout: RingLayout, rank: int, device):
 
 
 # ---------------------------------------------------------------------- forward backends
-def _fwd_fused(q, k, v, layout, causal, scale, group, status, wait_ns, fused=True):
-    """Transport inside the attention kernel (fused=True), or the same NVLink push
-    transport as a separate all-SM kernel on a second stream (fused=False, the
-    `p2p_unfused` ablation)."""
+def _fwd_fused(q, k, v, layout, causal, scale, group, status, wait_ns, mode="fused"):
+    """The native engine's ring. mode "fused": the transport runs inside the
+    attention kernel; "p2p_unfused": the same NVLink push as a separate all-SM
+    kernel on a second stream; "ce_unfused": the copy engine moves the shard on a
+    second stream (both ablations keep the flags and slots)."""
     rank, world = _world(group)
     qtp, kvtp, kv_lens = _meta(layout, rank, q.device)
     shard_bytes = k.numel() * k.element_size()
     eng = ENGINES.get(group, q.device, shard_bytes)
-    eng.set_fused(fused)
+    eng.set_transport_mode(_ENGINE_MODES[mode])
     try:
         o, lse = eng.forward(q, k, v, scale, causal, qtp if causal else None,
                              kvtp if causal else None, kv_lens, status, int(wait_ns))
     finally:
-        eng.set_fused(True)
+        eng.set_transport_mode(0)
     return o, lse
 
 
@@ -254,9 +257,9 @@ def ring_attention_forward(q, k, v, layout: RingLayout, causal: bool = False,
         out, lse = flash_attn_fwd(q, k[:, :kv_lens[0]], v[:, :kv_lens[0]], causal=causal,
                                   softmax_scale=scale, q_tile_pos=qtp, kv_tile_pos=kvtp[0],
                                   status=st, wait_limit_ns=wait_limit_ns)
-    elif backend in ("fused", "p2p_unfused"):
+    elif backend in _ENGINE_MODES:
         out, lse = _fwd_fused(q, k, v, layout, causal, scale, group, st, wait_limit_ns,
-                              fused=backend == "fused")
+                              mode=backend)
     elif backend == "nccl":
         out, lse = _fwd_nccl(q, k, v, layout, causal, scale, group, st, wait_limit_ns)
     else:

@@ -38,7 +38,7 @@ def _world():
     return min(torch.cuda.device_count(), 4)
 
 
-@pytest.mark.parametrize("backend", ["fused", "p2p_unfused", "nccl"])
+@pytest.mark.parametrize("backend", ["fused", "p2p_unfused", "ce_unfused", "nccl"])
 @pytest.mark.parametrize("kind,causal", [("zigzag", True), ("striped", True),
                                          ("contiguous", False), ("contiguous", True)])
 def test_ring_forward_matches_reference(backend, kind, causal):
