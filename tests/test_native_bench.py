@@ -141,3 +141,26 @@ def test_native_layout_tables_match_python(layout, world, causal):
         assert row["q_positions"] == lay.q_positions_for_mask(r).tolist()
         assert row["k_positions"] == [lay.k_positions_for_mask(r, o).tolist()
                                       for o in range(world)]
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+@pytest.mark.parametrize("extra", [["--backend", "nccl"], ["--backend", "staged"],
+                                   ["--backend", "nccl", "--overlap"]])
+def test_fp32_randn_seq4096_two_ranks(tmp_path, extra):
+    """fp32 N(0,1) q/k/v (seed 0), 1 head x d64, 4096 tokens over 2 ranks in
+    contiguous 2048-token shards, scale 1/8, non-causal: every rank's dump within
+    1e-4 (max abs) of the full single-device fp32 reference."""
+    import re
+    size = 2048 * 64 * 4
+    _torchrun(_exe("ring_attention_bench"),
+              [size, 1, 2, "--init", "randn", "--seed", 0] + extra, 2, tmp_path,
+              env={"ATTENTION_DUMP_OUTPUT": "1"})
+    vf = os.path.join(BIN, "verify_full")
+    if not os.path.exists(vf):
+        pytest.skip("verify_full not built")
+    p = subprocess.run([vf, str(tmp_path), "2", str(size), "--init", "randn", "--seed", "0"],
+                       capture_output=True, text=True, timeout=300)
+    assert p.returncode == 0 and "ALL PASS" in p.stdout, p.stdout[-2000:]
+    errs = [float(x) for x in re.findall(r"Max absolute error:\s*([0-9.eE+-]+)", p.stdout)]
+    assert len(errs) == 2 and max(errs) <= 1e-4, errs
