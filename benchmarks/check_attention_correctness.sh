@@ -6,7 +6,7 @@
 # pair element-wise (PASS iff max_abs <= ABS_TOL or max_rel <= REL_TOL).
 #
 # Env: NP (2) SIZE (262144) WARMUP (1) ITERS (1) ABS_TOL (1e-3) REL_TOL (1e-5)
-#      RESULTS_ROOT (results) RUN_LABEL (timestamp) INIT (legacy|randn)
+#      RESULTS_ROOT (results) RUN_LABEL (timestamp) INIT (legacy|randn) CHECK_P2P (1)
 set -euo pipefail
 cd "$(dirname "$0")/.."
 export PYTHONPATH="$PWD${PYTHONPATH:+:$PYTHONPATH}"
@@ -64,3 +64,10 @@ run_bench staged --backend staged
 run_bench staged_overlap --backend staged --overlap
 compare_pair nccl_vs_overlap "$OUT/nccl" "$OUT/nccl_overlap"
 compare_pair staged_vs_overlap "$OUT/staged" "$OUT/staged_overlap"
+if [[ "${CHECK_P2P:-1}" == 1 ]]; then
+  # the KV shard over NVLink: push kernel and copy engine (sequential order)
+  run_bench p2p --backend p2p
+  run_bench ce --backend ce
+  compare_pair nccl_vs_p2p "$OUT/nccl" "$OUT/p2p"
+  compare_pair nccl_vs_ce "$OUT/nccl" "$OUT/ce"
+fi

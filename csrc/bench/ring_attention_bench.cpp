@@ -5,7 +5,7 @@
 //
 //   torchrun --nproc-per-node N --no-python build/bin/ring_attention_bench \
 //       <kv_size_bytes> [warmup=10] [iters=100]
-//       [--backend fused|p2p_unfused|ce_unfused|nccl|staged]
+//       [--backend fused|p2p_unfused|ce_unfused|nccl|staged|p2p|ce]
 //       [--numerics fp32|bf16] [--init legacy|randn] [--layout contiguous|zigzag|
 //       striped|scheduler] [--policy dp|lpt] [--causal] [--heads H] [--kv-heads H]
 //       [--head-dim D] [--seed S] [--overlap] [--json]
@@ -14,7 +14,9 @@
 // so the global length grows with the ranks (ring_attention_nccl_gpu_bench.cu:180-200).
 //   --numerics fp32 (head_dim 64): the fp32 partial-attention / merge / normalise
 //     kernels of legacy_fp32.cu; backends nccl | staged, sequential or --overlap
-//     (the next shard moves while the current one is computed). --init legacy
+//     (the next shard moves while the current one is computed), and p2p | ce (the
+//     shard moves through RingExchange's slots by the NVLink push kernel / the
+//     copy engine; sequential order). --init legacy
 //     reproduces the reference's inputs (K == V, no softmax scale) so
 //     `verify_full <dir> N kv_size` checks the dumps.
 //   --numerics bf16 (head_dim 64 or 128): the sm_100a kernels; fused (transport
@@ -36,6 +38,7 @@
 #include <torch/types.h>
 
 #include <algorithm>
+#include <array>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -46,6 +49,7 @@
 #include <vector>
 
 #include "../comm/ring_engine.hpp"
+#include "../comm/ring_exchange.hpp"
 #include "../common/synth.hpp"
 #include "../sched/shard_plan.hpp"
 #include "dist_env.hpp"
@@ -118,7 +122,8 @@ bool parse(int argc, char** argv, Args* a) {
   if (a->backend.empty()) a->backend = a->numerics == "bf16" ? "fused" : "nccl";
   return (a->numerics == "fp32" || a->numerics == "bf16") &&
          (a->backend == "fused" || a->backend == "p2p_unfused" || a->backend == "ce_unfused" ||
-          a->backend == "nccl" || a->backend == "staged") &&
+          a->backend == "nccl" || a->backend == "staged" || a->backend == "p2p" ||
+          a->backend == "ce") &&
          (a->init == "legacy" || a->init == "randn");
 }
 
@@ -284,6 +289,20 @@ class Fp32Ring {
         cudaMallocHost(&h_recv_[i], nb);
       }
     }
+    if (a.backend == "p2p" || a.backend == "ce") {
+      // KV rotation through RingExchange's receive slots (K, then V unless K == V)
+      kv_bytes_ = k.numel() * 4 * (same_kv_ ? 1 : 2);
+      cudaDeviceProp prop;
+      cudaGetDeviceProperties(&prop, d.device());
+      ex_ = std::make_unique<mgfa::RingExchange>(d.rank(), d.world(), d.device(),
+                                                 (kv_bytes_ + 4095) / 4096 * 4096,
+                                                 2 * prop.multiProcessorCount);
+      ex_->connect(d.all_gather(ex_->ipc_handle()));
+      ex_status_ = torch::zeros({1}, torch::TensorOptions().dtype(torch::kInt32).device(
+                                         torch::kCUDA, d.device()));
+      cudaDeviceSynchronize();
+      d.barrier();
+    }
     comm_ = c10::cuda::getStreamFromPool(false, d.device());
   }
   ~Fp32Ring() {
@@ -293,7 +312,64 @@ class Fp32Ring {
     }
   }
 
+  // K / V views of RingExchange slot i.
+  std::array<torch::Tensor, 2> slot_kv(int i) {
+    auto b = ex_->slot(i).narrow(0, 0, kv_bytes_).view(torch::kFloat32);
+    const int64_t n = k_.numel();
+    auto kk = b.narrow(0, 0, n).view(k_.sizes());
+    return {kk, same_kv_ ? kk : b.narrow(0, n, n).view(v_.sizes())};
+  }
+
+  // Sequential ring over RingExchange: own shard, then per step one transfer into
+  // slot (s+1) % 2 and the attention on it. Each push hands its slot back only
+  // after reading it, and in this order every attention on a slot finishes
+  // before the push that forwards (and releases) it.
+  StepTimes run_exchange(bool log_steps) {
+    const int P = d_.world(), r = d_.rank();
+    cudaStream_t cs = at::cuda::getCurrentCUDAStream();
+    StepTimes st;
+    Ev t0, t1, c0, c1;
+    t0.record(cs);
+    c0.record(cs);
+    auto own = slot_kv(0);
+    own[0].copy_(k_);
+    if (!same_kv_) own[1].copy_(v_);
+    c1.record(cs);
+    st.comm += elapsed(c0, c1);
+    if (log_steps)
+      std::printf("[Rank %d] step=own compute_kv_owner=%d KV tokens=%s\n", r, r,
+                  m_.plan.describe(r).c_str());
+    attend(k_, v_, r, true, &st);
+    for (int s = 0; s < P - 1; ++s) {
+      Ev s0, s1;
+      s0.record(cs);
+      ex_->step(s, kv_bytes_, a_.backend, ex_status_, kWaitNs);
+      s1.record(cs);
+      st.comm += elapsed(s0, s1);
+      const int owner = m_.plan.receive_owner(r, s);
+      if (log_steps)
+        std::printf("[Rank %d] step=%d received_kv_owner=%d KV tokens=%s\n", r, s, owner,
+                    m_.plan.describe(owner).c_str());
+      auto kv = slot_kv((s + 1) & 1);
+      attend(kv[0], kv[1], owner, false, &st);
+    }
+    ex_->release(P - 1, a_.backend, ex_status_, kWaitNs);
+    Ev f0, f1;
+    f0.record(cs);
+    mgfa::legacy_normalize(acc_run_, l_run_, out_, c10::nullopt, c10::nullopt);
+    st.host = out_.cpu();
+    f1.record(cs);
+    t1.record(cs);
+    cudaDeviceSynchronize();
+    if (ex_status_.item<int>() != 0)
+      throw std::runtime_error("transport status " + std::to_string(ex_status_.item<int>()));
+    st.final = elapsed(f0, f1);
+    st.total = elapsed(t0, t1);
+    return st;
+  }
+
   StepTimes run(bool log_steps) {
+    if (ex_) return run_exchange(log_steps);
     const int P = d_.world(), r = d_.rank();
     cudaStream_t cs = at::cuda::getCurrentCUDAStream();
     StepTimes st;
@@ -434,6 +510,9 @@ class Fp32Ring {
   void* h_send_[2] = {nullptr, nullptr};
   void* h_recv_[2] = {nullptr, nullptr};
   c10::cuda::CUDAStream comm_ = c10::cuda::getDefaultCUDAStream();
+  std::unique_ptr<mgfa::RingExchange> ex_;
+  int64_t kv_bytes_ = 0;
+  torch::Tensor ex_status_;
 };
 
 // ----------------------------------------------------------------- 16-bit rings
@@ -643,7 +722,7 @@ static int run_main(int argc, char** argv) {
   Args a;
   if (!parse(argc, argv, &a)) {
     std::printf("Usage: ring_attention_bench <kv_size_bytes> [warmup] [iters] "
-                "[--backend fused|p2p_unfused|ce_unfused|nccl|staged] [--numerics fp32|bf16] "
+                "[--backend fused|p2p_unfused|ce_unfused|nccl|staged|p2p|ce] [--numerics fp32|bf16] "
                 "[--init legacy|randn] "
                 "[--layout contiguous|zigzag|striped|scheduler] [--policy dp|lpt] [--causal] "
                 "[--heads H] [--kv-heads H] [--head-dim D] [--seed S] [--overlap] [--json]\n");
@@ -672,8 +751,12 @@ static int run_main(int argc, char** argv) {
          ", warmup >= 0, iters > 0.");
     return 1;
   }
-  if (a.numerics == "fp32" && (D != 64 || (a.backend != "nccl" && a.backend != "staged"))) {
-    log0("fp32 numerics: head_dim 64, backends nccl or staged");
+  const bool exchange = a.backend == "p2p" || a.backend == "ce";
+  if ((a.numerics == "fp32" && (D != 64 || (a.backend != "nccl" && a.backend != "staged" &&
+                                            !exchange))) ||
+      (a.numerics == "bf16" && exchange) || (a.overlap && exchange)) {
+    log0("fp32 numerics: head_dim 64, backends nccl, staged, p2p or ce (p2p and ce run in the "
+         "sequential order only)");
     return 1;
   }
   if (a.numerics == "bf16" && D != 64 && D != 128) {
@@ -759,10 +842,10 @@ static int run_main(int argc, char** argv) {
     }
   }
   const std::string name = a.backend + (a.overlap ? "_overlap" : "");
-  const char* comm_name = a.backend == "nccl"         ? "NCCL"
-                          : a.backend == "staged"     ? "MPI"
-                          : a.backend == "ce_unfused" ? "CE"
-                                                      : "P2P";
+  const char* comm_name = a.backend == "nccl"                              ? "NCCL"
+                          : a.backend == "staged"                          ? "MPI"
+                          : a.backend == "ce_unfused" || a.backend == "ce" ? "CE"
+                                                                           : "P2P";
   if (r == 0) {
     const double n = a.iters;
     std::printf("%s bench: warmup=%d iters=%d\n", name.c_str(), a.warmup, a.iters);

@@ -69,16 +69,19 @@ class RingExchange {
     push.credit = buf_.flag(r, comm::kCredit0 + sn);
     push.credit_target = uses_[sn];
     push.n_chunks = chunks;
+    // Every step uses slot s and hands it back to the left neighbour once this
+    // push has read it. At t > 0 the left neighbour filled it during step t-1,
+    // so the push first waits for all its chunks; at t = 0 it holds this rank's
+    // own data (no wait), which the left neighbour's step-1 push (P >= 3) must
+    // not overwrite before this push is done -- hence the release at t = 0 too.
     RingConsume consume;
-    if (t > 0) {  // slot s was filled by the left neighbour during step t-1
-      consume.enabled = 1;
-      consume.arrivals = buf_.flag(r, comm::kArrivals0 + s);
-      consume.arrivals_target = chunks;
-      consume.done_counter = buf_.flag(r, comm::kDone0 + s);
-      consume.done_target = uint32_t(n_ctas_ - 1);
-      consume.left_credit = buf_.flag(left, comm::kCredit0 + s);
-      consume.left_credit_value = uses_[s] + 1;
-    }
+    consume.enabled = 1;
+    consume.arrivals = buf_.flag(r, comm::kArrivals0 + s);
+    consume.arrivals_target = t > 0 ? chunks : 0u;
+    consume.done_counter = buf_.flag(r, comm::kDone0 + s);
+    consume.done_target = uint32_t(n_ctas_ - 1);
+    consume.left_credit = buf_.flag(left, comm::kCredit0 + s);
+    consume.left_credit_value = uses_[s] + 1;
     uint32_t* st = reinterpret_cast<uint32_t*>(status.data_ptr<int>());
     if (transport == "p2p") {
       C10_CUDA_CHECK(ring_push_launch(push, consume, st, uint64_t(wait_limit_ns), n_ctas_, stream));
@@ -90,7 +93,7 @@ class RingExchange {
     } else {
       MGFA_CHECK(false, "transport must be p2p or ce");
     }
-    if (t > 0) uses_[s] += 1;
+    uses_[s] += 1;
   }
 
   // Finish with slot t % 2 after the last step: wait until it has fully

@@ -10,7 +10,9 @@ Shapes follow the reference: tokens per rank = kv_size_bytes / (heads * head_dim
 (ring/attention/bench/ring_attention_nccl_gpu_bench.cu:180-200).
 
 --numerics fp32 (default; head_dim 64): the fp32 kernels of csrc/kernels/legacy_fp32.cu,
-  backends nccl | staged. --init legacy reproduces the reference's inputs (K == V,
+  backends nccl | staged | p2p | ce (p2p / ce: the KV shard moves through
+  RingExchange's receive slots by the NVLink push kernel / the copy engine, in the
+  sequential order). --init legacy reproduces the reference's inputs (K == V,
   no softmax scale) so `verify_full <dir> N kv_size` checks the dumps;
   --init randn uses the seeded N(0,1) streams and scale 1/sqrt(d)
   (`verify_full <dir> N kv_size --init randn`).
@@ -40,7 +42,7 @@ from ..parallel.layouts import RingLayout
 from . import common
 
 COMM_NAME = {"nccl": "NCCL", "staged": "MPI", "fused": "P2P", "p2p_unfused": "P2P",
-             "ce_unfused": "CE"}
+             "ce_unfused": "CE", "p2p": "P2P", "ce": "CE"}
 
 
 def parse():
@@ -49,7 +51,7 @@ def parse():
     ap.add_argument("warmup", type=int, nargs="?", default=10)
     ap.add_argument("iters", type=int, nargs="?", default=100)
     ap.add_argument("--backend", default=None,
-                    choices=["fused", "p2p_unfused", "ce_unfused", "nccl", "staged"])
+                    choices=["fused", "p2p_unfused", "ce_unfused", "nccl", "staged", "p2p", "ce"])
     ap.add_argument("--numerics", default="fp32", choices=["fp32", "bf16"])
     ap.add_argument("--init", default="legacy", choices=["legacy", "randn"])
     ap.add_argument("--layout", default="contiguous",
@@ -138,7 +140,24 @@ class Fp32Ring:
         if args.backend == "staged":
             self.h_send = [torch.empty(self.k.shape, pin_memory=True) for _ in range(2)]
             self.h_recv = [torch.empty(self.k.shape, pin_memory=True) for _ in range(2)]
+        if args.backend in ("p2p", "ce"):
+            # KV rotation through RingExchange's two receive slots (K, then V
+            # unless K == V), moved by the push kernel or the copy engine
+            n = self.k.numel()
+            self.kv_bytes = n * 4 * (1 if self.same_kv else 2)
+            sms = torch.cuda.get_device_properties(dev).multi_processor_count
+            self.ex = C().RingExchange(ctx.rank, P, dev.index,
+                                       (self.kv_bytes + 4095) // 4096 * 4096, 2 * sms)
+            common.exchange_handles(self.ex, P)
+            self.ex_status = torch.zeros(1, dtype=torch.int32, device=dev)
+            torch.cuda.synchronize()
         self.comm_stream = torch.cuda.Stream(dev)
+
+    def _slot_kv(self, i):
+        b = self.ex.slot(i)[: self.kv_bytes].view(torch.float32)
+        n = self.k.numel()
+        kk = b[:n].view(self.k.shape)
+        return kk, (kk if self.same_kv else b[n: 2 * n].view(self.v.shape))
 
     def _attn_merge(self, kk, vv, owner, first):
         Cm = C()
@@ -185,7 +204,57 @@ class Fp32Ring:
     def _kv(self, pair):
         return (pair[0], pair[0]) if self.same_kv else (pair[0], pair[1])
 
+    def _run_exchange(self, log_steps):
+        """Sequential ring over RingExchange: own shard, then per step one
+        transfer into slot (s+1) % 2 and the attention on it. Each push hands its
+        slot back only after reading it, and in this order every attention on a
+        slot finishes before the push that forwards (and releases) it."""
+        ctx, lay, P, r = self.ctx, self.lay, self.ctx.world, self.ctx.rank
+        t_comm = t_attn = t_merge = 0.0
+        ex, limit = self.ex, 2_000_000_000
+        e_tot0, e_tot1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e_tot0.record()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record()
+        kk, vv = self._slot_kv(0)
+        kk.copy_(self.k)
+        if not self.same_kv:
+            vv.copy_(self.v)
+        c1.record()
+        torch.cuda.synchronize()
+        t_comm += c0.elapsed_time(c1)
+        if log_steps:
+            ctx.log(f"[Rank {r}] step=own compute_kv_owner={r} KV tokens={tokens(lay, r)}")
+        a, m = self._attn_merge(self.k, self.v, r, True)
+        t_attn += a
+        t_merge += m
+        for s in range(P - 1):
+            c0.record()
+            ex.step(s, self.kv_bytes, self.args.backend, self.ex_status, limit)
+            c1.record()
+            torch.cuda.synchronize()
+            t_comm += c0.elapsed_time(c1)
+            owner = lay.receive_owner(r, s)
+            if log_steps:
+                ctx.log(f"[Rank {r}] step={s} received_kv_owner={owner} KV tokens={tokens(lay, owner)}")
+            a, m = self._attn_merge(*self._slot_kv((s + 1) & 1), owner, False)
+            t_attn += a
+            t_merge += m
+        ex.release(P - 1, self.args.backend, self.ex_status, limit)
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        C().legacy_normalize(self.acc_run, self.l_run, self.out)
+        host = self.out.cpu()
+        f1.record()
+        e_tot1.record()
+        torch.cuda.synchronize()
+        if int(self.ex_status.item()):
+            raise RuntimeError(f"[Rank {r}] transport status {int(self.ex_status.item()):#x}")
+        return e_tot0.elapsed_time(e_tot1), t_comm, t_attn, t_merge, f0.elapsed_time(f1), host
+
     def run(self, log_steps):
+        if self.args.backend in ("p2p", "ce"):
+            return self._run_exchange(log_steps)
         ctx, lay, P, r = self.ctx, self.lay, self.ctx.world, self.ctx.rank
         t_comm = t_attn = t_merge = 0.0
         e_tot0, e_tot1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -331,8 +400,12 @@ def main():
                  "warmup >= 0, iters > 0.")
         ctx.close()
         return 1
-    if args.numerics == "fp32" and (D != 64 or args.backend == "fused"):
-        ctx.log0("fp32 numerics: head_dim 64, backends nccl or staged")
+    fp32_backends = ("nccl", "staged", "p2p", "ce")
+    if (args.numerics == "fp32" and (D != 64 or args.backend not in fp32_backends)) or \
+            (args.numerics == "bf16" and args.backend in ("p2p", "ce")) or \
+            (args.overlap and args.backend in ("p2p", "ce")):
+        ctx.log0("fp32 numerics: head_dim 64, backends nccl, staged, p2p or ce (p2p and ce "
+                 "run in the sequential order only)")
         ctx.close()
         return 1
     if args.init == "legacy" and (H != 1 or args.layout != "contiguous" or args.causal

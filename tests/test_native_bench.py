@@ -70,7 +70,8 @@ def test_ring_loop_bench_payload_mode(tmp_path):
 @pytest.mark.gpu
 @pytest.mark.multigpu
 @pytest.mark.parametrize("extra", [["--backend", "nccl"], ["--backend", "staged"],
-                                   ["--backend", "nccl", "--overlap"]])
+                                   ["--backend", "nccl", "--overlap"], ["--backend", "p2p"],
+                                   ["--backend", "ce"]])
 def test_ring_attention_bench_fp32_passes_verify_full(tmp_path, extra):
     size = 1024 * 64 * 4
     out = _torchrun(_exe("ring_attention_bench"), [size, 1, 2] + extra, _world(), tmp_path,
@@ -146,7 +147,7 @@ def test_native_layout_tables_match_python(layout, world, causal):
 @pytest.mark.gpu
 @pytest.mark.multigpu
 @pytest.mark.parametrize("extra", [["--backend", "nccl"], ["--backend", "staged"],
-                                   ["--backend", "nccl", "--overlap"]])
+                                   ["--backend", "nccl", "--overlap"], ["--backend", "p2p"]])
 def test_fp32_randn_seq4096_two_ranks(tmp_path, extra):
     """fp32 N(0,1) q/k/v (seed 0), 1 head x d64, 4096 tokens over 2 ranks in
     contiguous 2048-token shards, scale 1/8, non-causal: every rank's dump within
