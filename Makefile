@@ -30,7 +30,7 @@ NCCL_DIR  := $(shell $(PY) -c "import nvidia.nccl as n; print(list(n.__path__)[0
 CUDA_HOME ?= /usr/local/cuda
 TORCH_INC := -isystem $(TORCH_DIR)/include -isystem $(TORCH_DIR)/include/torch/csrc/api/include \
              -isystem $(NCCL_DIR)/include -isystem $(CUDA_HOME)/include -Icsrc
-TORCH_DEF := -D_GLIBCXX_USE_CXX11_ABI=1
+TORCH_DEF := -D_GLIBCXX_USE_CXX11_ABI=1 $(if $(filter 1,$(MGFA_DEBUG)),-DMGFA_DEBUG)
 GPU_CXX   := $(CXX) -O3 -std=c++17 -fPIC -pthread $(TORCH_DEF) $(TORCH_INC)
 GPU_NVCC  := $(NVCC) -O3 -std=c++17 -lineinfo --expt-relaxed-constexpr \
              -gencode arch=compute_100a,code=sm_100a -Xcompiler -fPIC $(TORCH_DEF) $(TORCH_INC) \

@@ -159,12 +159,16 @@ class RingBwdEngine {
         pk.ring.acc_in_dv = reinterpret_cast<const float*>(slot(r, s) + 4 * kv_bytes_);
       }
       pk.ring.enabled = 1;
+      // each accumulator region (slot or home) holds 2 * kv_bytes_ bytes of fp32
+      pk.ring.acc_out_elems = int64_t(kv_bytes_ / 2);
       if (t < P - 1) {
         pk.push.enabled = 1;
         pk.push.src_k = cur_k;
         pk.push.src_v = cur_v;
         pk.push.dst_k = slot(right, sn);
         pk.push.dst_v = slot(right, sn) + kv_bytes_;
+        pk.push.dst_k_end = pk.push.dst_v;
+        pk.push.dst_v_end = slot(right, sn) + 2 * kv_bytes_;
         pk.push.bytes = kvb;
         pk.push.peer_arrivals = buf_.flag(right, comm::kArrivals0 + sn);
         pk.push.credit = buf_.flag(r, comm::kCredit0 + sn);

@@ -202,6 +202,8 @@ class RingEngine {
         p.push.src_v = cur_v;
         p.push.dst_k = slot_k(right, sn);
         p.push.dst_v = slot_v(right, sn);
+        p.push.dst_k_end = p.push.dst_k + slot_bytes_;
+        p.push.dst_v_end = p.push.dst_v + slot_bytes_;
         p.push.bytes = shard_bytes;
         p.push.peer_arrivals = buf_.flag(right, comm::kArrivals0 + sn);
         p.push.credit = buf_.flag(r, comm::kCredit0 + sn);

@@ -64,6 +64,8 @@ class RingExchange {
     push.src_v = push.src_k + half;
     push.dst_k = buf_.payload(right) + size_t(sn) * slot_bytes_;
     push.dst_v = push.dst_k + half;
+    push.dst_k_end = push.dst_v;
+    push.dst_v_end = push.dst_k + slot_bytes_;
     push.bytes = half;
     push.peer_arrivals = buf_.flag(right, comm::kArrivals0 + sn);
     push.credit = buf_.flag(r, comm::kCredit0 + sn);

@@ -615,6 +615,9 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
       __syncwarp();
       ok = __all_sync(0xffffffffu, ok && *abort_flag == 0);
       auto add_store = [&](float* dst, const float* src, float mul) {
+        if (!MGFA_IN_BOUNDS(!p.ring.acc_out_elems || off + kD <= p.ring.acc_out_elems, p.status,
+                            95))
+          return;
         float4* d = reinterpret_cast<float4*>(dst + off);
         const float4* a = src ? reinterpret_cast<const float4*>(src + off) : nullptr;
 #pragma unroll

@@ -21,6 +21,8 @@ struct BwdRing {
   uint32_t* acc_arrivals = nullptr;   // right neighbour's arrival counter of the destination
   const uint32_t* acc_credit = nullptr;  // local: right's finished uses of the destination
   uint32_t acc_credit_target = 0;
+  int64_t acc_out_elems = 0;          // floats at acc_out_dk / acc_out_dv; debug builds
+                                      // skip (and report) a row store past them
   int enabled = 0;
 };
 

@@ -28,6 +28,8 @@ struct RingPush {
                                       // never signalled, so the receiver's wait must expire
   uint32_t* peer_tag = nullptr;       // right neighbour's tag word for that slot
   uint32_t tag = 0;                   // (owner + 1) | (call << 8): written before signalling
+  const uint8_t* dst_k_end = nullptr;  // ends of the destination buffers; debug builds
+  const uint8_t* dst_v_end = nullptr;  // skip (and report) a store past them
 };
 
 // Consumer side of one ring step.

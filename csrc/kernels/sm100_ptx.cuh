@@ -29,6 +29,7 @@ enum : uint32_t {
   kErrPeerTimeout = 2,   // a peer flag never reached the expected epoch
   kErrTagMismatch = 3,   // a received slot carried the wrong (step, owner) tag
   kErrBadArgument = 4,
+  kErrBounds = 5,        // (debug builds) an access outside its buffer was skipped
 };
 
 // Status word layout: code in bits [0,8), role/site in [8,16), step in [16,32).
@@ -36,6 +37,17 @@ __device__ __forceinline__ void record_error(uint32_t* status, uint32_t code, ui
                                              uint32_t step) {
   if (status) atomicCAS(status, 0u, code | (site << 8) | (step << 16));
 }
+
+// Bounds check of the debug build (MGFA_DEBUG): a false condition records
+// kErrBounds with `site` and evaluates to false, so the caller skips the access
+// (no trap, the kernel runs to its end). In normal builds it is `true`.
+#ifdef MGFA_DEBUG
+#define MGFA_IN_BOUNDS(cond, status, site)                                         \
+  ((cond) ? true                                                                  \
+          : (::mgfa::dev::record_error((status), ::mgfa::dev::kErrBounds, (site), 0), false))
+#else
+#define MGFA_IN_BOUNDS(cond, status, site) true
+#endif
 
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;

@@ -38,6 +38,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("q_tile_pos"), py::arg("kv_tile_pos"), py::arg("merge"), py::arg("final_out"),
         py::arg("status"), py::arg("wait_limit_ns") = int64_t(2000000000));
   m.def("flash_fwd_smem_bytes", &mgfa::flash_fwd_smem_bytes);
+  m.def("debug_build", []() {
+#ifdef MGFA_DEBUG
+    return true;
+#else
+    return false;
+#endif
+  });
   m.def("legacy_partial", &mgfa::legacy_partial, py::arg("q"), py::arg("k"), py::arg("v"),
         py::arg("scale"), py::arg("q_pos"), py::arg("k_pos"), py::arg("causal"), py::arg("acc"),
         py::arg("m"), py::arg("l"), py::arg("merge"));

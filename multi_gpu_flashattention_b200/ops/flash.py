@@ -29,7 +29,8 @@ class KernelStatusError(RuntimeError):
 
 
 _CODES = {1: "mbarrier wait timed out", 2: "peer flag wait timed out",
-          3: "received slot carried the wrong tag", 4: "bad argument"}
+          3: "received slot carried the wrong tag", 4: "bad argument",
+          5: "out-of-bounds store skipped (debug build)"}
 
 
 def check_status(status: torch.Tensor, what: str = "kernel") -> None:

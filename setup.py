@@ -18,6 +18,9 @@ which = os.environ.get("MGFA_BUILD", "all")
 
 SM100 = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CXX_FLAGS = ["-O3", "-std=c++17", "-Wall", "-Wno-unused-function"]
+# MGFA_DEBUG=1: device-side bounds checks on the peer stores of the ring
+# transports (a violation is reported in the status word and skipped)
+DEBUG = ["-DMGFA_DEBUG"] if os.environ.get("MGFA_DEBUG", "0") == "1" else []
 
 ext_modules = []
 cmdclass = {}
@@ -62,9 +65,9 @@ if which in ("all", "cuda"):
             ],
             include_dirs=[os.path.join(ROOT, "csrc")],
             extra_compile_args={
-                "cxx": ["-O3", "-std=c++17"],
+                "cxx": ["-O3", "-std=c++17"] + DEBUG,
                 "nvcc": ["-O3", "-std=c++17", "-lineinfo", "--expt-relaxed-constexpr",
-                         "-Xptxas=-v"] + SM100,
+                         "-Xptxas=-v"] + SM100 + DEBUG,
             },
             libraries=["cuda"] if os.path.exists("/usr/lib/x86_64-linux-gnu/libcuda.so") else [],
         )

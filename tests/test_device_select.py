@@ -36,3 +36,14 @@ def test_fallback_and_oversubscribe(clean_env):
 def test_no_devices(clean_env):
     dev, _, _, err = choose_device(0, 0)
     assert dev == -1 and "No CUDA devices" in err
+
+
+def test_product_build_is_not_the_debug_build():
+    """The in-tree extension is the normal build (MGFA_DEBUG adds bounds checks)."""
+    import pytest
+    try:
+        from multi_gpu_flashattention_b200._ext import C
+        m = C()
+    except Exception as e:  # pragma: no cover - extension not built
+        pytest.skip(f"extension not built: {e}")
+    assert m.debug_build() is False
