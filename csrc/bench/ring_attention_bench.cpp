@@ -344,6 +344,8 @@ class Fp32Ring {
       Ev s0, s1;
       s0.record(cs);
       ex_->step(s, kv_bytes_, a_.backend, ex_status_, kWaitNs);
+      // the left neighbour's transfer into the slot read next may still be in flight
+      ex_->wait_received(s, a_.backend, ex_status_, kWaitNs);
       s1.record(cs);
       st.comm += elapsed(s0, s1);
       const int owner = m_.plan.receive_owner(r, s);

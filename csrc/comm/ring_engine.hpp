@@ -189,9 +189,17 @@ class RingEngine {
       p.final_out = t == P - 1 ? 1 : 0;
       p.status = reinterpret_cast<uint32_t*>(status.data_ptr<int>());
       p.wait_limit_ns = uint64_t(wait_limit_ns);
-      // steps after the first overlap the previous step's tail (PDL); the first
-      // step of a call is fully ordered after everything before it
-      p.dependent_launch = (t > 0 && pdl_) ? 1 : 0;
+      // Steps after the first overlap the previous step's tail (dependent
+      // launch); the first step of a call is fully ordered after everything
+      // before it. Step t+1 releases its slot only after step t's grid is
+      // complete (the epilogue's griddepcontrol.wait), but when a grid is
+      // smaller than the SM count, steps t+1 and t+2 can be fully resident
+      // while step t runs, so step t+3 could start and see step t's arrival
+      // count on the slot they share before step t resets it (the owner tag
+      // check would then fail the call). With P >= 5, where such a step t+3
+      // exists, small grids therefore run without dependent launch.
+      const bool chain_hazard = P >= 5 && grid < num_sms_;
+      p.dependent_launch = (t > 0 && pdl_ && !chain_hazard) ? 1 : 0;
 
       RingPush push_x;     // the standalone push kernel's (unfused transport)
       RingConsume wait_x;  // its wait for the slot it forwards

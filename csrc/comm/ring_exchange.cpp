@@ -13,6 +13,7 @@ void register_ring_exchange(py::module& m) {
       .def("connect", &RingExchange::connect)
       .def("slot", &RingExchange::slot)
       .def("step", &RingExchange::step)
+      .def("wait_received", &RingExchange::wait_received)
       .def("rotate", &RingExchange::rotate)
       .def("release", &RingExchange::release)
       .def("reset", &RingExchange::reset)

@@ -98,6 +98,24 @@ class RingExchange {
     uses_[s] += 1;
   }
 
+  // Wait (on the current stream) until slot (t+1) % 2, which the left
+  // neighbour fills during step t, has fully arrived. step(t) itself only waits
+  // for the slot it forwards, so a caller that reads the received shard before
+  // the next step must call this first. The counter stays armed for the
+  // slot's next consumer (the next step or release()).
+  void wait_received(int t, const std::string& transport, torch::Tensor status,
+                     int64_t wait_limit_ns) {
+    const int sn = (t + 1) & 1;
+    c10::cuda::CUDAGuard guard(buf_.device());
+    cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+    RingConsume arrived;
+    arrived.enabled = 1;
+    arrived.arrivals = buf_.flag(buf_.rank(), comm::kArrivals0 + sn);
+    arrived.arrivals_target = transport == "p2p" ? uint32_t(n_ctas_) : 1u;
+    uint32_t* st = reinterpret_cast<uint32_t*>(status.data_ptr<int>());
+    C10_CUDA_CHECK(ring_wait_launch(RingPush(), arrived, st, uint64_t(wait_limit_ns), stream));
+  }
+
   // Finish with slot t % 2 after the last step: wait until it has fully
   // arrived, re-arm its counter and hand it back to the left neighbour (the data
   // stays readable until the next rotation overwrites it).

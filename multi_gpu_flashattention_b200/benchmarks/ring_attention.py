@@ -231,6 +231,9 @@ class Fp32Ring:
         for s in range(P - 1):
             c0.record()
             ex.step(s, self.kv_bytes, self.args.backend, self.ex_status, limit)
+            # the left neighbour's transfer into the slot we read next may still
+            # be in flight: wait for its arrivals
+            ex.wait_received(s, self.args.backend, self.ex_status, limit)
             c1.record()
             torch.cuda.synchronize()
             t_comm += c0.elapsed_time(c1)

@@ -203,6 +203,8 @@ def run(ctx, args):
                 recv_buf = bufs[cur ^ 1]
             else:
                 ex.step(step, kv_bytes, "p2p", status, 2_000_000_000)
+                # the left neighbour's push into our slot may still be in flight
+                ex.wait_received(step, "p2p", status, 2_000_000_000)
                 recv_buf = slot_view((step + 1) & 1)
             t2 = clk.mark()
             parts = [(LABEL[args.backend], clk.ms(t1, t2))]

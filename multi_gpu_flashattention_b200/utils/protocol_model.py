@@ -1,0 +1,319 @@
+"""Executable model of the ring transports' flag protocols, for race checks.
+
+The native engines move KV shards between ranks through receive slots in each
+rank's symmetric buffer, ordered only by flag words (arrival counters written by
+the sender, credit words written back by the receiver) and by CUDA stream
+order on each rank. This module restates those rules as small state machines,
+one per concurrent activity (the consumer and producer sides of an attention
+kernel, a standalone push kernel, a release kernel), and lets a seeded random
+scheduler interleave the activities of all ranks. The checker fails when
+
+  * a store into a slot begins while a reader of that slot is still reading, or
+  * a reader finds in its slot anything but the shard it expects (owner, call).
+
+Models:
+  fused      RingEngine forward, transport in the attention kernel: step t
+             reads slot t % 3 (own buffers at t = 0), pushes into the right
+             neighbour's slot (t + 1) % 3 once the credit allows, and the last
+             CTA releases slot t % 3 to the left neighbour after every read
+             (including the push's) is done. Step t + 1 may start while step t
+             runs (dependent launch), but its epilogue waits for step t's grid
+             (griddepcontrol.wait), so it releases and finishes after step t;
+             the first step of a call starts after the previous call's last
+             step has finished. `small_grid=True` lets dependent launches chain
+             more than one step deep (grids smaller than the GPU);
+             `chain_guard=False` drops the engine's rule that turns dependent
+             launch off for those grids at P >= 5, which races.
+  push, ce   RingEngine forward with the transport on a second stream (the
+             standalone push kernel or the copy engine): the attention kernel
+             only waits; the transfer of step t starts after the compute
+             stream's earlier work; a release kernel frees the slot after both.
+  exchange   RingExchange (two slots, the rank's own shard starts in slot 0):
+             step t forwards slot t % 2 into the right neighbour's slot
+             (t + 1) % 2 and releases slot t % 2 after reading it; the caller
+             reads the received slot between steps (sequential order).
+             `release_slot0=False` drops the step-0 release of slot 0 (the
+             protocol before that fix) and races for P >= 3;
+             `wait_received=False` reads the received slot as soon as the
+             rank's own step is done, without waiting for its arrivals (a race
+             at any P).
+
+The flag arithmetic (slot indices, the host's per-slot use counters, credit
+targets and published credit values) follows csrc/comm/ring_engine.hpp and
+csrc/comm/ring_exchange.hpp.
+"""
+from __future__ import annotations
+
+import random
+from dataclasses import dataclass, field
+from typing import Callable, Dict, Generator, List, Optional, Tuple
+
+
+class ProtocolViolation(AssertionError):
+    """A slot was overwritten while being read, or held the wrong shard."""
+
+
+@dataclass
+class Slot:
+    content: Optional[Tuple[int, int]] = None   # (owner, call) of the last completed store
+    readers: int = 0                            # reads in progress
+    writing: bool = False
+
+
+@dataclass
+class Rank:
+    slots: List[Slot]
+    arrivals: List[int]
+    credit: List[int]                 # credit words this rank holds (written by its right)
+    uses: List[int]                   # host-side use counters of its own slots
+    started: Dict[Tuple[int, int], bool] = field(default_factory=dict)
+    finished: Dict[Tuple[int, int], bool] = field(default_factory=dict)
+    pushed: Dict[Tuple[int, int], bool] = field(default_factory=dict)
+
+
+Wait = Callable[[], bool]
+Proc = Generator[Wait, None, None]
+
+
+class Model:
+    def __init__(self, world: int, kind: str, calls: int = 2, seed: int = 0,
+                 release_slot0: bool = True, wait_received: bool = True,
+                 small_grid: bool = False, chain_guard: bool = True):
+        if kind not in ("fused", "push", "ce", "exchange"):
+            raise ValueError(kind)
+        self.P, self.kind, self.calls = world, kind, calls
+        self.release_slot0 = release_slot0
+        self.wait_received = wait_received
+        # fused engine: with grids larger than the GPU holds at once, step t+2
+        # cannot start before step t completed (step t+1's CTAs must all have
+        # started, and its first ones wait for step t); small grids let the
+        # chain run deeper. The engine turns dependent launch off for small
+        # grids when P >= 5 (chain_guard).
+        self.small_grid = small_grid
+        self.pdl = not (chain_guard and small_grid and world >= 5)
+        self.rng = random.Random(seed)
+        n_slots = 2 if kind == "exchange" else 3
+        self.nslots = n_slots
+        self.ranks = [Rank([Slot() for _ in range(n_slots)], [0] * n_slots, [0] * n_slots,
+                           [0] * n_slots) for _ in range(world)]
+        self.procs: List[Proc] = []
+        self.waits: List[Optional[Wait]] = []
+
+    # ------------------------------------------------------------ slot access
+    def _begin_read(self, r: int, s: int, expect: Tuple[int, int]) -> None:
+        slot = self.ranks[r].slots[s]
+        if slot.writing:
+            raise ProtocolViolation(f"rank {r} slot {s}: read began during a store")
+        if slot.content != expect:
+            raise ProtocolViolation(f"rank {r} slot {s}: holds {slot.content}, expected {expect}")
+        slot.readers += 1
+
+    def _end_read(self, r: int, s: int) -> None:
+        self.ranks[r].slots[s].readers -= 1
+
+    def _begin_write(self, r: int, s: int) -> None:
+        slot = self.ranks[r].slots[s]
+        if slot.readers:
+            raise ProtocolViolation(f"rank {r} slot {s}: store began while {slot.readers} "
+                                    "reader(s) still read it")
+        slot.writing = True
+
+    def _end_write(self, r: int, s: int, data: Tuple[int, int]) -> None:
+        slot = self.ranks[r].slots[s]
+        slot.writing = False
+        slot.content = data
+
+    # ------------------------------------------------------------ engine (forward)
+    def _engine_call(self, r: int, c: int) -> Proc:
+        """Host loop of one forward() call on rank r: enqueues the step kernels."""
+        P, R = self.P, self.ranks[r]
+        right, left = (r + 1) % P, (r - 1) % P
+        for t in range(P):
+            s, sn = t % 3, (t + 1) % 3
+            owner = (r - t) % P
+            # parameters fixed at enqueue time (host counters)
+            credit_target = R.uses[sn]
+            credit_value = R.uses[s] + 1
+            key = (c, t)
+            prev = (c, t - 1) if t > 0 else ((c - 1, P - 1) if c > 0 else None)
+            if self.kind == "fused":
+                self._spawn(self._fused_kernel(r, c, t, s, sn, owner, credit_target,
+                                               credit_value, prev, right, left))
+            else:
+                self._spawn(self._unfused_compute(r, c, t, s, owner, credit_value, prev, left))
+                if t < P - 1:
+                    self._spawn(self._unfused_transfer(r, c, t, s, sn, owner, credit_target,
+                                                       prev, right))
+            if t > 0:
+                R.uses[s] += 1
+            yield lambda: True
+        return
+
+    def _fused_kernel(self, r, c, t, s, sn, owner, credit_target, credit_value, prev, right,
+                      left) -> Proc:
+        R = self.ranks[r]
+        key = (c, t)
+        if prev is not None:
+            if t == 0 or not self.pdl:   # fully ordered after the previous step
+                yield lambda: R.finished.get(prev, False)
+            else:        # dependent launch: may start once the previous step started
+                yield lambda: R.started.get(prev, False)
+                if not self.small_grid and t >= 2:
+                    yield lambda: R.finished.get((c, t - 2), False)
+        R.started[key] = True
+        reading = False
+        if t > 0:
+            yield lambda: R.arrivals[s] >= 1
+            self._begin_read(r, s, (owner, c))
+            reading = True
+        if t < self.P - 1:
+            yield lambda: R.credit[sn] >= credit_target
+            self._begin_write(right, sn)
+            yield lambda: True
+            self._end_write(right, sn, (owner, c))
+            self.ranks[right].arrivals[sn] += 1
+        yield lambda: True                   # the rest of the attention work
+        if t > 0 and prev is not None:
+            # the epilogue's griddepcontrol.wait: the previous step's grid has
+            # completed before any CTA merges, releases or exits
+            yield lambda: R.finished.get(prev, False)
+        if reading:
+            self._end_read(r, s)
+            # last CTA: rearm the counter, then hand the slot back
+            R.arrivals[s] = 0
+            self.ranks[left].credit[s] = credit_value
+        R.finished[key] = True
+
+    def _unfused_compute(self, r, c, t, s, owner, credit_value, prev, left) -> Proc:
+        R = self.ranks[r]
+        key = (c, t)
+        if prev is not None:   # stream order: the previous step, its transfer and release
+            yield lambda: R.finished.get(prev, False) and R.pushed.get(prev, True)
+        R.started[key] = True
+        if t > 0:
+            yield lambda: R.arrivals[s] >= 1
+            self._begin_read(r, s, (owner, c))
+            yield lambda: True
+            self._end_read(r, s)
+            # release kernel: after the attention and this step's transfer
+            yield lambda: R.pushed.get(key, True)
+            R.arrivals[s] = 0
+            self.ranks[left].credit[s] = credit_value
+        else:
+            yield lambda: True
+        R.finished[key] = True
+
+    def _unfused_transfer(self, r, c, t, s, sn, owner, credit_target, prev, right) -> Proc:
+        R = self.ranks[r]
+        key = (c, t)
+        R.pushed[key] = False
+        if prev is not None:  # starts after the compute stream's earlier work
+            yield lambda: R.finished.get(prev, False) and R.pushed.get(prev, True)
+        reading = False
+        if t > 0:
+            yield lambda: R.arrivals[s] >= 1
+            self._begin_read(r, s, (owner, c))
+            reading = True
+        yield lambda: R.credit[sn] >= credit_target
+        self._begin_write(right, sn)
+        yield lambda: True
+        self._end_write(right, sn, (owner, c))
+        if reading:
+            self._end_read(r, s)
+        self.ranks[right].arrivals[sn] += 1
+        R.pushed[key] = True
+
+    # ------------------------------------------------------------ RingExchange
+    def _exchange_call(self, r: int, c: int) -> Proc:
+        """One rotation on rank r in the sequential order: own shard into slot 0,
+        then per step a transfer and a read of the received slot."""
+        P, R = self.P, self.ranks[r]
+        right, left = (r + 1) % P, (r - 1) % P
+        if c > 0:  # rotations are separated by a barrier
+            yield lambda: all(x.finished.get((c - 1, "rot"), False) for x in self.ranks)
+        self._begin_write(r, 0)
+        self._end_write(r, 0, (r, c))
+        for t in range(P - 1):
+            s, sn = t % 2, (t + 1) % 2
+            owner = (r - t) % P
+            credit_target = R.uses[sn]
+            consume = t > 0 or self.release_slot0
+            credit_value = R.uses[s] + 1
+            if t > 0:
+                yield lambda s=s: R.arrivals[s] >= 1
+            self._begin_read(r, s, (owner, c))
+            yield lambda sn=sn, ct=credit_target: R.credit[sn] >= ct
+            self._begin_write(right, sn)
+            yield lambda: True
+            self._end_write(right, sn, (owner, c))
+            self._end_read(r, s)
+            self.ranks[right].arrivals[sn] += 1
+            if consume:
+                R.arrivals[s] = 0
+                self.ranks[left].credit[s] = credit_value
+                R.uses[s] += 1
+            # the caller reads the received slot before the next step: after
+            # waiting for its arrivals (wait_received), or -- the race -- as soon
+            # as its own step is done
+            if self.wait_received:
+                yield lambda sn=sn: R.arrivals[sn] >= 1
+            else:
+                yield lambda: True
+            self._begin_read(r, sn, ((owner - 1) % P, c))
+            yield lambda: True
+            self._end_read(r, sn)
+        # release of the last slot
+        s = (P - 1) % 2
+        yield lambda s=s: R.arrivals[s] >= 1
+        R.arrivals[s] = 0
+        self.ranks[left].credit[s] = R.uses[s] + 1
+        R.uses[s] += 1
+        R.finished[(c, "rot")] = True
+
+    # ------------------------------------------------------------ scheduler
+    def _spawn(self, proc: Proc) -> None:
+        self.procs.append(proc)
+        self.waits.append(None)
+        self._advance(len(self.procs) - 1)
+
+    def _advance(self, i: int) -> None:
+        try:
+            self.waits[i] = next(self.procs[i])
+        except StopIteration:
+            self.waits[i] = None
+            self.procs[i] = None
+
+    def run(self, max_events: int = 200000) -> int:
+        """Interleaves every activity at random until all finish; returns the
+        number of scheduling events. Raises ProtocolViolation on a race and
+        RuntimeError on a deadlock."""
+        for r in range(self.P):
+            if self.kind == "exchange":
+                calls = [self._exchange_call(r, c) for c in range(self.calls)]
+            else:
+                calls = [self._engine_call(r, c) for c in range(self.calls)]
+            self._spawn(_chain(calls))
+        events = 0
+        while any(p is not None for p in self.procs):
+            ready = [i for i, (p, w) in enumerate(zip(self.procs, self.waits))
+                     if p is not None and w is not None and w()]
+            if not ready:
+                raise RuntimeError("deadlock: no activity can proceed")
+            self._advance(self.rng.choice(ready))
+            events += 1
+            if events > max_events:
+                raise RuntimeError("event budget exhausted")
+        return events
+
+
+def _chain(gens: List[Proc]) -> Proc:
+    for g in gens:
+        yield from g
+
+
+def check(world: int, kind: str, calls: int = 2, seeds: int = 50, release_slot0: bool = True,
+          wait_received: bool = True, small_grid: bool = False, chain_guard: bool = True) -> None:
+    """Runs `seeds` random interleavings; raises on the first violation."""
+    for seed in range(seeds):
+        Model(world, kind, calls, seed, release_slot0, wait_received, small_grid,
+              chain_guard).run()

@@ -1,0 +1,44 @@
+"""Race checks of the ring transports' flag protocols (executable model in
+multi_gpu_flashattention_b200/utils/protocol_model.py), under seeded random
+interleavings of every rank's activities."""
+import pytest
+
+from multi_gpu_flashattention_b200.utils.protocol_model import ProtocolViolation, check
+
+
+@pytest.mark.parametrize("kind", ["fused", "push", "ce"])
+@pytest.mark.parametrize("world", [2, 3, 5, 8])
+@pytest.mark.parametrize("small_grid", [False, True])
+def test_engine_protocols_are_race_free(kind, world, small_grid):
+    check(world, kind, calls=3, seeds=12, small_grid=small_grid)
+
+
+@pytest.mark.parametrize("world", [2, 3, 4, 5])
+def test_exchange_protocol_is_race_free(world):
+    check(world, "exchange", calls=3, seeds=20)
+
+
+def test_engine_without_chain_guard_races_on_small_grids():
+    """Dependent launches chained deeper than one step let step t+3 read the
+    slot it shares with step t before step t resets its arrival count."""
+    with pytest.raises(ProtocolViolation):
+        check(5, "fused", calls=2, seeds=200, small_grid=True, chain_guard=False)
+
+
+def test_exchange_without_slot0_release_races():
+    """Without the step-0 release, a step-1 push can overwrite a rank's own
+    shard while its step-0 push still reads it (P >= 3)."""
+    with pytest.raises(ProtocolViolation, match="store began while"):
+        check(3, "exchange", calls=2, seeds=200, release_slot0=False)
+
+
+def test_reading_the_received_slot_needs_its_arrivals():
+    with pytest.raises(ProtocolViolation):
+        check(2, "exchange", calls=2, seeds=200, wait_received=False)
+
+
+def test_two_ranks_are_safe_without_the_guards():
+    """The races above need a third rank (slot 0) or a deep chain (P >= 5):
+    two-rank runs could not have shown them."""
+    check(2, "exchange", calls=3, seeds=50, release_slot0=False)
+    check(4, "fused", calls=3, seeds=50, small_grid=True, chain_guard=False)
