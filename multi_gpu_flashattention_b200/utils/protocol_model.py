@@ -28,6 +28,12 @@ Models:
              standalone push kernel or the copy engine): the attention kernel
              only waits; the transfer of step t starts after the compute
              stream's earlier work; a release kernel frees the slot after both.
+  backward   RingBwdEngine: per step the dK/dV kernel consumes slot t % 3 (K, V
+             and the incoming fp32 accumulators), pushes K/V and the updated
+             accumulators into the right neighbour's slot (t + 1) % 3 -- at the
+             last step into its home buffer -- and the dQ kernel releases slot
+             t % 3; each call ends by waiting for, reading and releasing the
+             rank's own home buffer (csrc/comm/ring_bwd_engine.hpp).
   exchange   RingExchange (two slots, the rank's own shard starts in slot 0):
              step t forwards slot t % 2 into the right neighbour's slot
              (t + 1) % 2 and releases slot t % 2 after reading it; the caller
@@ -39,8 +45,8 @@ Models:
              at any P).
 
 The flag arithmetic (slot indices, the host's per-slot use counters, credit
-targets and published credit values) follows csrc/comm/ring_engine.hpp and
-csrc/comm/ring_exchange.hpp.
+targets and published credit values) follows csrc/comm/ring_engine.hpp,
+csrc/comm/ring_bwd_engine.hpp and csrc/comm/ring_exchange.hpp.
 """
 from __future__ import annotations
 
@@ -79,7 +85,7 @@ class Model:
     def __init__(self, world: int, kind: str, calls: int = 2, seed: int = 0,
                  release_slot0: bool = True, wait_received: bool = True,
                  small_grid: bool = False, chain_guard: bool = True):
-        if kind not in ("fused", "push", "ce", "exchange"):
+        if kind not in ("fused", "push", "ce", "exchange", "backward"):
             raise ValueError(kind)
         self.P, self.kind, self.calls = world, kind, calls
         self.release_slot0 = release_slot0
@@ -96,6 +102,11 @@ class Model:
         self.nslots = n_slots
         self.ranks = [Rank([Slot() for _ in range(n_slots)], [0] * n_slots, [0] * n_slots,
                            [0] * n_slots) for _ in range(world)]
+        # backward engine: each rank's home buffer (its finished dK/dV)
+        self.home = [Slot() for _ in range(world)]
+        self.home_arrivals = [0] * world
+        self.home_credit = [0] * world
+        self.home_uses = [0] * world
         self.procs: List[Proc] = []
         self.waits: List[Optional[Wait]] = []
 
@@ -223,6 +234,62 @@ class Model:
         self.ranks[right].arrivals[sn] += 1
         R.pushed[key] = True
 
+    # ------------------------------------------------------------ backward engine
+    def _backward_call(self, r: int, c: int) -> Proc:
+        """One backward() on rank r: per step the dK/dV kernel then the dQ kernel
+        (stream order, no dependent launch), then the wait for the home buffer,
+        its copy-out and its release."""
+        P, R = self.P, self.ranks[r]
+        right, left = (r + 1) % P, (r - 1) % P
+        for t in range(P):
+            s, sn = t % 3, (t + 1) % 3
+            owner = (r - t) % P
+            credit_target, credit_value = R.uses[sn], R.uses[s] + 1
+            home_target = self.home_uses[r]
+            # dK/dV kernel: consume slot s (K, V and the incoming accumulators),
+            # push K/V and the updated accumulators into the right neighbour's
+            # slot sn -- or, at the last step, its home buffer
+            if t > 0:
+                yield lambda s=s: R.arrivals[s] >= 1
+                self._begin_read(r, s, (owner, c))
+            if t < P - 1:
+                yield lambda sn=sn, ct=credit_target: R.credit[sn] >= ct
+                self._begin_write(right, sn)
+                yield lambda: True
+                self._end_write(right, sn, (owner, c))
+                self.ranks[right].arrivals[sn] += 1
+            else:
+                yield lambda ht=home_target: self.home_credit[r] >= ht
+                h = self.home[right]
+                if h.readers:
+                    raise ProtocolViolation(f"rank {right} home: store began while it was read")
+                h.writing = True
+                yield lambda: True
+                h.writing = False
+                h.content = (owner, c)
+                self.home_arrivals[right] += 1
+            if t > 0:
+                self._end_read(r, s)
+            # dQ kernel: reads slot s again, then its last CTA releases it
+            if t > 0:
+                self._begin_read(r, s, (owner, c))
+                yield lambda: True
+                self._end_read(r, s)
+                R.arrivals[s] = 0
+                self.ranks[left].credit[s] = credit_value
+                R.uses[s] += 1
+        # the finished dK/dV of this rank arrive in its home buffer
+        yield lambda: self.home_arrivals[r] >= 1
+        h = self.home[r]
+        if h.writing or h.content != (r, c):
+            raise ProtocolViolation(f"rank {r} home: holds {h.content}, expected {(r, c)}")
+        h.readers += 1
+        yield lambda: True
+        h.readers -= 1
+        self.home_arrivals[r] = 0
+        self.home_credit[left] = self.home_uses[r] + 1
+        self.home_uses[r] += 1
+
     # ------------------------------------------------------------ RingExchange
     def _exchange_call(self, r: int, c: int) -> Proc:
         """One rotation on rank r in the sequential order: own shard into slot 0,
@@ -290,6 +357,8 @@ class Model:
         for r in range(self.P):
             if self.kind == "exchange":
                 calls = [self._exchange_call(r, c) for c in range(self.calls)]
+            elif self.kind == "backward":
+                calls = [self._backward_call(r, c) for c in range(self.calls)]
             else:
                 calls = [self._engine_call(r, c) for c in range(self.calls)]
             self._spawn(_chain(calls))

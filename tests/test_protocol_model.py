@@ -13,6 +13,11 @@ def test_engine_protocols_are_race_free(kind, world, small_grid):
     check(world, kind, calls=3, seeds=12, small_grid=small_grid)
 
 
+@pytest.mark.parametrize("world", [2, 3, 4, 5, 8])
+def test_backward_engine_protocol_is_race_free(world):
+    check(world, "backward", calls=3, seeds=15)
+
+
 @pytest.mark.parametrize("world", [2, 3, 4, 5])
 def test_exchange_protocol_is_race_free(world):
     check(world, "exchange", calls=3, seeds=20)
