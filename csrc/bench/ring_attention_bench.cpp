@@ -539,6 +539,8 @@ class Bf16Ring {
       slot = (slot + (2 << 20) - 1) / (2 << 20) * (2 << 20);
       const char* ch = std::getenv("MGFA_RING_CHUNKS");
       eng_ = std::make_unique<mgfa::RingEngine>(r, P, dev, slot, ch ? std::atoi(ch) : 0);
+      const char* tc = std::getenv("MGFA_TAG_CHECK");
+      eng_->set_tag_check(!(tc && std::string(tc) == "0"));
       eng_->connect(d.all_gather(eng_->ipc_handle()));
       eng_->set_transport_mode(a.backend == "fused"         ? mgfa::RingEngine::kFusedPush
                                : a.backend == "p2p_unfused" ? mgfa::RingEngine::kPushKernel

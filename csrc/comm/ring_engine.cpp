@@ -20,6 +20,7 @@ void register_ring_engine(py::module& m) {
       .def("set_fused", &RingEngine::set_fused)
       .def("fused", &RingEngine::fused)
       .def("set_transport_mode", &RingEngine::set_transport_mode)
+      .def("set_tag_check", &RingEngine::set_tag_check)
       .def("transport_mode", &RingEngine::transport_mode)
       .def("poison_slots", &RingEngine::poison_slots)
       .def("last_trace", &RingEngine::last_trace)

@@ -233,7 +233,7 @@ class RingEngine {
         p.consume.done_target = uint32_t(grid - 1);
         p.consume.left_credit = buf_.flag(left, comm::kCredit0 + s);
         p.consume.left_credit_value = uses_[s] + 1;
-        p.consume.tag = buf_.flag(r, comm::kTag0 + s);
+        p.consume.tag = tag_check_ ? buf_.flag(r, comm::kTag0 + s) : nullptr;
         p.consume.expected_tag = slot_tag(owner, calls_);
       }
       const bool unfused = transport && mode_ != kFusedPush;
@@ -324,6 +324,9 @@ class RingEngine {
     mode_ = m;
   }
   int transport_mode() const { return mode_; }
+  // Whether each consuming CTA verifies the slot's owner tag (one more
+  // system-scope load before its first K load; on by default).
+  void set_tag_check(bool on) { tag_check_ = on; }
   // false: the standalone push kernel (kept for callers of the two-way switch).
   void set_fused(bool on) { mode_ = on ? kFusedPush : kPushKernel; }
   bool fused() const { return mode_ == kFusedPush; }
@@ -370,6 +373,7 @@ class RingEngine {
   bool trace_ = false;
   bool pdl_ = true;
   int mode_ = kFusedPush;
+  bool tag_check_ = true;
   c10::optional<c10::cuda::CUDAStream> push_stream_;
   uint32_t calls_ = 0;
   int num_sms_ = 148;

@@ -72,6 +72,9 @@ class _Engines:
             self._by_key.pop(key)
             del eng
         eng = C().RingEngine(rank, world, device.index, slot, int(os.environ.get("MGFA_RING_CHUNKS", 0)))
+        # MGFA_TAG_CHECK=0 skips the consumers' owner-tag check (an experiment
+        # knob: one system-scope load less per CTA and step)
+        eng.set_tag_check(os.environ.get("MGFA_TAG_CHECK", "1") != "0")
         handles = [None] * world
         dist.all_gather_object(handles, eng.ipc_handle(), group=group)
         eng.connect(handles)
