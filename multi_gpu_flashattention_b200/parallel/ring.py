@@ -50,6 +50,27 @@ def _global_rank(group, r: int) -> int:
     return dist.get_global_rank(group, r) if group is not None else r
 
 
+_HOST_GROUPS: dict = {}
+
+
+def _host_group(group):
+    """Process group for the staged transport's pinned host buffers: `group`
+    itself when it is gloo, else a gloo group over the whole world, created
+    once (collectively) for the default group. A non-gloo sub-group needs an
+    explicit `cpu_group`, because creating a group is collective over every
+    rank of the job."""
+    if dist.get_backend(group) == "gloo":
+        return group
+    if group is not None:
+        raise ValueError("backend='staged' on a sub-group needs cpu_group=<gloo group over the "
+                         "same ranks>")
+    g = _HOST_GROUPS.get(None)
+    if g is None:
+        g = dist.new_group(list(range(dist.get_world_size())), backend="gloo")
+        _HOST_GROUPS[None] = g
+    return g
+
+
 # ---------------------------------------------------------------------- engine cache
 class _Engines:
     """One native RingEngine per (process group, device); grown on demand.
@@ -266,6 +287,8 @@ def ring_attention_forward(q, k, v, layout: RingLayout, causal: bool = False,
     elif backend == "nccl":
         out, lse = _fwd_nccl(q, k, v, layout, causal, scale, group, st, wait_limit_ns)
     else:
+        if cpu_group is None:
+            cpu_group = _host_group(group)
         out, lse = _fwd_staged(q, k, v, layout, causal, scale, group, st, wait_limit_ns,
                                cpu_group=cpu_group)
     if check:

@@ -33,3 +33,17 @@ def test_ring_torch_backend_world2(kind, causal):
 @pytest.mark.parametrize("kind", ["zigzag", "striped", "scheduler"])
 def test_ring_torch_backend_world4_causal_gqa(kind):
     run_ranks(_ring_case, 4, kind, True, 512, 4, 2)
+
+
+def _host_group_case(rank, world):
+    import torch.distributed as dist
+    from multi_gpu_flashattention_b200.parallel.ring import _host_group
+    # a gloo default group carries host buffers itself
+    assert _host_group(None) is None
+    sub = dist.new_group([0, 1], backend="gloo")
+    assert _host_group(sub) is sub
+
+
+def test_staged_transport_host_group_selection():
+    from dist_utils import run_ranks
+    run_ranks(_host_group_case, 2)
