@@ -23,7 +23,9 @@ Models:
              step has finished. `small_grid=True` lets dependent launches chain
              more than one step deep (grids smaller than the GPU);
              `chain_guard=False` drops the engine's rule that turns dependent
-             launch off for those grids at P >= 5, which races.
+             launch off for those grids at P >= 5, which races;
+             `cumulative=True` models arrival counters that are never reset,
+             with the host's cumulative targets (dependent launch always on).
   push, ce   RingEngine forward with the transport on a second stream (the
              standalone push kernel or the copy engine): the attention kernel
              only waits; the transfer of step t starts after the compute
@@ -84,7 +86,7 @@ Proc = Generator[Wait, None, None]
 class Model:
     def __init__(self, world: int, kind: str, calls: int = 2, seed: int = 0,
                  release_slot0: bool = True, wait_received: bool = True,
-                 small_grid: bool = False, chain_guard: bool = True):
+                 small_grid: bool = False, chain_guard: bool = True, cumulative: bool = False):
         if kind not in ("fused", "push", "ce", "exchange", "backward"):
             raise ValueError(kind)
         self.P, self.kind, self.calls = world, kind, calls
@@ -97,6 +99,13 @@ class Model:
         # grids when P >= 5 (chain_guard).
         self.small_grid = small_grid
         self.pdl = not (chain_guard and small_grid and world >= 5)
+        # fused engine with arrival counters that are never reset: the host
+        # keeps each slot's cumulative expected arrivals and the consumer waits
+        # for that total (the design that keeps dependent launch on everywhere)
+        self.cumulative = cumulative
+        if cumulative:
+            self.pdl = True
+        self.expected = [[0] * (2 if kind == "exchange" else 3) for _ in range(world)]
         self.rng = random.Random(seed)
         n_slots = 2 if kind == "exchange" else 3
         self.nslots = n_slots
@@ -148,8 +157,12 @@ class Model:
             key = (c, t)
             prev = (c, t - 1) if t > 0 else ((c - 1, P - 1) if c > 0 else None)
             if self.kind == "fused":
+                need = 1
+                if self.cumulative and t > 0:
+                    self.expected[r][s] += 1
+                    need = self.expected[r][s]
                 self._spawn(self._fused_kernel(r, c, t, s, sn, owner, credit_target,
-                                               credit_value, prev, right, left))
+                                               credit_value, prev, right, left, need))
             else:
                 self._spawn(self._unfused_compute(r, c, t, s, owner, credit_value, prev, left))
                 if t < P - 1:
@@ -161,7 +174,7 @@ class Model:
         return
 
     def _fused_kernel(self, r, c, t, s, sn, owner, credit_target, credit_value, prev, right,
-                      left) -> Proc:
+                      left, need=1) -> Proc:
         R = self.ranks[r]
         key = (c, t)
         if prev is not None:
@@ -174,7 +187,7 @@ class Model:
         R.started[key] = True
         reading = False
         if t > 0:
-            yield lambda: R.arrivals[s] >= 1
+            yield lambda: R.arrivals[s] >= need
             self._begin_read(r, s, (owner, c))
             reading = True
         if t < self.P - 1:
@@ -190,8 +203,10 @@ class Model:
             yield lambda: R.finished.get(prev, False)
         if reading:
             self._end_read(r, s)
-            # last CTA: rearm the counter, then hand the slot back
-            R.arrivals[s] = 0
+            # last CTA: rearm the counter (unless counts accumulate), then hand
+            # the slot back
+            if not self.cumulative:
+                R.arrivals[s] = 0
             self.ranks[left].credit[s] = credit_value
         R.finished[key] = True
 
@@ -381,8 +396,9 @@ def _chain(gens: List[Proc]) -> Proc:
 
 
 def check(world: int, kind: str, calls: int = 2, seeds: int = 50, release_slot0: bool = True,
-          wait_received: bool = True, small_grid: bool = False, chain_guard: bool = True) -> None:
+          wait_received: bool = True, small_grid: bool = False, chain_guard: bool = True,
+          cumulative: bool = False) -> None:
     """Runs `seeds` random interleavings; raises on the first violation."""
     for seed in range(seeds):
         Model(world, kind, calls, seed, release_slot0, wait_received, small_grid,
-              chain_guard).run()
+              chain_guard, cumulative).run()

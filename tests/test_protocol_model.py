@@ -47,3 +47,12 @@ def test_two_ranks_are_safe_without_the_guards():
     two-rank runs could not have shown them."""
     check(2, "exchange", calls=3, seeds=50, release_slot0=False)
     check(4, "fused", calls=3, seeds=50, small_grid=True, chain_guard=False)
+
+
+@pytest.mark.parametrize("world", [5, 8])
+def test_cumulative_arrival_counts_make_deep_chains_safe(world):
+    """The full fix of the chain hazard, checked before it is built: arrival
+    counters that are never reset, with cumulative targets, stay race-free with
+    dependent launch on for every grid size."""
+    check(world, "fused", calls=3, seeds=30, small_grid=True, chain_guard=False,
+          cumulative=True)
