@@ -13,7 +13,6 @@ import json
 import os
 
 import torch
-import torch.distributed as dist
 
 from ..parallel.layouts import RingLayout
 from ..parallel.ring import ENGINES, ring_attention_forward

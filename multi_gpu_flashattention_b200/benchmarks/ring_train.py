@@ -14,7 +14,6 @@ from __future__ import annotations
 
 import argparse
 import json
-import math
 
 import torch
 import torch.distributed as dist

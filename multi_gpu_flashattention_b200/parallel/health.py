@@ -12,7 +12,6 @@ themselves also bound every wait (see KernelStatusError)."""
 from __future__ import annotations
 
 import time
-from typing import Optional
 
 import torch.distributed as dist
 
