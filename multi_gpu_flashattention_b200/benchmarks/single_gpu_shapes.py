@@ -4,7 +4,7 @@ tests/benchmark_single_gpu_shapes.py, on this framework's sm_100a kernels).
     python -m multi_gpu_flashattention_b200.benchmarks.single_gpu_shapes \
         [--shapes 256x256 1024x1024 ...] [--batch-size 2] [--num-heads 8]
         [--head-dim 64|128] [--dtype float16|bfloat16] [--warmup 5] [--repeats 20]
-        [--causal|--no-causal] [--backward] [--csv-out results/single_gpu_shapes.csv]
+        [--causal|--no-causal] [--backward] [--graph] [--csv-out results/single_gpu_shapes.csv]
 
 Defaults, table and CSV columns are the reference's (fp16, head_dim 64, batch 2,
 8 heads, causal; tests/benchmark_single_gpu_shapes.py:188-210), with a TFLOP/s
@@ -56,11 +56,24 @@ def bench(sq, sk, a):
     out, lse = flash_attn_fwd(q, k, v, causal=a.causal)
     do = torch.randn_like(out)
 
-    def run():
+    if a.graph:
+        # replay CUDA graphs of the call (inputs copied into static buffers)
+        from ..ops.graphs import GraphedAttention
+        g = GraphedAttention(q, k, v, causal=a.causal, backward=a.backward)
         if a.backward:
-            flash_attn_bwd(do, q, k, v, out, lse, causal=a.causal)
-        else:
-            flash_attn_fwd(q, k, v, causal=a.causal)
+            g.forward(q, k, v)
+
+        def run():
+            if a.backward:
+                g.backward(do)
+            else:
+                g.forward(q, k, v)
+    else:
+        def run():
+            if a.backward:
+                flash_attn_bwd(do, q, k, v, out, lse, causal=a.causal)
+            else:
+                flash_attn_fwd(q, k, v, causal=a.causal)
     for _ in range(a.warmup):
         run()
     torch.cuda.synchronize(dev)
@@ -106,6 +119,8 @@ def main():
     ap.add_argument("--repeats", type=int, default=20)
     ap.add_argument("--device", type=int, default=0)
     ap.add_argument("--backward", action="store_true")
+    ap.add_argument("--graph", action="store_true",
+                    help="replay a CUDA graph of the call (fixed shapes; no host path per call)")
     ap.add_argument("--causal", action=argparse.BooleanOptionalAction, default=True)
     ap.add_argument("--csv-out", default="results/single_gpu_shapes.csv")
     a = ap.parse_args()
