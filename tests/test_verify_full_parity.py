@@ -1,7 +1,7 @@
 """verify_full (csrc/bench/verify_full.cpp) against the reference checker's
 reports (ring/attention/verify_full.c, recorded in tests/golden/
 verify_full_golden.txt) on deterministic dump sets: the same PASS/FAIL lines,
-element and NaN/Inf counts, overall verdict and exit code, and the same error
+element and NaN/Inf counts, overall result and exit code, and the same error
 figures and worst index (to the last printed digit where the reference values
 are exact, within one fp32 ulp of the ~6.6e4 outputs otherwise)."""
 import os
