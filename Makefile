@@ -5,6 +5,7 @@
 # NCCL and this tree's sm_100a kernels (launch with `torchrun --no-python`):
 #   build/bin/ring_loop_bench      pure ring exchange (p2p | ce | nccl | staged)
 #   build/bin/ring_attention_bench ring attention (fused | nccl | staged; fp32 | bf16)
+#   build/bin/check_peer           peer-access matrix (the reference's check_peer)
 CXX      ?= g++
 NVCC     ?= nvcc
 PY       ?= python
@@ -60,7 +61,10 @@ $(BIN)/ring_attention_bench: $(OBJ)/bench/ring_attention_bench.o $(COMM_OBJ) $(S
     $(OBJ)/ops/attn_api.o | $(BIN)
 	$(CXX) -o $@ $^ $(GPU_LIBS)
 
-cuda-tools: $(BIN)/ring_loop_bench $(BIN)/ring_attention_bench
+$(BIN)/check_peer: csrc/bench/check_peer.cpp | $(BIN)
+	$(CXX) -O2 -std=c++17 -isystem $(CUDA_HOME)/include -o $@ $< -L$(CUDA_HOME)/lib64 -Wl,-rpath,$(CUDA_HOME)/lib64 -lcudart
+
+cuda-tools: $(BIN)/ring_loop_bench $(BIN)/ring_attention_bench $(BIN)/check_peer
 
 clean:
 	rm -rf $(BIN) $(OBJ)

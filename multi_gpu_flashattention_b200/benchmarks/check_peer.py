@@ -50,11 +50,10 @@ def main():
     a = ap.parse_args()
     m = peer_matrix()
     n = len(m)
-    print(f"{n} CUDA device(s)")
     for i in range(n):
         for j in range(n):
-            if i != j:
-                print(f"GPU {i} -> GPU {j} : canAccessPeer = {int(m[i][j])}")
+            if i != j:  # the reference's line format
+                print(f"GPU {i} -> GPU {j}: {'YES' if m[i][j] else 'NO'}")
     nv = nvlink_report()
     if nv:
         for g in nv:

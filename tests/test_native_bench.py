@@ -3,6 +3,7 @@ launched by torchrun --no-python: argument handling on the host, and on 2+ GPUs
 the RESULT lines, the reference checker on fp32 dumps and the bf16 dumps
 against the fp32 oracle."""
 import os
+import re
 import socket
 import subprocess
 import sys
@@ -165,3 +166,20 @@ def test_fp32_randn_seq4096_two_ranks(tmp_path, extra):
     assert p.returncode == 0 and "ALL PASS" in p.stdout, p.stdout[-2000:]
     errs = [float(x) for x in re.findall(r"Max absolute error:\s*([0-9.eE+-]+)", p.stdout)]
     assert len(errs) == 2 and max(errs) <= 1e-4, errs
+
+
+def test_check_peer_runs():
+    p = subprocess.run([_exe("check_peer")], capture_output=True, text=True, timeout=60)
+    assert p.returncode == 0
+    for line in p.stdout.splitlines():
+        assert re.fullmatch(r"GPU \d+ -> GPU \d+: (YES|NO)", line), line
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+def test_check_peer_lists_every_pair():
+    n = torch.cuda.device_count()
+    p = subprocess.run([_exe("check_peer")], capture_output=True, text=True, timeout=60)
+    lines = p.stdout.splitlines()
+    assert len(lines) == n * (n - 1)
+    assert lines[0] == "GPU 0 -> GPU 1: YES"
