@@ -14,6 +14,10 @@ Backends
 fused   (default on CUDA) one sm_100a kernel per step that computes, merges
         in-kernel and pushes the current shard into the right neighbour's
         receive slot with peer stores (native RingEngine).
+p2p_unfused, ce_unfused
+        ablations of `fused`: the same engine, slots and flags, with the shard
+        moved on a second stream by the standalone push kernel or by the copy
+        engine (forward only; their backward uses the nccl path).
 nccl    baseline: NCCL send/recv on a side stream, overlapped with the same
         attention kernel (merge in-kernel).
 staged  baseline: device -> pinned host -> gloo send/recv -> device, the
