@@ -86,7 +86,8 @@ Proc = Generator[Wait, None, None]
 class Model:
     def __init__(self, world: int, kind: str, calls: int = 2, seed: int = 0,
                  release_slot0: bool = True, wait_received: bool = True,
-                 small_grid: bool = False, chain_guard: bool = True, cumulative: bool = False):
+                 small_grid: bool = False, chain_guard: bool = True, cumulative: bool = False,
+                 mutation: Optional[str] = None):
         if kind not in ("fused", "push", "ce", "exchange", "backward"):
             raise ValueError(kind)
         self.P, self.kind, self.calls = world, kind, calls
@@ -106,6 +107,10 @@ class Model:
         if cumulative:
             self.pdl = True
         self.expected = [[0] * (2 if kind == "exchange" else 3) for _ in range(world)]
+        # deliberately broken variants, to show the checker catches them:
+        # "credit"  credit targets one lower (a push may overwrite one use early)
+        # "release" the fused kernel hands its slot back before its reads end
+        self.mutation = mutation
         self.rng = random.Random(seed)
         n_slots = 2 if kind == "exchange" else 3
         self.nslots = n_slots
@@ -152,7 +157,7 @@ class Model:
             s, sn = t % 3, (t + 1) % 3
             owner = (r - t) % P
             # parameters fixed at enqueue time (host counters)
-            credit_target = R.uses[sn]
+            credit_target = R.uses[sn] - (1 if self.mutation == "credit" else 0)
             credit_value = R.uses[s] + 1
             key = (c, t)
             prev = (c, t - 1) if t > 0 else ((c - 1, P - 1) if c > 0 else None)
@@ -190,6 +195,8 @@ class Model:
             yield lambda: R.arrivals[s] >= need
             self._begin_read(r, s, (owner, c))
             reading = True
+            if self.mutation == "release":
+                self.ranks[left].credit[s] = credit_value
         if t < self.P - 1:
             yield lambda: R.credit[sn] >= credit_target
             self._begin_write(right, sn)
@@ -397,8 +404,8 @@ def _chain(gens: List[Proc]) -> Proc:
 
 def check(world: int, kind: str, calls: int = 2, seeds: int = 50, release_slot0: bool = True,
           wait_received: bool = True, small_grid: bool = False, chain_guard: bool = True,
-          cumulative: bool = False) -> None:
+          cumulative: bool = False, mutation: Optional[str] = None) -> None:
     """Runs `seeds` random interleavings; raises on the first violation."""
     for seed in range(seeds):
         Model(world, kind, calls, seed, release_slot0, wait_received, small_grid,
-              chain_guard, cumulative).run()
+              chain_guard, cumulative, mutation).run()

@@ -56,3 +56,12 @@ def test_cumulative_arrival_counts_make_deep_chains_safe(world):
     dependent launch on for every grid size."""
     check(world, "fused", calls=3, seeds=30, small_grid=True, chain_guard=False,
           cumulative=True)
+
+
+@pytest.mark.parametrize("mutation", ["credit", "release"])
+@pytest.mark.parametrize("world", [2, 4])
+def test_checker_catches_broken_variants(mutation, world):
+    """Sensitivity of the model: a credit target one too low, or a slot handed
+    back before its reads end, is caught."""
+    with pytest.raises(ProtocolViolation, match="store began while"):
+        check(world, "fused", calls=3, seeds=200, mutation=mutation)
