@@ -71,3 +71,11 @@ class RingHealth:
     def step(self, step: int, timeout_s: float = 10.0) -> None:
         self.beat(step)
         self.check(step, timeout_s)
+
+    def gate(self, timeout_s: float = 10.0) -> int:
+        """Before a ring call: announce the next call and wait (bounded) until
+        every peer announced it too. Raises PeerLostError -- before anything is
+        launched -- when a peer left or stays silent. Returns the call index."""
+        call = self._last + 1
+        self.step(call, timeout_s)
+        return call

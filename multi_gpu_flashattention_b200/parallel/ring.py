@@ -265,18 +265,22 @@ def ring_attention_forward(q, k, v, layout: RingLayout, causal: bool = False,
                            softmax_scale: Optional[float] = None, group=None,
                            backend: Optional[str] = None, status: Optional[torch.Tensor] = None,
                            wait_limit_ns: int = DEFAULT_WAIT_LIMIT_NS, check: bool = False,
-                           cpu_group=None):
+                           cpu_group=None, health=None):
     """Forward ring attention on local shards; returns (out, lse).
 
     out has q's dtype ([B, L, Hq, D]); lse is fp32 [B, Hq, L] (natural log).
     With check=True the kernels' status word is read back (a device sync) and a
-    KernelStatusError raised on any timeout."""
+    KernelStatusError raised on any timeout. With a `health` (RingHealth) every
+    rank first passes its gate, so a peer that left or went silent raises
+    PeerLostError here instead of leaving launched kernels waiting."""
     scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(q.shape[-1])
     if backend is None:
         backend = "fused" if q.is_cuda else "torch"
     if backend not in BACKENDS:
         raise ValueError(f"backend must be one of {BACKENDS}")
     rank, world = _world(group)
+    if health is not None and world > 1:
+        health.gate()
     if backend == "torch":
         return _fwd_torch(q, k, v, layout, causal, scale, group)
     st = status if status is not None else torch.zeros(1, dtype=torch.int32, device=q.device)

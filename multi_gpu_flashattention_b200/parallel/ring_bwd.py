@@ -44,9 +44,13 @@ def _p2p(group, sends, recvs, right, left):
 
 def ring_attention_backward(dout, q, k, v, out, lse, layout: RingLayout, causal: bool = False,
                             softmax_scale: Optional[float] = None, group=None,
-                            backend: Optional[str] = None):
+                            backend: Optional[str] = None, health=None):
+    """Gradients (dq, dk, dv) of the ring forward for this rank's shard. With a
+    `health` (RingHealth) every rank first passes its gate, as in the forward."""
     scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(q.shape[-1])
     rank, world = _world(group)
+    if health is not None and world > 1:
+        health.gate()
     if backend == "torch" or not q.is_cuda:
         return _bwd_torch(dout, q, k, v, layout, causal, scale, group)
     from .ring import _meta

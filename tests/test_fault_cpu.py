@@ -59,3 +59,27 @@ def _silent_rank(rank, world):
 
 def test_health_times_out_on_silent_rank():
     run_ranks(_silent_rank, 2, final_barrier=False)
+
+
+def _gated_ring(rank, world):
+    """A rank leaves after the first call; the other learns it at its next
+    call's gate, before any transfer is started."""
+    from multi_gpu_flashattention_b200 import ring_attention
+    from multi_gpu_flashattention_b200.parallel.health import PeerLostError, RingHealth
+    from multi_gpu_flashattention_b200.parallel.layouts import RingLayout
+    lay = RingLayout("zigzag", 256, world, mask="causal")
+    h = RingHealth()
+    q = torch.randn(1, lay.max_local_len, 2, 16, requires_grad=True)
+    out = ring_attention(q, q, q, causal=True, layout=lay, backend="torch", health=h)
+    out.sum().backward()  # forward and backward each pass the gate (calls 0 and 1)
+    if rank == 1:
+        h.leave()
+        return
+    t0 = time.monotonic()
+    with pytest.raises(PeerLostError, match="left"):
+        ring_attention(q, q, q, causal=True, layout=lay, backend="torch", health=h)
+    assert time.monotonic() - t0 < 10
+
+
+def test_health_gate_stops_the_next_call():
+    run_ranks(_gated_ring, 2, final_barrier=False)
