@@ -70,15 +70,22 @@ def _gated_ring(rank, world):
     lay = RingLayout("zigzag", 256, world, mask="causal")
     h = RingHealth()
     q = torch.randn(1, lay.max_local_len, 2, 16, requires_grad=True)
+    import torch.distributed as dist
+    store = dist.distributed_c10d._get_default_store()
     out = ring_attention(q, q, q, causal=True, layout=lay, backend="torch", health=h)
     out.sum().backward()  # forward and backward each pass the gate (calls 0 and 1)
     if rank == 1:
         h.leave()
-        return
-    t0 = time.monotonic()
-    with pytest.raises(PeerLostError, match="left"):
-        ring_attention(q, q, q, causal=True, layout=lay, backend="torch", health=h)
-    assert time.monotonic() - t0 < 10
+        # the process itself stays until the peer has seen the departure, so
+        # no live transport connection of the job is torn down under it
+        store.wait(["test/seen"])
+    else:
+        t0 = time.monotonic()
+        with pytest.raises(PeerLostError, match="left"):
+            ring_attention(q, q, q, causal=True, layout=lay, backend="torch", health=h)
+        assert time.monotonic() - t0 < 10
+        store.set("test/seen", "1")
+    dist.destroy_process_group()
 
 
 def test_health_gate_stops_the_next_call():
