@@ -27,16 +27,29 @@ def test_rank_exception_ends_peers_with_error():
     assert time.monotonic() - t0 < 90
 
 
+def _finish(rank, store, key):
+    """Rank 0 marks that it has seen the failure; every rank's process stays
+    until then and tears its process group down locally."""
+    import torch.distributed as dist
+    if rank == 0:
+        store.set(key, "1")
+    else:
+        store.wait([key])
+    dist.destroy_process_group()
+
+
 def _leaving_rank(rank, world):
+    import torch.distributed as dist
     from multi_gpu_flashattention_b200.parallel.health import PeerLostError, RingHealth
     h = RingHealth()
     h.step(0, timeout_s=20)          # both ranks take call 0
     if rank == 1:
         h.leave()                    # leaves between calls, nothing in flight
-        return
-    h.beat(1)
-    with pytest.raises(PeerLostError, match="rank 1 left"):
-        h.check(1, timeout_s=20)
+    else:
+        h.beat(1)
+        with pytest.raises(PeerLostError, match="rank 1 left"):
+            h.check(1, timeout_s=20)
+    _finish(rank, dist.distributed_c10d._get_default_store(), "test/leave_seen")
 
 
 def test_health_detects_departed_rank():
@@ -44,17 +57,17 @@ def test_health_detects_departed_rank():
 
 
 def _silent_rank(rank, world):
+    import torch.distributed as dist
     from multi_gpu_flashattention_b200.parallel.health import PeerLostError, RingHealth
     h = RingHealth()
     h.step(0, timeout_s=20)
-    if rank == 1:
-        time.sleep(4)                # never announces call 1
-        return
-    h.beat(1)
-    t0 = time.monotonic()
-    with pytest.raises(PeerLostError, match="did not reach call 1"):
-        h.check(1, timeout_s=1.0)
-    assert time.monotonic() - t0 < 3
+    if rank == 0:                    # rank 1 never announces call 1
+        h.beat(1)
+        t0 = time.monotonic()
+        with pytest.raises(PeerLostError, match="did not reach call 1"):
+            h.check(1, timeout_s=1.0)
+        assert time.monotonic() - t0 < 3
+    _finish(rank, dist.distributed_c10d._get_default_store(), "test/silence_seen")
 
 
 def test_health_times_out_on_silent_rank():
@@ -76,16 +89,12 @@ def _gated_ring(rank, world):
     out.sum().backward()  # forward and backward each pass the gate (calls 0 and 1)
     if rank == 1:
         h.leave()
-        # the process itself stays until the peer has seen the departure, so
-        # no live transport connection of the job is torn down under it
-        store.wait(["test/seen"])
     else:
         t0 = time.monotonic()
         with pytest.raises(PeerLostError, match="left"):
             ring_attention(q, q, q, causal=True, layout=lay, backend="torch", health=h)
         assert time.monotonic() - t0 < 10
-        store.set("test/seen", "1")
-    dist.destroy_process_group()
+    _finish(rank, store, "test/gate_seen")
 
 
 def test_health_gate_stops_the_next_call():
