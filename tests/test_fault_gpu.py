@@ -68,16 +68,21 @@ def _leave_between_calls(rank, world):
     dev = torch.device("cuda", rank)
     lay = RingLayout("contiguous", 1024, world, mask="full")
     q = (torch.randn(1, 512, 1, 128, device=dev) * 0.5).bfloat16()
+    import torch.distributed as dist
+    store = dist.distributed_c10d._get_default_store()
     h = RingHealth()
     h.step(0)
     ring_attention_forward(q, q, q, lay, backend="fused", check=True)
     torch.cuda.synchronize()  # nothing of ours in flight past this point
     if rank == 1:
         h.leave()
-        return
-    h.beat(1)
-    with pytest.raises(PeerLostError):
-        h.check(1, timeout_s=20)  # rank 0 learns it on the host and launches nothing
+        store.wait(["test/leave_seen"])  # the process stays until rank 0 saw it
+    else:
+        h.beat(1)
+        with pytest.raises(PeerLostError):
+            h.check(1, timeout_s=20)  # rank 0 learns it on the host and launches nothing
+        store.set("test/leave_seen", "1")
+    dist.destroy_process_group()
 
 
 @pytest.mark.multigpu
