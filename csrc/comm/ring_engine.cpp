@@ -13,6 +13,7 @@ void register_ring_engine(py::module& m) {
       .def("connect", &RingEngine::connect)
       .def("slot_bytes", &RingEngine::slot_bytes)
       .def("uses", &RingEngine::uses)
+      .def_static("plan", &RingEngine::plan, py::arg("world"), py::arg("rank"), py::arg("calls"))
       .def("reset", &RingEngine::reset)
       .def("set_drop_signal_step", &RingEngine::set_drop_signal_step)
       .def("set_trace", &RingEngine::set_trace)

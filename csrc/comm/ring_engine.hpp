@@ -48,6 +48,32 @@ cudaError_t ring_signal_launch(const RingPush& push, const RingConsume& consume,
 cudaError_t ring_wait_launch(const RingPush& push, const RingConsume& consume, uint32_t* status,
                              uint64_t limit_ns, cudaStream_t stream);
 
+// Host-side flag arithmetic of the forward ring: the per-slot use counters and
+// the call counter every rank advances identically, and the values a step's
+// kernels get from them. RingEngine::run() takes its flag values from here, and
+// RingEngine::plan() replays the same arithmetic without a GPU.
+struct RingCounters {
+  static constexpr int kSlots = 3;
+  uint32_t uses[kSlots] = {0, 0, 0};  // finished uses of each receive slot
+  uint32_t calls = 0;                 // transport calls so far
+
+  struct Step {
+    int slot, next_slot;       // read at step t (t > 0) / pushed into at step t
+    uint32_t credit_target;    // the push waits until the right neighbour released
+                               // next_slot this many times
+    uint32_t credit_value;     // what this step publishes when it releases slot
+    uint32_t tag;              // (owner + 1) | (call << 8) of the shard in flight
+  };
+  Step step(int t, int owner) const {
+    const int s = t % kSlots, sn = (t + 1) % kSlots;
+    return {s, sn, uses[sn], uses[s] + 1, uint32_t(owner + 1) | (calls << 8)};
+  }
+  void finish_step(int t) {
+    if (t > 0) uses[t % kSlots] += 1;
+  }
+  void finish_call() { calls += 1; }
+};
+
 class RingEngine {
  public:
   RingEngine(int rank, int world, int device, int64_t slot_bytes, int n_chunks)
@@ -65,7 +91,27 @@ class RingEngine {
 
   int64_t slot_bytes() const { return int64_t(slot_bytes_); }
   std::vector<int64_t> uses() const {
-    return {int64_t(uses_[0]), int64_t(uses_[1]), int64_t(uses_[2])};
+    return {int64_t(ctr_.uses[0]), int64_t(ctr_.uses[1]), int64_t(ctr_.uses[2])};
+  }
+
+  // The flag values of `calls` consecutive transport calls on `rank` of a
+  // `world`-rank ring, one row per step: {call, t, slot, next_slot,
+  // credit_target, credit_value, tag}. Computed by the same RingCounters that
+  // run() uses, without a GPU (checked against the protocol model).
+  static std::vector<std::vector<int64_t>> plan(int world, int rank, int calls) {
+    RingCounters c;
+    std::vector<std::vector<int64_t>> rows;
+    for (int k = 0; k < calls; ++k) {
+      for (int t = 0; t < world; ++t) {
+        const int owner = ((rank - t) % world + world) % world;
+        const RingCounters::Step f = c.step(t, owner);
+        rows.push_back({k, t, f.slot, f.next_slot, int64_t(f.credit_target),
+                        int64_t(f.credit_value), int64_t(f.tag)});
+        c.finish_step(t);
+      }
+      c.finish_call();
+    }
+    return rows;
   }
 
   // q [B,Sq,Hq,D]; k, v [B,L,Hkv,D] contiguous local shards, bf16 or fp16, D = 64 or
@@ -157,7 +203,8 @@ class RingEngine {
 
     for (int t = 0; t < P; ++t) {
       const int owner = ((r - t) % P + P) % P;
-      const int s = t % kSlots;
+      const RingCounters::Step f = ctr_.step(t, owner);
+      const int s = f.slot;
       const bool own = t == 0 || !transport;
       const uint8_t* cur_k = own ? static_cast<const uint8_t*>(k.data_ptr()) : slot_k(r, s);
       const uint8_t* cur_v = own ? static_cast<const uint8_t*>(v.data_ptr()) : slot_v(r, s);
@@ -204,7 +251,7 @@ class RingEngine {
       RingPush push_x;     // the standalone push kernel's (unfused transport)
       RingConsume wait_x;  // its wait for the slot it forwards
       if (transport && t < P - 1) {
-        const int sn = (t + 1) % kSlots;
+        const int sn = f.next_slot;
         p.push.enabled = 1;
         p.push.src_k = cur_k;
         p.push.src_v = cur_v;
@@ -215,7 +262,7 @@ class RingEngine {
         p.push.bytes = shard_bytes;
         p.push.peer_arrivals = buf_.flag(right, comm::kArrivals0 + sn);
         p.push.credit = buf_.flag(r, comm::kCredit0 + sn);
-        p.push.credit_target = uses_[sn];
+        p.push.credit_target = f.credit_target;
         // The first chunks CTAs of the grid push (two waves by default, so the
         // shard reaches the neighbour early in the step). Every rank launches the
         // same grid (shards are padded to one length), so the receiver's arrival
@@ -223,7 +270,7 @@ class RingEngine {
         p.push.n_chunks = push_chunks(grid);
         p.push.drop_signal = (drop_signal_step_ == t) ? 1 : 0;
         p.push.peer_tag = buf_.flag(right, comm::kTag0 + sn);
-        p.push.tag = slot_tag(owner, calls_);
+        p.push.tag = f.tag;
       }
       if (transport && t > 0) {
         p.consume.enabled = 1;
@@ -232,9 +279,9 @@ class RingEngine {
         p.consume.done_counter = buf_.flag(r, comm::kDone0 + s);
         p.consume.done_target = uint32_t(grid - 1);
         p.consume.left_credit = buf_.flag(left, comm::kCredit0 + s);
-        p.consume.left_credit_value = uses_[s] + 1;
+        p.consume.left_credit_value = f.credit_value;
         p.consume.tag = tag_check_ ? buf_.flag(r, comm::kTag0 + s) : nullptr;
-        p.consume.expected_tag = slot_tag(owner, calls_);
+        p.consume.expected_tag = f.tag;
       }
       const bool unfused = transport && mode_ != kFusedPush;
       // chunks (= arrival signals) of the unfused transports
@@ -302,17 +349,15 @@ class RingEngine {
         rel.enabled = 1;
         rel.arrivals = buf_.flag(r, comm::kArrivals0 + s);
         rel.left_credit = buf_.flag(left, comm::kCredit0 + s);
-        rel.left_credit_value = uses_[s] + 1;
+        rel.left_credit_value = f.credit_value;
         C10_CUDA_CHECK(ring_signal_launch(RingPush(), rel, stream));
       }
       nvtxRangePop();
-      if (transport && t > 0) uses_[s] += 1;
+      if (transport) ctr_.finish_step(t);
     }
-    if (transport) calls_ += 1;
+    if (transport) ctr_.finish_call();
     return {o, lse};
   }
-
-  static uint32_t slot_tag(int owner, uint32_t call) { return uint32_t(owner + 1) | (call << 8); }
 
  public:
   // Transport of forward(): the attention kernel's push warps (fused, the
@@ -359,23 +404,21 @@ class RingEngine {
   // Zero local flags and use counts (collective: every rank, then a barrier).
   void reset() {
     buf_.reset_flags(at::cuda::getCurrentCUDAStream());
-    for (auto& u : uses_) u = 0;
-    calls_ = 0;
+    ctr_ = RingCounters();
   }
 
  private:
   comm::SymmetricBuffer buf_;
   size_t slot_bytes_;
   int n_chunks_;
-  static constexpr int kSlots = 3;
-  uint32_t uses_[kSlots] = {0, 0, 0};
+  static constexpr int kSlots = RingCounters::kSlots;
+  RingCounters ctr_;
   int drop_signal_step_ = -1;
   bool trace_ = false;
   bool pdl_ = true;
   int mode_ = kFusedPush;
   bool tag_check_ = true;
   c10::optional<c10::cuda::CUDAStream> push_stream_;
-  uint32_t calls_ = 0;
   int num_sms_ = 148;
   torch::Tensor last_trace_;
 };

@@ -397,6 +397,23 @@ class Model:
         return events
 
 
+def engine_plan(world: int, rank: int, calls: int) -> List[List[int]]:
+    """The forward engine's flag values as this model derives them (the
+    arithmetic of `_engine_call`): one row per step of `calls` consecutive
+    calls, [call, t, slot, next_slot, credit_target, credit_value, tag]. The
+    native engine's RingEngine.plan() must produce the same rows."""
+    uses = [0, 0, 0]
+    rows = []
+    for c in range(calls):
+        for t in range(world):
+            s, sn = t % 3, (t + 1) % 3
+            owner = (rank - t) % world
+            rows.append([c, t, s, sn, uses[sn], uses[s] + 1, (owner + 1) | (c << 8)])
+            if t > 0:
+                uses[s] += 1
+    return rows
+
+
 def _chain(gens: List[Proc]) -> Proc:
     for g in gens:
         yield from g

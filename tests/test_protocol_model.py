@@ -65,3 +65,16 @@ def test_checker_catches_broken_variants(mutation, world):
     back before its reads end, is caught."""
     with pytest.raises(ProtocolViolation, match="store began while"):
         check(world, "fused", calls=3, seeds=200, mutation=mutation)
+
+
+@pytest.mark.parametrize("world,rank", [(2, 0), (3, 2), (5, 1), (8, 7)])
+def test_native_engine_flag_arithmetic_matches_the_model(world, rank):
+    """RingEngine.plan() replays the native engine's host counters (the code its
+    run() takes every flag value from); the rows equal the model's."""
+    from multi_gpu_flashattention_b200.utils.protocol_model import engine_plan
+    try:
+        from multi_gpu_flashattention_b200._ext import C
+        eng = C().RingEngine
+    except Exception as e:  # pragma: no cover - extension not built
+        pytest.skip(f"extension not built: {e}")
+    assert [list(r) for r in eng.plan(world, rank, 4)] == engine_plan(world, rank, 4)
