@@ -11,6 +11,8 @@ void register_ring_bwd_engine(py::module& m) {
            py::arg("device"), py::arg("kv_bytes"), py::arg("n_chunks") = 0)
       .def("ipc_handle", [](const RingBwdEngine& e) { return py::bytes(e.ipc_handle()); })
       .def("connect", &RingBwdEngine::connect)
+      .def_static("plan", &RingBwdEngine::plan, py::arg("world"), py::arg("rank"),
+                  py::arg("calls"))
       .def("kv_bytes", &RingBwdEngine::kv_bytes)
       .def("reset", &RingBwdEngine::reset)
       .def("backward", &RingBwdEngine::backward, py::arg("dout"), py::arg("q"), py::arg("k"),

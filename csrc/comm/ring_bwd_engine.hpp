@@ -24,6 +24,7 @@
 #include <memory>
 
 #include "../kernels/flash_bwd_sm100.cuh"
+#include "ring_counters.hpp"
 #include "symmetric.hpp"
 
 namespace mgfa {
@@ -50,11 +51,32 @@ class RingBwdEngine {
   void connect(const std::vector<std::string>& handles) { buf_.open_peers(handles); }
   int64_t kv_bytes() const { return int64_t(kv_bytes_); }
 
+  // The flag values of `calls` consecutive backward calls on `rank` of a
+  // `world`-rank ring, one row per step: {call, t, slot, next_slot,
+  // credit_target, credit_value, tag, home_credit_target}. Computed by the same
+  // counters backward() uses, without a GPU (checked against the protocol model).
+  static std::vector<std::vector<int64_t>> plan(int world, int rank, int calls) {
+    RingCounters c;
+    uint32_t home = 0;
+    std::vector<std::vector<int64_t>> rows;
+    for (int k = 0; k < calls; ++k) {
+      for (int t = 0; t < world; ++t) {
+        const int owner = ((rank - t) % world + world) % world;
+        const RingCounters::Step f = c.step(t, owner);
+        rows.push_back({k, t, f.slot, f.next_slot, int64_t(f.credit_target),
+                        int64_t(f.credit_value), int64_t(f.tag | kBwdTag), int64_t(home)});
+        c.finish_step(t);
+      }
+      home += 1;
+      c.finish_call();
+    }
+    return rows;
+  }
+
   void reset() {
     buf_.reset_flags(at::cuda::getCurrentCUDAStream());
-    for (auto& u : uses_) u = 0;
+    ctr_ = RingCounters();
     home_uses_ = 0;
-    calls_ = 0;
   }
 
   // Returns (dq fp32 [B,L,Hq,128], dk fp32 [B,L,Hkv,128], dv fp32) for this rank's
@@ -112,7 +134,9 @@ class RingBwdEngine {
 
     for (int t = 0; t < P; ++t) {
       const int owner = ((r - t) % P + P) % P;
-      const int s = t % kSlots, sn = (t + 1) % kSlots;
+      const RingCounters::Step f = ctr_.step(t, owner);
+      const uint32_t step_tag = f.tag | kBwdTag;
+      const int s = f.slot, sn = f.next_slot;
       const bool own = t == 0;
       const uint8_t* cur_k = own ? static_cast<const uint8_t*>(k.data_ptr()) : slot(r, s);
       const uint8_t* cur_v = own ? static_cast<const uint8_t*>(v.data_ptr()) : slot(r, s) + kv_bytes_;
@@ -154,7 +178,7 @@ class RingBwdEngine {
         pk.consume.arrivals = buf_.flag(r, comm::kArrivals0 + s);
         pk.consume.arrivals_target = slot_target;
         pk.consume.tag = buf_.flag(r, comm::kTag0 + s);
-        pk.consume.expected_tag = tag(owner);
+        pk.consume.expected_tag = step_tag;
         pk.ring.acc_in_dk = reinterpret_cast<const float*>(slot(r, s) + 2 * kv_bytes_);
         pk.ring.acc_in_dv = reinterpret_cast<const float*>(slot(r, s) + 4 * kv_bytes_);
       }
@@ -172,15 +196,15 @@ class RingBwdEngine {
         pk.push.bytes = kvb;
         pk.push.peer_arrivals = buf_.flag(right, comm::kArrivals0 + sn);
         pk.push.credit = buf_.flag(r, comm::kCredit0 + sn);
-        pk.push.credit_target = uses_[sn];
+        pk.push.credit_target = f.credit_target;
         pk.push.n_chunks = chunks;
         pk.push.peer_tag = buf_.flag(right, comm::kTag0 + sn);
-        pk.push.tag = tag(owner);
+        pk.push.tag = step_tag;
         pk.ring.acc_out_dk = reinterpret_cast<float*>(slot(right, sn) + 2 * kv_bytes_);
         pk.ring.acc_out_dv = reinterpret_cast<float*>(slot(right, sn) + 4 * kv_bytes_);
         pk.ring.acc_arrivals = buf_.flag(right, comm::kArrivals0 + sn);
         pk.ring.acc_credit = buf_.flag(r, comm::kCredit0 + sn);
-        pk.ring.acc_credit_target = uses_[sn];
+        pk.ring.acc_credit_target = f.credit_target;
       } else {  // the finished gradients of `owner` (= right) go home
         pk.ring.acc_out_dk = reinterpret_cast<float*>(home(right));
         pk.ring.acc_out_dv = reinterpret_cast<float*>(home(right) + 2 * kv_bytes_);
@@ -199,10 +223,10 @@ class RingBwdEngine {
         pq.consume.done_counter = buf_.flag(r, comm::kDone0 + s);
         pq.consume.done_target = uint32_t(dq_grid - 1);
         pq.consume.left_credit = buf_.flag(left, comm::kCredit0 + s);
-        pq.consume.left_credit_value = uses_[s] + 1;
+        pq.consume.left_credit_value = f.credit_value;
       }
       flash_bwd_dq_launch(mq, mdo, mk, mv, pq, stream);
-      if (t > 0) uses_[s] += 1;
+      ctr_.finish_step(t);
     }
 
     // ---- home: this rank's complete dK/dV arrived from the left neighbour
@@ -221,7 +245,7 @@ class RingBwdEngine {
     auto dv = hv.clone();
     C10_CUDA_CHECK(ring_signal_launch(none, hc, stream));  // hand the home buffer back
     home_uses_ += 1;
-    calls_ += 1;
+    ctr_.finish_call();
     return {dq, dk, dv};
   }
 
@@ -232,15 +256,14 @@ class RingBwdEngine {
     const uint32_t two_waves = 2u * uint32_t(num_sms_);
     return two_waves < uint32_t(grid) ? two_waves : uint32_t(grid);
   }
-  uint32_t tag(int owner) const { return uint32_t(owner + 1) | (calls_ << 8) | 0x80000000u; }
+  static constexpr uint32_t kBwdTag = 0x80000000u;  // backward tags differ from forward ones
 
   size_t kv_bytes_, slot_bytes_;
   comm::SymmetricBuffer buf_;
   int n_chunks_;
   int num_sms_ = 148;
-  uint32_t uses_[kSlots] = {0, 0, 0};
+  RingCounters ctr_;
   uint32_t home_uses_ = 0;
-  uint32_t calls_ = 0;
 };
 
 }  // namespace mgfa

@@ -37,6 +37,7 @@
 #include <nvtx3/nvToolsExt.h>
 
 #include "../kernels/flash_fwd_sm100.cuh"
+#include "ring_counters.hpp"
 #include "symmetric.hpp"
 
 namespace mgfa {
@@ -47,32 +48,6 @@ cudaError_t ring_signal_launch(const RingPush& push, const RingConsume& consume,
                                cudaStream_t stream);
 cudaError_t ring_wait_launch(const RingPush& push, const RingConsume& consume, uint32_t* status,
                              uint64_t limit_ns, cudaStream_t stream);
-
-// Host-side flag arithmetic of the forward ring: the per-slot use counters and
-// the call counter every rank advances identically, and the values a step's
-// kernels get from them. RingEngine::run() takes its flag values from here, and
-// RingEngine::plan() replays the same arithmetic without a GPU.
-struct RingCounters {
-  static constexpr int kSlots = 3;
-  uint32_t uses[kSlots] = {0, 0, 0};  // finished uses of each receive slot
-  uint32_t calls = 0;                 // transport calls so far
-
-  struct Step {
-    int slot, next_slot;       // read at step t (t > 0) / pushed into at step t
-    uint32_t credit_target;    // the push waits until the right neighbour released
-                               // next_slot this many times
-    uint32_t credit_value;     // what this step publishes when it releases slot
-    uint32_t tag;              // (owner + 1) | (call << 8) of the shard in flight
-  };
-  Step step(int t, int owner) const {
-    const int s = t % kSlots, sn = (t + 1) % kSlots;
-    return {s, sn, uses[sn], uses[s] + 1, uint32_t(owner + 1) | (calls << 8)};
-  }
-  void finish_step(int t) {
-    if (t > 0) uses[t % kSlots] += 1;
-  }
-  void finish_call() { calls += 1; }
-};
 
 class RingEngine {
  public:

@@ -414,6 +414,18 @@ def engine_plan(world: int, rank: int, calls: int) -> List[List[int]]:
     return rows
 
 
+def backward_plan(world: int, rank: int, calls: int) -> List[List[int]]:
+    """The backward engine's flag values as `_backward_call` derives them: rows
+    [call, t, slot, next_slot, credit_target, credit_value, tag,
+    home_credit_target]; RingBwdEngine.plan() must produce the same rows."""
+    rows = []
+    for r in engine_plan(world, rank, calls):
+        r = list(r)
+        r[6] |= 0x80000000  # backward tags carry the top bit
+        rows.append(r + [r[0]])  # one home use per earlier call
+    return rows
+
+
 def _chain(gens: List[Proc]) -> Proc:
     for g in gens:
         yield from g

@@ -78,3 +78,14 @@ def test_native_engine_flag_arithmetic_matches_the_model(world, rank):
     except Exception as e:  # pragma: no cover - extension not built
         pytest.skip(f"extension not built: {e}")
     assert [list(r) for r in eng.plan(world, rank, 4)] == engine_plan(world, rank, 4)
+
+
+@pytest.mark.parametrize("world,rank", [(2, 1), (4, 0), (8, 3)])
+def test_native_backward_engine_flag_arithmetic_matches_the_model(world, rank):
+    from multi_gpu_flashattention_b200.utils.protocol_model import backward_plan
+    try:
+        from multi_gpu_flashattention_b200._ext import C
+        eng = C().RingBwdEngine
+    except Exception as e:  # pragma: no cover - extension not built
+        pytest.skip(f"extension not built: {e}")
+    assert [list(r) for r in eng.plan(world, rank, 3)] == backward_plan(world, rank, 3)
