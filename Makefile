@@ -64,7 +64,11 @@ $(BIN)/ring_attention_bench: $(OBJ)/bench/ring_attention_bench.o $(COMM_OBJ) $(S
 $(BIN)/check_peer: csrc/bench/check_peer.cpp | $(BIN)
 	$(CXX) -O2 -std=c++17 -isystem $(CUDA_HOME)/include -o $@ $< -L$(CUDA_HOME)/lib64 -Wl,-rpath,$(CUDA_HOME)/lib64 -lcudart
 
-cuda-tools: $(BIN)/ring_loop_bench $(BIN)/ring_attention_bench $(BIN)/check_peer
+$(BIN)/dist_selftest: $(OBJ)/bench/dist_selftest.o $(OBJ)/bench/dist_env.o | $(BIN)
+	$(CXX) -o $@ $^ $(GPU_LIBS)
+
+cuda-tools: $(BIN)/ring_loop_bench $(BIN)/ring_attention_bench $(BIN)/check_peer \
+    $(BIN)/dist_selftest
 
 clean:
 	rm -rf $(BIN) $(OBJ)

@@ -32,20 +32,25 @@ void nccl_check(ncclResult_t r, const char* what) {
     throw std::runtime_error(std::string(what) + ": " + ncclGetErrorString(r));
 }
 
-Dist Dist::from_env(int timeout_s) {
+Dist Dist::from_env(int timeout_s, bool need_gpu) {
   Dist d;
   d.world_ = env_int("WORLD_SIZE", 1);
   d.rank_ = env_int("RANK", 0);
   if (d.world_ < 1 || d.rank_ < 0 || d.rank_ >= d.world_)
     throw std::runtime_error("bad RANK / WORLD_SIZE");
-  int count = 0;
-  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0)
-    throw std::runtime_error("no CUDA device");
-  const auto choice = mgfa::choose_device(count, d.rank_);
-  if (!choice.error.empty()) throw std::runtime_error(choice.error);
-  d.local_rank_ = choice.local_rank;
-  d.device_ = choice.device;
-  if (cudaSetDevice(d.device_) != cudaSuccess) throw std::runtime_error("cudaSetDevice failed");
+  if (need_gpu) {
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0)
+      throw std::runtime_error("no CUDA device");
+    const auto choice = mgfa::choose_device(count, d.rank_);
+    if (!choice.error.empty()) throw std::runtime_error(choice.error);
+    d.local_rank_ = choice.local_rank;
+    d.device_ = choice.device;
+    if (cudaSetDevice(d.device_) != cudaSuccess) throw std::runtime_error("cudaSetDevice failed");
+  } else {
+    d.local_rank_ = mgfa::local_rank_from_env();
+    d.device_ = -1;
+  }
   if (d.world_ > 1) {
     const char* addr = std::getenv("MASTER_ADDR");
     c10d::TCPStoreOptions o;

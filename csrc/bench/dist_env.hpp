@@ -27,7 +27,8 @@ class Dist {
   // Reads the environment, binds this process to its local GPU (same rules as
   // the Python layer: MPI/Slurm/PMI local-rank variables or LOCAL_RANK) and
   // connects to the store. Throws std::runtime_error on a bad environment.
-  static Dist from_env(int timeout_s = 300);
+  // need_gpu=false skips the device binding (host-only use of the store).
+  static Dist from_env(int timeout_s = 300, bool need_gpu = true);
 
   // Movable, not copyable: the NCCL communicator has one owner.
   Dist(Dist&& o) noexcept { *this = std::move(o); }

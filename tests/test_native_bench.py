@@ -183,3 +183,24 @@ def test_check_peer_lists_every_pair():
     lines = p.stdout.splitlines()
     assert len(lines) == n * (n - 1)
     assert lines[0] == "GPU 0 -> GPU 1: YES"
+
+
+@pytest.mark.parametrize("nproc", [2, 3])
+def test_dist_layer_under_torchrun(tmp_path, nproc):
+    """The native tools' process-group layer on CPU: torchrun's store, barriers,
+    all-gather, MAX reductions, host send/recv around the ring."""
+    out = _torchrun(_exe("dist_selftest"), [], nproc, tmp_path, timeout=120)
+    assert out.count("dist selftest ok") == nproc
+
+
+def test_dist_layer_with_rank0_hosting_the_store():
+    exe = _exe("dist_selftest")
+    port = _port()
+    env = dict(os.environ, WORLD_SIZE="2", MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    env.pop("TORCHELASTIC_USE_AGENT_STORE", None)
+    procs = [subprocess.Popen([exe], env=dict(env, RANK=str(r), LOCAL_RANK=str(r)),
+                              stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)
+             for r in range(2)]
+    outs = [p.communicate(timeout=120) for p in procs]
+    assert all(p.returncode == 0 for p in procs), outs
+    assert all("dist selftest ok" in o for o, _ in outs)
