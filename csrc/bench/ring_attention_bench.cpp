@@ -541,6 +541,8 @@ class Bf16Ring {
       eng_ = std::make_unique<mgfa::RingEngine>(r, P, dev, slot, ch ? std::atoi(ch) : 0);
       const char* tc = std::getenv("MGFA_TAG_CHECK");
       eng_->set_tag_check(!(tc && std::string(tc) == "0"));
+      const char* ca = std::getenv("MGFA_CUMULATIVE_ARRIVALS");
+      eng_->set_cumulative_arrivals(ca && std::string(ca) == "1");
       eng_->connect(d.all_gather(eng_->ipc_handle()));
       eng_->set_transport_mode(a.backend == "fused"         ? mgfa::RingEngine::kFusedPush
                                : a.backend == "p2p_unfused" ? mgfa::RingEngine::kPushKernel

@@ -22,6 +22,7 @@ void register_ring_engine(py::module& m) {
       .def("fused", &RingEngine::fused)
       .def("set_transport_mode", &RingEngine::set_transport_mode)
       .def("set_tag_check", &RingEngine::set_tag_check)
+      .def("set_cumulative_arrivals", &RingEngine::set_cumulative_arrivals)
       .def("transport_mode", &RingEngine::transport_mode)
       .def("poison_slots", &RingEngine::poison_slots)
       .def("last_trace", &RingEngine::last_trace)

@@ -220,8 +220,13 @@ class RingEngine {
       // count on the slot they share before step t resets it (the owner tag
       // check would then fail the call). With P >= 5, where such a step t+3
       // exists, small grids therefore run without dependent launch.
-      const bool chain_hazard = P >= 5 && grid < num_sms_;
+      // (Cumulative arrival counts remove the hazard: a stale count never
+      // reaches a later step's target.)
+      const bool chain_hazard = !cumulative_ && P >= 5 && grid < num_sms_;
       p.dependent_launch = (t > 0 && pdl_ && !chain_hazard) ? 1 : 0;
+      const bool unfused = transport && mode_ != kFusedPush;
+      // chunks (= arrival signals) of the unfused transports
+      const uint32_t x_chunks = mode_ == kCopyEngine ? 1u : uint32_t(2 * num_sms_);
 
       RingPush push_x;     // the standalone push kernel's (unfused transport)
       RingConsume wait_x;  // its wait for the slot it forwards
@@ -250,7 +255,14 @@ class RingEngine {
       if (transport && t > 0) {
         p.consume.enabled = 1;
         p.consume.arrivals = buf_.flag(r, comm::kArrivals0 + s);
-        p.consume.arrivals_target = push_chunks(grid) * kFwdPushParts;
+        const uint32_t per_use = unfused ? x_chunks : push_chunks(grid) * kFwdPushParts;
+        if (cumulative_) {
+          expected_[s] += per_use;
+          p.consume.arrivals_target = expected_[s];
+          p.consume.reset_arrivals = 0;
+        } else {
+          p.consume.arrivals_target = per_use;
+        }
         p.consume.done_counter = buf_.flag(r, comm::kDone0 + s);
         p.consume.done_target = uint32_t(grid - 1);
         p.consume.left_credit = buf_.flag(left, comm::kCredit0 + s);
@@ -258,9 +270,6 @@ class RingEngine {
         p.consume.tag = tag_check_ ? buf_.flag(r, comm::kTag0 + s) : nullptr;
         p.consume.expected_tag = f.tag;
       }
-      const bool unfused = transport && mode_ != kFusedPush;
-      // chunks (= arrival signals) of the unfused transports
-      const uint32_t x_chunks = mode_ == kCopyEngine ? 1u : uint32_t(2 * num_sms_);
       if (unfused) {
         // Unfused transports: the same flags, but the shard moves on a second
         // stream -- in the standalone all-SM push kernel, or by the copy engine
@@ -277,7 +286,6 @@ class RingEngine {
         push_x.peer_tag = nullptr;
         p.push = RingPush();
         if (t > 0) {
-          p.consume.arrivals_target = x_chunks;
           p.consume.done_counter = nullptr;
           p.consume.tag = nullptr;
           wait_x = p.consume;
@@ -325,6 +333,7 @@ class RingEngine {
         rel.arrivals = buf_.flag(r, comm::kArrivals0 + s);
         rel.left_credit = buf_.flag(left, comm::kCredit0 + s);
         rel.left_credit_value = f.credit_value;
+        rel.reset_arrivals = cumulative_ ? 0 : 1;
         C10_CUDA_CHECK(ring_signal_launch(RingPush(), rel, stream));
       }
       nvtxRangePop();
@@ -347,6 +356,11 @@ class RingEngine {
   // Whether each consuming CTA verifies the slot's owner tag (one more
   // system-scope load before its first K load; on by default).
   void set_tag_check(bool on) { tag_check_ = on; }
+  // Arrival counters that are never re-armed, with cumulative targets kept on
+  // the host (off by default): dependent launch then stays on for every grid
+  // size. Every rank must use the same setting; change it only right after
+  // reset(). The 32-bit counts wrap after about 7 million uses of a slot.
+  void set_cumulative_arrivals(bool on) { cumulative_ = on; }
   // false: the standalone push kernel (kept for callers of the two-way switch).
   void set_fused(bool on) { mode_ = on ? kFusedPush : kPushKernel; }
   bool fused() const { return mode_ == kFusedPush; }
@@ -380,6 +394,7 @@ class RingEngine {
   void reset() {
     buf_.reset_flags(at::cuda::getCurrentCUDAStream());
     ctr_ = RingCounters();
+    for (auto& e : expected_) e = 0;
   }
 
  private:
@@ -393,6 +408,8 @@ class RingEngine {
   bool pdl_ = true;
   int mode_ = kFusedPush;
   bool tag_check_ = true;
+  bool cumulative_ = false;
+  uint32_t expected_[kSlots] = {0, 0, 0};  // cumulative arrivals per slot (cumulative_)
   c10::optional<c10::cuda::CUDAStream> push_stream_;
   int num_sms_ = 148;
   torch::Tensor last_trace_;

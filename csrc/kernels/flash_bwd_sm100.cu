@@ -332,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t prev = atomicAdd(p.consume.done_counter, 1u);
     if (prev == p.consume.done_target) {
       *p.consume.done_counter = 0u;
-      *p.consume.arrivals = 0u;
+      if (p.consume.reset_arrivals) *p.consume.arrivals = 0u;
       fence_sys();
       st_release_sys(p.consume.left_credit, p.consume.left_credit_value);
     }

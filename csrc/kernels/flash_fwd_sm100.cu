@@ -457,7 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Every CTA has finished reading the slot: rearm the local counters, then
       // hand the slot back to the left neighbour.
       *p.consume.done_counter = 0u;
-      *p.consume.arrivals = 0u;
+      if (p.consume.reset_arrivals) *p.consume.arrivals = 0u;
       fence_sys();
       st_release_sys(p.consume.left_credit, p.consume.left_credit_value);
     }

@@ -45,6 +45,9 @@ struct RingConsume {
   uint32_t left_credit_value = 0;      // value the last CTA publishes
   const uint32_t* tag = nullptr;       // tag word of the slot being read
   uint32_t expected_tag = 0;           // must match once the shard has arrived
+  int reset_arrivals = 1;              // the release re-arms `arrivals` to 0; with 0
+                                       // the count keeps growing and targets are
+                                       // cumulative (set by the host)
   int enabled = 0;
 };
 

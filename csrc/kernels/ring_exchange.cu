@@ -68,7 +68,7 @@ __global__ void __launch_bounds__(512)
     const uint32_t prev = atomicAdd(consume.done_counter, 1u);
     if (prev == consume.done_target) {
       *consume.done_counter = 0u;
-      *consume.arrivals = 0u;
+      if (consume.reset_arrivals) *consume.arrivals = 0u;
       fence_sys();
       st_release_sys(consume.left_credit, consume.left_credit_value);
     }
@@ -89,7 +89,7 @@ __global__ void ring_signal_kernel(RingPush push, RingConsume consume) {
     red_release_sys_add(push.peer_arrivals, push.n_chunks);
   }
   if (consume.enabled) {
-    *consume.arrivals = 0u;
+    if (consume.reset_arrivals && consume.arrivals) *consume.arrivals = 0u;
     fence_sys();
     st_release_sys(consume.left_credit, consume.left_credit_value);
   }

@@ -100,6 +100,9 @@ class _Engines:
         # MGFA_TAG_CHECK=0 skips the consumers' owner-tag check (an experiment
         # knob: one system-scope load less per CTA and step)
         eng.set_tag_check(os.environ.get("MGFA_TAG_CHECK", "1") != "0")
+        # MGFA_CUMULATIVE_ARRIVALS=1: arrival counts keep growing (cumulative
+        # targets), so dependent launch stays on for every grid size
+        eng.set_cumulative_arrivals(os.environ.get("MGFA_CUMULATIVE_ARRIVALS", "0") == "1")
         handles = [None] * world
         dist.all_gather_object(handles, eng.ipc_handle(), group=group)
         eng.connect(handles)

@@ -45,6 +45,13 @@ def test_ring_forward_matches_reference(backend, kind, causal):
     run_ranks(_case, _world(), kind, causal, backend, 4096, 4, 2, 3, backend="nccl")
 
 
+def test_ring_forward_cumulative_arrival_counts():
+    """Arrival counters that keep growing (cumulative targets): repeated calls
+    stay correct with dependent launch on."""
+    run_ranks(_case, _world(), "zigzag", True, "fused", 4096, 4, 2, 4, backend="nccl",
+              env={"MGFA_CUMULATIVE_ARRIVALS": "1"})
+
+
 def test_ring_forward_scheduler_layout_fused():
     run_ranks(_case, _world(), "scheduler", True, "fused", 4096, 2, 2, 2, backend="nccl")
 
