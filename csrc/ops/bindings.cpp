@@ -15,6 +15,7 @@ void legacy_merge(torch::Tensor m_run, torch::Tensor l_run, torch::Tensor acc_ru
                   torch::Tensor m_new, torch::Tensor l_new, torch::Tensor acc_new);
 void legacy_normalize(torch::Tensor acc, torch::Tensor l, torch::Tensor out,
                       c10::optional<torch::Tensor> lse, c10::optional<torch::Tensor> m);
+void red_probe(torch::Tensor dq, int64_t n_kv_tiles, bool causal);
 void register_ring_engine(py::module& m);
 void register_ring_exchange(py::module& m);
 void register_ring_bwd_engine(py::module& m);
@@ -38,6 +39,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("q_tile_pos"), py::arg("kv_tile_pos"), py::arg("merge"), py::arg("final_out"),
         py::arg("status"), py::arg("wait_limit_ns") = int64_t(2000000000));
   m.def("flash_fwd_smem_bytes", &mgfa::flash_fwd_smem_bytes);
+  m.def("red_probe", &mgfa::red_probe, py::arg("dq"), py::arg("n_kv_tiles"),
+        py::arg("causal"));
   m.def("debug_build", []() {
 #ifdef MGFA_DEBUG
     return true;
