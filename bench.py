@@ -1,7 +1,8 @@
 """Headline benchmark: ring-attention forward at 128K tokens, causal, bf16,
 32 heads x head_dim 128, batch 1, zigzag shards, on N GPUs of one node.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--backend fused|nccl]
+    python bench.py [--gpus N] [--steps K] [--warmup W]
+                    [--backend fused|p2p_unfused|ce_unfused|nccl|staged]
     torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1)
     python bench.py --impl reference ...                   (the reference's own code path)
 
@@ -38,7 +39,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--backend", choices=["fused", "nccl"], default="fused")
+    ap.add_argument("--backend", choices=["fused", "p2p_unfused", "ce_unfused", "nccl", "staged"],
+                    default="fused")
     ap.add_argument("--seq", type=int, default=131072)
     ap.add_argument("--heads", type=int, default=32)
     ap.add_argument("--kv-heads", type=int, default=32)
@@ -197,7 +199,7 @@ def main():
 
     # ---------------- compute-only reference for the exposed-comm fraction
     exposed = None
-    if world > 1 and args.backend == "fused":
+    if world > 1 and args.backend in ("fused", "p2p_unfused", "ce_unfused"):
         eng = ENGINES.get(group, dev, k.numel() * k.element_size())
         from multi_gpu_flashattention_b200.parallel.ring import _meta
         qtp, kvtp, kv_lens = _meta(lay, rank, dev)
