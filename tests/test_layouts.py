@@ -53,3 +53,21 @@ def test_scheduler_layout_balances_better_than_contiguous():
         return max(w) / (sum(w) / world)
     assert imbalance(dp) < imbalance(cont)
     assert dp.max_local_len > seq // world  # uneven shards, padded
+
+
+def test_layout_balance_report():
+    """Per-rank causal work over the ring and the step-paced imbalance: zigzag,
+    striped and the row-LPT scheduler layout are even per step; the contiguous
+    layout has the reference's 1.875x at 8 ranks; the contiguous-DP scheduler
+    layout balances totals but not steps."""
+    from multi_gpu_flashattention_b200.benchmarks.layout_balance import balance
+    rows = {}
+    for kind, kw in [("contiguous", {}), ("zigzag", {}), ("striped", {}),
+                     ("scheduler", {"policy": "dp"}), ("scheduler", {"policy": "lpt"})]:
+        r = balance(kind, 16384, 8, "causal", 128, **kw)
+        rows[r["layout"]] = r
+    assert abs(rows["contiguous"]["imbalance"] - 1.875) < 1e-3
+    for name in ("zigzag", "striped", "scheduler-lpt"):
+        assert rows[name]["ring_paced_imbalance"] < 1.01, (name, rows[name])
+    assert rows["scheduler-dp"]["imbalance"] < 1.05
+    assert rows["scheduler-dp"]["ring_paced_imbalance"] > 2.0
