@@ -13,7 +13,9 @@
 //   * at most 4096 block tasks and 256 block rows (the table is cut short the
 //     same way); --max-tasks / --max-rows lift those caps;
 //   * only "--mask full" changes the mask, any other word leaves it as it was.
-// --report adds per-gpu loads and max/mean imbalance for every partition.
+// --report adds per-gpu loads and max/mean imbalance for every partition and,
+// for the row partitions, the step-paced imbalance of a ring whose ranks own
+// those rows (each ring step advances at its slowest rank's pace).
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -21,6 +23,7 @@
 #include <vector>
 
 #include "scheduler.hpp"
+#include "shard_plan.hpp"
 #include "workload.hpp"
 
 using namespace mgfa::sched;
@@ -39,6 +42,24 @@ static void print_loads(const char* name, const std::vector<double>& loads, doub
   std::printf("  %-8s max/mean=%.4f loads:", name, mean > 0 ? mx / mean : 1.0);
   for (double l : loads) std::printf(" %.4f", alpha + l);
   std::printf("\n");
+}
+
+// Sum over the ring's steps of the slowest rank's visible pairs, over the mean
+// per-rank total, when rank g owns the block rows with row_to_gpu[row] == g.
+static double ring_paced(int seq, int block, const std::vector<int>& row_to_gpu, int world,
+                         MaskKind mask) {
+  const ShardPlan plan = make_from_rows(seq, block, row_to_gpu, world);
+  double paced = 0.0, total = 0.0;
+  for (int t = 0; t < world; ++t) {
+    double slowest = 0.0;
+    for (int r = 0; r < world; ++r) {
+      const double w = double(step_active(plan, r, plan.compute_owner(r, t), mask));
+      slowest = w > slowest ? w : slowest;
+      total += w;
+    }
+    paced += slowest;
+  }
+  return total > 0.0 ? paced / (total / world) : 1.0;
 }
 
 int main(int argc, char** argv) {
@@ -117,6 +138,21 @@ int main(int argc, char** argv) {
       print_loads("DP", v, alpha);
       std::printf("  DP shards (block rows):");
       for (const RowShard& s : dp.shards) std::printf(" [%d,%d)", s.row_begin, s.row_end);
+      std::printf("\n");
+    }
+    const bool truncated = max_tasks > 0 && tasks.size() >= size_t(max_tasks);
+    if (truncated) {
+      std::printf("ring step-paced imbalance: n/a (block tasks truncated at --max-tasks)\n");
+    } else if (int(rows.size()) == num_row_blocks(shape)) {
+      std::vector<int> r2g(rows.size(), 0);
+      for (size_t i = 0; i < rows.size(); ++i) r2g[size_t(rows[i].row)] = row.task_to_gpu[i];
+      std::printf("ring step-paced imbalance: RowLPT=%.3f", ring_paced(seq, block, r2g, gpus, mask));
+      if (dp.ok) {
+        std::vector<int> d2g(rows.size(), 0);
+        for (size_t g = 0; g < dp.shards.size(); ++g)
+          for (int rr = dp.shards[g].row_begin; rr < dp.shards[g].row_end; ++rr) d2g[size_t(rr)] = int(g);
+        std::printf(" DP=%.3f", ring_paced(seq, block, d2g, gpus, mask));
+      }
       std::printf("\n");
     }
     std::printf("block rows:");

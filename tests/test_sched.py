@@ -143,3 +143,15 @@ def test_contiguous_dp_optimal_small():
         assert dp.makespan() == pytest.approx(best)
         assert sorted(set(dp.row_to_gpu)) == list(range(g))
     assert not sched.partition_rows_contiguous(rows, 9).ok
+
+
+def test_demo_report_ring_step_paced(demo_bin):
+    """--report adds the ring's step-paced imbalance of the row partitions, and
+    says n/a when the reference's task cap truncated the workload."""
+    p = subprocess.run([demo_bin, "--seq", "4096", "--gpus", "4", "--report"],
+                       capture_output=True, text=True)
+    line = [l for l in p.stdout.splitlines() if "step-paced" in l][0]
+    assert "RowLPT=1.000" in line and "DP=" in line
+    p = subprocess.run([demo_bin, "--seq", "16384", "--gpus", "8", "--report"],
+                       capture_output=True, text=True)
+    assert "n/a (block tasks truncated" in p.stdout
