@@ -6,6 +6,9 @@
 #   build/bin/ring_loop_bench      pure ring exchange (p2p | ce | nccl | staged)
 #   build/bin/ring_attention_bench ring attention (fused | nccl | staged; fp32 | bf16)
 #   build/bin/check_peer           peer-access matrix (the reference's check_peer)
+# `make mpi-shim` builds build/lib/libmpi_shim.so with csrc/mpi_shim/mpi.h: the
+# subset of the MPI C interface the reference prototype's programs call, over a
+# TCP store, so they build and run unmodified under torchrun without an MPI.
 CXX      ?= g++
 NVCC     ?= nvcc
 PY       ?= python
@@ -67,10 +70,18 @@ $(BIN)/check_peer: csrc/bench/check_peer.cpp | $(BIN)
 $(BIN)/dist_selftest: $(OBJ)/bench/dist_selftest.o $(OBJ)/bench/dist_env.o | $(BIN)
 	$(CXX) -o $@ $^ $(GPU_LIBS)
 
+LIB := build/lib
+$(LIB)/libmpi_shim.so: csrc/mpi_shim/mpi_shim.cpp csrc/mpi_shim/mpi.h
+	@mkdir -p $(LIB)
+	$(GPU_CXX) -Icsrc/mpi_shim -shared -o $@ $< -L$(TORCH_DIR)/lib -Wl,-rpath,$(TORCH_DIR)/lib \
+	    -ltorch_cpu -lc10 -L$(CUDA_HOME)/lib64 -Wl,-rpath,$(CUDA_HOME)/lib64 -lcudart
+
+mpi-shim: $(LIB)/libmpi_shim.so
+
 cuda-tools: $(BIN)/ring_loop_bench $(BIN)/ring_attention_bench $(BIN)/check_peer \
     $(BIN)/dist_selftest
 
 clean:
-	rm -rf $(BIN) $(OBJ)
+	rm -rf $(BIN) $(OBJ) $(LIB)
 
-.PHONY: all cuda-tools clean
+.PHONY: all cuda-tools mpi-shim clean

@@ -1,0 +1,110 @@
+/* Semantics check of the MPI subset in csrc/mpi_shim, run as several ranks
+ * under `torchrun --no-python`. Prints "rank <r> OK" or "rank <r> FAIL <what>"
+ * and exits non-zero on the first failed check. Covers: message order per
+ * (source, tag), tags that overtake each other, Isend/Irecv with Waitall and
+ * Testall, Sendrecv around the ring, Bcast from a non-zero root, Reduce
+ * (MAX, MIN, SUM over double, float and int), Barrier, the shared-memory
+ * split and Wtime. */
+#include <mpi.h>
+#include <stdio.h>
+#include <stdlib.h>
+
+static int rank_, size_;
+
+#define CHECK(cond, what)                                         \
+  do {                                                            \
+    if (!(cond)) {                                                \
+      printf("rank %d FAIL %s\n", rank_, what);                   \
+      fflush(stdout);                                             \
+      MPI_Abort(MPI_COMM_WORLD, 3);                               \
+    }                                                             \
+  } while (0)
+
+int main(int argc, char** argv) {
+  int provided = -1;
+  CHECK(MPI_Init_thread(&argc, &argv, MPI_THREAD_FUNNELED, &provided) == MPI_SUCCESS, "init");
+  CHECK(provided >= MPI_THREAD_FUNNELED, "thread level");
+  MPI_Comm_rank(MPI_COMM_WORLD, &rank_);
+  MPI_Comm_size(MPI_COMM_WORLD, &size_);
+  const int right = (rank_ + 1) % size_, left = (rank_ - 1 + size_) % size_;
+
+  /* shared-memory split: one node, so the local rank is the world rank */
+  MPI_Comm local;
+  int lr = -1, ls = -1;
+  MPI_Comm_split_type(MPI_COMM_WORLD, MPI_COMM_TYPE_SHARED, 0, MPI_INFO_NULL, &local);
+  MPI_Comm_rank(local, &lr);
+  MPI_Comm_size(local, &ls);
+  MPI_Comm_free(&local);
+  CHECK(lr == rank_ && ls == size_, "split_type");
+
+  /* three messages with tag 7 then one with tag 9: a receive of tag 9 posted
+   * first must get the tag-9 message, and tag-7 messages arrive in order */
+  double a[3][4], b[4];
+  for (int m = 0; m < 3; ++m)
+    for (int i = 0; i < 4; ++i) a[m][i] = rank_ * 100 + m * 10 + i;
+  for (int i = 0; i < 4; ++i) b[i] = -(rank_ * 100 + i);
+  for (int m = 0; m < 3; ++m) MPI_Send(a[m], 4, MPI_DOUBLE, right, 7, MPI_COMM_WORLD);
+  MPI_Send(b, 4, MPI_DOUBLE, right, 9, MPI_COMM_WORLD);
+  double rb[4];
+  MPI_Status st;
+  MPI_Recv(rb, 4, MPI_DOUBLE, left, 9, MPI_COMM_WORLD, &st);
+  CHECK(st.MPI_SOURCE == left && st.MPI_TAG == 9, "status");
+  for (int i = 0; i < 4; ++i) CHECK(rb[i] == -(left * 100 + i), "tag 9 payload");
+  for (int m = 0; m < 3; ++m) {
+    MPI_Recv(rb, 4, MPI_DOUBLE, left, 7, MPI_COMM_WORLD, MPI_STATUS_IGNORE);
+    for (int i = 0; i < 4; ++i) CHECK(rb[i] == left * 100 + m * 10 + i, "tag 7 order");
+  }
+
+  /* nonblocking pair, completed by Testall (polled) then Waitall */
+  float sendf[8], recvf[8];
+  for (int i = 0; i < 8; ++i) sendf[i] = (float)(rank_ * 8 + i);
+  MPI_Request req[2];
+  MPI_Irecv(recvf, 8, MPI_FLOAT, left, 3, MPI_COMM_WORLD, &req[0]);
+  MPI_Isend(sendf, 8, MPI_FLOAT, right, 3, MPI_COMM_WORLD, &req[1]);
+  int flag = 0;
+  const double t0 = MPI_Wtime();
+  while (!flag && MPI_Wtime() - t0 < 60.0)
+    MPI_Testall(2, req, &flag, MPI_STATUSES_IGNORE);
+  CHECK(flag, "testall");
+  CHECK(req[0] == MPI_REQUEST_NULL && req[1] == MPI_REQUEST_NULL, "requests freed");
+  for (int i = 0; i < 8; ++i) CHECK(recvf[i] == (float)(left * 8 + i), "isend payload");
+  MPI_Irecv(recvf, 8, MPI_FLOAT, left, 4, MPI_COMM_WORLD, &req[0]);
+  MPI_Isend(sendf, 8, MPI_FLOAT, right, 4, MPI_COMM_WORLD, &req[1]);
+  MPI_Waitall(2, req, MPI_STATUSES_IGNORE);
+  for (int i = 0; i < 8; ++i) CHECK(recvf[i] == (float)(left * 8 + i), "waitall payload");
+
+  /* ring rotation with Sendrecv: after size steps every rank holds its own value */
+  int token = rank_, got = -1;
+  for (int s = 0; s < size_; ++s) {
+    MPI_Sendrecv(&token, 1, MPI_INT, right, 0, &got, 1, MPI_INT, left, 0, MPI_COMM_WORLD,
+                 MPI_STATUS_IGNORE);
+    token = got;
+  }
+  CHECK(token == rank_, "sendrecv ring");
+
+  /* broadcast from the last rank */
+  char id[16];
+  for (int i = 0; i < 16; ++i) id[i] = (char)(rank_ == size_ - 1 ? 'a' + i : 0);
+  MPI_Bcast(id, 16, MPI_BYTE, size_ - 1, MPI_COMM_WORLD);
+  for (int i = 0; i < 16; ++i) CHECK(id[i] == 'a' + i, "bcast");
+
+  /* reductions to root 0 */
+  double dv[2] = {(double)rank_, -(double)rank_}, dmax[2] = {0, 0};
+  MPI_Reduce(dv, dmax, 2, MPI_DOUBLE, MPI_MAX, 0, MPI_COMM_WORLD);
+  float fv = (float)(rank_ + 1), fmin = 0;
+  MPI_Reduce(&fv, &fmin, 1, MPI_FLOAT, MPI_MIN, 0, MPI_COMM_WORLD);
+  int iv = rank_ + 1, isum = 0;
+  MPI_Reduce(&iv, &isum, 1, MPI_INT, MPI_SUM, 0, MPI_COMM_WORLD);
+  if (rank_ == 0) {
+    CHECK(dmax[0] == size_ - 1 && dmax[1] == 0.0, "reduce max");
+    CHECK(fmin == 1.0f, "reduce min");
+    CHECK(isum == size_ * (size_ + 1) / 2, "reduce sum");
+  }
+
+  MPI_Barrier(MPI_COMM_WORLD);
+  CHECK(MPI_Wtime() >= t0, "wtime");
+  printf("rank %d OK\n", rank_);
+  fflush(stdout);
+  MPI_Finalize();
+  return 0;
+}
