@@ -19,6 +19,7 @@ import datetime
 import json
 import math
 import os
+import re
 import statistics
 import subprocess
 import sys
@@ -49,6 +50,8 @@ def parse():
     ap.add_argument("--no-causal", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--ref-timeout", type=float, default=1200.0,
+                    help="wall-clock limit (s) for the reference program (--impl reference)")
     return ap.parse_args()
 
 
@@ -107,14 +110,95 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------- reference arm
+REF_BIN = os.environ.get("MGFA_REF_BIN", os.path.join(ROOT, "baseline", "_ref", "bin"))
+REF_HEAD_DIM = 64  # fixed in the reference's benchmarks (ring/attention/bench/*.cu)
+
+
 def reference_arm(args):
-    reason = ("the reference has no setup.py/pyproject (pip cannot install it) and its ring "
-              "benchmarks need MPI, which is absent here; its kernel is also fp32, 1 head, "
-              "d=64, non-causal with K=V, so it cannot run 128K causal bf16 32x128")
+    """Runs the reference's own NCCL ring-attention benchmark
+    (ring/attention/bench/ring_attention_nccl_gpu_bench.cu, built unmodified by
+    benchmarks/build_reference.sh against this repository's MPI subset) on the
+    same N GPUs and total sequence length, and reports it in the headline's
+    units. The reference's kernel computes only fp32, one head, head_dim 64,
+    non-causal attention with K=V, so that is the workload it is timed on; its
+    own timer (MPI_Wtime from a barrier to the host-normalised output, max over
+    ranks, averaged over its timed iterations) gives ms_per_step."""
     rank = int(os.environ.get("RANK", "0"))
-    if rank == 0:
-        print(json.dumps({"impl": "reference", "metric": METRIC, "n_gpus": args.gpus,
-                          "unavailable": reason}), flush=True)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+
+    def unavailable(reason):
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "metric": METRIC, "n_gpus": args.gpus,
+                              "unavailable": reason}), flush=True)
+        return 0
+
+    if world < 2:
+        return unavailable("the reference's ring attention benchmarks need at least 2 ranks "
+                           "(they exit with 'Need at least 2 processes.' at world size 1)")
+    exe = os.path.join(REF_BIN, "ring_attention_nccl_gpu_bench")
+    if not os.path.exists(exe):
+        return unavailable("the reference build is missing: benchmarks/build_reference.sh "
+                           "builds it from the reference source tree")
+    S = args.seq
+    if S % world:
+        return unavailable(f"seq {S} does not split evenly over {world} ranks")
+    seq_k = S // world
+    kv_bytes = seq_k * REF_HEAD_DIM * 4
+    env = dict(os.environ, MPI_LOCALRANKID=os.environ.get("LOCAL_RANK", str(rank)))
+    sampler = ClockSampler(list(range(world))) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    t_wall = time.time()
+    try:
+        p = subprocess.run([exe, str(kv_bytes), str(args.warmup), str(args.steps)], env=env,
+                           capture_output=True, text=True, timeout=args.ref_timeout)
+        out, rc = p.stdout + p.stderr, p.returncode
+    except subprocess.TimeoutExpired:
+        out, rc = f"timed out after {args.ref_timeout} s", -1
+    wall = time.time() - t_wall
+    clocks = sampler.stop() if sampler else None
+    if rank != 0:
+        return 0 if rc == 0 else 1
+    m = re.search(r"avg_total=([\d.]+) ms avg_NCCL=([\d.]+) avg_attn=([\d.]+) "
+                  r"avg_merge=([\d.]+) avg_final=([\d.]+)", out)
+    if rc != 0 or not m:
+        tail = " | ".join(out.strip().splitlines()[-3:])
+        return unavailable(f"the reference benchmark failed (exit {rc}): {tail}"[:400])
+    total, nccl, attn, merge, final = (float(x) for x in m.groups())
+    flops = 4.0 * REF_HEAD_DIM * S * S  # every query row against every key, one head
+    tflops = flops / (total * 1e-3) / 1e12
+    rec = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(tflops, 4),
+        "unit": "TFLOP/s (attention, summed over GPUs)",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(total, 3),
+        "tflops_per_gpu": round(tflops / world, 4),
+        "exposed_comm_pct": round(100.0 * nccl / total, 2),
+        "breakdown_ms": {"nccl": nccl, "attn": attn, "merge": merge, "final": final},
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "fp32",
+        "data": "synthetic: the reference's built-in inputs (K=V=rank*1000+i, "
+                "Q=(rank*500+(i%64)*0.01)*0.001)",
+        "config": {"model": "ring attention fwd, non-causal, 1 head x d64, K=V (the only "
+                            "shape the reference's kernel computes)",
+                   "global_batch": 1, "seq_len": S,
+                   "parallelism": f"cp{world} ring (contiguous shards), NCCL send/recv",
+                   "l2": "inputs per rank below L2; the reference does not flush"},
+        "timing": "the reference's own: MPI_Wtime from a barrier to the host-normalised "
+                  "output, max over ranks (MPI over this repository's TCP-store MPI subset)",
+        "program": "ring/attention/bench/ring_attention_nccl_gpu_bench.cu, unmodified, "
+                   f"args {kv_bytes} {args.warmup} {args.steps}",
+        "clocks": clocks,
+        "gpu_launches": 2 * world * args.steps,
+        "wall_s": round(wall, 3),
+    }
+    print(json.dumps(rec), flush=True)
     return 0
 
 
