@@ -50,7 +50,7 @@ def parse():
     ap.add_argument("--no-causal", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--ref-timeout", type=float, default=1200.0,
+    ap.add_argument("--ref-timeout", type=float, default=900.0,
                     help="wall-clock limit (s) for the reference program (--impl reference)")
     return ap.parse_args()
 

@@ -1,21 +1,49 @@
-// Implementation of the MPI subset in mpi.h over a c10d TCPStore.
+// Implementation of the MPI subset in mpi.h for the ranks of one node: a
+// shared-memory mailbox carries point-to-point messages and the barrier, CUDA
+// IPC carries device buffers, and a c10d TCPStore does the rendezvous, the
+// broadcast and reduce, and payloads too large for a mailbox slot.
 //
-// Point-to-point: a message from `src` to `dst` with tag `tag` is the store key
-// .../m/<src>/<dst>/<tag>/<n>, where n counts the messages of that (src, dst,
-// tag) triple on both sides, so receives match sends in posting order (MPI's
-// non-overtaking rule for one sender, tag and communicator). Sends are eager
-// (the store buffers them), so MPI_Isend completes at once; MPI_Irecv reserves
-// its key when posted and completes in MPI_Wait / MPI_Waitall / MPI_Testall.
-// Buffers in device memory are copied through host memory (cudaMemcpy), the
-// behaviour of a CUDA-aware MPI. Collectives (barrier, broadcast, reduce) use
-// keys numbered per call. Rendezvous: torchrun's store when it offers one
-// (TORCHELASTIC_USE_AGENT_STORE), otherwise rank 0 hosts it.
+// Matching: message n of the triple (src, dst, tag) carries sequence number n.
+// Both sides count, so receives match sends in posting order (MPI's
+// non-overtaking rule for one sender, tag and communicator).
+//
+// Mailbox: for every ordered pair (src, dst) a ring of slots in a POSIX shared
+// memory segment. The sender claims a free slot (state 0), fills it and
+// publishes it (state 1, release store); the receiver finds the slot with its
+// tag and sequence number (acquire load), consumes it and frees it (state 0),
+// or, for a device message, marks it copied (state 2) for the sender to free.
+// One thread per process drives the shim (MPI_THREAD_FUNNELED), so each slot
+// has one writer per transition. Slot kinds, chosen by the sender:
+//  * 'H': a host payload small enough for the slot, inline; the send completes
+//    once posted.
+//  * 'S': a larger host payload, put in the store under the message's key.
+//  * 'D' (device buffer; MPI_SHIM_CUDA_IPC=0 turns it off): a CUDA IPC handle
+//    of the allocation, offset and length, and the handle of an IPC event
+//    recorded on the legacy default stream at the send. The receiver opens the
+//    handle (once per allocation), orders a copy-engine copy after that event
+//    on its own non-blocking stream, and marks the slot copied when the copy
+//    has finished. The send completes when the sender sees the mark; only then
+//    may it reuse the buffer. The payload crosses NVLink directly.
+//
+// Progress: every wait, test and barrier advances all pending requests of the
+// process (post queued sends, match slots, start copies, poll their events,
+// free acknowledged slots), so blocking calls in any order cannot deadlock on
+// an acknowledgement. Every wait yields between polls and gives up after
+// MPI_SHIM_TIMEOUT_S seconds (default 600) with an error. The broadcast and
+// reduce wait in the store without driving progress.
 #include "mpi.h"
 
+#include <cuda.h>
 #include <cuda_runtime.h>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <unistd.h>
 #include <torch/csrc/distributed/c10d/TCPStore.hpp>
 
+#include <algorithm>
+#include <atomic>
 #include <chrono>
+#include <random>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -23,19 +51,68 @@
 #include <memory>
 #include <stdexcept>
 #include <string>
+#include <thread>
 #include <tuple>
 #include <vector>
 
+namespace mgfa_mpi_shim {
+
+constexpr int kSlots = 16;               // per ordered pair of ranks
+constexpr size_t kSlotBytes = 1024;
+constexpr size_t kSlotHeader = 24;
+constexpr size_t kInline = kSlotBytes - kSlotHeader;
+constexpr int kMaxWorld = 32;            // 16 MB of mailboxes at 32 ranks
+
+struct Slot {
+  std::atomic<uint32_t> state;  // 0 free, 1 posted, 2 copied (sender frees)
+  uint32_t kind;
+  int32_t tag;
+  uint32_t len;
+  uint64_t seq;
+  uint8_t data[kInline];
+};
+static_assert(sizeof(Slot) == kSlotBytes, "slot layout");
+static_assert(std::atomic<uint32_t>::is_always_lock_free, "address-free atomics");
+
+}  // namespace mgfa_mpi_shim
+
+using mgfa_mpi_shim::Slot;
+
 struct mgfa_mpi_request {
-  bool is_recv = false;
-  bool done = false;
+  enum Kind { kRecv, kSend } kind = kRecv;
+  // send: kQueued (no free slot yet) -> kPosted ('D': waiting for the copy) -> kDone
+  // receive: kPosted (matching) -> kCopying ('D') -> kDone
+  enum Phase { kQueued, kPosted, kCopying, kDone } phase = kPosted;
   void* buf = nullptr;
   size_t bytes = 0;
-  int source = 0, tag = 0;
-  std::string key;
+  int source = 0, tag = 0;       // for a send: the destination and tag
+  uint64_t seq = 0;
+  char slot_kind = 'H';
+  std::vector<uint8_t> record;   // send: the slot contents still to post
+  Slot* slot = nullptr;          // the slot this request posted or consumed
+  cudaEvent_t copy_done = nullptr;
 };
 
 namespace {
+
+using Clock = std::chrono::steady_clock;
+
+struct IpcRecord {  // contents of a 'D' slot
+  cudaIpcMemHandle_t mem;
+  cudaIpcEventHandle_t event;
+  uint64_t offset = 0, bytes = 0;
+};
+
+using mgfa_mpi_shim::kInline;
+using mgfa_mpi_shim::kMaxWorld;
+using mgfa_mpi_shim::kSlots;
+static_assert(sizeof(IpcRecord) <= kInline, "IPC record fits a slot");
+
+struct SegmentHeader {
+  std::atomic<uint32_t> barrier_count;
+  std::atomic<uint32_t> barrier_generation;
+  uint8_t pad[56];
+};
 
 struct State {
   int rank = 0, world = 1;
@@ -43,7 +120,26 @@ struct State {
   std::string prefix;
   std::map<std::tuple<int, int>, uint64_t> sent, received;  // (peer, tag) -> count
   uint64_t coll = 0;
-  std::chrono::steady_clock::time_point t0 = std::chrono::steady_clock::now();
+  Clock::time_point t0 = Clock::now();
+  double timeout_s = 600.0;
+  bool ipc = true;
+  // shared-memory segment: header, then world * world mailboxes of kSlots
+  void* seg = nullptr;
+  size_t seg_bytes = 0;
+  std::vector<int> next_slot;              // per destination: where the free-slot scan starts
+  std::vector<mgfa_mpi_request*> pending;  // started and not yet complete
+  // device side, created on first use on the current device
+  cudaEvent_t send_event = nullptr;
+  cudaIpcEventHandle_t send_event_handle{};
+  cudaStream_t copy_stream = nullptr;
+  std::map<std::string, char*> opened_mem;            // handle bytes -> mapped base
+  std::map<std::string, cudaEvent_t> opened_events;   // handle bytes -> event
+
+  SegmentHeader* header() const { return static_cast<SegmentHeader*>(seg); }
+  Slot* mailbox(int src, int dst) const {
+    return reinterpret_cast<Slot*>(static_cast<char*>(seg) + sizeof(SegmentHeader)) +
+           size_t(src * world + dst) * kSlots;
+  }
 };
 
 State* g = nullptr;
@@ -68,10 +164,14 @@ size_t type_size(MPI_Datatype t) {
   }
 }
 
+void cuda_ok(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
 bool on_device(const void* p) {
   cudaPointerAttributes a;
   if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
-    cudaGetLastError();  // host memory the runtime does not know
+    cudaGetLastError();  // no device, or memory the runtime does not know: host
     return false;
   }
   return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
@@ -80,24 +180,16 @@ bool on_device(const void* p) {
 std::vector<uint8_t> read_buffer(const void* buf, size_t bytes) {
   std::vector<uint8_t> v(bytes);
   if (bytes == 0) return v;
-  if (on_device(buf)) {
-    if (cudaMemcpy(v.data(), buf, bytes, cudaMemcpyDeviceToHost) != cudaSuccess)
-      throw std::runtime_error("device to host copy failed");
-  } else {
-    std::memcpy(v.data(), buf, bytes);
-  }
+  if (on_device(buf)) cuda_ok(cudaMemcpy(v.data(), buf, bytes, cudaMemcpyDeviceToHost), "D2H");
+  else std::memcpy(v.data(), buf, bytes);
   return v;
 }
 
-void write_buffer(void* buf, const std::vector<uint8_t>& v, size_t bytes) {
-  if (v.size() > bytes) throw std::runtime_error("message longer than the receive buffer");
-  if (v.empty()) return;
-  if (on_device(buf)) {
-    if (cudaMemcpy(buf, v.data(), v.size(), cudaMemcpyHostToDevice) != cudaSuccess)
-      throw std::runtime_error("host to device copy failed");
-  } else {
-    std::memcpy(buf, v.data(), v.size());
-  }
+void write_buffer(void* buf, const uint8_t* src, size_t n, size_t capacity) {
+  if (n > capacity) throw std::runtime_error("message longer than the receive buffer");
+  if (n == 0) return;
+  if (on_device(buf)) cuda_ok(cudaMemcpy(buf, src, n, cudaMemcpyHostToDevice), "H2D");
+  else std::memcpy(buf, src, n);
 }
 
 std::string msg_key(int src, int dst, int tag, uint64_t n) {
@@ -109,24 +201,238 @@ std::string coll_key(const char* kind) {
   return g->prefix + kind + "/" + std::to_string(g->coll++);
 }
 
+std::string bytes_of(const void* p, size_t n) {
+  return std::string(static_cast<const char*>(p), n);
+}
+
 int fail(const char* where, const std::exception& e) {
   std::fprintf(stderr, "[mpi shim rank %d] %s: %s\n", g ? g->rank : -1, where, e.what());
   return MPI_ERR_OTHER;
 }
 
-void complete_recv(mgfa_mpi_request* r, MPI_Status* st) {
-  if (!r->done) {
-    const std::vector<uint8_t> v = g->store->get(r->key);
-    write_buffer(r->buf, v, r->bytes);
-    g->store->deleteKey(r->key);
-    r->done = true;
+// Bounded poll loop: `done()` is re-evaluated after driving progress.
+template <class F>
+void spin_until(F done, const char* what);
+
+// ------------------------------------------------------------------ device sends
+char* allocation_base(const void* p, size_t* size) {
+  using Fn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static Fn fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    cuda_ok(cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &f, 12000, cudaEnableDefault,
+                                             &q),
+            "driver entry point");
+    if (q != cudaDriverEntryPointSuccess || !f)
+      throw std::runtime_error("cuMemGetAddressRange unavailable");
+    fn = reinterpret_cast<Fn>(f);
   }
-  if (st) {
-    st->MPI_SOURCE = r->source;
-    st->MPI_TAG = r->tag;
-    st->MPI_ERROR = MPI_SUCCESS;
-    st->count_bytes = int(r->bytes);
+  CUdeviceptr base = 0;
+  if (fn(&base, size, reinterpret_cast<CUdeviceptr>(p)) != CUDA_SUCCESS)
+    throw std::runtime_error("cuMemGetAddressRange failed");
+  return reinterpret_cast<char*>(base);
+}
+
+std::vector<uint8_t> device_record(const void* buf, size_t bytes) {
+  if (!g->send_event) {
+    cuda_ok(cudaEventCreateWithFlags(&g->send_event,
+                                     cudaEventDisableTiming | cudaEventInterprocess),
+            "event create");
+    cuda_ok(cudaIpcGetEventHandle(&g->send_event_handle, g->send_event), "event handle");
   }
+  size_t alloc = 0;
+  char* base = allocation_base(buf, &alloc);
+  IpcRecord r;
+  cuda_ok(cudaIpcGetMemHandle(&r.mem, base), "memory handle");
+  r.event = g->send_event_handle;
+  r.offset = uint64_t(static_cast<const char*>(buf) - base);
+  r.bytes = bytes;
+  // everything the program queued before the send (legacy stream semantics)
+  cuda_ok(cudaEventRecord(g->send_event, cudaStreamLegacy), "event record");
+  std::vector<uint8_t> v(sizeof(r));
+  std::memcpy(v.data(), &r, sizeof(r));
+  return v;
+}
+
+// ------------------------------------------------------------------ sends
+// Posts a queued send into a free slot of the mailbox to its destination.
+bool try_post(mgfa_mpi_request* q) {
+  Slot* box = g->mailbox(g->rank, q->source);
+  int& start = g->next_slot[q->source];
+  for (int k = 0; k < kSlots; ++k) {
+    Slot* s = box + (start + k) % kSlots;
+    if (s->state.load(std::memory_order_acquire) != 0) continue;
+    s->kind = uint32_t(q->slot_kind);
+    s->tag = q->tag;
+    s->seq = q->seq;
+    s->len = uint32_t(q->slot_kind == 'H' ? q->record.size() : q->bytes);
+    if (!q->record.empty()) std::memcpy(s->data, q->record.data(), q->record.size());
+    s->state.store(1, std::memory_order_release);
+    start = (start + k + 1) % kSlots;
+    q->record.clear();
+    q->slot = s;
+    q->phase = q->slot_kind == 'D' ? mgfa_mpi_request::kPosted : mgfa_mpi_request::kDone;
+    return true;
+  }
+  return false;
+}
+
+// ------------------------------------------------------------------ receives
+void start_ipc_copy(mgfa_mpi_request* q, const IpcRecord& r) {
+  if (r.bytes > q->bytes) throw std::runtime_error("message longer than the receive buffer");
+  if (!g->copy_stream)
+    cuda_ok(cudaStreamCreateWithFlags(&g->copy_stream, cudaStreamNonBlocking), "stream");
+  const std::string mk = bytes_of(&r.mem, sizeof(r.mem));
+  auto m = g->opened_mem.find(mk);
+  if (m == g->opened_mem.end()) {
+    void* p = nullptr;
+    cuda_ok(cudaIpcOpenMemHandle(&p, r.mem, cudaIpcMemLazyEnablePeerAccess), "open memory");
+    m = g->opened_mem.emplace(mk, static_cast<char*>(p)).first;
+  }
+  const std::string ek = bytes_of(&r.event, sizeof(r.event));
+  auto e = g->opened_events.find(ek);
+  if (e == g->opened_events.end()) {
+    cudaEvent_t ev = nullptr;
+    cuda_ok(cudaIpcOpenEventHandle(&ev, r.event), "open event");
+    e = g->opened_events.emplace(ek, ev).first;
+  }
+  cuda_ok(cudaStreamWaitEvent(g->copy_stream, e->second, 0), "stream wait");
+  if (r.bytes)
+    cuda_ok(cudaMemcpyAsync(q->buf, m->second + r.offset, r.bytes, cudaMemcpyDefault,
+                            g->copy_stream),
+            "peer copy");
+  cuda_ok(cudaEventCreateWithFlags(&q->copy_done, cudaEventDisableTiming), "event create");
+  cuda_ok(cudaEventRecord(q->copy_done, g->copy_stream), "event record");
+  q->phase = mgfa_mpi_request::kCopying;
+}
+
+Slot* match(const mgfa_mpi_request* q) {
+  Slot* box = g->mailbox(q->source, g->rank);
+  for (int k = 0; k < kSlots; ++k) {
+    Slot* s = box + k;
+    if (s->state.load(std::memory_order_acquire) == 1 && s->tag == q->tag && s->seq == q->seq)
+      return s;
+  }
+  return nullptr;
+}
+
+// One step of progress on request q; returns true when it is complete.
+bool advance(mgfa_mpi_request* q) {
+  using R = mgfa_mpi_request;
+  if (q->phase == R::kDone) return true;
+  if (q->kind == R::kSend) {
+    if (q->phase == R::kQueued && !try_post(q)) return false;
+    if (q->phase == R::kDone) return true;
+    // 'D': the receiver marks the slot copied; this side frees it
+    if (q->slot->state.load(std::memory_order_acquire) != 2) return false;
+    q->slot->state.store(0, std::memory_order_release);
+    q->phase = R::kDone;
+    return true;
+  }
+  if (q->phase == R::kPosted) {
+    Slot* s = match(q);
+    if (!s) return false;
+    q->slot = s;
+    if (s->kind == 'H') {
+      write_buffer(q->buf, s->data, s->len, q->bytes);
+      s->state.store(0, std::memory_order_release);
+      q->phase = R::kDone;
+      return true;
+    }
+    if (s->kind == 'S') {
+      const std::string key = msg_key(q->source, g->rank, q->tag, q->seq);
+      const std::vector<uint8_t> v = g->store->get(key);
+      g->store->deleteKey(key);
+      write_buffer(q->buf, v.data(), v.size(), q->bytes);
+      s->state.store(0, std::memory_order_release);
+      q->phase = R::kDone;
+      return true;
+    }
+    if (s->kind != 'D') throw std::runtime_error("malformed mailbox slot");
+    IpcRecord r;
+    std::memcpy(&r, s->data, sizeof(r));
+    start_ipc_copy(q, r);
+  }
+  const cudaError_t st = cudaEventQuery(q->copy_done);
+  if (st == cudaErrorNotReady) return false;
+  cuda_ok(st, "peer copy");
+  cudaEventDestroy(q->copy_done);
+  q->copy_done = nullptr;
+  q->slot->state.store(2, std::memory_order_release);
+  q->phase = R::kDone;
+  return true;
+}
+
+void progress_all() {
+  auto& p = g->pending;
+  p.erase(std::remove_if(p.begin(), p.end(), [](mgfa_mpi_request* q) { return advance(q); }),
+          p.end());
+}
+
+template <class F>
+void spin_until(F done, const char* what) {
+  const auto t0 = Clock::now();
+  for (int spins = 0;; ++spins) {
+    progress_all();
+    if (done()) return;
+    if (std::chrono::duration<double>(Clock::now() - t0).count() > g->timeout_s)
+      throw std::runtime_error(std::string("timed out waiting for ") + what);
+    if (spins > 1024) std::this_thread::sleep_for(std::chrono::microseconds(20));
+    else std::this_thread::yield();
+  }
+}
+
+void fill_status(const mgfa_mpi_request* r, MPI_Status* st) {
+  if (!st || !r) return;
+  st->MPI_SOURCE = r->source;
+  st->MPI_TAG = r->tag;
+  st->MPI_ERROR = MPI_SUCCESS;
+  st->count_bytes = int(r->bytes);
+}
+
+// ------------------------------------------------------------------ setup
+void store_barrier(const char* name) {
+  const std::string k = g->prefix + name;
+  if (g->store->add(k, 1) == g->world) g->store->set(k + "/done", {1});
+  g->store->wait({k + "/done"});
+}
+
+void map_segment() {
+  if (g->world > kMaxWorld)
+    throw std::runtime_error("more than " + std::to_string(kMaxWorld) + " ranks");
+  char host[256] = {0};
+  gethostname(host, sizeof(host) - 1);
+  g->store->set(g->prefix + "host/" + std::to_string(g->rank),
+                std::vector<uint8_t>(host, host + std::strlen(host)));
+  const std::vector<uint8_t> h0 = g->store->get(g->prefix + "host/0");
+  if (std::string(h0.begin(), h0.end()) != host)
+    throw std::runtime_error("this MPI subset runs the ranks of one node only");
+  g->seg_bytes = sizeof(SegmentHeader) + size_t(g->world) * g->world * kSlots * sizeof(Slot);
+  std::string name;
+  int fd = -1;
+  if (g->rank == 0) {
+    std::random_device rd;
+    name = "/mgfa_mpi_" + std::to_string(getpid()) + "_" + std::to_string(rd());
+    fd = shm_open(name.c_str(), O_CREAT | O_EXCL | O_RDWR, 0600);
+    if (fd < 0 || ftruncate(fd, off_t(g->seg_bytes)) != 0)
+      throw std::runtime_error("cannot create the shared-memory segment " + name);
+    g->store->set(g->prefix + "shm", std::vector<uint8_t>(name.begin(), name.end()));
+  } else {
+    const std::vector<uint8_t> v = g->store->get(g->prefix + "shm");
+    name.assign(v.begin(), v.end());
+    fd = shm_open(name.c_str(), O_RDWR, 0600);
+    if (fd < 0) throw std::runtime_error("cannot open the shared-memory segment " + name);
+  }
+  g->seg = mmap(nullptr, g->seg_bytes, PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0);
+  close(fd);
+  if (g->seg == MAP_FAILED) {
+    g->seg = nullptr;
+    throw std::runtime_error("cannot map the shared-memory segment");
+  }
+  store_barrier("mapped");
+  if (g->rank == 0) shm_unlink(name.c_str());  // lives on while mapped
+  g->next_slot.assign(size_t(g->world), 0);
 }
 
 }  // namespace
@@ -139,6 +445,8 @@ int MPI_Init_thread(int*, char***, int required, int* provided) {
     g = new State();
     g->world = env_int("WORLD_SIZE", 1);
     g->rank = env_int("RANK", 0);
+    g->timeout_s = env_int("MPI_SHIM_TIMEOUT_S", 600);
+    g->ipc = env_int("MPI_SHIM_CUDA_IPC", 1) != 0;
     if (g->world < 1 || g->rank < 0 || g->rank >= g->world)
       throw std::runtime_error("bad RANK / WORLD_SIZE");
     const char* run = std::getenv("TORCHELASTIC_RUN_ID");
@@ -151,9 +459,10 @@ int MPI_Init_thread(int*, char***, int required, int* provided) {
       o.isServer = !use_agent && g->rank == 0;
       o.numWorkers = use_agent ? std::nullopt : std::optional<size_t>(size_t(g->world));
       o.waitWorkers = !use_agent;
-      o.timeout = std::chrono::seconds(env_int("MPI_SHIM_TIMEOUT_S", 600));
+      o.timeout = std::chrono::milliseconds(int64_t(g->timeout_s * 1000));
       const char* addr = std::getenv("MASTER_ADDR");
       g->store = c10::make_intrusive<c10d::TCPStore>(addr && *addr ? addr : "127.0.0.1", o);
+      map_segment();
     }
     if (provided) *provided = required;
     return MPI_SUCCESS;
@@ -169,11 +478,24 @@ int MPI_Init(int* argc, char*** argv) {
 
 int MPI_Finalize(void) {
   if (!g) return MPI_SUCCESS;
-  // every rank leaves together, so the store's host (rank 0) outlives the others
-  MPI_Barrier(MPI_COMM_WORLD);
+  // every rank leaves together: no peer still reads this process's buffers,
+  // event or mailbox, and the store's host (rank 0) outlives the others
+  int rc = MPI_Barrier(MPI_COMM_WORLD);
+  if (g->world > 1) {
+    try {
+      store_barrier("finalize");
+    } catch (const std::exception& e) {
+      rc = fail("MPI_Finalize", e);
+    }
+  }
+  for (auto& m : g->opened_mem) cudaIpcCloseMemHandle(m.second);
+  for (auto& e : g->opened_events) cudaEventDestroy(e.second);
+  if (g->send_event) cudaEventDestroy(g->send_event);
+  if (g->copy_stream) cudaStreamDestroy(g->copy_stream);
+  if (g->seg) munmap(g->seg, g->seg_bytes);
   delete g;
   g = nullptr;
-  return MPI_SUCCESS;
+  return rc;
 }
 
 int MPI_Abort(MPI_Comm, int errorcode) {
@@ -204,17 +526,23 @@ int MPI_Comm_free(MPI_Comm* comm) {
 }
 
 double MPI_Wtime(void) {
-  const auto now = std::chrono::steady_clock::now();
-  const auto t0 = g ? g->t0 : now;
-  return std::chrono::duration<double>(now - t0).count();
+  const auto now = Clock::now();
+  return std::chrono::duration<double>(now - (g ? g->t0 : now)).count();
 }
 
+// Sense-reversing counter barrier in the segment; drives progress while waiting.
 int MPI_Barrier(MPI_Comm) {
   if (!g || g->world == 1) return MPI_SUCCESS;
   try {
-    const std::string k = coll_key("barrier");
-    if (g->store->add(k, 1) == g->world) g->store->set(k + "/done", {1});
-    g->store->wait({k + "/done"});
+    SegmentHeader* h = g->header();
+    const uint32_t gen = h->barrier_generation.load(std::memory_order_acquire);
+    if (h->barrier_count.fetch_add(1, std::memory_order_acq_rel) == uint32_t(g->world - 1)) {
+      h->barrier_count.store(0, std::memory_order_relaxed);
+      h->barrier_generation.fetch_add(1, std::memory_order_release);
+    } else {
+      spin_until([&] { return h->barrier_generation.load(std::memory_order_acquire) != gen; },
+                 "the barrier");
+    }
     return MPI_SUCCESS;
   } catch (const std::exception& e) {
     return fail("MPI_Barrier", e);
@@ -226,8 +554,12 @@ int MPI_Bcast(void* buffer, int count, MPI_Datatype datatype, int root, MPI_Comm
   try {
     const size_t bytes = size_t(count) * type_size(datatype);
     const std::string k = coll_key("bcast");
-    if (g->rank == root) g->store->set(k, read_buffer(buffer, bytes));
-    else write_buffer(buffer, g->store->get(k), bytes);
+    if (g->rank == root) {
+      g->store->set(k, read_buffer(buffer, bytes));
+    } else {
+      const std::vector<uint8_t> v = g->store->get(k);
+      write_buffer(buffer, v.data(), v.size(), bytes);
+    }
     return MPI_SUCCESS;
   } catch (const std::exception& e) {
     return fail("MPI_Bcast", e);
@@ -240,7 +572,7 @@ int MPI_Reduce(const void* sendbuf, void* recvbuf, int count, MPI_Datatype datat
     const size_t bytes = size_t(count) * type_size(datatype);
     std::vector<uint8_t> mine = read_buffer(sendbuf, bytes);
     if (!g || g->world == 1) {
-      if (recvbuf != sendbuf) write_buffer(recvbuf, mine, bytes);
+      if (recvbuf != sendbuf) write_buffer(recvbuf, mine.data(), bytes, bytes);
       return MPI_SUCCESS;
     }
     const std::string k = coll_key("reduce");
@@ -267,7 +599,7 @@ int MPI_Reduce(const void* sendbuf, void* recvbuf, int count, MPI_Datatype datat
         throw std::runtime_error("unsupported MPI_Reduce datatype");
     }
     for (int r = 0; r < g->world; ++r) g->store->deleteKey(k + "/" + std::to_string(r));
-    write_buffer(recvbuf, acc, bytes);
+    write_buffer(recvbuf, acc.data(), bytes, bytes);
     return MPI_SUCCESS;
   } catch (const std::exception& e) {
     return fail("MPI_Reduce", e);
@@ -277,14 +609,27 @@ int MPI_Reduce(const void* sendbuf, void* recvbuf, int count, MPI_Datatype datat
 int MPI_Isend(const void* buf, int count, MPI_Datatype datatype, int dest, int tag, MPI_Comm,
               MPI_Request* request) {
   try {
-    const size_t bytes = size_t(count) * type_size(datatype);
-    const uint64_t n = g->sent[{dest, tag}]++;
-    g->store->set(msg_key(g->rank, dest, tag, n), read_buffer(buf, bytes));
-    if (request) {
-      auto* r = new mgfa_mpi_request();
-      r->done = true;
-      *request = r;
+    if (!g || g->world == 1 || dest < 0 || dest >= g->world)
+      throw std::runtime_error("bad destination");
+    auto* r = new mgfa_mpi_request();
+    r->kind = mgfa_mpi_request::kSend;
+    r->bytes = size_t(count) * type_size(datatype);
+    r->source = dest;
+    r->tag = tag;
+    r->seq = g->sent[{dest, tag}]++;
+    if (g->ipc && r->bytes && on_device(buf)) {
+      r->slot_kind = 'D';
+      r->record = device_record(buf, r->bytes);
+    } else if (r->bytes <= kInline) {
+      r->slot_kind = 'H';
+      r->record = read_buffer(buf, r->bytes);
+    } else {
+      r->slot_kind = 'S';
+      g->store->set(msg_key(g->rank, dest, tag, r->seq), read_buffer(buf, r->bytes));
     }
+    r->phase = mgfa_mpi_request::kQueued;
+    if (!try_post(r) || r->phase != mgfa_mpi_request::kDone) g->pending.push_back(r);
+    *request = r;
     return MPI_SUCCESS;
   } catch (const std::exception& e) {
     return fail("MPI_Isend", e);
@@ -294,13 +639,16 @@ int MPI_Isend(const void* buf, int count, MPI_Datatype datatype, int dest, int t
 int MPI_Irecv(void* buf, int count, MPI_Datatype datatype, int source, int tag, MPI_Comm,
               MPI_Request* request) {
   try {
+    if (!g || g->world == 1 || source < 0 || source >= g->world)
+      throw std::runtime_error("bad source");
     auto* r = new mgfa_mpi_request();
-    r->is_recv = true;
+    r->kind = mgfa_mpi_request::kRecv;
     r->buf = buf;
     r->bytes = size_t(count) * type_size(datatype);
     r->source = source;
     r->tag = tag;
-    r->key = msg_key(source, g->rank, tag, g->received[{source, tag}]++);
+    r->seq = g->received[{source, tag}]++;
+    g->pending.push_back(r);
     *request = r;
     return MPI_SUCCESS;
   } catch (const std::exception& e) {
@@ -308,32 +656,35 @@ int MPI_Irecv(void* buf, int count, MPI_Datatype datatype, int source, int tag, 
   }
 }
 
-int MPI_Wait(MPI_Request* request, MPI_Status* status) {
+int MPI_Waitall(int count, MPI_Request reqs[], MPI_Status statuses[]) {
   try {
-    if (*request) {
-      if ((*request)->is_recv) complete_recv(*request, status);
-      delete *request;
-      *request = MPI_REQUEST_NULL;
+    spin_until(
+        [&] {
+          for (int i = 0; i < count; ++i)
+            if (reqs[i] && reqs[i]->phase != mgfa_mpi_request::kDone) return false;
+          return true;
+        },
+        "a message");
+    for (int i = 0; i < count; ++i) {
+      fill_status(reqs[i], statuses ? &statuses[i] : MPI_STATUS_IGNORE);
+      delete reqs[i];
+      reqs[i] = MPI_REQUEST_NULL;
     }
     return MPI_SUCCESS;
   } catch (const std::exception& e) {
-    return fail("MPI_Wait", e);
+    return fail("MPI_Waitall", e);
   }
 }
 
-int MPI_Waitall(int count, MPI_Request reqs[], MPI_Status statuses[]) {
-  for (int i = 0; i < count; ++i) {
-    const int rc = MPI_Wait(&reqs[i], statuses ? &statuses[i] : MPI_STATUS_IGNORE);
-    if (rc != MPI_SUCCESS) return rc;
-  }
-  return MPI_SUCCESS;
+int MPI_Wait(MPI_Request* request, MPI_Status* status) {
+  return MPI_Waitall(1, request, status);
 }
 
 int MPI_Testall(int count, MPI_Request reqs[], int* flag, MPI_Status statuses[]) {
   try {
+    progress_all();
     for (int i = 0; i < count; ++i) {
-      mgfa_mpi_request* r = reqs[i];
-      if (r && r->is_recv && !r->done && !g->store->check({r->key})) {
+      if (reqs[i] && reqs[i]->phase != mgfa_mpi_request::kDone) {
         *flag = 0;
         return MPI_SUCCESS;
       }
@@ -347,7 +698,9 @@ int MPI_Testall(int count, MPI_Request reqs[], int* flag, MPI_Status statuses[])
 
 int MPI_Send(const void* buf, int count, MPI_Datatype datatype, int dest, int tag,
              MPI_Comm comm) {
-  return MPI_Isend(buf, count, datatype, dest, tag, comm, nullptr);
+  MPI_Request r = MPI_REQUEST_NULL;
+  const int rc = MPI_Isend(buf, count, datatype, dest, tag, comm, &r);
+  return rc != MPI_SUCCESS ? rc : MPI_Wait(&r, MPI_STATUS_IGNORE);
 }
 
 int MPI_Recv(void* buf, int count, MPI_Datatype datatype, int source, int tag, MPI_Comm comm,
@@ -357,12 +710,20 @@ int MPI_Recv(void* buf, int count, MPI_Datatype datatype, int source, int tag, M
   return rc != MPI_SUCCESS ? rc : MPI_Wait(&r, status);
 }
 
+// The receive is posted before the send, so two ranks exchanging device buffers
+// with Sendrecv both make progress on their receive while waiting for the
+// acknowledgement of their send.
 int MPI_Sendrecv(const void* sendbuf, int sendcount, MPI_Datatype sendtype, int dest, int sendtag,
                  void* recvbuf, int recvcount, MPI_Datatype recvtype, int source, int recvtag,
                  MPI_Comm comm, MPI_Status* status) {
-  const int rc = MPI_Send(sendbuf, sendcount, sendtype, dest, sendtag, comm);
-  return rc != MPI_SUCCESS ? rc : MPI_Recv(recvbuf, recvcount, recvtype, source, recvtag, comm,
-                                           status);
+  MPI_Request r[2] = {MPI_REQUEST_NULL, MPI_REQUEST_NULL};
+  int rc = MPI_Irecv(recvbuf, recvcount, recvtype, source, recvtag, comm, &r[0]);
+  if (rc == MPI_SUCCESS) rc = MPI_Isend(sendbuf, sendcount, sendtype, dest, sendtag, comm, &r[1]);
+  if (rc != MPI_SUCCESS) return rc;
+  MPI_Status st[2];
+  rc = MPI_Waitall(2, r, st);
+  if (status) *status = st[0];
+  return rc;
 }
 
 }  // extern "C"

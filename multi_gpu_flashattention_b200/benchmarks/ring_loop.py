@@ -18,7 +18,7 @@ Backends
   nccl    NCCL send/recv per step (the reference's NCCL path)
   staged  device -> pinned host -> gloo send/recv -> device (the staged-MPI path)
 --payload-tokens T switches to the bf16 K+V payload [T x 8 heads x 128 x 2]
-filled with seeded uniform data (the sweep of BASELINE config 5); then the
+filled with seeded uniform data (the 1 MB - 256 MB payload sweep); then the
 precheck compares whole buffers with the expected owner's data.
 """
 from __future__ import annotations

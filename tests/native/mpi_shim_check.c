@@ -4,7 +4,9 @@
  * (source, tag), tags that overtake each other, Isend/Irecv with Waitall and
  * Testall, Sendrecv around the ring, Bcast from a non-zero root, Reduce
  * (MAX, MIN, SUM over double, float and int), Barrier, the shared-memory
- * split and Wtime. */
+ * split and Wtime; more sends in flight than a mailbox holds, a payload
+ * larger than a mailbox slot, and repeated barriers. Rank 0 also prints the
+ * host round-trip latency between ranks 0 and 1 ("latency_us <x>"). */
 #include <mpi.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -99,6 +101,54 @@ int main(int argc, char** argv) {
     CHECK(dmax[0] == size_ - 1 && dmax[1] == 0.0, "reduce max");
     CHECK(fmin == 1.0f, "reduce min");
     CHECK(isum == size_ * (size_ + 1) / 2, "reduce sum");
+  }
+
+  /* more sends in flight than a mailbox has slots: the excess wait in the
+   * sender's queue until the receiver frees slots */
+  enum { kMany = 40 };
+  int many_out[kMany], many_in[kMany];
+  MPI_Request mreq[2 * kMany];
+  for (int m = 0; m < kMany; ++m) {
+    many_out[m] = rank_ * 1000 + m;
+    MPI_Isend(&many_out[m], 1, MPI_INT, right, 11, MPI_COMM_WORLD, &mreq[m]);
+  }
+  for (int m = 0; m < kMany; ++m)
+    MPI_Irecv(&many_in[m], 1, MPI_INT, left, 11, MPI_COMM_WORLD, &mreq[kMany + m]);
+  MPI_Waitall(2 * kMany, mreq, MPI_STATUSES_IGNORE);
+  for (int m = 0; m < kMany; ++m) CHECK(many_in[m] == left * 1000 + m, "queued sends");
+
+  /* a payload larger than a slot */
+  enum { kBig = 300000 };
+  float* bo = (float*)malloc(kBig * sizeof(float));
+  float* bi = (float*)malloc(kBig * sizeof(float));
+  for (int i = 0; i < kBig; ++i) bo[i] = (float)(rank_ * 7 + i % 1000);
+  MPI_Sendrecv(bo, kBig, MPI_FLOAT, right, 12, bi, kBig, MPI_FLOAT, left, 12, MPI_COMM_WORLD,
+               MPI_STATUS_IGNORE);
+  for (int i = 0; i < kBig; ++i) CHECK(bi[i] == (float)(left * 7 + i % 1000), "large payload");
+  free(bo);
+  free(bi);
+
+  for (int i = 0; i < 200; ++i) CHECK(MPI_Barrier(MPI_COMM_WORLD) == MPI_SUCCESS, "barrier");
+
+  /* host round trip between ranks 0 and 1 */
+  if (rank_ < 2) {
+    const int peer = 1 - rank_, n = 2000;
+    double v = 0.0;
+    const double ts = MPI_Wtime();
+    for (int i = 0; i < n; ++i) {
+      if (rank_ == 0) {
+        MPI_Send(&v, 1, MPI_DOUBLE, peer, 13, MPI_COMM_WORLD);
+        MPI_Recv(&v, 1, MPI_DOUBLE, peer, 13, MPI_COMM_WORLD, MPI_STATUS_IGNORE);
+      } else {
+        MPI_Recv(&v, 1, MPI_DOUBLE, peer, 13, MPI_COMM_WORLD, MPI_STATUS_IGNORE);
+        v += 1.0;
+        MPI_Send(&v, 1, MPI_DOUBLE, peer, 13, MPI_COMM_WORLD);
+      }
+    }
+    if (rank_ == 0) {
+      CHECK(v == (double)n, "ping-pong");
+      printf("latency_us %.2f\n", (MPI_Wtime() - ts) / n * 1e6);
+    }
   }
 
   MPI_Barrier(MPI_COMM_WORLD);
