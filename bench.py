@@ -114,6 +114,37 @@ REF_BIN = os.environ.get("MGFA_REF_BIN", os.path.join(ROOT, "baseline", "_ref", 
 REF_HEAD_DIM = 64  # fixed in the reference's benchmarks (ring/attention/bench/*.cu)
 
 
+def run_child(cmd, env, timeout):
+    """Runs cmd in its own process group and returns (output, exit code). The
+    group is killed on timeout, and when this process is told to terminate
+    (the launcher ending a failed job), so no program outlives its rank."""
+    import signal
+
+    child = subprocess.Popen(cmd, env=env, stdout=subprocess.PIPE, stderr=subprocess.STDOUT,
+                             text=True, start_new_session=True)
+
+    def kill_group():
+        try:
+            os.killpg(child.pid, signal.SIGKILL)
+        except ProcessLookupError:
+            pass
+
+    def on_term(signum, frame):
+        kill_group()
+        raise SystemExit(128 + signum)
+
+    old = signal.signal(signal.SIGTERM, on_term)
+    try:
+        out, _ = child.communicate(timeout=timeout)
+        return out, child.returncode
+    except subprocess.TimeoutExpired:
+        kill_group()
+        child.communicate()
+        return f"timed out after {timeout} s", -1
+    finally:
+        signal.signal(signal.SIGTERM, old)
+
+
 def reference_arm(args):
     """Runs the reference's own NCCL ring-attention benchmark
     (ring/attention/bench/ring_attention_nccl_gpu_bench.cu, built unmodified by
@@ -149,12 +180,8 @@ def reference_arm(args):
     if sampler:
         sampler.start()
     t_wall = time.time()
-    try:
-        p = subprocess.run([exe, str(kv_bytes), str(args.warmup), str(args.steps)], env=env,
-                           capture_output=True, text=True, timeout=args.ref_timeout)
-        out, rc = p.stdout + p.stderr, p.returncode
-    except subprocess.TimeoutExpired:
-        out, rc = f"timed out after {args.ref_timeout} s", -1
+    out, rc = run_child([exe, str(kv_bytes), str(args.warmup), str(args.steps)], env,
+                        args.ref_timeout)
     wall = time.time() - t_wall
     clocks = sampler.stop() if sampler else None
     if rank != 0:
@@ -163,7 +190,8 @@ def reference_arm(args):
                   r"avg_merge=([\d.]+) avg_final=([\d.]+)", out)
     if rc != 0 or not m:
         tail = " | ".join(out.strip().splitlines()[-3:])
-        return unavailable(f"the reference benchmark failed (exit {rc}): {tail}"[:400])
+        unavailable(f"the reference benchmark failed (exit {rc}): {tail}"[:400])
+        return 1  # a failed rank ends the launcher's other ranks (and their programs)
     total, nccl, attn, merge, final = (float(x) for x in m.groups())
     flops = 4.0 * REF_HEAD_DIM * S * S  # every query row against every key, one head
     tflops = flops / (total * 1e-3) / 1e12

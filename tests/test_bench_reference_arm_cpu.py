@@ -56,3 +56,30 @@ def test_reference_arm_one_gpu_unavailable(tmp_path):
     rec, calls = _run(tmp_path, 1, 0)
     assert "unavailable" in rec and "at least 2 ranks" in rec["unavailable"]
     assert not calls.exists()
+
+
+HANG = """#!/bin/sh
+if [ "$RANK" = "0" ]; then echo "failing on purpose"; exit 3; fi
+sleep 600
+"""
+
+
+def test_failed_rank_ends_the_others(tmp_path):
+    """Rank 0's program fails while rank 1's would wait for it forever: the
+    launcher ends rank 1 and its program within seconds, not at the timeout."""
+    import time
+    exe = tmp_path / "ring_attention_nccl_gpu_bench"
+    exe.write_text(HANG)
+    exe.chmod(exe.stat().st_mode | stat.S_IEXEC)
+    env = dict(os.environ, MGFA_REF_BIN=str(tmp_path), OMP_NUM_THREADS="1")
+    t0 = time.time()
+    p = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+                        "--nproc-per-node=2", "--master-addr", "127.0.0.1",
+                        "--master-port", "29762", "bench.py", "--impl", "reference",
+                        "--gpus", "2", "--steps", "1", "--warmup", "3"],
+                       cwd=ROOT, env=env, capture_output=True, text=True, timeout=300)
+    assert time.time() - t0 < 120
+    line = [l for l in p.stdout.splitlines() if l.startswith("{")][0]
+    assert "failing on purpose" in json.loads(line)["unavailable"]
+    ps = subprocess.run(["pgrep", "-f", str(exe)], capture_output=True, text=True)
+    assert ps.stdout.strip() == "", "a reference program outlived its rank"
