@@ -16,7 +16,13 @@
 // has one writer per transition. Slot kinds, chosen by the sender:
 //  * 'H': a host payload small enough for the slot, inline; the send completes
 //    once posted.
-//  * 'S': a larger host payload, put in the store under the message's key.
+//  * 'B': a larger host payload, copied into a staging segment of shared
+//    memory that the sender keeps per destination (created on demand, grown
+//    when idle); the slot names the segment, the receiver copies out of it and
+//    marks the slot copied (state 2), which completes the send and frees the
+//    staging segment for the next message to that destination.
+//  * 'S': the same when no staging segment can be had (no room in
+//    /dev/shm): the payload goes into the store under the message's key.
 //  * 'D' (device buffer; MPI_SHIM_CUDA_IPC=0 turns it off): a CUDA IPC handle
 //    of the allocation, offset and length, and the handle of an IPC event
 //    recorded on the legacy default stream at the send. The receiver opens the
@@ -89,6 +95,7 @@ struct mgfa_mpi_request {
   uint64_t seq = 0;
   char slot_kind = 'H';
   std::vector<uint8_t> record;   // send: the slot contents still to post
+  const void* send_buf = nullptr; // send 'B': the payload, read when posted
   Slot* slot = nullptr;          // the slot this request posted or consumed
   cudaEvent_t copy_done = nullptr;
 };
@@ -103,10 +110,23 @@ struct IpcRecord {  // contents of a 'D' slot
   uint64_t offset = 0, bytes = 0;
 };
 
+struct BulkRecord {  // contents of a 'B' slot
+  char name[64];
+  uint64_t segment_bytes = 0, bytes = 0;
+};
+
+struct Segment {  // a named shared-memory segment, mapped in this process
+  std::string name;
+  char* ptr = nullptr;
+  size_t size = 0;
+  bool busy = false;  // staging: a posted message still lives in it
+};
+
 using mgfa_mpi_shim::kInline;
 using mgfa_mpi_shim::kMaxWorld;
 using mgfa_mpi_shim::kSlots;
 static_assert(sizeof(IpcRecord) <= kInline, "IPC record fits a slot");
+static_assert(sizeof(BulkRecord) <= kInline, "bulk record fits a slot");
 
 struct SegmentHeader {
   std::atomic<uint32_t> barrier_count;
@@ -128,6 +148,9 @@ struct State {
   size_t seg_bytes = 0;
   std::vector<int> next_slot;              // per destination: where the free-slot scan starts
   std::vector<mgfa_mpi_request*> pending;  // started and not yet complete
+  std::vector<Segment> staging;            // per destination ('B' sends)
+  std::vector<Segment> mapped;             // per source: its staging segment, mapped here
+  uint64_t staging_serial = 0;
   // device side, created on first use on the current device
   cudaEvent_t send_event = nullptr;
   cudaIpcEventHandle_t send_event_handle{};
@@ -177,11 +200,15 @@ bool on_device(const void* p) {
   return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
 }
 
+void read_into(void* host, const void* buf, size_t bytes) {
+  if (bytes == 0) return;
+  if (on_device(buf)) cuda_ok(cudaMemcpy(host, buf, bytes, cudaMemcpyDeviceToHost), "D2H");
+  else std::memcpy(host, buf, bytes);
+}
+
 std::vector<uint8_t> read_buffer(const void* buf, size_t bytes) {
   std::vector<uint8_t> v(bytes);
-  if (bytes == 0) return v;
-  if (on_device(buf)) cuda_ok(cudaMemcpy(v.data(), buf, bytes, cudaMemcpyDeviceToHost), "D2H");
-  else std::memcpy(v.data(), buf, bytes);
+  read_into(v.data(), buf, bytes);
   return v;
 }
 
@@ -255,27 +282,100 @@ std::vector<uint8_t> device_record(const void* buf, size_t bytes) {
   return v;
 }
 
+// ------------------------------------------------------------------ staging
+void unmap(Segment& seg, bool unlink) {
+  if (seg.ptr) munmap(seg.ptr, seg.size);
+  if (unlink && !seg.name.empty()) shm_unlink(seg.name.c_str());
+  seg = Segment{};
+}
+
+// A staging segment of at least `bytes` for sends to `dst`; false when
+// /dev/shm has no room (the caller falls back to the store).
+bool ensure_staging(int dst, size_t bytes) {
+  Segment& seg = g->staging[size_t(dst)];
+  if (seg.ptr && seg.size >= bytes) return true;
+  unmap(seg, true);  // idle: the receiver has copied everything out of it
+  const size_t size = (bytes + (1u << 20) - 1) & ~size_t((1u << 20) - 1);
+  const std::string name = "/mgfa_mpi_" + std::to_string(getpid()) + "_" + std::to_string(dst) +
+                           "_" + std::to_string(g->staging_serial++);
+  const int fd = shm_open(name.c_str(), O_CREAT | O_EXCL | O_RDWR, 0600);
+  if (fd < 0) return false;
+  // reserve the pages now, so that a full /dev/shm is an error here rather
+  // than a bus error on first touch
+  void* p = MAP_FAILED;
+  if (posix_fallocate(fd, 0, off_t(size)) == 0)
+    p = mmap(nullptr, size, PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0);
+  close(fd);
+  if (p == MAP_FAILED) {
+    shm_unlink(name.c_str());
+    return false;
+  }
+  seg.name = name;
+  seg.ptr = static_cast<char*>(p);
+  seg.size = size;
+  return true;
+}
+
+const Segment& map_from(int src, const BulkRecord& r) {
+  Segment& seg = g->mapped[size_t(src)];
+  if (seg.ptr && seg.name == r.name) return seg;
+  unmap(seg, false);  // the sender replaced it: it was idle
+  const int fd = shm_open(r.name, O_RDWR, 0600);
+  if (fd < 0) throw std::runtime_error(std::string("cannot open staging segment ") + r.name);
+  void* p = mmap(nullptr, r.segment_bytes, PROT_READ, MAP_SHARED, fd, 0);
+  close(fd);
+  if (p == MAP_FAILED) throw std::runtime_error("cannot map a staging segment");
+  seg.name = r.name;
+  seg.ptr = static_cast<char*>(p);
+  seg.size = r.segment_bytes;
+  return seg;
+}
+
 // ------------------------------------------------------------------ sends
 // Posts a queued send into a free slot of the mailbox to its destination.
 bool try_post(mgfa_mpi_request* q) {
-  Slot* box = g->mailbox(g->rank, q->source);
-  int& start = g->next_slot[q->source];
-  for (int k = 0; k < kSlots; ++k) {
-    Slot* s = box + (start + k) % kSlots;
-    if (s->state.load(std::memory_order_acquire) != 0) continue;
-    s->kind = uint32_t(q->slot_kind);
-    s->tag = q->tag;
-    s->seq = q->seq;
-    s->len = uint32_t(q->slot_kind == 'H' ? q->record.size() : q->bytes);
-    if (!q->record.empty()) std::memcpy(s->data, q->record.data(), q->record.size());
-    s->state.store(1, std::memory_order_release);
-    start = (start + k + 1) % kSlots;
-    q->record.clear();
-    q->slot = s;
-    q->phase = q->slot_kind == 'D' ? mgfa_mpi_request::kPosted : mgfa_mpi_request::kDone;
-    return true;
+  using R = mgfa_mpi_request;
+  const int dst = q->source;
+  if (q->slot_kind == 'B' && g->staging[size_t(dst)].busy) return false;
+  Slot* box = g->mailbox(g->rank, dst);
+  int& start = g->next_slot[size_t(dst)];
+  Slot* s = nullptr;
+  int k = 0;
+  for (; k < kSlots; ++k) {
+    Slot* c = box + (start + k) % kSlots;
+    if (c->state.load(std::memory_order_acquire) == 0) {
+      s = c;
+      break;
+    }
   }
-  return false;
+  if (!s) return false;
+  if (q->slot_kind == 'B') {
+    if (ensure_staging(dst, q->bytes)) {
+      Segment& seg = g->staging[size_t(dst)];
+      read_into(seg.ptr, q->send_buf, q->bytes);
+      BulkRecord r;
+      std::snprintf(r.name, sizeof(r.name), "%s", seg.name.c_str());
+      r.segment_bytes = seg.size;
+      r.bytes = q->bytes;
+      q->record.assign(reinterpret_cast<const uint8_t*>(&r),
+                       reinterpret_cast<const uint8_t*>(&r) + sizeof(r));
+      seg.busy = true;
+    } else {
+      q->slot_kind = 'S';
+      g->store->set(msg_key(g->rank, dst, q->tag, q->seq), read_buffer(q->send_buf, q->bytes));
+    }
+  }
+  s->kind = uint32_t(q->slot_kind);
+  s->tag = q->tag;
+  s->seq = q->seq;
+  s->len = uint32_t(q->slot_kind == 'H' ? q->record.size() : q->bytes);
+  if (!q->record.empty()) std::memcpy(s->data, q->record.data(), q->record.size());
+  s->state.store(1, std::memory_order_release);
+  start = (start + k + 1) % kSlots;
+  q->record.clear();
+  q->slot = s;
+  q->phase = (q->slot_kind == 'D' || q->slot_kind == 'B') ? R::kPosted : R::kDone;
+  return true;
 }
 
 // ------------------------------------------------------------------ receives
@@ -324,9 +424,10 @@ bool advance(mgfa_mpi_request* q) {
   if (q->kind == R::kSend) {
     if (q->phase == R::kQueued && !try_post(q)) return false;
     if (q->phase == R::kDone) return true;
-    // 'D': the receiver marks the slot copied; this side frees it
+    // 'D', 'B': the receiver marks the slot copied; this side frees it
     if (q->slot->state.load(std::memory_order_acquire) != 2) return false;
     q->slot->state.store(0, std::memory_order_release);
+    if (q->slot_kind == 'B') g->staging[size_t(q->source)].busy = false;
     q->phase = R::kDone;
     return true;
   }
@@ -346,6 +447,16 @@ bool advance(mgfa_mpi_request* q) {
       g->store->deleteKey(key);
       write_buffer(q->buf, v.data(), v.size(), q->bytes);
       s->state.store(0, std::memory_order_release);
+      q->phase = R::kDone;
+      return true;
+    }
+    if (s->kind == 'B') {
+      BulkRecord r;
+      std::memcpy(&r, s->data, sizeof(r));
+      const Segment& seg = map_from(q->source, r);
+      if (r.bytes > seg.size) throw std::runtime_error("malformed staging record");
+      write_buffer(q->buf, reinterpret_cast<const uint8_t*>(seg.ptr), r.bytes, q->bytes);
+      s->state.store(2, std::memory_order_release);
       q->phase = R::kDone;
       return true;
     }
@@ -433,6 +544,8 @@ void map_segment() {
   store_barrier("mapped");
   if (g->rank == 0) shm_unlink(name.c_str());  // lives on while mapped
   g->next_slot.assign(size_t(g->world), 0);
+  g->staging.assign(size_t(g->world), Segment{});
+  g->mapped.assign(size_t(g->world), Segment{});
 }
 
 }  // namespace
@@ -492,6 +605,8 @@ int MPI_Finalize(void) {
   for (auto& e : g->opened_events) cudaEventDestroy(e.second);
   if (g->send_event) cudaEventDestroy(g->send_event);
   if (g->copy_stream) cudaStreamDestroy(g->copy_stream);
+  for (auto& m : g->mapped) unmap(m, false);
+  for (auto& st : g->staging) unmap(st, true);  // every receiver is past the barrier
   if (g->seg) munmap(g->seg, g->seg_bytes);
   delete g;
   g = nullptr;
@@ -624,8 +739,8 @@ int MPI_Isend(const void* buf, int count, MPI_Datatype datatype, int dest, int t
       r->slot_kind = 'H';
       r->record = read_buffer(buf, r->bytes);
     } else {
-      r->slot_kind = 'S';
-      g->store->set(msg_key(g->rank, dest, tag, r->seq), read_buffer(buf, r->bytes));
+      r->slot_kind = 'B';  // copied into the staging segment when posted
+      r->send_buf = buf;
     }
     r->phase = mgfa_mpi_request::kQueued;
     if (!try_post(r) || r->phase != mgfa_mpi_request::kDone) g->pending.push_back(r);

@@ -6,7 +6,8 @@
  * (MAX, MIN, SUM over double, float and int), Barrier, the shared-memory
  * split and Wtime; more sends in flight than a mailbox holds, a payload
  * larger than a mailbox slot, and repeated barriers. Rank 0 also prints the
- * host round-trip latency between ranks 0 and 1 ("latency_us <x>"). */
+ * host round-trip latency between ranks 0 and 1 ("latency_us <x>") and the
+ * one-way rate of 16 MB host messages between them ("bulk_GBps <x>"). */
 #include <mpi.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -149,6 +150,24 @@ int main(int argc, char** argv) {
       CHECK(v == (double)n, "ping-pong");
       printf("latency_us %.2f\n", (MPI_Wtime() - ts) / n * 1e6);
     }
+    /* 16 MB messages, bounced back and forth: one-way bytes per second */
+    const size_t nb = (size_t)16 << 20;
+    const int reps = 10;
+    char* big = (char*)malloc(nb);
+    for (size_t i = 0; i < nb; ++i) big[i] = (char)(i * 7 + 3);
+    const double tb = MPI_Wtime();
+    for (int i = 0; i < reps; ++i) {
+      if (rank_ == 0) {
+        MPI_Send(big, (int)nb, MPI_BYTE, peer, 14, MPI_COMM_WORLD);
+        MPI_Recv(big, (int)nb, MPI_BYTE, peer, 14, MPI_COMM_WORLD, MPI_STATUS_IGNORE);
+      } else {
+        MPI_Recv(big, (int)nb, MPI_BYTE, peer, 14, MPI_COMM_WORLD, MPI_STATUS_IGNORE);
+        MPI_Send(big, (int)nb, MPI_BYTE, peer, 14, MPI_COMM_WORLD);
+      }
+    }
+    for (size_t i = 0; i < nb; i += 4099) CHECK(big[i] == (char)(i * 7 + 3), "bulk payload");
+    if (rank_ == 0) printf("bulk_GBps %.2f\n", 2.0 * reps * nb / (MPI_Wtime() - tb) / 1e9);
+    free(big);
   }
 
   MPI_Barrier(MPI_COMM_WORLD);
