@@ -24,12 +24,14 @@
 //  * 'S': the same when no staging segment can be had (no room in
 //    /dev/shm): the payload goes into the store under the message's key.
 //  * 'D' (device buffer; MPI_SHIM_CUDA_IPC=0 turns it off): a CUDA IPC handle
-//    of the allocation, offset and length, and the handle of an IPC event
-//    recorded on the legacy default stream at the send. The receiver opens the
-//    handle (once per allocation), orders a copy-engine copy after that event
-//    on its own non-blocking stream, and marks the slot copied when the copy
-//    has finished. The send completes when the sender sees the mark; only then
-//    may it reuse the buffer. The payload crosses NVLink directly.
+//    of the allocation with its buffer id, offset and length, and the handle
+//    of an IPC event (one from a pool per send in flight) recorded on the
+//    legacy default stream at the send. The receiver opens the handle once
+//    per (sender, buffer id), orders a copy-engine copy after that event on
+//    its own non-blocking stream, and marks the slot copied when the copy has
+//    finished. The send completes when the sender sees the mark; only then may
+//    it reuse the buffer or the event. The payload crosses NVLink directly.
+//    Allocations that cannot be exported (memory pools) are staged as 'B'.
 //
 // Progress: every wait, test and barrier advances all pending requests of the
 // process (post queued sends, match slots, start copies, poll their events,
@@ -96,6 +98,7 @@ struct mgfa_mpi_request {
   char slot_kind = 'H';
   std::vector<uint8_t> record;   // send: the slot contents still to post
   const void* send_buf = nullptr; // send 'B': the payload, read when posted
+  int event = -1;                 // send 'D': the pool event recorded at the send
   Slot* slot = nullptr;          // the slot this request posted or consumed
   cudaEvent_t copy_done = nullptr;
 };
@@ -107,7 +110,17 @@ using Clock = std::chrono::steady_clock;
 struct IpcRecord {  // contents of a 'D' slot
   cudaIpcMemHandle_t mem;
   cudaIpcEventHandle_t event;
-  uint64_t offset = 0, bytes = 0;
+  uint64_t buffer_id = 0, offset = 0, bytes = 0;
+};
+
+struct Export {  // a device allocation of this process, exported for IPC
+  char* base = nullptr;
+  cudaIpcMemHandle_t handle;
+};
+
+struct IpcEvent {
+  cudaEvent_t event = nullptr;
+  cudaIpcEventHandle_t handle;
 };
 
 struct BulkRecord {  // contents of a 'B' slot
@@ -152,11 +165,13 @@ struct State {
   std::vector<Segment> mapped;             // per source: its staging segment, mapped here
   uint64_t staging_serial = 0;
   // device side, created on first use on the current device
-  cudaEvent_t send_event = nullptr;
-  cudaIpcEventHandle_t send_event_handle{};
+  std::map<uint64_t, Export> exports;     // buffer id -> export
+  std::vector<IpcEvent> events;           // pool; a send holds one until it completes
+  std::vector<int> free_events;
   cudaStream_t copy_stream = nullptr;
-  std::map<std::string, char*> opened_mem;            // handle bytes -> mapped base
+  std::map<std::string, char*> opened_mem;            // "<src>/<buffer id>" -> mapped base
   std::map<std::string, cudaEvent_t> opened_events;   // handle bytes -> event
+  bool warned_ipc = false;
 
   SegmentHeader* header() const { return static_cast<SegmentHeader*>(seg); }
   Slot* mailbox(int src, int dst) const {
@@ -242,41 +257,66 @@ template <class F>
 void spin_until(F done, const char* what);
 
 // ------------------------------------------------------------------ device sends
-char* allocation_base(const void* p, size_t* size) {
-  using Fn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
-  static Fn fn = nullptr;
-  if (!fn) {
-    cudaDriverEntryPointQueryResult q;
-    void* f = nullptr;
-    cuda_ok(cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &f, 12000, cudaEnableDefault,
-                                             &q),
-            "driver entry point");
-    if (q != cudaDriverEntryPointSuccess || !f)
-      throw std::runtime_error("cuMemGetAddressRange unavailable");
-    fn = reinterpret_cast<Fn>(f);
-  }
-  CUdeviceptr base = 0;
-  if (fn(&base, size, reinterpret_cast<CUdeviceptr>(p)) != CUDA_SUCCESS)
-    throw std::runtime_error("cuMemGetAddressRange failed");
-  return reinterpret_cast<char*>(base);
+template <class Fn>
+Fn driver_fn(const char* name) {
+  cudaDriverEntryPointQueryResult q;
+  void* f = nullptr;
+  cuda_ok(cudaGetDriverEntryPointByVersion(name, &f, 12000, cudaEnableDefault, &q),
+          "driver entry point");
+  if (q != cudaDriverEntryPointSuccess || !f)
+    throw std::runtime_error(std::string(name) + " unavailable");
+  return reinterpret_cast<Fn>(f);
 }
 
-std::vector<uint8_t> device_record(const void* buf, size_t bytes) {
-  if (!g->send_event) {
-    cuda_ok(cudaEventCreateWithFlags(&g->send_event,
-                                     cudaEventDisableTiming | cudaEventInterprocess),
+// The allocation holding p: its IPC export (cached per buffer id, which the
+// driver makes unique per allocation in this process, so a freed and
+// reallocated range is exported afresh).
+const Export& export_allocation(const void* p, uint64_t* buffer_id) {
+  using RangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+  using AttrFn = CUresult (*)(void*, CUpointer_attribute, CUdeviceptr);
+  static const RangeFn range = driver_fn<RangeFn>("cuMemGetAddressRange");
+  static const AttrFn attr = driver_fn<AttrFn>("cuPointerGetAttribute");
+  const CUdeviceptr dp = reinterpret_cast<CUdeviceptr>(p);
+  unsigned long long id = 0;
+  if (attr(&id, CU_POINTER_ATTRIBUTE_BUFFER_ID, dp) != CUDA_SUCCESS)
+    throw std::runtime_error("no buffer id for a device pointer");
+  *buffer_id = id;
+  auto it = g->exports.find(id);
+  if (it != g->exports.end()) return it->second;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, dp) != CUDA_SUCCESS) throw std::runtime_error("no allocation range");
+  Export e;
+  e.base = reinterpret_cast<char*>(base);
+  cuda_ok(cudaIpcGetMemHandle(&e.handle, e.base), "memory handle");
+  return g->exports.emplace(id, e).first->second;
+}
+
+// An interprocess event from the pool (one per send in flight).
+int take_event() {
+  if (g->free_events.empty()) {
+    IpcEvent e;
+    cuda_ok(cudaEventCreateWithFlags(&e.event, cudaEventDisableTiming | cudaEventInterprocess),
             "event create");
-    cuda_ok(cudaIpcGetEventHandle(&g->send_event_handle, g->send_event), "event handle");
+    cuda_ok(cudaIpcGetEventHandle(&e.handle, e.event), "event handle");
+    g->events.push_back(e);
+    g->free_events.push_back(int(g->events.size()) - 1);
   }
-  size_t alloc = 0;
-  char* base = allocation_base(buf, &alloc);
+  const int i = g->free_events.back();
+  g->free_events.pop_back();
+  return i;
+}
+
+std::vector<uint8_t> device_record(const void* buf, size_t bytes, int* event) {
   IpcRecord r;
-  cuda_ok(cudaIpcGetMemHandle(&r.mem, base), "memory handle");
-  r.event = g->send_event_handle;
-  r.offset = uint64_t(static_cast<const char*>(buf) - base);
+  const Export& e = export_allocation(buf, &r.buffer_id);
+  r.mem = e.handle;
+  r.offset = uint64_t(static_cast<const char*>(buf) - e.base);
   r.bytes = bytes;
+  *event = take_event();
+  r.event = g->events[size_t(*event)].handle;
   // everything the program queued before the send (legacy stream semantics)
-  cuda_ok(cudaEventRecord(g->send_event, cudaStreamLegacy), "event record");
+  cuda_ok(cudaEventRecord(g->events[size_t(*event)].event, cudaStreamLegacy), "event record");
   std::vector<uint8_t> v(sizeof(r));
   std::memcpy(v.data(), &r, sizeof(r));
   return v;
@@ -383,7 +423,7 @@ void start_ipc_copy(mgfa_mpi_request* q, const IpcRecord& r) {
   if (r.bytes > q->bytes) throw std::runtime_error("message longer than the receive buffer");
   if (!g->copy_stream)
     cuda_ok(cudaStreamCreateWithFlags(&g->copy_stream, cudaStreamNonBlocking), "stream");
-  const std::string mk = bytes_of(&r.mem, sizeof(r.mem));
+  const std::string mk = std::to_string(q->source) + "/" + std::to_string(r.buffer_id);
   auto m = g->opened_mem.find(mk);
   if (m == g->opened_mem.end()) {
     void* p = nullptr;
@@ -428,6 +468,8 @@ bool advance(mgfa_mpi_request* q) {
     if (q->slot->state.load(std::memory_order_acquire) != 2) return false;
     q->slot->state.store(0, std::memory_order_release);
     if (q->slot_kind == 'B') g->staging[size_t(q->source)].busy = false;
+    if (q->event >= 0) g->free_events.push_back(q->event);
+    q->event = -1;
     q->phase = R::kDone;
     return true;
   }
@@ -603,7 +645,7 @@ int MPI_Finalize(void) {
   }
   for (auto& m : g->opened_mem) cudaIpcCloseMemHandle(m.second);
   for (auto& e : g->opened_events) cudaEventDestroy(e.second);
-  if (g->send_event) cudaEventDestroy(g->send_event);
+  for (auto& e : g->events) cudaEventDestroy(e.event);
   if (g->copy_stream) cudaStreamDestroy(g->copy_stream);
   for (auto& m : g->mapped) unmap(m, false);
   for (auto& st : g->staging) unmap(st, true);  // every receiver is past the barrier
@@ -732,16 +774,21 @@ int MPI_Isend(const void* buf, int count, MPI_Datatype datatype, int dest, int t
     r->source = dest;
     r->tag = tag;
     r->seq = g->sent[{dest, tag}]++;
+    r->slot_kind = r->bytes <= kInline ? 'H' : 'B';
     if (g->ipc && r->bytes && on_device(buf)) {
-      r->slot_kind = 'D';
-      r->record = device_record(buf, r->bytes);
-    } else if (r->bytes <= kInline) {
-      r->slot_kind = 'H';
-      r->record = read_buffer(buf, r->bytes);
-    } else {
-      r->slot_kind = 'B';  // copied into the staging segment when posted
-      r->send_buf = buf;
+      try {
+        r->record = device_record(buf, r->bytes, &r->event);
+        r->slot_kind = 'D';
+      } catch (const std::exception& e) {  // e.g. memory-pool allocations: stage instead
+        cudaGetLastError();
+        if (!g->warned_ipc)
+          std::fprintf(stderr, "[mpi shim rank %d] no CUDA IPC for a device buffer (%s); "
+                       "staging through host memory\n", g->rank, e.what());
+        g->warned_ipc = true;
+      }
     }
+    if (r->slot_kind == 'H') r->record = read_buffer(buf, r->bytes);
+    if (r->slot_kind == 'B') r->send_buf = buf;  // copied into the staging segment when posted
     r->phase = mgfa_mpi_request::kQueued;
     if (!try_post(r) || r->phase != mgfa_mpi_request::kDone) g->pending.push_back(r);
     *request = r;
