@@ -8,6 +8,7 @@
 #
 #   benchmarks/build_reference.sh            # build everything
 #   benchmarks/build_reference.sh --cpu-only # rattn_demo, verify_full, ring_test
+#   benchmarks/build_reference.sh --print-src # where the reference tree is read from
 #   REF_SRC=/path/to/reference OUT=dir benchmarks/build_reference.sh
 # Exit status 2: no reference tree at REF_SRC.
 set -euo pipefail
@@ -18,6 +19,7 @@ PY=${PY:-python}
 NVCC=${NVCC:-nvcc}
 CUDA_HOME=${CUDA_HOME:-/usr/local/cuda}
 [ -d "$REF/ring" ] || { echo "reference tree not found at $REF" >&2; exit 2; }
+if [ "${1:-}" = "--print-src" ]; then echo "$REF"; exit 0; fi
 
 make -s mpi-shim
 SHIM_INC="$PWD/csrc/mpi_shim"

@@ -5,7 +5,8 @@ its MPI programs run under torchrun.
 
 * rattn_demo (csrc/sched/rattn_demo.cpp) prints byte-identical reports to the
   reference's workload/demo.c over a grid of --seq/--gpus/--block/--mask/
-  --alpha/--beta values.
+  --alpha/--beta values, and benchmarks/run_experiments.sh prints the same
+  tables as the reference's workload/run_experiments.sh.
 * verify_full (csrc/bench/verify_full.cpp) gives the same report as the
   reference's ring/attention/verify_full.c on the deterministic dump sets.
 * ring/ring_test.c, the reference's pure-MPI ring step, runs on the shim at 2
@@ -82,6 +83,19 @@ def test_rattn_demo_matches_reference(ref_bin, our_bin):
         if ref != ours:
             bad.append(a)
     assert not bad, f"{len(bad)} of {len(DEMO_ARGS)} differ, first: {bad[0]!r}"
+
+
+def test_experiment_tables_match_reference(tmp_path, ref_bin, our_bin):
+    src = subprocess.run(["bash", os.path.join(ROOT, "benchmarks/build_reference.sh"),
+                          "--print-src"], capture_output=True, text=True).stdout.strip()
+    os.symlink(os.path.join(ref_bin, "rattn_demo"), tmp_path / "demo")
+    ref = subprocess.run(["bash", os.path.join(src, "workload", "run_experiments.sh")],
+                         cwd=tmp_path, capture_output=True, text=True, timeout=300)
+    ours = subprocess.run(["bash", os.path.join(ROOT, "benchmarks/run_experiments.sh")],
+                          capture_output=True, text=True, timeout=300)
+    assert ref.returncode == 0 and ours.returncode == 0, ref.stderr + ours.stderr
+    assert ours.stdout.strip() == ref.stdout.strip()
+    assert ours.stdout.count("\n") > 20
 
 
 @pytest.mark.parametrize("name", list(CASES))
