@@ -7,6 +7,10 @@
 #
 # Env: NP (2) SIZE (262144) WARMUP (1) ITERS (1) ABS_TOL (1e-3) REL_TOL (1e-5)
 #      RESULTS_ROOT (results) RUN_LABEL (timestamp) INIT (legacy|randn) CHECK_P2P (1)
+#      CHECK_REFERENCE (1 when baseline/_ref/bin holds the reference's programs,
+#      built by benchmarks/build_reference.sh; legacy inputs only): also run the
+#      reference's own NCCL and CUDA-aware overlap programs with dumps, check
+#      them with verify_full, and compare this framework's dumps with theirs.
 set -euo pipefail
 cd "$(dirname "$0")/.."
 export PYTHONPATH="$PWD${PYTHONPATH:+:$PYTHONPATH}"
@@ -70,4 +74,20 @@ if [[ "${CHECK_P2P:-1}" == 1 ]]; then
   run_bench ce --backend ce
   compare_pair nccl_vs_p2p "$OUT/nccl" "$OUT/p2p"
   compare_pair nccl_vs_ce "$OUT/nccl" "$OUT/ce"
+fi
+REF_BIN="$PWD/baseline/_ref/bin"
+if [[ "${CHECK_REFERENCE:-1}" == 1 && "$INIT" == legacy && -x "$REF_BIN/ring_attention_nccl_gpu_bench" ]]; then
+  run_reference() {  # label, program
+    local dir="$OUT/$1"
+    mkdir -p "$dir"
+    (cd "$dir" && ATTENTION_DUMP_OUTPUT=1 timeout -k 30 600 python -m torch.distributed.run \
+        --nnodes=1 --nproc-per-node "$NP" --master-addr 127.0.0.1 --master-port "$PORT" \
+        --no-python "$REF_BIN/$2" "$SIZE" "$WARMUP" "$ITERS" > bench.log 2>&1)
+    PORT=$((PORT + 1))
+    ./build/bin/verify_full "$dir" "$NP" "$SIZE" | tee "$dir/verify.log" | tail -1
+  }
+  run_reference reference_nccl ring_attention_nccl_gpu_bench
+  run_reference reference_cuda_aware_overlap ring_attention_cuda_aware_Isendrecv_overlap_gpu_bench
+  compare_pair nccl_vs_reference_nccl "$OUT/nccl" "$OUT/reference_nccl"
+  compare_pair nccl_overlap_vs_reference_overlap "$OUT/nccl_overlap" "$OUT/reference_cuda_aware_overlap"
 fi
