@@ -7,7 +7,13 @@
  * split and Wtime; more sends in flight than a mailbox holds, a payload
  * larger than a mailbox slot, and repeated barriers. Rank 0 also prints the
  * host round-trip latency between ranks 0 and 1 ("latency_us <x>") and the
- * one-way rate of 16 MB host messages between them ("bulk_GBps <x>"). */
+ * one-way rate of 16 MB host messages between them ("bulk_GBps <x>").
+ * Where a CUDA device is visible, the device section sends cudaMalloc'd
+ * buffers (CUDA IPC in the shim) around the ring, from an interior pointer
+ * and with Sendrecv and Isend/Irecv, and prints "rank <r> device OK";
+ * otherwise "rank <r> device skipped". Ranks share the visible devices
+ * round-robin. */
+#include <cuda_runtime.h>
 #include <mpi.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -168,6 +174,49 @@ int main(int argc, char** argv) {
     for (size_t i = 0; i < nb; i += 4099) CHECK(big[i] == (char)(i * 7 + 3), "bulk payload");
     if (rank_ == 0) printf("bulk_GBps %.2f\n", 2.0 * reps * nb / (MPI_Wtime() - tb) / 1e9);
     free(big);
+  }
+
+  /* device buffers */
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) == cudaSuccess && ndev > 0) {
+    CHECK(cudaSetDevice(rank_ % ndev) == cudaSuccess, "set device");
+    enum { kN = 1 << 20, kOff = 1234 };
+    float *d_a = NULL, *d_b = NULL;
+    CHECK(cudaMalloc((void**)&d_a, (kN + kOff) * sizeof(float)) == cudaSuccess, "malloc");
+    CHECK(cudaMalloc((void**)&d_b, kN * sizeof(float)) == cudaSuccess, "malloc");
+    float* h = (float*)malloc(kN * sizeof(float));
+    for (int i = 0; i < kN; ++i) h[i] = (float)(rank_ * 4096 + i % 4096);
+    CHECK(cudaMemcpy(d_a + kOff, h, kN * sizeof(float), cudaMemcpyHostToDevice) == cudaSuccess,
+          "H2D");
+    /* rotate the buffer once around the ring; step s holds rank (r - s - 1)'s data */
+    float* cur = d_a + kOff;  /* an interior pointer of its allocation */
+    float* nxt = d_b;
+    for (int s = 0; s < size_; ++s) {
+      const int owner = (rank_ - s - 1 + 2 * size_) % size_;
+      if (s % 2 == 0) {
+        MPI_Sendrecv(cur, kN, MPI_FLOAT, right, 20 + s, nxt, kN, MPI_FLOAT, left, 20 + s,
+                     MPI_COMM_WORLD, MPI_STATUS_IGNORE);
+      } else {
+        MPI_Request dr[2];
+        MPI_Irecv(nxt, kN, MPI_FLOAT, left, 20 + s, MPI_COMM_WORLD, &dr[0]);
+        MPI_Isend(cur, kN, MPI_FLOAT, right, 20 + s, MPI_COMM_WORLD, &dr[1]);
+        MPI_Waitall(2, dr, MPI_STATUSES_IGNORE);
+      }
+      CHECK(cudaMemcpy(h, nxt, kN * sizeof(float), cudaMemcpyDeviceToHost) == cudaSuccess,
+            "D2H");
+      for (int i = 0; i < kN; i += 997)
+        CHECK(h[i] == (float)(owner * 4096 + i % 4096), "device payload");
+      float* t = cur;
+      cur = nxt;
+      nxt = t;
+    }
+    cudaFree(d_a);
+    cudaFree(d_b);
+    free(h);
+    printf("rank %d device OK\n", rank_);
+  } else {
+    cudaGetLastError();
+    printf("rank %d device skipped\n", rank_);
   }
 
   MPI_Barrier(MPI_COMM_WORLD);

@@ -12,7 +12,8 @@ its MPI programs run under torchrun.
 * ring/ring_test.c, the reference's pure-MPI ring step, runs on the shim at 2
   and 3 ranks and receives its left neighbour's buffer.
 * tests/native/mpi_shim_check.c checks the shim's ordering, tag matching,
-  nonblocking completion and collectives at 3 ranks.
+  nonblocking completion, staging of large messages and collectives at 3
+  ranks (and device buffers where a GPU is visible).
 """
 import os
 import re
@@ -129,10 +130,16 @@ def test_reference_ring_test_on_shim(ref_bin, nproc, port):
 
 def test_shim_semantics(tmp_path, shim):
     exe = str(tmp_path / "mpi_shim_check")
+    cuda = os.environ.get("CUDA_HOME", "/usr/local/cuda")
     subprocess.check_call(["gcc", "-O2", "-std=gnu11", "-I", os.path.join(ROOT, "csrc/mpi_shim"),
+                           "-I", os.path.join(cuda, "include"),
                            "-o", exe, os.path.join(ROOT, "tests/native/mpi_shim_check.c"),
-                           "-L", shim, f"-Wl,-rpath,{shim}", "-lmpi_shim"])
+                           "-L", shim, f"-Wl,-rpath,{shim}", "-lmpi_shim",
+                           "-L", os.path.join(cuda, "lib64"),
+                           f"-Wl,-rpath,{os.path.join(cuda, 'lib64')}", "-lcudart"])
     p = _torchrun(3, exe, 29743)
     assert p.returncode == 0, p.stdout + p.stderr
     for r in range(3):
         assert f"rank {r} OK" in p.stdout, p.stdout
+        assert (f"rank {r} device skipped" in p.stdout or f"rank {r} device OK" in p.stdout), \
+            p.stdout
