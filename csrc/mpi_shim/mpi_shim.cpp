@@ -55,6 +55,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <exception>
 #include <map>
 #include <memory>
 #include <stdexcept>
@@ -111,6 +112,7 @@ struct IpcRecord {  // contents of a 'D' slot
   cudaIpcMemHandle_t mem;
   cudaIpcEventHandle_t event;
   uint64_t buffer_id = 0, offset = 0, bytes = 0;
+  uint64_t address = 0;  // the sender's pointer, used as is when sender == receiver
 };
 
 struct Export {  // a device allocation of this process, exported for IPC
@@ -313,6 +315,7 @@ std::vector<uint8_t> device_record(const void* buf, size_t bytes, int* event) {
   r.mem = e.handle;
   r.offset = uint64_t(static_cast<const char*>(buf) - e.base);
   r.bytes = bytes;
+  r.address = reinterpret_cast<uint64_t>(buf);
   *event = take_event();
   r.event = g->events[size_t(*event)].handle;
   // everything the program queued before the send (legacy stream semantics)
@@ -423,24 +426,34 @@ void start_ipc_copy(mgfa_mpi_request* q, const IpcRecord& r) {
   if (r.bytes > q->bytes) throw std::runtime_error("message longer than the receive buffer");
   if (!g->copy_stream)
     cuda_ok(cudaStreamCreateWithFlags(&g->copy_stream, cudaStreamNonBlocking), "stream");
-  const std::string mk = std::to_string(q->source) + "/" + std::to_string(r.buffer_id);
-  auto m = g->opened_mem.find(mk);
-  if (m == g->opened_mem.end()) {
-    void* p = nullptr;
-    cuda_ok(cudaIpcOpenMemHandle(&p, r.mem, cudaIpcMemLazyEnablePeerAccess), "open memory");
-    m = g->opened_mem.emplace(mk, static_cast<char*>(p)).first;
+  const char* src = nullptr;
+  cudaEvent_t ready = nullptr;
+  if (q->source == g->rank) {  // a message to itself: this process's own buffer and event
+    src = reinterpret_cast<const char*>(r.address);
+    for (const IpcEvent& ev : g->events)
+      if (std::memcmp(&ev.handle, &r.event, sizeof(r.event)) == 0) ready = ev.event;
+    if (!ready) throw std::runtime_error("unknown event in a message to self");
+  } else {
+    const std::string mk = std::to_string(q->source) + "/" + std::to_string(r.buffer_id);
+    auto m = g->opened_mem.find(mk);
+    if (m == g->opened_mem.end()) {
+      void* p = nullptr;
+      cuda_ok(cudaIpcOpenMemHandle(&p, r.mem, cudaIpcMemLazyEnablePeerAccess), "open memory");
+      m = g->opened_mem.emplace(mk, static_cast<char*>(p)).first;
+    }
+    src = m->second + r.offset;
+    const std::string ek = bytes_of(&r.event, sizeof(r.event));
+    auto e = g->opened_events.find(ek);
+    if (e == g->opened_events.end()) {
+      cudaEvent_t ev = nullptr;
+      cuda_ok(cudaIpcOpenEventHandle(&ev, r.event), "open event");
+      e = g->opened_events.emplace(ek, ev).first;
+    }
+    ready = e->second;
   }
-  const std::string ek = bytes_of(&r.event, sizeof(r.event));
-  auto e = g->opened_events.find(ek);
-  if (e == g->opened_events.end()) {
-    cudaEvent_t ev = nullptr;
-    cuda_ok(cudaIpcOpenEventHandle(&ev, r.event), "open event");
-    e = g->opened_events.emplace(ek, ev).first;
-  }
-  cuda_ok(cudaStreamWaitEvent(g->copy_stream, e->second, 0), "stream wait");
+  cuda_ok(cudaStreamWaitEvent(g->copy_stream, ready, 0), "stream wait");
   if (r.bytes)
-    cuda_ok(cudaMemcpyAsync(q->buf, m->second + r.offset, r.bytes, cudaMemcpyDefault,
-                            g->copy_stream),
+    cuda_ok(cudaMemcpyAsync(q->buf, src, r.bytes, cudaMemcpyDefault, g->copy_stream),
             "peer copy");
   cuda_ok(cudaEventCreateWithFlags(&q->copy_done, cudaEventDisableTiming), "event create");
   cuda_ok(cudaEventRecord(q->copy_done, g->copy_stream), "event record");
@@ -517,10 +530,26 @@ bool advance(mgfa_mpi_request* q) {
   return true;
 }
 
+// Advances every pending request once and drops the completed ones. After an
+// error the remaining requests stay pending, untouched, and the error is
+// rethrown.
 void progress_all() {
   auto& p = g->pending;
-  p.erase(std::remove_if(p.begin(), p.end(), [](mgfa_mpi_request* q) { return advance(q); }),
-          p.end());
+  size_t keep = 0;
+  std::exception_ptr err;
+  for (size_t i = 0; i < p.size(); ++i) {
+    bool done = false;
+    if (!err) {
+      try {
+        done = advance(p[i]);
+      } catch (...) {
+        err = std::current_exception();
+      }
+    }
+    if (!done) p[keep++] = p[i];
+  }
+  p.resize(keep);
+  if (err) std::rethrow_exception(err);
 }
 
 template <class F>
@@ -767,7 +796,7 @@ int MPI_Isend(const void* buf, int count, MPI_Datatype datatype, int dest, int t
               MPI_Request* request) {
   try {
     if (!g || g->world == 1 || dest < 0 || dest >= g->world)
-      throw std::runtime_error("bad destination");
+      throw std::runtime_error("bad destination (point-to-point needs 2 or more ranks)");
     auto* r = new mgfa_mpi_request();
     r->kind = mgfa_mpi_request::kSend;
     r->bytes = size_t(count) * type_size(datatype);

@@ -91,6 +91,12 @@ int main(int argc, char** argv) {
   }
   CHECK(token == rank_, "sendrecv ring");
 
+  /* a message to itself */
+  int self_out = 42 + rank_, self_in = -1;
+  MPI_Sendrecv(&self_out, 1, MPI_INT, rank_, 30, &self_in, 1, MPI_INT, rank_, 30, MPI_COMM_WORLD,
+               MPI_STATUS_IGNORE);
+  CHECK(self_in == 42 + rank_, "self message");
+
   /* broadcast from the last rank */
   char id[16];
   for (int i = 0; i < 16; ++i) id[i] = (char)(rank_ == size_ - 1 ? 'a' + i : 0);
@@ -210,6 +216,15 @@ int main(int argc, char** argv) {
       cur = nxt;
       nxt = t;
     }
+    /* a device message to itself (the ring left other ranks' data in d_a) */
+    for (int i = 0; i < kN; ++i) h[i] = (float)(rank_ * 4096 + i % 4096);
+    CHECK(cudaMemcpy(d_a + kOff, h, kN * sizeof(float), cudaMemcpyHostToDevice) == cudaSuccess,
+          "H2D");
+    MPI_Sendrecv(d_a + kOff, kN, MPI_FLOAT, rank_, 40, d_b, kN, MPI_FLOAT, rank_, 40,
+                 MPI_COMM_WORLD, MPI_STATUS_IGNORE);
+    CHECK(cudaMemcpy(h, d_b, kN * sizeof(float), cudaMemcpyDeviceToHost) == cudaSuccess, "D2H");
+    for (int i = 0; i < kN; i += 997)
+      CHECK(h[i] == (float)(rank_ * 4096 + i % 4096), "device self message");
     cudaFree(d_a);
     cudaFree(d_b);
     free(h);
