@@ -115,6 +115,10 @@ class RingTransformerLM(nn.Module):
             for _ in range(n_layers))
         self.norm = RMSNorm(d_model)
         self.head = nn.Linear(d_model, vocab, bias=False)
+        # small embeddings (std 0.02): with the default N(0, 1) and tied weights the
+        # initial logits would have std ~sqrt(d_model) and the first losses would be
+        # far above ln(vocab)
+        nn.init.normal_(self.embed.weight, std=0.02)
         if tie_embeddings:
             self.head.weight = self.embed.weight
 
