@@ -54,7 +54,8 @@ $(OBJ)/%.o: csrc/%.cu $(HDRS) | $(OBJ)
 	$(GPU_NVCC) -c $< -o $@
 
 SCHED_OBJ := $(OBJ)/sched/workload.o $(OBJ)/sched/scheduler.o $(OBJ)/sched/shard_plan.o
-COMM_OBJ  := $(OBJ)/bench/dist_env.o $(OBJ)/comm/symmetric.o $(OBJ)/kernels/ring_exchange.o
+COMM_OBJ  := $(OBJ)/bench/dist_env.o $(OBJ)/mpi_shim/mpi_shim.o $(OBJ)/comm/symmetric.o \
+             $(OBJ)/kernels/ring_exchange.o
 
 $(BIN)/ring_loop_bench: $(OBJ)/bench/ring_loop_bench.o $(COMM_OBJ) | $(BIN)
 	$(CXX) -o $@ $^ $(GPU_LIBS)
@@ -67,7 +68,8 @@ $(BIN)/ring_attention_bench: $(OBJ)/bench/ring_attention_bench.o $(COMM_OBJ) $(S
 $(BIN)/check_peer: csrc/bench/check_peer.cpp | $(BIN)
 	$(CXX) -O2 -std=c++17 -isystem $(CUDA_HOME)/include -o $@ $< -L$(CUDA_HOME)/lib64 -Wl,-rpath,$(CUDA_HOME)/lib64 -lcudart
 
-$(BIN)/dist_selftest: $(OBJ)/bench/dist_selftest.o $(OBJ)/bench/dist_env.o | $(BIN)
+$(BIN)/dist_selftest: $(OBJ)/bench/dist_selftest.o $(OBJ)/bench/dist_env.o \
+    $(OBJ)/mpi_shim/mpi_shim.o | $(BIN)
 	$(CXX) -o $@ $^ $(GPU_LIBS)
 
 LIB := build/lib

@@ -10,6 +10,8 @@
 #include <thread>
 
 #include "../common/device_select.hpp"
+#include "../mpi_shim/mpi.h"
+#include "../mpi_shim/mpi_shim_ext.hpp"
 
 namespace mgfa::bench {
 
@@ -78,12 +80,15 @@ Dist& Dist::operator=(Dist&& o) noexcept {
     p2p_seq_ = o.p2p_seq_;
     comm_ = o.comm_;
     o.comm_ = nullptr;
+    mpi_ = o.mpi_;
+    o.mpi_ = false;
   }
   return *this;
 }
 
 Dist::~Dist() {
   if (comm_) ncclCommDestroy(comm_);
+  if (mpi_) MPI_Finalize();  // collective, like every rank's destruction of its Dist
 }
 
 // Keys live under torchrun's run id (when set), so a reused agent store never
@@ -125,16 +130,25 @@ std::vector<double> Dist::max(const std::vector<double>& v) {
 }
 
 void Dist::host_sendrecv(const void* send, size_t n, int to, void* recv, int from) {
-  const uint64_t seq = p2p_seq_++;
-  const std::string out_key =
-      key("p2p", seq) + "/" + std::to_string(rank_) + "->" + std::to_string(to);
-  const std::string in_key =
-      key("p2p", seq) + "/" + std::to_string(from) + "->" + std::to_string(rank_);
-  store_->set(out_key, to_bytes(send, n));
-  const auto v = store_->get(in_key);
-  if (v.size() != n) throw std::runtime_error("host_sendrecv: size mismatch");
-  std::memcpy(recv, v.data(), n);
-  store_->deleteKey(in_key);
+  if (world_ == 1) {
+    if (send != recv) std::memcpy(recv, send, n);
+    return;
+  }
+  if (!mpi_) {  // collective: every rank's first host_sendrecv
+    mgfa::mpi_shim::init_with_store(store_, rank_, world_);
+    mpi_ = true;
+  }
+  // MPI counts are int: at most 1 GiB per message
+  constexpr size_t kMax = size_t(1) << 30;
+  const char* s = static_cast<const char*>(send);
+  char* r = static_cast<char*>(recv);
+  for (size_t off = 0; off < n || (n == 0 && off == 0); off += kMax) {
+    const int c = int(std::min(kMax, n - off));
+    if (MPI_Sendrecv(s + off, c, MPI_BYTE, to, 0, r + off, c, MPI_BYTE, from, 0, MPI_COMM_WORLD,
+                     MPI_STATUS_IGNORE) != MPI_SUCCESS)
+      throw std::runtime_error("host_sendrecv: MPI_Sendrecv failed");
+    if (n == 0) break;
+  }
 }
 
 ncclComm_t Dist::nccl() {

@@ -7,7 +7,8 @@
 // (TORCHELASTIC_USE_AGENT_STORE), otherwise rank 0 hosts it. On top of the store:
 // barriers, all-gather of small blobs, max-over-ranks reductions of timings (the
 // reference's MPI_Reduce(MAX), ring/attention/bench/ring_attention_nccl_gpu_bench.cu:409-416),
-// blocking host send/recv (the staged transport) and the NCCL communicator of
+// blocking host send/recv (the staged transport, through the MPI subset's
+// shared-memory mailbox and staging segments, csrc/mpi_shim) and the NCCL communicator of
 // the NCCL baselines (unique id published through the store, as the reference
 // broadcasts it with MPI_Bcast, ring_attention_nccl_gpu_bench.cu:231-238).
 #pragma once
@@ -58,6 +59,7 @@ class Dist {
   c10::intrusive_ptr<c10d::TCPStore> store_;
   uint64_t coll_seq_ = 0, p2p_seq_ = 0;
   ncclComm_t comm_ = nullptr;
+  bool mpi_ = false;  // the MPI subset was started on store_ (host_sendrecv)
 };
 
 // Prints "[tag] NCCL error ..." and aborts the process group on failure.

@@ -49,7 +49,7 @@ __global__ void __launch_bounds__(512)
           const uint64_t o = off + u * stride;
           if (o < e) {
             uint8_t* dst = o < push.bytes ? push.dst_k + o : push.dst_v + (o - push.bytes);
-            const uint8_t* end = o < push.bytes ? push.dst_k_end : push.dst_v_end;
+            [[maybe_unused]] const uint8_t* end = o < push.bytes ? push.dst_k_end : push.dst_v_end;
             if (MGFA_IN_BOUNDS(!end || dst + 16 <= end, status, 5))
               *reinterpret_cast<uint4*>(dst) = r[u];
           }

@@ -62,7 +62,7 @@ __device__ __forceinline__ void ring_push_warp(const RingPush& rp, const RingCon
         const uint64_t o = off + uint64_t(u) * 32 * 16;
         if (o < e) {
           uint8_t* dst = o < rp.bytes ? rp.dst_k + o : rp.dst_v + (o - rp.bytes);
-          const uint8_t* end = o < rp.bytes ? rp.dst_k_end : rp.dst_v_end;
+          [[maybe_unused]] const uint8_t* end = o < rp.bytes ? rp.dst_k_end : rp.dst_v_end;
           if (MGFA_IN_BOUNDS(!end || dst + 16 <= end, status, 12))
             *reinterpret_cast<uint4*>(dst) = r[u];
         }

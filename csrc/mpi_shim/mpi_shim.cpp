@@ -40,6 +40,7 @@
 // MPI_SHIM_TIMEOUT_S seconds (default 600) with an error. The broadcast and
 // reduce wait in the store without driving progress.
 #include "mpi.h"
+#include "mpi_shim_ext.hpp"
 
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -151,7 +152,7 @@ struct SegmentHeader {
 
 struct State {
   int rank = 0, world = 1;
-  c10::intrusive_ptr<c10d::TCPStore> store;
+  c10::intrusive_ptr<c10d::Store> store;
   std::string prefix;
   std::map<std::tuple<int, int>, uint64_t> sent, received;  // (peer, tag) -> count
   uint64_t coll = 0;
@@ -576,7 +577,7 @@ void fill_status(const mgfa_mpi_request* r, MPI_Status* st) {
 // ------------------------------------------------------------------ setup
 void store_barrier(const char* name) {
   const std::string k = g->prefix + name;
-  if (g->store->add(k, 1) == g->world) g->store->set(k + "/done", {1});
+  if (g->store->add(k, 1) == g->world) g->store->set(k + "/done", std::vector<uint8_t>{1});
   g->store->wait({k + "/done"});
 }
 
@@ -621,20 +622,44 @@ void map_segment() {
 
 }  // namespace
 
+namespace {
+
+State* new_state(int rank, int world) {
+  if (world < 1 || rank < 0 || rank >= world) throw std::runtime_error("bad RANK / WORLD_SIZE");
+  auto* s = new State();
+  s->rank = rank;
+  s->world = world;
+  s->timeout_s = env_int("MPI_SHIM_TIMEOUT_S", 600);
+  s->ipc = env_int("MPI_SHIM_CUDA_IPC", 1) != 0;
+  const char* run = std::getenv("TORCHELASTIC_RUN_ID");
+  s->prefix = std::string("mpi_shim/") + (run ? run : "") + "/";
+  return s;
+}
+
+}  // namespace
+
+void mgfa::mpi_shim::init_with_store(c10::intrusive_ptr<c10d::Store> store, int rank,
+                                     int world) {
+  if (g) return;
+  g = new_state(rank, world);
+  try {
+    if (world > 1) {
+      g->store = std::move(store);
+      map_segment();
+    }
+  } catch (...) {
+    delete g;
+    g = nullptr;
+    throw;
+  }
+}
+
 extern "C" {
 
 int MPI_Init_thread(int*, char***, int required, int* provided) {
   if (g) return MPI_SUCCESS;
   try {
-    g = new State();
-    g->world = env_int("WORLD_SIZE", 1);
-    g->rank = env_int("RANK", 0);
-    g->timeout_s = env_int("MPI_SHIM_TIMEOUT_S", 600);
-    g->ipc = env_int("MPI_SHIM_CUDA_IPC", 1) != 0;
-    if (g->world < 1 || g->rank < 0 || g->rank >= g->world)
-      throw std::runtime_error("bad RANK / WORLD_SIZE");
-    const char* run = std::getenv("TORCHELASTIC_RUN_ID");
-    g->prefix = std::string("mpi_shim/") + (run ? run : "") + "/";
+    g = new_state(env_int("RANK", 0), env_int("WORLD_SIZE", 1));
     if (g->world > 1) {
       c10d::TCPStoreOptions o;
       o.port = uint16_t(env_int("MASTER_PORT", 29500));
@@ -651,7 +676,10 @@ int MPI_Init_thread(int*, char***, int required, int* provided) {
     if (provided) *provided = required;
     return MPI_SUCCESS;
   } catch (const std::exception& e) {
-    return fail("MPI_Init", e);
+    const int rc = fail("MPI_Init", e);
+    delete g;
+    g = nullptr;
+    return rc;
   }
 }
 
