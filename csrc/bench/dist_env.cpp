@@ -4,6 +4,7 @@
 
 #include <algorithm>
 #include <chrono>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <stdexcept>
@@ -82,6 +83,7 @@ Dist& Dist::operator=(Dist&& o) noexcept {
     o.comm_ = nullptr;
     mpi_ = o.mpi_;
     o.mpi_ = false;
+    store_p2p_ = o.store_p2p_;
   }
   return *this;
 }
@@ -134,21 +136,41 @@ void Dist::host_sendrecv(const void* send, size_t n, int to, void* recv, int fro
     if (send != recv) std::memcpy(recv, send, n);
     return;
   }
-  if (!mpi_) {  // collective: every rank's first host_sendrecv
-    mgfa::mpi_shim::init_with_store(store_, rank_, world_);
-    mpi_ = true;
+  if (!mpi_ && !store_p2p_) {  // collective: every rank's first host_sendrecv
+    try {
+      mgfa::mpi_shim::init_with_store(store_, rank_, world_);
+      mpi_ = true;
+    } catch (const std::exception& e) {  // e.g. no /dev/shm: every rank falls back
+      std::fprintf(stderr, "[rank %d] shared-memory transport unavailable (%s); host send/recv "
+                   "through the store\n", rank_, e.what());
+      store_p2p_ = true;
+    }
+  }
+  if (store_p2p_) {
+    const uint64_t seq = p2p_seq_++;
+    const std::string out_key =
+        key("p2p", seq) + "/" + std::to_string(rank_) + "->" + std::to_string(to);
+    const std::string in_key =
+        key("p2p", seq) + "/" + std::to_string(from) + "->" + std::to_string(rank_);
+    store_->set(out_key, to_bytes(send, n));
+    const auto v = store_->get(in_key);
+    if (v.size() != n) throw std::runtime_error("host_sendrecv: size mismatch");
+    std::memcpy(recv, v.data(), n);
+    store_->deleteKey(in_key);
+    return;
   }
   // MPI counts are int: at most 1 GiB per message
   constexpr size_t kMax = size_t(1) << 30;
   const char* s = static_cast<const char*>(send);
   char* r = static_cast<char*>(recv);
-  for (size_t off = 0; off < n || (n == 0 && off == 0); off += kMax) {
+  size_t off = 0;
+  do {
     const int c = int(std::min(kMax, n - off));
     if (MPI_Sendrecv(s + off, c, MPI_BYTE, to, 0, r + off, c, MPI_BYTE, from, 0, MPI_COMM_WORLD,
                      MPI_STATUS_IGNORE) != MPI_SUCCESS)
       throw std::runtime_error("host_sendrecv: MPI_Sendrecv failed");
-    if (n == 0) break;
-  }
+    off += size_t(c);
+  } while (off < n);
 }
 
 ncclComm_t Dist::nccl() {

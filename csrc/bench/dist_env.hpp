@@ -59,7 +59,8 @@ class Dist {
   c10::intrusive_ptr<c10d::TCPStore> store_;
   uint64_t coll_seq_ = 0, p2p_seq_ = 0;
   ncclComm_t comm_ = nullptr;
-  bool mpi_ = false;  // the MPI subset was started on store_ (host_sendrecv)
+  bool mpi_ = false;        // the MPI subset was started on store_ (host_sendrecv)
+  bool store_p2p_ = false;  // it could not start: host_sendrecv goes through the store
 };
 
 // Prints "[tag] NCCL error ..." and aborts the process group on failure.

@@ -598,8 +598,14 @@ void map_segment() {
     std::random_device rd;
     name = "/mgfa_mpi_" + std::to_string(getpid()) + "_" + std::to_string(rd());
     fd = shm_open(name.c_str(), O_CREAT | O_EXCL | O_RDWR, 0600);
-    if (fd < 0 || ftruncate(fd, off_t(g->seg_bytes)) != 0)
+    // reserve the pages now (an error here, not a bus error on first touch)
+    if (fd < 0 || posix_fallocate(fd, 0, off_t(g->seg_bytes)) != 0) {
+      if (fd >= 0) {
+        close(fd);
+        shm_unlink(name.c_str());
+      }
       throw std::runtime_error("cannot create the shared-memory segment " + name);
+    }
     g->store->set(g->prefix + "shm", std::vector<uint8_t>(name.begin(), name.end()));
   } else {
     const std::vector<uint8_t> v = g->store->get(g->prefix + "shm");
