@@ -16,11 +16,16 @@
 // has one writer per transition. Slot kinds, chosen by the sender:
 //  * 'H': a host payload small enough for the slot, inline; the send completes
 //    once posted.
-//  * 'B': a larger host payload, copied into a staging segment of shared
-//    memory that the sender keeps per destination (created on demand, grown
-//    when idle); the slot names the segment, the receiver copies out of it and
-//    marks the slot copied (state 2), which completes the send and frees the
-//    staging segment for the next message to that destination.
+//  * 'B': a larger host payload, moved in pieces (1 MB, MPI_SHIM_PIECE_BYTES)
+//    through a staging segment of shared memory that the sender keeps per
+//    destination (created on demand, grown when idle, at most two pieces).
+//    Each piece's slot names the segment, the piece's place in it and in the
+//    message; the receiver copies the piece out and marks the slot copied
+//    (state 2), which frees that half of the segment for the piece after
+//    next, so copy-in and copy-out overlap and a piece is copied out while it
+//    is still in the caches (1 MB pieces ran 16 MB messages at 5.7 GB/s on a
+//    host whose plain memcpy runs at 3.8 GB/s; 4 MB pieces at 3.3, one piece
+//    at 2.3). The send completes when every piece has been copied out.
 //  * 'S': the same when no staging segment can be had (no room in
 //    /dev/shm): the payload goes into the store under the message's key.
 //  * 'D' (device buffer; MPI_SHIM_CUDA_IPC=0 turns it off): a CUDA IPC handle
@@ -53,6 +58,7 @@
 #include <atomic>
 #include <chrono>
 #include <random>
+#include <cstddef>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -103,6 +109,11 @@ struct mgfa_mpi_request {
   int event = -1;                 // send 'D': the pool event recorded at the send
   Slot* slot = nullptr;          // the slot this request posted or consumed
   cudaEvent_t copy_done = nullptr;
+  // 'B' (staged) messages: bytes posted (send) or copied out (receive) so far,
+  // the piece size, and the pieces in flight by half of the staging segment
+  size_t done_bytes = 0;
+  size_t piece = 0;
+  Slot* pieces[2] = {nullptr, nullptr};
 };
 
 namespace {
@@ -126,9 +137,13 @@ struct IpcEvent {
   cudaIpcEventHandle_t handle;
 };
 
-struct BulkRecord {  // contents of a 'B' slot
+struct BulkRecord {  // contents of a 'B' slot: one piece of a staged message
   char name[64];
-  uint64_t segment_bytes = 0, bytes = 0;
+  uint64_t segment_bytes = 0;
+  uint64_t offset = 0;      // of the piece in the message
+  uint64_t seg_offset = 0;  // of the piece in the segment
+  uint64_t bytes = 0;       // of the piece
+  uint64_t total = 0;       // of the message
 };
 
 struct Segment {  // a named shared-memory segment, mapped in this process
@@ -167,6 +182,7 @@ struct State {
   std::vector<Segment> staging;            // per destination ('B' sends)
   std::vector<Segment> mapped;             // per source: its staging segment, mapped here
   uint64_t staging_serial = 0;
+  size_t piece_bytes = size_t(1) << 20;    // 'B' piece size
   // device side, created on first use on the current device
   std::map<uint64_t, Export> exports;     // buffer id -> export
   std::vector<IpcEvent> events;           // pool; a send holds one until it completes
@@ -376,49 +392,91 @@ const Segment& map_from(int src, const BulkRecord& r) {
 }
 
 // ------------------------------------------------------------------ sends
-// Posts a queued send into a free slot of the mailbox to its destination.
+// A free slot of the mailbox to `dst` (claimed for this process to fill), or null.
+Slot* claim_slot(int dst) {
+  Slot* box = g->mailbox(g->rank, dst);
+  int& start = g->next_slot[size_t(dst)];
+  for (int k = 0; k < kSlots; ++k) {
+    Slot* c = box + (start + k) % kSlots;
+    if (c->state.load(std::memory_order_acquire) == 0) {
+      start = (start + k + 1) % kSlots;
+      return c;
+    }
+  }
+  return nullptr;
+}
+
+void publish(Slot* s, const mgfa_mpi_request* q, char kind, uint32_t len, const void* data,
+             size_t n) {
+  s->kind = uint32_t(kind);
+  s->tag = q->tag;
+  s->seq = q->seq;
+  s->len = len;
+  if (n) std::memcpy(s->data, data, n);
+  s->state.store(1, std::memory_order_release);
+}
+
+// A started 'B' send: frees the halves whose pieces were copied out and posts
+// the next pieces into free halves. True when every piece is posted and
+// copied out.
+bool pump_bulk(mgfa_mpi_request* q) {
+  Segment& seg = g->staging[size_t(q->source)];
+  for (Slot*& p : q->pieces) {
+    if (p && p->state.load(std::memory_order_acquire) == 2) {
+      p->state.store(0, std::memory_order_release);
+      p = nullptr;
+    }
+  }
+  while (q->done_bytes < q->bytes) {
+    const int h = !q->pieces[0] ? 0 : !q->pieces[1] ? 1 : -1;
+    if (h < 0) break;
+    Slot* s = claim_slot(q->source);
+    if (!s) break;
+    const size_t n = std::min(q->piece, q->bytes - q->done_bytes);
+    read_into(seg.ptr + size_t(h) * q->piece, static_cast<const char*>(q->send_buf) + q->done_bytes,
+              n);
+    BulkRecord r;
+    std::snprintf(r.name, sizeof(r.name), "%s", seg.name.c_str());
+    r.segment_bytes = seg.size;
+    r.offset = q->done_bytes;
+    r.seg_offset = size_t(h) * q->piece;
+    r.bytes = n;
+    r.total = q->bytes;
+    publish(s, q, 'B', uint32_t(n), &r, sizeof(r));
+    q->pieces[h] = s;
+    q->done_bytes += n;
+  }
+  return q->done_bytes == q->bytes && !q->pieces[0] && !q->pieces[1];
+}
+
+// Starts a queued send: posts it into a free slot of the mailbox to its
+// destination ('B': takes the destination's staging segment and posts the
+// first pieces). False when it has to stay queued.
 bool try_post(mgfa_mpi_request* q) {
   using R = mgfa_mpi_request;
   const int dst = q->source;
-  if (q->slot_kind == 'B' && g->staging[size_t(dst)].busy) return false;
-  Slot* box = g->mailbox(g->rank, dst);
-  int& start = g->next_slot[size_t(dst)];
-  Slot* s = nullptr;
-  int k = 0;
-  for (; k < kSlots; ++k) {
-    Slot* c = box + (start + k) % kSlots;
-    if (c->state.load(std::memory_order_acquire) == 0) {
-      s = c;
-      break;
-    }
-  }
-  if (!s) return false;
   if (q->slot_kind == 'B') {
-    if (ensure_staging(dst, q->bytes)) {
-      Segment& seg = g->staging[size_t(dst)];
-      read_into(seg.ptr, q->send_buf, q->bytes);
-      BulkRecord r;
-      std::snprintf(r.name, sizeof(r.name), "%s", seg.name.c_str());
-      r.segment_bytes = seg.size;
-      r.bytes = q->bytes;
-      q->record.assign(reinterpret_cast<const uint8_t*>(&r),
-                       reinterpret_cast<const uint8_t*>(&r) + sizeof(r));
+    Segment& seg = g->staging[size_t(dst)];
+    if (seg.busy) return false;  // another staged message to dst is under way
+    q->piece = std::min(q->bytes, g->piece_bytes);
+    const size_t halves = q->bytes > q->piece ? 2 : 1;
+    if (ensure_staging(dst, halves * q->piece)) {
       seg.busy = true;
-    } else {
-      q->slot_kind = 'S';
-      g->store->set(msg_key(g->rank, dst, q->tag, q->seq), read_buffer(q->send_buf, q->bytes));
+      q->phase = R::kPosted;
+      pump_bulk(q);  // the first pieces, as far as slots are free
+      return true;
     }
+    q->slot_kind = 'S';  // no room in /dev/shm: the whole payload through the store
   }
-  s->kind = uint32_t(q->slot_kind);
-  s->tag = q->tag;
-  s->seq = q->seq;
-  s->len = uint32_t(q->slot_kind == 'H' ? q->record.size() : q->bytes);
-  if (!q->record.empty()) std::memcpy(s->data, q->record.data(), q->record.size());
-  s->state.store(1, std::memory_order_release);
-  start = (start + k + 1) % kSlots;
+  Slot* s = claim_slot(dst);
+  if (!s) return false;
+  if (q->slot_kind == 'S')
+    g->store->set(msg_key(g->rank, dst, q->tag, q->seq), read_buffer(q->send_buf, q->bytes));
+  const uint32_t len = uint32_t(q->slot_kind == 'H' ? q->record.size() : q->bytes);
+  publish(s, q, q->slot_kind, len, q->record.data(), q->record.size());
   q->record.clear();
   q->slot = s;
-  q->phase = (q->slot_kind == 'D' || q->slot_kind == 'B') ? R::kPosted : R::kDone;
+  q->phase = q->slot_kind == 'D' ? R::kPosted : R::kDone;
   return true;
 }
 
@@ -461,12 +519,20 @@ void start_ipc_copy(mgfa_mpi_request* q, const IpcRecord& r) {
   q->phase = mgfa_mpi_request::kCopying;
 }
 
+// The posted slot for receive q: its tag and sequence number and, for a
+// staged message, the piece that starts where the copied part ends.
 Slot* match(const mgfa_mpi_request* q) {
   Slot* box = g->mailbox(q->source, g->rank);
   for (int k = 0; k < kSlots; ++k) {
     Slot* s = box + k;
-    if (s->state.load(std::memory_order_acquire) == 1 && s->tag == q->tag && s->seq == q->seq)
-      return s;
+    if (s->state.load(std::memory_order_acquire) != 1 || s->tag != q->tag || s->seq != q->seq)
+      continue;
+    if (s->kind == 'B') {
+      uint64_t off = 0;
+      std::memcpy(&off, s->data + offsetof(BulkRecord, offset), sizeof(off));
+      if (off != q->done_bytes) continue;
+    }
+    return s;
   }
   return nullptr;
 }
@@ -478,10 +544,15 @@ bool advance(mgfa_mpi_request* q) {
   if (q->kind == R::kSend) {
     if (q->phase == R::kQueued && !try_post(q)) return false;
     if (q->phase == R::kDone) return true;
-    // 'D', 'B': the receiver marks the slot copied; this side frees it
+    if (q->slot_kind == 'B') {
+      if (!pump_bulk(q)) return false;
+      g->staging[size_t(q->source)].busy = false;
+      q->phase = R::kDone;
+      return true;
+    }
+    // 'D': the receiver marks the slot copied; this side frees it
     if (q->slot->state.load(std::memory_order_acquire) != 2) return false;
     q->slot->state.store(0, std::memory_order_release);
-    if (q->slot_kind == 'B') g->staging[size_t(q->source)].busy = false;
     if (q->event >= 0) g->free_events.push_back(q->event);
     q->event = -1;
     q->phase = R::kDone;
@@ -506,13 +577,19 @@ bool advance(mgfa_mpi_request* q) {
       q->phase = R::kDone;
       return true;
     }
-    if (s->kind == 'B') {
+    if (s->kind == 'B') {  // the next piece (match() checks its offset)
       BulkRecord r;
       std::memcpy(&r, s->data, sizeof(r));
+      if (r.total > q->bytes) throw std::runtime_error("message longer than the receive buffer");
       const Segment& seg = map_from(q->source, r);
-      if (r.bytes > seg.size) throw std::runtime_error("malformed staging record");
-      write_buffer(q->buf, reinterpret_cast<const uint8_t*>(seg.ptr), r.bytes, q->bytes);
+      if (r.seg_offset + r.bytes > seg.size || r.offset + r.bytes > r.total)
+        throw std::runtime_error("malformed staging record");
+      write_buffer(static_cast<char*>(q->buf) + r.offset,
+                   reinterpret_cast<const uint8_t*>(seg.ptr) + r.seg_offset, r.bytes,
+                   q->bytes - r.offset);
       s->state.store(2, std::memory_order_release);
+      q->done_bytes += r.bytes;
+      if (q->done_bytes < r.total) return false;
       q->phase = R::kDone;
       return true;
     }
@@ -637,6 +714,8 @@ State* new_state(int rank, int world) {
   s->world = world;
   s->timeout_s = env_int("MPI_SHIM_TIMEOUT_S", 600);
   s->ipc = env_int("MPI_SHIM_CUDA_IPC", 1) != 0;
+  if (const char* pb = std::getenv("MPI_SHIM_PIECE_BYTES"); pb && *pb)
+    s->piece_bytes = std::max<size_t>(4096, std::strtoull(pb, nullptr, 10));
   const char* run = std::getenv("TORCHELASTIC_RUN_ID");
   s->prefix = std::string("mpi_shim/") + (run ? run : "") + "/";
   return s;

@@ -145,11 +145,12 @@ def test_shim_semantics(tmp_path, shim):
             p.stdout
 
 
-@pytest.mark.parametrize("nproc,seed,port", [(2, 3, 29744), (4, 11, 29745)])
-def test_shim_randomised_traffic(tmp_path, shim, nproc, seed, port):
+@pytest.mark.parametrize("nproc,seed,port,piece", [(2, 3, 29744, ""), (4, 11, 29745, "4096")])
+def test_shim_randomised_traffic(tmp_path, shim, nproc, seed, port, piece):
     """tests/native/mpi_shim_stress.c: random sources, destinations (self
-    included), repeating tags and sizes from inline slots to staging segments,
-    completed by Waitall or Testall; every payload byte checked."""
+    included), repeating tags and sizes from inline slots to staged messages of
+    many pieces (4 KB pieces in the second case), completed by Waitall or
+    Testall; every payload byte checked."""
     exe = str(tmp_path / "mpi_shim_stress")
     subprocess.check_call(["gcc", "-O2", "-std=gnu11", "-I", os.path.join(ROOT, "csrc/mpi_shim"),
                            "-o", exe, os.path.join(ROOT, "tests/native/mpi_shim_stress.c"),
@@ -158,7 +159,8 @@ def test_shim_randomised_traffic(tmp_path, shim, nproc, seed, port):
            f"--nproc-per-node={nproc}", "--master-addr", "127.0.0.1",
            "--master-port", str(port), "--no-python", exe, "25", "32", str(seed)]
     p = subprocess.run(cmd, capture_output=True, text=True, timeout=300,
-                       env=dict(os.environ, OMP_NUM_THREADS="1"), cwd=ROOT)
+                       env=dict(os.environ, OMP_NUM_THREADS="1", MPI_SHIM_PIECE_BYTES=piece),
+                       cwd=ROOT)
     assert p.returncode == 0, p.stdout + p.stderr
     counts = [int(l.split()[-1]) for l in p.stdout.splitlines() if "stress OK" in l]
     assert len(counts) == nproc and sum(counts) == 25 * 32, p.stdout
