@@ -7,7 +7,6 @@ import subprocess
 import sys
 
 import pytest
-import torch
 
 pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 

@@ -1,5 +1,4 @@
 """sm_100a tcgen05 attention forward against the fp32 PyTorch oracle."""
-import math
 
 import pytest
 import torch

@@ -4,7 +4,6 @@ with stand-in programs that print the reference's exact line formats
 (ring/loop/ring_loop_cuda_aware.cu:226-231, ring/attention/bench/
 ring_attention_cuda_aware_gpu_bench.cu and ring_attention_staged_gpu_bench.cu
 avg_total lines)."""
-import os
 import stat
 
 import pytest
