@@ -3,7 +3,7 @@
 // cuda_aware_Isendrecv,cuda_aware_Isendrecv_overlap,nccl}_gpu_bench.cu) as one
 // executable with a --backend flag, without MPI.
 //
-//   torchrun --nproc-per-node N --no-python build/bin/ring_attention_bench \
+//   torchrun --nproc-per-node N --no-python build/bin/ring_attention_bench
 //       <kv_size_bytes> [warmup=10] [iters=100]
 //       [--backend fused|p2p_unfused|ce_unfused|nccl|staged|p2p|ce]
 //       [--numerics fp32|bf16] [--init legacy|randn] [--layout contiguous|zigzag|

@@ -2,7 +2,7 @@
 // (ring_loop_{staged,staged_Isendrecv,cuda_aware,cuda_aware_Isendrecv,nccl}.cu)
 // as one executable with a --backend flag, without MPI.
 //
-//   torchrun --nproc-per-node N --no-python build/bin/ring_loop_bench \
+//   torchrun --nproc-per-node N --no-python build/bin/ring_loop_bench
 //       <kv_size_bytes> [warmup=10] [iters=100] [--backend p2p|ce|nccl|staged]
 //       [--payload-tokens T] [--kv-heads 8] [--ctas C] [--seed S] [--json]
 //
