@@ -86,6 +86,27 @@ def test_rattn_demo_matches_reference(ref_bin, our_bin):
     assert not bad, f"{len(bad)} of {len(DEMO_ARGS)} differ, first: {bad[0]!r}"
 
 
+def test_rattn_demo_matches_reference_random_args(ref_bin, our_bin):
+    """Seeded random sequence lengths, GPU counts (up to 64), block sizes (1 to
+    4096), masks and cost models, including tables cut short by the 4096-task
+    and 256-row caps: the same stdout and exit code."""
+    import random
+    rng = random.Random(5)
+    bad = []
+    for _ in range(200):
+        a = (f"--seq {rng.randint(1, 40000)} --gpus {rng.randint(1, 64)} "
+             f"--block {rng.choice([1, 3, 16, 48, 64, 100, 128, 256, 512, 4096])} "
+             f"--mask {rng.choice(['causal', 'full', 'other'])} "
+             f"--alpha {rng.uniform(0, 3):.4f} --beta {rng.uniform(0, 1e-4):.3g}").split()
+        ref = subprocess.run([os.path.join(ref_bin, "rattn_demo")] + a, capture_output=True,
+                             text=True, timeout=60)
+        ours = subprocess.run([os.path.join(our_bin, "rattn_demo")] + a, capture_output=True,
+                              text=True, timeout=60)
+        if (ref.stdout, ref.returncode) != (ours.stdout, ours.returncode):
+            bad.append(" ".join(a))
+    assert not bad, f"{len(bad)} differ, first: {bad[0]!r}"
+
+
 def test_experiment_tables_match_reference(tmp_path, ref_bin, our_bin):
     src = subprocess.run(["bash", os.path.join(ROOT, "benchmarks/build_reference.sh"),
                           "--print-src"], capture_output=True, text=True).stdout.strip()
