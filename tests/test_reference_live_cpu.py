@@ -138,6 +138,75 @@ def test_verify_full_matches_reference(tmp_path, ref_bin, our_bin, name):
                 assert a == b, f"{o!r} vs {r!r}"
 
 
+def _legacy_dumps(out_dir, P, L, rng):
+    """Dumps of the exact attention of the reference's legacy inputs for P ranks
+    of L tokens, then one random defect (or none). Returns a label."""
+    import numpy as np
+    from verify_full_cases import _legacy
+    dim = 64
+    kv = np.concatenate([_legacy(r, L * dim)[1] for r in range(P)]).reshape(P * L, dim)
+    kv = kv.astype(np.float64)
+    outs = []
+    for r in range(P):
+        q = _legacy(r, L * dim)[0].reshape(L, dim).astype(np.float64)
+        sc = q @ kv.T
+        sc -= sc.max(axis=1, keepdims=True)
+        w = np.exp(sc)
+        outs.append(((w @ kv) / w.sum(axis=1, keepdims=True)).astype(np.float32).reshape(-1))
+    kind = rng.choice(["none", "small", "large", "nan", "inf", "missing", "short", "long"])
+    r, idx = rng.randrange(P), rng.randrange(L * dim)
+    if kind == "small":
+        outs[r][idx] += np.float32(rng.choice([1e-3, 0.02]))
+    elif kind == "large":
+        outs[r][idx] += np.float32(rng.choice([0.06, 5.0, -300.0]))
+    elif kind == "nan":
+        outs[r][idx] = np.nan
+    elif kind == "inf":
+        outs[r][idx] = rng.choice([np.inf, -np.inf])
+    elif kind == "short":
+        outs[r] = outs[r][: rng.randrange(L * dim)]
+    elif kind == "long":
+        outs[r] = np.concatenate([outs[r], np.ones(7, np.float32)])
+    for rr in range(P):
+        if kind == "missing" and rr == r:
+            continue
+        outs[rr].astype("<f4").tofile(os.path.join(out_dir, f"ring_output_rank{rr}.bin"))
+    return kind
+
+
+def test_verify_full_matches_reference_random_dumps(tmp_path, ref_bin, our_bin):
+    """Seeded random rank counts, shard lengths and defects (small and large
+    errors, NaN, +/-Inf, missing, short and long dumps), plus argument sets
+    the checker must reject or default: the same reports and exit codes."""
+    import random
+    rng = random.Random(9)
+    num = re.compile(r"-?\d+\.\d+|-?\d+|nan|inf", re.I)
+    cases = []
+    for i in range(24):
+        d = tmp_path / f"case{i}"
+        d.mkdir()
+        P, L = rng.randint(1, 4), rng.choice([1, 3, 64, 200, 384])
+        kind = _legacy_dumps(str(d), P, L, rng)
+        cases.append((f"{kind} P={P} L={L}", [str(d), str(P), str(L * 256)]))
+    cases += [("defaults", []), ("bad size", [str(tmp_path), "2", "100"]),
+              ("zero gpus", [str(tmp_path), "0", "256"]), ("no dir", ["/nonexistent", "1", "256"])]
+    for label, args in cases:
+        ref, ref_rc = _run(os.path.join(ref_bin, "verify_full"), args)
+        ours, rc = _run(os.path.join(our_bin, "verify_full"), args)
+        assert rc == ref_rc, f"{label}: exit {rc} vs {ref_rc}\n{ours}\nvs\n{ref}"
+        rl, ol = ref.strip().splitlines(), ours.strip().splitlines()
+        assert len(rl) == len(ol), f"{label}:\n{ours}\nvs\n{ref}"
+        for r, o in zip(rl, ol):
+            assert num.sub("#", r) == num.sub("#", o), f"{label}: {o!r} vs {r!r}"
+            for a, b in zip(num.findall(o), num.findall(r)):
+                if "." in b:  # summation order: about one fp32 ulp of the ~6.6e4 outputs
+                    fa, fb = float(a), float(b)
+                    ok = (fa == fb) or abs(fa - fb) <= max(0.0079, 1e-6 * abs(fb))
+                    assert ok, f"{label}: {o!r} vs {r!r}"
+                else:
+                    assert a == b, f"{label}: {o!r} vs {r!r}"
+
+
 @pytest.mark.parametrize("nproc,port", [(2, 29741), (3, 29742)])
 def test_reference_ring_test_on_shim(ref_bin, nproc, port):
     p = _torchrun(nproc, os.path.join(ref_bin, "ring_test"), port)
