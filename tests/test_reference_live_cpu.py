@@ -254,3 +254,66 @@ def test_shim_randomised_traffic(tmp_path, shim, nproc, seed, port, piece):
     assert p.returncode == 0, p.stdout + p.stderr
     counts = [int(l.split()[-1]) for l in p.stdout.splitlines() if "stress OK" in l]
     assert len(counts) == nproc and sum(counts) == 25 * 32, p.stdout
+
+
+def _our_sched_lines(seq, block, gpus, causal, alpha, beta):
+    """The harness's records, from this repository's scheduler library."""
+    from multi_gpu_flashattention_b200._ext import sched as load
+    s = load()
+    shape = s.WorkloadShape(seq, seq, block, block)
+    mask = "causal" if causal else "full"
+    tasks = s.build_block_tasks(shape, mask, s.CostModel(alpha, beta), 4096)
+    g17 = lambda x: "%.17g" % x  # noqa: E731
+    out = [f"T {t.row} {t.col} {t.q_begin} {t.q_end} {t.k_begin} {t.k_end} {t.active} "
+           f"{t.total} {g17(t.cost)} {g17(t.density)}" for t in tasks]
+    fmt = lambda tag, m: " ".join([tag] + [str(x) for x in m])  # noqa: E731
+    costs = s.task_costs(tasks)
+    rr = s.assign_round_robin(tasks, gpus)
+    out.append(fmt("RR", rr.task_to_gpu))
+    moved, a = s.rebalance_move_once(costs, rr)
+    out.append(fmt(f"MOVE {int(moved)}", a.task_to_gpu))
+    if gpus <= len(tasks):
+        swapped, a = s.rebalance_swap_once(costs, s.assign_round_robin(tasks, gpus),
+                                           reference_partner_quirk=True)
+        out.append(fmt(f"SWAP {int(swapped)}", a.task_to_gpu))
+    else:
+        out.append("SWAP n/a")
+    out.append(fmt("LPT_SCAN", s.assign_block_lpt(tasks, gpus, "scan").task_to_gpu))
+    out.append(fmt("LPT_HEAP", s.assign_block_lpt(tasks, gpus, "heap").task_to_gpu))
+    if s.num_row_blocks(shape) <= 256:
+        rows = s.build_row_tasks(shape, tasks)
+        out += [f"R {r.row} {r.num_blocks} {r.num_cols_needed} {g17(r.comp_cost)} "
+                f"{g17(r.total_cost)}" for r in rows]
+        out.append(fmt("ROWLPT", s.assign_row_lpt(rows, gpus, "scan").task_to_gpu))
+        dp = s.partition_rows_contiguous(rows, gpus)
+        out.append(fmt(f"DP {0 if dp.ok else -1}", dp.row_to_gpu if dp.ok else []))
+    return out
+
+
+def test_scheduler_library_matches_reference_functions(tmp_path, ref_bin):
+    """Every intermediate of the workload model and the schedulers (block tasks
+    with ranges, counts, costs and densities; round-robin, one move repair, one
+    swap repair with the reference's partner indexing, block LPT in scan and
+    heap modes, row tasks, row LPT, contiguous DP maps) against the reference's
+    own workload.c / scheduler.c, on seeded random workloads."""
+    import random
+    src = subprocess.run(["bash", os.path.join(ROOT, "benchmarks/build_reference.sh"),
+                          "--print-src"], capture_output=True, text=True).stdout.strip()
+    exe = str(tmp_path / "sched_ref_harness")
+    wl = os.path.join(src, "workload")
+    subprocess.check_call(["gcc", "-O2", "-std=gnu11", "-I", wl, "-o", exe,
+                           os.path.join(ROOT, "tests/native/sched_ref_harness.c"),
+                           os.path.join(wl, "workload.c"), os.path.join(wl, "scheduler.c"), "-lm"])
+    rng = random.Random(17)
+    cases = [(4096, 128, 2, 1, 0.0, 3.84e-6), (1000, 100, 3, 0, 1.21, 3.84e-6)]
+    cases += [(rng.randint(1, 9000), rng.choice([16, 32, 64, 100, 128, 256]), rng.randint(1, 12),
+               rng.randint(0, 1), round(rng.uniform(0, 2), 3), rng.choice([3.84e-6, 6.94e-6, 1e-3]))
+              for _ in range(40)]
+    for c in cases:
+        ref = subprocess.run([exe] + [str(x) for x in c], capture_output=True, text=True,
+                             timeout=120)
+        assert ref.returncode == 0, ref.stderr
+        rl, ol = ref.stdout.strip().splitlines(), _our_sched_lines(*c)
+        assert len(rl) == len(ol), f"{c}: {len(ol)} records vs {len(rl)}"
+        for r, o in zip(rl, ol):
+            assert r.strip() == o.strip(), f"{c}:\nours {o[:200]}\nref  {r[:200]}"
