@@ -317,3 +317,32 @@ def test_scheduler_library_matches_reference_functions(tmp_path, ref_bin):
         assert len(rl) == len(ol), f"{c}: {len(ol)} records vs {len(rl)}"
         for r, o in zip(rl, ol):
             assert r.strip() == o.strip(), f"{c}:\nours {o[:200]}\nref  {r[:200]}"
+
+
+def test_cpu_attention_matches_reference_functions(tmp_path):
+    """csrc/host/cpu_attention.cpp (threaded) against the reference's own
+    cpu_attention_partial and merge_online_softmax (its source file included
+    with main renamed): a two-shard accumulation and normalisation on random
+    and on the reference's legacy inputs agrees bit for bit."""
+    src = subprocess.run(["bash", os.path.join(ROOT, "benchmarks/build_reference.sh"),
+                          "--print-src"], capture_output=True, text=True)
+    if src.returncode == 2:
+        pytest.skip("reference tree not present")
+    ref_file = os.path.join(src.stdout.strip(), "ring", "attention", "ring_attention_staged.cu")
+    subprocess.check_call(["make", "-s", "mpi-shim"], cwd=ROOT)
+    cuda = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    exe = str(tmp_path / "cpu_attention_harness")
+    lib = os.path.join(ROOT, "build", "lib")
+    subprocess.check_call(
+        ["g++", "-O2", "-std=c++17", "-x", "c++", f'-DREF_FILE="{ref_file}"',
+         "-I", os.path.join(ROOT, "csrc"), "-I", os.path.join(ROOT, "csrc/mpi_shim"),
+         "-I", os.path.join(cuda, "include"), "-o", exe,
+         os.path.join(ROOT, "tests/native/cpu_attention_harness.cpp"), "-x", "none",
+         os.path.join(ROOT, "csrc/host/cpu_attention.cpp"), "-L", lib, f"-Wl,-rpath,{lib}",
+         "-lmpi_shim", "-L", os.path.join(cuda, "lib64"),
+         f"-Wl,-rpath,{os.path.join(cuda, 'lib64')}", "-lcudart", "-pthread"])
+    for args in ("64 64 64 1", "200 333 64 2", "1024 1024 64 3", "17 5 32 4"):
+        p = subprocess.run([exe] + args.split(), capture_output=True, text=True, timeout=120)
+        assert p.returncode == 0, p.stderr
+        assert p.stdout.split() == ["max_abs", "0", "max_rel", "0", "legacy_max_abs", "0",
+                                    "legacy_max_rel", "0"], (args, p.stdout)
