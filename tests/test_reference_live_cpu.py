@@ -346,3 +346,48 @@ def test_cpu_attention_matches_reference_functions(tmp_path):
         assert p.returncode == 0, p.stderr
         assert p.stdout.split() == ["max_abs", "0", "max_rel", "0", "legacy_max_abs", "0",
                                     "legacy_max_rel", "0"], (args, p.stdout)
+
+
+def test_device_binding_matches_reference(tmp_path):
+    """The local-rank variables' precedence, values and the oversubscription
+    rule (csrc/common/device_select.hpp) against the reference's own
+    device_utils.cuh on seeded random environments and device counts (a
+    stand-in device count; no GPU). LOCAL_RANK, which only this repository
+    reads (torchrun), is left unset here."""
+    import random
+    src = subprocess.run(["bash", os.path.join(ROOT, "benchmarks/build_reference.sh"),
+                          "--print-src"], capture_output=True, text=True)
+    if src.returncode == 2:
+        pytest.skip("reference tree not present")
+    header = os.path.join(src.stdout.strip(), "ring", "attention", "common", "device_utils.cuh")
+    subprocess.check_call(["make", "-s", "mpi-shim"], cwd=ROOT)
+    cuda = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    exe = str(tmp_path / "device_select_harness")
+    lib = os.path.join(ROOT, "build", "lib")
+    subprocess.check_call(
+        ["g++", "-O2", "-std=c++17", f'-DREF_HEADER="{header}"', "-I", os.path.join(ROOT, "csrc"),
+         "-I", os.path.join(ROOT, "csrc/mpi_shim"), "-I", os.path.join(cuda, "include"), "-o", exe,
+         os.path.join(ROOT, "tests/native/device_select_harness.cpp"), "-L", lib,
+         f"-Wl,-rpath,{lib}", "-lmpi_shim"])
+    names = ["OMPI_COMM_WORLD_LOCAL_RANK", "MV2_COMM_WORLD_LOCAL_RANK", "SLURM_LOCALID",
+             "MPI_LOCALRANKID", "PMI_LOCAL_RANK", "PALS_LOCAL_RANK"]
+    base = {k: v for k, v in os.environ.items()
+            if k not in names + ["LOCAL_RANK", "ALLOW_GPU_OVERSUBSCRIBE", "RANK", "WORLD_SIZE"]}
+    rng = random.Random(23)
+    for _ in range(40):
+        env = dict(base)
+        for n in rng.sample(names, rng.randint(0, 3)):
+            env[n] = rng.choice(["0", "1", "3", "7", "12", "", "-1", "abc", "02"])
+        if rng.random() < 0.3:
+            env["ALLOW_GPU_OVERSUBSCRIBE"] = "1"
+        count = rng.choice([0, 1, 2, 4, 8])
+        got = [subprocess.run([exe, mode, str(count)], env=env, capture_output=True, text=True,
+                              timeout=60) for mode in ("ref", "ours")]
+        ref, ours = got
+        assert ref.returncode == ours.returncode, (env, count, ref.stdout + ref.stderr,
+                                                   ours.stdout + ours.stderr)
+        if ref.returncode == 0:
+            assert ref.stdout == ours.stdout, (env, count, ref.stdout, ours.stdout)
+        else:  # refused for the same reason (the messages are worded alike)
+            key = "No CUDA devices" if count == 0 else "ALLOW_GPU_OVERSUBSCRIBE"
+            assert key in ref.stdout + ref.stderr and key in ours.stdout + ours.stderr
