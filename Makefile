@@ -6,6 +6,7 @@
 #   build/bin/ring_loop_bench      pure ring exchange (p2p | ce | nccl | staged)
 #   build/bin/ring_attention_bench ring attention (fused | nccl | staged; fp32 | bf16)
 #   build/bin/check_peer           peer-access matrix (the reference's check_peer)
+#   build/bin/ring_oneshot         one-shot legacy rings (gpu/ and CPU-attention programs)
 # `make mpi-shim` builds build/lib/libmpi_shim.so with csrc/mpi_shim/mpi.h: the
 # subset of the MPI C interface the reference prototype's programs call, over a
 # TCP store, so they build and run unmodified under torchrun without an MPI.
@@ -65,6 +66,10 @@ $(BIN)/ring_attention_bench: $(OBJ)/bench/ring_attention_bench.o $(COMM_OBJ) $(S
     $(OBJ)/ops/attn_api.o | $(BIN)
 	$(CXX) -o $@ $^ $(GPU_LIBS)
 
+$(BIN)/ring_oneshot: $(OBJ)/bench/ring_oneshot.o $(COMM_OBJ) $(OBJ)/kernels/legacy_fp32.o \
+    $(OBJ)/host/cpu_attention.o | $(BIN)
+	$(CXX) -o $@ $^ $(GPU_LIBS)
+
 $(BIN)/check_peer: csrc/bench/check_peer.cpp | $(BIN)
 	$(CXX) -O2 -std=c++17 -isystem $(CUDA_HOME)/include -o $@ $< -L$(CUDA_HOME)/lib64 -Wl,-rpath,$(CUDA_HOME)/lib64 -lcudart
 
@@ -81,7 +86,7 @@ $(LIB)/libmpi_shim.so: csrc/mpi_shim/mpi_shim.cpp csrc/mpi_shim/mpi.h
 mpi-shim: $(LIB)/libmpi_shim.so
 
 cuda-tools: $(BIN)/ring_loop_bench $(BIN)/ring_attention_bench $(BIN)/check_peer \
-    $(BIN)/dist_selftest
+    $(BIN)/dist_selftest $(BIN)/ring_oneshot
 
 clean:
 	rm -rf $(BIN) $(OBJ) $(LIB)

@@ -30,6 +30,36 @@ def test_usage_and_bad_arguments():
         assert p.returncode == 1 and "Usage:" in p.stdout
 
 
+@pytest.mark.parametrize("nproc", [2, 3])
+def test_oneshot_native_host_ring(tmp_path, nproc):
+    """build/bin/ring_oneshot --cpu: the CPU-attention legacy ring on host
+    memory only (staged transport through the MPI subset), the reference's
+    per-step lines, and dumps that pass verify_full."""
+    exe = _exe("ring_oneshot")
+    out = _torchrun(exe, ["--attention", "cpu", "--cpu", "--seq", "384", "--out-dir",
+                          str(tmp_path)], nproc, tmp_path)
+    for r in range(nproc):
+        assert f"[Rank {r}] step 0: attention on own KV" in out
+        for s in range(1, nproc):
+            assert f"[Rank {r}] step {s}: KV from rank {(r - s) % nproc} | MPI=" in out
+        assert f"[Rank {r}] output dumped to ring_output_rank{r}.bin" in out
+    v = subprocess.run([_exe("verify_full"), str(tmp_path), str(nproc), str(384 * 64 * 4)],
+                       capture_output=True, text=True, timeout=300)
+    assert v.returncode == 0 and "Overall: ALL PASS" in v.stdout, v.stdout
+
+
+def test_oneshot_native_arguments():
+    exe = _exe("ring_oneshot")
+    p = subprocess.run([exe, "--backend", "bogus"], capture_output=True, text=True, timeout=60)
+    assert p.returncode == 1 and "Usage:" in p.stdout
+    p = subprocess.run([exe, "--cpu", "--attention", "gpu"], capture_output=True, text=True,
+                       timeout=60)
+    assert p.returncode == 1
+    p = subprocess.run([exe, "--attention", "cpu", "--cpu"], capture_output=True, text=True,
+                       timeout=60, env={k: v for k, v in os.environ.items() if k != "WORLD_SIZE"})
+    assert p.returncode == 1 and "Need at least 2 processes" in p.stdout
+
+
 def _port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
