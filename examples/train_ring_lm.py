@@ -12,6 +12,11 @@ the ranks use gloo and the fp32 `torch` backend (use small sizes). The data is
 synthetic: a fixed seeded batch of a repeating token pattern with noise, which
 a working model learns quickly, so the printed loss should fall well below
 ln(vocab). Rank 0 prints one line per step and a final JSON summary.
+
+--save PATH writes a checkpoint (model and optimizer state, step count) at the
+end; --resume PATH starts from one. Parameters are replicated, so rank 0 writes
+and every rank reads the same file; a resumed run continues exactly where the
+saved one stopped (same losses as an uninterrupted run on the same ranks).
 """
 from __future__ import annotations
 
@@ -49,6 +54,8 @@ def parse(argv=None):
     ap.add_argument("--backend", default=None,
                     help="ring backend (default: fused on GPUs, torch without)")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--save", default=None, help="checkpoint written at the end")
+    ap.add_argument("--resume", default=None, help="checkpoint to start from")
     return ap.parse_args(argv)
 
 
@@ -84,9 +91,15 @@ def main(argv=None):
     local_ids = lay.shard(ids, rank).to(dev)
     targets = shard_targets(ids, lay, rank).to(dev)
 
+    start = 0
+    if a.resume:
+        ck = torch.load(a.resume, map_location=dev, weights_only=True)
+        model.load_state_dict(ck["model"])
+        opt.load_state_dict(ck["optimizer"])
+        start = int(ck["step"])
     losses = []
     t0 = time.time()
-    for step in range(a.steps):
+    for step in range(start, start + a.steps):
         opt.zero_grad(set_to_none=True)
         loss = model.loss(local_ids, targets, lay, rank, backend=backend)
         loss.backward()
@@ -104,6 +117,9 @@ def main(argv=None):
     if use_cuda:
         torch.cuda.synchronize()
     wall = time.time() - t0
+    if a.save and rank == 0:
+        torch.save({"model": model.state_dict(), "optimizer": opt.state_dict(),
+                    "step": start + a.steps}, a.save)
     if rank == 0:
         print(json.dumps({"world": world, "seq": a.seq, "layout": a.layout, "backend": backend,
                           "dtype": str(dtype).replace("torch.", ""), "steps": a.steps,
