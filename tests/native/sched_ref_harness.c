@@ -9,7 +9,7 @@
  *
  * Output (one record per line, doubles with 17 significant digits):
  *   T row col q_begin q_end k_begin k_end active total cost density
- *   RR gpu... | LPT_SCAN gpu... | LPT_HEAP gpu...        task -> gpu maps
+ *   RR gpu... | LPT_SCAN gpu... | LPT_HEAP gpu... | LPT_AUTO gpu...  task -> gpu maps
  *   MOVE moved gpu...        one move repair applied to the round-robin map
  *   SWAP swapped gpu...      one swap repair applied to the round-robin map
  *                            ("SWAP n/a" with more gpus than tasks: the
@@ -61,6 +61,8 @@ int main(int argc, char** argv) {
   print_map("LPT_SCAN", map, n);
   assign_lpt(tasks, n, loads, gpus, map, LPT_HEAP);
   print_map("LPT_HEAP", map, n);
+  assign_lpt(tasks, n, loads, gpus, map, LPT_AUTO);
+  print_map("LPT_AUTO", map, n);
   struct row_task* rows = malloc(kMaxRows * sizeof(*rows));
   const int nr = build_row_tasks(&op, tasks, n, rows, kMaxRows);
   if (nr > 0) {

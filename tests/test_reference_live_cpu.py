@@ -280,6 +280,7 @@ def _our_sched_lines(seq, block, gpus, causal, alpha, beta):
         out.append("SWAP n/a")
     out.append(fmt("LPT_SCAN", s.assign_block_lpt(tasks, gpus, "scan").task_to_gpu))
     out.append(fmt("LPT_HEAP", s.assign_block_lpt(tasks, gpus, "heap").task_to_gpu))
+    out.append(fmt("LPT_AUTO", s.assign_block_lpt(tasks, gpus, "auto").task_to_gpu))
     if s.num_row_blocks(shape) <= 256:
         rows = s.build_row_tasks(shape, tasks)
         out += [f"R {r.row} {r.num_blocks} {r.num_cols_needed} {g17(r.comp_cost)} "
@@ -293,8 +294,8 @@ def _our_sched_lines(seq, block, gpus, causal, alpha, beta):
 def test_scheduler_library_matches_reference_functions(tmp_path, ref_bin):
     """Every intermediate of the workload model and the schedulers (block tasks
     with ranges, counts, costs and densities; round-robin, one move repair, one
-    swap repair with the reference's partner indexing, block LPT in scan and
-    heap modes, row tasks, row LPT, contiguous DP maps) against the reference's
+    swap repair with the reference's partner indexing, block LPT in scan,
+    heap and auto modes, row tasks, row LPT, contiguous DP maps) against the reference's
     own workload.c / scheduler.c, on seeded random workloads."""
     import random
     src = subprocess.run(["bash", os.path.join(ROOT, "benchmarks/build_reference.sh"),
