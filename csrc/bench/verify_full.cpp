@@ -58,25 +58,46 @@ void parallel_for(int64_t n, F&& f) {
 }
 
 // Reference-faithful fp32 oracle (two passes, fp32 sums, no scale, K == V).
+// Every sum runs in the reference checker's order (over d for a score, over j
+// for the row sum and each output element); rows are processed kRows at a time
+// with the row index innermost, so the compiler can put the rows in SIMD lanes
+// without reordering any one row's sums.
 void legacy_attention(const std::vector<float>& Q, int seq_q, const std::vector<float>& KV,
                       int total_k, int dim, std::vector<float>& out) {
-  parallel_for(seq_q, [&](int64_t i) {
-    std::vector<float> scores(total_k);
-    float row_max = -FLT_MAX;
+  constexpr int kRows = 8;
+  const int64_t blocks = (seq_q + kRows - 1) / kRows;
+  parallel_for(blocks, [&](int64_t b) {
+    const int i0 = int(b) * kRows, nr = std::min(kRows, seq_q - i0);
+    std::vector<float> qt(size_t(dim) * kRows, 0.0f);  // [d][row]
+    for (int r = 0; r < nr; ++r)
+      for (int d = 0; d < dim; ++d) qt[size_t(d) * kRows + r] = Q[size_t(i0 + r) * dim + d];
+    std::vector<float> scores(size_t(total_k) * kRows);  // [j][row]
+    float row_max[kRows], row_sum[kRows];
+    for (int r = 0; r < kRows; ++r) row_max[r] = -FLT_MAX, row_sum[r] = 0.0f;
     for (int j = 0; j < total_k; ++j) {
-      float s = 0.0f;
-      for (int d = 0; d < dim; ++d) s += Q[i * dim + d] * KV[size_t(j) * dim + d];
-      scores[j] = s;
-      row_max = std::max(row_max, s);
+      float s[kRows] = {};
+      const float* kvj = &KV[size_t(j) * dim];
+      for (int d = 0; d < dim; ++d)
+        for (int r = 0; r < kRows; ++r) s[r] += qt[size_t(d) * kRows + r] * kvj[d];
+      for (int r = 0; r < kRows; ++r) {
+        scores[size_t(j) * kRows + r] = s[r];
+        row_max[r] = std::max(row_max[r], s[r]);
+      }
     }
-    float row_sum = 0.0f;
-    std::vector<float> acc(dim, 0.0f);
+    std::vector<float> acc(size_t(dim) * kRows, 0.0f);  // [d][row]
     for (int j = 0; j < total_k; ++j) {
-      const float w = std::exp(scores[j] - row_max);
-      row_sum += w;
-      for (int d = 0; d < dim; ++d) acc[d] += w * KV[size_t(j) * dim + d];
+      float w[kRows];
+      for (int r = 0; r < kRows; ++r) {
+        w[r] = std::exp(scores[size_t(j) * kRows + r] - row_max[r]);
+        row_sum[r] += w[r];
+      }
+      const float* kvj = &KV[size_t(j) * dim];
+      for (int d = 0; d < dim; ++d)
+        for (int r = 0; r < kRows; ++r) acc[size_t(d) * kRows + r] += w[r] * kvj[d];
     }
-    for (int d = 0; d < dim; ++d) out[i * dim + d] = acc[d] / row_sum;
+    for (int r = 0; r < nr; ++r)
+      for (int d = 0; d < dim; ++d)
+        out[size_t(i0 + r) * dim + d] = acc[size_t(d) * kRows + r] / row_sum[r];
   });
 }
 
