@@ -44,3 +44,18 @@ def test_checkpoint_resume_continues_exactly(tmp_path):
     first = _train(tmp_path, 29795, ["--steps", "4", "--save", ck])
     second = _train(tmp_path, 29796, ["--steps", "4", "--resume", ck])
     assert first + second == full
+
+
+def test_quickstart_example_matches_single_device():
+    """examples/ring_attention_quickstart.py on 3 gloo ranks: the gathered
+    output and query gradient match attention over the whole sequence."""
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=3",
+           "--master-addr", "127.0.0.1", "--master-port", "29797",
+           os.path.join(ROOT, "examples", "ring_attention_quickstart.py"), "--seq", "384",
+           "--heads", "4", "--kv-heads", "2", "--head-dim", "32"]
+    p = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True, timeout=300,
+                       env=dict(os.environ, OMP_NUM_THREADS="1", CUDA_VISIBLE_DEVICES=""))
+    assert p.returncode == 0, p.stdout + p.stderr
+    line = [l for l in p.stdout.splitlines() if l.startswith("world=3")][0]
+    vals = dict(kv.split("=") for kv in line.split() if kv.startswith("max"))
+    assert float(vals["max|out-ref|"]) < 1e-5 and float(vals["max|dq-ref|"]) < 1e-5
