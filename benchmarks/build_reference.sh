@@ -31,10 +31,10 @@ ARCH=(-gencode arch=compute_100a,code=sm_100a)
 mkdir -p "$OUT/bin"
 BIN=$(cd "$OUT/bin" && pwd)
 
-cc_c() {   # name sources... -- extra flags
+cc_c() {   # name sources... (flags as the reference's own build lines: -O2)
   local name=$1; shift
   echo "  gcc  $name"
-  gcc -O3 -std=gnu11 -o "$BIN/$name" "$@" -lm
+  gcc -O2 -o "$BIN/$name" "$@" -lm
 }
 cc_cu() {  # name source [extra flags]
   local name=$1 src=$2; shift 2
@@ -44,7 +44,7 @@ cc_cu() {  # name source [extra flags]
 
 echo "building the reference from $REF into $OUT/bin"
 # CPU programs
-cc_c rattn_demo "$REF/workload/demo.c" "$REF/workload/workload.c" "$REF/workload/scheduler.c" -I"$REF/workload"
+cc_c rattn_demo -std=c11 "$REF/workload/demo.c" "$REF/workload/workload.c" "$REF/workload/scheduler.c" -I"$REF/workload"
 cc_c verify_full "$REF/ring/attention/verify_full.c"
 cc_c ring_test "$REF/ring/ring_test.c" -I"$SHIM_INC" -L"$SHIM_LIB" -Wl,-rpath,"$SHIM_LIB" -lmpi_shim
 if [ "${1:-}" = "--cpu-only" ]; then
