@@ -8,6 +8,10 @@
 #
 # Env: NP (2) SEQ (1024 tokens per rank) ABS_TOL (1e-3) REL_TOL (1e-5)
 #      RESULTS_ROOT (results) RUN_LABEL (timestamp) CHECK_P2P (1) CHECK_CPU (1)
+#      NATIVE (0; 1 runs build/bin/ring_oneshot instead of the Python driver)
+#      REFERENCE (0; 1 also runs the reference's own one-shot programs,
+#      gpu/ring_attention_{staged,cuda_aware,nccl}_gpu built unmodified by
+#      benchmarks/build_reference.sh, seq 1024 only, and compares their dumps)
 set -euo pipefail
 cd "$(dirname "$0")/.."
 export PYTHONPATH="$PWD${PYTHONPATH:+:$PYTHONPATH}"
@@ -34,9 +38,14 @@ run_backend() {  # label, args...
   mkdir -p "$dir"
   echo ""
   echo "===== gpu backend=$label ====="
+  if [[ "${NATIVE:-0}" == 1 ]]; then
+    local prog=(--no-python "$PWD/build/bin/ring_oneshot")
+  else
+    local prog=(-m multi_gpu_flashattention_b200.benchmarks.ring_oneshot)
+  fi
   timeout -k 30 600 python -m torch.distributed.run --nnodes=1 --nproc-per-node "$NP" \
       --master-addr 127.0.0.1 --master-port "$PORT" \
-      -m multi_gpu_flashattention_b200.benchmarks.ring_oneshot --seq "$SEQ" --out-dir "$dir" "$@" \
+      "${prog[@]}" --seq "$SEQ" --out-dir "$dir" "$@" \
       2>&1 | tee "$dir/run.log" | grep -E "step|done" || true
   PORT=$((PORT + 1))
   echo "--- full reference check: $label ---"
@@ -77,6 +86,22 @@ fi
 if [[ "$CHECK_CPU" == 1 ]]; then
   run_backend cpu_staged --attention cpu --backend staged
   compare_pair gpu_vs_cpu_attention "$OUT/staged" "$OUT/cpu_staged"
+fi
+if [[ "${REFERENCE:-0}" == 1 && "$SEQ" == 1024 ]]; then
+  [ -x baseline/_ref/bin/ring_attention_nccl_gpu ] || benchmarks/build_reference.sh
+  for prog in staged cuda_aware nccl; do
+    dir="$OUT/reference_$prog"
+    mkdir -p "$dir"
+    echo ""
+    echo "===== reference program ring_attention_${prog}_gpu ====="
+    (cd "$dir" && timeout -k 30 600 python -m torch.distributed.run --nnodes=1 \
+        --nproc-per-node "$NP" --master-addr 127.0.0.1 --master-port "$PORT" --no-python \
+        "$OLDPWD/baseline/_ref/bin/ring_attention_${prog}_gpu" 2>&1 | tee run.log \
+        | grep -E "step|done" || true)
+    PORT=$((PORT + 1))
+    ./build/bin/verify_full "$dir" "$NP" "$SIZE" | tee "$dir/verify.log" | tail -1
+    compare_pair "staged_vs_reference_$prog" "$OUT/staged" "$dir"
+  done
 fi
 echo ""
 echo "========== GPU Correctness Check Done =========="
