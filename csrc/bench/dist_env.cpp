@@ -37,6 +37,7 @@ void nccl_check(ncclResult_t r, const char* what) {
 
 Dist Dist::from_env(int timeout_s, bool need_gpu) {
   Dist d;
+  d.timeout_s_ = timeout_s;
   d.world_ = env_int("WORLD_SIZE", 1);
   d.rank_ = env_int("RANK", 0);
   if (d.world_ < 1 || d.rank_ < 0 || d.rank_ >= d.world_)
@@ -84,6 +85,7 @@ Dist& Dist::operator=(Dist&& o) noexcept {
     mpi_ = o.mpi_;
     o.mpi_ = false;
     store_p2p_ = o.store_p2p_;
+    timeout_s_ = o.timeout_s_;
   }
   return *this;
 }
@@ -138,7 +140,7 @@ void Dist::host_sendrecv(const void* send, size_t n, int to, void* recv, int fro
   }
   if (!mpi_ && !store_p2p_) {  // collective: every rank's first host_sendrecv
     try {
-      mgfa::mpi_shim::init_with_store(store_, rank_, world_);
+      mgfa::mpi_shim::init_with_store(store_, rank_, world_, timeout_s_);
       mpi_ = true;
     } catch (const std::exception& e) {  // e.g. no /dev/shm: every rank falls back
       std::fprintf(stderr, "[rank %d] shared-memory transport unavailable (%s); host send/recv "

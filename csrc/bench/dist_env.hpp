@@ -61,6 +61,7 @@ class Dist {
   ncclComm_t comm_ = nullptr;
   bool mpi_ = false;        // the MPI subset was started on store_ (host_sendrecv)
   bool store_p2p_ = false;  // it could not start: host_sendrecv goes through the store
+  int timeout_s_ = 300;     // bound of the store's and the MPI subset's waits
 };
 
 // Prints "[tag] NCCL error ..." and aborts the process group on failure.

@@ -724,9 +724,10 @@ State* new_state(int rank, int world) {
 }  // namespace
 
 void mgfa::mpi_shim::init_with_store(c10::intrusive_ptr<c10d::Store> store, int rank,
-                                     int world) {
+                                     int world, int timeout_s) {
   if (g) return;
   g = new_state(rank, world);
+  if (timeout_s > 0) g->timeout_s = timeout_s;
   try {
     if (world > 1) {
       g->store = std::move(store);

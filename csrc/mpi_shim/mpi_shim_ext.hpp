@@ -9,7 +9,9 @@
 namespace mgfa::mpi_shim {
 
 // Collective over all `world` ranks (maps the shared-memory mailbox). Throws
-// std::runtime_error on failure; a second call is a no-op.
-void init_with_store(c10::intrusive_ptr<c10d::Store> store, int rank, int world);
+// std::runtime_error on failure; a second call is a no-op. timeout_s > 0 bounds
+// every wait of the subset (otherwise MPI_SHIM_TIMEOUT_S, default 600 s).
+void init_with_store(c10::intrusive_ptr<c10d::Store> store, int rank, int world,
+                     int timeout_s = 0);
 
 }  // namespace mgfa::mpi_shim
