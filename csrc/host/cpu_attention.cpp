@@ -29,32 +29,52 @@ void parallel_rows(int64_t rows, int threads, Fn fn) {
 
 }  // namespace
 
+// Rows go kRows at a time with the row index innermost, so the compiler can put
+// rows in SIMD lanes; every sum still runs in the reference's order (over d for
+// a score, over j for the row sum and each accumulator element), so the results
+// are the reference's bit for bit.
 void cpu_attention_partial(const float* q, int64_t seq_q, const float* k, const float* v,
                            int64_t seq_k, int64_t dim, float scale, float* acc, float* m,
                            float* l, int threads) {
+  constexpr int kRows = 8;
   parallel_rows(seq_q, threads, [=](int64_t r0, int64_t r1) {
-    std::vector<float> s(size_t(std::max<int64_t>(seq_k, 1)));
-    for (int64_t i = r0; i < r1; ++i) {
-      const float* qi = q + i * dim;
-      float mx = -FLT_MAX;
+    std::vector<float> qt(size_t(dim) * kRows), at(size_t(dim) * kRows);  // [d][row]
+    std::vector<float> s(size_t(std::max<int64_t>(seq_k, 1)) * kRows);    // [j][row]
+    for (int64_t i0 = r0; i0 < r1; i0 += kRows) {
+      const int nr = int(std::min<int64_t>(kRows, r1 - i0));
+      std::fill(qt.begin(), qt.end(), 0.f);
+      for (int r = 0; r < nr; ++r)
+        for (int64_t d = 0; d < dim; ++d) qt[size_t(d) * kRows + r] = q[(i0 + r) * dim + d];
+      float mx[kRows], sum[kRows];
+      for (int r = 0; r < kRows; ++r) mx[r] = -FLT_MAX, sum[r] = 0.f;
       for (int64_t j = 0; j < seq_k; ++j) {
         const float* kj = k + j * dim;
-        float dot = 0.f;
-        for (int64_t d = 0; d < dim; ++d) dot += qi[d] * kj[d];
-        s[size_t(j)] = dot * scale;
-        mx = std::max(mx, s[size_t(j)]);
+        float dot[kRows] = {};
+        for (int64_t d = 0; d < dim; ++d)
+          for (int r = 0; r < kRows; ++r) dot[r] += qt[size_t(d) * kRows + r] * kj[d];
+        for (int r = 0; r < kRows; ++r) {
+          const float sc = dot[r] * scale;
+          s[size_t(j) * kRows + r] = sc;
+          mx[r] = std::max(mx[r], sc);
+        }
       }
-      float* ai = acc + i * dim;
-      std::fill(ai, ai + dim, 0.f);
-      float sum = 0.f;
+      std::fill(at.begin(), at.end(), 0.f);
       for (int64_t j = 0; j < seq_k; ++j) {
-        const float w = std::exp(s[size_t(j)] - mx);
-        sum += w;
+        float w[kRows];
+        for (int r = 0; r < kRows; ++r) {
+          w[r] = std::exp(s[size_t(j) * kRows + r] - mx[r]);
+          sum[r] += w[r];
+        }
         const float* vj = v + j * dim;
-        for (int64_t d = 0; d < dim; ++d) ai[d] += w * vj[d];
+        for (int64_t d = 0; d < dim; ++d)
+          for (int r = 0; r < kRows; ++r) at[size_t(d) * kRows + r] += w[r] * vj[d];
       }
-      m[i] = mx;
-      l[i] = sum;
+      for (int r = 0; r < nr; ++r) {
+        float* ai = acc + (i0 + r) * dim;
+        for (int64_t d = 0; d < dim; ++d) ai[d] = at[size_t(d) * kRows + r];
+        m[i0 + r] = mx[r];
+        l[i0 + r] = sum[r];
+      }
     }
   });
 }
