@@ -109,3 +109,28 @@ def _probe_rank(rank, world, which):
 @pytest.mark.parametrize("which,world", [("ring_test", 3), ("ring_cuda", 2)])
 def test_transport_probes(which, world):
     run_ranks(_probe_rank, world, which)
+
+
+def test_native_and_python_oneshot_dumps_identical(tmp_path):
+    """The native one-shot ring (build/bin/ring_oneshot --cpu) and the Python
+    driver run the same host attention on the same inputs: their dumps agree
+    bit for bit."""
+    import sys
+    exe = os.path.join(ROOT, "build", "bin", "ring_oneshot")
+    if not os.path.exists(exe):
+        pytest.skip("ring_oneshot not built (make cuda-tools)")
+    seq, world = 256, 3
+    py_dir, nat_dir = tmp_path / "py", tmp_path / "native"
+    py_dir.mkdir()
+    nat_dir.mkdir()
+    run_ranks(_oneshot_rank, world, str(py_dir), seq)
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={world}", "--master-addr", "127.0.0.1", "--master-port", "29798",
+           "--no-python", exe, "--attention", "cpu", "--cpu", "--seq", str(seq), "--out-dir",
+           str(nat_dir)]
+    p = subprocess.run(cmd, capture_output=True, text=True, timeout=300, cwd=ROOT)
+    assert p.returncode == 0, p.stdout + p.stderr
+    for r in range(world):
+        a = (py_dir / f"ring_output_rank{r}.bin").read_bytes()
+        b = (nat_dir / f"ring_output_rank{r}.bin").read_bytes()
+        assert len(a) == seq * 64 * 4 and a == b, r
