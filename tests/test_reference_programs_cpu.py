@@ -4,6 +4,7 @@ with stand-in programs that print the reference's exact line formats
 (ring/loop/ring_loop_cuda_aware.cu:226-231, ring/attention/bench/
 ring_attention_cuda_aware_gpu_bench.cu and ring_attention_staged_gpu_bench.cu
 avg_total lines)."""
+import os
 import stat
 
 import pytest
@@ -62,3 +63,16 @@ def test_missing_program(tmp_path, monkeypatch):
     monkeypatch.setenv("MGFA_REF_BIN", str(tmp_path))
     rec = rp.run("ring_loop_nccl", 2, 1024, 1, 1, 29783, 60)
     assert "unavailable" in rec
+
+
+def test_build_script_reports_a_missing_reference_tree(tmp_path):
+    """benchmarks/build_reference.sh exits 2 (the callers' 'skip' signal) when
+    no reference tree is found, and builds nothing."""
+    import subprocess
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, REF_SRC=str(tmp_path / "absent"), OUT=str(tmp_path / "out"))
+    for args in ([], ["--cpu-only"], ["--print-src"]):
+        p = subprocess.run(["bash", "benchmarks/build_reference.sh"] + args, cwd=root, env=env,
+                           capture_output=True, text=True, timeout=120)
+        assert p.returncode == 2, (args, p.stdout, p.stderr)
+    assert not (tmp_path / "out").exists()
