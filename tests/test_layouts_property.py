@@ -75,3 +75,19 @@ def test_ring_owners(world, rank, step):
 def test_unsplittable_sizes_are_rejected(kind, seq, world):
     with pytest.raises(Exception):
         RingLayout(kind, seq, world)
+
+
+@settings(max_examples=60, deadline=None)
+@given(layouts())
+def test_step_work_equals_brute_force(lay):
+    """Each (rank, owner) pair's visible (query, key) count equals a direct
+    count over the two shards' global positions."""
+    if lay.seq > 2048:
+        return
+    for r in range(lay.world):
+        qp = lay.positions(r)
+        for o in range(lay.world):
+            kp = lay.positions(o)
+            want = int((kp[None, :] <= qp[:, None]).sum()) if lay.mask == "causal" \
+                else qp.numel() * kp.numel()
+            assert lay.step_work(r, o) == want
