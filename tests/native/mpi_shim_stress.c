@@ -6,9 +6,12 @@
  * sends of a round as Isend/Irecv in a shuffled order that keeps plan order
  * within every (peer, tag) stream (MPI matches the n-th receive of a stream
  * with the n-th send), completes them with Waitall or a Testall loop, and
- * checks every payload byte. Prints "rank <r> stress OK
- * <messages>" or "rank <r> FAIL <what>". Arguments: [rounds] [messages per
- * round] [seed]. */
+ * checks every payload byte. Where a CUDA device is visible, about half of the
+ * buffers (chosen per message and side) are device buffers, so host-to-device,
+ * device-to-host and device-to-device messages mix with host ones. Prints
+ * "rank <r> stress OK <messages> device <0|1>" or "rank <r> FAIL <what>".
+ * Arguments: [rounds] [messages per round] [seed]. */
+#include <cuda_runtime.h>
 #include <mpi.h>
 #include <stdint.h>
 #include <stdio.h>
@@ -59,6 +62,11 @@ int main(int argc, char** argv) {
   uint8_t** bufs = (uint8_t**)calloc(2 * (size_t)per_round, sizeof(uint8_t*));
   int* order = (int*)malloc(sizeof(int) * 2 * (size_t)per_round);
   long checked = 0;
+  int ndev = 0;
+  const int gpu = cudaGetDeviceCount(&ndev) == cudaSuccess && ndev > 0;
+  if (!gpu) cudaGetLastError();
+  else CHECK(cudaSetDevice(rank_ % ndev) == cudaSuccess, "set device");
+  uint8_t** devs = (uint8_t**)calloc(2 * (size_t)per_round, sizeof(uint8_t*));
   rng_state = seed * 0x9E3779B97F4A7C15ull + 1;
   for (int round = 0; round < rounds; ++round) {
     for (int i = 0; i < per_round; ++i) {  /* the same plan on every rank */
@@ -106,12 +114,23 @@ int main(int argc, char** argv) {
       const Msg* m = &plan[op / 2];
       uint8_t* b = (uint8_t*)malloc(m->bytes ? m->bytes : 1);
       bufs[k] = b;
+      devs[k] = NULL;
+      /* device or host buffer, decided per message and side from its salt */
+      const int on_dev = gpu && ((m->salt >> (op % 2 ? 3 : 7)) & 1);
+      if (on_dev) CHECK(cudaMalloc((void**)&devs[k], m->bytes ? m->bytes : 1) == cudaSuccess,
+                        "cudaMalloc");
       if (op % 2 == 0) {
         for (size_t i = 0; i < m->bytes; ++i) b[i] = byte_of(m, i);
-        MPI_Isend(b, (int)m->bytes, MPI_BYTE, m->dst, m->tag, MPI_COMM_WORLD, &reqs[k]);
+        if (on_dev) CHECK(cudaMemcpy(devs[k], b, m->bytes, cudaMemcpyHostToDevice) == cudaSuccess,
+                          "H2D");
+        MPI_Isend(on_dev ? devs[k] : b, (int)m->bytes, MPI_BYTE, m->dst, m->tag, MPI_COMM_WORLD,
+                  &reqs[k]);
       } else {
         memset(b, 0xEE, m->bytes ? m->bytes : 1);
-        MPI_Irecv(b, (int)m->bytes, MPI_BYTE, m->src, m->tag, MPI_COMM_WORLD, &reqs[k]);
+        if (on_dev) CHECK(cudaMemset(devs[k], 0xEE, m->bytes ? m->bytes : 1) == cudaSuccess,
+                          "memset");
+        MPI_Irecv(on_dev ? devs[k] : b, (int)m->bytes, MPI_BYTE, m->src, m->tag, MPI_COMM_WORLD,
+                  &reqs[k]);
       }
     }
     if (mode == 0) {
@@ -128,20 +147,25 @@ int main(int argc, char** argv) {
       const int op = order[k];
       const Msg* m = &plan[op / 2];
       if (op % 2 == 1) {
+        if (devs[k])
+          CHECK(cudaMemcpy(bufs[k], devs[k], m->bytes, cudaMemcpyDeviceToHost) == cudaSuccess,
+                "D2H");
         for (size_t i = 0; i < m->bytes; ++i)
           if (bufs[k][i] != byte_of(m, i)) CHECK(0, "payload");
         ++checked;
       }
+      if (devs[k]) cudaFree(devs[k]);
       free(bufs[k]);
     }
   }
   CHECK(MPI_Barrier(MPI_COMM_WORLD) == MPI_SUCCESS, "barrier");
-  printf("rank %d stress OK %ld\n", rank_, checked);
+  printf("rank %d stress OK %ld device %d\n", rank_, checked, gpu);
   fflush(stdout);
   free(plan);
   free(reqs);
   free(bufs);
   free(order);
+  free(devs);
   MPI_Finalize();
   return 0;
 }

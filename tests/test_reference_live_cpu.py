@@ -242,9 +242,13 @@ def test_shim_randomised_traffic(tmp_path, shim, nproc, seed, port, piece):
     many pieces (4 KB pieces in the second case), completed by Waitall or
     Testall; every payload byte checked."""
     exe = str(tmp_path / "mpi_shim_stress")
+    cuda = os.environ.get("CUDA_HOME", "/usr/local/cuda")
     subprocess.check_call(["gcc", "-O2", "-std=gnu11", "-I", os.path.join(ROOT, "csrc/mpi_shim"),
-                           "-o", exe, os.path.join(ROOT, "tests/native/mpi_shim_stress.c"),
-                           "-L", shim, f"-Wl,-rpath,{shim}", "-lmpi_shim"])
+                           "-I", os.path.join(cuda, "include"), "-o", exe,
+                           os.path.join(ROOT, "tests/native/mpi_shim_stress.c"),
+                           "-L", shim, f"-Wl,-rpath,{shim}", "-lmpi_shim",
+                           "-L", os.path.join(cuda, "lib64"),
+                           f"-Wl,-rpath,{os.path.join(cuda, 'lib64')}", "-lcudart"])
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={nproc}", "--master-addr", "127.0.0.1",
            "--master-port", str(port), "--no-python", exe, "25", "32", str(seed)]
@@ -252,7 +256,7 @@ def test_shim_randomised_traffic(tmp_path, shim, nproc, seed, port, piece):
                        env=dict(os.environ, OMP_NUM_THREADS="1", MPI_SHIM_PIECE_BYTES=piece),
                        cwd=ROOT)
     assert p.returncode == 0, p.stdout + p.stderr
-    counts = [int(l.split()[-1]) for l in p.stdout.splitlines() if "stress OK" in l]
+    counts = [int(l.split()[-3]) for l in p.stdout.splitlines() if "stress OK" in l]
     assert len(counts) == nproc and sum(counts) == 25 * 32, p.stdout
 
 
