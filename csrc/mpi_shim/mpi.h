@@ -4,7 +4,8 @@
  * environment variables (RANK, WORLD_SIZE, MASTER_ADDR, MASTER_PORT); messages
  * travel through a TCP key-value store, and buffers in device memory are staged
  * through host memory (CUDA-aware semantics). One communicator (the world) and
- * the point-to-point, barrier, broadcast and reduce calls the benchmarks use. */
+ * the point-to-point, barrier, broadcast and reduce calls the benchmarks use,
+ * plus allreduce, gather, allgather and scatter. */
 #ifndef MGFA_MPI_SHIM_H
 #define MGFA_MPI_SHIM_H
 
@@ -63,10 +64,21 @@ int MPI_Comm_split_type(MPI_Comm comm, int split_type, int key, MPI_Info info,
 int MPI_Comm_free(MPI_Comm* comm);
 double MPI_Wtime(void);
 
+int MPI_Type_size(MPI_Datatype datatype, int* size);
+int MPI_Get_count(const MPI_Status* status, MPI_Datatype datatype, int* count);
+
 int MPI_Barrier(MPI_Comm comm);
 int MPI_Bcast(void* buffer, int count, MPI_Datatype datatype, int root, MPI_Comm comm);
 int MPI_Reduce(const void* sendbuf, void* recvbuf, int count, MPI_Datatype datatype, MPI_Op op,
                int root, MPI_Comm comm);
+int MPI_Allreduce(const void* sendbuf, void* recvbuf, int count, MPI_Datatype datatype,
+                  MPI_Op op, MPI_Comm comm);
+int MPI_Gather(const void* sendbuf, int sendcount, MPI_Datatype sendtype, void* recvbuf,
+               int recvcount, MPI_Datatype recvtype, int root, MPI_Comm comm);
+int MPI_Allgather(const void* sendbuf, int sendcount, MPI_Datatype sendtype, void* recvbuf,
+                  int recvcount, MPI_Datatype recvtype, MPI_Comm comm);
+int MPI_Scatter(const void* sendbuf, int sendcount, MPI_Datatype sendtype, void* recvbuf,
+                int recvcount, MPI_Datatype recvtype, int root, MPI_Comm comm);
 
 int MPI_Send(const void* buf, int count, MPI_Datatype datatype, int dest, int tag,
              MPI_Comm comm);

@@ -42,8 +42,8 @@
 // process (post queued sends, match slots, start copies, poll their events,
 // free acknowledged slots), so blocking calls in any order cannot deadlock on
 // an acknowledgement. Every wait yields between polls and gives up after
-// MPI_SHIM_TIMEOUT_S seconds (default 600) with an error. The broadcast and
-// reduce wait in the store without driving progress.
+// MPI_SHIM_TIMEOUT_S seconds (default 600) with an error. The broadcast,
+// reduce, gather and scatter wait in the store without driving progress.
 #include "mpi.h"
 #include "mpi_shim_ext.hpp"
 
@@ -903,6 +903,96 @@ int MPI_Reduce(const void* sendbuf, void* recvbuf, int count, MPI_Datatype datat
     return MPI_SUCCESS;
   } catch (const std::exception& e) {
     return fail("MPI_Reduce", e);
+  }
+}
+
+int MPI_Type_size(MPI_Datatype datatype, int* size) {
+  try {
+    *size = int(type_size(datatype));
+    return MPI_SUCCESS;
+  } catch (const std::exception& e) {
+    return fail("MPI_Type_size", e);
+  }
+}
+
+int MPI_Get_count(const MPI_Status* status, MPI_Datatype datatype, int* count) {
+  try {
+    *count = status->count_bytes / int(type_size(datatype));
+    return MPI_SUCCESS;
+  } catch (const std::exception& e) {
+    return fail("MPI_Get_count", e);
+  }
+}
+
+int MPI_Allreduce(const void* sendbuf, void* recvbuf, int count, MPI_Datatype datatype,
+                  MPI_Op op, MPI_Comm comm) {
+  const int rc = MPI_Reduce(sendbuf, recvbuf, count, datatype, op, 0, comm);
+  return rc != MPI_SUCCESS ? rc : MPI_Bcast(recvbuf, count, datatype, 0, comm);
+}
+
+// Gather, allgather and scatter go through the store: every rank's block under
+// the call's key (host staging for device buffers, as the broadcast does).
+int MPI_Gather(const void* sendbuf, int sendcount, MPI_Datatype sendtype, void* recvbuf,
+               int recvcount, MPI_Datatype recvtype, int root, MPI_Comm) {
+  try {
+    const size_t sb = size_t(sendcount) * type_size(sendtype);
+    const size_t rb = size_t(recvcount) * type_size(recvtype);
+    if (!g || g->world == 1) {
+      if (g && g->rank == root) write_buffer(recvbuf, read_buffer(sendbuf, sb).data(), sb, rb);
+      return MPI_SUCCESS;
+    }
+    const std::string k = coll_key("gather");
+    g->store->set(k + "/" + std::to_string(g->rank), read_buffer(sendbuf, sb));
+    if (g->rank != root) return MPI_SUCCESS;
+    for (int r = 0; r < g->world; ++r) {
+      const std::string kr = k + "/" + std::to_string(r);
+      const std::vector<uint8_t> v = g->store->get(kr);
+      g->store->deleteKey(kr);
+      write_buffer(static_cast<char*>(recvbuf) + size_t(r) * rb, v.data(), v.size(), rb);
+    }
+    return MPI_SUCCESS;
+  } catch (const std::exception& e) {
+    return fail("MPI_Gather", e);
+  }
+}
+
+int MPI_Allgather(const void* sendbuf, int sendcount, MPI_Datatype sendtype, void* recvbuf,
+                  int recvcount, MPI_Datatype recvtype, MPI_Comm comm) {
+  try {
+    const int rc = MPI_Gather(sendbuf, sendcount, sendtype, recvbuf, recvcount, recvtype, 0, comm);
+    if (rc != MPI_SUCCESS) return rc;
+    const int world = g ? g->world : 1;
+    const size_t total = size_t(recvcount) * size_t(world);
+    return MPI_Bcast(recvbuf, int(total), recvtype, 0, comm);
+  } catch (const std::exception& e) {
+    return fail("MPI_Allgather", e);
+  }
+}
+
+int MPI_Scatter(const void* sendbuf, int sendcount, MPI_Datatype sendtype, void* recvbuf,
+                int recvcount, MPI_Datatype recvtype, int root, MPI_Comm) {
+  try {
+    const size_t sb = size_t(sendcount) * type_size(sendtype);
+    const size_t rb = size_t(recvcount) * type_size(recvtype);
+    if (!g || g->world == 1) {
+      write_buffer(recvbuf, read_buffer(sendbuf, sb).data(), sb, rb);
+      return MPI_SUCCESS;
+    }
+    const std::string k = coll_key("scatter");
+    if (g->rank == root) {
+      const std::vector<uint8_t> all = read_buffer(sendbuf, sb * size_t(g->world));
+      for (int r = 0; r < g->world; ++r)
+        g->store->set(k + "/" + std::to_string(r),
+                      std::vector<uint8_t>(all.begin() + long(size_t(r) * sb),
+                                           all.begin() + long(size_t(r + 1) * sb)));
+    }
+    const std::string mine = k + "/" + std::to_string(g->rank);
+    const std::vector<uint8_t> v = g->store->get(mine);
+    g->store->deleteKey(mine);
+    write_buffer(recvbuf, v.data(), v.size(), rb);
+    return MPI_SUCCESS;
+  } catch (const std::exception& e) {
+    return fail("MPI_Scatter", e);
   }
 }
 

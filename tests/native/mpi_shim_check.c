@@ -3,7 +3,8 @@
  * and exits non-zero on the first failed check. Covers: message order per
  * (source, tag), tags that overtake each other, Isend/Irecv with Waitall and
  * Testall, Sendrecv around the ring, Bcast from a non-zero root, Reduce
- * (MAX, MIN, SUM over double, float and int), Barrier, the shared-memory
+ * (MAX, MIN, SUM over double, float and int), Allreduce, Gather, Allgather,
+ * Scatter, Get_count and Type_size, Barrier, the shared-memory
  * split and Wtime; more sends in flight than a mailbox holds, a payload
  * larger than a mailbox slot, and repeated barriers. Rank 0 also prints the
  * host round-trip latency between ranks 0 and 1 ("latency_us <x>") and the
@@ -115,6 +116,30 @@ int main(int argc, char** argv) {
     CHECK(fmin == 1.0f, "reduce min");
     CHECK(isum == size_ * (size_ + 1) / 2, "reduce sum");
   }
+
+  /* allreduce, gather (to the last rank), allgather, scatter (from rank 0), counts */
+  double sin3[3] = {(double)rank_, 2.0 * rank_, 1.0}, sout3[3] = {0, 0, 0};
+  MPI_Allreduce(sin3, sout3, 3, MPI_DOUBLE, MPI_SUM, MPI_COMM_WORLD);
+  CHECK(sout3[0] == size_ * (size_ - 1) / 2.0 && sout3[1] == 2.0 * sout3[0] &&
+            sout3[2] == (double)size_, "allreduce");
+  int mine[2] = {rank_ * 10, rank_ * 10 + 1};
+  int* allv = (int*)malloc(2 * (size_t)size_ * sizeof(int));
+  MPI_Allgather(mine, 2, MPI_INT, allv, 2, MPI_INT, MPI_COMM_WORLD);
+  for (int r = 0; r < size_; ++r)
+    CHECK(allv[2 * r] == r * 10 && allv[2 * r + 1] == r * 10 + 1, "allgather");
+  for (int i = 0; i < 2 * size_; ++i) allv[i] = -1;
+  MPI_Gather(mine, 2, MPI_INT, allv, 2, MPI_INT, size_ - 1, MPI_COMM_WORLD);
+  if (rank_ == size_ - 1)
+    for (int r = 0; r < size_; ++r) CHECK(allv[2 * r] == r * 10, "gather");
+  for (int i = 0; i < 2 * size_; ++i) allv[i] = 100 + i;
+  int part[2] = {-1, -1};
+  MPI_Scatter(allv, 2, MPI_INT, part, 2, MPI_INT, 0, MPI_COMM_WORLD);
+  CHECK(part[0] == 100 + 2 * rank_ && part[1] == 101 + 2 * rank_, "scatter");
+  free(allv);
+  int cnt = -1, tsz = -1;
+  MPI_Get_count(&st, MPI_DOUBLE, &cnt);
+  MPI_Type_size(MPI_DOUBLE, &tsz);
+  CHECK(cnt == 4 && tsz == 8, "counts");
 
   /* more sends in flight than a mailbox has slots: the excess wait in the
    * sender's queue until the receiver frees slots */
