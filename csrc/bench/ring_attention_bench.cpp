@@ -80,7 +80,7 @@ struct Args {
   int64_t kv_size = 0;
   bool have_size = false;
   int warmup = 10, iters = 100;
-  std::string backend, numerics = "fp32", init = "legacy", layout = "contiguous", policy = "dp";
+  std::string backend, numerics = "fp32", init = "legacy", layout = "contiguous", policy = "lpt";
   bool causal = false, overlap = false, json = false;
   int heads = 1, kv_heads = 0, head_dim = 0;
   uint64_t seed = 0;

@@ -5,7 +5,8 @@
 // status, causal tile positions) lives here in a file-scope device array. Host
 // code never uses the array's name as a device pointer: in host code that name
 // is only a stand-in for the symbol, so each device's real address is looked up
-// once with cudaGetSymbolAddress and cached.
+// with cudaGetSymbolAddress (on every call outside stream capture; a captured
+// call reuses the last address found on its device).
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -48,8 +49,11 @@ void report(const char* what, cudaError_t e) {
   std::fprintf(stderr, "mgfa_attn_bwd_noalloc: %s: %s\n", what, cudaGetErrorString(e));
 }
 
-// Device address of the scratch array on the current device (set-up on first use).
-int scratch_for_current_device(unsigned char** out) {
+// Device address of the scratch array on the current device. Outside stream
+// capture the address is looked up on every call (cheap), so a call after a
+// device reset, which reloads the module, sees the new array; under capture
+// the address of the last uncaptured call on this device is reused.
+int scratch_for_current_device(bool capturing, unsigned char** out) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) {
@@ -58,7 +62,7 @@ int scratch_for_current_device(unsigned char** out) {
   }
   if (dev < 0 || dev >= kMaxDevices) return MGFA_NOALLOC_BAD_ARGUMENT;
   std::lock_guard<std::mutex> lock(g_mutex);
-  if (!g_scratch_ptr[dev]) {
+  if (!capturing) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_bwd_scratch);
     if (e != cudaSuccess || p == nullptr) {
@@ -66,6 +70,12 @@ int scratch_for_current_device(unsigned char** out) {
       return MGFA_NOALLOC_CUDA_ERROR;
     }
     g_scratch_ptr[dev] = p;
+  } else if (!g_scratch_ptr[dev]) {
+    std::fprintf(stderr,
+                 "mgfa_attn_bwd_noalloc: first call on device %d is under stream capture; "
+                 "make one call on this device outside capture first\n",
+                 dev);
+    return MGFA_NOALLOC_CUDA_ERROR;
   }
   *out = static_cast<unsigned char*>(g_scratch_ptr[dev]);
   return MGFA_NOALLOC_OK;
@@ -103,15 +113,29 @@ extern "C" __attribute__((visibility("default"))) int mgfa_attn_bwd_noalloc(
     return MGFA_NOALLOC_TOO_LARGE;
   }
 
+  // An error left pending by earlier, unrelated work belongs to its owner:
+  // report it without clearing it. From here on every error is this call's.
+  cudaError_t pending = cudaPeekAtLastError();
+  if (pending != cudaSuccess) {
+    report("a CUDA error was already pending on entry (left in place)", pending);
+    return MGFA_NOALLOC_CUDA_ERROR;
+  }
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  cudaError_t ce = cudaStreamIsCapturing(stream, &cap);
+  if (ce != cudaSuccess) {
+    cudaGetLastError();  // this call's own query error
+    report("cudaStreamIsCapturing", ce);
+    return MGFA_NOALLOC_CUDA_ERROR;
+  }
   unsigned char* scratch = nullptr;
-  int rc = scratch_for_current_device(&scratch);
+  int rc = scratch_for_current_device(cap != cudaStreamCaptureStatusNone, &scratch);
   if (rc != MGFA_NOALLOC_OK) return rc;
   uint32_t* status = reinterpret_cast<uint32_t*>(scratch);
   int* q_pos = reinterpret_cast<int*>(scratch + kStatusBytes);
   int* k_pos = q_pos + n_q_tiles;
   float* lse2 = reinterpret_cast<float*>(scratch + kStatusBytes + pos_region);
   float* delta = reinterpret_cast<float*>(scratch + kStatusBytes + pos_region + vec_bytes);
-  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
 
   try {
     cudaError_t e = cudaMemsetAsync(status, 0, kStatusBytes, stream);  // the status starts at 0
@@ -171,6 +195,36 @@ extern "C" __attribute__((visibility("default"))) int mgfa_attn_bwd_noalloc(
     }
   } catch (const std::exception& ex) {  // tensor-map encoding failures
     std::fprintf(stderr, "mgfa_attn_bwd_noalloc: %s\n", ex.what());
+    return MGFA_NOALLOC_CUDA_ERROR;
+  }
+  return MGFA_NOALLOC_OK;
+}
+
+extern "C" __attribute__((visibility("default"))) int mgfa_attn_bwd_noalloc_status(
+    unsigned int* host_status, void* stream_ptr) {
+  if (!host_status) return MGFA_NOALLOC_BAD_ARGUMENT;
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    if (e != cudaSuccess) report("cudaGetDevice", e);
+    return MGFA_NOALLOC_CUDA_ERROR;
+  }
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    scratch = g_scratch_ptr[dev];
+  }
+  if (!scratch) {
+    std::fprintf(stderr, "mgfa_attn_bwd_noalloc_status: no call was made on device %d yet\n",
+                 dev);
+    return MGFA_NOALLOC_CUDA_ERROR;
+  }
+  // The status word sits at the start of the scratch array (the call clears it
+  // before its kernels run, stream-ordered).
+  e = cudaMemcpyAsync(host_status, scratch, sizeof(unsigned int), cudaMemcpyDeviceToHost,
+                      static_cast<cudaStream_t>(stream_ptr));
+  if (e != cudaSuccess) {
+    report("status copy", e);
     return MGFA_NOALLOC_CUDA_ERROR;
   }
   return MGFA_NOALLOC_OK;

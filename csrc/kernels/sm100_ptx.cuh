@@ -412,14 +412,22 @@ __device__ __forceinline__ void red_release_sys_add(uint32_t* p, uint32_t v) {
 
 __device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
-// Spin until *flag >= target (epoch counters only grow); bounded by limit_ns.
+// Whether counter value v has reached target, for counters that only grow and
+// may wrap around 2^32: the signed distance is used, so the answer stays right
+// across a wrap as long as v and target are less than 2^31 apart.
+__device__ __forceinline__ bool count_reached(uint32_t v, uint32_t target) {
+  return int32_t(v - target) >= 0;
+}
+
+// Spin until *flag has reached target (epoch counters only grow, wrap-safe);
+// bounded by limit_ns.
 __device__ __forceinline__ bool wait_flag_geq(const uint32_t* flag, uint32_t target,
                                               uint64_t limit_ns, uint32_t* status,
                                               uint32_t site, uint32_t step) {
-  if (ld_acquire_sys(flag) >= target) return true;
+  if (count_reached(ld_acquire_sys(flag), target)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
-    if (ld_acquire_sys(flag) >= target) return true;
+    if (count_reached(ld_acquire_sys(flag), target)) return true;
     if (globaltimer() - t0 > limit_ns) {
       record_error(status, kErrPeerTimeout, site, step);
       return false;

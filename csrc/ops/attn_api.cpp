@@ -249,15 +249,24 @@ namespace mgfa {
 // Failure-path check: one forward launch whose KV "arrival" flag is a local word
 // that nothing ever sets. The producer's bounded wait must expire after
 // wait_limit_ns, record kErrPeerTimeout in the status word and end the kernel
-// cleanly (no hang, no fault). Returns the status word (int32 CUDA tensor).
+// cleanly (no hang, no fault). Returns the status word (int32 CUDA tensor):
+// `status` when given (so a test can aim the error at a caller's word), else a
+// fresh one.
 torch::Tensor fwd_timeout_probe(torch::Tensor q, torch::Tensor k, torch::Tensor v,
-                                int64_t wait_limit_ns) {
+                                int64_t wait_limit_ns, c10::optional<torch::Tensor> status_in) {
   check_bshd(q, "q");
   check_bshd(k, "k");
   check_bshd(v, "v");
   c10::cuda::CUDAGuard guard(q.device());
   auto flags = torch::zeros({64}, q.options().dtype(at::kInt));
-  auto status = torch::zeros({1}, q.options().dtype(at::kInt));
+  torch::Tensor status;
+  if (status_in.has_value()) {
+    status = *status_in;
+    MGFA_CHECK(status.is_cuda() && status.scalar_type() == at::kInt && status.numel() >= 1,
+               "status must be an int32 CUDA tensor");
+  } else {
+    status = torch::zeros({1}, q.options().dtype(at::kInt));
+  }
   auto o = torch::empty_like(q);
   auto lse = torch::empty({q.size(0), q.size(2), q.size(1)}, q.options().dtype(at::kFloat));
   FwdParams p;

@@ -20,7 +20,7 @@ void register_ring_engine(py::module& m);
 void register_ring_exchange(py::module& m);
 void register_ring_bwd_engine(py::module& m);
 torch::Tensor fwd_timeout_probe(torch::Tensor q, torch::Tensor k, torch::Tensor v,
-                                int64_t wait_limit_ns);
+                                int64_t wait_limit_ns, c10::optional<torch::Tensor> status);
 void flash_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
                torch::Tensor out, torch::Tensor lse, torch::Tensor dq, torch::Tensor dk,
                torch::Tensor dv, double scale, bool causal,
@@ -61,7 +61,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("status"), py::arg("wait_limit_ns") = int64_t(2000000000));
   m.def("flash_bwd_preprocess", &mgfa::flash_bwd_preprocess);
   m.def("fwd_timeout_probe", &mgfa::fwd_timeout_probe,
-        "forward launch whose arrival flag is never set (bounded-wait failure path)");
+        "forward launch whose arrival flag is never set (bounded-wait failure path)",
+        py::arg("q"), py::arg("k"), py::arg("v"), py::arg("wait_limit_ns"),
+        py::arg("status") = py::none());
   mgfa::register_ring_engine(m);
   mgfa::register_ring_exchange(m);
   mgfa::register_ring_bwd_engine(m);

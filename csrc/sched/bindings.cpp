@@ -174,7 +174,7 @@ PYBIND11_MODULE(_sched, m) {
       [](int64_t seq, int world, int block, const std::string& mk, const std::string& policy,
          double beta) { return make_scheduled(seq, world, block, to_mask(mk), policy, beta); },
       py::arg("seq"), py::arg("world"), py::arg("block") = 128, py::arg("mask") = "causal",
-      py::arg("policy") = "dp", py::arg("beta") = 1.0);
+      py::arg("policy") = "lpt", py::arg("beta") = 1.0);
   m.def("step_active", [](const ShardPlan& p, int q, int kv, const std::string& mk) {
     return step_active(p, q, kv, to_mask(mk));
   });

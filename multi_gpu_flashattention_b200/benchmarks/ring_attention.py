@@ -56,8 +56,8 @@ def parse():
     ap.add_argument("--init", default="legacy", choices=["legacy", "randn"])
     ap.add_argument("--layout", default="contiguous",
                     choices=["contiguous", "zigzag", "striped", "scheduler"])
-    ap.add_argument("--policy", default="dp", choices=["dp", "lpt"],
-                    help="scheduler layout: contiguous-row DP or row LPT partition")
+    ap.add_argument("--policy", default="lpt", choices=["dp", "lpt"],
+                    help="scheduler layout: row LPT (default) or contiguous-row DP partition")
     ap.add_argument("--dump-format", default="bin", choices=["bin", "npy", "pt"],
                     help="with ATTENTION_DUMP_OUTPUT: raw fp32 (reference format), or .npy / .pt "
                          "with the output and the fp32 LSE")

@@ -14,6 +14,7 @@ sides (top-left aligned); sharded layouts pass the positions of their tiles.
 from __future__ import annotations
 
 import math
+import os
 from typing import Optional
 
 import torch
@@ -21,7 +22,8 @@ import torch
 from .._ext import C
 
 TILE = 128
-DEFAULT_WAIT_LIMIT_NS = 2_000_000_000
+# bound of every in-kernel wait (ns); MGFA_WAIT_LIMIT_NS overrides it
+DEFAULT_WAIT_LIMIT_NS = int(os.environ.get("MGFA_WAIT_LIMIT_NS", 2_000_000_000))
 
 
 class KernelStatusError(RuntimeError):
@@ -33,14 +35,119 @@ _CODES = {1: "mbarrier wait timed out", 2: "peer flag wait timed out",
           5: "out-of-bounds store skipped (debug build)"}
 
 
+def _status_error(v: int, what: str) -> KernelStatusError:
+    code, site, step = v & 0xFF, (v >> 8) & 0xFF, v >> 16
+    return KernelStatusError(
+        f"{what}: {_CODES.get(code, 'error')} (code {code}, site {site}, step {step})")
+
+
 def check_status(status: torch.Tensor, what: str = "kernel") -> None:
     """Raise KernelStatusError when `status` (int32 CUDA tensor) is non-zero.
     Synchronises with the device."""
     v = int(status.view(-1)[0].item()) & 0xFFFFFFFF
     if v:
-        code, site, step = v & 0xFF, (v >> 8) & 0xFF, v >> 16
-        raise KernelStatusError(
-            f"{what}: {_CODES.get(code, 'error')} (code {code}, site {site}, step {step})")
+        raise _status_error(v, what)
+
+
+class StatusMonitor:
+    """The status word of public-API calls that pass none, for one device, and
+    its asynchronous read-back.
+
+    Every such call runs its kernels against this word (they record the first
+    error with an atomic compare-and-swap from 0, so the word is sticky) and
+    then enqueues a 4-byte copy of it into a pinned host slot, followed by an
+    event. The next public call on the device (and check_errors()) looks at the
+    read-backs whose events have completed, without waiting for the device, and
+    raises KernelStatusError for a non-zero word; the word is re-armed (zeroed,
+    stream-ordered) first. At most `depth` read-backs stay in flight; a call
+    that would exceed that waits for the oldest one. So a kernel error surfaces
+    at the latest a few calls later, without a device synchronisation per call
+    (the reference aborts the job instead: ring/attention/bench/
+    ring_attention_nccl_gpu_bench.cu:28-45).
+
+    After a KernelStatusError from a ring call the ranks' flag states may
+    disagree; re-arm them collectively with parallel.ring.reset_ring()."""
+
+    def __init__(self, device, depth: int = 8):
+        self.device = torch.device(device)
+        self.word = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.depth = depth
+        self.pending = []  # (event or None, pinned host slot, what)
+        self._free = []
+
+    def _slot(self):
+        if self._free:
+            return self._free.pop()
+        return torch.zeros(1, dtype=torch.int32, pin_memory=self.device.type == "cuda")
+
+    def after_launch(self, what: str) -> None:
+        """Enqueue the read-back of the word behind the work just launched on
+        the current stream (skipped under CUDA graph capture)."""
+        cuda = self.device.type == "cuda"
+        if cuda and torch.cuda.is_current_stream_capturing():
+            return
+        if len(self.pending) >= self.depth:
+            self.poll(wait_oldest=True)
+        host = self._slot()
+        if cuda:
+            with torch.cuda.device(self.device):
+                host.copy_(self.word, non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record()
+        else:
+            host.copy_(self.word)
+            ev = None
+        self.pending.append((ev, host, what))
+
+    def poll(self, wait: bool = False, wait_oldest: bool = False) -> None:
+        """Raise KernelStatusError for the first completed read-back that holds
+        an error. wait=True waits for every read-back in flight;
+        wait_oldest=True for the oldest one only."""
+        done = []
+        while self.pending:
+            ev, host, what = self.pending[0]
+            if ev is not None and not ev.query():
+                if not (wait or (wait_oldest and not done)):
+                    break
+                ev.synchronize()
+            self.pending.pop(0)
+            done.append((host, what))
+        bad = None
+        for host, what in done:
+            v = int(host[0]) & 0xFFFFFFFF
+            if v and bad is None:
+                bad = (v, what)
+            self._free.append(host)
+        if bad is not None:
+            # later read-backs carry the same sticky word: drop them, re-arm
+            for _, host, _ in self.pending:
+                self._free.append(host)
+            self.pending.clear()
+            self.word.zero_()
+            raise _status_error(*bad)
+
+
+_MONITORS: dict = {}
+
+
+def status_monitor(device) -> StatusMonitor:
+    """The StatusMonitor of `device` (created on first use)."""
+    key = str(torch.device(device))
+    m = _MONITORS.get(key)
+    if m is None:
+        m = StatusMonitor(device)
+        _MONITORS[key] = m
+    return m
+
+
+def check_errors(device=None, wait: bool = True) -> None:
+    """Raise KernelStatusError if a kernel launched by a public call (one that
+    was given no explicit status word) on `device` (default: every device used
+    so far) reported an error. wait=True first waits for those calls to finish;
+    wait=False only looks at the ones already finished."""
+    mons = [status_monitor(device)] if device is not None else list(_MONITORS.values())
+    for m in mons:
+        m.poll(wait=wait)
 
 
 def tile_positions(n_tokens: int, device, start: int = 0) -> torch.Tensor:
@@ -50,7 +157,6 @@ def tile_positions(n_tokens: int, device, start: int = 0) -> torch.Tensor:
 
 
 _POS_CACHE: dict = {}
-_STATUS_CACHE: dict = {}
 
 
 def _default_positions(n_tokens: int, device) -> torch.Tensor:
@@ -63,17 +169,6 @@ def _default_positions(n_tokens: int, device) -> torch.Tensor:
     if t is None:
         t = torch.tensor([i * TILE for i in range(n)], dtype=torch.int32).to(device)
         _POS_CACHE[key] = t
-    return t
-
-
-def _scratch_status(device) -> torch.Tensor:
-    """Status word for calls that pass none: kernels only write it on an error
-    nobody asked to see, so one zeroed word per device serves every such call."""
-    key = str(device)
-    t = _STATUS_CACHE.get(key)
-    if t is None:
-        t = torch.zeros(1, dtype=torch.int32, device=device)
-        _STATUS_CACHE[key] = t
     return t
 
 
@@ -97,9 +192,14 @@ def flash_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bo
             kv_tile_pos = _default_positions(k.shape[1], q.device)
     o = out if out is not None else torch.empty_like(q)
     lse = torch.empty(B, Hq, Sq, dtype=torch.float32, device=q.device)
-    st = status if status is not None else _scratch_status(q.device)
+    mon = status_monitor(q.device) if status is None else None
+    if mon is not None:
+        mon.poll()  # an error of an earlier, finished call surfaces here
+    st = status if status is not None else mon.word
     C().flash_fwd(q, k, v, o, None, lse, _scale(q, softmax_scale), causal, q_tile_pos,
                   kv_tile_pos, False, True, st, int(wait_limit_ns))
+    if mon is not None:
+        mon.after_launch("flash_attn_fwd")
     return o, lse
 
 
@@ -135,9 +235,14 @@ def flash_attn_bwd(dout, q, k, v, out, lse, causal: bool = False,
     dq = dq if dq is not None else torch.empty(q.shape, **f32)
     dk = dk if dk is not None else torch.empty(k.shape, **f32)
     dv = dv if dv is not None else torch.empty(v.shape, **f32)
-    st = status if status is not None else _scratch_status(q.device)
+    mon = status_monitor(q.device) if status is None else None
+    if mon is not None:
+        mon.poll()
+    st = status if status is not None else mon.word
     C().flash_bwd(dout.contiguous(), q, k, v, out, lse, dq, dk, dv, _scale(q, softmax_scale),
                   causal, q_tile_pos, kv_tile_pos, accumulate, lse2, delta, st, int(wait_limit_ns))
+    if mon is not None:
+        mon.after_launch("flash_attn_bwd")
     return dq, dk, dv
 
 

@@ -35,7 +35,7 @@ import torch.distributed as dist
 
 from .._ext import C
 from ..ops.flash import (DEFAULT_WAIT_LIMIT_NS, check_status, flash_attn_fwd,
-                         flash_attn_fwd_step)
+                         flash_attn_fwd_step, status_monitor)
 from ..ops.reference import attention_ref
 from .layouts import RingLayout
 
@@ -272,10 +272,15 @@ def ring_attention_forward(q, k, v, layout: RingLayout, causal: bool = False,
     """Forward ring attention on local shards; returns (out, lse).
 
     out has q's dtype ([B, L, Hq, D]); lse is fp32 [B, Hq, L] (natural log).
-    With check=True the kernels' status word is read back (a device sync) and a
-    KernelStatusError raised on any timeout. With a `health` (RingHealth) every
-    rank first passes its gate, so a peer that left or went silent raises
-    PeerLostError here instead of leaving launched kernels waiting."""
+    Without a `status` the kernels report into the device's StatusMonitor
+    word: an error (a bounded wait that expired, a wrong slot tag) raises
+    KernelStatusError at the entry of a later public call on this device, or
+    in ops.flash.check_errors(), without a device sync per call. With
+    check=True the status is read back right away (a device sync) and the
+    error raised here. After such an error re-arm the ring on every rank with
+    reset_ring(group). With a `health` (RingHealth) every rank first passes
+    its gate, so a peer that left or went silent raises PeerLostError here
+    instead of leaving launched kernels waiting."""
     scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(q.shape[-1])
     if backend is None:
         backend = "fused" if q.is_cuda else "torch"
@@ -286,7 +291,13 @@ def ring_attention_forward(q, k, v, layout: RingLayout, causal: bool = False,
         health.gate()
     if backend == "torch":
         return _fwd_torch(q, k, v, layout, causal, scale, group)
-    st = status if status is not None else torch.zeros(1, dtype=torch.int32, device=q.device)
+    mon = None
+    if status is None:
+        mon = status_monitor(q.device)
+        mon.poll()  # an error of an earlier, finished call surfaces before any launch
+        st = mon.word
+    else:
+        st = status
     if world == 1:
         qtp, kvtp, kv_lens = _meta(layout, rank, q.device)
         out, lse = flash_attn_fwd(q, k[:, :kv_lens[0]], v[:, :kv_lens[0]], causal=causal,
@@ -302,6 +313,35 @@ def ring_attention_forward(q, k, v, layout: RingLayout, causal: bool = False,
             cpu_group = _host_group(group)
         out, lse = _fwd_staged(q, k, v, layout, causal, scale, group, st, wait_limit_ns,
                                cpu_group=cpu_group)
-    if check:
-        check_status(st, f"ring attention ({backend})")
+    what = f"ring attention ({backend})"
+    if mon is not None:
+        mon.after_launch(what)
+        if check:
+            mon.poll(wait=True)
+    elif check:
+        check_status(st, what)
     return out, lse
+
+
+def reset_ring(group=None) -> None:
+    """Re-arm the ring after a KernelStatusError (collective: every rank of
+    `group` calls it). Waits for this device's work, then past a barrier zeroes
+    the flag words and use counters of the group's forward and backward
+    engines and this device's status word, and meets the other ranks again, so
+    the next ring call starts from the same state everywhere."""
+    from .ring_bwd import BWD_ENGINES
+    rank, world = _world(group)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier(group)
+    for engines in (ENGINES, BWD_ENGINES):
+        eng = engines._by_key.get((id(group), dev.index))
+        if eng is not None:
+            eng.reset()
+    mon = status_monitor(dev)
+    mon.pending.clear()
+    mon.word.zero_()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier(group)

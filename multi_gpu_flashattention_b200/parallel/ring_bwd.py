@@ -22,7 +22,7 @@ import torch
 import torch.distributed as dist
 
 from .._ext import C
-from ..ops.flash import flash_attn_bwd
+from ..ops.flash import DEFAULT_WAIT_LIMIT_NS, flash_attn_bwd, status_monitor
 from .layouts import RingLayout
 
 
@@ -191,13 +191,21 @@ BWD_ENGINES = _BwdEngines()
 
 
 def _bwd_fused(dout, q, k, v, out, lse, causal, scale, group, qtp, kvtp, kv_lens,
-               status=None, wait_limit_ns=2_000_000_000):
+               status=None, wait_limit_ns=DEFAULT_WAIT_LIMIT_NS):
     rank, world = _world(group)
     eng = BWD_ENGINES.get(group, q.device, k.numel() * k.element_size())
-    st = status if status is not None else torch.zeros(1, dtype=torch.int32, device=q.device)
+    mon = None
+    if status is None:  # report into the device's StatusMonitor (see ops.flash)
+        mon = status_monitor(q.device)
+        mon.poll()
+        st = mon.word
+    else:
+        st = status
     dq, dk, dv = eng.backward(dout, q.contiguous(), k.contiguous(), v.contiguous(), out.contiguous(),
                               lse, scale, causal, qtp if causal else None,
                               kvtp if causal else None, kv_lens, st, int(wait_limit_ns))
+    if mon is not None:
+        mon.after_launch("ring attention backward (fused)")
     kl = kv_lens[rank]
     if kl < k.shape[1]:  # padding rows of a shorter shard carry no gradient
         dk[:, kl:].zero_()

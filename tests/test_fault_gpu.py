@@ -25,6 +25,62 @@ def test_bounded_wait_expires_with_status_and_context_survives():
     assert torch.isfinite(o.float()).all()
 
 
+def test_public_call_raises_error_of_an_earlier_kernel():
+    """A kernel whose bounded wait expires while reporting into the public API's
+    status word (the device's StatusMonitor) makes a later public call raise
+    KernelStatusError before it launches anything; the word is re-armed and
+    the next call runs clean."""
+    from multi_gpu_flashattention_b200._ext import C
+    from multi_gpu_flashattention_b200.ops.flash import (KernelStatusError, check_errors,
+                                                         flash_attn_fwd, status_monitor)
+    q = (torch.randn(1, 256, 1, 128, device="cuda") * 0.5).bfloat16()
+    check_errors()
+    mon = status_monitor(q.device)
+    C().fwd_timeout_probe(q, q, q, 200_000_000, mon.word)  # records a peer-flag timeout
+    flash_attn_fwd(q, q, q)  # runs behind it; its read-back carries the sticky word
+    torch.cuda.synchronize()  # (a user's loss.item() or the like)
+    with pytest.raises(KernelStatusError, match="peer flag wait timed out"):
+        flash_attn_fwd(q, q, q)
+    o, _ = flash_attn_fwd(q, q, q)
+    check_errors()
+    assert torch.isfinite(o.float()).all()
+
+
+def _drop_signal_public(rank, world):
+    """The dropped signal surfaces through mgfa.ring_attention() itself (no
+    check=True, no status argument): the receiving rank's next public call
+    raises, and reset_ring() re-arms the ring on both ranks."""
+    import multi_gpu_flashattention_b200 as mgfa
+    from multi_gpu_flashattention_b200.ops.flash import KernelStatusError, check_errors
+    from multi_gpu_flashattention_b200.parallel.ring import ENGINES, reset_ring
+    dev = torch.device("cuda", rank)
+    g = torch.Generator(device=dev).manual_seed(rank)
+    q = (torch.randn(1, 512, 2, 128, device=dev, generator=g) * 0.5).bfloat16()
+    out_ok = mgfa.ring_attention(q, q, q, backend="fused")
+    check_errors()
+    eng = ENGINES.get(None, dev, q.numel() * 2)
+    if rank == 0:
+        eng.set_drop_signal_step(0)  # rank 1 never hears about one chunk of step 0
+    mgfa.ring_attention(q, q, q, backend="fused")
+    eng.set_drop_signal_step(-1)
+    torch.cuda.synchronize()
+    if rank == 1:
+        with pytest.raises(KernelStatusError, match="peer flag wait timed out"):
+            mgfa.ring_attention(q, q, q, backend="fused")
+    else:
+        check_errors()  # the sending side finished its work
+    reset_ring()
+    out = mgfa.ring_attention(q, q, q, backend="fused")
+    check_errors()
+    torch.testing.assert_close(out, out_ok, rtol=0, atol=0)
+
+
+@pytest.mark.multigpu
+def test_dropped_signal_raises_through_public_ring_attention():
+    run_ranks(_drop_signal_public, 2, backend="nccl",
+              env={"NCCL_NVLS_ENABLE": "0", "MGFA_WAIT_LIMIT_NS": "300000000"})
+
+
 def _drop_signal(rank, world):
     from multi_gpu_flashattention_b200.ops.flash import KernelStatusError
     from multi_gpu_flashattention_b200.parallel.layouts import RingLayout

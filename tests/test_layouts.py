@@ -71,3 +71,13 @@ def test_layout_balance_report():
         assert rows[name]["ring_paced_imbalance"] < 1.01, (name, rows[name])
     assert rows["scheduler-dp"]["imbalance"] < 1.05
     assert rows["scheduler-dp"]["ring_paced_imbalance"] > 2.0
+
+
+def test_default_scheduler_layout_is_paced_evenly():
+    """The scheduler layout's default partition (row LPT) keeps every ring step
+    even: step-paced imbalance <= 1.01 at 8 ranks, causal 128K."""
+    from multi_gpu_flashattention_b200.benchmarks.layout_balance import balance
+    lay = RingLayout("scheduler", 131072, 8)
+    assert lay.policy == "lpt"
+    r = balance("scheduler", 131072, 8, "causal", 128)
+    assert r["ring_paced_imbalance"] <= 1.01, r
