@@ -299,3 +299,100 @@ torch::Tensor fwd_timeout_probe(torch::Tensor q, torch::Tensor k, torch::Tensor 
 }
 
 }  // namespace mgfa
+
+// ---------------------------------------------------------------------- persistent forward
+#include "../kernels/attn_fwd_persistent.cuh"
+
+namespace mgfa {
+
+CUtensorMap make_bshd_map_dt(const void* base, int64_t B, int64_t S, int64_t H, int64_t stride_b,
+                             int64_t stride_s, int64_t stride_h, int D, bool fp16);
+
+int device_sm_count(int device) {
+  static int counts[64] = {};
+  if (device < 0 || device >= 64) return 148;
+  if (!counts[device])
+    C10_CUDA_CHECK(cudaDeviceGetAttribute(&counts[device], cudaDevAttrMultiProcessorCount, device));
+  return counts[device];
+}
+
+// Single-GPU forward on the persistent kernel: o [B,Sq,Hq,D] (input dtype) and
+// lse [B,Hq,Sq] fp32 are written. `sched` is an int32 CUDA tensor of at least 2
+// zeros that no concurrent launch uses; the kernel leaves it zeroed. grid <= 0:
+// one CTA per SM (at most one per work item). With `seg_lens` the keys are
+// several segments that all read (k, v) -- segment s its first seg_lens[s] rows
+// at the tile positions in row s of kv_tile_pos [n_seg, n] -- and attention
+// runs over their union (the ring's compute pattern on one GPU).
+void flash_fwd_persistent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
+                          torch::Tensor lse, double scale, bool causal,
+                          c10::optional<torch::Tensor> q_tile_pos,
+                          c10::optional<torch::Tensor> kv_tile_pos, torch::Tensor status,
+                          int64_t wait_limit_ns, torch::Tensor sched, int64_t poly8,
+                          int64_t grid, std::vector<int64_t> seg_lens) {
+  check_bshd(q, "q");
+  check_bshd(k, "k");
+  check_bshd(v, "v");
+  MGFA_CHECK(k.sizes() == v.sizes() && k.strides() == v.strides(), "k and v must match");
+  check_same_kind(q, k, "q/k");
+  check_same_kind(q, v, "q/v");
+  MGFA_CHECK(q.size(0) == k.size(0), "batch mismatch");
+  const int B = int(q.size(0)), Sq = int(q.size(1)), Hq = int(q.size(2));
+  const int Sk = int(k.size(1)), Hkv = int(k.size(2)), D = int(q.size(3));
+  const bool f16 = q.scalar_type() == at::kHalf;
+  MGFA_CHECK(Hq % Hkv == 0, "query heads must be a multiple of kv heads");
+  MGFA_CHECK(o.scalar_type() == q.scalar_type() && o.sizes() == q.sizes() && o.stride(3) == 1 &&
+                 o.stride(2) == D,
+             "o must have q's dtype and shape, with packed heads");
+  MGFA_CHECK(lse.is_cuda() && lse.scalar_type() == at::kFloat && lse.is_contiguous() &&
+                 lse.numel() == int64_t(B) * Hq * Sq,
+             "lse must be a contiguous float32 [B, Hq, Sq] tensor");
+  MGFA_CHECK(status.is_cuda() && status.scalar_type() == at::kInt && status.numel() >= 1,
+             "status must be an int32 CUDA tensor");
+  MGFA_CHECK(sched.is_cuda() && sched.scalar_type() == at::kInt && sched.numel() >= 2,
+             "sched must be an int32 CUDA tensor of at least 2 zeros");
+  c10::cuda::CUDAGuard guard(q.device());
+  if (Sq == 0 || B == 0) return;
+  PFwdParams p;
+  p.batch = B;
+  p.hq = Hq;
+  p.hkv = Hkv;
+  p.sq = Sq;
+  p.n_q_tiles = (Sq + 127) / 128;
+  p.n_items = B * Hq * ((p.n_q_tiles + 1) / 2);
+  if (seg_lens.empty()) seg_lens.push_back(Sk);
+  MGFA_CHECK(int(seg_lens.size()) <= kPMaxSeg, "at most 16 segments");
+  p.n_seg = int(seg_lens.size());
+  p.kv_rows = Sk;
+  for (int i = 0; i < p.n_seg; ++i) {
+    MGFA_CHECK(seg_lens[i] >= 0 && seg_lens[i] <= Sk, "segment length out of range");
+    p.seg_len[i] = int(seg_lens[i]);
+  }
+  p.scale_log2 = float(scale * 1.4426950408889634);
+  p.causal = causal ? 1 : 0;
+  if (causal) {
+    const int n_kv_tiles = (Sk + 127) / 128;
+    p.q_tile_pos = tile_pos_ptr(q_tile_pos, p.n_q_tiles, "q_tile_pos");
+    p.kv_tile_pos = tile_pos_ptr(kv_tile_pos, n_kv_tiles * p.n_seg, "kv_tile_pos");
+    p.kv_pos_stride = int(kv_tile_pos->numel() / p.n_seg);
+    MGFA_CHECK(p.kv_pos_stride >= n_kv_tiles, "kv_tile_pos needs a row per segment");
+  }
+  p.o = o.data_ptr();
+  p.lse = lse.data_ptr<float>();
+  p.o_batch_stride = o.stride(0);
+  p.o_row_stride = o.stride(1);
+  p.status = reinterpret_cast<uint32_t*>(status.data_ptr<int>());
+  p.wait_limit_ns = uint64_t(wait_limit_ns);
+  p.sched = reinterpret_cast<uint32_t*>(sched.data_ptr<int>());
+  auto map = [&](const torch::Tensor& t) {
+    return make_bshd_map_dt(t.data_ptr(), t.size(0), t.size(1), t.size(2), t.stride(0),
+                            t.stride(1), t.stride(2), D, f16);
+  };
+  const CUtensorMap mq = map(q), mk = map(k), mv = map(v);
+  int g = int(grid);
+  if (g <= 0) g = device_sm_count(q.get_device());
+  if (g > p.n_items) g = p.n_items;
+  attn_fwd_persistent_launch(mq, mk, mv, mk, D, f16, p, g, int(poly8),
+                             at::cuda::getCurrentCUDAStream());
+}
+
+}  // namespace mgfa

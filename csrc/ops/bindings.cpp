@@ -8,6 +8,12 @@ void flash_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, c10::optional<
                c10::optional<torch::Tensor> q_tile_pos, c10::optional<torch::Tensor> kv_tile_pos,
                bool merge, bool final_out, torch::Tensor status, int64_t wait_limit_ns);
 size_t flash_fwd_smem_bytes();
+void flash_fwd_persistent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
+                          torch::Tensor lse, double scale, bool causal,
+                          c10::optional<torch::Tensor> q_tile_pos,
+                          c10::optional<torch::Tensor> kv_tile_pos, torch::Tensor status,
+                          int64_t wait_limit_ns, torch::Tensor sched, int64_t poly8,
+                          int64_t grid, std::vector<int64_t> seg_lens);
 void legacy_partial(torch::Tensor q, torch::Tensor k, torch::Tensor v, double scale,
                     c10::optional<torch::Tensor> q_pos, c10::optional<torch::Tensor> k_pos,
                     bool causal, torch::Tensor acc, torch::Tensor m, torch::Tensor l, bool merge);
@@ -39,6 +45,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("q_tile_pos"), py::arg("kv_tile_pos"), py::arg("merge"), py::arg("final_out"),
         py::arg("status"), py::arg("wait_limit_ns") = int64_t(2000000000));
   m.def("flash_fwd_smem_bytes", &mgfa::flash_fwd_smem_bytes);
+  m.def("flash_fwd_persistent", &mgfa::flash_fwd_persistent, py::arg("q"), py::arg("k"),
+        py::arg("v"), py::arg("o"), py::arg("lse"), py::arg("scale"), py::arg("causal"),
+        py::arg("q_tile_pos"), py::arg("kv_tile_pos"), py::arg("status"),
+        py::arg("wait_limit_ns"), py::arg("sched"), py::arg("poly8") = int64_t(-1),
+        py::arg("grid") = int64_t(0), py::arg("seg_lens") = std::vector<int64_t>());
   m.def("red_probe", &mgfa::red_probe, py::arg("dq"), py::arg("n_kv_tiles"),
         py::arg("causal"));
   m.def("debug_build", []() {

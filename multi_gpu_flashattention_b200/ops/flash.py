@@ -172,6 +172,29 @@ def _default_positions(n_tokens: int, device) -> torch.Tensor:
     return t
 
 
+# Forward kernel of flash_attn_fwd: "persistent" (one CTA per SM, dynamic tile
+# scheduler, attn_fwd_persistent.cu) or "stepwise" (one CTA per query-tile pair,
+# flash_fwd_sm100.cu, the kernel the per-step ring and the merge path use).
+FWD_KERNEL = os.environ.get("MGFA_FWD_KERNEL", "persistent")
+# exponential pairs (of every 8) computed on the FMA pipe; -1: the kernel's default
+POLY8 = int(os.environ.get("MGFA_POLY8", "-1"))
+
+_SCHED: dict = {}
+
+
+def sched_counters(device) -> torch.Tensor:
+    """Work counters of the persistent forward for the current stream of
+    `device`: two int32 zeros, which every launch leaves zeroed again. One pair
+    per (device, stream), so launches that may overlap never share one."""
+    dev = torch.device(device)
+    key = (str(dev), torch.cuda.current_stream(dev).cuda_stream)
+    t = _SCHED.get(key)
+    if t is None:
+        t = torch.zeros(2, dtype=torch.int32, device=dev)
+        _SCHED[key] = t
+    return t
+
+
 def _scale(q: torch.Tensor, softmax_scale: Optional[float]) -> float:
     return softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(q.shape[-1])
 
@@ -196,8 +219,13 @@ def flash_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bo
     if mon is not None:
         mon.poll()  # an error of an earlier, finished call surfaces here
     st = status if status is not None else mon.word
-    C().flash_fwd(q, k, v, o, None, lse, _scale(q, softmax_scale), causal, q_tile_pos,
-                  kv_tile_pos, False, True, st, int(wait_limit_ns))
+    if FWD_KERNEL == "persistent":
+        C().flash_fwd_persistent(q, k, v, o, lse, _scale(q, softmax_scale), causal, q_tile_pos,
+                                 kv_tile_pos, st, int(wait_limit_ns), sched_counters(q.device),
+                                 POLY8)
+    else:
+        C().flash_fwd(q, k, v, o, None, lse, _scale(q, softmax_scale), causal, q_tile_pos,
+                      kv_tile_pos, False, True, st, int(wait_limit_ns))
     if mon is not None:
         mon.after_launch("flash_attn_fwd")
     return o, lse

@@ -54,6 +54,7 @@ if which in ("all", "cuda"):
                 "csrc/ops/attn_api.cpp",
                 "csrc/kernels/umma_probe.cu",
                 "csrc/kernels/flash_fwd_sm100.cu",
+                "csrc/kernels/attn_fwd_persistent.cu",
                 "csrc/kernels/flash_bwd_sm100.cu",
                 "csrc/kernels/attn_bwd_noalloc.cu",
                 "csrc/kernels/legacy_fp32.cu",
