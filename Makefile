@@ -63,7 +63,7 @@ $(BIN)/ring_loop_bench: $(OBJ)/bench/ring_loop_bench.o $(COMM_OBJ) | $(BIN)
 
 $(BIN)/ring_attention_bench: $(OBJ)/bench/ring_attention_bench.o $(COMM_OBJ) $(SCHED_OBJ) \
     $(OBJ)/kernels/flash_fwd_sm100.o $(OBJ)/kernels/flash_bwd_sm100.o $(OBJ)/kernels/legacy_fp32.o \
-    $(OBJ)/ops/attn_api.o | $(BIN)
+    $(OBJ)/kernels/attn_fwd_persistent.o $(OBJ)/ops/attn_api.o | $(BIN)
 	$(CXX) -o $@ $^ $(GPU_LIBS)
 
 $(BIN)/ring_oneshot: $(OBJ)/bench/ring_oneshot.o $(COMM_OBJ) $(OBJ)/kernels/legacy_fp32.o \

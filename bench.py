@@ -40,7 +40,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--backend", choices=["fused", "p2p_unfused", "ce_unfused", "nccl", "staged"],
+    ap.add_argument("--backend", choices=["fused", "fused_stepwise", "p2p_unfused", "ce_unfused",
+                                          "nccl", "staged"],
                     default="fused")
     ap.add_argument("--seq", type=int, default=131072)
     ap.add_argument("--heads", type=int, default=32)
@@ -311,9 +312,11 @@ def main():
 
     # ---------------- compute-only reference for the exposed-comm fraction
     exposed = None
-    if world > 1 and args.backend in ("fused", "p2p_unfused", "ce_unfused"):
-        eng = ENGINES.get(group, dev, k.numel() * k.element_size())
-        from multi_gpu_flashattention_b200.parallel.ring import _meta
+    if world > 1 and args.backend in ("fused", "fused_stepwise", "p2p_unfused", "ce_unfused"):
+        from multi_gpu_flashattention_b200.parallel.ring import P_ENGINES, _meta
+        nbytes = k.numel() * k.element_size()
+        eng = P_ENGINES.get(group, dev, nbytes) if args.backend == "fused" else \
+            ENGINES.get(group, dev, nbytes)
         qtp, kvtp, kv_lens = _meta(lay, rank, dev)
         def compute_only():
             return eng.forward_compute_only(q, k, v, 1.0 / math.sqrt(D), causal,
@@ -399,7 +402,9 @@ def main():
         peak = json.load(open(peaks_path))["bf16_tflops_sustained"] if os.path.exists(peaks_path) else 1400.0
         comm_bytes = (world - 1) * 2 * B * L * Hkv * D * 2
         t_roof = max(flops / world / (peak * 1e12), comm_bytes / 770e9) * 1e3
-        launches_per_step = world  # one attention kernel per ring step
+        # the one-launch ring runs one kernel per forward (so does a single GPU);
+        # the per-step engines and the baselines one attention kernel per step
+        launches_per_step = 1 if args.backend == "fused" else world
         rec = {
             "metric": METRIC,
             "value": round(tflops_total, 2),
@@ -442,7 +447,9 @@ def main():
                                   "download with step i's compute)"}
         print(json.dumps(rec), flush=True)
     if world > 1:
+        from multi_gpu_flashattention_b200.parallel.ring import P_ENGINES
         ENGINES.clear()
+        P_ENGINES.clear()
         dist.barrier()
         dist.destroy_process_group()
     return 0

@@ -22,14 +22,19 @@ struct DeviceScope {
 };
 }  // namespace
 
-SymmetricBuffer::SymmetricBuffer(size_t payload_bytes, int rank, int world, int device)
-    : rank_(rank), world_(world), device_(device), payload_bytes_((payload_bytes + 4095) & ~size_t(4095)) {
+SymmetricBuffer::SymmetricBuffer(size_t payload_bytes, int rank, int world, int device,
+                                 size_t flag_bytes)
+    : rank_(rank),
+      world_(world),
+      device_(device),
+      payload_bytes_((payload_bytes + 4095) & ~size_t(4095)),
+      flag_bytes_((flag_bytes + 4095) & ~size_t(4095)) {
   if (world <= 0 || rank < 0 || rank >= world) throw std::invalid_argument("bad rank/world");
   DeviceScope ds(device_);
   void* p = nullptr;
-  check(cudaMalloc(&p, kFlagBytes + payload_bytes_), "cudaMalloc(symmetric buffer)");
+  check(cudaMalloc(&p, flag_bytes_ + payload_bytes_), "cudaMalloc(symmetric buffer)");
   local_ = static_cast<uint8_t*>(p);
-  check(cudaMemset(local_, 0, kFlagBytes), "cudaMemset(flags)");
+  check(cudaMemset(local_, 0, flag_bytes_), "cudaMemset(flags)");
   check(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
   peers_.assign(world_, nullptr);
   peers_[rank_] = local_;
@@ -67,7 +72,7 @@ void SymmetricBuffer::open_peers(const std::vector<std::string>& handles) {
 
 void SymmetricBuffer::reset_flags(cudaStream_t stream) {
   DeviceScope ds(device_);
-  check(cudaMemsetAsync(local_, 0, kFlagBytes, stream), "cudaMemsetAsync(flags)");
+  check(cudaMemsetAsync(local_, 0, flag_bytes_, stream), "cudaMemsetAsync(flags)");
 }
 
 }  // namespace mgfa::comm

@@ -5,8 +5,9 @@
 // (torch.distributed from Python, a TCP store from the standalone benchmarks).
 //
 // Layout of one buffer:
-//   [0, kFlagBytes)          flag words, each on its own 128-byte line
-//   [kFlagBytes, ...)        payload (receive slots), 4 KB aligned
+//   [0, flag_bytes)          flag words (kFlagBytes by default, each named flag on
+//                            its own 128-byte line)
+//   [flag_bytes, ...)        payload (receive slots), 4 KB aligned
 #pragma once
 
 #include <cuda_runtime.h>
@@ -36,7 +37,9 @@ enum FlagIndex : int {
 
 class SymmetricBuffer {
  public:
-  SymmetricBuffer(size_t payload_bytes, int rank, int world, int device);
+  // flag_bytes: size of the flag area (rounded up to 4 KB).
+  SymmetricBuffer(size_t payload_bytes, int rank, int world, int device,
+                  size_t flag_bytes = kFlagBytes);
   ~SymmetricBuffer();
   SymmetricBuffer(const SymmetricBuffer&) = delete;
   SymmetricBuffer& operator=(const SymmetricBuffer&) = delete;
@@ -53,7 +56,12 @@ class SymmetricBuffer {
   bool connected() const { return connected_; }
 
   uint8_t* base(int r) const { return r == rank_ ? local_ : peers_.at(r); }
-  uint8_t* payload(int r) const { return base(r) + kFlagBytes; }
+  uint8_t* payload(int r) const { return base(r) + flag_bytes_; }
+  // Flag word `index` of rank r's packed uint32 flag array (no 128-byte spacing).
+  uint32_t* word(int r, size_t index) const {
+    return reinterpret_cast<uint32_t*>(base(r)) + index;
+  }
+  size_t flag_bytes() const { return flag_bytes_; }
   uint32_t* flag(int r, int index) const {
     return reinterpret_cast<uint32_t*>(base(r) + size_t(index) * kFlagStride);
   }
@@ -63,6 +71,7 @@ class SymmetricBuffer {
  private:
   int rank_, world_, device_;
   size_t payload_bytes_;
+  size_t flag_bytes_;
   uint8_t* local_ = nullptr;
   std::vector<uint8_t*> peers_;
   bool connected_ = false;

@@ -120,30 +120,76 @@ __device__ __forceinline__ uint64_t exp2_fma2(uint64_t x2) {
                  __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23)));
 }
 
+// 2^x for one x on the FMA pipe: the same method as exp2_fma2, scalar.
+__device__ __forceinline__ float exp2_fma1(float x) {
+  constexpr float kC0 = 9.999195933e-01f, kC1 = 6.932621598e-01f, kC2 = 2.427141368e-01f,
+                  kC3 = 5.521299317e-02f, kRound = 12582912.0f;  // 1.5 * 2^23
+  const float xc = fmaxf(x, -126.f);
+  const float t = xc + kRound;
+  const float f = xc - (t - kRound);
+  const float pv = fmaf(fmaf(fmaf(kC3, f, kC2), f, kC1), f, kC0);
+  return __uint_as_float(__float_as_uint(pv) + (__float_as_uint(t) << 23));
+}
+
 // Probabilities of one 64-key half of a row: p = 2^(s * scale - m), summed into
-// two packed accumulators and packed to 16-bit pairs for the PV MMA.
-template <bool kF16, int kPoly8>
-__device__ __forceinline__ void exp_half(const uint32_t (&sr)[128], int half, uint64_t sc2,
-                                         uint64_t nm2, uint32_t (&pk)[32], uint64_t& acc0,
-                                         uint64_t& acc1) {
+// the row-sum accumulators and packed to 16-bit pairs for the PV MMA. kPacked
+// uses the f32x2 instructions (two lanes of work per instruction); kPoly8 of
+// every 8 pairs go through the FMA-pipe polynomial instead of MUFU.EX2.
+template <bool kF16, int kPoly8, bool kPacked>
+__device__ __forceinline__ void exp_half(const uint32_t (&sr)[128], int half, float scale,
+                                         float neg_m, uint32_t (&pk)[32], float (&lacc)[4]) {
+  if constexpr (kPacked) {
+    const uint64_t sc2 = f2_pack(scale, scale), nm2 = f2_pack(neg_m, neg_m);
+    uint64_t acc0 = f2_pack(0.f, 0.f), acc1 = f2_pack(0.f, 0.f);
 #pragma unroll
-  for (int cc = 0; cc < 32; ++cc) {
-    const int c = half * 32 + cc;
-    const uint64_t x2 =
-        f2_fma(f2_pack(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), sc2, nm2);
-    uint64_t e2;
-    if ((cc & 7) >= 8 - kPoly8) {
-      e2 = exp2_fma2(x2);
-    } else {
-      float a, b;
-      f2_unpack(x2, a, b);
-      e2 = f2_pack(ex2_approx(a), ex2_approx(b));
+    for (int cc = 0; cc < 32; ++cc) {
+      const int c = half * 32 + cc;
+      const uint64_t x2 = f2_fma(
+          f2_pack(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), sc2, nm2);
+      uint64_t e2;
+      if ((cc & 7) >= 8 - kPoly8) {
+        e2 = exp2_fma2(x2);
+      } else {
+        float a, b;
+        f2_unpack(x2, a, b);
+        e2 = f2_pack(ex2_approx(a), ex2_approx(b));
+      }
+      if (cc & 1) acc1 = f2_add(acc1, e2);
+      else acc0 = f2_add(acc0, e2);
+      float e0, e1;
+      f2_unpack(e2, e0, e1);
+      pk[cc] = pack16<kF16>(e0, e1);
     }
-    if (cc & 1) acc1 = f2_add(acc1, e2);
-    else acc0 = f2_add(acc0, e2);
-    float e0, e1;
-    f2_unpack(e2, e0, e1);
-    pk[cc] = pack16<kF16>(e0, e1);
+    float a0, a1, b0, b1;
+    f2_unpack(acc0, a0, a1);
+    f2_unpack(acc1, b0, b1);
+    lacc[0] += a0;
+    lacc[1] += a1;
+    lacc[2] += b0;
+    lacc[3] += b1;
+  } else {
+#pragma unroll
+    for (int cc = 0; cc < 32; ++cc) {
+      const int c = half * 32 + cc;
+      const float x0 = fmaf(__uint_as_float(sr[2 * c]), scale, neg_m);
+      const float x1 = fmaf(__uint_as_float(sr[2 * c + 1]), scale, neg_m);
+      float p0, p1;
+      if ((cc & 7) >= 8 - kPoly8) {
+        p0 = exp2_fma1(x0);
+        p1 = exp2_fma1(x1);
+      } else {
+        p0 = ex2_approx(x0);
+        p1 = ex2_approx(x1);
+      }
+      if (cc & 1) {
+        lacc[2] += p0;
+        lacc[3] += p1;
+      } else {
+        lacc[0] += p0;
+        lacc[1] += p1;
+      }
+      pk[cc] = pack16<kF16>(p0, p1);
+    }
   }
 }
 
@@ -270,7 +316,8 @@ __device__ void push_units(const PFwdParams& p, int pw, int n_pw, volatile uint3
 }
 
 // ------------------------------------------------------------------ kernel
-template <int kD, bool kF16, int kPoly8, bool kRing>
+// kVar: bit 0 packed f32x2 softmax arithmetic, bit 1 P handed over in two halves.
+template <int kD, bool kF16, int kPoly8, bool kRing, int kVar>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_persistent_kernel(const __grid_constant__ CUtensorMap map_q,
                                const __grid_constant__ CUtensorMap map_k,
@@ -282,6 +329,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kKSteps = kD / 16;
   constexpr int kOChunks = kD / 32;
   constexpr uint32_t kOCol = 256;
+  constexpr bool kPacked = (kVar & 1) != 0;
+  constexpr bool kSplit = (kVar & 2) != 0;
   extern __shared__ uint8_t smem_raw[];
   PSmem<kD>& s = *reinterpret_cast<PSmem<kD>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -553,7 +602,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;
     const uint32_t s_addr = tmem + lane_off + t * 128;
     const uint32_t o_addr = tmem + lane_off + kOCol + t * kD;
-    const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2);
     uint32_t g = 0;
     int n = 0;
     bool ok = true;
@@ -634,8 +682,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           first = false;
           const float m_use = (m == -INFINITY) ? 0.f : m;
-          const uint64_t nm2 = f2_pack(-m_use, -m_use);
-          uint64_t acc0 = f2_pack(0.f, 0.f), acc1 = f2_pack(0.f, 0.f);
+          float lacc[4] = {0.f, 0.f, 0.f, 0.f};
           // O already holds the previous tiles' PV (their MMAs completed before
           // this tile's S was committed) and must be rescaled before this tile's
           // PV starts. Rare: without a rescale the first half of P goes to the
@@ -643,17 +690,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           // once the scores are no longer needed (register pressure) and both
           // halves are released together.
           const bool resc = __any_sync(0xffffffffu, rescale);
+          const bool early = kSplit && !resc;
           uint32_t pk0[32], pk1[32];
-          if (full) exp_half<kF16, kPoly8>(sr, 0, sc2, nm2, pk0, acc0, acc1);
-          else exp_half<kF16, 0>(sr, 0, sc2, nm2, pk0, acc0, acc1);
-          if (!resc) {
+          if (full) exp_half<kF16, kPoly8, kPacked>(sr, 0, p.scale_log2, -m_use, pk0, lacc);
+          else exp_half<kF16, 0, kPacked>(sr, 0, p.scale_log2, -m_use, pk0, lacc);
+          if (early) {
             tmem_st32(s_addr, pk0);
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(&s.p_full[t][0]);
           }
-          if (full) exp_half<kF16, kPoly8>(sr, 1, sc2, nm2, pk1, acc0, acc1);
-          else exp_half<kF16, 0>(sr, 1, sc2, nm2, pk1, acc0, acc1);
+          if (full) exp_half<kF16, kPoly8, kPacked>(sr, 1, p.scale_log2, -m_use, pk1, lacc);
+          else exp_half<kF16, 0, kPacked>(sr, 1, p.scale_log2, -m_use, pk1, lacc);
           if (resc) {
 #pragma unroll
             for (int ch = 0; ch < kOChunks; ++ch) {
@@ -665,17 +713,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 orow[c] = __float_as_uint(__uint_as_float(orow[c]) * alpha);
               tmem_st32(o_addr + ch * 32, orow);
             }
-            tmem_st32(s_addr, pk0);
           }
+          if (!early) tmem_st32(s_addr, pk0);
           tmem_st32(s_addr + 32, pk1);
           tmem_wait_st();
           tc_fence_before();
-          if (resc) mbar_arrive(&s.p_full[t][0]);
+          if (!early) mbar_arrive(&s.p_full[t][0]);
           mbar_arrive(&s.p_full[t][1]);
-          float a0, a1, b0, b1;
-          f2_unpack(acc0, a0, a1);
-          f2_unpack(acc1, b0, b1);
-          l = l * alpha + ((a0 + a1) + (b0 + b1));
+          l = l * alpha + ((lacc[0] + lacc[1]) + (lacc[2] + lacc[3]));
         }
       }
       if (!ok) break;
@@ -784,20 +829,35 @@ using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMa
                           const CUtensorMap, const PFwdParams);
 
 constexpr int kDefaultPoly8 = 2;
+constexpr int kDefaultVar = 3;
+
+// poly8 / variant tuning space (head_dim 128 bf16 without the ring); every
+// other combination runs the defaults.
+template <int kPoly8>
+KernelFn pick_var(int var) {
+  switch (var) {
+    case 0: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 0>;
+    case 1: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 1>;
+    case 2: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 2>;
+    default: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 3>;
+  }
+}
 
 template <int kD, bool kF16, bool kRing>
-KernelFn pick_poly(int poly8) {
+KernelFn pick_poly(int poly8, int var) {
   if constexpr (kD == 128 && !kF16 && !kRing) {
-    if (poly8 == 0) return attn_fwd_persistent_kernel<128, false, 0, false>;
-    if (poly8 == 3) return attn_fwd_persistent_kernel<128, false, 3, false>;
+    if (poly8 == 0) return pick_var<0>(var);
+    if (poly8 == 4) return pick_var<4>(var);
+    if (poly8 == 2 || poly8 < 0) return pick_var<2>(var);
   }
-  return attn_fwd_persistent_kernel<kD, kF16, kDefaultPoly8, kRing>;
+  return attn_fwd_persistent_kernel<kD, kF16, kDefaultPoly8, kRing, kDefaultVar>;
 }
 
 template <int kD>
-KernelFn pick(bool fp16, bool ring, int poly8) {
-  if (ring) return fp16 ? pick_poly<kD, true, true>(poly8) : pick_poly<kD, false, true>(poly8);
-  return fp16 ? pick_poly<kD, true, false>(poly8) : pick_poly<kD, false, false>(poly8);
+KernelFn pick(bool fp16, bool ring, int poly8, int var) {
+  if (ring)
+    return fp16 ? pick_poly<kD, true, true>(poly8, var) : pick_poly<kD, false, true>(poly8, var);
+  return fp16 ? pick_poly<kD, true, false>(poly8, var) : pick_poly<kD, false, false>(poly8, var);
 }
 
 }  // namespace
@@ -808,14 +868,17 @@ int attn_fwd_persistent_smem_bytes(int head_dim) {
 
 void attn_fwd_persistent_launch(const CUtensorMap& mq, const CUtensorMap& mk,
                                 const CUtensorMap& mv, const CUtensorMap& mslots, int head_dim,
-                                bool fp16, PFwdParams& p, int grid, int poly8,
+                                bool fp16, PFwdParams& p, int grid, int tune,
                                 cudaStream_t stream) {
   MGFA_CHECK(head_dim == 64 || head_dim == 128, "head_dim must be 64 or 128");
   MGFA_CHECK(p.n_seg >= 1 && p.n_seg <= kPMaxSeg, "segment count out of range");
   MGFA_CHECK(p.sched != nullptr, "the persistent forward needs its work counters");
   MGFA_CHECK(!p.ring.enabled || p.batch * p.hkv <= kPMaxChunks, "too many kv-head chunks");
   const bool ring = p.ring.enabled != 0;
-  const KernelFn fn = head_dim == 64 ? pick<64>(fp16, ring, poly8) : pick<128>(fp16, ring, poly8);
+  const int var = tune < 0 ? kDefaultVar : (tune >> 8) & 3;
+  const int poly8 = tune < 0 ? -1 : tune & 0xff;
+  const KernelFn fn =
+      head_dim == 64 ? pick<64>(fp16, ring, poly8, var) : pick<128>(fp16, ring, poly8, var);
   const int smem = attn_fwd_persistent_smem_bytes(head_dim);
   {
     static std::mutex mu;

@@ -80,13 +80,15 @@ struct PFwdParams {
   PRing ring;
 };
 
-// Host side (attn_fwd_persistent.cu). `poly8` selects how many of every 8
-// exponential pairs run as a polynomial on the FMA pipe instead of the MUFU
-// unit (0, 2 or 3 for head_dim 128 bf16 without the ring; every other variant
-// uses the default); negative means the default.
+// Host side (attn_fwd_persistent.cu). `tune` selects the softmax variant of
+// the head_dim 128 bf16 kernel without the ring (every other kernel uses the
+// default): bits 0-7 how many of every 8 exponential pairs run as a polynomial
+// on the FMA pipe instead of MUFU.EX2 (0, 2 or 4), bits 8-9 the arithmetic
+// (bit 8: packed f32x2) and the P hand-over (bit 9: two halves); negative
+// means the default.
 void attn_fwd_persistent_launch(const CUtensorMap& mq, const CUtensorMap& mk,
                                 const CUtensorMap& mv, const CUtensorMap& mslots, int head_dim,
-                                bool fp16, PFwdParams& p, int grid, int poly8,
+                                bool fp16, PFwdParams& p, int grid, int tune,
                                 cudaStream_t stream);
 int attn_fwd_persistent_smem_bytes(int head_dim);
 

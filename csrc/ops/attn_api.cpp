@@ -327,7 +327,7 @@ void flash_fwd_persistent(torch::Tensor q, torch::Tensor k, torch::Tensor v, tor
                           torch::Tensor lse, double scale, bool causal,
                           c10::optional<torch::Tensor> q_tile_pos,
                           c10::optional<torch::Tensor> kv_tile_pos, torch::Tensor status,
-                          int64_t wait_limit_ns, torch::Tensor sched, int64_t poly8,
+                          int64_t wait_limit_ns, torch::Tensor sched, int64_t tune,
                           int64_t grid, std::vector<int64_t> seg_lens) {
   check_bshd(q, "q");
   check_bshd(k, "k");
@@ -391,7 +391,7 @@ void flash_fwd_persistent(torch::Tensor q, torch::Tensor k, torch::Tensor v, tor
   int g = int(grid);
   if (g <= 0) g = device_sm_count(q.get_device());
   if (g > p.n_items) g = p.n_items;
-  attn_fwd_persistent_launch(mq, mk, mv, mk, D, f16, p, g, int(poly8),
+  attn_fwd_persistent_launch(mq, mk, mv, mk, D, f16, p, g, int(tune),
                              at::cuda::getCurrentCUDAStream());
 }
 

@@ -12,7 +12,7 @@ void flash_fwd_persistent(torch::Tensor q, torch::Tensor k, torch::Tensor v, tor
                           torch::Tensor lse, double scale, bool causal,
                           c10::optional<torch::Tensor> q_tile_pos,
                           c10::optional<torch::Tensor> kv_tile_pos, torch::Tensor status,
-                          int64_t wait_limit_ns, torch::Tensor sched, int64_t poly8,
+                          int64_t wait_limit_ns, torch::Tensor sched, int64_t tune,
                           int64_t grid, std::vector<int64_t> seg_lens);
 void legacy_partial(torch::Tensor q, torch::Tensor k, torch::Tensor v, double scale,
                     c10::optional<torch::Tensor> q_pos, c10::optional<torch::Tensor> k_pos,
@@ -23,6 +23,7 @@ void legacy_normalize(torch::Tensor acc, torch::Tensor l, torch::Tensor out,
                       c10::optional<torch::Tensor> lse, c10::optional<torch::Tensor> m);
 void red_probe(torch::Tensor dq, int64_t n_kv_tiles, bool causal);
 void register_ring_engine(py::module& m);
+void register_ring_engine_p(py::module& m);
 void register_ring_exchange(py::module& m);
 void register_ring_bwd_engine(py::module& m);
 torch::Tensor fwd_timeout_probe(torch::Tensor q, torch::Tensor k, torch::Tensor v,
@@ -48,7 +49,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_fwd_persistent", &mgfa::flash_fwd_persistent, py::arg("q"), py::arg("k"),
         py::arg("v"), py::arg("o"), py::arg("lse"), py::arg("scale"), py::arg("causal"),
         py::arg("q_tile_pos"), py::arg("kv_tile_pos"), py::arg("status"),
-        py::arg("wait_limit_ns"), py::arg("sched"), py::arg("poly8") = int64_t(-1),
+        py::arg("wait_limit_ns"), py::arg("sched"), py::arg("tune") = int64_t(-1),
         py::arg("grid") = int64_t(0), py::arg("seg_lens") = std::vector<int64_t>());
   m.def("red_probe", &mgfa::red_probe, py::arg("dq"), py::arg("n_kv_tiles"),
         py::arg("causal"));
@@ -76,6 +77,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("q"), py::arg("k"), py::arg("v"), py::arg("wait_limit_ns"),
         py::arg("status") = py::none());
   mgfa::register_ring_engine(m);
+  mgfa::register_ring_engine_p(m);
   mgfa::register_ring_exchange(m);
   mgfa::register_ring_bwd_engine(m);
 }

@@ -1,0 +1,85 @@
+"""Forward-kernel variant sweep on one GPU (CUDA-event timing, L2 flushed
+between launches): the per-query-tile-pair kernel (flash_fwd_sm100.cu) against
+the persistent kernel (attn_fwd_persistent.cu) in each of its softmax variants.
+
+    python -m multi_gpu_flashattention_b200.benchmarks.fwd_tuning [--seq 131072]
+        [--heads 32] [--kv-heads 32] [--no-causal] [--reps 5] [--tunes 0x002,0x302,...]
+
+A tune value is the persistent kernel's variant word (attn_fwd_persistent.cuh):
+bits 0-7 exponential pairs of every 8 on the FMA pipe (0, 2 or 4), bit 8 packed
+f32x2 arithmetic, bit 9 P handed over in two halves. Prints one JSON line per
+variant with the median time and attention TFLOP/s."""
+from __future__ import annotations
+
+import argparse
+import json
+import statistics
+
+import torch
+
+from .._ext import C
+from ..ops.flash import tile_positions
+
+DEFAULT_TUNES = "-1,0x000,0x100,0x200,0x300,0x002,0x102,0x202,0x302,0x004,0x104,0x304"
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--seq", type=int, default=131072)
+    ap.add_argument("--heads", type=int, default=32)
+    ap.add_argument("--kv-heads", type=int, default=32)
+    ap.add_argument("--no-causal", action="store_true")
+    ap.add_argument("--reps", type=int, default=5)
+    ap.add_argument("--tunes", default=DEFAULT_TUNES)
+    a = ap.parse_args(argv)
+    causal = not a.no_causal
+    S, H, Hkv, D = a.seq, a.heads, a.kv_heads, 128
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q = (torch.randn(1, S, H, D, device="cuda", generator=g) * 0.5).bfloat16()
+    k = (torch.randn(1, S, Hkv, D, device="cuda", generator=g) * 0.5).bfloat16()
+    v = (torch.randn(1, S, Hkv, D, device="cuda", generator=g) * 0.5).bfloat16()
+    o = torch.empty_like(q)
+    lse = torch.empty(1, H, S, device="cuda")
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    sched = torch.zeros(2, dtype=torch.int32, device="cuda")
+    pos = tile_positions(S, "cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    scale = D ** -0.5
+    pairs = S * (S + 1) // 2 if causal else S * S
+    flops = 4.0 * D * H * pairs
+
+    def stepwise():
+        C().flash_fwd(q, k, v, o, None, lse, scale, causal, pos, pos, False, True, st,
+                      2_000_000_000)
+
+    def persistent(tune):
+        return lambda: C().flash_fwd_persistent(q, k, v, o, lse, scale, causal, pos, pos, st,
+                                                2_000_000_000, sched, tune)
+
+    cases = [("stepwise", None, stepwise)]
+    for t in a.tunes.split(","):
+        tv = int(t, 0)
+        cases.append(("persistent", tv, persistent(tv)))
+    for name, tune, fn in cases:
+        for _ in range(2):
+            fn()
+        times = []
+        for i in range(a.reps):
+            flush.fill_(i & 0xFF)
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record()
+            fn()
+            s1.record()
+            torch.cuda.synchronize()
+            times.append(s0.elapsed_time(s1))
+        if int(st.item()) != 0:
+            raise SystemExit(f"{name} {tune}: kernel status {int(st.item()):#x}")
+        ms = statistics.median(times)
+        print(json.dumps({"kernel": name, "tune": None if tune is None else hex(tune) if tune >= 0
+                          else -1, "seq": S, "heads": H, "causal": causal, "ms": round(ms, 3),
+                          "tflops": round(flops / ms / 1e9, 1)}), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

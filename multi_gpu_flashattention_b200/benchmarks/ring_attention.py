@@ -41,7 +41,8 @@ from .._ext import C, sched as _sched
 from ..parallel.layouts import RingLayout
 from . import common
 
-COMM_NAME = {"nccl": "NCCL", "staged": "MPI", "fused": "P2P", "p2p_unfused": "P2P",
+COMM_NAME = {"nccl": "NCCL", "staged": "MPI", "fused": "P2P", "fused_stepwise": "P2P",
+             "p2p_unfused": "P2P",
              "ce_unfused": "CE", "p2p": "P2P", "ce": "CE"}
 
 
@@ -51,7 +52,8 @@ def parse():
     ap.add_argument("warmup", type=int, nargs="?", default=10)
     ap.add_argument("iters", type=int, nargs="?", default=100)
     ap.add_argument("--backend", default=None,
-                    choices=["fused", "p2p_unfused", "ce_unfused", "nccl", "staged", "p2p", "ce"])
+                    choices=["fused", "fused_stepwise", "p2p_unfused", "ce_unfused", "nccl",
+                             "staged", "p2p", "ce"])
     ap.add_argument("--numerics", default="fp32", choices=["fp32", "bf16"])
     ap.add_argument("--init", default="legacy", choices=["legacy", "randn"])
     ap.add_argument("--layout", default="contiguous",
@@ -336,7 +338,7 @@ class Bf16Ring:
         self.status = torch.zeros(1, dtype=torch.int32, device=ctx.device)
 
     def run(self, log_steps):
-        from ..parallel.ring import ENGINES, _meta, ring_attention_forward
+        from ..parallel.ring import ENGINES, P_ENGINES, _meta, ring_attention_forward
         ctx, lay, P, r = self.ctx, self.lay, self.ctx.world, self.ctx.rank
         if log_steps:
             for s in range(P - 1):
@@ -345,9 +347,11 @@ class Bf16Ring:
                         f"receiving_kv_owner={ro} KV tokens={tokens(lay, ro)}")
             o = lay.compute_owner(r, P - 1)
             ctx.log(f"[Rank {r}] final compute_kv_owner={o} KV tokens={tokens(lay, o)}")
-        fused = self.args.backend in ("fused", "p2p_unfused", "ce_unfused") and P > 1
+        fused = self.args.backend in ("fused", "fused_stepwise", "p2p_unfused",
+                                      "ce_unfused") and P > 1
         if fused:
-            eng = ENGINES.get(None, ctx.device, self.k.numel() * self.k.element_size())
+            engines = P_ENGINES if self.args.backend == "fused" else ENGINES
+            eng = engines.get(None, ctx.device, self.k.numel() * self.k.element_size())
             qtp, kvtp, kv_lens = _meta(lay, r, ctx.device)
 
             def compute_only():

@@ -176,8 +176,10 @@ def _default_positions(n_tokens: int, device) -> torch.Tensor:
 # scheduler, attn_fwd_persistent.cu) or "stepwise" (one CTA per query-tile pair,
 # flash_fwd_sm100.cu, the kernel the per-step ring and the merge path use).
 FWD_KERNEL = os.environ.get("MGFA_FWD_KERNEL", "persistent")
-# exponential pairs (of every 8) computed on the FMA pipe; -1: the kernel's default
-POLY8 = int(os.environ.get("MGFA_POLY8", "-1"))
+# softmax variant of the persistent forward (attn_fwd_persistent.cuh: bits 0-7
+# exponential pairs of every 8 on the FMA pipe, bit 8 packed f32x2 arithmetic,
+# bit 9 P handed over in two halves); -1: the kernel's default
+FWD_TUNE = int(os.environ.get("MGFA_FWD_TUNE", "-1"), 0)
 
 _SCHED: dict = {}
 
@@ -187,6 +189,8 @@ def sched_counters(device) -> torch.Tensor:
     `device`: two int32 zeros, which every launch leaves zeroed again. One pair
     per (device, stream), so launches that may overlap never share one."""
     dev = torch.device(device)
+    if dev.type != "cuda":  # the kernel's argument checks reject host tensors
+        return torch.zeros(2, dtype=torch.int32)
     key = (str(dev), torch.cuda.current_stream(dev).cuda_stream)
     t = _SCHED.get(key)
     if t is None:
@@ -222,7 +226,7 @@ def flash_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bo
     if FWD_KERNEL == "persistent":
         C().flash_fwd_persistent(q, k, v, o, lse, _scale(q, softmax_scale), causal, q_tile_pos,
                                  kv_tile_pos, st, int(wait_limit_ns), sched_counters(q.device),
-                                 POLY8)
+                                 FWD_TUNE)
     else:
         C().flash_fwd(q, k, v, o, None, lse, _scale(q, softmax_scale), causal, q_tile_pos,
                       kv_tile_pos, False, True, st, int(wait_limit_ns))

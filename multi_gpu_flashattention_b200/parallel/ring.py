@@ -11,13 +11,21 @@ ring/attention/bench/ring_attention_nccl_gpu_bench.cu:349-397).
 
 Backends
 --------
-fused   (default on CUDA) one sm_100a kernel per step that computes, merges
-        in-kernel and pushes the current shard into the right neighbour's
-        receive slot with peer stores (native RingEngine).
+fused   (default on CUDA) the whole ring in ONE launch of the persistent
+        sm_100a kernel (native RingEngineP): every rank keeps a receive slot per
+        ring step, computes each query tile against its own shard and then
+        every received shard as its kv-head chunk arrives, with the softmax
+        state on chip across steps (no per-step merge), while the kernel's
+        push warps forward each received chunk to the right neighbour with peer
+        stores.
+fused_stepwise
+        one sm_100a kernel launch per ring step that computes, merges in-kernel
+        and pushes the current shard into the right neighbour's receive slot
+        (native RingEngine).
 p2p_unfused, ce_unfused
-        ablations of `fused`: the same engine, slots and flags, with the shard
-        moved on a second stream by the standalone push kernel or by the copy
-        engine (forward only; their backward uses the nccl path).
+        ablations of `fused_stepwise`: the same engine, slots and flags, with the
+        shard moved on a second stream by the standalone push kernel or by the
+        copy engine (forward only; their backward uses the nccl path).
 nccl    baseline: NCCL send/recv on a side stream, overlapped with the same
         attention kernel (merge in-kernel).
 staged  baseline: device -> pinned host -> gloo send/recv -> device, the
@@ -39,9 +47,9 @@ from ..ops.flash import (DEFAULT_WAIT_LIMIT_NS, check_status, flash_attn_fwd,
 from ..ops.reference import attention_ref
 from .layouts import RingLayout
 
-BACKENDS = ("fused", "p2p_unfused", "ce_unfused", "nccl", "staged", "torch")
-# transport modes of the fused engine (RingEngine.set_transport_mode)
-_ENGINE_MODES = {"fused": 0, "p2p_unfused": 1, "ce_unfused": 2}
+BACKENDS = ("fused", "fused_stepwise", "p2p_unfused", "ce_unfused", "nccl", "staged", "torch")
+# transport modes of the per-step engine (RingEngine.set_transport_mode)
+_ENGINE_MODES = {"fused_stepwise": 0, "p2p_unfused": 1, "ce_unfused": 2}
 
 
 def _world(group) -> Tuple[int, int]:
@@ -118,6 +126,42 @@ class _Engines:
 ENGINES = _Engines()
 
 
+class _PEngines:
+    """One native RingEngineP (the one-launch ring) per (process group,
+    device); grown on demand. Creating or growing an engine is collective."""
+
+    def __init__(self):
+        self._by_key = {}
+
+    def get(self, group, device: torch.device, shard_bytes: int):
+        rank, world = _world(group)
+        key = (id(group), device.index)
+        eng = self._by_key.get(key)
+        if eng is not None and eng.shard_bytes() >= shard_bytes:
+            return eng
+        cap = max(shard_bytes, 1 << 20)
+        cap = (cap + (2 << 20) - 1) // (2 << 20) * (2 << 20)
+        if eng is not None:
+            torch.cuda.synchronize(device)
+            dist.barrier(group)  # every rank is past its last use of the old slots
+            self._by_key.pop(key)
+            del eng
+        eng = C().RingEngineP(rank, world, device.index, cap)
+        handles = [None] * world
+        dist.all_gather_object(handles, eng.ipc_handle(), group=group)
+        eng.connect(handles)
+        torch.cuda.synchronize(device)
+        dist.barrier(group)
+        self._by_key[key] = eng
+        return eng
+
+    def clear(self):
+        self._by_key.clear()
+
+
+P_ENGINES = _PEngines()
+
+
 # ---------------------------------------------------------------------- metadata cache
 _META = {}
 
@@ -133,11 +177,12 @@ def _meta(layout: RingLayout, rank: int, device):
 
 
 # ---------------------------------------------------------------------- forward backends
-def _fwd_fused(q, k, v, layout, causal, scale, group, status, wait_ns, mode="fused"):
-    """The native engine's ring. mode "fused": the transport runs inside the
-    attention kernel; "p2p_unfused": the same NVLink push as a separate all-SM
-    kernel on a second stream; "ce_unfused": the copy engine moves the shard on a
-    second stream (both ablations keep the flags and slots)."""
+def _fwd_fused(q, k, v, layout, causal, scale, group, status, wait_ns, mode="fused_stepwise"):
+    """The per-step engine's ring. mode "fused_stepwise": the transport runs
+    inside each step's attention kernel; "p2p_unfused": the same NVLink push as
+    a separate all-SM kernel on a second stream; "ce_unfused": the copy engine
+    moves the shard on a second stream (both ablations keep the flags and
+    slots)."""
     rank, world = _world(group)
     qtp, kvtp, kv_lens = _meta(layout, rank, q.device)
     shard_bytes = k.numel() * k.element_size()
@@ -149,6 +194,15 @@ def _fwd_fused(q, k, v, layout, causal, scale, group, status, wait_ns, mode="fus
     finally:
         eng.set_transport_mode(0)
     return o, lse
+
+
+def _fwd_persistent(q, k, v, layout, causal, scale, group, status, wait_ns):
+    """The one-launch ring of the persistent kernel (RingEngineP)."""
+    rank, world = _world(group)
+    qtp, kvtp, kv_lens = _meta(layout, rank, q.device)
+    eng = P_ENGINES.get(group, q.device, k.numel() * k.element_size())
+    return eng.forward(q, k, v, scale, causal, qtp if causal else None,
+                       kvtp if causal else None, kv_lens, status, int(wait_ns))
 
 
 def _fwd_nccl(q, k, v, layout, causal, scale, group, status, wait_ns, overlap=True):
@@ -303,6 +357,8 @@ def ring_attention_forward(q, k, v, layout: RingLayout, causal: bool = False,
         out, lse = flash_attn_fwd(q, k[:, :kv_lens[0]], v[:, :kv_lens[0]], causal=causal,
                                   softmax_scale=scale, q_tile_pos=qtp, kv_tile_pos=kvtp[0],
                                   status=st, wait_limit_ns=wait_limit_ns)
+    elif backend == "fused":
+        out, lse = _fwd_persistent(q, k, v, layout, causal, scale, group, st, wait_limit_ns)
     elif backend in _ENGINE_MODES:
         out, lse = _fwd_fused(q, k, v, layout, causal, scale, group, st, wait_limit_ns,
                               mode=backend)
@@ -335,7 +391,7 @@ def reset_ring(group=None) -> None:
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier(group)
-    for engines in (ENGINES, BWD_ENGINES):
+    for engines in (ENGINES, P_ENGINES, BWD_ENGINES):
         eng = engines._by_key.get((id(group), dev.index))
         if eng is not None:
             eng.reset()

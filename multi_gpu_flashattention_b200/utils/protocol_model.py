@@ -438,3 +438,156 @@ def check(world: int, kind: str, calls: int = 2, seeds: int = 50, release_slot0:
     for seed in range(seeds):
         Model(world, kind, calls, seed, release_slot0, wait_received, small_grid,
               chain_guard, cumulative, mutation).run()
+
+
+# ---------------------------------------------------------------- one-launch ring
+class OneLaunchModel:
+    """The one-launch ring (csrc/comm/ring_engine_p.hpp, kernels/attn_fwd_persistent.cu).
+
+    Every rank has one receive slot per ring step s = 1..P-1 and kv-head chunk
+    c; the shard in slot (s, c) belongs to owner (rank - s) mod P. One kernel per
+    call and rank, launched after the rank's previous call finished (stream
+    order), runs concurrently:
+      * `workers` push workers (the push warps): wait until the right neighbour
+        finished the previous call (credit >= call), then for every chunk c and
+        step s < P-1, in that order, wait for unit (s, c) to have arrived (s >= 1),
+        store their part of it into the right neighbour's slot (s + 1, c) and add
+        one arrival there;
+      * compute workers (the CTAs' producers): read each unit after all its
+        parts arrived, chunks in order, a random subset of them (causal
+        visibility decides which a rank needs);
+      * the last CTA: after every worker finished, wait until every unit of the
+        call arrived, re-arm the arrival counts to 0 and publish call + 1 to the
+        left neighbour's credit word.
+    Violations: a store into a slot whose previous contents the right neighbour
+    may still read (it has not finished the call they belong to), or a read
+    that finds another (owner, call) than expected.
+    Mutations: "no_credit" (pushes skip the credit wait), "no_final_wait" (the
+    last CTA re-arms the counts without waiting for late arrivals)."""
+
+    def __init__(self, world: int, chunks: int = 2, workers: int = 2, calls: int = 3,
+                 seed: int = 0, mutation: Optional[str] = None):
+        self.P, self.C, self.W, self.calls = world, chunks, workers, calls
+        self.rng = random.Random(seed)
+        self.mutation = mutation
+        P, C = world, chunks
+        # slot[r][s][c] = (owner, call) of the last completed store; readers
+        self.content = [[[None] * C for _ in range(P)] for _ in range(P)]
+        self.readers = [[[0] * C for _ in range(P)] for _ in range(P)]
+        self.arrivals = [[[0] * C for _ in range(P)] for _ in range(P)]
+        self.credit = [0] * P
+        self.finished = [0] * P          # calls each rank's kernel completed
+        self.procs: List[Proc] = []
+        self.waits: List[Optional[Wait]] = []
+
+    def _spawn(self, proc: Proc) -> None:
+        self.procs.append(proc)
+        self.waits.append(None)
+        try:
+            self.waits[-1] = next(proc)
+        except StopIteration:
+            self.procs[-1] = None
+
+    def _call(self, r: int, k: int) -> Proc:
+        """Rank r's call k: launched once call k - 1 finished on this rank."""
+        yield lambda: self.finished[r] >= k
+        done = [0]
+        n_workers = 2 * self.W
+        for w in range(self.W):
+            self._spawn(self._push(r, k, w, done))
+            self._spawn(self._compute(r, k, done))
+        yield lambda: done[0] == n_workers
+        # last CTA
+        P, C = self.P, self.C
+        if self.mutation != "no_final_wait":
+            yield lambda: all(self.arrivals[r][s][c] == self.W
+                              for s in range(1, P) for c in range(C))
+        for s in range(1, P):
+            for c in range(C):
+                self.arrivals[r][s][c] = 0
+        self.credit[(r - 1) % P] = k + 1
+        self.finished[r] = k + 1
+
+    def _push(self, r: int, k: int, w: int, done: List[int]) -> Proc:
+        P, C = self.P, self.C
+        right = (r + 1) % P
+        if self.mutation != "no_credit":
+            yield lambda: self.credit[r] >= k
+        for c in range(C):
+            for s in range(P - 1):
+                if s >= 1:
+                    yield lambda s=s, c=c: self.arrivals[r][s][c] >= self.W
+                    self._read(r, s, c, k)
+                owner = (r - s) % P
+                # the store: the right neighbour must be done with what it holds
+                old = self.content[right][s + 1][c]
+                stale = old is not None and old[1] != k and self.finished[right] <= old[1]
+                if (self.readers[right][s + 1][c] and old is not None and old[1] != k) or stale:
+                    raise ProtocolViolation(
+                        f"rank {right} slot ({s + 1}, {c}): store of call {k} while call "
+                        f"{old[1] if old else None} may still read it")
+                yield lambda: True
+                if w == 0:
+                    self.content[right][s + 1][c] = (owner, k)
+                self.arrivals[right][s + 1][c] += 1
+                if s >= 1:
+                    self.readers[r][s][c] -= 1
+        done[0] += 1
+
+    def _read(self, r: int, s: int, c: int, k: int) -> None:
+        expect = ((r - s) % self.P, k)
+        if self.content[r][s][c] != expect:
+            raise ProtocolViolation(f"rank {r} slot ({s}, {c}): holds "
+                                    f"{self.content[r][s][c]}, expected {expect}")
+        self.readers[r][s][c] += 1
+
+    def _compute(self, r: int, k: int, done: List[int]) -> Proc:
+        for c in range(self.C):
+            for s in range(1, self.P):
+                if self.rng.random() < 0.3:
+                    continue  # a unit nobody on this rank needs (causal visibility)
+                yield lambda s=s, c=c: self.arrivals[r][s][c] >= self.W
+                self._read(r, s, c, k)
+                yield lambda: True
+                self.readers[r][s][c] -= 1
+        done[0] += 1
+
+    def run(self, max_events: int = 500000) -> int:
+        for r in range(self.P):
+            self._spawn(_chain([self._call(r, k) for k in range(self.calls)]))
+        events = 0
+        while any(p is not None for p in self.procs):
+            ready = [i for i, (p, w) in enumerate(zip(self.procs, self.waits))
+                     if p is not None and w is not None and w()]
+            if not ready:
+                raise RuntimeError("deadlock: no activity can proceed")
+            i = self.rng.choice(ready)
+            try:
+                self.waits[i] = next(self.procs[i])
+            except StopIteration:
+                self.waits[i] = None
+                self.procs[i] = None
+            events += 1
+            if events > max_events:
+                raise RuntimeError("event budget exhausted")
+        return events
+
+
+def one_launch_plan(world: int, rank: int, calls: int) -> List[List[int]]:
+    """The one-launch engine's flag values as the model uses them: one row per
+    call, [call, credit the pushes wait for, credit published at the end, tag of
+    segment 0, ..., tag of segment world-1] with tag (owner + 1) | call << 8;
+    RingEngineP.plan() must produce the same rows."""
+    rows = []
+    for k in range(calls):
+        rows.append([k, k, k + 1] + [((rank - s) % world + 1) | (k << 8)
+                                     for s in range(world)])
+    return rows
+
+
+def check_one_launch(world: int, chunks: int = 2, workers: int = 2, calls: int = 3,
+                     seeds: int = 50, mutation: Optional[str] = None) -> None:
+    """Runs `seeds` random interleavings of the one-launch ring; raises on the
+    first violation."""
+    for seed in range(seeds):
+        OneLaunchModel(world, chunks, workers, calls, seed, mutation).run()

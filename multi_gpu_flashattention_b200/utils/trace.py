@@ -1,11 +1,16 @@
-"""Kernel timelines of the fused ring engine as Chrome trace events.
+"""Kernel timelines of the ring engines as Chrome trace events.
 
-Enable with `ENGINES.get(...).set_trace(True)` (or `ring_trace(...)` below),
-run a forward, then `engine.last_trace()` holds [steps, CTAs, 8] int64 words
+Per-step engine (backend "fused_stepwise"): enable with
+`ENGINES.get(...).set_trace(True)`, run a forward, then `engine.last_trace()`
+holds [steps, CTAs, 8] int64 words
 per call: {sm << 32 | cta, start, kv_ready, epilogue, push_start, push_end,
 end, visible key tiles} in %globaltimer nanoseconds. `to_chrome_events` turns
 them into complete ("X") events -- one process per rank, one thread per SM --
-for chrome://tracing or Perfetto."""
+for chrome://tracing or Perfetto.
+
+One-launch engine (backend "fused"): `P_ENGINES.get(...).set_trace(True)`
+gives [grid, 8] words per call; see summarize_one_launch and
+one_launch_chrome_events."""
 from __future__ import annotations
 
 import json
@@ -79,3 +84,50 @@ def summarize(trace: torch.Tensor) -> dict:
             entry["push_done_ms"] = (pw[:, 5].max() - w[:, 1].min()).item() / 1e6
         out.append(entry)
     return {"steps": out}
+
+
+def summarize_one_launch(trace: torch.Tensor) -> dict:
+    """Summary of a one-launch ring call's per-CTA trace ([grid, 8] int64:
+    {sm << 32 | cta, start, end, items, ns waiting for arrivals, -, push start,
+    push end}), in ms: kernel span, CTA busy time (mean / min / max), how long
+    CTAs waited for received shards (mean / max), and the push window (first
+    start to last end, mean per push warp)."""
+    t = trace.detach().cpu().to(torch.int64)
+    ok = t[:, 1] != 0
+    t = t[ok]
+    if t.shape[0] == 0:
+        return {}
+    t0 = int(t[:, 1].min())
+    busy = (t[:, 2] - t[:, 1]).double() / 1e6
+    wait = t[:, 4].double() / 1e6
+    out = {"span_ms": (int(t[:, 2].max()) - t0) / 1e6, "n_ctas": int(t.shape[0]),
+           "items": int(t[:, 3].sum()), "cta_ms_mean": busy.mean().item(),
+           "cta_ms_min": busy.min().item(), "cta_ms_max": busy.max().item(),
+           "arrival_wait_ms_mean": wait.mean().item(), "arrival_wait_ms_max": wait.max().item()}
+    pushed = t[:, 6] != 0
+    if pushed.any():
+        p = t[pushed]
+        out["push_start_ms"] = (int(p[:, 6].min()) - t0) / 1e6
+        out["push_end_ms"] = (int(p[:, 7].max()) - t0) / 1e6
+        out["push_ms_mean"] = ((p[:, 7] - p[:, 6]).double() / 1e6).mean().item()
+    return out
+
+
+def one_launch_chrome_events(trace: torch.Tensor, rank: int = 0) -> List[dict]:
+    """Chrome trace events of a one-launch ring call: per CTA its busy span and
+    the push window of its push warps."""
+    t = trace.detach().cpu().to(torch.int64)
+    ok = t[:, 1] != 0
+    if not ok.any():
+        return []
+    t0 = int(t[ok, 1].min())
+    ev = []
+    for w in t[ok].tolist():
+        sm = w[0] >> 32
+        args = {"cta": w[0] & 0xFFFFFFFF, "items": w[3], "arrival_wait_us": w[4] / 1e3}
+        ev.append({"name": "attention", "ph": "X", "pid": rank, "tid": sm,
+                   "ts": (w[1] - t0) / 1e3, "dur": (w[2] - w[1]) / 1e3, "args": args})
+        if w[6] and w[7]:
+            ev.append({"name": "push", "ph": "X", "pid": rank, "tid": 1000 + sm,
+                       "ts": (w[6] - t0) / 1e3, "dur": (w[7] - w[6]) / 1e3, "args": args})
+    return ev

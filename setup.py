@@ -60,6 +60,7 @@ if which in ("all", "cuda"):
                 "csrc/kernels/legacy_fp32.cu",
                 "csrc/comm/symmetric.cpp",
                 "csrc/comm/ring_engine.cpp",
+                "csrc/comm/ring_engine_p.cpp",
                 "csrc/comm/ring_exchange.cpp",
                 "csrc/comm/ring_bwd_engine.cpp",
                 "csrc/kernels/ring_exchange.cu",

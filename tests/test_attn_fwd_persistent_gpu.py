@@ -31,7 +31,7 @@ def _check(o, lse, q, k, v, causal, q_pos=None, k_pos=None):
     torch.testing.assert_close(lse[finite], ref_lse[finite], rtol=0, atol=2e-3)
 
 
-def _run(q, k, v, causal, qtp=None, ktp=None, poly8=-1, grid=0, seg_lens=(), calls=1):
+def _run(q, k, v, causal, qtp=None, ktp=None, tune=-1, grid=0, seg_lens=(), calls=1):
     from multi_gpu_flashattention_b200.ops.flash import check_status, tile_positions
     if causal and qtp is None:
         qtp = tile_positions(q.shape[1], "cuda")
@@ -44,7 +44,7 @@ def _run(q, k, v, causal, qtp=None, ktp=None, poly8=-1, grid=0, seg_lens=(), cal
         o = torch.full_like(q, float("nan"))
         lse = torch.empty(q.shape[0], q.shape[2], q.shape[1], device="cuda")
         _C().flash_fwd_persistent(q, k, v, o, lse, q.shape[-1] ** -0.5, causal, qtp, ktp, st,
-                                  2_000_000_000, sched, poly8, grid, list(seg_lens))
+                                  2_000_000_000, sched, tune, grid, list(seg_lens))
         check_status(st)
         outs.append((o, lse))
     torch.cuda.synchronize()
@@ -52,12 +52,17 @@ def _run(q, k, v, causal, qtp=None, ktp=None, poly8=-1, grid=0, seg_lens=(), cal
     return outs
 
 
-@pytest.mark.parametrize("poly8", [0, 2, 3])
+# softmax variants: polynomial pairs of 8 (0, 2, 4) x scalar / packed x whole /
+# split P hand-over
+TUNES = [-1, 0x000, 0x002, 0x004, 0x100, 0x200, 0x302, 0x304]
+
+
+@pytest.mark.parametrize("tune", TUNES)
 @pytest.mark.parametrize("causal", [False, True])
 @pytest.mark.parametrize("B,S,Hq,Hkv", [(1, 256, 2, 2), (2, 640, 4, 1), (1, 1024, 3, 3)])
-def test_self_attention(B, S, Hq, Hkv, causal, poly8):
+def test_self_attention(B, S, Hq, Hkv, causal, tune):
     q, k, v = _inputs(B, S, S, Hq, Hkv)
-    (o, lse), = _run(q, k, v, causal, poly8=poly8)
+    (o, lse), = _run(q, k, v, causal, tune=tune)
     _check(o, lse, q, k, v, causal)
 
 

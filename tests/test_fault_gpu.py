@@ -47,30 +47,31 @@ def test_public_call_raises_error_of_an_earlier_kernel():
 
 
 def _drop_signal_public(rank, world):
-    """The dropped signal surfaces through mgfa.ring_attention() itself (no
-    check=True, no status argument): the receiving rank's next public call
-    raises, and reset_ring() re-arms the ring on both ranks."""
+    """A dropped signal of the one-launch ring surfaces through
+    mgfa.ring_attention() itself (no check=True, no status argument): the
+    receiving rank's next public call raises, and reset_ring() re-arms the ring
+    on both ranks."""
     import multi_gpu_flashattention_b200 as mgfa
     from multi_gpu_flashattention_b200.ops.flash import KernelStatusError, check_errors
-    from multi_gpu_flashattention_b200.parallel.ring import ENGINES, reset_ring
+    from multi_gpu_flashattention_b200.parallel.ring import P_ENGINES, reset_ring
     dev = torch.device("cuda", rank)
     g = torch.Generator(device=dev).manual_seed(rank)
     q = (torch.randn(1, 512, 2, 128, device=dev, generator=g) * 0.5).bfloat16()
-    out_ok = mgfa.ring_attention(q, q, q, backend="fused")
+    out_ok = mgfa.ring_attention(q, q, q)
     check_errors()
-    eng = ENGINES.get(None, dev, q.numel() * 2)
+    eng = P_ENGINES.get(None, dev, q.numel() * 2)
     if rank == 0:
-        eng.set_drop_signal_step(0)  # rank 1 never hears about one chunk of step 0
-    mgfa.ring_attention(q, q, q, backend="fused")
-    eng.set_drop_signal_step(-1)
+        eng.set_drop_signal(True)  # rank 1 never hears about one part of kv head 0
+    mgfa.ring_attention(q, q, q)
+    eng.set_drop_signal(False)
     torch.cuda.synchronize()
     if rank == 1:
         with pytest.raises(KernelStatusError, match="peer flag wait timed out"):
-            mgfa.ring_attention(q, q, q, backend="fused")
+            mgfa.ring_attention(q, q, q)
     else:
         check_errors()  # the sending side finished its work
     reset_ring()
-    out = mgfa.ring_attention(q, q, q, backend="fused")
+    out = mgfa.ring_attention(q, q, q)
     check_errors()
     torch.testing.assert_close(out, out_ok, rtol=0, atol=0)
 
@@ -89,17 +90,17 @@ def _drop_signal(rank, world):
     lay = RingLayout("contiguous", 1024, world, mask="full")
     g = torch.Generator(device=dev).manual_seed(rank)
     q = (torch.randn(1, 512, 2, 128, device=dev, generator=g) * 0.5).bfloat16()
-    out_ok, _ = ring_attention_forward(q, q, q, lay, backend="fused", check=True)
+    out_ok, _ = ring_attention_forward(q, q, q, lay, backend="fused_stepwise", check=True)
     eng = ENGINES.get(None, dev, q.numel() * 2)
     if rank == 0:
         eng.set_drop_signal_step(0)  # rank 1 never hears about one chunk of step 0
     st = torch.zeros(1, dtype=torch.int32, device=dev)
     if rank == 1:
         with pytest.raises(KernelStatusError, match="peer flag wait timed out"):
-            ring_attention_forward(q, q, q, lay, backend="fused", status=st,
+            ring_attention_forward(q, q, q, lay, backend="fused_stepwise", status=st,
                                    wait_limit_ns=300_000_000, check=True)
     else:
-        ring_attention_forward(q, q, q, lay, backend="fused", status=st,
+        ring_attention_forward(q, q, q, lay, backend="fused_stepwise", status=st,
                                wait_limit_ns=300_000_000, check=True)
     # recover: every rank idle, flags re-armed, then a clean call matches the first
     eng.set_drop_signal_step(-1)
@@ -108,7 +109,7 @@ def _drop_signal(rank, world):
     eng.reset()
     torch.cuda.synchronize()
     torch.distributed.barrier()
-    out, _ = ring_attention_forward(q, q, q, lay, backend="fused", check=True)
+    out, _ = ring_attention_forward(q, q, q, lay, backend="fused_stepwise", check=True)
     torch.testing.assert_close(out, out_ok, rtol=0, atol=0)
 
 

@@ -89,3 +89,25 @@ def test_native_backward_engine_flag_arithmetic_matches_the_model(world, rank):
     except Exception as e:  # pragma: no cover - extension not built
         pytest.skip(f"extension not built: {e}")
     assert [list(r) for r in eng.plan(world, rank, 3)] == backward_plan(world, rank, 3)
+
+
+@pytest.mark.parametrize("world", [2, 3, 5, 8])
+def test_one_launch_ring_is_race_free(world):
+    from multi_gpu_flashattention_b200.utils.protocol_model import check_one_launch
+    check_one_launch(world, chunks=2, workers=2, calls=3, seeds=40)
+
+
+@pytest.mark.parametrize("mutation", ["no_credit", "no_final_wait"])
+def test_one_launch_checker_catches_broken_variants(mutation):
+    from multi_gpu_flashattention_b200.utils.protocol_model import (ProtocolViolation,
+                                                                    check_one_launch)
+    with pytest.raises(ProtocolViolation):
+        check_one_launch(3, chunks=2, workers=2, calls=3, seeds=200, mutation=mutation)
+
+
+@pytest.mark.parametrize("world,rank", [(2, 1), (5, 3), (8, 0)])
+def test_native_one_launch_engine_flags_match_the_model(world, rank):
+    from multi_gpu_flashattention_b200._ext import C
+    from multi_gpu_flashattention_b200.utils.protocol_model import one_launch_plan
+    assert [list(r) for r in C().RingEngineP.plan(world, rank, 4)] == \
+        one_launch_plan(world, rank, 4)

@@ -35,10 +35,14 @@ def _case(rank, world, kind, causal, backend, seq, hq, hkv, iters):
 
 
 def _world():
-    return min(torch.cuda.device_count(), 4)
+    # every visible GPU, up to MGFA_TEST_MAX_WORLD (default 8), so an 8-GPU run
+    # tests the ring at P = 8
+    import os
+    return min(torch.cuda.device_count(), int(os.environ.get("MGFA_TEST_MAX_WORLD", "8")))
 
 
-@pytest.mark.parametrize("backend", ["fused", "p2p_unfused", "ce_unfused", "nccl"])
+@pytest.mark.parametrize("backend", ["fused", "fused_stepwise", "p2p_unfused", "ce_unfused",
+                                     "nccl"])
 @pytest.mark.parametrize("kind,causal", [("zigzag", True), ("striped", True),
                                          ("contiguous", False), ("contiguous", True)])
 def test_ring_forward_matches_reference(backend, kind, causal):
@@ -48,12 +52,20 @@ def test_ring_forward_matches_reference(backend, kind, causal):
 def test_ring_forward_cumulative_arrival_counts():
     """Arrival counters that keep growing (cumulative targets): repeated calls
     stay correct with dependent launch on."""
-    run_ranks(_case, _world(), "zigzag", True, "fused", 4096, 4, 2, 4, backend="nccl",
+    run_ranks(_case, _world(), "zigzag", True, "fused_stepwise", 4096, 4, 2, 4, backend="nccl",
               env={"MGFA_CUMULATIVE_ARRIVALS": "1"})
 
 
-def test_ring_forward_scheduler_layout_fused():
-    run_ranks(_case, _world(), "scheduler", True, "fused", 4096, 2, 2, 2, backend="nccl")
+@pytest.mark.parametrize("backend", ["fused", "fused_stepwise"])
+def test_ring_forward_scheduler_layout_fused(backend):
+    run_ranks(_case, _world(), "scheduler", True, backend, 4096, 2, 2, 2, backend="nccl")
+
+
+def test_ring_forward_one_launch_gqa_batch_and_many_calls():
+    """The one-launch ring with GQA (8 query heads on 2 kv heads), ragged
+    striped shards and six calls in a row (slots, arrivals, tags and the call
+    credit are reused every call)."""
+    run_ranks(_case, _world(), "striped", True, "fused", 5000, 8, 2, 6, backend="nccl")
 
 
 def _bwd_case(rank, world, kind, causal, bwd_backend="nccl", head_dim=128,
@@ -132,10 +144,10 @@ def _trace_case(rank, world):
     dev = torch.device("cuda", rank)
     lay = RingLayout("zigzag", 4096, world, mask="causal")
     q = (torch.randn(1, lay.max_local_len, 2, 128, device=dev) * 0.5).bfloat16()
-    ring_attention_forward(q, q, q, lay, causal=True, backend="fused", check=True)
+    ring_attention_forward(q, q, q, lay, causal=True, backend="fused_stepwise", check=True)
     eng = ENGINES.get(None, dev, q.numel() * 2)
     eng.set_trace(True)
-    ring_attention_forward(q, q, q, lay, causal=True, backend="fused", check=True)
+    ring_attention_forward(q, q, q, lay, causal=True, backend="fused_stepwise", check=True)
     eng.set_trace(False)
     tr = eng.last_trace()
     assert tr.shape[0] == world and tr.shape[2] == 8
@@ -152,30 +164,57 @@ def test_ring_forward_trace_records_timeline():
     run_ranks(_trace_case, _world(), backend="nccl")
 
 
-def _poison_case(rank, world):
+def _trace_case_one_launch(rank, world):
+    from multi_gpu_flashattention_b200.parallel.layouts import RingLayout
+    from multi_gpu_flashattention_b200.parallel.ring import P_ENGINES, ring_attention_forward
+    dev = torch.device("cuda", rank)
+    lay = RingLayout("zigzag", 8192, world, mask="causal")
+    q = (torch.randn(1, lay.max_local_len, 4, 128, device=dev) * 0.5).bfloat16()
+    ring_attention_forward(q, q, q, lay, causal=True, backend="fused", check=True)
+    eng = P_ENGINES.get(None, dev, q.numel() * 2)
+    eng.set_trace(True)
+    ring_attention_forward(q, q, q, lay, causal=True, backend="fused", check=True)
+    eng.set_trace(False)
+    tr = eng.last_trace().cpu()
+    assert tr.shape == (eng.grid(), 8)
+    assert (tr[:, 2] >= tr[:, 1]).all() and (tr[:, 1] > 0).all()
+    assert int(tr[:, 3].sum()) == 4 * ((lay.max_local_len + 255) // 256), "every item ran once"
+    pushed = tr[:, 6] > 0
+    assert pushed.sum() >= min(eng.grid(), 128), "push warps record their push window"
+    assert (tr[pushed, 7] >= tr[pushed, 6]).all()
+
+
+def test_ring_forward_one_launch_trace():
+    run_ranks(_trace_case_one_launch, _world(), backend="nccl")
+
+
+def _poison_case(rank, world, backend):
     """NaN-poisoned receive slots must never leak into the output (no read races
     ahead of its data), and every slot carries the right owner tag."""
     from multi_gpu_flashattention_b200.parallel.layouts import RingLayout
-    from multi_gpu_flashattention_b200.parallel.ring import ENGINES, ring_attention_forward
+    from multi_gpu_flashattention_b200.parallel.ring import (ENGINES, P_ENGINES,
+                                                             ring_attention_forward)
     dev = torch.device("cuda", rank)
     lay = RingLayout("zigzag", 8192, world, mask="causal")
     g = torch.Generator(device=dev).manual_seed(rank)
     q = (torch.randn(1, lay.max_local_len, 4, 128, device=dev, generator=g) * 0.5).bfloat16()
-    ref, _ = ring_attention_forward(q, q, q, lay, causal=True, backend="fused", check=True)
-    eng = ENGINES.get(None, dev, q.numel() * 2)
+    ref, _ = ring_attention_forward(q, q, q, lay, causal=True, backend=backend, check=True)
+    engines = P_ENGINES if backend == "fused" else ENGINES
+    eng = engines.get(None, dev, q.numel() * 2)
     for _ in range(3):
         torch.cuda.synchronize()
         torch.distributed.barrier()
         eng.poison_slots()
         torch.cuda.synchronize()
         torch.distributed.barrier()
-        out, _ = ring_attention_forward(q, q, q, lay, causal=True, backend="fused", check=True)
+        out, _ = ring_attention_forward(q, q, q, lay, causal=True, backend=backend, check=True)
         assert torch.isfinite(out.float()).all()
         torch.testing.assert_close(out, ref, rtol=0, atol=0)
 
 
-def test_ring_forward_poisoned_slots_and_tags():
-    run_ranks(_poison_case, _world(), backend="nccl")
+@pytest.mark.parametrize("ring_backend", ["fused", "fused_stepwise"])
+def test_ring_forward_poisoned_slots_and_tags(ring_backend):
+    run_ranks(_poison_case, _world(), ring_backend, backend="nccl")
 
 
 def _oneshot_case(rank, world, attention, backend, out_dir):
