@@ -5,7 +5,7 @@
 //
 //   torchrun --nproc-per-node N --no-python build/bin/ring_attention_bench
 //       <kv_size_bytes> [warmup=10] [iters=100]
-//       [--backend fused|p2p_unfused|ce_unfused|nccl|staged|p2p|ce]
+//       [--backend fused|fused_stepwise|p2p_unfused|ce_unfused|nccl|staged|p2p|ce]
 //       [--numerics fp32|bf16] [--init legacy|randn] [--layout contiguous|zigzag|
 //       striped|scheduler] [--policy dp|lpt] [--causal] [--heads H] [--kv-heads H]
 //       [--head-dim D] [--seed S] [--overlap] [--json]
@@ -19,11 +19,15 @@
 //     copy engine; sequential order). --init legacy
 //     reproduces the reference's inputs (K == V, no softmax scale) so
 //     `verify_full <dir> N kv_size` checks the dumps.
-//   --numerics bf16 (head_dim 64 or 128): the sm_100a kernels; fused (transport
-//     inside the attention kernel), p2p_unfused (the same NVLink push transport as
-//     a separate kernel on a second stream), ce_unfused (the copy engine moves the
-//     shard on a second stream), nccl (attention kernel per step + NCCL
-//     send/recv on a second stream) or staged (device -> host -> store -> device).
+//   --numerics bf16 (head_dim 64 or 128): the sm_100a kernels; fused (the whole
+//     ring in one launch of the persistent kernel, transport inside it),
+//     fused_stepwise (one attention launch per step with the transport inside
+//     it), p2p_unfused (the same NVLink push transport as a separate kernel on a
+//     second stream), ce_unfused (the copy engine moves the shard on a second
+//     stream), nccl (attention kernel per step + NCCL send/recv on a second
+//     stream) or staged (device -> host -> store -> device). The bf16 total is
+//     the ring on the device; the output's download into pinned memory is
+//     avg_final.
 // Environment as in the reference: ATTENTION_PRINT_SHARDS=1 prints token ranges
 // and per-step owners of iteration 0; ATTENTION_DUMP_OUTPUT=1 writes
 // ring_output_rank<r>.bin (raw little-endian fp32 [tokens x heads x dim]).
@@ -49,6 +53,7 @@
 #include <vector>
 
 #include "../comm/ring_engine.hpp"
+#include "../comm/ring_engine_p.hpp"
 #include "../comm/ring_exchange.hpp"
 #include "../common/synth.hpp"
 #include "../sched/shard_plan.hpp"
@@ -121,7 +126,8 @@ bool parse(int argc, char** argv, Args* a) {
   }
   if (a->backend.empty()) a->backend = a->numerics == "bf16" ? "fused" : "nccl";
   return (a->numerics == "fp32" || a->numerics == "bf16") &&
-         (a->backend == "fused" || a->backend == "p2p_unfused" || a->backend == "ce_unfused" ||
+         (a->backend == "fused" || a->backend == "fused_stepwise" ||
+          a->backend == "p2p_unfused" || a->backend == "ce_unfused" ||
           a->backend == "nccl" || a->backend == "staged" || a->backend == "p2p" ||
           a->backend == "ce") &&
          (a->init == "legacy" || a->init == "randn");
@@ -533,7 +539,16 @@ class Bf16Ring {
       kv_lens_.push_back(m.plan.local_len(o));
     }
     kvtp_ = i32_dev(all, dev).view({P, -1});
-    if (a.backend == "fused" || a.backend == "p2p_unfused" || a.backend == "ce_unfused") {
+    if (a.backend == "fused") {
+      // the one-launch ring: a receive slot per step, one kernel per forward
+      int64_t cap = std::max<int64_t>(k.numel() * k.element_size(), 1 << 20);
+      cap = (cap + (2 << 20) - 1) / (2 << 20) * (2 << 20);
+      peng_ = std::make_unique<mgfa::RingEngineP>(r, P, dev, cap);
+      peng_->connect(d.all_gather(peng_->ipc_handle()));
+      cudaDeviceSynchronize();
+      d.barrier();
+    } else if (a.backend == "fused_stepwise" || a.backend == "p2p_unfused" ||
+               a.backend == "ce_unfused") {
       const int64_t shard = k.numel() * k.element_size();
       int64_t slot = std::max<int64_t>(shard, 1 << 20);
       slot = (slot + (2 << 20) - 1) / (2 << 20) * (2 << 20);
@@ -544,9 +559,9 @@ class Bf16Ring {
       const char* ca = std::getenv("MGFA_CUMULATIVE_ARRIVALS");
       eng_->set_cumulative_arrivals(ca && std::string(ca) == "1");
       eng_->connect(d.all_gather(eng_->ipc_handle()));
-      eng_->set_transport_mode(a.backend == "fused"         ? mgfa::RingEngine::kFusedPush
-                               : a.backend == "p2p_unfused" ? mgfa::RingEngine::kPushKernel
-                                                            : mgfa::RingEngine::kCopyEngine);
+      eng_->set_transport_mode(a.backend == "fused_stepwise" ? mgfa::RingEngine::kFusedPush
+                               : a.backend == "p2p_unfused"  ? mgfa::RingEngine::kPushKernel
+                                                             : mgfa::RingEngine::kCopyEngine);
       cudaDeviceSynchronize();
       d.barrier();
     } else {
@@ -591,12 +606,16 @@ class Bf16Ring {
     // The compute-only reference (same launches, transport off) runs right
     // before and right after the ring, and the two are averaged, so clock drift
     // under the power cap does not land on one side of the comparison.
-    const bool ref = eng_ && P > 1;
+    const bool ref = (eng_ || peng_) && P > 1;
     auto compute_only = [&]() {
       Ev c0, c1;
       c0.record(cs);
-      eng_->forward_compute_only(q_, k_, v_, scale_, a_.causal, opt(qtp_), opt(kvtp_), kv_lens_,
-                                 status_);
+      if (peng_)
+        peng_->forward_compute_only(q_, k_, v_, scale_, a_.causal, opt(qtp_), opt(kvtp_),
+                                    kv_lens_, status_);
+      else
+        eng_->forward_compute_only(q_, k_, v_, scale_, a_.causal, opt(qtp_), opt(kvtp_),
+                                   kv_lens_, status_);
       c1.record(cs);
       return double(elapsed(c0, c1));
     };
@@ -605,10 +624,16 @@ class Bf16Ring {
     e0.record(cs);
     torch::Tensor out = forward();
     e1.record(cs);
-    st.host = out[0].to(torch::kFloat32).cpu();
+    // The output is already normalised on the device; its download into pinned
+    // memory is timed on its own (avg_final), outside the ring's total.
+    if (!host_out_.defined() || host_out_.sizes() != out[0].sizes())
+      host_out_ = torch::empty(out[0].sizes(),
+                               out.options().device(torch::kCPU).pinned_memory(true));
+    host_out_.copy_(out[0], /*non_blocking=*/true);
     e2.record(cs);
     cudaDeviceSynchronize();
-    st.total = elapsed(e0, e2);
+    st.host = host_out_.to(torch::kFloat32);
+    st.total = elapsed(e0, e1);
     st.attn = elapsed(e0, e1);
     st.final = elapsed(e1, e2);
     if (ref) {
@@ -625,6 +650,9 @@ class Bf16Ring {
   }
 
   torch::Tensor forward() {
+    if (peng_)
+      return peng_->forward(q_, k_, v_, scale_, a_.causal, opt(qtp_), opt(kvtp_), kv_lens_,
+                            status_, kWaitNs)[0];
     if (eng_)
       return eng_->forward(q_, k_, v_, scale_, a_.causal, opt(qtp_), opt(kvtp_), kv_lens_,
                            status_, kWaitNs)[0];
@@ -687,6 +715,8 @@ class Bf16Ring {
   torch::Tensor status_, qtp_, kvtp_;
   std::vector<int64_t> kv_lens_;
   std::unique_ptr<mgfa::RingEngine> eng_;
+  std::unique_ptr<mgfa::RingEngineP> peng_;
+  torch::Tensor host_out_;    // pinned download target of the output
   torch::Tensor recv_[2][2];  // two receive pairs (K, V)
   void* h_send_[2] = {nullptr, nullptr};
   void* h_recv_[2] = {nullptr, nullptr};
@@ -728,7 +758,7 @@ static int run_main(int argc, char** argv) {
   Args a;
   if (!parse(argc, argv, &a)) {
     std::printf("Usage: ring_attention_bench <kv_size_bytes> [warmup] [iters] "
-                "[--backend fused|p2p_unfused|ce_unfused|nccl|staged|p2p|ce] [--numerics fp32|bf16] "
+                "[--backend fused|fused_stepwise|p2p_unfused|ce_unfused|nccl|staged|p2p|ce] [--numerics fp32|bf16] "
                 "[--init legacy|randn] "
                 "[--layout contiguous|zigzag|striped|scheduler] [--policy dp|lpt] [--causal] "
                 "[--heads H] [--kv-heads H] [--head-dim D] [--seed S] [--overlap] [--json]\n");
