@@ -193,6 +193,26 @@ __device__ __forceinline__ void exp_half(const uint32_t (&sr)[128], int half, fl
   }
 }
 
+// Phase profile of the kernel variant with bit 10 of the tune word set: per CTA
+// kProfWords clock64 sums, written to PFwdParams::trace ([grid][kProfWords]).
+// Softmax (lane 0 of warps 0 and 4, summed): [0] waiting for S, [1] TMEM load
+// of S, [2] row max, [3] first half of P (exponentials, store, hand-over),
+// [4] second half of P, [5] tiles; MMA thread: [6] waiting for V, [7] for
+// P half 0 of tile 0, [8] for P half 1 of tile 0, [9] for K of the next tile,
+// [10] for P half 0 of tile 1, [11] for P half 1 of tile 1, [12] tiles,
+// [13] cycles of the MMA thread's whole loop.
+constexpr int kProfWords = 16;
+
+struct Prof {
+  unsigned long long acc[kProfWords];
+};
+
+__device__ __forceinline__ unsigned long long clk() {
+  unsigned long long c;
+  asm volatile("mov.u64 %0, %%clock64;" : "=l"(c));
+  return c;
+}
+
 struct Item {
   int b, h, hk, qt0;
 };
@@ -316,7 +336,8 @@ __device__ void push_units(const PFwdParams& p, int pw, int n_pw, volatile uint3
 }
 
 // ------------------------------------------------------------------ kernel
-// kVar: bit 0 packed f32x2 softmax arithmetic, bit 1 P handed over in two halves.
+// kVar: bit 0 packed f32x2 softmax arithmetic, bit 1 P handed over in two halves,
+// bit 2 phase profile (see Prof), bit 3 row max as a shallow tree.
 template <int kD, bool kF16, int kPoly8, bool kRing, int kVar>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_persistent_kernel(const __grid_constant__ CUtensorMap map_q,
@@ -331,6 +352,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t kOCol = 256;
   constexpr bool kPacked = (kVar & 1) != 0;
   constexpr bool kSplit = (kVar & 2) != 0;
+  constexpr bool kProfile = (kVar & 4) != 0;
+  constexpr bool kTreeMax = (kVar & 8) != 0;
+  unsigned long long pa[kProfWords];
+#pragma unroll
+  for (int i = 0; i < kProfWords; ++i) pa[i] = 0;
+  [[maybe_unused]] unsigned long long c0 = 0, c1 = 0;
   extern __shared__ uint8_t smem_raw[];
   PSmem<kD>& s = *reinterpret_cast<PSmem<kD>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -505,6 +532,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t it = 0;
     int n = 0;
     bool ok = true;
+    [[maybe_unused]] const unsigned long long mma_t0 = kProfile ? clk() : 0ull;
     while (true) {
       const int slot = n & 1;
       int item = kNoItem;
@@ -544,26 +572,37 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int st1 = int((g + 1) & 1);
             const uint32_t ph1 = ((g + 1) >> 1) & 1;
             const bool more = j + 1 < T;
+            if constexpr (kProfile) c0 = clk();
             if (!(ok = mbar_wait(&s.v_full[st], ph, ab, 93))) break;
+            if constexpr (kProfile) { c1 = clk(); pa[6] += c1 - c0; c0 = c1; }
             if (j == 0 && !(ok = mbar_wait(&s.o_empty[0], (n & 1) ^ 1, ab, 94))) break;
             if (!(ok = mbar_wait(&s.p_full[0][0], pp, ab, 95))) break;
+            if constexpr (kProfile) { c1 = clk(); pa[7] += c1 - c0; }
             tc_fence_after();
             issue_o(0, st, 0, j > 0);
+            if constexpr (kProfile) c0 = clk();
             if (!(ok = mbar_wait(&s.p_full[0][1], pp, ab, 96))) break;
+            if constexpr (kProfile) { c1 = clk(); pa[8] += c1 - c0; }
             tc_fence_after();
             issue_o(0, st, 1, true);
             if (!more) mma_commit(&s.o_full[0]);
             if (more) {
+              if constexpr (kProfile) c0 = clk();
               if (!(ok = mbar_wait(&s.k_full[st1], ph1, ab, 97))) break;
+              if constexpr (kProfile) { c1 = clk(); pa[9] += c1 - c0; }
               tc_fence_after();
               issue_s(0, st1);
               mma_commit(&s.s_full[0]);
             }
             if (j == 0 && !(ok = mbar_wait(&s.o_empty[1], (n & 1) ^ 1, ab, 98))) break;
+            if constexpr (kProfile) c0 = clk();
             if (!(ok = mbar_wait(&s.p_full[1][0], pp, ab, 99))) break;
+            if constexpr (kProfile) { c1 = clk(); pa[10] += c1 - c0; }
             tc_fence_after();
             issue_o(1, st, 0, j > 0);
+            if constexpr (kProfile) c0 = clk();
             if (!(ok = mbar_wait(&s.p_full[1][1], pp, ab, 100))) break;
+            if constexpr (kProfile) { c1 = clk(); pa[11] += c1 - c0; pa[12] += 1; }
             tc_fence_after();
             issue_o(1, st, 1, true);
             mma_commit(&s.v_empty[st]);
@@ -583,6 +622,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++n;
       if (!ok) break;
     }
+    if constexpr (kProfile) pa[13] = clk() - mma_t0;
     if (lane == 0) {
       // Drain: every issued MMA has finished before TMEM is released.
       mma_commit(&s.drain);
@@ -636,8 +676,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!q_valid) full_hi = 0;
         for (int j = 0; j < n_act; ++j, ++g) {
+          if constexpr (kProfile) c0 = clk();
           ok = __all_sync(0xffffffffu, mbar_wait(&s.s_full[t], g & 1, ab, 22 + t));
           if (!ok) break;
+          if constexpr (kProfile) { c1 = clk(); pa[0] += c1 - c0; c0 = c1; pa[5] += 1; }
           tc_fence_after();
           uint32_t sr[128];
           tmem_ld32(s_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
@@ -655,21 +697,38 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!q_valid) n_vis = 0;
           }
           tmem_wait_ld();
+          if constexpr (kProfile) { c1 = clk(); pa[1] += c1 - c0; c0 = c1; }
           if (!full) {
 #pragma unroll
             for (int c = 0; c < 128; ++c)
               if (c >= n_vis) sr[c] = 0xff800000u;  // -inf
           }
-          float mx0 = __uint_as_float(sr[0]), mx1 = __uint_as_float(sr[1]);
-          float mx2 = __uint_as_float(sr[2]), mx3 = __uint_as_float(sr[3]);
+          float tmax;
+          if constexpr (kTreeMax) {
+            // 16 independent chains of 8 scores, then a 3-level tree: the
+            // dependent depth is 7 instead of 16
+            float g[16];
 #pragma unroll
-          for (int c = 4; c < 128; c += 8) {
-            mx0 = max3f(mx0, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
-            mx1 = max3f(mx1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
-            mx2 = max3f(mx2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
-            mx3 = max3f(mx3, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
+            for (int i = 0; i < 16; ++i) {
+              const float* f = reinterpret_cast<const float*>(sr) + 8 * i;
+              g[i] = fmaxf(max3f(max3f(max3f(f[0], f[1], f[2]), f[3], f[4]), f[5], f[6]), f[7]);
+            }
+            const float h0 = max3f(g[0], g[1], g[2]), h1 = max3f(g[3], g[4], g[5]);
+            const float h2 = max3f(g[6], g[7], g[8]), h3 = max3f(g[9], g[10], g[11]);
+            const float h4 = max3f(g[12], g[13], g[14]);
+            tmax = max3f(max3f(h0, h1, h2), max3f(h3, h4, g[15]), h0) * p.scale_log2;
+          } else {
+            float mx0 = __uint_as_float(sr[0]), mx1 = __uint_as_float(sr[1]);
+            float mx2 = __uint_as_float(sr[2]), mx3 = __uint_as_float(sr[3]);
+#pragma unroll
+            for (int c = 4; c < 128; c += 8) {
+              mx0 = max3f(mx0, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+              mx1 = max3f(mx1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
+              mx2 = max3f(mx2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
+              mx3 = max3f(mx3, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
+            }
+            tmax = fmaxf(max3f(mx0, mx1, mx2), mx3) * p.scale_log2;
           }
-          const float tmax = fmaxf(max3f(mx0, mx1, mx2), mx3) * p.scale_log2;
           const float m_new = fmaxf(m, tmax);
           float alpha = 1.f;
           bool rescale = false;
@@ -689,6 +748,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // tensor core while the second is computed; with one, O is rescaled
           // once the scores are no longer needed (register pressure) and both
           // halves are released together.
+          if constexpr (kProfile) { c1 = clk(); pa[2] += c1 - c0; c0 = c1; }
           const bool resc = __any_sync(0xffffffffu, rescale);
           const bool early = kSplit && !resc;
           uint32_t pk0[32], pk1[32];
@@ -700,6 +760,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_before();
             mbar_arrive(&s.p_full[t][0]);
           }
+          if constexpr (kProfile) { c1 = clk(); pa[3] += c1 - c0; c0 = c1; }
           if (full) exp_half<kF16, kPoly8, kPacked>(sr, 1, p.scale_log2, -m_use, pk1, lacc);
           else exp_half<kF16, 0, kPacked>(sr, 1, p.scale_log2, -m_use, pk1, lacc);
           if (resc) {
@@ -720,6 +781,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_before();
           if (!early) mbar_arrive(&s.p_full[t][0]);
           mbar_arrive(&s.p_full[t][1]);
+          if constexpr (kProfile) { c1 = clk(); pa[4] += c1 - c0; }
           l = l * alpha + ((lacc[0] + lacc[1]) + (lacc[2] + lacc[3]));
         }
       }
@@ -771,6 +833,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   // ---- teardown
+  if constexpr (kProfile) {
+    // softmax lane 0 of warps 0 and 4 and the MMA thread add their sums
+    if (p.trace && lane == 0 && (warp == 0 || warp == 4 || warp == 9)) {
+      unsigned long long* dst =
+          reinterpret_cast<unsigned long long*>(p.trace) + uint64_t(blockIdx.x) * kProfWords;
+      for (int i = 0; i < kProfWords; ++i)
+        if (pa[i]) atomicAdd(dst + i, pa[i]);
+    }
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc<512>(tmem);
@@ -781,7 +852,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tr[7] = tr_push1;
     }
   }
-  if (warp == 8 && lane == 0 && p.trace) {
+  if (warp == 8 && lane == 0 && p.trace && !kProfile) {
     uint64_t* tr = p.trace + uint64_t(blockIdx.x) * kPTraceWords;
     tr[0] = (uint64_t(sm_id()) << 32) | blockIdx.x;
     tr[1] = tr_start;
@@ -839,6 +910,10 @@ KernelFn pick_var(int var) {
     case 0: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 0>;
     case 1: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 1>;
     case 2: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 2>;
+    case 4: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 4>;
+    case 7: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 7>;
+    case 11: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 11>;
+    case 15: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 15>;
     default: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 3>;
   }
 }
@@ -875,7 +950,7 @@ void attn_fwd_persistent_launch(const CUtensorMap& mq, const CUtensorMap& mk,
   MGFA_CHECK(p.sched != nullptr, "the persistent forward needs its work counters");
   MGFA_CHECK(!p.ring.enabled || p.batch * p.hkv <= kPMaxChunks, "too many kv-head chunks");
   const bool ring = p.ring.enabled != 0;
-  const int var = tune < 0 ? kDefaultVar : (tune >> 8) & 3;
+  const int var = tune < 0 ? kDefaultVar : (tune >> 8) & 15;
   const int poly8 = tune < 0 ? -1 : tune & 0xff;
   const KernelFn fn =
       head_dim == 64 ? pick<64>(fp16, ring, poly8, var) : pick<128>(fp16, ring, poly8, var);

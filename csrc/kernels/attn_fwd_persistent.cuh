@@ -84,8 +84,10 @@ struct PFwdParams {
 // the head_dim 128 bf16 kernel without the ring (every other kernel uses the
 // default): bits 0-7 how many of every 8 exponential pairs run as a polynomial
 // on the FMA pipe instead of MUFU.EX2 (0, 2 or 4), bits 8-9 the arithmetic
-// (bit 8: packed f32x2) and the P hand-over (bit 9: two halves); negative
-// means the default.
+// (bit 8: packed f32x2) and the P hand-over (bit 9: two halves); bit 10 selects
+// a variant that sums per-phase clock counts into `trace` ([grid][16] int64,
+// layout in attn_fwd_persistent.cu), bit 11 computes the row max as a shallow
+// tree; negative means the default.
 void attn_fwd_persistent_launch(const CUtensorMap& mq, const CUtensorMap& mk,
                                 const CUtensorMap& mv, const CUtensorMap& mslots, int head_dim,
                                 bool fp16, PFwdParams& p, int grid, int tune,

@@ -328,7 +328,8 @@ void flash_fwd_persistent(torch::Tensor q, torch::Tensor k, torch::Tensor v, tor
                           c10::optional<torch::Tensor> q_tile_pos,
                           c10::optional<torch::Tensor> kv_tile_pos, torch::Tensor status,
                           int64_t wait_limit_ns, torch::Tensor sched, int64_t tune,
-                          int64_t grid, std::vector<int64_t> seg_lens) {
+                          int64_t grid, std::vector<int64_t> seg_lens,
+                          c10::optional<torch::Tensor> trace) {
   check_bshd(q, "q");
   check_bshd(k, "k");
   check_bshd(v, "v");
@@ -383,6 +384,11 @@ void flash_fwd_persistent(torch::Tensor q, torch::Tensor k, torch::Tensor v, tor
   p.status = reinterpret_cast<uint32_t*>(status.data_ptr<int>());
   p.wait_limit_ns = uint64_t(wait_limit_ns);
   p.sched = reinterpret_cast<uint32_t*>(sched.data_ptr<int>());
+  if (trace.has_value()) {
+    MGFA_CHECK(trace->is_cuda() && trace->scalar_type() == at::kLong && trace->is_contiguous(),
+               "trace must be a contiguous int64 CUDA tensor");
+    p.trace = reinterpret_cast<uint64_t*>(trace->data_ptr<int64_t>());
+  }
   auto map = [&](const torch::Tensor& t) {
     return make_bshd_map_dt(t.data_ptr(), t.size(0), t.size(1), t.size(2), t.stride(0),
                             t.stride(1), t.stride(2), D, f16);

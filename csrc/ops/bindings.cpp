@@ -13,7 +13,8 @@ void flash_fwd_persistent(torch::Tensor q, torch::Tensor k, torch::Tensor v, tor
                           c10::optional<torch::Tensor> q_tile_pos,
                           c10::optional<torch::Tensor> kv_tile_pos, torch::Tensor status,
                           int64_t wait_limit_ns, torch::Tensor sched, int64_t tune,
-                          int64_t grid, std::vector<int64_t> seg_lens);
+                          int64_t grid, std::vector<int64_t> seg_lens,
+                          c10::optional<torch::Tensor> trace);
 void legacy_partial(torch::Tensor q, torch::Tensor k, torch::Tensor v, double scale,
                     c10::optional<torch::Tensor> q_pos, c10::optional<torch::Tensor> k_pos,
                     bool causal, torch::Tensor acc, torch::Tensor m, torch::Tensor l, bool merge);
@@ -21,7 +22,6 @@ void legacy_merge(torch::Tensor m_run, torch::Tensor l_run, torch::Tensor acc_ru
                   torch::Tensor m_new, torch::Tensor l_new, torch::Tensor acc_new);
 void legacy_normalize(torch::Tensor acc, torch::Tensor l, torch::Tensor out,
                       c10::optional<torch::Tensor> lse, c10::optional<torch::Tensor> m);
-void red_probe(torch::Tensor dq, int64_t n_kv_tiles, bool causal);
 void register_ring_engine(py::module& m);
 void register_ring_engine_p(py::module& m);
 void register_ring_exchange(py::module& m);
@@ -50,9 +50,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("v"), py::arg("o"), py::arg("lse"), py::arg("scale"), py::arg("causal"),
         py::arg("q_tile_pos"), py::arg("kv_tile_pos"), py::arg("status"),
         py::arg("wait_limit_ns"), py::arg("sched"), py::arg("tune") = int64_t(-1),
-        py::arg("grid") = int64_t(0), py::arg("seg_lens") = std::vector<int64_t>());
-  m.def("red_probe", &mgfa::red_probe, py::arg("dq"), py::arg("n_kv_tiles"),
-        py::arg("causal"));
+        py::arg("grid") = int64_t(0), py::arg("seg_lens") = std::vector<int64_t>(),
+        py::arg("trace") = py::none());
   m.def("debug_build", []() {
 #ifdef MGFA_DEBUG
     return true;

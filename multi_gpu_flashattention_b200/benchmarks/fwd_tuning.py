@@ -8,7 +8,9 @@ the persistent kernel (attn_fwd_persistent.cu) in each of its softmax variants.
 A tune value is the persistent kernel's variant word (attn_fwd_persistent.cuh):
 bits 0-7 exponential pairs of every 8 on the FMA pipe (0, 2 or 4), bit 8 packed
 f32x2 arithmetic, bit 9 P handed over in two halves. Prints one JSON line per
-variant with the median time and attention TFLOP/s."""
+variant with the median time and attention TFLOP/s. --profile T runs variant T
+with its phase counters (bit 10) once and prints the mean clock cycles per key
+tile of each softmax and MMA-thread phase."""
 from __future__ import annotations
 
 import argparse
@@ -31,6 +33,8 @@ def main(argv=None):
     ap.add_argument("--no-causal", action="store_true")
     ap.add_argument("--reps", type=int, default=5)
     ap.add_argument("--tunes", default=DEFAULT_TUNES)
+    ap.add_argument("--profile", default=None,
+                    help="comma-separated tune values to profile by phase instead")
     a = ap.parse_args(argv)
     causal = not a.no_causal
     S, H, Hkv, D = a.seq, a.heads, a.kv_heads, 128
@@ -55,6 +59,33 @@ def main(argv=None):
     def persistent(tune):
         return lambda: C().flash_fwd_persistent(q, k, v, o, lse, scale, causal, pos, pos, st,
                                                 2_000_000_000, sched, tune)
+
+    if a.profile:
+        names = ["wait_S", "ld_S", "max", "P_half0", "P_half1", "tiles", "mma_wait_V",
+                 "mma_wait_P0h0", "mma_wait_P0h1", "mma_wait_K", "mma_wait_P1h0",
+                 "mma_wait_P1h1", "mma_tiles", "mma_loop"]
+        for t in a.profile.split(","):
+            tv = int(t, 0) | 0x400
+            tr = torch.zeros(512, 16, dtype=torch.int64, device="cuda")
+            persistent(tv)()  # warm-up
+            tr.zero_()
+            flush.fill_(1)
+            C().flash_fwd_persistent(q, k, v, o, lse, scale, causal, pos, pos, st,
+                                     2_000_000_000, sched, tv, 0, [], tr)
+            torch.cuda.synchronize()
+            tot = tr.sum(0).double().tolist()
+            rec = {"tune": hex(tv), "seq": S}
+            for i, nm in enumerate(names):
+                if nm in ("tiles", "mma_tiles"):
+                    rec[nm] = int(tot[i])
+                elif nm == "mma_loop":
+                    rec["mma_loop_cycles_per_tile"] = round(tot[i] / max(tot[12], 1), 1)
+                elif nm.startswith("mma"):
+                    rec[nm] = round(tot[i] / max(tot[12], 1), 1)
+                else:
+                    rec[nm] = round(tot[i] / max(tot[5], 1), 1)
+            print(json.dumps(rec), flush=True)
+        return 0
 
     cases = [("stepwise", None, stepwise)]
     for t in a.tunes.split(","):

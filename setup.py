@@ -64,7 +64,6 @@ if which in ("all", "cuda"):
                 "csrc/comm/ring_exchange.cpp",
                 "csrc/comm/ring_bwd_engine.cpp",
                 "csrc/kernels/ring_exchange.cu",
-                "csrc/kernels/red_probe.cu",
             ],
             include_dirs=[os.path.join(ROOT, "csrc")],
             extra_compile_args={

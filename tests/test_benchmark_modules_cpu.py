@@ -8,7 +8,7 @@ import sys
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-MODULES = ["profile_kernels", "reduction_probe", "ring_trace", "ring_train",
+MODULES = ["profile_kernels", "ring_trace", "ring_train",
            "single_gpu_baseline", "single_gpu_shapes", "ring_attention", "ring_loop",
            "ring_oneshot", "layout_balance", "check_peer", "probes", "reference_programs",
            "fwd_tuning"]
