@@ -131,19 +131,29 @@ __device__ __forceinline__ float exp2_fma1(float x) {
   return __uint_as_float(__float_as_uint(pv) + (__float_as_uint(t) << 23));
 }
 
-// Probabilities of one 64-key half of a row: p = 2^(s * scale - m), summed into
-// the row-sum accumulators and packed to 16-bit pairs for the PV MMA. kPacked
-// uses the f32x2 instructions (two lanes of work per instruction); kPoly8 of
-// every 8 pairs go through the FMA-pipe polynomial instead of MUFU.EX2.
-template <bool kF16, int kPoly8, bool kPacked>
-__device__ __forceinline__ void exp_half(const uint32_t (&sr)[128], int half, float scale,
-                                         float neg_m, uint32_t (&pk)[32], float (&lacc)[4]) {
+// Probabilities of pairs [c0, c0 + kN) of a row (pair c = keys 2c, 2c+1):
+// p = 2^(s * scale - m), summed into the row-sum accumulators and packed to
+// 16-bit pairs (pk[c - c0]) for the PV MMA. kPacked uses the f32x2
+// instructions (two lanes of work per instruction); kPoly8 of every 8 pairs go
+// through the FMA-pipe polynomial instead of MUFU.EX2. With kMax the loop also
+// folds 128 / (2 kN) * 2 further raw scores per pair into `mx` (four running
+// maxima), so the row max of all 128 scores is computed alongside.
+template <bool kF16, int kPoly8, bool kPacked, int kN, bool kMax = false>
+__device__ __forceinline__ void exp_pairs(const uint32_t (&sr)[128], int c0, float scale,
+                                          float neg_m, uint32_t* pk, float (&lacc)[4],
+                                          float (&mx)[4]) {
+  constexpr int kPer = 128 / kN;  // raw scores folded into the max per pair step
   if constexpr (kPacked) {
     const uint64_t sc2 = f2_pack(scale, scale), nm2 = f2_pack(neg_m, neg_m);
     uint64_t acc0 = f2_pack(0.f, 0.f), acc1 = f2_pack(0.f, 0.f);
 #pragma unroll
-    for (int cc = 0; cc < 32; ++cc) {
-      const int c = half * 32 + cc;
+    for (int cc = 0; cc < kN; ++cc) {
+      const int c = c0 + cc;
+      if constexpr (kMax) {
+        const float* f = reinterpret_cast<const float*>(sr) + kPer * cc;
+#pragma unroll
+        for (int u = 0; u < kPer; u += 2) mx[(u >> 1) & 3] = max3f(mx[(u >> 1) & 3], f[u], f[u + 1]);
+      }
       const uint64_t x2 = f2_fma(
           f2_pack(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), sc2, nm2);
       uint64_t e2;
@@ -169,8 +179,13 @@ __device__ __forceinline__ void exp_half(const uint32_t (&sr)[128], int half, fl
     lacc[3] += b1;
   } else {
 #pragma unroll
-    for (int cc = 0; cc < 32; ++cc) {
-      const int c = half * 32 + cc;
+    for (int cc = 0; cc < kN; ++cc) {
+      const int c = c0 + cc;
+      if constexpr (kMax) {
+        const float* f = reinterpret_cast<const float*>(sr) + kPer * cc;
+#pragma unroll
+        for (int u = 0; u < kPer; u += 2) mx[(u >> 1) & 3] = max3f(mx[(u >> 1) & 3], f[u], f[u + 1]);
+      }
       const float x0 = fmaf(__uint_as_float(sr[2 * c]), scale, neg_m);
       const float x1 = fmaf(__uint_as_float(sr[2 * c + 1]), scale, neg_m);
       float p0, p1;
@@ -191,6 +206,13 @@ __device__ __forceinline__ void exp_half(const uint32_t (&sr)[128], int half, fl
       pk[cc] = pack16<kF16>(p0, p1);
     }
   }
+}
+
+template <bool kF16, int kPoly8, bool kPacked>
+__device__ __forceinline__ void exp_half(const uint32_t (&sr)[128], int half, float scale,
+                                         float neg_m, uint32_t (&pk)[32], float (&lacc)[4]) {
+  float unused[4];
+  exp_pairs<kF16, kPoly8, kPacked, 32, false>(sr, half * 32, scale, neg_m, pk, lacc, unused);
 }
 
 // Phase profile of the kernel variant with bit 10 of the tune word set: per CTA
@@ -337,7 +359,11 @@ __device__ void push_units(const PFwdParams& p, int pw, int n_pw, volatile uint3
 
 // ------------------------------------------------------------------ kernel
 // kVar: bit 0 packed f32x2 softmax arithmetic, bit 1 P handed over in two halves,
-// bit 2 phase profile (see Prof), bit 3 row max as a shallow tree.
+// bit 2 phase profile (see Prof), bit 3 row max as a shallow tree, bit 4
+// speculative exponentials against the running max (the tile max is folded in
+// alongside and a tile whose max grew by more than 2^8 is redone), bit 5 the
+// wait for the first half's P store hidden behind the next quarter's
+// exponentials.
 template <int kD, bool kF16, int kPoly8, bool kRing, int kVar>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_persistent_kernel(const __grid_constant__ CUtensorMap map_q,
@@ -354,6 +380,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr bool kSplit = (kVar & 2) != 0;
   constexpr bool kProfile = (kVar & 4) != 0;
   constexpr bool kTreeMax = (kVar & 8) != 0;
+  constexpr bool kSpec = (kVar & 16) != 0;  // speculative exponentials (running max)
+  constexpr bool kLate = (kVar & 32) != 0;  // P-store wait behind the next quarter
   unsigned long long pa[kProfWords];
 #pragma unroll
   for (int i = 0; i < kProfWords; ++i) pa[i] = 0;
@@ -703,66 +731,120 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int c = 0; c < 128; ++c)
               if (c >= n_vis) sr[c] = 0xff800000u;  // -inf
           }
-          float tmax;
-          if constexpr (kTreeMax) {
-            // 16 independent chains of 8 scores, then a 3-level tree: the
-            // dependent depth is 7 instead of 16
-            float g[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const float* f = reinterpret_cast<const float*>(sr) + 8 * i;
-              g[i] = fmaxf(max3f(max3f(max3f(f[0], f[1], f[2]), f[3], f[4]), f[5], f[6]), f[7]);
-            }
-            const float h0 = max3f(g[0], g[1], g[2]), h1 = max3f(g[3], g[4], g[5]);
-            const float h2 = max3f(g[6], g[7], g[8]), h3 = max3f(g[9], g[10], g[11]);
-            const float h4 = max3f(g[12], g[13], g[14]);
-            tmax = max3f(max3f(h0, h1, h2), max3f(h3, h4, g[15]), h0) * p.scale_log2;
-          } else {
-            float mx0 = __uint_as_float(sr[0]), mx1 = __uint_as_float(sr[1]);
-            float mx2 = __uint_as_float(sr[2]), mx3 = __uint_as_float(sr[3]);
-#pragma unroll
-            for (int c = 4; c < 128; c += 8) {
-              mx0 = max3f(mx0, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
-              mx1 = max3f(mx1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
-              mx2 = max3f(mx2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
-              mx3 = max3f(mx3, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
-            }
-            tmax = fmaxf(max3f(mx0, mx1, mx2), mx3) * p.scale_log2;
-          }
-          const float m_new = fmaxf(m, tmax);
           float alpha = 1.f;
           bool rescale = false;
-          if (first) {
-            m = m_new;
-          } else if (m_new > m + kRescaleThreshold) {
-            alpha = ex2_approx(m - m_new);
-            m = m_new;
-            rescale = true;
+          float lacc[4] = {0.f, 0.f, 0.f, 0.f};
+          uint32_t pk0[32], pk1[32];
+          // Speculation: the first half's exponentials use the running max
+          // while the tile max is folded in alongside; a row whose max grew by
+          // more than 2^8 redoes the half (rare once a row's max has settled).
+          const bool spec =
+              kSpec && full && !first && __all_sync(0xffffffffu, m != -INFINITY);
+          if (spec) {
+            float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+            exp_pairs<kF16, kPoly8, kPacked, 32, true>(sr, 0, p.scale_log2, -m, pk0, lacc, mx);
+            const float tmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * p.scale_log2;
+            const bool redo = tmax > m + kRescaleThreshold;
+            if (__any_sync(0xffffffffu, redo)) {
+              // S of the first half is still in TMEM (P has not overwritten it):
+              // reload it a quarter at a time rather than keep it in registers
+              if (redo) {
+                alpha = ex2_approx(m - tmax);
+                m = tmax;
+                rescale = true;
+                lacc[0] = lacc[1] = lacc[2] = lacc[3] = 0.f;
+              }
+              const float nm = redo ? -m : 0.f;
+#pragma unroll
+              for (int qq = 0; qq < 2; ++qq) {
+                tmem_ld32(s_addr + qq * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[qq * 32]));
+                tmem_wait_ld();
+                if (redo) {
+                  uint32_t pq[16];
+                  float unused_mx[4];
+                  exp_pairs<kF16, kPoly8, kPacked, 16>(sr, qq * 16, p.scale_log2, nm, pq, lacc,
+                                                       unused_mx);
+#pragma unroll
+                  for (int i = 0; i < 16; ++i) pk0[qq * 16 + i] = pq[i];
+                }
+              }
+            }
+            if constexpr (kProfile) { c1 = clk(); pa[2] += c1 - c0; c0 = c1; }
+          } else {
+            float tmax;
+            if constexpr (kTreeMax) {
+              // 16 independent chains of 8 scores, then a 3-level tree: the
+              // dependent depth is 7 instead of 16
+              float gm[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const float* f = reinterpret_cast<const float*>(sr) + 8 * i;
+                gm[i] = fmaxf(max3f(max3f(max3f(f[0], f[1], f[2]), f[3], f[4]), f[5], f[6]), f[7]);
+              }
+              const float h0 = max3f(gm[0], gm[1], gm[2]), h1 = max3f(gm[3], gm[4], gm[5]);
+              const float h2 = max3f(gm[6], gm[7], gm[8]), h3 = max3f(gm[9], gm[10], gm[11]);
+              const float h4 = max3f(gm[12], gm[13], gm[14]);
+              tmax = max3f(max3f(h0, h1, h2), max3f(h3, h4, gm[15]), h0) * p.scale_log2;
+            } else {
+              float mx0 = __uint_as_float(sr[0]), mx1 = __uint_as_float(sr[1]);
+              float mx2 = __uint_as_float(sr[2]), mx3 = __uint_as_float(sr[3]);
+#pragma unroll
+              for (int c = 4; c < 128; c += 8) {
+                mx0 = max3f(mx0, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+                mx1 = max3f(mx1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
+                mx2 = max3f(mx2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
+                mx3 = max3f(mx3, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
+              }
+              tmax = fmaxf(max3f(mx0, mx1, mx2), mx3) * p.scale_log2;
+            }
+            const float m_new = fmaxf(m, tmax);
+            if (first) {
+              m = m_new;
+            } else if (m_new > m + kRescaleThreshold) {
+              alpha = ex2_approx(m - m_new);
+              m = m_new;
+              rescale = true;
+            }
+            if constexpr (kProfile) { c1 = clk(); pa[2] += c1 - c0; c0 = c1; }
+            const float m0 = (m == -INFINITY) ? 0.f : m;
+            if (full) exp_half<kF16, kPoly8, kPacked>(sr, 0, p.scale_log2, -m0, pk0, lacc);
+            else exp_half<kF16, 0, kPacked>(sr, 0, p.scale_log2, -m0, pk0, lacc);
           }
           first = false;
           const float m_use = (m == -INFINITY) ? 0.f : m;
-          float lacc[4] = {0.f, 0.f, 0.f, 0.f};
           // O already holds the previous tiles' PV (their MMAs completed before
           // this tile's S was committed) and must be rescaled before this tile's
           // PV starts. Rare: without a rescale the first half of P goes to the
           // tensor core while the second is computed; with one, O is rescaled
           // once the scores are no longer needed (register pressure) and both
           // halves are released together.
-          if constexpr (kProfile) { c1 = clk(); pa[2] += c1 - c0; c0 = c1; }
           const bool resc = __any_sync(0xffffffffu, rescale);
           const bool early = kSplit && !resc;
-          uint32_t pk0[32], pk1[32];
-          if (full) exp_half<kF16, kPoly8, kPacked>(sr, 0, p.scale_log2, -m_use, pk0, lacc);
-          else exp_half<kF16, 0, kPacked>(sr, 0, p.scale_log2, -m_use, pk0, lacc);
+          float unused[4];
           if (early) {
             tmem_st32(s_addr, pk0);
+            if constexpr (kLate) {
+              // the store's completion wait goes behind a quarter of the
+              // second half's exponentials
+              if (full)
+                exp_pairs<kF16, kPoly8, kPacked, 16>(sr, 32, p.scale_log2, -m_use, pk1, lacc, unused);
+              else
+                exp_pairs<kF16, 0, kPacked, 16>(sr, 32, p.scale_log2, -m_use, pk1, lacc, unused);
+            }
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(&s.p_full[t][0]);
           }
           if constexpr (kProfile) { c1 = clk(); pa[3] += c1 - c0; c0 = c1; }
-          if (full) exp_half<kF16, kPoly8, kPacked>(sr, 1, p.scale_log2, -m_use, pk1, lacc);
-          else exp_half<kF16, 0, kPacked>(sr, 1, p.scale_log2, -m_use, pk1, lacc);
+          if (kLate && early) {
+            if (full)
+              exp_pairs<kF16, kPoly8, kPacked, 16>(sr, 48, p.scale_log2, -m_use, pk1 + 16, lacc, unused);
+            else
+              exp_pairs<kF16, 0, kPacked, 16>(sr, 48, p.scale_log2, -m_use, pk1 + 16, lacc, unused);
+          } else {
+            if (full) exp_half<kF16, kPoly8, kPacked>(sr, 1, p.scale_log2, -m_use, pk1, lacc);
+            else exp_half<kF16, 0, kPacked>(sr, 1, p.scale_log2, -m_use, pk1, lacc);
+          }
           if (resc) {
 #pragma unroll
             for (int ch = 0; ch < kOChunks; ++ch) {
@@ -914,6 +996,11 @@ KernelFn pick_var(int var) {
     case 7: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 7>;
     case 11: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 11>;
     case 15: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 15>;
+    case 27: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 27>;
+    case 31: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 31>;
+    case 43: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 43>;
+    case 59: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 59>;
+    case 63: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 63>;
     default: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 3>;
   }
 }
@@ -950,7 +1037,7 @@ void attn_fwd_persistent_launch(const CUtensorMap& mq, const CUtensorMap& mk,
   MGFA_CHECK(p.sched != nullptr, "the persistent forward needs its work counters");
   MGFA_CHECK(!p.ring.enabled || p.batch * p.hkv <= kPMaxChunks, "too many kv-head chunks");
   const bool ring = p.ring.enabled != 0;
-  const int var = tune < 0 ? kDefaultVar : (tune >> 8) & 15;
+  const int var = tune < 0 ? kDefaultVar : (tune >> 8) & 63;
   const int poly8 = tune < 0 ? -1 : tune & 0xff;
   const KernelFn fn =
       head_dim == 64 ? pick<64>(fp16, ring, poly8, var) : pick<128>(fp16, ring, poly8, var);

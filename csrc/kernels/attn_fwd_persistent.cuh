@@ -87,7 +87,9 @@ struct PFwdParams {
 // (bit 8: packed f32x2) and the P hand-over (bit 9: two halves); bit 10 selects
 // a variant that sums per-phase clock counts into `trace` ([grid][16] int64,
 // layout in attn_fwd_persistent.cu), bit 11 computes the row max as a shallow
-// tree; negative means the default.
+// tree, bit 12 computes the first half's exponentials speculatively against
+// the running max, bit 13 hides the first P store's wait behind the next
+// exponentials; negative means the default.
 void attn_fwd_persistent_launch(const CUtensorMap& mq, const CUtensorMap& mk,
                                 const CUtensorMap& mv, const CUtensorMap& mslots, int head_dim,
                                 bool fp16, PFwdParams& p, int grid, int tune,

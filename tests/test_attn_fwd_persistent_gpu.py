@@ -53,8 +53,10 @@ def _run(q, k, v, causal, qtp=None, ktp=None, tune=-1, grid=0, seg_lens=(), call
 
 
 # softmax variants: polynomial pairs of 8 (0, 2, 4) x scalar / packed x whole /
-# split P hand-over
-TUNES = [-1, 0x000, 0x002, 0x004, 0x100, 0x200, 0x302, 0x304]
+# split P hand-over x chained / tree row max x exact / speculative max x P-store
+# wait in place / hidden
+TUNES = [-1, 0x000, 0x002, 0x004, 0x100, 0x200, 0x302, 0x304, 0xb00, 0xb02, 0x1b00, 0x1b02,
+         0x2b00, 0x3b00, 0x3b02]
 
 
 @pytest.mark.parametrize("tune", TUNES)
