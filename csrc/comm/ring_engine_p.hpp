@@ -105,6 +105,11 @@ class RingEngineP {
   // push end} (%globaltimer ns).
   void set_trace(bool on) { trace_ = on; }
   torch::Tensor last_trace() const { return last_trace_; }
+  // Diagnostic knobs: the softmax variant word of the kernel (see
+  // attn_fwd_persistent.cuh; -1 default) and whether push warps start only
+  // after their CTA's compute.
+  void set_tune(int tune) { tune_ = tune; }
+  void set_push_after_compute(bool on) { push_after_ = on; }
   // Test knob: the next calls drop the signal of unit (segment 0, chunk 0),
   // part 0, so the right neighbour's wait for it must expire.
   void set_drop_signal(bool on) { drop_signal_ = on; }
@@ -228,8 +233,9 @@ class RingEngineP {
       for (int s = 0; s < P; ++s) R.seg_tag[s] = seg_tag(P, r, s, calls_);
       R.drop_signal = drop_signal_ ? 1 : 0;
     }
+    if (ring) p.ring.push_after_compute = push_after_ ? 1 : 0;
     nvtxRangePushA(ring ? "ring attention (persistent)" : "ring attention compute only");
-    attn_fwd_persistent_launch(mq, mk, mv, mslots, D, f16, p, grid, -1, stream);
+    attn_fwd_persistent_launch(mq, mk, mv, mslots, D, f16, p, grid, tune_, stream);
     nvtxRangePop();
     if (ring) calls_ += 1;
     return {o, lse};
@@ -257,6 +263,8 @@ class RingEngineP {
   int num_sms_ = 148;
   bool trace_ = false;
   bool drop_signal_ = false;
+  int tune_ = -1;
+  bool push_after_ = false;
   torch::Tensor last_trace_;
   torch::Tensor pos_src_, pos_seg_;
   uint32_t pos_version_ = 0;

@@ -45,6 +45,7 @@
 #include <torch/types.h>
 #include <c10/cuda/CUDAException.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <set>
 #include <utility>
@@ -83,6 +84,7 @@ struct __align__(1024) PSmem {
   uint32_t tmem_base;
   uint32_t abort_flag;
   uint64_t wait_ns;  // producer time spent waiting for ring arrivals (trace)
+  uint32_t softmax_done;  // softmax warps that left their item loop
 };
 
 __device__ __forceinline__ uint32_t sm_id() {
@@ -397,6 +399,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     s.abort_flag = 0;
     s.wait_ns = 0;
+    s.softmax_done = 0;
     mbar_init(&s.q_full, 1);
     mbar_init(&s.q_empty, 1);
     for (int i = 0; i < 2; ++i) {
@@ -660,9 +663,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= 10) {
     // ------------------------------------------------------------ ring push
-    if (kRing)
+    if (kRing) {
+      if (p.ring.push_after_compute) {
+        // diagnostic: start pushing only once this CTA's compute is over
+        volatile uint32_t* done = &s.softmax_done;
+        const uint64_t t0 = globaltimer();
+        while (*done < 8u && globaltimer() - t0 < p.wait_limit_ns) __nanosleep(256);
+      }
       push_units<kD>(p, int(blockIdx.x) * 2 + int(warp - 10), int(gridDim.x) * 2, &s.abort_flag,
                      &tr_push0, &tr_push1);
+    }
   } else {
     // ------------------------------------------------------------ softmax + epilogue
     const int t = int(warp >> 2);  // query tile within the pair
@@ -725,6 +735,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!q_valid) n_vis = 0;
           }
           tmem_wait_ld();
+          regs_defined32(&sr[0]);
+          regs_defined32(&sr[32]);
+          regs_defined32(&sr[64]);
+          regs_defined32(&sr[96]);
           if constexpr (kProfile) { c1 = clk(); pa[1] += c1 - c0; c0 = c1; }
           if (!full) {
 #pragma unroll
@@ -759,6 +773,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int qq = 0; qq < 2; ++qq) {
                 tmem_ld32(s_addr + qq * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[qq * 32]));
                 tmem_wait_ld();
+                regs_defined32(&sr[qq * 32]);
                 if (redo) {
                   uint32_t pq[16];
                   float unused_mx[4];
@@ -832,6 +847,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 exp_pairs<kF16, 0, kPacked, 16>(sr, 32, p.scale_log2, -m_use, pk1, lacc, unused);
             }
             tmem_wait_st();
+            regs_live32(pk0);
             tc_fence_before();
             mbar_arrive(&s.p_full[t][0]);
           }
@@ -851,15 +867,20 @@ __global__ void __launch_bounds__(kThreads, 1)
               uint32_t orow[32];
               tmem_ld32(o_addr + ch * 32, orow);
               tmem_wait_ld();
+              regs_defined32(orow);
 #pragma unroll
               for (int c = 0; c < 32; ++c)
                 orow[c] = __float_as_uint(__uint_as_float(orow[c]) * alpha);
               tmem_st32(o_addr + ch * 32, orow);
+              tmem_wait_st();
+              regs_live32(orow);
             }
           }
           if (!early) tmem_st32(s_addr, pk0);
           tmem_st32(s_addr + 32, pk1);
           tmem_wait_st();
+          regs_live32(pk0);
+          regs_live32(pk1);
           tc_fence_before();
           if (!early) mbar_arrive(&s.p_full[t][0]);
           mbar_arrive(&s.p_full[t][1]);
@@ -887,6 +908,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (any) {
           tmem_ld32(o_addr + ch * 32, o);
           tmem_wait_ld();
+          regs_defined32(o);
         } else {
 #pragma unroll
           for (int c = 0; c < 32; ++c) o[c] = 0u;
@@ -912,6 +934,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       ++n;
     }
+    __syncwarp();
+    if (lane == 0) atomicAdd(&s.softmax_done, 1u);
   }
 
   // ---- teardown
@@ -978,6 +1002,12 @@ constexpr int smem_bytes() {
   return int(sizeof(PSmem<kD>)) + 1024;
 }
 
+// Diagnostic switch: an environment variable set to "0".
+bool getenv_flag_off(const char* name) {
+  const char* v = std::getenv(name);
+  return v && v[0] == '0' && v[1] == 0;
+}
+
 using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap,
                           const CUtensorMap, const PFwdParams);
 
@@ -1011,6 +1041,11 @@ KernelFn pick_poly(int poly8, int var) {
     if (poly8 == 0) return pick_var<0>(var);
     if (poly8 == 4) return pick_var<4>(var);
     if (poly8 == 2 || poly8 < 0) return pick_var<2>(var);
+  }
+  if constexpr (kD == 128 && !kF16 && kRing) {
+    if (poly8 == 0 && var == 1) return attn_fwd_persistent_kernel<128, false, 0, true, 1>;
+    if (poly8 == 0 && var == 3) return attn_fwd_persistent_kernel<128, false, 0, true, 3>;
+    if (poly8 == 2 && var == 1) return attn_fwd_persistent_kernel<128, false, 2, true, 1>;
   }
   return attn_fwd_persistent_kernel<kD, kF16, kDefaultPoly8, kRing, kDefaultVar>;
 }
@@ -1062,7 +1097,7 @@ void attn_fwd_persistent_launch(const CUtensorMap& mq, const CUtensorMap& mk,
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = ring ? 1 : 0;
+  cfg.numAttrs = ring && !getenv_flag_off("MGFA_P_COOP") ? 1 : 0;
   C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, fn, mq, mk, mv, mslots, p));
 }
 

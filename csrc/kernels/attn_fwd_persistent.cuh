@@ -55,6 +55,8 @@ struct PRing {
   uint32_t seg_tag[kPMaxSeg] = {};   // tag of segment s's data: (owner + 1) | call << 8
   int drop_signal = 0;               // test knob: unit (segment 0, chunk 0) part 0 is
                                      // copied but never signalled
+  int push_after_compute = 0;        // diagnostic knob: a CTA's push warps start only
+                                     // once its softmax warps have finished every item
 };
 
 struct PFwdParams {

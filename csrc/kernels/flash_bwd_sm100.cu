@@ -67,6 +67,8 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t addr, uint32_t (&r)[kN]) {
 #pragma unroll
   for (int c = 0; c < kN; c += 32) tmem_ld32(addr + c, *reinterpret_cast<uint32_t(*)[32]>(&r[c]));
   tmem_wait_ld();
+#pragma unroll
+  for (int c = 0; c < kN; c += 32) regs_defined32(&r[c]);  // uses only after the wait
 }
 
 __device__ __forceinline__ void tmem_ld128(uint32_t addr, uint32_t (&r)[128]) {
@@ -285,24 +287,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu, mbar_wait(&s.dp_full, it & 1, ab, 61));
       if (!ok) break;
       tc_fence_after();
+      uint32_t pk[4][16];
 #pragma unroll
       for (int ch = 0; ch < 4; ++ch) {
         uint32_t dpr[32];
         tmem_ld32(tmem + lane_off + DP_COL + ch * 32, dpr);
         tmem_wait_ld();
-        uint32_t pk[16];
+        regs_defined32(dpr);
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
           const float d0 = pr[ch * 32 + 2 * c] * (__uint_as_float(dpr[2 * c]) - dlt);
           const float d1 = pr[ch * 32 + 2 * c + 1] * (__uint_as_float(dpr[2 * c + 1]) - dlt);
-          pk[c] = pack16<kF16>(d0, d1);
+          pk[ch][c] = pack16<kF16>(d0, d1);
         }
         // dS over the first 64 columns of the dP region (column ch*16.. holds
         // keys ch*32 .. ch*32+31); the chunk just read is never overwritten before
         // it is read because chunk ch's output lands in columns [16ch, 16ch+16).
-        tmem_st16(tmem + lane_off + DP_COL + ch * 16, pk);
+        tmem_st16(tmem + lane_off + DP_COL + ch * 16, pk[ch]);
       }
       tmem_wait_st();
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) regs_live16(pk[ch]);
       tc_fence_before();
       mbar_arrive(&s.ds_full);
       ++it;
@@ -554,28 +559,33 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
         tmem_st32(tmem + lane_off + ST_COL, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
         tmem_st32(tmem + lane_off + ST_COL + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
         tmem_wait_st();
+        regs_live32(&pk[0]);
+        regs_live32(&pk[32]);
         tc_fence_before();
         mbar_arrive(&s.p_full);
         ok = __all_sync(0xffffffffu, mbar_wait(&s.dp_full, it & 1, ab, 91));
         if (!ok) break;
         tc_fence_after();
         const float* dl = s.delta[st];
+        uint32_t dk[4][16];
 #pragma unroll
         for (int ch = 0; ch < 4; ++ch) {
           uint32_t dpr[32];
           tmem_ld32(tmem + lane_off + DPT_COL + ch * 32, dpr);
           tmem_wait_ld();
-          uint32_t dk[16];
+          regs_defined32(dpr);
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
             const int c0 = ch * 32 + 2 * c;
             const float d0 = pr[c0] * (__uint_as_float(dpr[2 * c]) - dl[c0]);
             const float d1 = pr[c0 + 1] * (__uint_as_float(dpr[2 * c + 1]) - dl[c0 + 1]);
-            dk[c] = pack16<kF16>(d0, d1);
+            dk[ch][c] = pack16<kF16>(d0, d1);
           }
-          tmem_st16(tmem + lane_off + DPT_COL + ch * 16, dk);
+          tmem_st16(tmem + lane_off + DPT_COL + ch * 16, dk[ch]);
         }
         tmem_wait_st();
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) regs_live16(dk[ch]);
         tc_fence_before();
         mbar_arrive(&s.ds_full);
         ++it;

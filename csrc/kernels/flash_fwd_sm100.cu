@@ -300,6 +300,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!q_valid_tile) n_vis = 0;
       }
       tmem_wait_ld();
+      regs_defined32(&sr[0]);
+      regs_defined32(&sr[32]);
+      regs_defined32(&sr[64]);
+      regs_defined32(&sr[96]);
       if (!full) {
 #pragma unroll
         for (int c = 0; c < 128; ++c)
@@ -330,18 +334,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       l *= alpha;
       const float neg_m = -m_use;
       float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
+      uint32_t pk[2][32];
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
-        uint32_t pk[32];
 #pragma unroll
         for (int cc = 0; cc < 32; ++cc) {
           const int c = half * 32 + cc;
           const float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * c]), p.scale_log2, neg_m));
           const float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * c + 1]), p.scale_log2, neg_m));
           if (c & 1) { l2 += p0; l3 += p1; } else { l0 += p0; l1 += p1; }
-          pk[cc] = pack16<kF16>(p0, p1);
+          pk[half][cc] = pack16<kF16>(p0, p1);
         }
-        tmem_st32(s_addr + half * 32, pk);
+        tmem_st32(s_addr + half * 32, pk[half]);
       }
       l += (l0 + l1) + (l2 + l3);
       if (__any_sync(0xffffffffu, rescale)) {
@@ -350,12 +354,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t orow[32];
           tmem_ld32(o_addr + ch * 32, orow);
           tmem_wait_ld();
+          regs_defined32(orow);
 #pragma unroll
           for (int c = 0; c < 32; ++c) orow[c] = __float_as_uint(__uint_as_float(orow[c]) * alpha);
           tmem_st32(o_addr + ch * 32, orow);
+          tmem_wait_st();
+          regs_live32(orow);
         }
       }
       tmem_wait_st();
+      regs_live32(pk[0]);
+      regs_live32(pk[1]);
       tc_fence_before();
       mbar_arrive(&s.p_full[t]);
     }
@@ -399,6 +408,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!skip_compute && ok) {
         tmem_ld32(o_addr + ch * 32, orow);
         tmem_wait_ld();
+        regs_defined32(orow);
       } else {
 #pragma unroll
         for (int c = 0; c < 32; ++c) orow[c] = 0u;

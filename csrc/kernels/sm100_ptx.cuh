@@ -259,6 +259,36 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       "r"(r[15]));
 }
 
+// tcgen05.ld writes its destination registers asynchronously: they hold the
+// loaded values only once tcgen05.wait::ld has returned. To the compiler the
+// load's outputs look defined at the load itself, and the wait (an asm
+// statement without register operands) does not keep it from scheduling
+// register-only uses of them -- arithmetic, non-volatile asm, copies, spills --
+// before the wait, which then read whatever the registers held before. So
+// after every wait the loaded registers go through regs_defined*, an empty
+// volatile asm that claims to redefine them: every use is ordered after it,
+// and it is ordered after the wait. Likewise regs_live* after
+// tcgen05.wait::st keeps a store's source registers unchanged until the store
+// has completed.
+#define MGFA_R8(r, o) "+r"(r[o]), "+r"(r[o + 1]), "+r"(r[o + 2]), "+r"(r[o + 3]), \
+    "+r"(r[o + 4]), "+r"(r[o + 5]), "+r"(r[o + 6]), "+r"(r[o + 7])
+#define MGFA_I8(r, o) "r"(r[o]), "r"(r[o + 1]), "r"(r[o + 2]), "r"(r[o + 3]), \
+    "r"(r[o + 4]), "r"(r[o + 5]), "r"(r[o + 6]), "r"(r[o + 7])
+__device__ __forceinline__ void regs_defined16(uint32_t* r) {
+  asm volatile("" : MGFA_R8(r, 0), MGFA_R8(r, 8)::"memory");
+}
+__device__ __forceinline__ void regs_defined32(uint32_t* r) {
+  asm volatile("" : MGFA_R8(r, 0), MGFA_R8(r, 8), MGFA_R8(r, 16), MGFA_R8(r, 24)::"memory");
+}
+__device__ __forceinline__ void regs_live16(const uint32_t* r) {
+  asm volatile("" ::MGFA_I8(r, 0), MGFA_I8(r, 8) : "memory");
+}
+__device__ __forceinline__ void regs_live32(const uint32_t* r) {
+  asm volatile("" ::MGFA_I8(r, 0), MGFA_I8(r, 8), MGFA_I8(r, 16), MGFA_I8(r, 24) : "memory");
+}
+#undef MGFA_R8
+#undef MGFA_I8
+
 // ---------------------------------------------------------------- descriptors
 // bf16 x bf16 -> fp32, M x N tile, operand majors (0 = K-major, 1 = MN-major).
 __host__ __device__ constexpr uint32_t make_idesc_bf16(uint32_t M, uint32_t N, uint32_t a_mn,

@@ -70,6 +70,7 @@ __global__ void __launch_bounds__(128, 1)
     }
     tmem_st32(tmem + ((warp * 32) << 16) + a_col, packed);
     tmem_wait_st();
+    regs_live32(packed);
   }
   tc_fence_before();
   __syncthreads();
@@ -100,9 +101,11 @@ __global__ void __launch_bounds__(128, 1)
       uint32_t r[32];
       tmem_ld32(tmem + ((warp * 32) << 16) + c1_col + chunk * 32, r);
       tmem_wait_ld();
+      regs_defined32(r);
       for (int j = 0; j < 32; ++j) c1[row * 128 + chunk * 32 + j] = __uint_as_float(r[j]);
       tmem_ld32(tmem + ((warp * 32) << 16) + c2_col + chunk * 32, r);
       tmem_wait_ld();
+      regs_defined32(r);
       for (int j = 0; j < 32; ++j) c2[row * 128 + chunk * 32 + j] = __uint_as_float(r[j]);
     }
   }
