@@ -408,10 +408,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s.v_full[i], 1);
       mbar_init(&s.v_empty[i], 1);
       mbar_init(&s.s_full[i], 1);
-      mbar_init(&s.p_full[i][0], 128);
-      mbar_init(&s.p_full[i][1], 128);
+      mbar_init(&s.p_full[i][0], 4);  // one arrive per softmax warp
+      mbar_init(&s.p_full[i][1], 4);
       mbar_init(&s.o_full[i], 1);
-      mbar_init(&s.o_empty[i], 128);
+      mbar_init(&s.o_empty[i], 4);
       mbar_init(&s.sched_full[i], 1);
       mbar_init(&s.sched_empty[i], 9);  // MMA thread + 8 softmax warps
     }
@@ -849,7 +849,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_wait_st();
             regs_live32(pk0);
             tc_fence_before();
-            mbar_arrive(&s.p_full[t][0]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s.p_full[t][0]);
           }
           if constexpr (kProfile) { c1 = clk(); pa[3] += c1 - c0; c0 = c1; }
           if (kLate && early) {
@@ -882,8 +883,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           regs_live32(pk0);
           regs_live32(pk1);
           tc_fence_before();
-          if (!early) mbar_arrive(&s.p_full[t][0]);
-          mbar_arrive(&s.p_full[t][1]);
+          __syncwarp();
+          if (lane == 0) {
+            if (!early) mbar_arrive(&s.p_full[t][0]);
+            mbar_arrive(&s.p_full[t][1]);
+          }
           if constexpr (kProfile) { c1 = clk(); pa[4] += c1 - c0; }
           l = l * alpha + ((lacc[0] + lacc[1]) + (lacc[2] + lacc[3]));
         }
@@ -915,7 +919,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (ch == kOChunks - 1) {
           tc_fence_before();
-          mbar_arrive(&s.o_empty[t]);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s.o_empty[t]);
         }
         if (row_ok) {
 #pragma unroll

@@ -141,9 +141,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s.v_empty[i], 1);
     }
     mbar_init(&s.s_full, 1);
-    mbar_init(&s.s_free, 128);
+    mbar_init(&s.s_free, 4);  // one arrive per softmax warp
     mbar_init(&s.dp_full, 1);
-    mbar_init(&s.ds_full, 128);
+    mbar_init(&s.ds_full, 4);
     mbar_init(&s.dq_full, 1);
     mbar_init(&s.drain, 1);
     fence_mbar_init();
@@ -267,7 +267,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t sr[128];
       tmem_ld128(tmem + lane_off + S_COL, sr);
       tc_fence_before();
-      mbar_arrive(&s.s_free);
+      __syncwarp();
+      if ((threadIdx.x & 31) == 0) mbar_arrive(&s.s_free);
       float pr[128];
       if (j < full_hi) {  // warp-uniform fast path: no mask
 #pragma unroll
@@ -309,7 +310,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int ch = 0; ch < 4; ++ch) regs_live16(pk[ch]);
       tc_fence_before();
-      mbar_arrive(&s.ds_full);
+      __syncwarp();
+      if ((threadIdx.x & 31) == 0) mbar_arrive(&s.ds_full);
       ++it;
     }
     if (n_active > 0 && ok) ok = __all_sync(0xffffffffu, mbar_wait(&s.dq_full, 0, ab, 62));
@@ -393,8 +395,8 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
     }
     mbar_init(&s.s_full, 1);
     mbar_init(&s.dp_full, 1);
-    mbar_init(&s.p_full, 128);
-    mbar_init(&s.ds_full, 128);
+    mbar_init(&s.p_full, 4);  // one arrive per softmax warp
+    mbar_init(&s.ds_full, 4);
     mbar_init(&s.dkv_full, 1);
     mbar_init(&s.drain, 1);
     fence_mbar_init();
@@ -562,7 +564,8 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
         regs_live32(&pk[0]);
         regs_live32(&pk[32]);
         tc_fence_before();
-        mbar_arrive(&s.p_full);
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) mbar_arrive(&s.p_full);
         ok = __all_sync(0xffffffffu, mbar_wait(&s.dp_full, it & 1, ab, 91));
         if (!ok) break;
         tc_fence_after();
@@ -587,7 +590,8 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
 #pragma unroll
         for (int ch = 0; ch < 4; ++ch) regs_live16(dk[ch]);
         tc_fence_before();
-        mbar_arrive(&s.ds_full);
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) mbar_arrive(&s.ds_full);
         ++it;
       }
     }

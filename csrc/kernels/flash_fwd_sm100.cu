@@ -124,7 +124,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s.v_full[i], 1);
       mbar_init(&s.v_empty[i], 1);
       mbar_init(&s.s_full[i], 1);
-      mbar_init(&s.p_full[i], 128);
+      mbar_init(&s.p_full[i], 4);  // one arrive per softmax warp
     }
     mbar_init(&s.o_full, 1);
     mbar_init(&s.drain, 1);
@@ -366,7 +366,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       regs_live32(pk[0]);
       regs_live32(pk[1]);
       tc_fence_before();
-      mbar_arrive(&s.p_full[t]);
+      __syncwarp();
+      if ((threadIdx.x & 31) == 0) mbar_arrive(&s.p_full[t]);
     }
     if (!skip_compute && ok) ok = __all_sync(0xffffffffu, mbar_wait(&s.o_full, 0, ab, 30 + t));
     ok = __all_sync(0xffffffffu, ok);
