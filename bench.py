@@ -40,8 +40,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--backend", choices=["fused", "fused_stepwise", "p2p_unfused", "ce_unfused",
-                                          "nccl", "staged"],
+    ap.add_argument("--backend", choices=["fused", "fused_stepwise", "fused_one_launch",
+                                          "p2p_unfused", "ce_unfused", "nccl", "staged"],
                     default="fused")
     ap.add_argument("--seq", type=int, default=131072)
     ap.add_argument("--heads", type=int, default=32)
@@ -312,10 +312,13 @@ def main():
 
     # ---------------- compute-only reference for the exposed-comm fraction
     exposed = None
-    if world > 1 and args.backend in ("fused", "fused_stepwise", "p2p_unfused", "ce_unfused"):
+    from multi_gpu_flashattention_b200.parallel.ring import resolve_backend
+    concrete = resolve_backend(args.backend)
+    if world > 1 and concrete in ("fused_stepwise", "fused_one_launch", "p2p_unfused",
+                                  "ce_unfused"):
         from multi_gpu_flashattention_b200.parallel.ring import P_ENGINES, _meta
         nbytes = k.numel() * k.element_size()
-        eng = P_ENGINES.get(group, dev, nbytes) if args.backend == "fused" else \
+        eng = P_ENGINES.get(group, dev, nbytes) if concrete == "fused_one_launch" else \
             ENGINES.get(group, dev, nbytes)
         qtp, kvtp, kv_lens = _meta(lay, rank, dev)
         def compute_only():
@@ -404,7 +407,7 @@ def main():
         t_roof = max(flops / world / (peak * 1e12), comm_bytes / 770e9) * 1e3
         # the one-launch ring runs one kernel per forward (so does a single GPU);
         # the per-step engines and the baselines one attention kernel per step
-        launches_per_step = 1 if args.backend == "fused" else world
+        launches_per_step = 1 if concrete == "fused_one_launch" or world == 1 else world
         rec = {
             "metric": METRIC,
             "value": round(tflops_total, 2),
@@ -425,7 +428,7 @@ def main():
             "dtype": "bf16",
             "data": "synthetic: seeded N(0,1)*0.5 q/k/v, no weights (attention op)",
             "impl": "ours",
-            "backend": args.backend,
+            "backend": concrete,
             "config": {"model": f"ring attention fwd, causal={causal}, {H} q heads / {Hkv} kv "
                                 f"heads x d{D}",
                        "global_batch": B, "seq_len": S,

@@ -5,7 +5,8 @@
 //
 //   torchrun --nproc-per-node N --no-python build/bin/ring_attention_bench
 //       <kv_size_bytes> [warmup=10] [iters=100]
-//       [--backend fused|fused_stepwise|p2p_unfused|ce_unfused|nccl|staged|p2p|ce]
+//       [--backend fused|fused_stepwise|fused_one_launch|p2p_unfused|ce_unfused|nccl|
+//        staged|p2p|ce]
 //       [--numerics fp32|bf16] [--init legacy|randn] [--layout contiguous|zigzag|
 //       striped|scheduler] [--policy dp|lpt] [--causal] [--heads H] [--kv-heads H]
 //       [--head-dim D] [--seed S] [--overlap] [--json]
@@ -19,10 +20,11 @@
 //     copy engine; sequential order). --init legacy
 //     reproduces the reference's inputs (K == V, no softmax scale) so
 //     `verify_full <dir> N kv_size` checks the dumps.
-//   --numerics bf16 (head_dim 64 or 128): the sm_100a kernels; fused (the whole
-//     ring in one launch of the persistent kernel, transport inside it),
+//   --numerics bf16 (head_dim 64 or 128): the sm_100a kernels; fused (the engine
+//     MGFA_RING_ENGINE names: stepwise by default, or one_launch),
 //     fused_stepwise (one attention launch per step with the transport inside
-//     it), p2p_unfused (the same NVLink push transport as a separate kernel on a
+//     it), fused_one_launch (the whole ring in one launch of the persistent
+//     kernel, transport inside it), p2p_unfused (the same NVLink push transport as a separate kernel on a
 //     second stream), ce_unfused (the copy engine moves the shard on a second
 //     stream), nccl (attention kernel per step + NCCL send/recv on a second
 //     stream) or staged (device -> host -> store -> device). The bf16 total is
@@ -127,6 +129,7 @@ bool parse(int argc, char** argv, Args* a) {
   if (a->backend.empty()) a->backend = a->numerics == "bf16" ? "fused" : "nccl";
   return (a->numerics == "fp32" || a->numerics == "bf16") &&
          (a->backend == "fused" || a->backend == "fused_stepwise" ||
+          a->backend == "fused_one_launch" ||
           a->backend == "p2p_unfused" || a->backend == "ce_unfused" ||
           a->backend == "nccl" || a->backend == "staged" || a->backend == "p2p" ||
           a->backend == "ce") &&
@@ -539,7 +542,11 @@ class Bf16Ring {
       kv_lens_.push_back(m.plan.local_len(o));
     }
     kvtp_ = i32_dev(all, dev).view({P, -1});
-    if (a.backend == "fused") {
+    const char* engine_env = std::getenv("MGFA_RING_ENGINE");
+    const bool one_launch = a.backend == "fused_one_launch" ||
+                            (a.backend == "fused" && engine_env &&
+                             std::string(engine_env) == "one_launch");
+    if (one_launch) {
       // the one-launch ring: a receive slot per step, one kernel per forward
       int64_t cap = std::max<int64_t>(k.numel() * k.element_size(), 1 << 20);
       cap = (cap + (2 << 20) - 1) / (2 << 20) * (2 << 20);
@@ -547,8 +554,8 @@ class Bf16Ring {
       peng_->connect(d.all_gather(peng_->ipc_handle()));
       cudaDeviceSynchronize();
       d.barrier();
-    } else if (a.backend == "fused_stepwise" || a.backend == "p2p_unfused" ||
-               a.backend == "ce_unfused") {
+    } else if (a.backend == "fused" || a.backend == "fused_stepwise" ||
+               a.backend == "p2p_unfused" || a.backend == "ce_unfused") {
       const int64_t shard = k.numel() * k.element_size();
       int64_t slot = std::max<int64_t>(shard, 1 << 20);
       slot = (slot + (2 << 20) - 1) / (2 << 20) * (2 << 20);
@@ -559,7 +566,8 @@ class Bf16Ring {
       const char* ca = std::getenv("MGFA_CUMULATIVE_ARRIVALS");
       eng_->set_cumulative_arrivals(ca && std::string(ca) == "1");
       eng_->connect(d.all_gather(eng_->ipc_handle()));
-      eng_->set_transport_mode(a.backend == "fused_stepwise" ? mgfa::RingEngine::kFusedPush
+      eng_->set_transport_mode(a.backend == "fused" || a.backend == "fused_stepwise"
+                                   ? mgfa::RingEngine::kFusedPush
                                : a.backend == "p2p_unfused"  ? mgfa::RingEngine::kPushKernel
                                                              : mgfa::RingEngine::kCopyEngine);
       cudaDeviceSynchronize();
@@ -758,7 +766,8 @@ static int run_main(int argc, char** argv) {
   Args a;
   if (!parse(argc, argv, &a)) {
     std::printf("Usage: ring_attention_bench <kv_size_bytes> [warmup] [iters] "
-                "[--backend fused|fused_stepwise|p2p_unfused|ce_unfused|nccl|staged|p2p|ce] [--numerics fp32|bf16] "
+                "[--backend fused|fused_stepwise|fused_one_launch|p2p_unfused|ce_unfused|nccl|staged|p2p|ce] "
+                "[--numerics fp32|bf16] "
                 "[--init legacy|randn] "
                 "[--layout contiguous|zigzag|striped|scheduler] [--policy dp|lpt] [--causal] "
                 "[--heads H] [--kv-heads H] [--head-dim D] [--seed S] [--overlap] [--json]\n");

@@ -822,7 +822,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if constexpr (kProfile) { c1 = clk(); pa[2] += c1 - c0; c0 = c1; }
             const float m0 = (m == -INFINITY) ? 0.f : m;
-            if (full) exp_half<kF16, kPoly8, kPacked>(sr, 0, p.scale_log2, -m0, pk0, lacc);
+            if (kPoly8 > 0 && full) exp_half<kF16, kPoly8, kPacked>(sr, 0, p.scale_log2, -m0, pk0, lacc);
             else exp_half<kF16, 0, kPacked>(sr, 0, p.scale_log2, -m0, pk0, lacc);
           }
           first = false;
@@ -841,7 +841,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if constexpr (kLate) {
               // the store's completion wait goes behind a quarter of the
               // second half's exponentials
-              if (full)
+              if (kPoly8 > 0 && full)
                 exp_pairs<kF16, kPoly8, kPacked, 16>(sr, 32, p.scale_log2, -m_use, pk1, lacc, unused);
               else
                 exp_pairs<kF16, 0, kPacked, 16>(sr, 32, p.scale_log2, -m_use, pk1, lacc, unused);
@@ -854,12 +854,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if constexpr (kProfile) { c1 = clk(); pa[3] += c1 - c0; c0 = c1; }
           if (kLate && early) {
-            if (full)
+            if (kPoly8 > 0 && full)
               exp_pairs<kF16, kPoly8, kPacked, 16>(sr, 48, p.scale_log2, -m_use, pk1 + 16, lacc, unused);
             else
               exp_pairs<kF16, 0, kPacked, 16>(sr, 48, p.scale_log2, -m_use, pk1 + 16, lacc, unused);
           } else {
-            if (full) exp_half<kF16, kPoly8, kPacked>(sr, 1, p.scale_log2, -m_use, pk1, lacc);
+            if (kPoly8 > 0 && full) exp_half<kF16, kPoly8, kPacked>(sr, 1, p.scale_log2, -m_use, pk1, lacc);
             else exp_half<kF16, 0, kPacked>(sr, 1, p.scale_log2, -m_use, pk1, lacc);
           }
           if (resc) {

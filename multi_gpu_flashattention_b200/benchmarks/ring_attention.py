@@ -42,6 +42,7 @@ from ..parallel.layouts import RingLayout
 from . import common
 
 COMM_NAME = {"nccl": "NCCL", "staged": "MPI", "fused": "P2P", "fused_stepwise": "P2P",
+             "fused_one_launch": "P2P",
              "p2p_unfused": "P2P",
              "ce_unfused": "CE", "p2p": "P2P", "ce": "CE"}
 
@@ -52,8 +53,8 @@ def parse():
     ap.add_argument("warmup", type=int, nargs="?", default=10)
     ap.add_argument("iters", type=int, nargs="?", default=100)
     ap.add_argument("--backend", default=None,
-                    choices=["fused", "fused_stepwise", "p2p_unfused", "ce_unfused", "nccl",
-                             "staged", "p2p", "ce"])
+                    choices=["fused", "fused_stepwise", "fused_one_launch", "p2p_unfused",
+                             "ce_unfused", "nccl", "staged", "p2p", "ce"])
     ap.add_argument("--numerics", default="fp32", choices=["fp32", "bf16"])
     ap.add_argument("--init", default="legacy", choices=["legacy", "randn"])
     ap.add_argument("--layout", default="contiguous",
@@ -347,10 +348,12 @@ class Bf16Ring:
                         f"receiving_kv_owner={ro} KV tokens={tokens(lay, ro)}")
             o = lay.compute_owner(r, P - 1)
             ctx.log(f"[Rank {r}] final compute_kv_owner={o} KV tokens={tokens(lay, o)}")
-        fused = self.args.backend in ("fused", "fused_stepwise", "p2p_unfused",
-                                      "ce_unfused") and P > 1
+        fused = self.args.backend in ("fused", "fused_stepwise", "fused_one_launch",
+                                      "p2p_unfused", "ce_unfused") and P > 1
         if fused:
-            engines = P_ENGINES if self.args.backend == "fused" else ENGINES
+            from ..parallel.ring import resolve_backend
+            one = resolve_backend(self.args.backend) == "fused_one_launch"
+            engines = P_ENGINES if one else ENGINES
             eng = engines.get(None, ctx.device, self.k.numel() * self.k.element_size())
             qtp, kvtp, kv_lens = _meta(lay, r, ctx.device)
 

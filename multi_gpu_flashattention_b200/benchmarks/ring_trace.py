@@ -1,10 +1,10 @@
 """Record a ring engine's per-CTA timeline for one forward call.
 
     torchrun --nproc-per-node N -m multi_gpu_flashattention_b200.benchmarks.ring_trace \
-        [--seq 131072] [--heads 32] [--out DIR] [--backend fused|fused_stepwise]
+        [--seq 131072] [--heads 32] [--out DIR] [--backend fused_one_launch|fused_stepwise]
 
 After 3 untraced calls, one traced call writes DIR/summary_rank<r>.json and
-DIR/trace_rank0.json (Chrome trace of rank 0). One-launch ring ("fused"):
+DIR/trace_rank0.json (Chrome trace of rank 0). One-launch ring ("fused_one_launch"):
 kernel span, CTA busy times, time CTAs waited for received shards, push window.
 Per-step engine ("fused_stepwise"): per step the wall span, longest wait for
 the KV shard, mean push time per pushing CTA."""
@@ -29,7 +29,8 @@ def main():
     ap.add_argument("--heads", type=int, default=32)
     ap.add_argument("--layout", default="zigzag")
     ap.add_argument("--out", default="ring_trace")
-    ap.add_argument("--backend", default="fused", choices=["fused", "fused_stepwise"])
+    ap.add_argument("--backend", default="fused_one_launch",
+                    choices=["fused_one_launch", "fused_stepwise"])
     a = ap.parse_args()
     ctx = common.init(need_world_gt1=True)
     lay = RingLayout(a.layout, a.seq, ctx.world, mask="causal")
@@ -39,7 +40,7 @@ def main():
     q, k, v = mk(), mk(), mk()
     for _ in range(3):
         ring_attention_forward(q, k, v, lay, causal=True, backend=a.backend, check=True)
-    one = a.backend == "fused"
+    one = a.backend == "fused_one_launch"
     eng = (P_ENGINES if one else ENGINES).get(None, ctx.device, k.numel() * 2)
     eng.set_trace(True)
     torch.cuda.synchronize()

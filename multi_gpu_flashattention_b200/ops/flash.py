@@ -172,10 +172,11 @@ def _default_positions(n_tokens: int, device) -> torch.Tensor:
     return t
 
 
-# Forward kernel of flash_attn_fwd: "persistent" (one CTA per SM, dynamic tile
-# scheduler, attn_fwd_persistent.cu) or "stepwise" (one CTA per query-tile pair,
-# flash_fwd_sm100.cu, the kernel the per-step ring and the merge path use).
-FWD_KERNEL = os.environ.get("MGFA_FWD_KERNEL", "persistent")
+# Forward kernel of flash_attn_fwd: "stepwise" (one CTA per query-tile pair,
+# flash_fwd_sm100.cu, the kernel the per-step ring and the merge path use; the
+# default, it measured faster at 128K) or "persistent" (one CTA per SM, dynamic
+# tile scheduler, attn_fwd_persistent.cu).
+FWD_KERNEL = os.environ.get("MGFA_FWD_KERNEL", "stepwise")
 # softmax variant of the persistent forward (attn_fwd_persistent.cuh: bits 0-7
 # exponential pairs of every 8 on the FMA pipe, bit 8 packed f32x2 arithmetic,
 # bit 9 P handed over in two halves); -1: the kernel's default

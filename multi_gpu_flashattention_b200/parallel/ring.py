@@ -11,17 +11,19 @@ ring/attention/bench/ring_attention_nccl_gpu_bench.cu:349-397).
 
 Backends
 --------
-fused   (default on CUDA) the whole ring in ONE launch of the persistent
-        sm_100a kernel (native RingEngineP): every rank keeps a receive slot per
-        ring step, computes each query tile against its own shard and then
-        every received shard as its kv-head chunk arrives, with the softmax
-        state on chip across steps (no per-step merge), while the kernel's
-        push warps forward each received chunk to the right neighbour with peer
-        stores.
+fused   (default on CUDA) the fused ring engine that MGFA_RING_ENGINE selects:
+        "stepwise" (default) or "one_launch".
 fused_stepwise
         one sm_100a kernel launch per ring step that computes, merges in-kernel
         and pushes the current shard into the right neighbour's receive slot
         (native RingEngine).
+fused_one_launch
+        the whole ring in ONE launch of the persistent sm_100a kernel (native
+        RingEngineP): every rank keeps a receive slot per ring step, computes
+        each query tile against its own shard and then every received shard as
+        its kv-head chunk arrives, with the softmax state on chip across steps
+        (no per-step merge), while the kernel's push warps forward each received
+        chunk to the right neighbour with peer stores.
 p2p_unfused, ce_unfused
         ablations of `fused_stepwise`: the same engine, slots and flags, with the
         shard moved on a second stream by the standalone push kernel or by the
@@ -47,7 +49,21 @@ from ..ops.flash import (DEFAULT_WAIT_LIMIT_NS, check_status, flash_attn_fwd,
 from ..ops.reference import attention_ref
 from .layouts import RingLayout
 
-BACKENDS = ("fused", "fused_stepwise", "p2p_unfused", "ce_unfused", "nccl", "staged", "torch")
+BACKENDS = ("fused", "fused_stepwise", "fused_one_launch", "p2p_unfused", "ce_unfused", "nccl",
+            "staged", "torch")
+# The engine behind backend "fused": "stepwise" (one kernel launch per ring step,
+# the default) or "one_launch" (the whole ring in one persistent-kernel launch).
+RING_ENGINE = os.environ.get("MGFA_RING_ENGINE", "stepwise")
+
+
+def resolve_backend(backend: Optional[str], is_cuda: bool = True) -> str:
+    """The concrete backend a name selects: None means "fused" on CUDA and
+    "torch" elsewhere, and "fused" means the engine MGFA_RING_ENGINE names."""
+    if backend is None:
+        backend = "fused" if is_cuda else "torch"
+    if backend == "fused":
+        backend = "fused_one_launch" if RING_ENGINE == "one_launch" else "fused_stepwise"
+    return backend
 # transport modes of the per-step engine (RingEngine.set_transport_mode)
 _ENGINE_MODES = {"fused_stepwise": 0, "p2p_unfused": 1, "ce_unfused": 2}
 
@@ -336,10 +352,9 @@ def ring_attention_forward(q, k, v, layout: RingLayout, causal: bool = False,
     its gate, so a peer that left or went silent raises PeerLostError here
     instead of leaving launched kernels waiting."""
     scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(q.shape[-1])
-    if backend is None:
-        backend = "fused" if q.is_cuda else "torch"
-    if backend not in BACKENDS:
+    if backend is not None and backend not in BACKENDS:
         raise ValueError(f"backend must be one of {BACKENDS}")
+    backend = resolve_backend(backend, q.is_cuda)
     rank, world = _world(group)
     if health is not None and world > 1:
         health.gate()
@@ -357,7 +372,7 @@ def ring_attention_forward(q, k, v, layout: RingLayout, causal: bool = False,
         out, lse = flash_attn_fwd(q, k[:, :kv_lens[0]], v[:, :kv_lens[0]], causal=causal,
                                   softmax_scale=scale, q_tile_pos=qtp, kv_tile_pos=kvtp[0],
                                   status=st, wait_limit_ns=wait_limit_ns)
-    elif backend == "fused":
+    elif backend == "fused_one_launch":
         out, lse = _fwd_persistent(q, k, v, layout, causal, scale, group, st, wait_limit_ns)
     elif backend in _ENGINE_MODES:
         out, lse = _fwd_fused(q, k, v, layout, causal, scale, group, st, wait_limit_ns,

@@ -66,7 +66,7 @@ def ring_attention_backward(dout, q, k, v, out, lse, layout: RingLayout, causal:
         dv_full[:, :kv_lens[0]] = dv
         return dq.to(q.dtype), dk_full.to(k.dtype), dv_full.to(v.dtype)
 
-    if backend in (None, "fused", "fused_stepwise"):
+    if backend in (None, "fused", "fused_stepwise", "fused_one_launch"):
         return _bwd_fused(dout, q, k, v, out, lse, causal, scale, group, qtp, kvtp, kv_lens)
     right, left = _global(group, (rank + 1) % world), _global(group, (rank - 1) % world)
     lse2, delta = C().flash_bwd_preprocess(dout, out, lse)

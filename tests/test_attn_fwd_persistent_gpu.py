@@ -128,11 +128,12 @@ def test_segments_accumulate_in_one_launch(causal):
     _check(o, lse, q, k_all, v_all, causal, q_pos=torch.arange(2 * L).cuda(), k_pos=k_pos)
 
 
-def test_public_flash_attn_fwd_uses_it_on_its_own_stream():
-    """flash_attn_fwd on two streams: each stream gets its own counter pair."""
-    from multi_gpu_flashattention_b200.ops.flash import (FWD_KERNEL, check_errors,
-                                                         flash_attn_fwd, sched_counters)
-    assert FWD_KERNEL == "persistent"
+def test_public_flash_attn_fwd_uses_it_on_its_own_stream(monkeypatch):
+    """flash_attn_fwd with the persistent kernel selected, on two streams: each
+    stream gets its own counter pair."""
+    from multi_gpu_flashattention_b200.ops import flash
+    from multi_gpu_flashattention_b200.ops.flash import check_errors, flash_attn_fwd, sched_counters
+    monkeypatch.setattr(flash, "FWD_KERNEL", "persistent")
     q, k, v = _inputs(1, 1024, 1024, 8, 8, seed=9)
     s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
     s1.wait_stream(torch.cuda.current_stream())

@@ -46,39 +46,44 @@ def test_public_call_raises_error_of_an_earlier_kernel():
     assert torch.isfinite(o.float()).all()
 
 
-def _drop_signal_public(rank, world):
-    """A dropped signal of the one-launch ring surfaces through
-    mgfa.ring_attention() itself (no check=True, no status argument): the
-    receiving rank's next public call raises, and reset_ring() re-arms the ring
-    on both ranks."""
+def _drop_signal_public(rank, world, backend):
+    """A dropped push signal surfaces through mgfa.ring_attention() itself (no
+    check=True, no status argument): the receiving rank's next public call
+    raises, and reset_ring() re-arms the ring on both ranks. Both fused engines:
+    the per-step ring (one chunk of step 0 never signalled) and the one-launch
+    ring (one part of kv head 0's step-0 unit never signalled)."""
     import multi_gpu_flashattention_b200 as mgfa
     from multi_gpu_flashattention_b200.ops.flash import KernelStatusError, check_errors
-    from multi_gpu_flashattention_b200.parallel.ring import P_ENGINES, reset_ring
+    from multi_gpu_flashattention_b200.parallel.ring import ENGINES, P_ENGINES, reset_ring
     dev = torch.device("cuda", rank)
     g = torch.Generator(device=dev).manual_seed(rank)
     q = (torch.randn(1, 512, 2, 128, device=dev, generator=g) * 0.5).bfloat16()
-    out_ok = mgfa.ring_attention(q, q, q)
+    out_ok = mgfa.ring_attention(q, q, q, backend=backend)
     check_errors()
-    eng = P_ENGINES.get(None, dev, q.numel() * 2)
+    one = backend == "fused_one_launch"
+    eng = (P_ENGINES if one else ENGINES).get(None, dev, q.numel() * 2)
+    drop = (lambda on: eng.set_drop_signal(on)) if one else \
+        (lambda on: eng.set_drop_signal_step(0 if on else -1))
     if rank == 0:
-        eng.set_drop_signal(True)  # rank 1 never hears about one part of kv head 0
-    mgfa.ring_attention(q, q, q)
-    eng.set_drop_signal(False)
+        drop(True)
+    mgfa.ring_attention(q, q, q, backend=backend)
+    drop(False)
     torch.cuda.synchronize()
     if rank == 1:
         with pytest.raises(KernelStatusError, match="peer flag wait timed out"):
-            mgfa.ring_attention(q, q, q)
+            mgfa.ring_attention(q, q, q, backend=backend)
     else:
         check_errors()  # the sending side finished its work
     reset_ring()
-    out = mgfa.ring_attention(q, q, q)
+    out = mgfa.ring_attention(q, q, q, backend=backend)
     check_errors()
     torch.testing.assert_close(out, out_ok, rtol=0, atol=0)
 
 
 @pytest.mark.multigpu
-def test_dropped_signal_raises_through_public_ring_attention():
-    run_ranks(_drop_signal_public, 2, backend="nccl",
+@pytest.mark.parametrize("backend", ["fused", "fused_one_launch"])
+def test_dropped_signal_raises_through_public_ring_attention(backend):
+    run_ranks(_drop_signal_public, 2, backend, backend="nccl",
               env={"NCCL_NVLS_ENABLE": "0", "MGFA_WAIT_LIMIT_NS": "300000000"})
 
 

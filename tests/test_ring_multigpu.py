@@ -41,8 +41,8 @@ def _world():
     return min(torch.cuda.device_count(), int(os.environ.get("MGFA_TEST_MAX_WORLD", "8")))
 
 
-@pytest.mark.parametrize("backend", ["fused", "fused_stepwise", "p2p_unfused", "ce_unfused",
-                                     "nccl"])
+@pytest.mark.parametrize("backend", ["fused", "fused_stepwise", "fused_one_launch", "p2p_unfused",
+                                     "ce_unfused", "nccl"])
 @pytest.mark.parametrize("kind,causal", [("zigzag", True), ("striped", True),
                                          ("contiguous", False), ("contiguous", True)])
 def test_ring_forward_matches_reference(backend, kind, causal):
@@ -56,7 +56,7 @@ def test_ring_forward_cumulative_arrival_counts():
               env={"MGFA_CUMULATIVE_ARRIVALS": "1"})
 
 
-@pytest.mark.parametrize("backend", ["fused", "fused_stepwise"])
+@pytest.mark.parametrize("backend", ["fused_one_launch", "fused_stepwise"])
 def test_ring_forward_scheduler_layout_fused(backend):
     run_ranks(_case, _world(), "scheduler", True, backend, 4096, 2, 2, 2, backend="nccl")
 
@@ -65,7 +65,7 @@ def test_ring_forward_one_launch_gqa_batch_and_many_calls():
     """The one-launch ring with GQA (8 query heads on 2 kv heads), ragged
     striped shards and six calls in a row (slots, arrivals, tags and the call
     credit are reused every call)."""
-    run_ranks(_case, _world(), "striped", True, "fused", 5000, 8, 2, 6, backend="nccl")
+    run_ranks(_case, _world(), "striped", True, "fused_one_launch", 5000, 8, 2, 6, backend="nccl")
 
 
 def _bwd_case(rank, world, kind, causal, bwd_backend="nccl", head_dim=128,
@@ -170,10 +170,10 @@ def _trace_case_one_launch(rank, world):
     dev = torch.device("cuda", rank)
     lay = RingLayout("zigzag", 8192, world, mask="causal")
     q = (torch.randn(1, lay.max_local_len, 4, 128, device=dev) * 0.5).bfloat16()
-    ring_attention_forward(q, q, q, lay, causal=True, backend="fused", check=True)
+    ring_attention_forward(q, q, q, lay, causal=True, backend="fused_one_launch", check=True)
     eng = P_ENGINES.get(None, dev, q.numel() * 2)
     eng.set_trace(True)
-    ring_attention_forward(q, q, q, lay, causal=True, backend="fused", check=True)
+    ring_attention_forward(q, q, q, lay, causal=True, backend="fused_one_launch", check=True)
     eng.set_trace(False)
     tr = eng.last_trace().cpu()
     assert tr.shape == (eng.grid(), 8)
@@ -199,7 +199,7 @@ def _poison_case(rank, world, backend):
     g = torch.Generator(device=dev).manual_seed(rank)
     q = (torch.randn(1, lay.max_local_len, 4, 128, device=dev, generator=g) * 0.5).bfloat16()
     ref, _ = ring_attention_forward(q, q, q, lay, causal=True, backend=backend, check=True)
-    engines = P_ENGINES if backend == "fused" else ENGINES
+    engines = P_ENGINES if backend == "fused_one_launch" else ENGINES
     eng = engines.get(None, dev, q.numel() * 2)
     for _ in range(3):
         torch.cuda.synchronize()
@@ -212,7 +212,7 @@ def _poison_case(rank, world, backend):
         torch.testing.assert_close(out, ref, rtol=0, atol=0)
 
 
-@pytest.mark.parametrize("ring_backend", ["fused", "fused_stepwise"])
+@pytest.mark.parametrize("ring_backend", ["fused_one_launch", "fused_stepwise"])
 def test_ring_forward_poisoned_slots_and_tags(ring_backend):
     run_ranks(_poison_case, _world(), ring_backend, backend="nccl")
 
