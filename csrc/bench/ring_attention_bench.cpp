@@ -65,7 +65,8 @@ namespace mgfa {
 void flash_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, c10::optional<torch::Tensor> o,
                c10::optional<torch::Tensor> o_state, torch::Tensor lse, double scale, bool causal,
                c10::optional<torch::Tensor> q_tile_pos, c10::optional<torch::Tensor> kv_tile_pos,
-               bool merge, bool final_out, torch::Tensor status, int64_t wait_limit_ns);
+               bool merge, bool final_out, torch::Tensor status, int64_t wait_limit_ns,
+               int64_t variant);
 void legacy_partial(torch::Tensor q, torch::Tensor k, torch::Tensor v, double scale,
                     c10::optional<torch::Tensor> q_pos, c10::optional<torch::Tensor> k_pos,
                     bool causal, torch::Tensor acc, torch::Tensor m, torch::Tensor l, bool merge);
@@ -697,7 +698,7 @@ class Bf16Ring {
       mgfa::flash_fwd(q_, cur[0].narrow(1, 0, kl), cur[1].narrow(1, 0, kl), out, o_state, lse,
                       scale_, a_.causal, opt(qtp_),
                       a_.causal ? c10::optional<torch::Tensor>(kvtp_[owner]) : c10::nullopt,
-                      t > 0, t == P - 1, status_, kWaitNs);
+                      t > 0, t == P - 1, status_, kWaitNs, -1);
       if (!more) break;
       if (a_.backend == "nccl") {
         cudaStreamWaitEvent(cs, done.e, 0);

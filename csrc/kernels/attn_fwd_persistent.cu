@@ -53,6 +53,7 @@
 #include "../common/check.hpp"
 #include "attn_fwd_persistent.cuh"
 #include "sm100_ptx.cuh"
+#include "softmax_exp.cuh"
 
 namespace mgfa {
 namespace {
@@ -91,130 +92,6 @@ __device__ __forceinline__ uint32_t sm_id() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%smid;" : "=r"(r));
   return r;
-}
-
-// 2^x for a pair of x on the FMA pipe. Cody-Waite style range reduction
-// x = n + f with n = round(x), f in [-1/2, 1/2] (Cody & Waite, "Software Manual
-// for the Elementary Functions", 1980), the rounding done by adding and
-// subtracting 1.5 * 2^23; 2^f by a degree-3 polynomial whose coefficients were
-// fitted for this project by Lawson's iteratively reweighted least squares on
-// the relative error over [-1/2, 1/2] (max relative error 8.4e-5 in fp32 Horner
-// form, far below the 16-bit rounding the probabilities get next); 2^n by
-// adding n to the exponent field (the low mantissa bits of the rounding sum
-// hold n, and shifting them by 23 moves them there). x is clamped at -126, so
-// the result is at least about 1e-38 (never used for masked columns).
-__device__ __forceinline__ uint64_t exp2_fma2(uint64_t x2) {
-  constexpr float kC0 = 9.999195933e-01f, kC1 = 6.932621598e-01f, kC2 = 2.427141368e-01f,
-                  kC3 = 5.521299317e-02f, kRound = 12582912.0f;  // 1.5 * 2^23
-  float x0, x1;
-  f2_unpack(x2, x0, x1);
-  const uint64_t xc = f2_pack(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
-  const uint64_t t = f2_add(xc, f2_pack(kRound, kRound));
-  const uint64_t n = f2_add(t, f2_pack(-kRound, -kRound));
-  const uint64_t f = f2_fma(n, f2_pack(-1.f, -1.f), xc);
-  uint64_t pv = f2_fma(f2_pack(kC3, kC3), f, f2_pack(kC2, kC2));
-  pv = f2_fma(pv, f, f2_pack(kC1, kC1));
-  pv = f2_fma(pv, f, f2_pack(kC0, kC0));
-  float p0, p1, t0, t1;
-  f2_unpack(pv, p0, p1);
-  f2_unpack(t, t0, t1);
-  return f2_pack(__uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23)),
-                 __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23)));
-}
-
-// 2^x for one x on the FMA pipe: the same method as exp2_fma2, scalar.
-__device__ __forceinline__ float exp2_fma1(float x) {
-  constexpr float kC0 = 9.999195933e-01f, kC1 = 6.932621598e-01f, kC2 = 2.427141368e-01f,
-                  kC3 = 5.521299317e-02f, kRound = 12582912.0f;  // 1.5 * 2^23
-  const float xc = fmaxf(x, -126.f);
-  const float t = xc + kRound;
-  const float f = xc - (t - kRound);
-  const float pv = fmaf(fmaf(fmaf(kC3, f, kC2), f, kC1), f, kC0);
-  return __uint_as_float(__float_as_uint(pv) + (__float_as_uint(t) << 23));
-}
-
-// Probabilities of pairs [c0, c0 + kN) of a row (pair c = keys 2c, 2c+1):
-// p = 2^(s * scale - m), summed into the row-sum accumulators and packed to
-// 16-bit pairs (pk[c - c0]) for the PV MMA. kPacked uses the f32x2
-// instructions (two lanes of work per instruction); kPoly8 of every 8 pairs go
-// through the FMA-pipe polynomial instead of MUFU.EX2. With kMax the loop also
-// folds 128 / (2 kN) * 2 further raw scores per pair into `mx` (four running
-// maxima), so the row max of all 128 scores is computed alongside.
-template <bool kF16, int kPoly8, bool kPacked, int kN, bool kMax = false>
-__device__ __forceinline__ void exp_pairs(const uint32_t (&sr)[128], int c0, float scale,
-                                          float neg_m, uint32_t* pk, float (&lacc)[4],
-                                          float (&mx)[4]) {
-  constexpr int kPer = 128 / kN;  // raw scores folded into the max per pair step
-  if constexpr (kPacked) {
-    const uint64_t sc2 = f2_pack(scale, scale), nm2 = f2_pack(neg_m, neg_m);
-    uint64_t acc0 = f2_pack(0.f, 0.f), acc1 = f2_pack(0.f, 0.f);
-#pragma unroll
-    for (int cc = 0; cc < kN; ++cc) {
-      const int c = c0 + cc;
-      if constexpr (kMax) {
-        const float* f = reinterpret_cast<const float*>(sr) + kPer * cc;
-#pragma unroll
-        for (int u = 0; u < kPer; u += 2) mx[(u >> 1) & 3] = max3f(mx[(u >> 1) & 3], f[u], f[u + 1]);
-      }
-      const uint64_t x2 = f2_fma(
-          f2_pack(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), sc2, nm2);
-      uint64_t e2;
-      if ((cc & 7) >= 8 - kPoly8) {
-        e2 = exp2_fma2(x2);
-      } else {
-        float a, b;
-        f2_unpack(x2, a, b);
-        e2 = f2_pack(ex2_approx(a), ex2_approx(b));
-      }
-      if (cc & 1) acc1 = f2_add(acc1, e2);
-      else acc0 = f2_add(acc0, e2);
-      float e0, e1;
-      f2_unpack(e2, e0, e1);
-      pk[cc] = pack16<kF16>(e0, e1);
-    }
-    float a0, a1, b0, b1;
-    f2_unpack(acc0, a0, a1);
-    f2_unpack(acc1, b0, b1);
-    lacc[0] += a0;
-    lacc[1] += a1;
-    lacc[2] += b0;
-    lacc[3] += b1;
-  } else {
-#pragma unroll
-    for (int cc = 0; cc < kN; ++cc) {
-      const int c = c0 + cc;
-      if constexpr (kMax) {
-        const float* f = reinterpret_cast<const float*>(sr) + kPer * cc;
-#pragma unroll
-        for (int u = 0; u < kPer; u += 2) mx[(u >> 1) & 3] = max3f(mx[(u >> 1) & 3], f[u], f[u + 1]);
-      }
-      const float x0 = fmaf(__uint_as_float(sr[2 * c]), scale, neg_m);
-      const float x1 = fmaf(__uint_as_float(sr[2 * c + 1]), scale, neg_m);
-      float p0, p1;
-      if ((cc & 7) >= 8 - kPoly8) {
-        p0 = exp2_fma1(x0);
-        p1 = exp2_fma1(x1);
-      } else {
-        p0 = ex2_approx(x0);
-        p1 = ex2_approx(x1);
-      }
-      if (cc & 1) {
-        lacc[2] += p0;
-        lacc[3] += p1;
-      } else {
-        lacc[0] += p0;
-        lacc[1] += p1;
-      }
-      pk[cc] = pack16<kF16>(p0, p1);
-    }
-  }
-}
-
-template <bool kF16, int kPoly8, bool kPacked>
-__device__ __forceinline__ void exp_half(const uint32_t (&sr)[128], int half, float scale,
-                                         float neg_m, uint32_t (&pk)[32], float (&lacc)[4]) {
-  float unused[4];
-  exp_pairs<kF16, kPoly8, kPacked, 32, false>(sr, half * 32, scale, neg_m, pk, lacc, unused);
 }
 
 // Phase profile of the kernel variant with bit 10 of the tune word set: per CTA

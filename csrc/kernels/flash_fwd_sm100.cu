@@ -16,9 +16,18 @@
 //              P read from TMEM where it overwrote S)
 //   warps 10-11 ring push (only when a RingPush is enabled)
 // TMEM (512 columns): S0/P0 [0,128) S1/P1 [128,256) O0 [256,384) O1 [384,512).
-// The MMA order S0(j+1) after PV0(j) and S1(j+1) after PV1(j) lets one softmax
-// warpgroup work while the tensor core runs the other tile's GEMMs; a commit
-// for S(j+1) also proves PV(j) finished, so softmax may rescale O right away.
+// Two pipelines (template kVar):
+//   kVar 0, whole tiles: S_t(j) fills its 128 columns, P_t(j) overwrites it,
+//     and the MMA order S0(j+1) after PV0(j), S1(j+1) after PV1(j) lets one
+//     softmax warpgroup work while the tensor core runs the other tile's GEMMs.
+//     A softmax warpgroup waits for PV_t(j) and S_t(j+1) after every tile.
+//   kVar 1-2, half tiles: the 128 columns of tile t are two 64-key slots;
+//     S_t(j, h) (N = 64) lands in slot h, P_t(j, h) overwrites it, and
+//     S_t(j+1, h) is issued right after PV_t(j, h). While the softmax works on
+//     half 1 of key tile j, the tensor core runs PV(j, 0) and S(j+1, 0), so
+//     the next half is ready when the softmax gets to it: both warpgroups run
+//     continuously instead of waiting for their own GEMMs. kVar 2 computes 2
+//     of every 8 exponential pairs on the FMA pipe (softmax_exp.cuh).
 // O is rescaled only when the running max grows by more than 2^8 (the stale
 // max keeps P <= 256, exact in fp32 sums and bf16 P).
 #include <torch/types.h>
@@ -26,9 +35,11 @@
 #include <ATen/cuda/CUDAContext.h>
 
 #include <cmath>
+#include <cstdlib>
 
 #include "flash_fwd_sm100.cuh"
 #include "sm100_ptx.cuh"
+#include "softmax_exp.cuh"
 #include "ring_push.cuh"
 #include "tma_host.hpp"
 
@@ -42,6 +53,7 @@ constexpr int kHalfBytes = kTile * 64 * 2;   // one 128 x 64 16-bit swizzled box
 constexpr int kWarps = 12;
 constexpr int kThreads = kWarps * 32;
 constexpr float kRescaleThreshold = 8.0f;    // log2 units
+constexpr int kDefaultFwdVariant = 0;
 
 // kD = head_dim (64 or 128) is kD / 64 swizzled 64-column boxes per 128-row tile.
 template <int kD>
@@ -54,6 +66,8 @@ struct __align__(1024) FwdSmem {
   uint64_t k_full[2], k_empty[2];
   uint64_t v_full[2], v_empty[2];
   uint64_t s_full[2], p_full[2];
+  uint64_t sh_full[2][2], ph_full[2][2];  // half-tile pipeline: [query tile][slot]
+  uint64_t o_done[2];                     // half-tile pipeline: one phase per PV_t
   uint64_t o_full;
   uint64_t drain;
   uint64_t trace[kTraceWords];
@@ -68,8 +82,9 @@ __device__ __forceinline__ uint32_t sm_id() {
 }
 
 // ------------------------------------------------------------------ kernel
-// kD: head_dim (64 or 128); kF16: fp16 inputs/outputs (else bf16).
-template <int kD, bool kF16>
+// kD: head_dim (64 or 128); kF16: fp16 inputs/outputs (else bf16); kVar: the
+// pipeline (0 whole tiles, 1 half tiles, 2 half tiles with FMA-pipe exponentials).
+template <int kD, bool kF16, int kVar>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap map_q,
                      const __grid_constant__ CUtensorMap map_k,
@@ -78,6 +93,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kTileBytes = kHalves * kHalfBytes;  // one 128 x kD tile
   constexpr int kKSteps = kD / 16;                  // MMA K steps of S = Q K^T
   constexpr int kOChunks = kD / 32;                 // 32-column TMEM chunks of O
+  constexpr bool kHalfPipe = kVar >= 1;
+  constexpr int kPoly8 = kVar == 2 ? 2 : 0;
   extern __shared__ uint8_t smem_raw[];
   FwdSmem<kD>& s = *reinterpret_cast<FwdSmem<kD>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -125,6 +142,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s.v_empty[i], 1);
       mbar_init(&s.s_full[i], 1);
       mbar_init(&s.p_full[i], 4);  // one arrive per softmax warp
+      for (int hh = 0; hh < 2; ++hh) {
+        mbar_init(&s.sh_full[i][hh], 1);
+        mbar_init(&s.ph_full[i][hh], 4);
+      }
+      mbar_init(&s.o_done[i], 1);
     }
     mbar_init(&s.o_full, 1);
     mbar_init(&s.drain, 1);
@@ -212,17 +234,77 @@ __global__ void __launch_bounds__(kThreads, 1)
                  (acc || kk > 0) ? 1u : 0u);
         }
       };
+      // half-tile pipeline: S_t(j, hh) = Q_t K(j)[64 hh, 64 hh + 64)^T into slot hh
+      const uint32_t idesc_s64 = make_idesc_16(128, 64, 0, 0, kF16);
+      auto issue_s_half = [&](int t, int st, int hh) {
+        const uint32_t kb = smem_u32(s.k[st][0]) + uint32_t(hh) * 64 * 128;
+#pragma unroll
+        for (int kk = 0; kk < kKSteps; ++kk) {
+          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+          mma_ss(tmem + t * 128 + hh * 64, make_sdesc_sw128(q_base[t] + off, 16, 1024),
+                 make_sdesc_sw128(kb + off, 16, 1024), idesc_s64, kk > 0);
+        }
+      };
+      // O_t += P_t(j, hh) V(j)[64 hh, 64 hh + 64)
+      auto issue_o_half = [&](int t, int st, int hh, uint32_t acc) {
+        const uint32_t vb = smem_u32(s.v[st][0]);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_ts(tmem + kOCol + t * kD, tmem + t * 128 + hh * 64 + kk * 8,
+                 make_sdesc_sw128(vb + (hh * 4 + kk) * 2048, kHalfBytes, 1024), idesc_o,
+                 (acc || kk > 0) ? 1u : 0u);
+      };
       bool ok = mbar_wait(&s.q_full, 0, ab, 90);
       if (ok) ok = mbar_wait(&s.k_full[0], 0, ab, 91);
       if (ok) {
         tc_fence_after();
-        issue_s(0, 0);
-        mma_commit(&s.s_full[0]);
-        issue_s(1, 0);
-        mma_commit(&s.s_full[1]);
+        if constexpr (kHalfPipe) {
+          for (int hh = 0; hh < 2; ++hh)
+            for (int t = 0; t < 2; ++t) {
+              issue_s_half(t, 0, hh);
+              mma_commit(&s.sh_full[t][hh]);
+            }
+        } else {
+          issue_s(0, 0);
+          mma_commit(&s.s_full[0]);
+          issue_s(1, 0);
+          mma_commit(&s.s_full[1]);
+        }
         mma_commit(&s.k_empty[0]);
       }
-      for (int it = 0; ok && it < n_active; ++it) {
+      // Half tiles: PV_0(j,0) S_0(j+1,0) PV_1(j,0) S_1(j+1,0) PV_0(j,1) S_0(j+1,1)
+      // PV_1(j,1) S_1(j+1,1). S_t(j+1, hh) reuses slot hh right after the PV that
+      // read P_t(j, hh) from it (the tensor core runs them in issue order).
+      for (int it = 0; kHalfPipe && ok && it < n_active; ++it) {
+        const int st = it & 1;
+        const uint32_t ph = (it >> 1) & 1;
+        const int st1 = (it + 1) & 1;
+        const uint32_t ph1 = ((it + 1) >> 1) & 1;
+        const bool more = it + 1 < n_active;
+        if (!(ok = mbar_wait(&s.v_full[st], ph, ab, 92))) break;
+        bool k_next = false;
+        for (int hh = 0; ok && hh < 2; ++hh) {
+          for (int t = 0; t < 2; ++t) {
+            if (!(ok = mbar_wait(&s.ph_full[t][hh], it & 1, ab, 93 + t))) break;
+            tc_fence_after();
+            issue_o_half(t, st, hh, (it > 0 || hh > 0) ? 1u : 0u);
+            mma_commit(&s.o_done[t]);
+            if (more) {
+              if (!k_next) {
+                if (!(ok = mbar_wait(&s.k_full[st1], ph1, ab, 96))) break;
+                tc_fence_after();
+                k_next = true;
+              }
+              issue_s_half(t, st1, hh);
+              mma_commit(&s.sh_full[t][hh]);
+            }
+          }
+        }
+        if (!ok) break;
+        mma_commit(&s.v_empty[st]);
+        if (more) mma_commit(&s.k_empty[st1]);
+      }
+      for (int it = 0; !kHalfPipe && ok && it < n_active; ++it) {
         const int st = it & 1;
         const uint32_t ph = (it >> 1) & 1;
         const int st1 = (it + 1) & 1;
@@ -280,7 +362,88 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!q_valid_tile) full_hi = 0;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int it = 0; !skip_compute && it < n_active; ++it) {
+    // ---- half-tile pipeline: 64 keys per step, slot hh of this tile's columns
+    for (int it = 0; kHalfPipe && !skip_compute && it < n_active; ++it) {
+      const bool full = it < full_hi;  // warp-uniform
+      int n_vis = 128;
+      if (!full) {  // diagonal / ragged / invisible tile: this row's visible keys
+        n_vis = p.sk - it * kTile;
+        if (p.causal) {
+          const int lim = q_pos - __ldg(p.kv_tile_pos + it) + 1;
+          n_vis = lim < n_vis ? lim : n_vis;
+        }
+        if (!q_valid_tile) n_vis = 0;
+      }
+#pragma unroll 1
+      for (int hh = 0; hh < 2; ++hh) {
+        const int kidx = 2 * it + hh;  // PV_t steps so far
+        ok = __all_sync(0xffffffffu, mbar_wait(&s.sh_full[t][hh], it & 1, ab, 20 + t));
+        if (!ok) break;
+        tc_fence_after();
+        uint32_t sr[64];
+        tmem_ld32(s_addr + hh * 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+        tmem_ld32(s_addr + hh * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+        tmem_wait_ld();
+        regs_defined32(&sr[0]);
+        regs_defined32(&sr[32]);
+        if (!full) {
+          const int nv = n_vis - hh * 64;
+#pragma unroll
+          for (int c = 0; c < 64; ++c)
+            if (c >= nv) sr[c] = 0xff800000u;  // -inf
+        }
+        const float tmax = row_max<64>(sr) * p.scale_log2;
+        const float m_new = fmaxf(m, tmax);
+        float alpha = 1.f;
+        bool rescale = false;
+        if (kidx == 0) {
+          m = m_new;
+        } else if (m_new > m + kRescaleThreshold) {
+          alpha = ex2_approx(m - m_new);
+          m = m_new;
+          rescale = true;
+        }
+        const float neg_m = (m == -INFINITY) ? 0.f : -m;
+        float lacc[4] = {0.f, 0.f, 0.f, 0.f}, unused[4];
+        uint32_t pk[32];
+        if (kPoly8 > 0 && full)
+          exp_pairs<kF16, kPoly8, true, 32>(sr, 0, p.scale_log2, neg_m, pk, lacc, unused);
+        else
+          exp_pairs<kF16, 0, true, 32>(sr, 0, p.scale_log2, neg_m, pk, lacc, unused);
+        tmem_st32(s_addr + hh * 64, pk);
+        // PV_t of the previous step must have finished: O is rescaled below, and
+        // waiting on every phase keeps the parity of o_done exact.
+        if (kidx > 0) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&s.o_done[t], (kidx - 1) & 1, ab, 24 + t));
+          if (!ok) break;
+        }
+        if (__any_sync(0xffffffffu, rescale)) {
+          tc_fence_after();
+#pragma unroll
+          for (int ch = 0; ch < kOChunks; ++ch) {
+            uint32_t orow[32];
+            tmem_ld32(o_addr + ch * 32, orow);
+            tmem_wait_ld();
+            regs_defined32(orow);
+#pragma unroll
+            for (int c = 0; c < 32; ++c)
+              orow[c] = __float_as_uint(__uint_as_float(orow[c]) * alpha);
+            tmem_st32(o_addr + ch * 32, orow);
+            tmem_wait_st();
+            regs_live32(orow);
+          }
+        }
+        tmem_wait_st();
+        regs_live32(pk);
+        tc_fence_before();
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) mbar_arrive(&s.ph_full[t][hh]);
+        l = l * alpha + ((lacc[0] + lacc[1]) + (lacc[2] + lacc[3]));
+      }
+      if (!ok) break;
+    }
+    // ---- whole-tile pipeline
+    for (int it = 0; !kHalfPipe && !skip_compute && it < n_active; ++it) {
       ok = __all_sync(0xffffffffu, mbar_wait(&s.s_full[t], it & 1, ab, 20 + t));
       if (!ok) break;
       tc_fence_after();
@@ -503,21 +666,38 @@ struct FwdVariant {
   FwdKernelFn fn;
   int smem;
 };
-FwdVariant fwd_variant(int head_dim, bool fp16) {
-  if (head_dim == 64)
-    return fp16 ? FwdVariant{flash_fwd_kernel<64, true>, int(sizeof(FwdSmem<64>) + 1024)}
-                : FwdVariant{flash_fwd_kernel<64, false>, int(sizeof(FwdSmem<64>) + 1024)};
-  return fp16 ? FwdVariant{flash_fwd_kernel<128, true>, int(sizeof(FwdSmem<128>) + 1024)}
-              : FwdVariant{flash_fwd_kernel<128, false>, int(sizeof(FwdSmem<128>) + 1024)};
+template <int kD, bool kF16>
+FwdVariant fwd_variant_d(int var) {
+  constexpr int smem = int(sizeof(FwdSmem<kD>) + 1024);
+  switch (var) {
+    case 0: return FwdVariant{flash_fwd_kernel<kD, kF16, 0>, smem};
+    case 1: return FwdVariant{flash_fwd_kernel<kD, kF16, 1>, smem};
+    default: return FwdVariant{flash_fwd_kernel<kD, kF16, 2>, smem};
+  }
+}
+FwdVariant fwd_variant(int head_dim, bool fp16, int var) {
+  if (head_dim == 64) return fp16 ? fwd_variant_d<64, true>(var) : fwd_variant_d<64, false>(var);
+  return fp16 ? fwd_variant_d<128, true>(var) : fwd_variant_d<128, false>(var);
+}
+// Pipeline of FwdParams::variant -1: MGFA_FWD_VARIANT (0, 1 or 2), else kDefaultFwdVariant.
+int default_fwd_variant() {
+  static const int v = [] {
+    const char* e = std::getenv("MGFA_FWD_VARIANT");
+    if (e && e[0] >= '0' && e[0] <= '2' && e[1] == 0) return e[0] - '0';
+    return kDefaultFwdVariant;
+  }();
+  return v;
 }
 }  // namespace
 
 void flash_fwd_launch_maps(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                            FwdParams& p, cudaStream_t stream) {
   MGFA_CHECK(p.head_dim == 64 || p.head_dim == 128, "head_dim must be 64 or 128");
-  static int attr_device[4] = {-1, -1, -1, -1};
-  const FwdVariant var = fwd_variant(p.head_dim, p.fp16 != 0);
-  const int vi = (p.head_dim == 64 ? 0 : 2) + (p.fp16 ? 1 : 0);
+  static int attr_device[12] = {-1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1};
+  if (p.variant < 0) p.variant = default_fwd_variant();
+  MGFA_CHECK(p.variant <= 2, "forward variant must be 0, 1 or 2");
+  const FwdVariant var = fwd_variant(p.head_dim, p.fp16 != 0, p.variant);
+  const int vi = ((p.head_dim == 64 ? 0 : 2) + (p.fp16 ? 1 : 0)) * 3 + p.variant;
   int dev = 0;
   C10_CUDA_CHECK(cudaGetDevice(&dev));
   if (attr_device[vi] != dev) {

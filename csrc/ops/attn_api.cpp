@@ -57,7 +57,8 @@ const int* tile_pos_ptr(const c10::optional<torch::Tensor>& t, int n, const char
 void flash_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, c10::optional<torch::Tensor> o,
                c10::optional<torch::Tensor> o_state, torch::Tensor lse, double scale, bool causal,
                c10::optional<torch::Tensor> q_tile_pos, c10::optional<torch::Tensor> kv_tile_pos,
-               bool merge, bool final_out, torch::Tensor status, int64_t wait_limit_ns) {
+               bool merge, bool final_out, torch::Tensor status, int64_t wait_limit_ns,
+               int64_t variant) {
   check_bshd(q, "q");
   check_bshd(k, "k");
   check_bshd(v, "v");
@@ -120,6 +121,8 @@ void flash_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, c10::optional<
   p.final_out = final_out ? 1 : 0;
   p.status = reinterpret_cast<uint32_t*>(status.data_ptr<int>());
   p.wait_limit_ns = uint64_t(wait_limit_ns);
+  MGFA_CHECK(variant >= -1 && variant <= 2, "variant must be -1, 0, 1 or 2");
+  p.variant = int(variant);
   if (Sq == 0 || B == 0) return;
   flash_fwd_launch(q, k, v, p, at::cuda::getCurrentCUDAStream());
 }

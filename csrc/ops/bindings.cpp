@@ -6,7 +6,8 @@ std::vector<torch::Tensor> umma_probe(torch::Tensor a, torch::Tensor b, torch::T
 void flash_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, c10::optional<torch::Tensor> o,
                c10::optional<torch::Tensor> o_state, torch::Tensor lse, double scale, bool causal,
                c10::optional<torch::Tensor> q_tile_pos, c10::optional<torch::Tensor> kv_tile_pos,
-               bool merge, bool final_out, torch::Tensor status, int64_t wait_limit_ns);
+               bool merge, bool final_out, torch::Tensor status, int64_t wait_limit_ns,
+               int64_t variant);
 size_t flash_fwd_smem_bytes();
 void flash_fwd_persistent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
                           torch::Tensor lse, double scale, bool causal,
@@ -44,7 +45,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_fwd", &mgfa::flash_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"),
         py::arg("o_state"), py::arg("lse"), py::arg("scale"), py::arg("causal"),
         py::arg("q_tile_pos"), py::arg("kv_tile_pos"), py::arg("merge"), py::arg("final_out"),
-        py::arg("status"), py::arg("wait_limit_ns") = int64_t(2000000000));
+        py::arg("status"), py::arg("wait_limit_ns") = int64_t(2000000000),
+        py::arg("variant") = int64_t(-1));
   m.def("flash_fwd_smem_bytes", &mgfa::flash_fwd_smem_bytes);
   m.def("flash_fwd_persistent", &mgfa::flash_fwd_persistent, py::arg("q"), py::arg("k"),
         py::arg("v"), py::arg("o"), py::arg("lse"), py::arg("scale"), py::arg("causal"),

@@ -1,9 +1,12 @@
 """Forward-kernel variant sweep on one GPU (CUDA-event timing, L2 flushed
-between launches): the per-query-tile-pair kernel (flash_fwd_sm100.cu) against
-the persistent kernel (attn_fwd_persistent.cu) in each of its softmax variants.
+between launches): the per-query-tile-pair kernel (flash_fwd_sm100.cu) in each
+of its pipelines (--variants: 0 whole tiles, 1 half tiles, 2 half tiles with
+FMA-pipe exponentials) against the persistent kernel (attn_fwd_persistent.cu)
+in each of its softmax variants.
 
     python -m multi_gpu_flashattention_b200.benchmarks.fwd_tuning [--seq 131072]
-        [--heads 32] [--kv-heads 32] [--no-causal] [--reps 5] [--tunes 0x002,0x302,...]
+        [--heads 32] [--kv-heads 32] [--no-causal] [--reps 5] [--variants 0,1,2]
+        [--tunes=0x002,0x302,...]   (--tunes= with no value: stepwise only)
 
 A tune value is the persistent kernel's variant word (attn_fwd_persistent.cuh):
 bits 0-7 exponential pairs of every 8 on the FMA pipe (0, 2 or 4), bit 8 packed
@@ -33,6 +36,7 @@ def main(argv=None):
     ap.add_argument("--no-causal", action="store_true")
     ap.add_argument("--reps", type=int, default=5)
     ap.add_argument("--tunes", default=DEFAULT_TUNES)
+    ap.add_argument("--variants", default="0,1,2")
     ap.add_argument("--profile", default=None,
                     help="comma-separated tune values to profile by phase instead")
     a = ap.parse_args(argv)
@@ -52,9 +56,9 @@ def main(argv=None):
     pairs = S * (S + 1) // 2 if causal else S * S
     flops = 4.0 * D * H * pairs
 
-    def stepwise():
-        C().flash_fwd(q, k, v, o, None, lse, scale, causal, pos, pos, False, True, st,
-                      2_000_000_000)
+    def stepwise(variant):
+        return lambda: C().flash_fwd(q, k, v, o, None, lse, scale, causal, pos, pos, False,
+                                     True, st, 2_000_000_000, variant)
 
     def persistent(tune):
         return lambda: C().flash_fwd_persistent(q, k, v, o, lse, scale, causal, pos, pos, st,
@@ -87,8 +91,8 @@ def main(argv=None):
             print(json.dumps(rec), flush=True)
         return 0
 
-    cases = [("stepwise", None, stepwise)]
-    for t in a.tunes.split(","):
+    cases = [("stepwise", int(vr), stepwise(int(vr))) for vr in a.variants.split(",") if vr]
+    for t in filter(None, a.tunes.split(",")):
         tv = int(t, 0)
         cases.append(("persistent", tv, persistent(tv)))
     for name, tune, fn in cases:
@@ -106,8 +110,9 @@ def main(argv=None):
         if int(st.item()) != 0:
             raise SystemExit(f"{name} {tune}: kernel status {int(st.item()):#x}")
         ms = statistics.median(times)
-        print(json.dumps({"kernel": name, "tune": None if tune is None else hex(tune) if tune >= 0
-                          else -1, "seq": S, "heads": H, "causal": causal, "ms": round(ms, 3),
+        label = tune if name == "stepwise" else hex(tune) if tune >= 0 else -1
+        print(json.dumps({"kernel": name, "variant" if name == "stepwise" else "tune": label,
+                          "seq": S, "heads": H, "causal": causal, "ms": round(ms, 3),
                           "tflops": round(flops / ms / 1e9, 1)}), flush=True)
     return 0
 
