@@ -565,7 +565,7 @@ class Bf16Ring {
       const char* tc = std::getenv("MGFA_TAG_CHECK");
       eng_->set_tag_check(!(tc && std::string(tc) == "0"));
       const char* ca = std::getenv("MGFA_CUMULATIVE_ARRIVALS");
-      eng_->set_cumulative_arrivals(ca && std::string(ca) == "1");
+      eng_->set_cumulative_arrivals(!(ca && std::string(ca) == "0"));
       eng_->connect(d.all_gather(eng_->ipc_handle()));
       eng_->set_transport_mode(a.backend == "fused" || a.backend == "fused_stepwise"
                                    ? mgfa::RingEngine::kFusedPush

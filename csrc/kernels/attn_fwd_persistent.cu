@@ -21,13 +21,14 @@
 //   warps 10-11 ring push (ring launches only)
 // TMEM (512 columns): S0/P0 [0,128) S1/P1 [128,256) O0 [256,256+D) O1 after it.
 // Pipeline per key tile: PV0(j) S0(j+1) PV1(j) S1(j+1), so one softmax
-// warpgroup works while the tensor core runs the other tile's GEMMs. P is
-// handed over in two 64-key halves: the PV MMAs on the first half start while
-// the softmax warps still exponentiate the second. A fraction of the
-// exponentials (kPoly8 of every 8 pairs, full tiles only) runs as a polynomial
-// on the FMA pipe instead of the MUFU unit, whose throughput otherwise equals
-// the tensor core's demand at head_dim 128. O is rescaled only when the running
-// max grows by more than 2^8.
+// warpgroup works while the tensor core runs the other tile's GEMMs. The
+// default softmax uses packed f32x2 arithmetic; template variants hand P over
+// in two 64-key halves (the PV MMAs on the first half start while the softmax
+// warps still exponentiate the second) or run a fraction of the exponentials
+// (kPoly8 of every 8 pairs, full tiles only) as a polynomial on the FMA pipe
+// instead of the MUFU unit. Both measured slower under the 1 kW power cap and
+// stay selectable for tuning. O is rescaled only when the running max grows by
+// more than 2^8.
 //
 // Ring launches (PRing::enabled): segment s >= 1 sits in this rank's receive
 // slot s; the producer waits (bounded, system-scope acquire) for unit
@@ -893,8 +894,8 @@ bool getenv_flag_off(const char* name) {
 using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap,
                           const CUtensorMap, const PFwdParams);
 
-constexpr int kDefaultPoly8 = 2;
-constexpr int kDefaultVar = 3;
+constexpr int kDefaultPoly8 = 0;
+constexpr int kDefaultVar = 1;
 
 // poly8 / variant tuning space (head_dim 128 bf16 without the ring); every
 // other combination runs the defaults.
@@ -922,7 +923,7 @@ KernelFn pick_poly(int poly8, int var) {
   if constexpr (kD == 128 && !kF16 && !kRing) {
     if (poly8 == 0) return pick_var<0>(var);
     if (poly8 == 4) return pick_var<4>(var);
-    if (poly8 == 2 || poly8 < 0) return pick_var<2>(var);
+    if (poly8 == 2) return pick_var<2>(var);
   }
   if constexpr (kD == 128 && !kF16 && kRing) {
     if (poly8 == 0 && var == 1) return attn_fwd_persistent_kernel<128, false, 0, true, 1>;

@@ -91,7 +91,10 @@ struct PFwdParams {
 // layout in attn_fwd_persistent.cu), bit 11 computes the row max as a shallow
 // tree, bit 12 computes the first half's exponentials speculatively against
 // the running max, bit 13 hides the first P store's wait behind the next
-// exponentials; negative means the default.
+// exponentials; negative means the default (0x100: packed f32x2 arithmetic,
+// every exponential on MUFU, P handed over whole, which measured fastest at
+// 32K-128K tokens under the power cap: the polynomial and the split hand-over
+// add instructions that cost more clock than they save).
 void attn_fwd_persistent_launch(const CUtensorMap& mq, const CUtensorMap& mk,
                                 const CUtensorMap& mv, const CUtensorMap& mslots, int head_dim,
                                 bool fp16, PFwdParams& p, int grid, int tune,

@@ -16,18 +16,19 @@
 //              P read from TMEM where it overwrote S)
 //   warps 10-11 ring push (only when a RingPush is enabled)
 // TMEM (512 columns): S0/P0 [0,128) S1/P1 [128,256) O0 [256,384) O1 [384,512).
-// Two pipelines (template kVar):
-//   kVar 0, whole tiles: S_t(j) fills its 128 columns, P_t(j) overwrites it,
-//     and the MMA order S0(j+1) after PV0(j), S1(j+1) after PV1(j) lets one
-//     softmax warpgroup work while the tensor core runs the other tile's GEMMs.
-//     A softmax warpgroup waits for PV_t(j) and S_t(j+1) after every tile.
-//   kVar 1-2, half tiles: the 128 columns of tile t are two 64-key slots;
+// Pipelines (template kVar):
+//   kVar 0, whole tiles (the default): S_t(j) fills its 128 columns, P_t(j)
+//     overwrites it, and the MMA order S0(j+1) after PV0(j), S1(j+1) after
+//     PV1(j) lets one softmax warpgroup work while the tensor core runs the
+//     other tile's GEMMs. The softmax uses packed f32x2 FMAs and adds (one
+//     instruction per pair of scores).
+//   kVar 2: kVar 0 with scalar fp32 softmax arithmetic.
+//   kVar 1, half tiles: the 128 columns of tile t are two 64-key slots;
 //     S_t(j, h) (N = 64) lands in slot h, P_t(j, h) overwrites it, and
-//     S_t(j+1, h) is issued right after PV_t(j, h). While the softmax works on
-//     half 1 of key tile j, the tensor core runs PV(j, 0) and S(j+1, 0), so
-//     the next half is ready when the softmax gets to it: both warpgroups run
-//     continuously instead of waiting for their own GEMMs. kVar 2 computes 2
-//     of every 8 exponential pairs on the FMA pipe (softmax_exp.cuh).
+//     S_t(j+1, h) is issued right after PV_t(j, h), so the next half is
+//     computed while the softmax works on the current one. Measured slower
+//     than kVar 0 on B200 (twice the S instructions at N = 64 and twice the
+//     hand-overs outweigh the overlap), kept for comparison.
 // O is rescaled only when the running max grows by more than 2^8 (the stale
 // max keeps P <= 256, exact in fp32 sums and bf16 P).
 #include <torch/types.h>
@@ -67,7 +68,7 @@ struct __align__(1024) FwdSmem {
   uint64_t v_full[2], v_empty[2];
   uint64_t s_full[2], p_full[2];
   uint64_t sh_full[2][2], ph_full[2][2];  // half-tile pipeline: [query tile][slot]
-  uint64_t o_done[2];                     // half-tile pipeline: one phase per PV_t
+  uint64_t o_done[2][2];  // half-tile pipeline: [query tile][key half], one phase per tile
   uint64_t o_full;
   uint64_t drain;
   uint64_t trace[kTraceWords];
@@ -83,7 +84,7 @@ __device__ __forceinline__ uint32_t sm_id() {
 
 // ------------------------------------------------------------------ kernel
 // kD: head_dim (64 or 128); kF16: fp16 inputs/outputs (else bf16); kVar: the
-// pipeline (0 whole tiles, 1 half tiles, 2 half tiles with FMA-pipe exponentials).
+// pipeline (0 whole tiles, 1 half tiles, 2 whole tiles with scalar fp32 softmax).
 template <int kD, bool kF16, int kVar>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap map_q,
@@ -93,8 +94,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kTileBytes = kHalves * kHalfBytes;  // one 128 x kD tile
   constexpr int kKSteps = kD / 16;                  // MMA K steps of S = Q K^T
   constexpr int kOChunks = kD / 32;                 // 32-column TMEM chunks of O
-  constexpr bool kHalfPipe = kVar >= 1;
-  constexpr int kPoly8 = kVar == 2 ? 2 : 0;
+  constexpr bool kHalfPipe = kVar == 1;
+  constexpr bool kPackedExp = kVar != 2;
   extern __shared__ uint8_t smem_raw[];
   FwdSmem<kD>& s = *reinterpret_cast<FwdSmem<kD>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -146,7 +147,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(&s.sh_full[i][hh], 1);
         mbar_init(&s.ph_full[i][hh], 4);
       }
-      mbar_init(&s.o_done[i], 1);
+      mbar_init(&s.o_done[i][0], 1);
+      mbar_init(&s.o_done[i][1], 1);
     }
     mbar_init(&s.o_full, 1);
     mbar_init(&s.drain, 1);
@@ -288,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!(ok = mbar_wait(&s.ph_full[t][hh], it & 1, ab, 93 + t))) break;
             tc_fence_after();
             issue_o_half(t, st, hh, (it > 0 || hh > 0) ? 1u : 0u);
-            mma_commit(&s.o_done[t]);
+            mma_commit(&s.o_done[t][hh]);
             if (more) {
               if (!k_next) {
                 if (!(ok = mbar_wait(&s.k_full[st1], ph1, ab, 96))) break;
@@ -406,18 +408,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float neg_m = (m == -INFINITY) ? 0.f : -m;
         float lacc[4] = {0.f, 0.f, 0.f, 0.f}, unused[4];
         uint32_t pk[32];
-        if (kPoly8 > 0 && full)
-          exp_pairs<kF16, kPoly8, true, 32>(sr, 0, p.scale_log2, neg_m, pk, lacc, unused);
-        else
-          exp_pairs<kF16, 0, true, 32>(sr, 0, p.scale_log2, neg_m, pk, lacc, unused);
+        exp_pairs<kF16, 0, true, 32>(sr, 0, p.scale_log2, neg_m, pk, lacc, unused);
         tmem_st32(s_addr + hh * 64, pk);
-        // PV_t of the previous step must have finished: O is rescaled below, and
-        // waiting on every phase keeps the parity of o_done exact.
+        // O may only be rescaled once PV_t of the previous half step has
+        // finished (o_done[t][hh ^ 1], phase `it` after half 0, `it - 1` after
+        // half 1). The wait runs at every step, so every phase of both barriers
+        // is waited for in order and the parity never aliases.
+        const bool resc = __any_sync(0xffffffffu, rescale);
         if (kidx > 0) {
-          ok = __all_sync(0xffffffffu, mbar_wait(&s.o_done[t], (kidx - 1) & 1, ab, 24 + t));
+          const uint32_t par = uint32_t(hh ? it : it - 1) & 1u;
+          ok = __all_sync(0xffffffffu, mbar_wait(&s.o_done[t][hh ^ 1], par, ab, 24 + t));
           if (!ok) break;
         }
-        if (__any_sync(0xffffffffu, rescale)) {
+        if (resc) {
           tc_fence_after();
 #pragma unroll
           for (int ch = 0; ch < kOChunks; ++ch) {
@@ -496,21 +499,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float m_use = (m == -INFINITY) ? 0.f : m;
       l *= alpha;
       const float neg_m = -m_use;
-      float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
       uint32_t pk[2][32];
+      if constexpr (kPackedExp) {
+        // f32x2 arithmetic: one FMA and one add instruction per pair of scores
+        float lacc[4] = {0.f, 0.f, 0.f, 0.f};
+        exp_half<kF16, 0, true>(sr, 0, p.scale_log2, neg_m, pk[0], lacc);
+        tmem_st32(s_addr, pk[0]);
+        exp_half<kF16, 0, true>(sr, 1, p.scale_log2, neg_m, pk[1], lacc);
+        tmem_st32(s_addr + 32, pk[1]);
+        l += (lacc[0] + lacc[1]) + (lacc[2] + lacc[3]);
+      } else {
+        float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
+        for (int half = 0; half < 2; ++half) {
 #pragma unroll
-        for (int cc = 0; cc < 32; ++cc) {
-          const int c = half * 32 + cc;
-          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * c]), p.scale_log2, neg_m));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * c + 1]), p.scale_log2, neg_m));
-          if (c & 1) { l2 += p0; l3 += p1; } else { l0 += p0; l1 += p1; }
-          pk[half][cc] = pack16<kF16>(p0, p1);
+          for (int cc = 0; cc < 32; ++cc) {
+            const int c = half * 32 + cc;
+            const float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * c]), p.scale_log2, neg_m));
+            const float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * c + 1]), p.scale_log2, neg_m));
+            if (c & 1) { l2 += p0; l3 += p1; } else { l0 += p0; l1 += p1; }
+            pk[half][cc] = pack16<kF16>(p0, p1);
+          }
+          tmem_st32(s_addr + half * 32, pk[half]);
         }
-        tmem_st32(s_addr + half * 32, pk[half]);
+        l += (l0 + l1) + (l2 + l3);
       }
-      l += (l0 + l1) + (l2 + l3);
       if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
         for (int ch = 0; ch < kOChunks; ++ch) {
@@ -679,7 +692,7 @@ FwdVariant fwd_variant(int head_dim, bool fp16, int var) {
   if (head_dim == 64) return fp16 ? fwd_variant_d<64, true>(var) : fwd_variant_d<64, false>(var);
   return fp16 ? fwd_variant_d<128, true>(var) : fwd_variant_d<128, false>(var);
 }
-// Pipeline of FwdParams::variant -1: MGFA_FWD_VARIANT (0, 1 or 2), else kDefaultFwdVariant.
+// Pipeline of FwdParams::variant -1: MGFA_FWD_VARIANT (0-2), else kDefaultFwdVariant.
 int default_fwd_variant() {
   static const int v = [] {
     const char* e = std::getenv("MGFA_FWD_VARIANT");

@@ -81,10 +81,10 @@ struct FwdParams {
   // previous step's grid is still running; it waits for that grid only before
   // its epilogue touches the running state (o_state / lse / o).
   int dependent_launch = 0;
-  // Pipeline: 0 whole 128-key tiles; 1 half tiles (the next half's S computed
-  // while the softmax works on the current one); 2 half tiles with a quarter of
-  // the exponentials on the FMA pipe; -1 the build's default (or
-  // MGFA_FWD_VARIANT). The launcher replaces -1 with the value it used.
+  // Pipeline: 0 whole 128-key tiles, packed f32x2 softmax; 1 half tiles (the
+  // next half's S computed while the softmax works on the current one); 2
+  // whole tiles, scalar softmax; -1 the build's default (or MGFA_FWD_VARIANT).
+  // The launcher replaces -1 with the value it used.
   int variant = -1;
 };
 

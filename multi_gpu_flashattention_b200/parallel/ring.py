@@ -124,9 +124,11 @@ class _Engines:
         # MGFA_TAG_CHECK=0 skips the consumers' owner-tag check (an experiment
         # knob: one system-scope load less per CTA and step)
         eng.set_tag_check(os.environ.get("MGFA_TAG_CHECK", "1") != "0")
-        # MGFA_CUMULATIVE_ARRIVALS=1: arrival counts keep growing (cumulative
-        # targets), so dependent launch stays on for every grid size
-        eng.set_cumulative_arrivals(os.environ.get("MGFA_CUMULATIVE_ARRIVALS", "0") == "1")
+        # Arrival counts keep growing (cumulative targets, wrap-safe waits), so
+        # dependent launch stays on for every grid size; MGFA_CUMULATIVE_ARRIVALS=0
+        # re-arms them per use instead (small grids then run without dependent
+        # launch at P >= 5)
+        eng.set_cumulative_arrivals(os.environ.get("MGFA_CUMULATIVE_ARRIVALS", "1") != "0")
         handles = [None] * world
         dist.all_gather_object(handles, eng.ipc_handle(), group=group)
         eng.connect(handles)

@@ -1,5 +1,5 @@
 """Every pipeline of the per-step sm_100a forward kernel (flash_fwd_sm100.cu:
-whole 128-key tiles, half tiles, half tiles with FMA-pipe exponentials) against
+whole 128-key tiles with packed or scalar softmax arithmetic, half tiles) against
 the fp32 PyTorch oracle: causal and full masks, GQA, ragged lengths, tile
 positions of a zigzag-like shard, head_dim 64, fp16, the in-kernel merge with
 a running state, and scores whose row max keeps growing (O rescaled in TMEM at
