@@ -271,9 +271,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       if ((threadIdx.x & 31) == 0) mbar_arrive(&s.s_free);
       float pr[128];
       if (j < full_hi) {  // warp-uniform fast path: no mask
+        // one f32x2 FMA per pair of scores
+        const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2), nl2 = f2_pack(-lse2, -lse2);
 #pragma unroll
-        for (int c = 0; c < 128; ++c)
-          pr[c] = ex2_approx(fmaf(__uint_as_float(sr[c]), p.scale_log2, -lse2));
+        for (int c = 0; c < 128; c += 2) {
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), sc2, nl2),
+                    x0, x1);
+          pr[c] = ex2_approx(x0);
+          pr[c + 1] = ex2_approx(x1);
+        }
       } else {
         int n_vis = p.sk - j * kTile;
         if (p.causal) {
@@ -295,10 +302,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld32(tmem + lane_off + DP_COL + ch * 32, dpr);
         tmem_wait_ld();
         regs_defined32(dpr);
+        const uint64_t dl2 = f2_pack(dlt, dlt);
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
-          const float d0 = pr[ch * 32 + 2 * c] * (__uint_as_float(dpr[2 * c]) - dlt);
-          const float d1 = pr[ch * 32 + 2 * c + 1] * (__uint_as_float(dpr[2 * c + 1]) - dlt);
+          // dS = P (dP - delta), one f32x2 subtract and multiply per pair
+          float d0, d1;
+          f2_unpack(f2_mul(f2_pack(pr[ch * 32 + 2 * c], pr[ch * 32 + 2 * c + 1]),
+                           f2_sub(f2_pack(__uint_as_float(dpr[2 * c]),
+                                          __uint_as_float(dpr[2 * c + 1])), dl2)),
+                    d0, d1);
           pk[ch][c] = pack16<kF16>(d0, d1);
         }
         // dS over the first 64 columns of the dP region (column ch*16.. holds
@@ -579,9 +591,14 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
           regs_defined32(dpr);
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
+            // dS^T = P^T (dP^T - delta), one f32x2 subtract and multiply per pair
             const int c0 = ch * 32 + 2 * c;
-            const float d0 = pr[c0] * (__uint_as_float(dpr[2 * c]) - dl[c0]);
-            const float d1 = pr[c0 + 1] * (__uint_as_float(dpr[2 * c + 1]) - dl[c0 + 1]);
+            float d0, d1;
+            f2_unpack(f2_mul(f2_pack(pr[c0], pr[c0 + 1]),
+                             f2_sub(f2_pack(__uint_as_float(dpr[2 * c]),
+                                            __uint_as_float(dpr[2 * c + 1])),
+                                    f2_pack(dl[c0], dl[c0 + 1]))),
+                      d0, d1);
             dk[ch][c] = pack16<kF16>(d0, d1);
           }
           tmem_st16(tmem + lane_off + DPT_COL + ch * 16, dk[ch]);
