@@ -22,6 +22,7 @@ void register_ring_engine_p(py::module& m) {
       .def("set_drop_signal", &RingEngineP::set_drop_signal)
       .def("set_tune", &RingEngineP::set_tune)
       .def("set_push_after_compute", &RingEngineP::set_push_after_compute)
+      .def("set_push_ctas", &RingEngineP::set_push_ctas)
       .def("poison_slots", &RingEngineP::poison_slots)
       .def("forward", &RingEngineP::forward, py::arg("q"), py::arg("k"), py::arg("v"),
            py::arg("scale"), py::arg("causal"), py::arg("q_tile_pos"), py::arg("kv_tile_pos"),

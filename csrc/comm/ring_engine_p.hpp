@@ -110,6 +110,9 @@ class RingEngineP {
   // after their CTA's compute.
   void set_tune(int tune) { tune_ = tune; }
   void set_push_after_compute(bool on) { push_after_ = on; }
+  // Experiment knob: the last k CTAs only push, the others only compute (0: two
+  // push warps in every CTA). Clamped to [0, grid / 2].
+  void set_push_ctas(int k) { push_ctas_ = k < 0 ? 0 : k; }
   // Test knob: the next calls drop the signal of unit (segment 0, chunk 0),
   // part 0, so the right neighbour's wait for it must expire.
   void set_drop_signal(bool on) { drop_signal_ = on; }
@@ -233,7 +236,10 @@ class RingEngineP {
       for (int s = 0; s < P; ++s) R.seg_tag[s] = seg_tag(P, r, s, calls_);
       R.drop_signal = drop_signal_ ? 1 : 0;
     }
-    if (ring) p.ring.push_after_compute = push_after_ ? 1 : 0;
+    if (ring) {
+      p.ring.push_after_compute = push_after_ ? 1 : 0;
+      p.ring.push_ctas = push_ctas_ < grid / 2 ? push_ctas_ : grid / 2;
+    }
     nvtxRangePushA(ring ? "ring attention (persistent)" : "ring attention compute only");
     attn_fwd_persistent_launch(mq, mk, mv, mslots, D, f16, p, grid, tune_, stream);
     nvtxRangePop();
@@ -265,6 +271,7 @@ class RingEngineP {
   bool drop_signal_ = false;
   int tune_ = -1;
   bool push_after_ = false;
+  int push_ctas_ = 0;
   torch::Tensor last_trace_;
   torch::Tensor pos_src_, pos_seg_;
   uint32_t pos_version_ = 0;

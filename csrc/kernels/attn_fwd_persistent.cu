@@ -302,7 +302,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = s.tmem_base;
   int items_done = 0;
 
-  if (warp == 8) {
+  // Push-only CTAs (PRing::push_ctas > 0): every warp pushes; these CTAs take
+  // no work item, so the dynamic scheduler hands all items to the others.
+  const int first_push_cta = kRing ? int(gridDim.x) - p.ring.push_ctas : int(gridDim.x);
+  const bool push_cta = kRing && p.ring.push_ctas > 0 && int(blockIdx.x) >= first_push_cta;
+  if (push_cta) {
+    push_units<kD>(p, (int(blockIdx.x) - first_push_cta) * kWarps + int(warp),
+                   p.ring.push_ctas * kWarps, &s.abort_flag, &tr_push0, &tr_push1);
+  } else if (warp == 8) {
     // ------------------------------------------------------------ scheduler + TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&map_q);
@@ -541,7 +548,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= 10) {
     // ------------------------------------------------------------ ring push
-    if (kRing) {
+    if (kRing && p.ring.push_ctas == 0) {
       if (p.ring.push_after_compute) {
         // diagnostic: start pushing only once this CTA's compute is over
         volatile uint32_t* done = &s.softmax_done;
@@ -836,7 +843,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) tmem_dealloc<512>(tmem);
   if (warp >= 10 && lane == 0 && p.trace && kRing) {
     uint64_t* tr = p.trace + uint64_t(blockIdx.x) * kPTraceWords;
-    if (warp == 10) {
+    if (warp == 10) {  // (in a push-only CTA: warp 10's own push times)
       tr[6] = tr_push0;
       tr[7] = tr_push1;
     }

@@ -57,6 +57,10 @@ struct PRing {
                                      // copied but never signalled
   int push_after_compute = 0;        // diagnostic knob: a CTA's push warps start only
                                      // once its softmax warps have finished every item
+  int push_ctas = 0;                 // > 0: the last push_ctas CTAs of the grid only
+                                     // push (all their warps) and compute nothing, and
+                                     // the other CTAs only compute, so no CTA mixes the
+                                     // two; 0: two push warps in every CTA
 };
 
 struct PFwdParams {

@@ -165,6 +165,9 @@ class _PEngines:
             self._by_key.pop(key)
             del eng
         eng = C().RingEngineP(rank, world, device.index, cap)
+        # MGFA_P_PUSH_CTAS=k: the last k CTAs of the one-launch grid only push and
+        # the others only compute (an experiment on the ring's open defect)
+        eng.set_push_ctas(int(os.environ.get("MGFA_P_PUSH_CTAS", "0")))
         handles = [None] * world
         dist.all_gather_object(handles, eng.ipc_handle(), group=group)
         eng.connect(handles)
