@@ -64,6 +64,8 @@ def resolve_backend(backend: Optional[str], is_cuda: bool = True) -> str:
     if backend == "fused":
         backend = "fused_one_launch" if RING_ENGINE == "one_launch" else "fused_stepwise"
     return backend
+
+
 # transport modes of the per-step engine (RingEngine.set_transport_mode)
 _ENGINE_MODES = {"fused_stepwise": 0, "p2p_unfused": 1, "ce_unfused": 2}
 
