@@ -465,9 +465,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) {
         ok = mbar_wait(&s.q_full, n & 1, ab, 91);
         if (ok && T == 0) {
+          // No visible key tile: no MMA, but the item still takes one phase of
+          // each O hand-over. Without the o_empty waits this thread would run a
+          // phase ahead of a slow epilogue, whose parity wait then aliases (a
+          // stall, or the next item's first PV overwriting O while the previous
+          // item's epilogue still reads it).
           mma_commit(&s.q_empty);
-          mma_commit(&s.o_full[0]);
-          mma_commit(&s.o_full[1]);
+          ok = mbar_wait(&s.o_empty[0], (n & 1) ^ 1, ab, 94) &&
+               mbar_wait(&s.o_empty[1], (n & 1) ^ 1, ab, 98);
+          if (ok) {
+            mma_commit(&s.o_full[0]);
+            mma_commit(&s.o_full[1]);
+          }
         } else if (ok) {
           {
             const int st = int(it & 1);

@@ -77,6 +77,23 @@ def test_small_grid_many_items_per_cta(grid):
     torch.testing.assert_close(outs[0][0], outs[1][0], rtol=0, atol=0)
 
 
+@pytest.mark.parametrize("grid", [1, 2])
+def test_items_without_visible_keys_between_others(grid):
+    """Causal query pairs that see no key at all (no MMA, but an O hand-over
+    phase) alternate with pairs that do, in one or two CTAs, so every CTA runs
+    both kinds back to back: the output of the visible pairs must be exact and
+    the others zero with an LSE of -inf."""
+    q, k, v = _inputs(1, 1024, 256, 2, 2, seed=11)
+    starts = [0, 128, 640, 768, 128, 256, 1024, 1152]  # pairs: none, both, none, both
+    qtp = torch.tensor(starts, dtype=torch.int32, device="cuda")
+    ktp = torch.tensor([512, 640], dtype=torch.int32, device="cuda")
+    q_pos = torch.cat([torch.arange(128) + s0 for s0 in starts]).cuda()
+    k_pos = torch.cat([torch.arange(128) + s0 for s0 in (512, 640)]).cuda()
+    outs = _run(q, k, v, True, qtp=qtp, ktp=ktp, grid=grid, calls=3)
+    for o, lse in outs:
+        _check(o, lse, q, k, v, True, q_pos=q_pos, k_pos=k_pos)
+
+
 def test_ragged_lengths_noncausal():
     q, k, v = _inputs(1, 200, 333, 2, 2, seed=3)
     (o, lse), = _run(q, k, v, False)
