@@ -614,10 +614,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if constexpr (kProfile) { c1 = clk(); pa[0] += c1 - c0; c0 = c1; pa[5] += 1; }
           tc_fence_after();
           uint32_t sr[128];
-          tmem_ld32(s_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-          tmem_ld32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
-          tmem_ld32(s_addr + 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
-          tmem_ld32(s_addr + 96, *reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
+          tmem_ld128_sync(s_addr, sr);  // load and wait in one statement
           const bool full = j < full_hi;  // warp-uniform
           int n_vis = 128;
           if (!full) {  // diagonal / ragged / invisible tile: this row's visible keys
@@ -628,11 +625,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (!q_valid) n_vis = 0;
           }
-          tmem_wait_ld();
-          regs_defined32(&sr[0]);
-          regs_defined32(&sr[32]);
-          regs_defined32(&sr[64]);
-          regs_defined32(&sr[96]);
           if constexpr (kProfile) { c1 = clk(); pa[1] += c1 - c0; c0 = c1; }
           if (!full) {
 #pragma unroll
@@ -665,9 +657,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const float nm = redo ? -m : 0.f;
 #pragma unroll
               for (int qq = 0; qq < 2; ++qq) {
-                tmem_ld32(s_addr + qq * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[qq * 32]));
-                tmem_wait_ld();
-                regs_defined32(&sr[qq * 32]);
+                tmem_ld32_sync(s_addr + qq * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[qq * 32]));
                 if (redo) {
                   uint32_t pq[16];
                   float unused_mx[4];
@@ -760,9 +750,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int ch = 0; ch < kOChunks; ++ch) {
               uint32_t orow[32];
-              tmem_ld32(o_addr + ch * 32, orow);
-              tmem_wait_ld();
-              regs_defined32(orow);
+              tmem_ld32_sync(o_addr + ch * 32, orow);
 #pragma unroll
               for (int c = 0; c < 32; ++c)
                 orow[c] = __float_as_uint(__uint_as_float(orow[c]) * alpha);
@@ -804,9 +792,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int ch = 0; ch < kOChunks; ++ch) {
         uint32_t o[32];
         if (any) {
-          tmem_ld32(o_addr + ch * 32, o);
-          tmem_wait_ld();
-          regs_defined32(o);
+          tmem_ld32_sync(o_addr + ch * 32, o);
         } else {
 #pragma unroll
           for (int c = 0; c < 32; ++c) o[c] = 0u;
