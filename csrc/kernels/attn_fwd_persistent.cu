@@ -754,16 +754,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int c = 0; c < 32; ++c)
                 orow[c] = __float_as_uint(__uint_as_float(orow[c]) * alpha);
-              tmem_st32(o_addr + ch * 32, orow);
-              tmem_wait_st();
-              regs_live32(orow);
+              tmem_st32_sync(o_addr + ch * 32, orow);
             }
           }
-          if (!early) tmem_st32(s_addr, pk0);
-          tmem_st32(s_addr + 32, pk1);
-          tmem_wait_st();
-          regs_live32(pk0);
-          regs_live32(pk1);
+          if (early) {
+            tmem_st32_sync(s_addr + 32, pk1);
+          } else {
+            tmem_st32x2_sync(s_addr, pk0, pk1);
+          }
           tc_fence_before();
           __syncwarp();
           if (lane == 0) {

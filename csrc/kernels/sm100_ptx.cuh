@@ -321,6 +321,53 @@ __device__ __forceinline__ void tmem_ld128_sync(uint32_t taddr, uint32_t (&r)[12
       : "memory");
 }
 
+// Store and wait in one asm statement: the source registers are read by the
+// asynchronous store, so they must keep their values until tcgen05.wait::st;
+// as inputs of the same statement that ends with the wait, the compiler cannot
+// reuse them before it.
+__device__ __forceinline__ void tmem_st32_sync(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {"
+      "%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32"
+      "};\n\t"
+      "tcgen05.wait::st.sync.aligned;"
+      ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
+        "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]),
+        "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]),
+        "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+// Two 32-column stores (a at taddr, b at taddr + 32) and one wait.
+__device__ __forceinline__ void tmem_st32x2_sync(uint32_t taddr, const uint32_t (&a)[32],
+                                                 const uint32_t (&b)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {"
+      "%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
+      "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33"
+      "};\n\t"
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%1], {"
+      "%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,"
+      "%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64,%65"
+      "};\n\t"
+      "tcgen05.wait::st.sync.aligned;"
+      ::"r"(taddr), "r"(taddr + 32),
+        "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(a[4]), "r"(a[5]), "r"(a[6]),
+        "r"(a[7]), "r"(a[8]), "r"(a[9]), "r"(a[10]), "r"(a[11]), "r"(a[12]), "r"(a[13]),
+        "r"(a[14]), "r"(a[15]), "r"(a[16]), "r"(a[17]), "r"(a[18]), "r"(a[19]), "r"(a[20]),
+        "r"(a[21]), "r"(a[22]), "r"(a[23]), "r"(a[24]), "r"(a[25]), "r"(a[26]), "r"(a[27]),
+        "r"(a[28]), "r"(a[29]), "r"(a[30]), "r"(a[31]), "r"(b[0]), "r"(b[1]), "r"(b[2]),
+        "r"(b[3]), "r"(b[4]), "r"(b[5]), "r"(b[6]), "r"(b[7]), "r"(b[8]), "r"(b[9]),
+        "r"(b[10]), "r"(b[11]), "r"(b[12]), "r"(b[13]), "r"(b[14]), "r"(b[15]), "r"(b[16]),
+        "r"(b[17]), "r"(b[18]), "r"(b[19]), "r"(b[20]), "r"(b[21]), "r"(b[22]), "r"(b[23]),
+        "r"(b[24]), "r"(b[25]), "r"(b[26]), "r"(b[27]), "r"(b[28]), "r"(b[29]), "r"(b[30]),
+        "r"(b[31])
+      : "memory");
+}
+
 // tcgen05.ld writes its destination registers asynchronously: they hold the
 // loaded values only once tcgen05.wait::ld has returned. To the compiler the
 // load's outputs look defined at the load itself, and the wait (an asm
