@@ -1,7 +1,7 @@
 """Record a ring engine's per-CTA timeline for one forward call.
 
     torchrun --nproc-per-node N -m multi_gpu_flashattention_b200.benchmarks.ring_trace \
-        [--seq 131072] [--heads 32] [--out DIR] [--backend fused_one_launch|fused_stepwise]
+        [--seq 131072] [--heads 32] [--out DIR] [--backend fused_stepwise|fused_one_launch]
 
 After 3 untraced calls, one traced call writes DIR/summary_rank<r>.json and
 DIR/trace_rank0.json (Chrome trace of rank 0). One-launch ring ("fused_one_launch"):
@@ -29,7 +29,7 @@ def main():
     ap.add_argument("--heads", type=int, default=32)
     ap.add_argument("--layout", default="zigzag")
     ap.add_argument("--out", default="ring_trace")
-    ap.add_argument("--backend", default="fused_one_launch",
+    ap.add_argument("--backend", default="fused_stepwise",
                     choices=["fused_one_launch", "fused_stepwise"])
     a = ap.parse_args()
     ctx = common.init(need_world_gt1=True)
