@@ -614,7 +614,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if constexpr (kProfile) { c1 = clk(); pa[0] += c1 - c0; c0 = c1; pa[5] += 1; }
           tc_fence_after();
           uint32_t sr[128];
-          tmem_ld128_sync(s_addr, sr);  // load and wait in one statement
+          tmem_ld64_sync(s_addr, sr);  // load and wait in one statement
+          tmem_ld64_sync(s_addr + 64, sr + 64);
           const bool full = j < full_hi;  // warp-uniform
           int n_vis = 128;
           if (!full) {  // diagonal / ragged / invisible tile: this row's visible keys
