@@ -907,6 +907,7 @@ KernelFn pick_var(int var) {
     case 1: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 1>;
     case 2: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 2>;
     case 4: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 4>;
+    case 5: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 5>;
     case 7: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 7>;
     case 11: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 11>;
     case 15: return attn_fwd_persistent_kernel<128, false, kPoly8, false, 15>;

@@ -13,7 +13,9 @@ bits 0-7 exponential pairs of every 8 on the FMA pipe (0, 2 or 4), bit 8 packed
 f32x2 arithmetic, bit 9 P handed over in two halves. Prints one JSON line per
 variant with the median time and attention TFLOP/s. --profile T runs variant T
 with its phase counters (bit 10) once and prints the mean clock cycles per key
-tile of each softmax and MMA-thread phase."""
+tile of each softmax and MMA-thread phase; T = -1 profiles the default variant
+(packed arithmetic, 0x100). The profiled variants built are the scalar, packed,
+packed + split and the tree / speculative combinations of those."""
 from __future__ import annotations
 
 import argparse
@@ -69,7 +71,7 @@ def main(argv=None):
                  "mma_wait_P0h0", "mma_wait_P0h1", "mma_wait_K", "mma_wait_P1h0",
                  "mma_wait_P1h1", "mma_tiles", "mma_loop"]
         for t in a.profile.split(","):
-            tv = int(t, 0) | 0x400
+            tv = (0x100 if int(t, 0) < 0 else int(t, 0)) | 0x400
             tr = torch.zeros(512, 16, dtype=torch.int64, device="cuda")
             persistent(tv)()  # warm-up
             tr.zero_()
