@@ -60,15 +60,37 @@ def _rearmed_case(rank, world, push_ctas):
     ql, kl, vl = lay.shard(q, rank), lay.shard(k, rank), lay.shard(v, rank)
     exp = lay.shard(attention_ref(q, k, v)[0], rank)
     P_ENGINES.get(None, dev, kl.numel() * kl.element_size()).set_push_ctas(push_ctas)
+    # candidates for a wrong row: attention over the rank's own shard only, over
+    # the other shards only, and exact (all keys)
+    own = slice(rank * 512, rank * 512 + 512)
+    mask_own = torch.zeros(seq, dtype=torch.bool, device=dev)
+    mask_own[own] = True
+
+    def nearest(row, h, got):
+        qrow = q[0, rank * 512 + row, h].float()
+        kk, vv = k[0, :, h].float(), v[0, :, h].float()
+        sc = (kk @ qrow) * 128 ** -0.5
+        cands = {"exact": torch.ones_like(mask_own), "own_shard_only": mask_own,
+                 "other_shards_only": ~mask_own}
+        dist = {}
+        for name, m in cands.items():
+            pr = torch.softmax(sc.masked_fill(~m, float("-inf")), 0)
+            dist[name] = round((got - pr @ vv).abs().max().item(), 4)
+        return dist
+
     bad = []
     for it in range(10):
         reset_ring()
         out, _ = ring_attention_forward(ql, kl, vl, lay, causal=False,
                                         backend="fused_one_launch", check=True)
-        err = (out.float() - exp).abs().amax(dim=(0, 2, 3))
-        tiles = sorted({int(r) // 128 for r in (err > 2e-2).nonzero().flatten().tolist()})
+        err = (out.float() - exp).abs()
+        rows = (err.amax(dim=(0, 2, 3)) > 2e-2).nonzero().flatten().tolist()
+        tiles = sorted({int(r) // 128 for r in rows})
         if tiles:
-            bad.append((it, tiles))
+            r0 = int(rows[0])
+            h0 = int(err[0, r0].amax(dim=1).argmax())
+            bad.append((it, tiles, {"row": r0, "head": h0,
+                                    "distance_to": nearest(r0, h0, out[0, r0, h0].float())}))
     P_ENGINES.get(None, dev, kl.numel() * kl.element_size()).set_push_ctas(0)
     assert not bad, f"rank {rank}: calls with wrong query tiles {bad}"
 
